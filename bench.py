@@ -1,0 +1,390 @@
+"""Benchmark of the B200 MoE hot path (BASELINE.json metric: MoE-layer tokens/s, achieved HBM GB/s and %
+of roofline).
+
+Default workload: one decode step = T=1 token through all 58 DeepSeek-R1 MoE layers on
+one B200, every layer's 256 IQ2_XXS experts + shared expert + router resident in HBM (58 distinct layers,
+~170 GB; a step streams ~6.35 GB of weights, far above the 126 MB L2, so no flush is needed between steps).
+Each layer takes its own seeded N(0,1) fp32 input row and residual; layers run back to back on one stream,
+captured as one CUDA graph per step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill|imbalance] [--impl ours|reference]
+
+N > 1 (torchrun): the decode workload runs N independent replicas (one per GPU, each with all 58 layers:
+the weights fit one B200); value = tokens of all ranks / max-over-ranks time.  --impl reference times the
+CPU oracle (the restatement of the reference's CPU path) on the host cores on a bounded sample.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+N_LAYERS = 58
+SEED = 0x10C1
+HIDDEN, INTER, NE = 7168, 2048, 256
+MAT = INTER * (HIDDEN // 256) * 66                       # 3 784 704 bytes per expert matrix
+ROUTER_BYTES = NE * HIDDEN * 4
+
+
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def ncu_traffic(kernel, workload):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary (profiles/ncu_traffic.txt), or None."""
+    p = os.path.join(REPO, "profiles", "ncu_traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        f = line.split()
+        if len(f) >= 3 and not line.startswith("#") and f[0] == kernel and f[1] == workload:
+            return float(f[2])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu):
+        self.gpu, self.proc, self.lines = gpu, None, []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1])); mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_setup(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def dist_init(ws, local):
+    import torch
+    import torch.distributed as dist
+    if ws > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    return dist if ws > 1 else None
+
+
+def barrier(dist):
+    import torch
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(dist, v):
+    import torch
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle)
+def cpu_decode_sample(n_layers, keep=8, seed=SEED):
+    """Time the CPU oracle on T=1 decode for n_layers layers (router + experts + combine); returns
+    (seconds per layer, cores).  Weights for the selected experts are generated before the clock starts."""
+    from oracle import oracle as O
+    O.build()
+    times = []
+    for L in range(n_layers):
+        rng = np.random.default_rng(seed + L)
+        x = rng.standard_normal((1, HIDDEN)).astype(np.float32)
+        r = rng.standard_normal((1, HIDDEN)).astype(np.float32)
+        W = (rng.standard_normal((NE, HIDDEN)) * 0.02).astype(np.float32)
+        bias = (rng.standard_normal(NE) * 0.01).astype(np.float32)
+        cfg = O.route_cfg(8, keep)
+        _, sel, w = O.router(x, W, bias, cfg)
+        used = sorted(set(int(e) for e in sel[0]))
+        remap = {e: i for i, e in enumerate(used)}
+        ids = np.array([[remap[int(e)] for e in sel[0]]], np.int32)
+        gate = np.concatenate([O.gen_iq2(seed, L, 0, e, INTER, HIDDEN) for e in used])
+        up = np.concatenate([O.gen_iq2(seed, L, 1, e, INTER, HIDDEN) for e in used])
+        down = np.concatenate([O.gen_iq2(seed, L, 2, e, HIDDEN, INTER) for e in used])
+        sh = [O.gen_iq2(seed, L, m, 256, *((INTER, HIDDEN) if m < 2 else (HIDDEN, INTER))) for m in range(3)]
+        t0 = time.perf_counter()
+        _, sel2, w2 = O.router(x, W, bias, cfg)
+        O.moe_layer(x, r, gate, up, down, MAT, ids, w2, sh[0], sh[1], sh[2])
+        times.append(time.perf_counter() - t0)
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return float(np.mean(times)), cores
+
+
+# ------------------------------------------------------------------ decode workload (config 1)
+def build_decode(dev, n_layers, keep):
+    import torch
+    from loki_b200 import moe as M
+    free, total = torch.cuda.mem_get_info(dev)
+    per_layer = (3 * NE + 3) * MAT + ROUTER_BYTES
+    fit = int((free - (6 << 30)) // per_layer)
+    distinct = max(1, min(n_layers, fit))
+    layers = [M.LayerWeights(dev, SEED, L) for L in range(distinct)]
+    torch.cuda.synchronize(dev)
+    return layers, distinct
+
+
+def run_decode(args, ws, rank, local, dist):
+    import torch
+    import ctypes
+    from loki_b200 import moe as M
+    from loki_b200 import native as N
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    layers, distinct = build_decode(dev, args.layers, args.keep)
+    layer_of = [L % distinct for L in range(args.layers)]
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    xs = torch.randn(args.layers, 1, HIDDEN, device=dev, generator=g)
+    rs = torch.randn(args.layers, 1, HIDDEN, device=dev, generator=g)
+    hs = torch.empty(args.layers, 1, HIDDEN, device=dev)
+    mos = torch.empty(args.layers, 1, HIDDEN, device=dev)
+    ctx = M.MoeLayer(local, keep=args.keep, max_tokens=1)
+    structs = [l.struct() for l in layers]
+    L = N.lib()
+    stream = torch.cuda.Stream(dev)
+
+    def step(events=None):
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for i in range(args.layers):
+            if events is not None:
+                arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in events[i]])
+                L.lk_moe_set_events(ctx.ctx, arr)
+            rc = L.lk_moe_forward(ctx.ctx, ctypes.byref(structs[layer_of[i]]), ctypes.c_void_p(xs[i].data_ptr()),
+                                  ctypes.c_void_p(rs[i].data_ptr()), 1, None, ctypes.c_void_p(hs[i].data_ptr()),
+                                  ctypes.c_void_p(mos[i].data_ptr()), None, None, s)
+            N.check(rc, ctx.ctx)
+        if events is not None:
+            L.lk_moe_set_events(ctx.ctx, None)
+
+    # warm-up eager (sets kernel attributes, first-touch), then capture one step as a graph
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize(dev)
+    ctx.device_error()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.layers)]
+    graph_ev = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_ev, stream=stream):
+        step(ev)
+    torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        graph.replay()
+    barrier(dist)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        t1.record(stream)
+    barrier(dist)
+    ms = t0.elapsed_time(t1)
+    # per-kernel pass: the same step with events around each layer's gate/up, down and combine launches
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.steps // 4)):
+            graph_ev.replay()
+    torch.cuda.synchronize(dev)
+    cl = clocks.stop() if clocks else None
+    ctx.device_error()
+    gu = np.array([ev[i][0].elapsed_time(ev[i][1]) for i in range(args.layers)])
+    dn = np.array([ev[i][1].elapsed_time(ev[i][2]) for i in range(args.layers)])
+    cb = np.array([ev[i][2].elapsed_time(ev[i][3]) for i in range(args.layers)])
+    ms_max = max_over_ranks(dist, ms)
+    tokens = args.steps * ws
+    value = tokens / (ms_max / 1e3)
+    hbm, bf16, peak_kind = measured_peaks()
+    n_slots = args.keep + 1
+    gu_bytes = n_slots * 2 * MAT + 4 * HIDDEN                       # 8 routed + shared gate/up rows, x in
+    dn_bytes = n_slots * MAT + n_slots * (INTER + INTER // 32 * 4) + n_slots * HIDDEN * 4
+    layer_bytes = n_slots * 3 * MAT + ROUTER_BYTES + 3 * 4 * HIDDEN
+    gu_ms = float(gu.mean())
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    traffic = ncu_traffic("k_gate_up", "decode_T1")
+    out = {
+        "metric": "MoE-layer tokens/s (T=1 decode through 58 layers)", "value": round(value, 2), "unit": "tokens/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "iq2_xxs x q8 (int8 dp4a, fp32 accumulate)",
+        "data": "synthetic: seeded IQ2_XXS experts (BASELINE config 0 generator), router W N(0,0.02), bias N(0,0.01), x/resid N(0,1) fp32",
+        "config": {"workload": "config1_decode_T1_58layers", "model": "DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)",
+                   "global_batch": ws, "seq_len": 1, "layers": args.layers, "distinct_layers_resident": distinct,
+                   "top_k": 8, "keep": args.keep, "parallelism": "replicas" if ws > 1 else "single",
+                   "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (args.layers * layer_bytes / 1e9)},
+        "layer": {"ms_per_layer": round(ms_max / args.steps / args.layers * 1e3, 3), "unit_ms_per_layer": "us",
+                  "bytes_per_layer": layer_bytes,
+                  "achieved_gbs": round(layer_bytes * args.layers * args.steps / (ms_max / 1e3) / 1e9, 1),
+                  "frac_of_hbm": round(layer_bytes * args.layers * args.steps / (ms_max / 1e3) / 1e9 / hbm, 4),
+                  "kernel_us": {"gate_up": round(gu_ms * 1e3, 2), "down": round(float(dn.mean()) * 1e3, 2),
+                                "combine": round(float(cb.mean()) * 1e3, 2)}},
+        "roofline": {"kernel": "k_gate_up<1> (routed + shared gate/up + SwiGLU + q8)", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "traffic": traffic, "algorithmic_bytes_per_launch": gu_bytes, "peak_source": peak_kind,
+                     "down_kernel_frac": round(dn_bytes / (float(dn.mean()) / 1e3) / 1e9 / hbm, 4)},
+        "gpu_launches": args.steps * args.layers * 5,
+    }
+    if cl:
+        out["clocks"] = cl
+    return out, layers, ctx, structs, xs, rs
+
+
+def e2e_decode(args, layers, distinct, keep):
+    """Decode through the engine-facing fl_* ABI with host buffers: per layer fl_moe_prepare (H2D x/resid,
+    router, shared expert) -> fl_fetch (D2H sel/wts/ncur/fi) -> host keep pass -> fl_moe (D2H h, moe).
+    Wall clock; every copy and host synchronisation is inside the timed region."""
+    from loki_b200 import fused as F
+    from loki_b200 import native as N
+    fc = F.FusedCtx()
+    rng = np.random.default_rng(77)
+    xs = rng.standard_normal((args.layers, 1, HIDDEN)).astype(np.float32)
+    rs = rng.standard_normal((args.layers, 1, HIDDEN)).astype(np.float32)
+    mws = []
+    for l in layers:
+        mws.append(N.FLMoeW(l.router_w.data_ptr(), 0, l.router_bias.data_ptr(), l.sh_gate, l.sh_up, l.sh_down))
+
+    def one_step():
+        for i in range(args.layers):
+            lw = layers[i % distinct]
+            fc.prepare(mws[i % distinct], xs[i], rs[i])
+            r = fc.fetch(1, 1)
+            ids, w = F.keep_pass(r["sel"], r["wts"], keep)
+            fc.moe(lw.gate, lw.up, lw.down, NE, ids, w)
+
+    for _ in range(max(1, args.warmup)):
+        one_step()
+    n = max(1, args.steps // 2)
+    t0 = time.perf_counter()
+    for _ in range(n):
+        one_step()
+    dt = time.perf_counter() - t0
+    err = fc.error()
+    fc.close()
+    h2d = args.layers * (2 * HIDDEN * 4 + keep * 8)
+    d2h = args.layers * (8 * 8 + 2 * HIDDEN * 4 + 2 * HIDDEN * 4)
+    return {"value": round(n / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "fl_moe_prepare -> fl_fetch -> host keep pass -> fl_moe (pinned host mirrors, wall clock)",
+            "steps": n, "error": err}
+
+
+def reference_arm(args, ws, rank):
+    """--impl reference: the CPU oracle (restatement of the reference's path) on the host cores."""
+    if rank != 0:
+        return None
+    per_step = []
+    for s in range(args.warmup + args.steps):
+        t, cores = cpu_decode_sample(1, keep=args.keep, seed=SEED + 1000 * s)
+        if s >= args.warmup:
+            per_step.append(t)
+    t_layer = float(np.mean(per_step))
+    value = 1.0 / (t_layer * args.layers)
+    sample = "1 layer (T=1, top-8 + shared) per step, scaled to %d layers" % args.layers
+    return {"impl": "reference", "metric": "MoE-layer tokens/s (T=1 decode through 58 layers)", "value": round(value, 4),
+            "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_layer * args.layers * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "iq2_xxs x q8 (int32 dot, fp64 accumulate)", "data": "synthetic",
+            "config": {"workload": "config1_decode_T1_58layers", "global_batch": 1, "seq_len": 1, "layers": args.layers,
+                       "keep": args.keep, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode"])
+    ap.add_argument("--layers", type=int, default=N_LAYERS)
+    ap.add_argument("--keep", type=int, default=8)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU-baseline sample")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    ws, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        out = reference_arm(args, ws, rank)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+    import torch
+    dist = dist_init(ws, local)
+    out, layers, ctx, structs, xs, rs = run_decode(args, ws, rank, local, dist)
+    if not args.no_e2e:
+        e2e = e2e_decode(args, layers, len(layers), args.keep)
+        e2e_v = max_over_ranks(dist, 1.0 / e2e["value"])
+        e2e["value"] = round(ws / e2e_v, 2)
+        out["e2e"] = e2e
+    if rank == 0 and ws == 1:
+        t_layer, cores = cpu_decode_sample(args.cpu_layers, keep=args.keep)
+        out["cpu_baseline"] = {"value": round(1.0 / (t_layer * args.layers), 4), "unit": "tokens/s", "cores": cores,
+                               "kind": "port", "sample": "%d layers of T=1 decode through the C++ oracle, scaled to %d layers"
+                               % (args.cpu_layers, args.layers)}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,97 @@
+/* loki_fused_moe.h -- the MoE entry points of loki's fused-layer ABI, served by libloki_moe.so.
+ *
+ * The names, argument lists and meanings are those of the reference's src/fused_layer.h, so that
+ * src/server_core_fused.cpp links against this library for its MoE calls without source changes; the
+ * attention half of that header (fl_attn, fl_spec, fl_sketch) is out of scope and stays with the
+ * reference build.  What replaces what (reference line numbers):
+ *   fl_init          src/fused_layer.h:24     context: stream, buffers, pinned host mirrors
+ *   fl_wide_init     src/fused_layer.h:29     buffers for a wide (prefill) pass of up to wmax rows
+ *   fl_wide_moe      src/fused_layer.h:30     one arena batch of expert slots (<= 8 (row, k) pairs each)
+ *   fl_wide_mark     src/fused_layer.h:31     record the parity's event
+ *   fl_wide_wait     src/fused_layer.h:32     host wait on that event
+ *   fl_wide_finish   src/fused_layer.h:33     h = base + sum_k out, moe = sum_k out, to pinned mirrors
+ *   fl_moe_outs      src/fused_layer.h:35     one row's weighted expert pushes (narrow pass)
+ *   fl_wide_outs     src/fused_layer.h:36     one row's weighted expert pushes (wide pass)
+ *   fl_wide_skip     src/fused_layer.h:37     h = base + stored output (wide pass)
+ *   fl_fetch         src/fused_layer.h:43     sel/wts/ncur/fi (what & 1) and h (what & 32) to the host
+ *   fl_moe           src/fused_layer.h:45     narrow pass: routed experts for n <= 8 rows, combined
+ *   fl_skip          src/fused_layer.h:47     h = stored output + shared + ffn_inp
+ *   fl_h2d           src/fused_layer.h:49     host -> device on the context stream
+ *   fl_wait_event    src/fused_layer.h:51     the context stream waits for an event
+ *   fl_gpu_ms        src/fused_layer.h:52     accumulated GPU time (1: experts, 2: prepare)
+ * Additive (no counterpart: it is the MoE half of fl_attn, src/fused_layer.cu:506-525):
+ *   fl_moe_prepare   router + shared expert on the rows' normalised hidden state `ncur` with residual
+ *                    `ffn_inp`; leaves the context as fl_attn does for the MoE calls that follow.
+ *
+ * Behaviour kept from the reference: host arrays (ids, w, slot tables) are copied before the call
+ * returns; FLOut points into library-owned pinned mirrors valid until the next call on the context;
+ * fl_moe, fl_fetch, fl_wide_finish, fl_skip, fl_wide_skip block the host until their results are in
+ * the mirrors.  Differences: errors are printed and recorded (fl_moe_error) instead of exit(7); the
+ * down projection format must be FL_IQ2 (Q2_K / Q3_K downs return LK_ERR_UNSUPPORTED through
+ * fl_moe_error); with HBM-resident shards, ids may be global expert ids into the full 256-expert arena.
+ */
+#ifndef LOKI_FUSED_MOE_H
+#define LOKI_FUSED_MOE_H
+#include <stdint.h>
+#include <stddef.h>
+
+#ifndef LK_API
+#if defined(__GNUC__)
+#define LK_API __attribute__((visibility("default")))
+#else
+#define LK_API
+#endif
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+struct FLCtx;
+typedef struct FLCtx FLCtx;
+typedef struct CUevent_st* fl_event_t;        /* == cudaEvent_t */
+enum { FL_Q4K = 0, FL_Q6K = 1, FL_Q80 = 2, FL_Q5K = 3, FL_IQ2 = 4, FL_Q2K = 5, FL_Q3K = 6 };
+
+/* host (pinned) mirrors filled by fl_fetch / fl_moe / fl_skip / fl_wide_finish; null where not produced.
+ * Field order and meaning as the reference's FLOut. */
+typedef struct FLOut {
+    const int* sel; const float* wts; const float* ncur; const float* fi; const float* skt; const int* sel_s;
+    const float* wts_s; const float* sc; const float* ccat; const float* h; const float* moe;
+} FLOut;
+
+/* the MoE weights fl_moe_prepare needs: router (F32 or F16 [256][7168]) + bias, shared expert (IQ2_XXS) */
+typedef struct FLMoeW {
+    const void* gate_inp; int gate_f16; const float* probs_b;
+    const void* sh_gate; const void* sh_up; const void* sh_down;
+} FLMoeW;
+
+LK_API FLCtx* fl_init(int kvp, int sc_cap);
+LK_API int    fl_wide_init(FLCtx* c, int wmax, int KE);
+LK_API void   fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int nexp,
+                   const int* midx, const int* rows, const int* kidx, const float* wk, int nslots, int KE, int par);
+LK_API void   fl_wide_mark(FLCtx* c, int par);
+LK_API void   fl_wide_wait(FLCtx* c, int par);
+LK_API void   fl_wide_finish(FLCtx* c, int n, int KE, FLOut* out);
+LK_API void   fl_moe_outs(FLCtx* c, int b, const int* ids, const float* w, int KE, float* out);
+LK_API void   fl_wide_outs(FLCtx* c, int row, int KE, float* out);
+LK_API void   fl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out);
+LK_API void   fl_fetch(FLCtx* c, int n, int what, FLOut* out);
+LK_API void   fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int nexp, int down_fmt,
+              const int* ids, const float* w, int KE, int n, FLOut* out);
+LK_API void   fl_skip(FLCtx* c, const float* mo, int n, FLOut* out);
+LK_API void   fl_h2d(FLCtx* c, void* dst, const void* src, size_t bytes);
+LK_API void   fl_wait_event(FLCtx* c, fl_event_t ev);
+LK_API double fl_gpu_ms(FLCtx* c, int which);
+
+/* additive: the MoE half of fl_attn.  ncur / ffn_inp: N x 7168 fp32 rows, host pointers (host = 1) or
+ * device pointers (host = 0).  wrow >= 0: these rows are rows wrow.. of a wide pass (their ncur and
+ * ffn_inp + shared output go to the pass-wide buffers, as fl_attn's wrow does). */
+LK_API void   fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow);
+/* additive: last error recorded on the context (0 = none), cleared by the call */
+LK_API int    fl_moe_error(FLCtx* c);
+LK_API void   fl_free(FLCtx* c);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

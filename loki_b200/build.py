@@ -1,0 +1,80 @@
+"""Build libloki_moe.so in-tree with nvcc for sm_100a (no JIT cache, no torch extension machinery).
+
+    python -m loki_b200.build            # incremental: per-file objects under loki_b200/_build/
+    python -m loki_b200.build --force    # rebuild everything
+
+The library links the CUDA runtime statically (nvcc's default), so it does not depend on which
+libcudart the host process (e.g. torch) loaded.
+"""
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libloki_moe.so")
+SOURCES = ["expert_gemv.cu", "router.cu", "dispatch.cu", "moe_api.cu", "fl_abi.cu"]
+HEADERS = ["moe_format.h", "moe_device.cuh", "moe_internal.h", "iq2_grid.inc",
+           os.path.join("..", "..", "include", "loki_moe.h"), os.path.join("..", "..", "include", "loki_fused_moe.h")]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+         "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
+
+
+def nvcc():
+    for cand in (os.environ.get("NVCC"), os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc"), "nvcc"):
+        if cand and (os.path.isabs(cand) and os.path.exists(cand) or shutil.which(cand)):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def host_cxx():
+    return "/usr/bin/g++" if os.path.exists("/usr/bin/g++") else "g++"
+
+
+def _stale(target, deps):
+    if not os.path.exists(target):
+        return True
+    t = os.path.getmtime(target)
+    return any(os.path.getmtime(d) > t for d in deps if os.path.exists(d))
+
+
+def build(force=False, verbose=False, ptxas_verbose=False):
+    os.makedirs(BUILD, exist_ok=True)
+    nv = nvcc()
+    hdrs = [os.path.join(CSRC, h) for h in HEADERS]
+    objs = []
+    for src in SOURCES:
+        s = os.path.join(CSRC, src)
+        if not os.path.exists(s):
+            continue
+        o = os.path.join(BUILD, src.replace(".cu", ".o"))
+        objs.append(o)
+        if force or _stale(o, [s, __file__] + hdrs):
+            cmd = [nv, "-ccbin", host_cxx()] + ARCH + FLAGS + (["-Xptxas", "-v"] if ptxas_verbose else []) + ["-c", s, "-o", o]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0 or verbose or ptxas_verbose:
+                sys.stderr.write(r.stdout + r.stderr)
+            if r.returncode != 0:
+                raise RuntimeError("nvcc failed on %s" % src)
+    if force or _stale(LIB, objs):
+        cmd = [nv, "-ccbin", host_cxx()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("link failed")
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--ptxas", action="store_true", help="print -Xptxas -v register/spill/smem reports")
+    a = ap.parse_args()
+    print(build(a.force, a.verbose, a.ptxas))

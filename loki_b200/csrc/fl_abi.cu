@@ -1,0 +1,406 @@
+// fl_abi.cu -- loki's fused-layer MoE entry points (include/loki_fused_moe.h) on the B200 kernels.
+//
+// Same call sequence and ownership rules as the reference (src/fused_layer.cu:528-620): one stream per
+// context, host arrays copied before return, results in library-owned pinned mirrors, the blocking calls
+// synchronise the stream.  The state fl_attn leaves for the MoE calls (ncur, ffn_inp, router outputs,
+// shared-expert output; src/fused_layer.cu:506-525) is produced by the additive fl_moe_prepare.
+#include <cstdio>
+#include <cstring>
+#include <cstdlib>
+#include <vector>
+#include <algorithm>
+#include "../../include/loki_fused_moe.h"
+#include "../../include/loki_moe.h"
+#include "moe_internal.h"
+
+using namespace lk;
+
+namespace {
+constexpr int NB = 8;                 // narrow pass rows (fl_moe's n <= 8)
+constexpr int PREP_ROWS = 64;         // rows per fl_moe_prepare call (fl_attn's 8 groups of 8)
+constexpr int WIDE_SLOTS = 72;        // slots per wide launch set (the reference's XH_SLOTS)
+constexpr int NARROW_SLOTS = NB * MAX_TOPK;
+}
+
+struct FLCtx {
+    cudaStream_t st = nullptr; int dev = 0, nsm = 0;
+    // prepare / narrow state (device)
+    float* ncur = nullptr; float* ffn_inp = nullptr; float* logits = nullptr; float* probs = nullptr;
+    int* sel = nullptr; float* wts = nullptr; float* shared_y = nullptr; float* h = nullptr; float* moe = nullptr;
+    int* ids = nullptr; float* w = nullptr; float* mo = nullptr;
+    int *s_expert = nullptr, *s_tok = nullptr, *s_out = nullptr; float* s_w = nullptr; int* s_n = nullptr;
+    int *counts = nullptr, *offsets = nullptr, *perm = nullptr;
+    int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
+    int* err = nullptr;
+    // host mirrors (pinned)
+    int* h_sel = nullptr; float* h_wts = nullptr; float* h_ncur = nullptr; float* h_fi = nullptr; float* h_h = nullptr;
+    float* h_moe = nullptr; int* h_tab = nullptr; float* h_tabw = nullptr; float* h_in = nullptr;
+    // wide pass
+    int wmax = 0, wke = 0;
+    float* ncur_all = nullptr; float* base_all = nullptr; float* out_all = nullptr; int8_t* whq = nullptr; float* whd = nullptr;
+    int *w_expert[2] = {}, *w_tok[2] = {}, *w_out[2] = {}, *w_n[2] = {}; float* w_w[2] = {};
+    int* hw_tab[2] = {}; float* hw_w[2] = {};
+    float* h_wh = nullptr; float* h_wmoe = nullptr;
+    cudaEvent_t wev[2] = {}, em0 = nullptr, em1 = nullptr, ep0 = nullptr, ep1 = nullptr;
+    double ms_moe = 0, ms_prep = 0;
+    // last narrow call (for fl_moe_outs)
+    int last_n = 0, last_ke = 0; std::vector<int> last_ids; std::vector<float> last_w;
+    int last_err = 0; int prep_n = 0;
+};
+
+static int fl_fail(FLCtx* c, int code, const char* what, cudaError_t e = cudaSuccess) {
+    std::fprintf(stderr, "[loki_moe] %s%s%s\n", what, e != cudaSuccess ? ": " : "", e != cudaSuccess ? cudaGetErrorString(e) : "");
+    if (c && !c->last_err) c->last_err = code;
+    return code;
+}
+#define FLCK(call) do { cudaError_t e_ = (call); if (e_ != cudaSuccess) { fl_fail(c, LK_ERR_CUDA, #call, e_); return; } } while (0)
+#define FLCKR(call, r) do { cudaError_t e_ = (call); if (e_ != cudaSuccess) { fl_fail(c, LK_ERR_CUDA, #call, e_); return r; } } while (0)
+
+template <class T> static cudaError_t dz(T** p, size_t n) {
+    cudaError_t e = cudaMalloc((void**)p, (n ? n : 1) * sizeof(T));
+    if (e == cudaSuccess) e = cudaMemset(*p, 0, (n ? n : 1) * sizeof(T));
+    return e;
+}
+template <class T> static cudaError_t hz(T** p, size_t n) {
+    cudaError_t e = cudaHostAlloc((void**)p, (n ? n : 1) * sizeof(T), cudaHostAllocDefault);
+    if (e == cudaSuccess) std::memset(*p, 0, (n ? n : 1) * sizeof(T));
+    return e;
+}
+
+static int nt_for(int n) { return n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8; }
+
+// device error word -> recorded error (called after a stream synchronisation)
+static void check_dev(FLCtx* c) {
+    int e = 0;
+    if (cudaMemcpy(&e, c->err, 4, cudaMemcpyDeviceToHost) == cudaSuccess && e) {
+        cudaMemset(c->err, 0, 4);
+        fl_fail(c, LK_ERR_DEVICE, "device-side error recorded by a kernel");
+    }
+}
+
+static ExpertParams expert_params(FLCtx* c, const void* gate, const void* up, const void* down, int64_t sg, int64_t sd,
+                                  const float* x, int* se, int* stok, int* sout, float* sw, int* sn,
+                                  int8_t* hq, float* hd, float* y) {
+    ExpertParams e{};
+    e.gate = (const uint8_t*)gate; e.up = (const uint8_t*)up; e.down = (const uint8_t*)down;
+    e.gate_stride = sg; e.up_stride = sg; e.down_stride = sd;
+    e.x = x; e.ld_x = HIDDEN; e.slot_expert = se; e.slot_tok = stok; e.slot_out = sout; e.slot_w = sw; e.nslots = sn;
+    e.hq = hq; e.hd = hd; e.y = y; e.err = c->err;
+    return e;
+}
+
+extern "C" {
+
+FLCtx* fl_init(int kvp, int sc_cap) {
+    (void)kvp; (void)sc_cap;          // attention-side sizes: not used by the MoE path
+    FLCtx* c = new FLCtx();
+    cudaGetDevice(&c->dev);
+    c->nsm = num_sms(c->dev);
+    const size_t R = (size_t)PREP_ROWS * HIDDEN;
+    const size_t rows = (size_t)std::max(NARROW_SLOTS, PREP_ROWS);    // hq / y rows of a narrow or prepare launch
+    const int ms = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1);
+    bool ok =
+        cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) == cudaSuccess &&
+        dz(&c->ncur, R) == cudaSuccess && dz(&c->ffn_inp, R) == cudaSuccess && dz(&c->logits, PREP_ROWS * N_EXPERTS) == cudaSuccess &&
+        dz(&c->probs, PREP_ROWS * N_EXPERTS) == cudaSuccess && dz(&c->sel, PREP_ROWS * MAX_TOPK) == cudaSuccess &&
+        dz(&c->wts, PREP_ROWS * MAX_TOPK) == cudaSuccess && dz(&c->shared_y, R) == cudaSuccess && dz(&c->h, R) == cudaSuccess &&
+        dz(&c->moe, R) == cudaSuccess && dz(&c->ids, NB * MAX_TOPK) == cudaSuccess && dz(&c->w, NB * MAX_TOPK) == cudaSuccess &&
+        dz(&c->mo, R) == cudaSuccess &&
+        dz(&c->s_expert, ms) == cudaSuccess && dz(&c->s_tok, (size_t)ms * MAX_NT) == cudaSuccess &&
+        dz(&c->s_out, (size_t)ms * MAX_NT) == cudaSuccess && dz(&c->s_w, (size_t)ms * MAX_NT) == cudaSuccess && dz(&c->s_n, 1) == cudaSuccess &&
+        dz(&c->counts, N_EXPERTS) == cudaSuccess && dz(&c->offsets, N_EXPERTS + 1) == cudaSuccess && dz(&c->perm, NB * MAX_TOPK) == cudaSuccess &&
+        dz(&c->hq, rows * MOE_INTER) == cudaSuccess && dz(&c->hd, rows * (MOE_INTER / 32)) == cudaSuccess &&
+        dz(&c->y, rows * HIDDEN) == cudaSuccess && dz(&c->err, 1) == cudaSuccess &&
+        hz(&c->h_sel, PREP_ROWS * MAX_TOPK) == cudaSuccess && hz(&c->h_wts, PREP_ROWS * MAX_TOPK) == cudaSuccess &&
+        hz(&c->h_ncur, R) == cudaSuccess && hz(&c->h_fi, R) == cudaSuccess && hz(&c->h_h, R) == cudaSuccess &&
+        hz(&c->h_moe, R) == cudaSuccess && hz(&c->h_tab, (size_t)4 * ms * MAX_NT + 8) == cudaSuccess &&
+        hz(&c->h_tabw, (size_t)ms * MAX_NT) == cudaSuccess && hz(&c->h_in, R) == cudaSuccess &&
+        cudaEventCreate(&c->em0) == cudaSuccess && cudaEventCreate(&c->em1) == cudaSuccess &&
+        cudaEventCreate(&c->ep0) == cudaSuccess && cudaEventCreate(&c->ep1) == cudaSuccess;
+    if (!ok) { fl_fail(c, LK_ERR_CUDA, "fl_init: allocation failed", cudaGetLastError()); fl_free(c); return nullptr; }
+    return c;
+}
+
+void fl_free(FLCtx* c) {
+    if (!c) return;
+    if (c->st) cudaStreamSynchronize(c->st);
+    void* d[] = { c->ncur, c->ffn_inp, c->logits, c->probs, c->sel, c->wts, c->shared_y, c->h, c->moe, c->ids, c->w, c->mo,
+                  c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->counts, c->offsets, c->perm, c->hq, c->hd, c->y, c->err,
+                  c->ncur_all, c->base_all, c->out_all, c->whq, c->whd };
+    for (void* p : d) if (p) cudaFree(p);
+    for (int p = 0; p < 2; ++p) {
+        void* dd[] = { c->w_expert[p], c->w_tok[p], c->w_out[p], c->w_n[p], c->w_w[p] };
+        for (void* q : dd) if (q) cudaFree(q);
+        if (c->hw_tab[p]) cudaFreeHost(c->hw_tab[p]);
+        if (c->hw_w[p]) cudaFreeHost(c->hw_w[p]);
+        if (c->wev[p]) cudaEventDestroy(c->wev[p]);
+    }
+    void* h[] = { c->h_sel, c->h_wts, c->h_ncur, c->h_fi, c->h_h, c->h_moe, c->h_tab, c->h_tabw, c->h_in, c->h_wh, c->h_wmoe };
+    for (void* p : h) if (p) cudaFreeHost(p);
+    cudaEvent_t ev[] = { c->em0, c->em1, c->ep0, c->ep1 };
+    for (cudaEvent_t e : ev) if (e) cudaEventDestroy(e);
+    if (c->st) cudaStreamDestroy(c->st);
+    delete c;
+}
+
+int fl_moe_error(FLCtx* c) { if (!c) return LK_ERR_ARG; const int e = c->last_err; c->last_err = 0; return e; }
+
+void fl_h2d(FLCtx* c, void* dst, const void* src, size_t bytes) {
+    if (!c || !bytes) return;
+    FLCK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, c->st));
+}
+
+void fl_wait_event(FLCtx* c, fl_event_t ev) { if (c) FLCK(cudaStreamWaitEvent(c->st, (cudaEvent_t)ev, 0)); }
+
+double fl_gpu_ms(FLCtx* c, int which) { return !c ? 0.0 : which == 1 ? c->ms_moe : c->ms_prep; }
+
+// shared-expert-only slot table for rows [0, n): written on the host, copied on the stream
+static void shared_slots(FLCtx* c, int n, int nt) {
+    const int ns = (n + nt - 1) / nt;
+    int* he = c->h_tab; int* ht = he + ns; int* ho = ht + ns * nt; float* hw = c->h_tabw;
+    for (int j = 0; j < ns; ++j) {
+        he[j] = SHARED_SLOT;
+        for (int m = 0; m < nt; ++m) { const int t = j * nt + m; ht[j * nt + m] = t < n ? t : -1; ho[j * nt + m] = t < n ? t : -1; hw[j * nt + m] = t < n ? 1.f : 0.f; }
+    }
+    ho[ns * nt] = ns;
+    FLCK(cudaMemcpyAsync(c->s_expert, he, ns * 4, cudaMemcpyHostToDevice, c->st));
+    FLCK(cudaMemcpyAsync(c->s_tok, ht, (size_t)ns * nt * 4, cudaMemcpyHostToDevice, c->st));
+    FLCK(cudaMemcpyAsync(c->s_out, ho, (size_t)ns * nt * 4, cudaMemcpyHostToDevice, c->st));
+    FLCK(cudaMemcpyAsync(c->s_w, hw, (size_t)ns * nt * 4, cudaMemcpyHostToDevice, c->st));
+    FLCK(cudaMemcpyAsync(c->s_n, ho + ns * nt, 4, cudaMemcpyHostToDevice, c->st));
+}
+
+void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
+    if (!c || !W || !ncur || !ffn_inp || N < 1 || N > PREP_ROWS) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: bad argument"); return; }
+    if (wrow >= 0 && (!c->ncur_all || wrow + N > c->wmax)) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: wide rows outside fl_wide_init capacity"); return; }
+    cudaStream_t st = c->st;
+    FLCK(cudaEventRecord(c->ep0, st));
+    const size_t bytes = (size_t)N * HIDDEN * 4;
+    if (host) {
+        std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes);
+        FLCK(cudaMemcpyAsync(c->ncur, c->h_ncur, bytes, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->ffn_inp, c->h_fi, bytes, cudaMemcpyHostToDevice, st));
+    } else {
+        FLCK(cudaMemcpyAsync(c->ncur, ncur, bytes, cudaMemcpyDeviceToDevice, st));
+        FLCK(cudaMemcpyAsync(c->ffn_inp, ffn_inp, bytes, cudaMemcpyDeviceToDevice, st));
+    }
+    c->prep_n = N;
+    // router: full top-8 (the engine applies its keep-KE pass on the fetched rows)
+    RouterParams rp{};
+    rp.x = c->ncur; rp.T = N; rp.ld_x = HIDDEN; rp.W = W->gate_inp; rp.w_f16 = W->gate_f16; rp.bias = W->probs_b;
+    rp.logits = c->logits; rp.probs = c->probs; rp.sel = c->sel; rp.w = c->wts;
+    rp.n_experts = N_EXPERTS; rp.topk = MAX_TOPK; rp.keep = MAX_TOPK; rp.renorm = 0; rp.n_group = 1; rp.topk_group = 1; rp.scale = 2.5f;
+    launch_router(rp, st);
+    // shared expert on all rows
+    if (W->sh_gate && W->sh_up && W->sh_down) {
+        const int nt = nt_for(N);
+        shared_slots(c, N, nt);
+        ExpertParams e = expert_params(c, nullptr, nullptr, nullptr, 0, 0, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n,
+                                       c->hq, c->hd, c->shared_y);
+        e.sh_gate = (const uint8_t*)W->sh_gate; e.sh_up = (const uint8_t*)W->sh_up; e.sh_down = (const uint8_t*)W->sh_down;
+        launch_gate_up(e, nt, c->nsm, st);
+        launch_down(e, nt, c->nsm, st);
+    } else {
+        FLCK(cudaMemsetAsync(c->shared_y, 0, bytes, st));
+    }
+    if (wrow >= 0) {                  // wide pass: this group's ncur and base = ffn_inp + shared
+        FLCK(cudaMemcpyAsync(c->ncur_all + (size_t)wrow * HIDDEN, c->ncur, bytes, cudaMemcpyDeviceToDevice, st));
+        CombineParams cp{};
+        cp.y = nullptr; cp.resid = c->ffn_inp; cp.T = N; cp.keep = 0; cp.with_shared = 0; cp.shared = c->shared_y;
+        cp.h = c->base_all + (size_t)wrow * HIDDEN; cp.moe = nullptr; cp.ld_out = HIDDEN;
+        launch_combine(cp, st);
+    }
+    FLCK(cudaEventRecord(c->ep1, st));
+    FLCK(cudaGetLastError());
+}
+
+void fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
+    if (!c || !out) return;
+    std::memset(out, 0, sizeof(FLOut));
+    n = std::min(n, c->prep_n > 0 ? c->prep_n : n);
+    cudaStream_t st = c->st;
+    if (what & 1) {
+        FLCK(cudaMemcpyAsync(c->h_sel, c->sel, (size_t)n * MAX_TOPK * 4, cudaMemcpyDeviceToHost, st));
+        FLCK(cudaMemcpyAsync(c->h_wts, c->wts, (size_t)n * MAX_TOPK * 4, cudaMemcpyDeviceToHost, st));
+        FLCK(cudaMemcpyAsync(c->h_ncur, c->ncur, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+        FLCK(cudaMemcpyAsync(c->h_fi, c->ffn_inp, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+        out->sel = c->h_sel; out->wts = c->h_wts; out->ncur = c->h_ncur; out->fi = c->h_fi;
+    }
+    if (what & 32) { FLCK(cudaMemcpyAsync(c->h_h, c->h, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st)); out->h = c->h_h; }
+    FLCK(cudaStreamSynchronize(st));
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, c->ep0, c->ep1) == cudaSuccess) c->ms_prep += ms;
+    check_dev(c);
+}
+
+void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int nexp, int down_fmt, const int* ids, const float* w,
+            int KE, int n, FLOut* out) {
+    if (!c || !out) return;
+    std::memset(out, 0, sizeof(FLOut));
+    if (down_fmt != FL_IQ2) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe: down format must be FL_IQ2 in this build"); return; }
+    if (n < 1 || n > NB || KE < 1 || KE > MAX_TOPK || nexp < 1 || nexp > N_EXPERTS || !ids || !w) { fl_fail(c, LK_ERR_ARG, "fl_moe: bad argument"); return; }
+    if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_moe: arena not 16-byte aligned"); return; }
+    for (int i = 0; i < n * KE; ++i) if (ids[i] < 0 || ids[i] >= nexp) { fl_fail(c, LK_ERR_ARG, "fl_moe: slot id out of range"); return; }
+    cudaStream_t st = c->st;
+    FLCK(cudaEventRecord(c->em0, st));
+    int* hi = c->h_tab; float* hw = c->h_tabw;
+    std::memcpy(hi, ids, (size_t)n * KE * 4); std::memcpy(hw, w, (size_t)n * KE * 4);
+    FLCK(cudaMemcpyAsync(c->ids, hi, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
+    FLCK(cudaMemcpyAsync(c->w, hw, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
+    c->last_ids.assign(ids, ids + n * KE); c->last_w.assign(w, w + n * KE); c->last_n = n; c->last_ke = KE;
+    const int nt = nt_for(n);
+    SlotParams sp{};
+    sp.sel = c->ids; sp.w = c->w; sp.T = n; sp.keep = KE; sp.n_experts = N_EXPERTS; sp.nt = nt; sp.with_shared = 0;
+    sp.counts = c->counts; sp.offsets = c->offsets; sp.perm = c->perm;
+    sp.slot_expert = c->s_expert; sp.slot_tok = c->s_tok; sp.slot_out = c->s_out; sp.slot_w = c->s_w; sp.nslots = c->s_n;
+    sp.max_slots = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1);
+    launch_build_slots(sp, st);
+    const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)EXPERT_DOWN_BYTES;
+    ExpertParams e = expert_params(c, gate, up, down, sg, sd, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->hq, c->hd, c->y);
+    launch_gate_up(e, nt, c->nsm, st);
+    launch_down(e, nt, c->nsm, st);
+    CombineParams cp{};
+    cp.y = c->y; cp.resid = c->ffn_inp; cp.T = n; cp.keep = KE; cp.with_shared = 0; cp.shared = c->shared_y;
+    cp.h = c->h; cp.moe = c->moe; cp.ld_out = HIDDEN;
+    launch_combine(cp, st);
+    FLCK(cudaMemcpyAsync(c->h_h, c->h, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+    FLCK(cudaMemcpyAsync(c->h_moe, c->moe, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+    FLCK(cudaEventRecord(c->em1, st));
+    FLCK(cudaStreamSynchronize(st));
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, c->em0, c->em1) == cudaSuccess) c->ms_moe += ms;
+    check_dev(c);
+    out->h = c->h_h; out->moe = c->h_moe;
+}
+
+void fl_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
+    if (!c || !out || !mo || n < 1 || n > PREP_ROWS) return;
+    std::memset(out, 0, sizeof(FLOut));
+    cudaStream_t st = c->st;
+    std::memcpy(c->h_in, mo, (size_t)n * HIDDEN * 4);
+    FLCK(cudaMemcpyAsync(c->mo, c->h_in, (size_t)n * HIDDEN * 4, cudaMemcpyHostToDevice, st));
+    CombineParams cp{};
+    cp.y = c->mo; cp.resid = c->ffn_inp; cp.T = n; cp.keep = 1; cp.with_shared = 0; cp.shared = c->shared_y;
+    cp.h = c->h; cp.moe = nullptr; cp.ld_out = HIDDEN;
+    launch_combine(cp, st);
+    FLCK(cudaMemcpyAsync(c->h_h, c->h, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+    FLCK(cudaStreamSynchronize(st));
+    out->h = c->h_h;
+}
+
+void fl_moe_outs(FLCtx* c, int b, const int* ids, const float* w, int KE, float* out) {
+    if (!c || !ids || !w || !out || b < 0 || b >= c->last_n || KE != c->last_ke) { fl_fail(c, LK_ERR_ARG, "fl_moe_outs: no matching narrow pass"); return; }
+    std::vector<float> rows((size_t)KE * HIDDEN);
+    FLCK(cudaStreamSynchronize(c->st));
+    FLCK(cudaMemcpy(rows.data(), c->y + (size_t)b * KE * HIDDEN, rows.size() * 4, cudaMemcpyDeviceToHost));
+    for (int k = 0; k < KE; ++k) {
+        int src = -1;
+        for (int j = 0; j < KE; ++j) if (c->last_ids[b * KE + j] == ids[k]) { src = j; break; }
+        const float lw = src >= 0 ? c->last_w[b * KE + src] : 0.f;
+        for (int e = 0; e < HIDDEN; ++e)
+            out[(size_t)k * HIDDEN + e] = (src >= 0 && lw != 0.f) ? rows[(size_t)src * HIDDEN + e] / lw * w[k] : 0.f;
+    }
+}
+
+int fl_wide_init(FLCtx* c, int wmax, int KE) {
+    if (!c || wmax < 1 || KE < 1 || KE > MAX_TOPK) return 0;
+    c->wmax = wmax; c->wke = KE;
+    const size_t R = (size_t)wmax * HIDDEN;
+    const size_t ent = (size_t)wmax * KE;
+    if (dz(&c->ncur_all, R) || dz(&c->base_all, R) || dz(&c->out_all, ent * HIDDEN) || dz(&c->whq, ent * MOE_INTER) ||
+        dz(&c->whd, ent * (MOE_INTER / 32)) || hz(&c->h_wh, R) || hz(&c->h_wmoe, R)) { fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0; }
+    for (int p = 0; p < 2; ++p) {
+        if (dz(&c->w_expert[p], WIDE_SLOTS) || dz(&c->w_tok[p], WIDE_SLOTS * NB) || dz(&c->w_out[p], WIDE_SLOTS * NB) ||
+            dz(&c->w_w[p], WIDE_SLOTS * NB) || dz(&c->w_n[p], 1) || hz(&c->hw_tab[p], WIDE_SLOTS * (1 + 2 * NB) + 1) ||
+            hz(&c->hw_w[p], WIDE_SLOTS * NB) || cudaEventCreateWithFlags(&c->wev[p], cudaEventDisableTiming)) {
+            fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0;
+        }
+    }
+    return 1;
+}
+
+void fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int nexp, const int* midx, const int* rows,
+                 const int* kidx, const float* wk, int nslots, int KE, int par) {
+    if (!c || !c->ncur_all) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: fl_wide_init first"); return; }
+    if (down_fmt != FL_IQ2) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_wide_moe: down format must be FL_IQ2 in this build"); return; }
+    if (KE != c->wke || nslots < 0 || nexp < 1) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: bad argument"); return; }
+    if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: arena not 16-byte aligned"); return; }
+    par &= 1;
+    cudaStream_t st = c->st;
+    const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)EXPERT_DOWN_BYTES;
+    for (int s0 = 0; s0 < nslots; s0 += WIDE_SLOTS) {
+        const int ns = std::min(WIDE_SLOTS, nslots - s0);
+        if (s0 > 0) FLCK(cudaStreamSynchronize(st));          // the tables of this parity are reused
+        int* he = c->hw_tab[par]; int* ht = he + WIDE_SLOTS; int* ho = ht + WIDE_SLOTS * NB; float* hw = c->hw_w[par];
+        for (int s = 0; s < ns; ++s) {
+            const int m = midx[s0 + s];
+            if (m < 0 || m >= nexp) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: slot expert out of range"); return; }
+            he[s] = m;
+            for (int i = 0; i < NB; ++i) {
+                const int r = rows[(size_t)(s0 + s) * NB + i], k = kidx[(size_t)(s0 + s) * NB + i];
+                const bool live = r >= 0 && r < c->wmax && k >= 0 && k < KE;
+                ht[s * NB + i] = live ? r : -1; ho[s * NB + i] = live ? r * KE + k : -1; hw[s * NB + i] = live ? wk[(size_t)(s0 + s) * NB + i] : 0.f;
+            }
+        }
+        ho[ns * NB] = ns;
+        FLCK(cudaMemcpyAsync(c->w_expert[par], he, ns * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_tok[par], ht, (size_t)ns * NB * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_out[par], ho, (size_t)ns * NB * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_w[par], hw, (size_t)ns * NB * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_n[par], ho + ns * NB, 4, cudaMemcpyHostToDevice, st));
+        ExpertParams e = expert_params(c, gate, up, down, sg, sd, c->ncur_all, c->w_expert[par], c->w_tok[par], c->w_out[par],
+                                       c->w_w[par], c->w_n[par], c->whq, c->whd, c->out_all);
+        launch_gate_up(e, NB, c->nsm, st);
+        launch_down(e, NB, c->nsm, st);
+    }
+    FLCK(cudaGetLastError());
+}
+
+void fl_wide_mark(FLCtx* c, int par) { if (c && c->wev[par & 1]) FLCK(cudaEventRecord(c->wev[par & 1], c->st)); }
+void fl_wide_wait(FLCtx* c, int par) { if (c && c->wev[par & 1]) FLCK(cudaEventSynchronize(c->wev[par & 1])); }
+
+void fl_wide_finish(FLCtx* c, int n, int KE, FLOut* out) {
+    if (!c || !out) return;
+    std::memset(out, 0, sizeof(FLOut));
+    if (!c->ncur_all || n < 1 || n > c->wmax || KE != c->wke) { fl_fail(c, LK_ERR_ARG, "fl_wide_finish: bad argument"); return; }
+    cudaStream_t st = c->st;
+    // moe goes to ncur_all (free after the pass), h to a fresh pass over base_all into the pinned mirror
+    CombineParams cp{};
+    cp.y = c->out_all; cp.resid = c->base_all; cp.T = n; cp.keep = KE; cp.with_shared = 0; cp.shared = nullptr;
+    cp.h = c->ncur_all; cp.moe = nullptr; cp.ld_out = HIDDEN;
+    float* hbuf = nullptr;
+    FLCK(cudaMalloc(&hbuf, (size_t)n * HIDDEN * 4 * 2));
+    cp.h = hbuf; cp.moe = hbuf + (size_t)n * HIDDEN;
+    launch_combine(cp, st);
+    FLCK(cudaMemcpyAsync(c->h_wh, hbuf, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+    FLCK(cudaMemcpyAsync(c->h_wmoe, hbuf + (size_t)n * HIDDEN, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+    FLCK(cudaStreamSynchronize(st));
+    cudaFree(hbuf);
+    check_dev(c);
+    out->h = c->h_wh; out->moe = c->h_wmoe;
+}
+
+void fl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
+    if (!c || !out || !mo || !c->ncur_all || n < 1 || n > c->wmax) return;
+    std::memset(out, 0, sizeof(FLOut));
+    cudaStream_t st = c->st;
+    float* dmo = nullptr;
+    FLCK(cudaMalloc(&dmo, (size_t)n * HIDDEN * 4 * 2));
+    FLCK(cudaMemcpyAsync(dmo, mo, (size_t)n * HIDDEN * 4, cudaMemcpyHostToDevice, st));
+    CombineParams cp{};
+    cp.y = dmo; cp.resid = c->base_all; cp.T = n; cp.keep = 1; cp.with_shared = 0; cp.shared = nullptr;
+    cp.h = dmo + (size_t)n * HIDDEN; cp.moe = nullptr; cp.ld_out = HIDDEN;
+    launch_combine(cp, st);
+    FLCK(cudaMemcpyAsync(c->h_wh, dmo + (size_t)n * HIDDEN, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+    FLCK(cudaStreamSynchronize(st));
+    cudaFree(dmo);
+    out->h = c->h_wh;
+}
+
+void fl_wide_outs(FLCtx* c, int row, int KE, float* out) {
+    if (!c || !out || !c->out_all || row < 0 || row >= c->wmax || KE != c->wke) { fl_fail(c, LK_ERR_ARG, "fl_wide_outs: bad argument"); return; }
+    FLCK(cudaStreamSynchronize(c->st));
+    FLCK(cudaMemcpy(out, c->out_all + (size_t)row * KE * HIDDEN, (size_t)KE * HIDDEN * 4, cudaMemcpyDeviceToHost));
+}
+
+}  // extern "C"

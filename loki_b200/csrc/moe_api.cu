@@ -1,0 +1,243 @@
+// moe_api.cu -- the lk_* C ABI (include/loki_moe.h): context, scratch buffers and the launch sequence
+// of one MoE layer: router -> (dispatch) -> gate/up + SwiGLU -> down -> combine, all on the caller's
+// stream, no host synchronisation.
+#include <cstdio>
+#include <cstring>
+#include <cstdarg>
+#include <string>
+#include <algorithm>
+#include "../../include/loki_moe.h"
+#include "moe_internal.h"
+
+using namespace lk;
+
+struct LkMoeCtx {
+    LkMoeConfig cfg;
+    int device = 0, nsm = 0;
+    // scratch (device)
+    float* logits = nullptr; float* probs = nullptr; int* sel = nullptr; float* w = nullptr;
+    int* counts = nullptr; int* offsets = nullptr; int* perm = nullptr;
+    int* slot_expert = nullptr; int* slot_tok = nullptr; int* slot_out = nullptr; float* slot_w = nullptr;
+    int* nslots = nullptr; int max_slots = 0;
+    int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
+    int* err = nullptr;
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    char msg[256] = {0};
+};
+
+static int set_err(LkMoeCtx* c, int code, const char* fmt, ...) {
+    if (c) { va_list ap; va_start(ap, fmt); vsnprintf(c->msg, sizeof(c->msg), fmt, ap); va_end(ap); }
+    return code;
+}
+
+#define LK_CU(call) do { cudaError_t e_ = (call); if (e_ != cudaSuccess) \
+    return set_err(c, LK_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); } while (0)
+
+template <class T> static cudaError_t dalloc(T** p, size_t n) { return cudaMalloc((void**)p, (n ? n : 1) * sizeof(T)); }
+
+static int slot_nt(int T) { return T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8; }
+
+extern "C" {
+
+const char* lk_moe_strerror(int code) {
+    switch (code) {
+        case LK_OK: return "ok";
+        case LK_ERR_ARG: return "bad argument";
+        case LK_ERR_CUDA: return "CUDA error";
+        case LK_ERR_UNSUPPORTED: return "unsupported configuration";
+        case LK_ERR_CAPACITY: return "token count above context capacity";
+        case LK_ERR_DEVICE: return "device-side error (bounded wait expired or bad slot)";
+        default: return "unknown";
+    }
+}
+
+const char* lk_moe_last_error(LkMoeCtx* c) { return c ? c->msg : "null context"; }
+
+int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
+    LkMoeCtx* c = nullptr;
+    if (!cfg || !out) return LK_ERR_ARG;
+    *out = nullptr;
+    if (cfg->n_experts != N_EXPERTS || cfg->topk < 1 || cfg->topk > MAX_TOPK || cfg->keep < 1 || cfg->keep > cfg->topk ||
+        cfg->max_tokens < 1 || !(cfg->n_group == 1 || (cfg->n_group * 32 == cfg->n_experts && cfg->topk_group >= 1 &&
+        cfg->topk_group <= cfg->n_group)))
+        return LK_ERR_UNSUPPORTED;
+    c = new LkMoeCtx();
+    c->cfg = *cfg; c->device = device;
+    int prev = 0; cudaGetDevice(&prev);
+    LK_CU(cudaSetDevice(device));
+    c->nsm = num_sms(device);
+    const int T = cfg->max_tokens, NE = cfg->n_experts, KE = cfg->keep;
+    const size_t rows = (size_t)T * KE + (cfg->with_shared ? T : 0);
+    c->max_slots = 0;
+    for (int nt = 1; nt <= MAX_NT; nt *= 2) c->max_slots = std::max(c->max_slots, max_slots_for(T, KE, NE, nt, cfg->with_shared));
+    LK_CU(dalloc(&c->logits, (size_t)T * NE)); LK_CU(dalloc(&c->probs, (size_t)T * NE));
+    LK_CU(dalloc(&c->sel, (size_t)T * KE)); LK_CU(dalloc(&c->w, (size_t)T * KE));
+    LK_CU(dalloc(&c->counts, NE)); LK_CU(dalloc(&c->offsets, NE + 1)); LK_CU(dalloc(&c->perm, (size_t)T * KE));
+    LK_CU(dalloc(&c->slot_expert, c->max_slots)); LK_CU(dalloc(&c->slot_tok, (size_t)c->max_slots * MAX_NT));
+    LK_CU(dalloc(&c->slot_out, (size_t)c->max_slots * MAX_NT)); LK_CU(dalloc(&c->slot_w, (size_t)c->max_slots * MAX_NT));
+    LK_CU(dalloc(&c->nslots, 1));
+    LK_CU(dalloc(&c->hq, rows * MOE_INTER)); LK_CU(dalloc(&c->hd, rows * (MOE_INTER / 32)));
+    LK_CU(dalloc(&c->y, rows * HIDDEN));
+    LK_CU(dalloc(&c->err, 1));
+    LK_CU(cudaMemset(c->err, 0, sizeof(int)));
+    LK_CU(cudaMemset(c->y, 0, rows * HIDDEN * sizeof(float)));
+    LK_CU(cudaDeviceSynchronize());
+    cudaSetDevice(prev);
+    *out = c;
+    return LK_OK;
+}
+
+void lk_moe_destroy(LkMoeCtx* c) {
+    if (!c) return;
+    void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
+                     c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err };
+    for (void* p : ptrs) if (p) cudaFree(p);
+    delete c;
+}
+
+static int check_weights(LkMoeCtx* c, const LkMoeWeights* W, bool need_router) {
+    if (!W) return set_err(c, LK_ERR_ARG, "null weights");
+    if (W->down_fmt != LK_FMT_IQ2) return set_err(c, LK_ERR_UNSUPPORTED, "down format %d: only IQ2_XXS (4) is implemented", W->down_fmt);
+    const void* mats[] = { W->gate, W->up, W->down };
+    for (const void* m : mats) if (!m || ((uintptr_t)m & 15)) return set_err(c, LK_ERR_ARG, "expert arena null or not 16-byte aligned");
+    if ((W->gate_stride & 15) || (W->up_stride & 15) || (W->down_stride & 15))
+        return set_err(c, LK_ERR_ARG, "expert strides must be multiples of 16 bytes");
+    if (c->cfg.with_shared) {
+        const void* sm[] = { W->sh_gate, W->sh_up, W->sh_down };
+        for (const void* m : sm) if (!m || ((uintptr_t)m & 15)) return set_err(c, LK_ERR_ARG, "shared expert null or not 16-byte aligned");
+    }
+    if (need_router && (!W->router_w || !W->router_bias)) return set_err(c, LK_ERR_ARG, "router weights missing");
+    return LK_OK;
+}
+
+static RouterParams router_params(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int T, const float* logits_override,
+                                  int* sel, float* w, bool decode_slots) {
+    RouterParams p{};
+    p.x = x; p.T = T; p.ld_x = HIDDEN; p.W = W->router_w; p.w_f16 = W->router_w_f16;
+    p.logits_override = logits_override; p.bias = W->router_bias;
+    p.logits = c->logits; p.probs = c->probs; p.sel = sel; p.w = w;
+    p.n_experts = c->cfg.n_experts; p.topk = c->cfg.topk; p.keep = c->cfg.keep; p.renorm = c->cfg.renorm;
+    p.n_group = c->cfg.n_group; p.topk_group = c->cfg.topk_group; p.scale = c->cfg.scale;
+    if (decode_slots) {
+        p.slot_expert = c->slot_expert; p.slot_tok = c->slot_tok; p.slot_out = c->slot_out; p.slot_w = c->slot_w;
+        p.nslots = c->nslots; p.with_shared = c->cfg.with_shared;
+    }
+    return p;
+}
+
+int lk_moe_route(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int T, const float* logits_override,
+                 int* sel, float* w, float* probs, lk_stream_t stream) {
+    if (!c || !x || T < 0) return set_err(c, LK_ERR_ARG, "null argument");
+    if (T == 0) return LK_OK;
+    if (T > c->cfg.max_tokens) return set_err(c, LK_ERR_CAPACITY, "T=%d > capacity %d", T, c->cfg.max_tokens);
+    if (!W || !W->router_w || !W->router_bias) return set_err(c, LK_ERR_ARG, "router weights missing");
+    cudaStream_t st = (cudaStream_t)stream;
+    RouterParams p = router_params(c, W, x, T, logits_override, sel ? sel : c->sel, w ? w : c->w, false);
+    launch_router(p, st);
+    if (probs) LK_CU(cudaMemcpyAsync(probs, c->probs, (size_t)T * c->cfg.n_experts * 4, cudaMemcpyDeviceToDevice, st));
+    LK_CU(cudaGetLastError());
+    return LK_OK;
+}
+
+int lk_moe_dispatch(LkMoeCtx* c, const int* sel, const float* w, int T, int keep, int* counts, int* offsets, int* perm,
+                    lk_stream_t stream) {
+    if (!c || !sel || !w || T < 0 || keep < 1 || keep > MAX_TOPK) return set_err(c, LK_ERR_ARG, "bad argument");
+    if (T > c->cfg.max_tokens || keep > c->cfg.keep) return set_err(c, LK_ERR_CAPACITY, "T=%d keep=%d above capacity", T, keep);
+    SlotParams s{};
+    s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = slot_nt(T);
+    s.with_shared = c->cfg.with_shared;
+    s.counts = counts ? counts : c->counts; s.offsets = offsets ? offsets : c->offsets; s.perm = perm ? perm : c->perm;
+    s.slot_expert = c->slot_expert; s.slot_tok = c->slot_tok; s.slot_out = c->slot_out; s.slot_w = c->slot_w;
+    s.nslots = c->nslots; s.max_slots = c->max_slots;
+    launch_build_slots(s, (cudaStream_t)stream);
+    LK_CU(cudaGetLastError());
+    return LK_OK;
+}
+
+// experts for routing already in c->slot_* (built by the router for T == 1, or by the dispatch kernel)
+static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, int keep,
+                       float* h, float* moe, int nt, cudaStream_t st) {
+    ExpertParams e{};
+    e.gate = (const uint8_t*)W->gate; e.up = (const uint8_t*)W->up; e.down = (const uint8_t*)W->down;
+    e.gate_stride = W->gate_stride; e.up_stride = W->up_stride; e.down_stride = W->down_stride;
+    e.sh_gate = (const uint8_t*)W->sh_gate; e.sh_up = (const uint8_t*)W->sh_up; e.sh_down = (const uint8_t*)W->sh_down;
+    e.x = x; e.ld_x = HIDDEN;
+    e.slot_expert = c->slot_expert; e.slot_tok = c->slot_tok; e.slot_out = c->slot_out; e.slot_w = c->slot_w; e.nslots = c->nslots;
+    e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err;
+    if (c->ev[0]) LK_CU(cudaEventRecord(c->ev[0], st));
+    launch_gate_up(e, nt, c->nsm, st);
+    if (c->ev[1]) LK_CU(cudaEventRecord(c->ev[1], st));
+    launch_down(e, nt, c->nsm, st);
+    if (c->ev[2]) LK_CU(cudaEventRecord(c->ev[2], st));
+    CombineParams cp{};
+    cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared;
+    cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN;
+    if (h || moe) {
+        if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
+        launch_combine(cp, st);
+    }
+    if (c->ev[3]) LK_CU(cudaEventRecord(c->ev[3], st));
+    LK_CU(cudaGetLastError());
+    return LK_OK;
+}
+
+int lk_moe_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, const int* sel,
+                   const float* w, int keep, float* h, float* moe, lk_stream_t stream) {
+    if (!c || !x || !sel || !w || T < 0 || keep < 1) return set_err(c, LK_ERR_ARG, "bad argument");
+    if (T == 0) return LK_OK;
+    int rc = check_weights(c, W, false);
+    if (rc) return rc;
+    if (T > c->cfg.max_tokens || keep > c->cfg.keep) return set_err(c, LK_ERR_CAPACITY, "T=%d keep=%d above capacity", T, keep);
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = lk_moe_dispatch(c, sel, w, T, keep, nullptr, nullptr, nullptr, stream);
+    if (rc) return rc;
+    return run_experts(c, W, x, resid, T, keep, h, moe, slot_nt(T), st);
+}
+
+int lk_moe_forward(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T,
+                   const float* logits_override, float* h, float* moe, int* sel, float* w, lk_stream_t stream) {
+    if (!c || !x || T < 0) return set_err(c, LK_ERR_ARG, "bad argument");
+    if (T == 0) return LK_OK;
+    int rc = check_weights(c, W, true);
+    if (rc) return rc;
+    if (T > c->cfg.max_tokens) return set_err(c, LK_ERR_CAPACITY, "T=%d > capacity %d", T, c->cfg.max_tokens);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int keep = c->cfg.keep;
+    RouterParams p = router_params(c, W, x, T, logits_override, c->sel, c->w, T == 1);
+    launch_router(p, st);
+    if (T > 1) {
+        rc = lk_moe_dispatch(c, c->sel, c->w, T, keep, nullptr, nullptr, nullptr, stream);
+        if (rc) return rc;
+    }
+    rc = run_experts(c, W, x, resid, T, keep, h, moe, slot_nt(T), st);
+    if (rc) return rc;
+    if (sel) LK_CU(cudaMemcpyAsync(sel, c->sel, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));
+    if (w) LK_CU(cudaMemcpyAsync(w, c->w, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));
+    return LK_OK;
+}
+
+const float* lk_moe_slot_outputs(LkMoeCtx* c) { return c ? c->y : nullptr; }
+
+int lk_moe_set_events(LkMoeCtx* c, void* const* events) {
+    if (!c) return LK_ERR_ARG;
+    for (int i = 0; i < 4; ++i) c->ev[i] = events ? (cudaEvent_t)events[i] : nullptr;
+    return LK_OK;
+}
+
+int lk_moe_get_error(LkMoeCtx* c, lk_stream_t stream) {
+    if (!c) return LK_ERR_ARG;
+    LK_CU(cudaStreamSynchronize((cudaStream_t)stream));
+    int e = 0;
+    LK_CU(cudaMemcpy(&e, c->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) { cudaMemset(c->err, 0, sizeof(int)); return set_err(c, LK_ERR_DEVICE, "device error code %d", e); }
+    return LK_OK;
+}
+
+int lk_gen_iq2(void* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K, int64_t stride,
+               lk_stream_t stream) {
+    if (!dst || rows < 1 || K < QK || (K % QK) || n_exp < 1) return LK_ERR_ARG;
+    launch_gen_iq2((uint8_t*)dst, seed, layer, matrix, expert0, n_exp, rows, K, stride, (cudaStream_t)stream);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,169 @@
+// moe_format.h -- formats, shapes and bit-exact helpers shared by the CUDA kernels and the CPU oracle.
+//
+// Everything here is plain C++ that compiles for the host and, under nvcc, for the device
+// (LK_HD = __host__ __device__), so the oracle and the kernels evaluate the same operations in the
+// same order:
+//   * IQ2_XXS block layout (GGUF / ggml format, 66 bytes per 256 weights),
+//   * the seeded counter-based IQ2_XXS weight generator (identical bytes on CPU and GPU),
+//   * software fp32 <-> fp16 conversion (round to nearest even),
+//   * lk_expf: an exp restated from its mathematics (Cody-Waite reduction + Taylor polynomial),
+//     used for the router sigmoid and SwiGLU on both sides,
+//   * q8-per-32 activation quantisation of one 32-element group.
+#pragma once
+#include <stdint.h>
+#include <string.h>
+#include <math.h>
+
+#if defined(__CUDACC__)
+#define LK_HD __host__ __device__ __forceinline__
+#else
+#define LK_HD inline
+#endif
+
+namespace lk {
+
+// ---- DeepSeek-R1 MoE layer shapes (the reference's fused_layer.cu:18 constants E, HSH, QK)
+constexpr int HIDDEN = 7168;        // E: model width, K of gate/up, rows of down
+constexpr int MOE_INTER = 2048;     // HSH: expert intermediate width, rows of gate/up, K of down
+constexpr int N_EXPERTS = 256;      // routed experts per layer
+constexpr int MAX_TOPK = 8;         // router keeps up to 8 (the engine's KE <= 8)
+constexpr int QK = 256;             // weights per IQ2_XXS superblock
+constexpr int BLK_IQ2 = 66;         // bytes per IQ2_XXS superblock: fp16 d + 8 x (4 grid idx, u32 aux)
+
+// ---- IQ2_XXS sizes (ggml_row_size(IQ2_XXS, K) = K/256*66)
+LK_HD constexpr size_t iq2_row_bytes(int K) { return (size_t)(K / QK) * BLK_IQ2; }
+LK_HD constexpr size_t iq2_matrix_bytes(int rows, int K) { return (size_t)rows * iq2_row_bytes(K); }
+// one expert's gate (or up) = [MOE_INTER rows][HIDDEN]; down = [HIDDEN rows][MOE_INTER]; both 3 784 704 B
+constexpr size_t EXPERT_GU_BYTES = (size_t)MOE_INTER * (HIDDEN / QK) * BLK_IQ2;
+constexpr size_t EXPERT_DOWN_BYTES = (size_t)HIDDEN * (MOE_INTER / QK) * BLK_IQ2;
+
+// ---- format ids, numerically equal to the reference's FL_IQ2 / FL_Q2K / FL_Q3K
+enum { FMT_IQ2 = 4, FMT_Q2K = 5, FMT_Q3K = 6 };
+
+// ---- fp16 <-> fp32 in software (IEEE binary16, round to nearest even), identical on host and device
+LK_HD uint32_t f32_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+LK_HD float bits_f32(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+LK_HD float half_to_float(uint16_t h) {
+    const uint32_t s = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1Fu, m = h & 0x3FFu;
+    if (e == 0) {                                   // zero / subnormal: m * 2^-24, exact in fp32
+        const float v = (float)m * 5.9604644775390625e-08f;
+        return s ? -v : v;
+    }
+    if (e == 31) return bits_f32(s | 0x7F800000u | (m << 13));
+    return bits_f32(s | ((e + 112u) << 23) | (m << 13));
+}
+
+LK_HD uint16_t float_to_half_rne(float f) {
+    const uint32_t x = f32_bits(f), s = (x >> 16) & 0x8000u;
+    const uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) return (uint16_t)(s | 0x7C00u | (ax > 0x7F800000u ? 0x200u : 0u));
+    if (ax >= 0x477FF000u) return (uint16_t)(s | 0x7C00u);          // rounds to >= 65520: inf
+    if (ax < 0x38800000u) {                                         // result subnormal (or zero)
+        if (ax < 0x33000000u) return (uint16_t)s;                   // < 2^-25: rounds to 0
+        const uint32_t e = ax >> 23, m = (ax & 0x7FFFFFu) | 0x800000u;
+        const uint32_t shift = 126u - e;                            // 14..24 (value = m * 2^(e-150), unit 2^-24)
+        uint32_t q = m >> shift; const uint32_t rem = m & ((1u << shift) - 1u), half = 1u << (shift - 1u);
+        if (rem > half || (rem == half && (q & 1u))) ++q;
+        return (uint16_t)(s | q);
+    }
+    uint32_t q = ((ax >> 13) - (112u << 10));                       // rebias exponent, keep 10 mantissa bits
+    const uint32_t rem = ax & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) ++q;        // carry into the exponent is correct
+    return (uint16_t)(s | q);
+}
+
+// ---- exp(x) for fp32, restated from its mathematics, bit-identical on CPU and GPU.
+//  n = rint(x / ln2); r = x - n*ln2 with ln2 split into a short high part (exact product) and a low
+//  correction (Cody & Waite 1980); exp(r) on |r| <= ln2/2 by the degree-7 Taylor series in Horner form
+//  (truncation < 6e-9 relative); scale by 2^n through the exponent field.  Only fmaf, mul, add and
+//  integer ops are used, each correctly rounded, so every platform returns the same bits.
+//  x is clamped to [-86, 88] so 2^n stays a normal float (exp(-86) ~ 4e-38, exp(88) ~ 1.7e38).
+LK_HD float lk_expf(float x) {
+    x = x < -86.0f ? -86.0f : (x > 88.0f ? 88.0f : x);
+    const float LOG2E = 1.44269504088896341f;
+    const float LN2_HI = 0.693145751953125f;          // 0x3F317200: 16 significant bits, n*LN2_HI exact
+    const float LN2_LO = 1.42860676533018740e-06f;    // ln2 - LN2_HI
+    const float n = rintf(x * LOG2E);
+    float r = fmaf(-n, LN2_HI, x);
+    r = fmaf(-n, LN2_LO, r);
+    float p = 1.0f / 5040.0f;
+    p = fmaf(p, r, 1.0f / 720.0f);
+    p = fmaf(p, r, 1.0f / 120.0f);
+    p = fmaf(p, r, 1.0f / 24.0f);
+    p = fmaf(p, r, 1.0f / 6.0f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ni = (int)n;
+    return p * bits_f32((uint32_t)(ni + 127) << 23);
+}
+
+// sigmoid as the router uses it: 1 / (1 + exp(-v)) (fused_layer.cu:321), with lk_expf.
+LK_HD float lk_sigmoid(float v) { return 1.0f / (1.0f + lk_expf(-v)); }
+// silu(g) * u as SwiGLU uses it: g / (1 + exp(-g)) * u (fused_layer.cu:337), with lk_expf.
+LK_HD float lk_swiglu(float g, float u) { return g / (1.0f + lk_expf(-g)) * u; }
+
+// ---- q8 per 32 (fused_layer.cu:40-47): d = amax/127, q = round-half-even(x / d) via x * (1/d)
+//  Returns d; q[0..32) receive the int8 values.  Round-half-even is rintf under the default rounding
+//  mode on the host and __float2int_rn on the device; both are exact functions of (x*id).
+LK_HD float quant_q8_group(const float* x, int8_t* q) {
+    float amax = 0.0f;
+    for (int j = 0; j < 32; ++j) { const float a = fabsf(x[j]); amax = amax > a ? amax : a; }
+    const float d = amax / 127.0f, id = d > 0.0f ? 1.0f / d : 0.0f;
+    for (int j = 0; j < 32; ++j) q[j] = (int8_t)(int)rintf(x[j] * id);
+    return d;
+}
+
+// ---- IQ2_XXS group helpers.  A 66-byte block = fp16 d, then 8 groups of 8 bytes; group s of a block =
+//  bytes [2+8s, 10+8s): aux0 (4 grid indices, one per 8-weight sub-group) and aux1 (4 x 7-bit sign
+//  indices in bits 0..27, 4-bit scale in bits 28..31).  Weight value = d * (0.5 + scale) * 0.25 *
+//  grid[idx][j] * sign, sign bits = ksigns(sign index) (gguf-py IQ2_XXS.dequantize_blocks; the
+//  reference's iq2_unpack4, fused_layer.cu:30-33, and its scale, :191).
+LK_HD uint32_t iq2_ksigns(uint32_t i7) {           // 7 stored sign bits + even-parity bit 7
+    uint32_t p = i7 ^ (i7 >> 4); p ^= p >> 2; p ^= p >> 1;
+    return i7 | ((p & 1u) << 7);
+}
+
+// ---- seeded synthetic IQ2_XXS weights (counter-based; the same bytes on CPU and GPU)
+//  key chain: seed -> layer -> matrix (0 gate, 1 up, 2 down) -> expert (256 = shared expert);
+//  block b of the matrix (b = row * (K/256) + column block): 8 x splitmix64 draws give the 8 groups'
+//  64 bits verbatim (every bit pattern is a valid grid index / sign index / scale: uniform fields),
+//  3 more draws give 12 x 16-bit uniforms whose Irwin-Hall sum approximates N(0,1); d = fp16(|N|*1e-3).
+LK_HD uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+LK_HD uint64_t iq2_gen_key(uint64_t seed, uint32_t layer, uint32_t matrix, uint32_t expert) {
+    uint64_t h = splitmix64(seed);
+    h = splitmix64(h ^ (uint64_t)layer);
+    h = splitmix64(h ^ ((uint64_t)matrix << 32));
+    return splitmix64(h ^ ((uint64_t)expert << 16));
+}
+LK_HD uint16_t iq2_gen_d(uint64_t key, uint64_t block) {
+    int32_t s = 0;
+    for (int w = 0; w < 3; ++w) {
+        const uint64_t r = splitmix64(key ^ (block * 16ull + 8ull + (uint64_t)w));
+        for (int j = 0; j < 4; ++j) s += (int32_t)((r >> (16 * j)) & 0xFFFFull);
+    }
+    const int32_t c = 2 * s - 12 * 65535;            // 2 * (sum - 12 * 65535/2): exact integer
+    const float n = (float)c * (1.0f / 131072.0f);   // / 2^17: unit-variance Irwin-Hall(12), exact
+    const float a = fabsf(n) * 1.0e-3f;
+    return float_to_half_rne(a);
+}
+LK_HD uint64_t iq2_gen_group(uint64_t key, uint64_t block, int g) {
+    return splitmix64(key ^ (block * 16ull + (uint64_t)g));
+}
+// write block `block` (66 bytes) of the matrix identified by key
+LK_HD void iq2_gen_block(uint64_t key, uint64_t block, uint8_t* out) {
+    const uint16_t d = iq2_gen_d(key, block);
+    out[0] = (uint8_t)(d & 0xFF); out[1] = (uint8_t)(d >> 8);
+    for (int g = 0; g < 8; ++g) {
+        const uint64_t v = iq2_gen_group(key, block, g);
+        for (int j = 0; j < 8; ++j) out[2 + 8 * g + j] = (uint8_t)(v >> (8 * j));
+    }
+}
+
+}  // namespace lk

@@ -1,0 +1,69 @@
+// moe_internal.h -- kernel parameter blocks and launchers shared by the library's translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "moe_format.h"
+
+namespace lk {
+
+constexpr int SHARED_SLOT = -1;      // slot_expert value of the shared expert
+constexpr int MAX_NT = 8;            // tokens per work slot of the grouped matvecs
+
+// ---- router
+struct RouterParams {
+    const float* x; int T; int ld_x;        // activations [T][HIDDEN], row stride ld_x floats
+    const void* W; int w_f16;               // router weights [n_experts][HIDDEN], fp32 or fp16
+    const float* logits_override;           // optional [T][n_experts]: selection from these logits instead
+    const float* bias;                      // e_score_correction bias [n_experts]
+    float* logits;                          // [T][n_experts] out (the GEMV result)
+    float* probs;                           // [T][n_experts] out: sigmoid of the logits used for selection
+    int* sel; float* w;                     // [T][keep] out
+    int n_experts, topk, keep, renorm, n_group, topk_group; float scale;
+    // optional slot table written directly for T == 1 (decode): keep routed slots + shared slot
+    int* slot_expert; int* slot_tok; int* slot_out; float* slot_w; int* nslots; int with_shared;
+};
+void launch_router(const RouterParams& p, cudaStream_t st);
+
+// ---- dispatch: per-expert stable token lists and the work-slot table of the grouped matvecs
+struct SlotParams {
+    const int* sel; const float* w; int T; int keep;   // [T][keep]
+    int n_experts; int nt;                              // tokens per slot (<= MAX_NT)
+    int with_shared;
+    int* counts; int* offsets; int* perm;               // [n_experts], [n_experts+1], [T*keep]
+    int* slot_expert; int* slot_tok; int* slot_out; float* slot_w; int* nslots;   // slot tables
+    int max_slots;
+};
+void launch_build_slots(const SlotParams& p, cudaStream_t st);
+int max_slots_for(int T, int keep, int n_experts, int nt, int with_shared);
+
+// ---- grouped IQ2_XXS matvecs on work slots
+struct ExpertParams {
+    // arenas: routed expert e's matrices at base + e*stride; the shared expert's at sh_*
+    const uint8_t* gate; const uint8_t* up; const uint8_t* down;
+    int64_t gate_stride, up_stride, down_stride;
+    const uint8_t* sh_gate; const uint8_t* sh_up; const uint8_t* sh_down;
+    const float* x; int ld_x;                         // activations [T][HIDDEN] (fp32; quantised to q8 in-kernel)
+    const int* slot_expert; const int* slot_tok; const int* slot_out; const float* slot_w; const int* nslots;
+    int8_t* hq; float* hd;                            // SwiGLU output q8: [rows][MOE_INTER], scales [rows][MOE_INTER/32]
+    float* y;                                         // weighted expert outputs [rows][HIDDEN]
+    int* err;
+};
+void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st);
+void launch_down(const ExpertParams& p, int nt, int grid, cudaStream_t st);
+
+// ---- combine: h = resid + shared + sum_k y[t*keep+k], moe = sum_k y[t*keep+k]
+//      (shared = the y rows T*keep + t when with_shared, and/or the separate `shared` rows)
+struct CombineParams {
+    const float* y; const float* resid; int T; int keep; int with_shared;
+    const float* shared;              // optional [T][HIDDEN] shared-expert output added to h
+    float* h; float* moe; int ld_out;
+};
+void launch_combine(const CombineParams& p, cudaStream_t st);
+
+// ---- seeded IQ2_XXS weight generation (moe_format.h generator) for n_experts consecutive experts
+void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
+                    int64_t stride, cudaStream_t st);
+
+int num_sms(int device);
+
+}  // namespace lk

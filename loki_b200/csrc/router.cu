@@ -1,0 +1,188 @@
+// router.cu -- the DeepSeek-R1 router on sm_100a.
+//
+// k_router_logits: logits[t][e] = W[e] . x[t] (fp32 or fp16 weights), then probs = sigmoid(logits or an
+//   override).  Replaces router_probs (reference src/fused_layer.cu:314-322).  One CTA = 2 experts x a
+//   tile of tokens; 128 threads per expert each own the float4 chunks c = p, p+128, ... of the row
+//   (fmaf over the 4 components in order), then a warp xor-butterfly and (s0+s1)+(s2+s3) across the 4
+//   warps.  The order is fixed and restated by the oracle (orc_router_logits), so probabilities -- and
+//   with them the selected experts -- are bit-identical to it.  Weights are streamed once per token tile.
+// k_router_topk: one warp per token: top-k of p + bias with ties to the lower expert id (reference
+//   router_topk, src/fused_layer.cu:323-332), or the DeepSeek-V3 grouped mode (n_group groups of 32
+//   experts, group score = sum of the group's top-2, keep topk_group groups); weights p/max(sum, 2^-14)
+//   * scale; then the engine's keep-KE compaction (src/server_core_fused.cpp:793-813: order by weight,
+//   keep KE, rescale the kept weights to sum to `scale`).  For T == 1 it also writes the decode slot
+//   table (one slot per kept expert + the shared expert), so no dispatch kernel is needed at decode.
+#include "moe_internal.h"
+#include "moe_device.cuh"
+#include <cuda_fp16.h>
+
+namespace lk {
+
+template <int NTT>
+__global__ void __launch_bounds__(256) k_router_logits(RouterParams p) {
+    __shared__ float ws[2][4][NTT];
+    const int half = threadIdx.x >> 7, q = threadIdx.x & 127, warp = q >> 5, lane = q & 31;
+    const int e = blockIdx.x * 2 + half;
+    const int t0 = blockIdx.y * NTT;
+    const int nt = min(NTT, p.T - t0);
+    constexpr int NCH = HIDDEN / 4;                 // 1792 float4 chunks
+    float acc[NTT];
+    #pragma unroll
+    for (int t = 0; t < NTT; ++t) acc[t] = 0.0f;
+    if (e < p.n_experts) {
+        #pragma unroll 7
+        for (int c = q; c < NCH; c += 128) {
+            float4 w;
+            if (p.w_f16) {
+                const uint2 raw = __ldg((const uint2*)((const __half*)p.W + (size_t)e * HIDDEN) + c);
+                const float2 a = __half22float2(*(const __half2*)&raw.x), b = __half22float2(*(const __half2*)&raw.y);
+                w = make_float4(a.x, a.y, b.x, b.y);
+            } else {
+                w = __ldg((const float4*)((const float*)p.W + (size_t)e * HIDDEN) + c);
+            }
+            #pragma unroll
+            for (int t = 0; t < NTT; ++t) {
+                if (t < nt) {
+                    const float4 xv = *((const float4*)(p.x + (size_t)(t0 + t) * p.ld_x) + c);
+                    acc[t] = fmaf(w.x, xv.x, acc[t]);
+                    acc[t] = fmaf(w.y, xv.y, acc[t]);
+                    acc[t] = fmaf(w.z, xv.z, acc[t]);
+                    acc[t] = fmaf(w.w, xv.w, acc[t]);
+                }
+            }
+        }
+    }
+    #pragma unroll
+    for (int t = 0; t < NTT; ++t) {
+        float a = acc[t];
+        #pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane == 0) ws[half][warp][t] = a;
+    }
+    __syncthreads();
+    if (q < nt && e < p.n_experts) {
+        const int t = q;
+        const float lg = __fadd_rn(__fadd_rn(ws[half][0][t], ws[half][1][t]), __fadd_rn(ws[half][2][t], ws[half][3][t]));
+        const size_t o = (size_t)(t0 + t) * p.n_experts + e;
+        p.logits[o] = lg;
+        const float v = p.logits_override ? p.logits_override[o] : lg;
+        p.probs[o] = lk_sigmoid(v);
+    }
+}
+
+// warp argmax over (value, index) pairs, ties -> lower index; every lane returns the winner
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+    }
+}
+
+__global__ void __launch_bounds__(256) k_router_topk(RouterParams p) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= p.T) return;
+    const float* pr = p.probs + (size_t)t * p.n_experts;
+    constexpr int PER = N_EXPERTS / 32;             // 8 experts per lane: e = lane + 32*i
+    float sc[PER], pv[PER];
+    bool allowed[PER];
+    #pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const int e = lane + 32 * i;
+        pv[i] = pr[e];
+        sc[i] = __fadd_rn(pv[i], p.bias[e]);
+        allowed[i] = true;
+    }
+    if (p.n_group > 1) {                            // n_group == 8 groups of 32: group g = register i
+        float gs[PER];
+        #pragma unroll
+        for (int g = 0; g < PER; ++g) {
+            float v1 = sc[g]; int i1 = lane + 32 * g;
+            warp_argmax(v1, i1);
+            float v2 = (lane + 32 * g == i1) ? -INFINITY : sc[g]; int i2 = (lane + 32 * g == i1) ? 0x7fffffff : lane + 32 * g;
+            warp_argmax(v2, i2);
+            gs[g] = __fadd_rn(v1, v2);
+        }
+        bool keepg[PER];
+        #pragma unroll
+        for (int g = 0; g < PER; ++g) keepg[g] = false;
+        for (int r = 0; r < p.topk_group; ++r) {
+            int bg = -1; float bv = 0.0f;
+            #pragma unroll
+            for (int g = 0; g < PER; ++g) if (!keepg[g] && (bg < 0 || gs[g] > bv)) { bg = g; bv = gs[g]; }
+            #pragma unroll
+            for (int g = 0; g < PER; ++g) if (g == bg) keepg[g] = true;
+        }
+        #pragma unroll
+        for (int i = 0; i < PER; ++i) allowed[i] = keepg[i];
+    }
+    int sel[MAX_TOPK]; float ps[MAX_TOPK];
+    for (int k = 0; k < p.topk; ++k) {
+        float bv = -INFINITY; int bi = 0x7fffffff;
+        #pragma unroll
+        for (int i = 0; i < PER; ++i)
+            if (allowed[i] && (bi == 0x7fffffff || sc[i] > bv)) { bv = sc[i]; bi = lane + 32 * i; }
+        warp_argmax(bv, bi);
+        sel[k] = bi;
+        #pragma unroll
+        for (int i = 0; i < PER; ++i) if (lane + 32 * i == bi) allowed[i] = false;
+        ps[k] = pr[bi];
+    }
+    float sum = 0.0f;
+    for (int k = 0; k < p.topk; ++k) sum = __fadd_rn(sum, ps[k]);
+    sum = fmaxf(sum, 6.103515625e-5f);
+    float wt[MAX_TOPK];
+    for (int k = 0; k < p.topk; ++k) wt[k] = __fmul_rn(__fdiv_rn(ps[k], sum), p.scale);
+    int osel[MAX_TOPK]; float ow[MAX_TOPK];
+    const int keep = p.keep;
+    if (keep >= p.topk) {
+        for (int k = 0; k < p.topk; ++k) { osel[k] = sel[k]; ow[k] = wt[k]; }
+    } else {
+        int ord[MAX_TOPK];
+        for (int k = 0; k < p.topk; ++k) ord[k] = k;
+        for (int a = 1; a < p.topk; ++a) {          // stable insertion sort by weight, descending
+            const int v = ord[a]; int b = a - 1;
+            while (b >= 0 && wt[ord[b]] < wt[v]) { ord[b + 1] = ord[b]; --b; }
+            ord[b + 1] = v;
+        }
+        float sw = 0.0f;
+        for (int k = 0; k < keep; ++k) { osel[k] = sel[ord[k]]; ow[k] = wt[ord[k]]; sw = __fadd_rn(sw, ow[k]); }
+        if (p.renorm && sw > 1e-6f) {
+            const float f = __fdiv_rn(p.scale, sw);
+            for (int k = 0; k < keep; ++k) ow[k] = __fmul_rn(ow[k], f);
+        }
+    }
+    if (lane < keep) {
+        int sv = 0; float wv = 0.0f;
+        for (int k = 0; k < MAX_TOPK; ++k) if (k == lane) { sv = osel[k]; wv = ow[k]; }
+        p.sel[(size_t)t * keep + lane] = sv;
+        p.w[(size_t)t * keep + lane] = wv;
+        if (p.slot_expert && p.T == 1) {            // decode slot table, one token per slot
+            p.slot_expert[lane] = sv; p.slot_tok[lane] = 0; p.slot_out[lane] = lane; p.slot_w[lane] = wv;
+        }
+    }
+    if (p.slot_expert && p.T == 1 && lane == 0) {
+        if (p.with_shared) {
+            p.slot_expert[keep] = SHARED_SLOT; p.slot_tok[keep] = 0; p.slot_out[keep] = keep; p.slot_w[keep] = 1.0f;
+        }
+        *p.nslots = keep + (p.with_shared ? 1 : 0);
+    }
+}
+
+void launch_router(const RouterParams& p, cudaStream_t st) {
+    const int pairs = (p.n_experts + 1) / 2;
+    if (p.T <= 1) {
+        k_router_logits<1><<<dim3(pairs, 1), 256, 0, st>>>(p);
+    } else if (p.T <= 2) {
+        k_router_logits<2><<<dim3(pairs, 1), 256, 0, st>>>(p);
+    } else if (p.T <= 4) {
+        k_router_logits<4><<<dim3(pairs, 1), 256, 0, st>>>(p);
+    } else {
+        k_router_logits<8><<<dim3(pairs, (p.T + 7) / 8), 256, 0, st>>>(p);
+    }
+    k_router_topk<<<(p.T + 7) / 8, 256, 0, st>>>(p);
+}
+
+}  // namespace lk

@@ -1,0 +1,168 @@
+"""Python mirror of loki's fused-layer MoE calls (include/loki_fused_moe.h), the engine-facing ABI.
+
+Host arrays in, host arrays out, exactly as server_core_fused.cpp drives src/fused_layer.h: per layer
+fl_moe_prepare (the MoE half of fl_attn) -> fl_fetch(what=1) -> host keep-KE pass -> fl_moe, or for a wide
+(prefill) pass fl_moe_prepare(wrow=...) per group -> fl_wide_moe per arena batch -> fl_wide_finish.
+"""
+import ctypes
+
+import numpy as np
+
+from . import native as N
+from .native import HIDDEN, lib
+
+FL_IQ2 = 4
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _view(addr, n, dtype):
+    if not addr:
+        return None
+    ct = {np.float32: ctypes.c_float, np.int32: ctypes.c_int32}[dtype]
+    return np.ctypeslib.as_array(ctypes.cast(addr, ctypes.POINTER(ct)), shape=(n,))
+
+
+def keep_pass(sel, wts, KE, renorm=True, scale=2.5):
+    """The engine's keep-KE compaction (src/server_core_fused.cpp:793-813) on host arrays [n][8]."""
+    if KE >= sel.shape[1]:
+        return sel.astype(np.int32), wts.astype(np.float32)
+    order = np.argsort(-wts, axis=1, kind="stable")[:, :KE]
+    s = np.take_along_axis(sel, order, 1).astype(np.int32)
+    w = np.take_along_axis(wts, order, 1).astype(np.float32)
+    if renorm:
+        sw = np.zeros(w.shape[0], np.float32)
+        for k in range(KE):
+            sw = (sw + w[:, k]).astype(np.float32)
+        f = np.where(sw > 1e-6, np.float32(scale) / np.where(sw > 1e-6, sw, 1), 1).astype(np.float32)
+        w = (w * f[:, None]).astype(np.float32)
+    return s, w
+
+
+class FusedCtx:
+    def __init__(self, kvp=512, sc_cap=64):
+        self.c = lib().fl_init(kvp, sc_cap)
+        if not self.c:
+            raise N.NativeError("fl_init failed")
+        self.out = N.FLOut()
+
+    def close(self):
+        if self.c:
+            lib().fl_free(self.c)
+            self.c = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def error(self):
+        return lib().fl_moe_error(self.c)
+
+    def prepare(self, mw, ncur, ffn_inp, wrow=-1):
+        ncur = np.ascontiguousarray(ncur, np.float32)
+        ffn_inp = np.ascontiguousarray(ffn_inp, np.float32)
+        lib().fl_moe_prepare(self.c, ctypes.byref(mw), _p(ncur), _p(ffn_inp), ncur.shape[0], 1, wrow)
+
+    def prepare_device(self, mw, ncur_ptr, ffn_ptr, n, wrow=-1):
+        lib().fl_moe_prepare(self.c, ctypes.byref(mw), ctypes.c_void_p(ncur_ptr), ctypes.c_void_p(ffn_ptr), n, 0, wrow)
+
+    def fetch(self, n, what=1):
+        lib().fl_fetch(self.c, n, what, ctypes.byref(self.out))
+        o = self.out
+        r = {}
+        if o.sel:
+            r["sel"] = _view(o.sel, n * 8, np.int32).reshape(n, 8).copy()
+            r["wts"] = _view(o.wts, n * 8, np.float32).reshape(n, 8).copy()
+            r["ncur"] = _view(o.ncur, n * HIDDEN, np.float32).reshape(n, HIDDEN)
+            r["fi"] = _view(o.fi, n * HIDDEN, np.float32).reshape(n, HIDDEN)
+        if o.h:
+            r["h"] = _view(o.h, n * HIDDEN, np.float32).reshape(n, HIDDEN)
+        return r
+
+    def moe(self, gate, up, down, nexp, ids, w, down_fmt=FL_IQ2):
+        ids = np.ascontiguousarray(ids, np.int32)
+        w = np.ascontiguousarray(w, np.float32)
+        n, KE = ids.shape
+        lib().fl_moe(self.c, ctypes.c_void_p(gate), ctypes.c_void_p(up), ctypes.c_void_p(down), nexp, down_fmt, _p(ids), _p(w),
+                     KE, n, ctypes.byref(self.out))
+        o = self.out
+        return (_view(o.h, n * HIDDEN, np.float32).reshape(n, HIDDEN) if o.h else None,
+                _view(o.moe, n * HIDDEN, np.float32).reshape(n, HIDDEN) if o.moe else None)
+
+    def skip(self, mo):
+        mo = np.ascontiguousarray(mo, np.float32)
+        lib().fl_skip(self.c, _p(mo), mo.shape[0], ctypes.byref(self.out))
+        return _view(self.out.h, mo.shape[0] * HIDDEN, np.float32).reshape(-1, HIDDEN) if self.out.h else None
+
+    def moe_outs(self, b, ids, w):
+        ids = np.ascontiguousarray(ids, np.int32)
+        w = np.ascontiguousarray(w, np.float32)
+        out = np.empty((len(ids), HIDDEN), np.float32)
+        lib().fl_moe_outs(self.c, b, _p(ids), _p(w), len(ids), _p(out))
+        return out
+
+    def wide_init(self, wmax, KE):
+        return lib().fl_wide_init(self.c, wmax, KE)
+
+    def wide_moe(self, gate, up, down, nexp, midx, rows, kidx, wk, KE, par, down_fmt=FL_IQ2):
+        midx = np.ascontiguousarray(midx, np.int32)
+        rows = np.ascontiguousarray(rows, np.int32)
+        kidx = np.ascontiguousarray(kidx, np.int32)
+        wk = np.ascontiguousarray(wk, np.float32)
+        lib().fl_wide_moe(self.c, ctypes.c_void_p(gate), ctypes.c_void_p(up), ctypes.c_void_p(down), down_fmt, nexp,
+                          _p(midx), _p(rows), _p(kidx), _p(wk), len(midx), KE, par)
+
+    def wide_mark(self, par):
+        lib().fl_wide_mark(self.c, par)
+
+    def wide_wait(self, par):
+        lib().fl_wide_wait(self.c, par)
+
+    def wide_finish(self, n, KE):
+        lib().fl_wide_finish(self.c, n, KE, ctypes.byref(self.out))
+        o = self.out
+        return (_view(o.h, n * HIDDEN, np.float32).reshape(n, HIDDEN) if o.h else None,
+                _view(o.moe, n * HIDDEN, np.float32).reshape(n, HIDDEN) if o.moe else None)
+
+    def wide_skip(self, mo):
+        mo = np.ascontiguousarray(mo, np.float32)
+        lib().fl_wide_skip(self.c, _p(mo), mo.shape[0], ctypes.byref(self.out))
+        return _view(self.out.h, mo.shape[0] * HIDDEN, np.float32).reshape(-1, HIDDEN) if self.out.h else None
+
+    def wide_outs(self, row, KE):
+        out = np.empty((KE, HIDDEN), np.float32)
+        lib().fl_wide_outs(self.c, row, KE, _p(out))
+        return out
+
+    def gpu_ms(self, which):
+        return lib().fl_gpu_ms(self.c, which)
+
+
+def wide_slots(sel, w, KE, used, eb=16):
+    """The engine's wide-pass batching (src/server_core_fused.cpp:937-946): per arena batch of <= eb experts
+    from `used`, slots of <= 8 (row, k) pairs; returns [(batch_experts, midx, rows, kidx, wk)]."""
+    byexp = {e: [] for e in used}
+    n = sel.shape[0]
+    for i in range(n):
+        for k in range(KE):
+            byexp[int(sel[i, k])].append((i, k))
+    out = []
+    for b0 in range(0, len(used), eb):
+        batch = used[b0:b0 + eb]
+        midx, rows, kidx, wk = [], [], [], []
+        for u, e in enumerate(batch):
+            lst = byexp[e]
+            for i0 in range(0, len(lst), 8):
+                midx.append(u)
+                for j in range(8):
+                    if i0 + j < len(lst):
+                        r, k = lst[i0 + j]
+                        rows.append(r); kidx.append(k); wk.append(w[r, k])
+                    else:
+                        rows.append(-1); kidx.append(0); wk.append(0.0)
+        out.append((batch, midx, rows, kidx, wk))
+    return out

@@ -1,0 +1,327 @@
+// oracle.cpp -- CPU restatement of loki's MoE hot path.  TEST INFRASTRUCTURE ONLY: tests/, the smoke
+// check and bench.py's CPU-baseline leg load it as the checker; the product never links or calls it.
+//
+// Parity anchors (reference = grimnier/loki, paths inside that project):
+//   IQ2_XXS decode ........ src/fused_layer.cu:30-33 (iq2_unpack4), :185-191 (block walk, scale d*(0.5+s)*0.25);
+//                           cross-checked against gguf-py 0.19.0 gguf.quants.IQ2_XXS.dequantize_blocks
+//   q8 activations ........ src/fused_layer.cu:40-47 (quant_x: d = amax/127, q = rint(x/d) half-even)
+//   router ................ src/fused_layer.cu:314-332 (sigmoid(W.x), top-8 of p+bias, ties -> lower id,
+//                           w = p/max(sum p, 2^-14) * 2.5); src/server_core_fused.cpp:646-651 (ggml twin)
+//   grouped top-k ......... not in the reference (the BASELINE's DeepSeek-V3 mode): n_group groups of
+//                           consecutive experts, group score = sum of its top-2 (p+bias), keep topk_group
+//                           groups, top-k inside them
+//   keep-KE + renorm ...... src/server_core_fused.cpp:793-813 (sort by w desc, keep KE, scale to sum 2.5)
+//   SwiGLU + q8 ........... src/fused_layer.cu:334-341 (h = g/(1+exp(-g))*u, re-quantised per 32)
+//   expert products ....... src/fused_layer.cu:178-202 (IQ2 gate/up/down: sum_g fa_g * dx_g * isum_g)
+//   combine ............... src/fused_layer.cu:366-373 and 354-360 (routed = sum_k w_k y_k; h = routed +
+//                           shared + ffn_inp; moe = routed)
+//   permute ............... src/server_core_fused.cpp:937 (byexp: per expert, (row, k) pairs in row-major
+//                           order) -- the per-expert token lists, stable by (token, k)
+//
+// Arithmetic: the router logits follow the GPU kernel's fixed reduction order exactly (see
+// orc_router_logits), and exp is lk_expf from moe_format.h on both sides, so router probabilities,
+// selected ids and weights are bit-identical to the kernels.  Expert products are evaluated in double
+// from the same quantised operands (integer group sums are exact), i.e. the ideal value of the q8
+// scheme; the kernels' fp32 accumulation differs from it by reassociation only.
+#include <cstdint>
+#include <cstring>
+#include <cmath>
+#include <vector>
+#include <algorithm>
+#include "../loki_b200/csrc/moe_format.h"
+
+using namespace lk;
+
+static const uint64_t IQ2_GRID[256] = {
+#include "../loki_b200/csrc/iq2_grid.inc"
+};
+
+extern "C" {
+
+// ------------------------------------------------------------------ formats
+// out[rows*K] = dequantised IQ2_XXS weights (gguf-py dequantize_blocks semantics)
+void orc_iq2_dequant(const uint8_t* blocks, int64_t nblk, float* out) {
+    #pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nblk; ++b) {
+        const uint8_t* blk = blocks + b * BLK_IQ2;
+        uint16_t dh; memcpy(&dh, blk, 2);
+        const float d = half_to_float(dh);
+        for (int g = 0; g < 8; ++g) {
+            uint32_t aux0, aux1; memcpy(&aux0, blk + 2 + 8 * g, 4); memcpy(&aux1, blk + 6 + 8 * g, 4);
+            const float db = d * (0.5f + (float)(aux1 >> 28)) * 0.25f;
+            for (int l = 0; l < 4; ++l) {
+                const uint64_t gv = IQ2_GRID[(aux0 >> (8 * l)) & 0xFF];
+                const uint32_t s = iq2_ksigns((aux1 >> (7 * l)) & 127u);
+                for (int j = 0; j < 8; ++j) {
+                    const float m = (float)((gv >> (8 * j)) & 0xFF);
+                    out[b * 256 + g * 32 + l * 8 + j] = db * m * ((s >> j) & 1 ? -1.0f : 1.0f);
+                }
+            }
+        }
+    }
+}
+
+// seeded generator (moe_format.h): rows x K matrix of (layer, matrix, expert)
+void orc_gen_iq2(uint64_t seed, int layer, int matrix, int expert, int rows, int K, uint8_t* out) {
+    const uint64_t key = iq2_gen_key(seed, (uint32_t)layer, (uint32_t)matrix, (uint32_t)expert);
+    const int64_t nblk = (int64_t)rows * (K / QK);
+    #pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nblk; ++b) iq2_gen_block(key, (uint64_t)b, out + b * BLK_IQ2);
+}
+
+void orc_gen_d_only(uint64_t seed, int layer, int matrix, int expert, int64_t nblk, uint16_t* out) {
+    const uint64_t key = iq2_gen_key(seed, (uint32_t)layer, (uint32_t)matrix, (uint32_t)expert);
+    for (int64_t b = 0; b < nblk; ++b) out[b] = iq2_gen_d(key, (uint64_t)b);
+}
+
+float orc_expf(float x) { return lk_expf(x); }
+uint16_t orc_f2h(float x) { return float_to_half_rne(x); }
+float orc_h2f(uint16_t h) { return half_to_float(h); }
+
+// q8 per 32 of n values (n % 32 == 0): q[n], d[n/32]
+void orc_quant_q8(const float* x, int64_t n, int8_t* q, float* d) {
+    for (int64_t g = 0; g < n / 32; ++g) d[g] = quant_q8_group(x + g * 32, q + g * 32);
+}
+
+// ------------------------------------------------------------------ router
+// logits[t][e] = W[e] . x[t] in the GPU router kernel's order: 128 partial sums per (t, e); partial p
+// (p = 32*warp + lane) runs over float4 chunks c = p, p+128, ... (14 chunks for 7168) and within a chunk
+// over its 4 components, each step acc = fmaf(w, x, acc); each warp's 32 partials are combined by the
+// xor butterfly (offsets 16, 8, 4, 2, 1: a_l <- a_l + a_(l^o)); the 4 warp sums as (s0 + s1) + (s2 + s3).
+void orc_router_logits(const float* x, int T, const float* W, int n_experts, int K, float* logits) {
+    const int NCH = K / 4;
+    #pragma omp parallel for collapse(2) schedule(static)
+    for (int t = 0; t < T; ++t)
+        for (int e = 0; e < n_experts; ++e) {
+            const float* xr = x + (size_t)t * K; const float* wr = W + (size_t)e * K;
+            float ws[4];
+            for (int w = 0; w < 4; ++w) {
+                float a[32];
+                for (int l = 0; l < 32; ++l) {
+                    float acc = 0.0f;
+                    for (int c = 32 * w + l; c < NCH; c += 128)
+                        for (int j = 0; j < 4; ++j) acc = fmaf(wr[4 * c + j], xr[4 * c + j], acc);
+                    a[l] = acc;
+                }
+                for (int o = 16; o > 0; o >>= 1) {
+                    float b[32];
+                    for (int l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ o];
+                    memcpy(a, b, sizeof(a));
+                }
+                ws[w] = a[0];
+            }
+            logits[(size_t)t * n_experts + e] = (ws[0] + ws[1]) + (ws[2] + ws[3]);
+        }
+}
+
+struct OrcRouteCfg {
+    int n_experts;    // 256
+    int topk;         // experts selected by score (8)
+    int keep;         // experts kept per token after the weight sort (KE <= topk)
+    int renorm;       // 1: kept weights rescaled to sum to `scale` (engine default)
+    int n_group;      // 1 = plain top-k (the reference); 8 = DeepSeek-V3 grouped
+    int topk_group;   // groups kept in grouped mode (4)
+    float scale;      // routed scaling factor (2.5)
+};
+
+// one token: probs[n_experts] -> sel[keep], w[keep]
+static void route_one(const float* p, const float* bias, const OrcRouteCfg& c, int* sel, float* w) {
+    const int NE = c.n_experts;
+    std::vector<float> sc(NE);
+    for (int e = 0; e < NE; ++e) sc[e] = p[e] + bias[e];
+    std::vector<char> allowed(NE, 1);
+    if (c.n_group > 1) {
+        const int gs = NE / c.n_group;
+        std::vector<float> gscore(c.n_group);
+        for (int g = 0; g < c.n_group; ++g) {   // top-2 of the group (ties -> lower id), summed larger-first
+            int i1 = -1, i2 = -1;
+            for (int e = g * gs; e < (g + 1) * gs; ++e) {
+                if (i1 < 0 || sc[e] > sc[i1]) { i2 = i1; i1 = e; }
+                else if (i2 < 0 || sc[e] > sc[i2]) i2 = e;
+            }
+            gscore[g] = sc[i1] + sc[i2];
+        }
+        std::vector<char> gkeep(c.n_group, 0);
+        for (int r = 0; r < c.topk_group; ++r) {
+            int bg = -1;
+            for (int g = 0; g < c.n_group; ++g) if (!gkeep[g] && (bg < 0 || gscore[g] > gscore[bg])) bg = g;
+            gkeep[bg] = 1;
+        }
+        for (int e = 0; e < NE; ++e) allowed[e] = gkeep[e / gs];
+    }
+    int top[MAX_TOPK]; std::vector<char> taken(NE, 0);
+    for (int k = 0; k < c.topk; ++k) {                    // argmax rounds, ties -> lower id
+        int bi = -1;
+        for (int e = 0; e < NE; ++e) if (allowed[e] && !taken[e] && (bi < 0 || sc[e] > sc[bi])) bi = e;
+        top[k] = bi; taken[bi] = 1;
+    }
+    float sum = 0.0f;
+    for (int k = 0; k < c.topk; ++k) sum += p[top[k]];
+    sum = fmaxf(sum, 6.103515625e-5f);
+    float wt[MAX_TOPK];
+    for (int k = 0; k < c.topk; ++k) wt[k] = p[top[k]] / sum * c.scale;
+    if (c.keep >= c.topk) { for (int k = 0; k < c.topk; ++k) { sel[k] = top[k]; w[k] = wt[k]; } return; }
+    int ord[MAX_TOPK]; for (int k = 0; k < c.topk; ++k) ord[k] = k;
+    std::stable_sort(ord, ord + c.topk, [&](int a, int b) { return wt[a] > wt[b]; });   // ties keep position order
+    float kw[MAX_TOPK]; float sw = 0.0f;
+    for (int k = 0; k < c.keep; ++k) { sel[k] = top[ord[k]]; kw[k] = wt[ord[k]]; sw += kw[k]; }
+    if (c.renorm && sw > 1e-6f) { const float f = c.scale / sw; for (int k = 0; k < c.keep; ++k) kw[k] *= f; }
+    for (int k = 0; k < c.keep; ++k) w[k] = kw[k];
+}
+
+// probs may be null; logits_in: optional precomputed logits (replaces W.x; the "uniform-random logits" mode)
+void orc_router(const float* x, int T, const float* W, const float* logits_in, const float* bias,
+                const OrcRouteCfg* cfg, float* probs_out, int* sel, float* w) {
+    const int NE = cfg->n_experts;
+    std::vector<float> logit((size_t)T * NE);
+    if (logits_in) memcpy(logit.data(), logits_in, logit.size() * 4);
+    else orc_router_logits(x, T, W, NE, HIDDEN, logit.data());
+    std::vector<float> p(logit.size());
+    for (size_t i = 0; i < p.size(); ++i) p[i] = lk_sigmoid(logit[i]);
+    if (probs_out) memcpy(probs_out, p.data(), p.size() * 4);
+    #pragma omp parallel for schedule(static)
+    for (int t = 0; t < T; ++t) route_one(&p[(size_t)t * NE], bias, *cfg, sel + (size_t)t * cfg->keep, w + (size_t)t * cfg->keep);
+}
+
+// ------------------------------------------------------------------ permute (dispatch order)
+// counts[NE], offsets[NE+1], perm[T*KE] = flat (t*KE + k) indices grouped by expert, stable by (t, k)
+void orc_permute(const int* sel, int T, int KE, int NE, int* counts, int* offsets, int* perm) {
+    for (int e = 0; e < NE; ++e) counts[e] = 0;
+    for (int i = 0; i < T * KE; ++i) counts[sel[i]]++;
+    offsets[0] = 0;
+    for (int e = 0; e < NE; ++e) offsets[e + 1] = offsets[e] + counts[e];
+    std::vector<int> fill(offsets, offsets + NE);
+    for (int i = 0; i < T * KE; ++i) perm[fill[sel[i]]++] = i;
+}
+
+// ------------------------------------------------------------------ expert products
+// integer dot of IQ2 group g of a row with 32 q8 activations
+static inline int32_t iq2_group_isum(const uint8_t* grp, const int8_t* xq) {
+    uint32_t aux0, aux1; memcpy(&aux0, grp, 4); memcpy(&aux1, grp + 4, 4);
+    int32_t s = 0;
+    for (int l = 0; l < 4; ++l) {
+        const uint64_t gv = IQ2_GRID[(aux0 >> (8 * l)) & 0xFF];
+        const uint32_t sg = iq2_ksigns((aux1 >> (7 * l)) & 127u);
+        for (int j = 0; j < 8; ++j) {
+            const int32_t m = (int32_t)((gv >> (8 * j)) & 0xFF);
+            s += ((sg >> j) & 1 ? -m : m) * (int32_t)xq[8 * l + j];
+        }
+    }
+    return s;
+}
+
+// y = W . dequant(xq, xd) for `ntok` activation rows (each K int8 + K/32 scales), W = rows x K IQ2_XXS
+static void iq2_matvec_multi(const uint8_t* W, int rows, int K, const int8_t* const* xq, const float* const* xd,
+                             int ntok, float* const* y) {
+    const int NB = K / QK;
+    #pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t* row = W + (size_t)r * NB * BLK_IQ2;
+        std::vector<double> acc(ntok, 0.0);
+        for (int b = 0; b < NB; ++b) {
+            const uint8_t* blk = row + (size_t)b * BLK_IQ2;
+            uint16_t dh; memcpy(&dh, blk, 2); const float d = half_to_float(dh);
+            for (int g = 0; g < 8; ++g) {
+                uint32_t aux1; memcpy(&aux1, blk + 6 + 8 * g, 4);
+                const float fa = d * (0.5f + (float)(aux1 >> 28)) * 0.25f;
+                const int col = b * 8 + g;
+                for (int t = 0; t < ntok; ++t) {
+                    const int32_t is = iq2_group_isum(blk + 2 + 8 * g, xq[t] + col * 32);
+                    acc[t] += (double)fa * (double)xd[t][col] * (double)is;
+                }
+            }
+        }
+        for (int t = 0; t < ntok; ++t) y[t][r] = (float)acc[t];
+    }
+}
+
+void orc_iq2_matvec(const uint8_t* W, int rows, int K, const int8_t* xq, const float* xd, float* y) {
+    iq2_matvec_multi(W, rows, K, &xq, &xd, 1, &y);
+}
+
+// ------------------------------------------------------------------ the MoE layer
+// Weights in the engine's arena layout: expert m's gate at gate + m*gate_stride (bytes), likewise up/down;
+// ids are expert (slot) indices into those arenas.  Shared expert (IQ2_XXS) optional (null = none).
+// Outputs: h[T][E] = routed + shared + resid, moe[T][E] = routed; optional y_slot[T][KE][E] (w-weighted
+// per-slot outputs, the reference's out_all), hq/hd: SwiGLU q8 per (t, k) slot [T*KE][2048] / [T*KE][64].
+struct OrcLayerW {
+    const uint8_t* gate; const uint8_t* up; const uint8_t* down; int64_t gate_stride, up_stride, down_stride;
+    const uint8_t* sh_gate; const uint8_t* sh_up; const uint8_t* sh_down;
+};
+
+int orc_moe_layer(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
+                  int KE, float* h, float* moe, float* y_slot, float* shared_out) {
+    const int E = HIDDEN, H = MOE_INTER;
+    // q8 of every token's x
+    std::vector<int8_t> xq((size_t)T * E); std::vector<float> xd((size_t)T * E / 32);
+    orc_quant_q8(x, (int64_t)T * E, xq.data(), xd.data());
+    // per-expert token lists (stable by (t, k))
+    int maxid = 0; for (int i = 0; i < T * KE; ++i) maxid = std::max(maxid, ids[i]);
+    const int NE = maxid + 1;
+    std::vector<int> cnt(NE), off(NE + 1), perm((size_t)T * KE);
+    orc_permute(ids, T, KE, NE, cnt.data(), off.data(), perm.data());
+    std::vector<float> yslot((size_t)T * KE * E, 0.0f);
+    std::vector<float> g((size_t)T * KE * H), u((size_t)T * KE * H);
+    std::vector<int8_t> hq((size_t)T * KE * H); std::vector<float> hd((size_t)T * KE * H / 32);
+    for (int m = 0; m < NE; ++m) {
+        if (cnt[m] == 0) continue;
+        const int n = cnt[m];
+        std::vector<const int8_t*> xqp(n); std::vector<const float*> xdp(n); std::vector<float*> gp(n), up(n);
+        for (int i = 0; i < n; ++i) {
+            const int s = perm[off[m] + i], t = s / KE;
+            xqp[i] = xq.data() + (size_t)t * E; xdp[i] = xd.data() + (size_t)t * E / 32;
+            gp[i] = g.data() + (size_t)s * H; up[i] = u.data() + (size_t)s * H;
+        }
+        iq2_matvec_multi(Wl->gate + m * Wl->gate_stride, H, E, xqp.data(), xdp.data(), n, gp.data());
+        iq2_matvec_multi(Wl->up + m * Wl->up_stride, H, E, xqp.data(), xdp.data(), n, up.data());
+        std::vector<const int8_t*> hqp(n); std::vector<const float*> hdp(n); std::vector<float*> yp(n);
+        std::vector<std::vector<float>> ytmp(n, std::vector<float>(E));
+        for (int i = 0; i < n; ++i) {
+            const int s = perm[off[m] + i];
+            std::vector<float> hv(H);
+            for (int j = 0; j < H; ++j) hv[j] = lk_swiglu(g[(size_t)s * H + j], u[(size_t)s * H + j]);
+            orc_quant_q8(hv.data(), H, hq.data() + (size_t)s * H, hd.data() + (size_t)s * H / 32);
+            hqp[i] = hq.data() + (size_t)s * H; hdp[i] = hd.data() + (size_t)s * H / 32; yp[i] = ytmp[i].data();
+        }
+        iq2_matvec_multi(Wl->down + m * Wl->down_stride, E, H, hqp.data(), hdp.data(), n, yp.data());
+        for (int i = 0; i < n; ++i) {
+            const int s = perm[off[m] + i];
+            for (int j = 0; j < E; ++j) yslot[(size_t)s * E + j] = w[s] * ytmp[i][j];
+        }
+    }
+    // shared expert on every token
+    std::vector<float> sh((size_t)T * E, 0.0f);
+    if (Wl->sh_gate) {
+        std::vector<const int8_t*> xqp(T); std::vector<const float*> xdp(T);
+        std::vector<float> sg((size_t)T * H), su((size_t)T * H); std::vector<float*> sgp(T), sup(T), shp(T);
+        for (int t = 0; t < T; ++t) {
+            xqp[t] = xq.data() + (size_t)t * E; xdp[t] = xd.data() + (size_t)t * E / 32;
+            sgp[t] = sg.data() + (size_t)t * H; sup[t] = su.data() + (size_t)t * H; shp[t] = sh.data() + (size_t)t * E;
+        }
+        iq2_matvec_multi(Wl->sh_gate, H, E, xqp.data(), xdp.data(), T, sgp.data());
+        iq2_matvec_multi(Wl->sh_up, H, E, xqp.data(), xdp.data(), T, sup.data());
+        std::vector<int8_t> shq((size_t)T * H); std::vector<float> shd((size_t)T * H / 32);
+        std::vector<const int8_t*> hqp(T); std::vector<const float*> hdp(T);
+        for (int t = 0; t < T; ++t) {
+            std::vector<float> hv(H);
+            for (int j = 0; j < H; ++j) hv[j] = lk_swiglu(sg[(size_t)t * H + j], su[(size_t)t * H + j]);
+            orc_quant_q8(hv.data(), H, shq.data() + (size_t)t * H, shd.data() + (size_t)t * H / 32);
+            hqp[t] = shq.data() + (size_t)t * H; hdp[t] = shd.data() + (size_t)t * H / 32;
+        }
+        iq2_matvec_multi(Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
+    }
+    // combine in fixed k order
+    #pragma omp parallel for schedule(static)
+    for (int t = 0; t < T; ++t)
+        for (int j = 0; j < E; ++j) {
+            double r = 0.0;
+            for (int k = 0; k < KE; ++k) r += (double)yslot[((size_t)t * KE + k) * E + j];
+            if (moe) moe[(size_t)t * E + j] = (float)r;
+            if (h) h[(size_t)t * E + j] = (float)(r + (double)sh[(size_t)t * E + j] + (double)resid[(size_t)t * E + j]);
+        }
+    if (y_slot) memcpy(y_slot, yslot.data(), yslot.size() * 4);
+    if (shared_out) memcpy(shared_out, sh.data(), sh.size() * 4);
+    return 0;
+}
+
+}  // extern "C"

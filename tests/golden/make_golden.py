@@ -1,0 +1,97 @@
+"""Generate the committed golden fixtures (tests/golden/*.npz).
+
+The reference ships no kernel tests or vectors for its MoE path, so the fixtures pin the oracle against an
+independent implementation of the same format and against itself over time:
+
+  iq2_xxs_gguf.npz   IQ2_XXS blocks (seeded + hand-built edge blocks covering every grid index, sign index
+                     and scale, plus zero / subnormal / negative / large d) and their dequantisation by
+                     gguf-py 0.19.0 (gguf.quants.dequantize, the Python port of ggml's
+                     dequantize_row_iq2_xxs) -- the independent decode reference.
+  generator_kat.npz  the first bytes of seeded weight matrices (seed 0x10C1) for several (layer, matrix,
+                     expert) keys -- pins the counter-based generator shared by CPU and GPU.
+  router_kat.npz     router outputs (probs, top-8 ids/weights; keep-2 ids/weights; grouped mode) of the
+                     oracle on numpy-seeded inputs -- pins routing semantics.
+  moe_layer_kat.npz  h / moe of the oracle layer on a small arena (6 experts, T=3) -- pins the layer math.
+
+Run from the repository root:  python tests/golden/make_golden.py
+"""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from oracle import oracle as O  # noqa: E402
+
+SEED = 0x10C1
+
+
+def edge_blocks():
+    """Blocks whose groups walk every grid index (256), sign index (128) and scale (16)."""
+    rng = np.random.default_rng(7)
+    blocks = []
+    ds = [0.0, 1e-3, -2.5e-3, 6.0e-8, 1.0, 65504.0, 3.0517578125e-05, 0.5]
+    gi = 0
+    si = 0
+    for b in range(40):
+        blk = bytearray(66)
+        d = np.float16(ds[b % len(ds)]) if b < len(ds) else np.float16(abs(rng.standard_normal()) * 1e-3)
+        blk[0:2] = np.array([d], np.float16).tobytes()
+        for g in range(8):
+            idx = [(gi + j) % 256 for j in range(4)]
+            gi += 4
+            sg = [(si + j) % 128 for j in range(4)]
+            si += 4
+            scale = (b * 8 + g) % 16
+            aux1 = sg[0] | (sg[1] << 7) | (sg[2] << 14) | (sg[3] << 21) | (scale << 28)
+            blk[2 + 8 * g: 6 + 8 * g] = bytes(idx)
+            blk[6 + 8 * g: 10 + 8 * g] = int(aux1).to_bytes(4, "little")
+        blocks.append(bytes(blk))
+    return np.frombuffer(b"".join(blocks), np.uint8)
+
+
+def main():
+    from gguf.quants import dequantize
+    from gguf import GGMLQuantizationType as QT
+
+    seeded = O.gen_iq2(SEED, 0, 0, 3, 8, 7168)            # 8 rows x 28 blocks
+    blocks = np.concatenate([edge_blocks(), seeded[: 66 * 64]])
+    deq = dequantize(blocks, QT.IQ2_XXS).reshape(-1).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "iq2_xxs_gguf.npz"), blocks=blocks, dequant=deq)
+
+    keys = [(0, 0, 0), (0, 1, 0), (0, 2, 0), (1, 0, 255), (57, 2, 256), (3, 1, 17)]
+    kat = np.stack([O.gen_iq2(SEED, l, m, e, 2, 7168)[: 2 * 66] for (l, m, e) in keys])
+    np.savez_compressed(os.path.join(HERE, "generator_kat.npz"), keys=np.array(keys, np.int32), bytes=kat)
+
+    rng = np.random.default_rng(2024)
+    T = 5
+    x = rng.standard_normal((T, 7168)).astype(np.float32)
+    W = (rng.standard_normal((256, 7168)) * 0.02).astype(np.float32)
+    bias = (rng.standard_normal(256) * 0.01).astype(np.float32)
+    p8, s8, w8 = O.router(x, W, bias, O.route_cfg(8, 8))
+    _, s2, w2 = O.router(x, W, bias, O.route_cfg(8, 2))
+    _, sg, wg = O.router(x, W, bias, O.route_cfg(8, 8, n_group=8, topk_group=4))
+    np.savez_compressed(os.path.join(HERE, "router_kat.npz"), probs=p8, sel8=s8, w8=w8, sel2=s2, w2=w2, selg=sg, wg=wg)
+
+    NE = 6
+    S = 2048 * 28 * 66
+    gate = np.concatenate([O.gen_iq2(SEED, 9, 0, e, 2048, 7168) for e in range(NE)])
+    up = np.concatenate([O.gen_iq2(SEED, 9, 1, e, 2048, 7168) for e in range(NE)])
+    down = np.concatenate([O.gen_iq2(SEED, 9, 2, e, 7168, 2048) for e in range(NE)])
+    shg, shu, shd = (O.gen_iq2(SEED, 9, 0, 256, 2048, 7168), O.gen_iq2(SEED, 9, 1, 256, 2048, 7168),
+                     O.gen_iq2(SEED, 9, 2, 256, 7168, 2048))
+    rng = np.random.default_rng(99)
+    T, KE = 3, 4
+    xs = rng.standard_normal((T, 7168)).astype(np.float32)
+    rs = rng.standard_normal((T, 7168)).astype(np.float32)
+    ids = np.array([[0, 2, 5, 1], [3, 2, 4, 0], [5, 1, 0, 3]], np.int32)
+    wk = rng.uniform(0.1, 1.0, (T, KE)).astype(np.float32)
+    out = O.moe_layer(xs, rs, gate, up, down, S, ids, wk, shg, shu, shd)
+    np.savez_compressed(os.path.join(HERE, "moe_layer_kat.npz"), ids=ids, w=wk, h=out["h"], moe=out["moe"])
+    print("fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,199 @@
+"""GPU parity of the CUDA path (through libloki_moe.so's C ABI) against the CPU oracle.
+
+Bit-exact: generated weights, router probabilities, selected expert ids and weights, dispatch
+permutations.  Layer outputs h / moe: relative L2 <= 2e-3 (RTOL_L2) of the oracle using the same q8 scheme.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from moe_helpers import SEED, HIDDEN, INTER, MAT, RTOL_L2, rel_l2, oracle_layer, host_arena
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def moe(native):
+    from loki_b200 import moe as M
+    return M
+
+
+def _dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t if dtype is None else t.to(dtype)
+
+
+def router_only_weights(native, W, bias, f16=False):
+    ws = native.LkMoeWeights()
+    ws.router_w = W.data_ptr()
+    ws.router_w_f16 = 1 if f16 else 0
+    ws.router_bias = bias.data_ptr()
+    ws.down_fmt = native.FMT_IQ2
+    return ws
+
+
+# ---------------------------------------------------------------- generator
+@pytest.mark.parametrize("key", [(0, 0, 0), (3, 1, 77), (57, 2, 255), (7, 0, 256)])
+def test_generator_bitexact(native, moe, oracle, key):
+    layer, m, e = key
+    rows, K = (INTER, HIDDEN) if m < 2 else (HIDDEN, INTER)
+    buf = torch.empty(MAT, dtype=torch.uint8, device="cuda")
+    moe.gen_iq2(buf, SEED, layer, m, e, 1, rows, K, MAT)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(buf.cpu().numpy(), oracle.gen_iq2(SEED, layer, m, e, rows, K))
+
+
+# ---------------------------------------------------------------- router
+ROUTE_MODES = {
+    "top8": dict(keep=8), "keep2": dict(keep=2), "keep2_norenorm": dict(keep=2, renorm=False),
+    "grouped": dict(keep=8, n_group=8, topk_group=4), "grouped_keep2": dict(keep=2, n_group=8, topk_group=4),
+}
+
+
+@pytest.mark.parametrize("T", [1, 3, 16, 512])
+@pytest.mark.parametrize("f16", [False, True])
+@pytest.mark.parametrize("mode", list(ROUTE_MODES))
+def test_router_bitexact(native, moe, oracle, T, f16, mode):
+    md = ROUTE_MODES[mode]
+    rng = np.random.default_rng(100 + T)
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    W = (rng.standard_normal((256, HIDDEN)) * 0.02).astype(np.float32)
+    if f16:
+        W = W.astype(np.float16)
+    bias = (rng.standard_normal(256) * 0.01).astype(np.float32)
+    layer = moe.MoeLayer(0, keep=md["keep"], renorm=md.get("renorm", True), n_group=md.get("n_group", 1),
+                         topk_group=md.get("topk_group", 1), max_tokens=T)
+    Wd, bd = _dev(W), _dev(bias)
+    probs, sel, w = layer.route(router_only_weights(native, Wd, bd, f16), _dev(x))
+    torch.cuda.synchronize()
+    cfg = oracle.route_cfg(8, md["keep"], int(md.get("renorm", True)), md.get("n_group", 1), md.get("topk_group", 1))
+    op, osel, ow = oracle.router(x, W.astype(np.float32), bias, cfg)
+    np.testing.assert_array_equal(probs.cpu().numpy(), op)
+    np.testing.assert_array_equal(sel.cpu().numpy(), osel)
+    np.testing.assert_array_equal(w.cpu().numpy(), ow)
+    layer.device_error()
+
+
+def test_router_logits_override(native, moe, oracle):
+    rng = np.random.default_rng(7)
+    T = 64
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    W = (rng.standard_normal((256, HIDDEN)) * 0.02).astype(np.float32)
+    bias = (rng.standard_normal(256) * 0.01).astype(np.float32)
+    logits = rng.uniform(-1, 1, (T, 256)).astype(np.float32)
+    layer = moe.MoeLayer(0, max_tokens=T)
+    probs, sel, w = layer.route(router_only_weights(native, _dev(W), _dev(bias)), _dev(x), logits_override=_dev(logits))
+    op, osel, ow = oracle.router(None, None, bias, oracle.route_cfg(8, 8), logits=logits)
+    np.testing.assert_array_equal(probs.cpu().numpy(), op)
+    np.testing.assert_array_equal(sel.cpu().numpy(), osel)
+    np.testing.assert_array_equal(w.cpu().numpy(), ow)
+
+
+# ---------------------------------------------------------------- dispatch
+def zipf_sel(rng, T, keep, s=1.2):
+    p = 1.0 / np.arange(1, 257) ** s
+    p /= p.sum()
+    out = np.empty((T, keep), np.int32)
+    for t in range(T):
+        out[t] = rng.choice(256, keep, replace=False, p=p)
+    return out
+
+
+@pytest.mark.parametrize("T,keep,skew", [(1, 8, False), (5, 2, False), (512, 8, False), (4096, 8, False), (512, 2, True), (3000, 8, True)])
+def test_dispatch_bitexact(native, moe, oracle, T, keep, skew):
+    rng = np.random.default_rng(T + keep)
+    sel = zipf_sel(rng, T, keep) if skew else np.stack([rng.choice(256, keep, replace=False) for _ in range(T)]).astype(np.int32)
+    w = rng.uniform(0, 1, (T, keep)).astype(np.float32)
+    layer = moe.MoeLayer(0, keep=keep, max_tokens=T)
+    counts, offsets, perm = layer.dispatch(_dev(sel), _dev(w))
+    oc, oo, op = oracle.permute(sel)
+    np.testing.assert_array_equal(counts.cpu().numpy(), oc)
+    np.testing.assert_array_equal(offsets.cpu().numpy(), oo)
+    np.testing.assert_array_equal(perm.cpu().numpy(), op)
+
+
+# ---------------------------------------------------------------- experts on a small arena
+@pytest.mark.parametrize("T,keep", [(1, 8), (1, 2), (3, 2), (8, 8), (20, 4)])
+def test_experts_small_arena(native, moe, oracle, T, keep):
+    NE = 12
+    layer_id = 11
+    buf = torch.empty(3 * NE * MAT + 3 * MAT, dtype=torch.uint8, device="cuda")
+    base = buf.data_ptr()
+    for m in range(3):
+        rows, K = (INTER, HIDDEN) if m < 2 else (HIDDEN, INTER)
+        moe.gen_iq2(base + m * NE * MAT, SEED, layer_id, m, 0, NE, rows, K, MAT)
+        moe.gen_iq2(base + 3 * NE * MAT + m * MAT, SEED, layer_id, m, 256, 1, rows, K, MAT)
+    ws = native.LkMoeWeights(base, base + NE * MAT, base + 2 * NE * MAT, MAT, MAT, MAT, native.FMT_IQ2,
+                             base + 3 * NE * MAT, base + 3 * NE * MAT + MAT, base + 3 * NE * MAT + 2 * MAT, None, 0, None)
+    rng = np.random.default_rng(T * 10 + keep)
+    sel = np.stack([rng.choice(NE, keep, replace=False) for _ in range(T)]).astype(np.int32)
+    w = rng.uniform(0.05, 1.0, (T, keep)).astype(np.float32)
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    layer = moe.MoeLayer(0, keep=keep, max_tokens=T)
+    h, mo = layer.experts(ws, _dev(x), _dev(r), _dev(sel), _dev(w))
+    layer.device_error()
+    ref = oracle_layer(oracle, SEED, layer_id, x, r, sel, w)
+    e_moe, e_h = rel_l2(mo.cpu().numpy(), ref["moe"]), rel_l2(h.cpu().numpy(), ref["h"])
+    assert e_moe < RTOL_L2 and e_h < RTOL_L2, (e_moe, e_h)
+
+
+# ---------------------------------------------------------------- the whole layer (256 experts resident)
+@pytest.fixture(scope="module")
+def layer_weights(moe):
+    W = moe.LayerWeights("cuda", SEED, 0)
+    torch.cuda.synchronize()
+    yield W
+    del W
+    torch.cuda.empty_cache()
+
+
+def _layer_case(moe, oracle, W, T, keep=8, n_group=1, topk_group=1, logits=None, sample=None, seed=0):
+    rng = np.random.default_rng(1000 + T + seed)
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    layer = moe.MoeLayer(0, keep=keep, n_group=n_group, topk_group=topk_group, max_tokens=T)
+    h, mo, sel, w = layer.forward(W, _dev(x), _dev(r), logits_override=None if logits is None else _dev(logits))
+    layer.device_error()
+    sel, w = sel.cpu().numpy(), w.cpu().numpy()
+    Wr = W.router_w.float().cpu().numpy()
+    bias = W.router_bias.cpu().numpy()
+    cfg = oracle.route_cfg(8, keep, 1, n_group, topk_group)
+    _, osel, ow = oracle.router(x, Wr, bias, cfg, logits=logits)
+    np.testing.assert_array_equal(sel, osel)
+    np.testing.assert_array_equal(w, ow)
+    ref = oracle_layer(oracle, SEED, 0, x, r, sel, w, tokens=sample)
+    tok = list(range(T)) if sample is None else list(sample)
+    e_moe = rel_l2(mo.cpu().numpy()[tok], ref["moe"])
+    e_h = rel_l2(h.cpu().numpy()[tok], ref["h"])
+    assert e_moe < RTOL_L2 and e_h < RTOL_L2, (e_moe, e_h)
+    return e_moe, e_h
+
+
+def test_layer_config0_T16(moe, oracle, layer_weights):
+    """T=16, hidden 7168, 256 experts, top-8, shared expert."""
+    _layer_case(moe, oracle, layer_weights, 16)
+
+
+@pytest.mark.parametrize("keep,n_group", [(8, 1), (2, 1), (8, 8), (2, 8)])
+def test_layer_decode_T1(moe, oracle, layer_weights, keep, n_group):
+    _layer_case(moe, oracle, layer_weights, 1, keep=keep, n_group=n_group, topk_group=4 if n_group > 1 else 1)
+
+
+def test_layer_prefill_T512_uniform_logits(moe, oracle, layer_weights):
+    """BASELINE config 2 shape: T=512 with uniform-random router logits; oracle on a token sample."""
+    rng = np.random.default_rng(512)
+    logits = rng.uniform(-1, 1, (512, 256)).astype(np.float32)
+    _layer_case(moe, oracle, layer_weights, 512, logits=logits, sample=[0, 1, 77, 255, 256, 400, 510, 511])
+
+
+def test_layer_deterministic(moe, layer_weights):
+    rng = np.random.default_rng(3)
+    x = _dev(rng.standard_normal((64, HIDDEN)).astype(np.float32))
+    r = _dev(rng.standard_normal((64, HIDDEN)).astype(np.float32))
+    layer = moe.MoeLayer(0, max_tokens=64)
+    h1 = layer.forward(layer_weights, x, r)[0].clone()
+    h2 = layer.forward(layer_weights, x, r)[0].clone()
+    assert torch.equal(h1, h2)
