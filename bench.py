@@ -53,6 +53,28 @@ def ncu_traffic(kernel, workload):
     return None
 
 
+class DriverEvents:
+    """Timing events created through the CUDA driver API: the library records them on its launch stream
+    (also inside graph capture), and elapsed times are read with cuEventElapsedTime."""
+
+    def __init__(self, n):
+        import ctypes
+        self.ct = ctypes
+        self.cu = ctypes.CDLL("libcuda.so.1")
+        self.ev = [ctypes.c_void_p() for _ in range(n)]
+        for e in self.ev:
+            rc = self.cu.cuEventCreate(ctypes.byref(e), 0)
+            if rc != 0:
+                raise RuntimeError("cuEventCreate failed: %d" % rc)
+
+    def elapsed(self, a, b):
+        ms = self.ct.c_float()
+        rc = self.cu.cuEventElapsedTime(self.ct.byref(ms), self.ev[a], self.ev[b])
+        if rc != 0:
+            raise RuntimeError("cuEventElapsedTime failed: %d" % rc)
+        return ms.value
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled during the timed region."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
@@ -200,7 +222,7 @@ def run_decode(args, ws, rank, local, dist):
         s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
         for i in range(args.layers):
             if events is not None:
-                arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in events[i]])
+                arr = (ctypes.c_void_p * 4)(*[events.ev[4 * i + j].value for j in range(4)])
                 L.lk_moe_set_events(ctx.ctx, arr)
             rc = L.lk_moe_forward(ctx.ctx, ctypes.byref(structs[layer_of[i]]), ctypes.c_void_p(xs[i].data_ptr()),
                                   ctypes.c_void_p(rs[i].data_ptr()), 1, None, ctypes.c_void_p(hs[i].data_ptr()),
@@ -217,7 +239,7 @@ def run_decode(args, ws, rank, local, dist):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.layers)]
+    ev = DriverEvents(4 * args.layers)
     graph_ev = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph_ev, stream=stream):
         step(ev)
@@ -247,9 +269,9 @@ def run_decode(args, ws, rank, local, dist):
     torch.cuda.synchronize(dev)
     cl = clocks.stop() if clocks else None
     ctx.device_error()
-    gu = np.array([ev[i][0].elapsed_time(ev[i][1]) for i in range(args.layers)])
-    dn = np.array([ev[i][1].elapsed_time(ev[i][2]) for i in range(args.layers)])
-    cb = np.array([ev[i][2].elapsed_time(ev[i][3]) for i in range(args.layers)])
+    gu = np.array([ev.elapsed(4 * i, 4 * i + 1) for i in range(args.layers)])
+    dn = np.array([ev.elapsed(4 * i + 1, 4 * i + 2) for i in range(args.layers)])
+    cb = np.array([ev.elapsed(4 * i + 2, 4 * i + 3) for i in range(args.layers)])
     ms_max = max_over_ranks(dist, ms)
     tokens = args.steps * ws
     value = tokens / (ms_max / 1e3)

@@ -29,7 +29,12 @@ __global__ void __launch_bounds__(DS_THREADS) k_build_slots(SlotParams p) {
     for (int i = tid; i < NE; i += DS_THREADS) { cnt[i] = 0; run[i] = 0; }
     for (int i = tid; i < (DS_THREADS / 32) * N_EXPERTS; i += DS_THREADS) (&wcnt[0][0])[i] = 0;
     __syncthreads();
-    for (int i = tid; i < entries; i += DS_THREADS) atomicAdd(&cnt[p.sel[i]], 1);
+    // ids outside [0, n_experts) are reported through the error word and dropped from every table
+    for (int i = tid; i < entries; i += DS_THREADS) {
+        const int e = p.sel[i];
+        if (e >= 0 && e < NE) atomicAdd(&cnt[e], 1);
+        else if (p.err) atomicCAS(p.err, 0, DEV_ERR_BAD_SLOT);
+    }
     __syncthreads();
     if (tid == 0) {
         int a = 0, s = 0;
@@ -40,8 +45,9 @@ __global__ void __launch_bounds__(DS_THREADS) k_build_slots(SlotParams p) {
     // stable ranks, one chunk of DS_THREADS entries at a time
     for (int c0 = 0; c0 < entries; c0 += DS_THREADS) {
         const int i = c0 + tid;
-        const bool live = i < entries;
-        const int e = live ? p.sel[i] : -1 - lane;   // distinct negative keys for dead lanes
+        const int ev = i < entries ? p.sel[i] : -1;
+        const bool live = ev >= 0 && ev < NE;
+        const int e = live ? ev : -1 - lane;         // distinct negative keys for dead lanes
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         const int rank_w = __popc(peers & ((1u << lane) - 1u));
         if (live && rank_w == 0) wcnt[warp][e] = (unsigned short)__popc(peers);

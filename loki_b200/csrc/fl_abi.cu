@@ -253,7 +253,7 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     sp.sel = c->ids; sp.w = c->w; sp.T = n; sp.keep = KE; sp.n_experts = N_EXPERTS; sp.nt = nt; sp.with_shared = 0;
     sp.counts = c->counts; sp.offsets = c->offsets; sp.perm = c->perm;
     sp.slot_expert = c->s_expert; sp.slot_tok = c->s_tok; sp.slot_out = c->s_out; sp.slot_w = c->s_w; sp.nslots = c->s_n;
-    sp.max_slots = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1);
+    sp.max_slots = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1); sp.err = c->err;
     launch_build_slots(sp, st);
     const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)EXPERT_DOWN_BYTES;
     ExpertParams e = expert_params(c, gate, up, down, sg, sd, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->hq, c->hd, c->y);

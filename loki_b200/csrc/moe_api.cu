@@ -35,6 +35,15 @@ static int set_err(LkMoeCtx* c, int code, const char* fmt, ...) {
 
 template <class T> static cudaError_t dalloc(T** p, size_t n) { return cudaMalloc((void**)p, (n ? n : 1) * sizeof(T)); }
 
+// event record that also becomes a graph node under stream capture (a plain record only marks a
+// capture dependency there)
+static cudaError_t record_event(cudaEvent_t ev, cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(st, &cs);
+    if (e != cudaSuccess) return e;
+    return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal) : cudaEventRecord(ev, st);
+}
+
 static int slot_nt(int T) { return T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8; }
 
 extern "C" {
@@ -148,7 +157,7 @@ int lk_moe_dispatch(LkMoeCtx* c, const int* sel, const float* w, int T, int keep
     s.with_shared = c->cfg.with_shared;
     s.counts = counts ? counts : c->counts; s.offsets = offsets ? offsets : c->offsets; s.perm = perm ? perm : c->perm;
     s.slot_expert = c->slot_expert; s.slot_tok = c->slot_tok; s.slot_out = c->slot_out; s.slot_w = c->slot_w;
-    s.nslots = c->nslots; s.max_slots = c->max_slots;
+    s.nslots = c->nslots; s.max_slots = c->max_slots; s.err = c->err;
     launch_build_slots(s, (cudaStream_t)stream);
     LK_CU(cudaGetLastError());
     return LK_OK;
@@ -164,11 +173,11 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const
     e.x = x; e.ld_x = HIDDEN;
     e.slot_expert = c->slot_expert; e.slot_tok = c->slot_tok; e.slot_out = c->slot_out; e.slot_w = c->slot_w; e.nslots = c->nslots;
     e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err;
-    if (c->ev[0]) LK_CU(cudaEventRecord(c->ev[0], st));
+    if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
-    if (c->ev[1]) LK_CU(cudaEventRecord(c->ev[1], st));
+    if (c->ev[1]) LK_CU(record_event(c->ev[1], st));
     launch_down(e, nt, c->nsm, st);
-    if (c->ev[2]) LK_CU(cudaEventRecord(c->ev[2], st));
+    if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
     CombineParams cp{};
     cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared;
     cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN;
@@ -176,7 +185,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const
         if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
         launch_combine(cp, st);
     }
-    if (c->ev[3]) LK_CU(cudaEventRecord(c->ev[3], st));
+    if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
     LK_CU(cudaGetLastError());
     return LK_OK;
 }

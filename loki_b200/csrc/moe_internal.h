@@ -32,6 +32,7 @@ struct SlotParams {
     int* counts; int* offsets; int* perm;               // [n_experts], [n_experts+1], [T*keep]
     int* slot_expert; int* slot_tok; int* slot_out; float* slot_w; int* nslots;   // slot tables
     int max_slots;
+    int* err;                                           // device error word (bad expert ids)
 };
 void launch_build_slots(const SlotParams& p, cudaStream_t st);
 int max_slots_for(int T, int keep, int n_experts, int nt, int with_shared);

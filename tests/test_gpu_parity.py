@@ -84,7 +84,8 @@ def test_router_logits_override(native, moe, oracle):
     bias = (rng.standard_normal(256) * 0.01).astype(np.float32)
     logits = rng.uniform(-1, 1, (T, 256)).astype(np.float32)
     layer = moe.MoeLayer(0, max_tokens=T)
-    probs, sel, w = layer.route(router_only_weights(native, _dev(W), _dev(bias)), _dev(x), logits_override=_dev(logits))
+    Wd, bd, xd, ld = _dev(W), _dev(bias), _dev(x), _dev(logits)      # kept alive: the struct holds raw pointers
+    probs, sel, w = layer.route(router_only_weights(native, Wd, bd), xd, logits_override=ld)
     op, osel, ow = oracle.router(None, None, bias, oracle.route_cfg(8, 8), logits=logits)
     np.testing.assert_array_equal(probs.cpu().numpy(), op)
     np.testing.assert_array_equal(sel.cpu().numpy(), osel)
