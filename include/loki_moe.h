@@ -104,6 +104,24 @@ LK_API int lk_moe_get_error(LkMoeCtx* ctx, lk_stream_t stream);
 LK_API const char* lk_moe_strerror(int code);
 LK_API const char* lk_moe_last_error(LkMoeCtx* ctx);
 
+/* lk_moe_experts_noalloc -- no counterpart in the reference.  The expert stage of lk_moe_experts
+ * (dispatch, gate/up + SwiGLU, down, combine) for callers that cannot allocate device memory: an engine
+ * that has already given all free HBM to resident expert shards and KV cache (a further cudaMalloc would
+ * fail or evict), or a latency-critical caller that cannot take cudaMalloc's device-wide synchronisation.
+ * No context: nothing is allocated or freed.  Its scratch is one static device array of
+ * LK_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until exit, so it serves at most
+ * LK_NOALLOC_MAX_TOKENS tokens and keep <= 8 per call; larger calls return LK_ERR_CAPACITY (with a message
+ * on stderr).  The first call on a device looks the array's address up (cudaGetSymbolAddress, with that
+ * device current): make that first call before any stream capture.  All calls share the array and it keeps
+ * the last call's contents; calls that overlap on the GPU race on it, so serialise them.  The kernel error
+ * word is cleared at the start of each call and, if `status` (a device int) is given, copied there at the
+ * end (0 = no error).  Arguments as lk_moe_experts, plus with_shared (run the shared expert W->sh_*). */
+#define LK_NOALLOC_MAX_TOKENS 8
+#define LK_NOALLOC_SCRATCH_BYTES 2241536
+LK_API int lk_moe_experts_noalloc(const LkMoeWeights* W, const float* x, const float* resid, int T, const int* sel,
+                                  const float* w, int keep, int with_shared, float* h, float* moe, int* status,
+                                  lk_stream_t stream);
+
 /* seeded synthetic IQ2_XXS weights: n_exp consecutive experts [rows][K] of (layer, matrix 0 gate / 1 up
  * / 2 down), expert expert0+i written at dst + i * stride; the same bytes as the CPU generator. */
 LK_API int lk_gen_iq2(void* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,

@@ -58,6 +58,7 @@ SIGNATURES = {
     "lk_moe_get_error": (_I, [_P, _P]),
     "lk_moe_strerror": (ctypes.c_char_p, [_I]),
     "lk_moe_last_error": (ctypes.c_char_p, [_P]),
+    "lk_moe_experts_noalloc": (_I, [ctypes.POINTER(LkMoeWeights), _P, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "lk_gen_iq2": (_I, [_P, ctypes.c_uint64, _I, _I, _I, _I, _I, _I, _I64, _P]),
     "fl_init": (_P, [_I, _I]),
     "fl_wide_init": (_I, [_P, _I, _I]),
