@@ -1,0 +1,73 @@
+// aux_kernels.cu -- small kernels around the expert stage: the combine (h = resid + shared + sum_k y;
+// reference moe_combine / wide_finish, src/fused_layer.cu:358-373) and the seeded IQ2_XXS generator.
+#include "moe_internal.h"
+#include "moe_device.cuh"
+
+namespace lk {
+
+// ------------------------------------------------------------------ combine
+__global__ void k_combine(CombineParams p) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;       // float4 index over T x HIDDEN
+    const int per = HIDDEN / 4;
+    if (i >= p.T * per) return;
+    const int t = i / per, c = i % per;
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < p.keep; ++k) {
+        const float4 v = ((const float4*)(p.y + ((size_t)t * p.keep + k) * HIDDEN))[c];
+        r.x += v.x; r.y += v.y; r.z += v.z; r.w += v.w;
+    }
+    if (p.moe) ((float4*)(p.moe + (size_t)t * p.ld_out))[c] = r;
+    float4 h = ((const float4*)(p.resid + (size_t)t * p.ld_out))[c];
+    if (p.with_shared) {
+        const float4 v = ((const float4*)(p.y + ((size_t)p.T * p.keep + t) * HIDDEN))[c];
+        h.x += v.x; h.y += v.y; h.z += v.z; h.w += v.w;
+    }
+    if (p.shared) {
+        const float4 v = ((const float4*)(p.shared + (size_t)t * HIDDEN))[c];
+        h.x += v.x; h.y += v.y; h.z += v.z; h.w += v.w;
+    }
+    h.x += r.x; h.y += r.y; h.z += r.z; h.w += r.w;
+    if (p.h) ((float4*)(p.h + (size_t)t * p.ld_out))[c] = h;
+}
+
+void launch_combine(const CombineParams& p, cudaStream_t st) {
+    const int n = p.T * (HIDDEN / 4);
+    k_combine<<<(n + 255) / 256, 256, 0, st>>>(p);
+}
+
+// ------------------------------------------------------------------ seeded weight generation
+// one CTA = 64 consecutive blocks of one expert matrix, staged in shared memory, written as 16-byte words
+__global__ void __launch_bounds__(64) k_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0,
+                                                int rows, int K, int64_t stride) {
+    __shared__ __align__(16) uint8_t buf[64 * BLK_IQ2];
+    const int e = expert0 + blockIdx.y;
+    const uint64_t key = iq2_gen_key(seed, (uint32_t)layer, (uint32_t)matrix, (uint32_t)e);
+    const int64_t nblk = (int64_t)rows * (K / QK);
+    const int64_t b0 = (int64_t)blockIdx.x * 64;
+    const int64_t b = b0 + threadIdx.x;
+    if (b < nblk) iq2_gen_block(key, (uint64_t)b, buf + threadIdx.x * BLK_IQ2);
+    __syncthreads();
+    uint8_t* out = dst + (size_t)blockIdx.y * stride + (size_t)b0 * BLK_IQ2;
+    const int nb = (int)(nblk - b0 < 64 ? nblk - b0 : 64);
+    const int bytes = nb * BLK_IQ2;
+    if (((uintptr_t)out & 15) == 0 && (bytes & 15) == 0) {
+        for (int i = threadIdx.x; i < bytes / 16; i += 64) ((uint4*)out)[i] = ((const uint4*)buf)[i];
+    } else {
+        for (int i = threadIdx.x; i < bytes; i += 64) out[i] = buf[i];
+    }
+}
+
+void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
+                    int64_t stride, cudaStream_t st) {
+    const int64_t nblk = (int64_t)rows * (K / QK);
+    dim3 grid((unsigned)((nblk + 63) / 64), (unsigned)n_exp);
+    k_gen_iq2<<<grid, 64, 0, st>>>(dst, seed, layer, matrix, expert0, rows, K, stride);
+}
+
+int num_sms(int device) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    return n;
+}
+
+}  // namespace lk

@@ -2,47 +2,26 @@
 //
 // Replaces tc_matvec<F_IQ2> + swiglu_q8 + the IQ2 down (reference src/fused_layer.cu:178-202, 334-341,
 // launched at :605-608 and :548-550).  Work is a list of slots (expert, up to NT tokens); a persistent
-// CTA walks (slot, row tile) tiles.  Per CTA:
-//   * one producer warp streams whole weight-row chunks (contiguous in the IQ2_XXS matrix) into a
+// CTA per SM walks (slot, row tile) tiles.  Per CTA:
+//   * one producer thread streams whole weight-row chunks (contiguous in the IQ2_XXS matrix) into a
 //     shared-memory ring with cp.async.bulk (1-D TMA) and mbarrier transaction counts;
-//   * each consumer thread owns one 32-weight group (column block) of K and keeps that group's q8
-//     activations of the slot's tokens in registers, so activations are read once per tile;
-//   * per row it decodes its group with lane-private shared-memory tables (grid magnitudes by 64-bit
-//     loads, sign selectors applied with one byte-permute per 4 weights) and dp4a's against the q8
-//     activations: exact int32 group sums, scaled by d * (2*scale+1) * dx (the 0.125 is applied after
-//     the reduction, exactly);
-//   * 32 (row, token) partials per thread are summed across the row's threads by a warp
-//     transpose-reduction and a fixed-order cross-warp sum (deterministic, no atomics).
-// gate/up: 224 consumers (= 7168/32 groups), tile = 32 h rows = 32 gate + 32 up rows (8 chunks of 8
-//   rows); the tile's SwiGLU and its q8 re-quantisation (per 32 rows, one tile) are fused in.
-// down: 256 consumers = 4 row streams x 64 groups (K = 2048), tile = 128 rows (4 chunks of 32 rows);
+//   * consumer threads each own one 32-weight group (column block) of K and keep that group's q8
+//     activations of the slot's tokens in registers; several consumer streams work on different chunks;
+//   * per row a thread decodes its group with the 64 KB lane-private selector table (moe_device.cuh:
+//     two conflict-free 32-bit lookups and two byte-permutes per 8 weights) and dp4a's the signed int8
+//     weights against the activations: exact int32 group sums, scaled by d * (2*scale+1) * dx (the
+//     format's 0.125 is applied after the reduction, exactly);
+//   * 8 (row, token) partials per thread are summed over the warp (warp_reduce8) and across the row's
+//     warps in a fixed order: deterministic, no atomics.
+// gate/up: 2 streams x 224 consumers (7168/32 groups), tile = 32 h rows = 32 gate + 32 up rows (8 chunks
+//   of 8 rows, even chunks to stream 0, odd to stream 1); SwiGLU and its q8 re-quantisation (per 32 rows
+//   = one tile) are fused in.
+// down: 8 streams x 64 consumers (2048/32 groups), tile = 64 rows (8 chunks of 8 rows, one per stream);
 //   output y[entry][row] = w * (W_down h)[row].
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
 namespace lk {
-
-// ------------------------------------------------------------------ gate / up
-constexpr int GU_CONS = HIDDEN / 32;                 // 224 consumer threads (7 warps)
-constexpr int GU_CWARPS = GU_CONS / 32;
-constexpr int GU_THREADS = GU_CONS + 32;             // + producer warp
-constexpr int GU_ROWB = (HIDDEN / QK) * BLK_IQ2;     // 1848 bytes per row
-constexpr int GU_CH_ROWS = 8;
-constexpr int GU_CH_BYTES = GU_CH_ROWS * GU_ROWB;    // 14784
-constexpr int GU_NST = 6;
-constexpr int GU_TILE = 32;                          // h rows per tile
-constexpr int GU_TILES_PER_SLOT = MOE_INTER / GU_TILE;   // 64
-constexpr int GU_CHUNKS = 2 * GU_TILE / GU_CH_ROWS;       // 8 per tile (4 gate, 4 up)
-
-constexpr int GU_OFF_GRID = 0;
-constexpr int GU_OFF_SIGN = GU_OFF_GRID + GRID_TAB_BYTES;
-constexpr int GU_OFF_RING = GU_OFF_SIGN + SIGN_TAB_BYTES;
-constexpr int GU_OFF_RED = GU_OFF_RING + GU_NST * GU_CH_BYTES;
-constexpr int GU_OFF_GS = GU_OFF_RED + 2 * GU_CWARPS * 32 * 4;
-constexpr int GU_OFF_US = GU_OFF_GS + GU_TILE * MAX_NT * 4;
-constexpr int GU_OFF_BAR = GU_OFF_US + GU_TILE * MAX_NT * 4;
-constexpr int GU_OFF_ABORT = GU_OFF_BAR + 2 * GU_NST * 8;
-constexpr int GU_SMEM = GU_OFF_ABORT + 16;
 
 __device__ __forceinline__ const uint8_t* slot_matrix(const ExpertParams& p, int e, int which) {
     // which: 0 gate, 1 up, 2 down
@@ -51,11 +30,70 @@ __device__ __forceinline__ const uint8_t* slot_matrix(const ExpertParams& p, int
          : which == 1 ? p.up + (size_t)e * p.up_stride : p.down + (size_t)e * p.down_stride;
 }
 
+// q8 of this thread's 32-wide group of token `tok`'s activation row (zeros for a pad member)
+__device__ __forceinline__ float load_q8_group(const float* x, int ld, int tok, int g, uint32_t (&xr)[8]) {
+    float xv[32];
+    if (tok >= 0) {
+        const float4* src = (const float4*)(x + (size_t)tok * ld + g * 32);
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) { const float4 v = src[j]; xv[4*j] = v.x; xv[4*j+1] = v.y; xv[4*j+2] = v.z; xv[4*j+3] = v.w; }
+    } else {
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) xv[j] = 0.0f;
+    }
+    int8_t q[32];
+    const float d = quant_q8_group(xv, q);
+    #pragma unroll
+    for (int j = 0; j < 8; ++j)
+        xr[j] = (uint32_t)(uint8_t)q[4*j] | ((uint32_t)(uint8_t)q[4*j+1] << 8) |
+                ((uint32_t)(uint8_t)q[4*j+2] << 16) | ((uint32_t)(uint8_t)q[4*j+3] << 24);
+    return d;
+}
+
+// one row of a staged chunk: this thread's group -> NT partials v[m]
+template <int NT>
+__device__ __forceinline__ void row_partials(const uint8_t* row, int goff, int boff, const uint32_t (&xr)[NT][8],
+                                             const float (&dx)[NT], const unsigned char* tab, uint32_t lane4,
+                                             float* v) {
+    uint32_t aux0, aux1;
+    load_group_smem(row, goff, aux0, aux1);
+    const float d = load_d_smem(row, boff);
+    int acc[NT];
+    #pragma unroll
+    for (int m = 0; m < NT; ++m) acc[m] = 0;
+    iq2_dot_sel<NT>(aux0, aux1, xr, acc, tab, lane4);
+    const int mult = (int)((aux1 >> 27) & 0x1Eu) + 1;          // 2*scale + 1
+    #pragma unroll
+    for (int m = 0; m < NT; ++m) v[m] = (float)(acc[m] * mult) * (d * dx[m]);
+}
+
+// ------------------------------------------------------------------ gate / up
+constexpr int GU_KG = HIDDEN / 32;                   // 224 groups = consumers per stream
+constexpr int GU_NS = 2;
+constexpr int GU_SW = GU_KG / 32;                    // 7 warps per stream
+constexpr int GU_CONS = GU_KG * GU_NS;               // 448
+constexpr int GU_THREADS = GU_CONS + 32;             // + producer warp
+constexpr int GU_ROWB = (HIDDEN / QK) * BLK_IQ2;     // 1848 bytes per row
+constexpr int GU_CH_ROWS = 8;
+constexpr int GU_CH_BYTES = GU_CH_ROWS * GU_ROWB;    // 14784
+constexpr int GU_TILE = 32;                          // h rows per tile
+constexpr int GU_CHUNKS = 2 * GU_TILE / GU_CH_ROWS;  // 8 per tile (0-3 gate, 4-7 up)
+constexpr int GU_NST = GU_CHUNKS;                    // one tile in flight: chunk c always uses stage c
+constexpr int GU_TILES_PER_SLOT = MOE_INTER / GU_TILE;   // 64
+
+constexpr int GU_OFF_TAB = 0;
+constexpr int GU_OFF_RING = GU_OFF_TAB + SEL_TAB_BYTES;
+constexpr int GU_OFF_RED = GU_OFF_RING + GU_NST * GU_CH_BYTES;
+constexpr int GU_OFF_GS = GU_OFF_RED + GU_NS * 2 * GU_SW * 32 * 4;
+constexpr int GU_OFF_US = GU_OFF_GS + 2 * GU_TILE * MAX_NT * 4;
+constexpr int GU_OFF_BAR = GU_OFF_US + 2 * GU_TILE * MAX_NT * 4;
+constexpr int GU_OFF_ABORT = GU_OFF_BAR + 2 * GU_NST * 8;
+constexpr int GU_SMEM = GU_OFF_ABORT + 16;
+
 template <int NT>
 __global__ void __launch_bounds__(GU_THREADS, 1) k_gate_up(ExpertParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint2* gtab = (uint2*)(smem + GU_OFF_GRID);
-    uint32_t* stab = (uint32_t*)(smem + GU_OFF_SIGN);
+    const unsigned char* tab = smem + GU_OFF_TAB;
     uint8_t* ring = smem + GU_OFF_RING;
     float* red = (float*)(smem + GU_OFF_RED);
     float* gs = (float*)(smem + GU_OFF_GS);
@@ -68,110 +106,95 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gate_up(ExpertParams p) {
     const int ntiles = nslots * GU_TILES_PER_SLOT;
     if ((int)blockIdx.x >= ntiles) return;
 
-    init_iq2_tables(gtab, stab, tid, GU_THREADS);
+    init_sel_table((uint32_t*)(smem + GU_OFF_TAB), tid, GU_THREADS);
     if (tid == 0) {
         *abort_flag = 0;
-        for (int s = 0; s < GU_NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], GU_CWARPS); }
+        for (int s = 0; s < GU_NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], GU_SW); }
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == GU_CWARPS) {                          // ---------------- producer
+    if (warp == GU_CONS / 32) {                       // ---------------- producer
         if (lane == 0) {
-            uint32_t it = 0; bool ok = true;
-            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            uint32_t it = 0;                          // copies issued; copy j uses stage j % 8 in phase j / 8
+            for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
                 const int s = tile % nslots, rt = tile / nslots;
                 const int e = p.slot_expert[s];
                 const uint8_t* g = slot_matrix(p, e, 0);
                 const uint8_t* u = slot_matrix(p, e, 1);
                 for (int c = 0; c < GU_CHUNKS; ++c, ++it) {
-                    const int st = it % GU_NST;
-                    if (!mbar_wait(&empty[st], ((it / GU_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                    if (*abort_flag || !mbar_wait(&empty[c], ((it / GU_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; goto drain; }
                     const uint8_t* src = (c < 4 ? g : u) + (size_t)(rt * GU_TILE + (c & 3) * GU_CH_ROWS) * GU_ROWB;
-                    mbar_arrive_expect_tx(&full[st], GU_CH_BYTES);
-                    bulk_g2s(ring + st * GU_CH_BYTES, src, GU_CH_BYTES, &full[st]);
+                    mbar_arrive_expect_tx(&full[c], GU_CH_BYTES);
+                    bulk_g2s(ring + c * GU_CH_BYTES, src, GU_CH_BYTES, &full[c]);
                 }
             }
-            // drain: every issued copy must land before the CTA may exit
-            const uint32_t first = it > GU_NST ? it - GU_NST : 0;
-            for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % GU_NST], (j / GU_NST) & 1, p.err, DEV_ERR_TIMEOUT_DRAIN);
+        drain:
+            {   // every issued copy must land before the CTA may exit
+                const uint32_t first = it > GU_NST ? it - GU_NST : 0;
+                for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % GU_NST], (j / GU_NST) & 1, nullptr, 0);
+            }
         }
         return;
     }
 
     // ---------------------------------------------------------------- consumers
-    const int g = tid;                                // K group owned by this thread
+    const int strm = tid / GU_KG, g = tid % GU_KG, sw = g >> 5;
     const int goff = 2 + BLK_IQ2 * (g >> 3) + 8 * (g & 7);
     const int boff = BLK_IQ2 * (g >> 3);
-    const uint2* gt = gtab + lane;
-    const uint32_t* stl = stab + lane;
-    constexpr int RB = 32 / NT;                       // rows per reduction batch
-    constexpr int NB = 2 * GU_TILE / RB;              // batches per tile
-    uint32_t it = 0; int rbuf = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const uint32_t lane4 = (uint32_t)lane << 2;
+    constexpr int RB = 8 / NT;                        // rows per reduction batch (8 values)
+    uint32_t xr[NT][8]; float dx[NT]; int xtok[NT];
+    #pragma unroll
+    for (int m = 0; m < NT; ++m) xtok[m] = -2;
+    uint32_t ti = 0; int ebuf = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++ti) {
         const int s = tile % nslots, rt = tile / nslots;
-        // this slot's tokens: q8 of this thread's 32-wide group, in registers
-        uint32_t xr[NT][8]; float dx[NT];
         #pragma unroll
         for (int m = 0; m < NT; ++m) {
             const int tok = p.slot_tok[s * NT + m];
-            float xv[32];
-            if (tok >= 0) {
-                const float4* src = (const float4*)(p.x + (size_t)tok * p.ld_x + g * 32);
-                #pragma unroll
-                for (int j = 0; j < 8; ++j) { const float4 v = src[j]; xv[4*j] = v.x; xv[4*j+1] = v.y; xv[4*j+2] = v.z; xv[4*j+3] = v.w; }
-            } else {
-                #pragma unroll
-                for (int j = 0; j < 32; ++j) xv[j] = 0.0f;
-            }
-            int8_t q[32];
-            dx[m] = quant_q8_group(xv, q);
-            #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                xr[m][j] = (uint32_t)(uint8_t)q[4*j] | ((uint32_t)(uint8_t)q[4*j+1] << 8) |
-                           ((uint32_t)(uint8_t)q[4*j+2] << 16) | ((uint32_t)(uint8_t)q[4*j+3] << 24);
+            if (tok != xtok[m]) { dx[m] = load_q8_group(p.x, p.ld_x, tok, g, xr[m]); xtok[m] = tok; }
         }
-        bool aborted = false;
-        for (int b = 0; b < NB; ++b) {
-            float v[32];
+        const int tb = ti & 1;
+        for (int e = 0; e < NT; ++e) {                // NT exchanges of 4 batches per stream and tile
+            float kept = 0.0f;
             #pragma unroll
-            for (int rr = 0; rr < RB; ++rr) {
-                const int trow = b * RB + rr;          // 0..63 within the tile (gate rows, then up rows)
-                const int rc = trow % GU_CH_ROWS;
-                if (rc == 0) { if (!mbar_wait(&full[it % GU_NST], (it / GU_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) *abort_flag = 1; }
-                const uint8_t* row = ring + (it % GU_NST) * GU_CH_BYTES + rc * GU_ROWB;
-                uint32_t aux0, aux1;
-                load_group_smem(row, goff, aux0, aux1);
-                const float f = load_d_smem(row, boff) * (float)(2 * (int)(aux1 >> 28) + 1);
+            for (int bb = 0; bb < 4; ++bb) {
+                const int b = e * 4 + bb;
+                const int r0 = b * RB;                // first row of the batch within this stream's 32 rows
+                const int ci = r0 >> 3, r8 = r0 & 7;
+                const int c = strm + GU_NS * ci;      // chunk (= stage) index in the tile
+                if (r8 == 0 && !*abort_flag && !mbar_wait(&full[c], ti & 1, p.err, DEV_ERR_TIMEOUT_FULL)) *abort_flag = 1;
+                const uint8_t* base = ring + c * GU_CH_BYTES + r8 * GU_ROWB;
+                float v[8];
                 #pragma unroll
-                for (int m = 0; m < NT; ++m) {
-                    const int isum = iq2_group_dot(aux0, aux1, xr[m], gt, stl);
-                    v[rr * NT + m] = (float)isum * (f * dx[m]);
-                }
-                if (rc == GU_CH_ROWS - 1) { __syncwarp(); if (lane == 0) mbar_arrive(&empty[it % GU_NST]); ++it; }
+                for (int rr = 0; rr < RB; ++rr) row_partials<NT>(base + rr * GU_ROWB, goff, boff, xr, dx, tab, lane4, v + rr * NT);
+                if (r8 + RB == GU_CH_ROWS) { __syncwarp(); if (lane == 0) mbar_arrive(&empty[c]); }
+                const float r = warp_reduce8(v, lane);
+                if ((lane & 3) == bb) kept = r;
             }
-            const float tot = warp_transpose_reduce32(v, lane);
-            float* rb_ = red + rbuf * GU_CWARPS * 32;
-            rb_[warp * 32 + lane] = tot;
-            named_bar_sync(1, GU_CONS);
-            if (*abort_flag) { aborted = true; break; }   // every consumer warp sees the same flag here
-            if (warp == 0) {
-                float a = rb_[lane];
+            float* rb = red + ((strm * 2 + ebuf) * GU_SW) * 32;
+            rb[sw * 32 + lane] = kept;
+            named_bar_sync(1 + strm, GU_KG);
+            if (sw == 0) {
+                float a = rb[lane];
                 #pragma unroll
-                for (int w = 1; w < GU_CWARPS; ++w) a += rb_[w * 32 + lane];
-                const int rr = lane / NT, m = lane % NT;
-                const int trow = b * RB + rr;
-                if (trow < GU_TILE) gs[trow * MAX_NT + m] = a * 0.125f;
-                else us[(trow - GU_TILE) * MAX_NT + m] = a * 0.125f;
+                for (int w = 1; w < GU_SW; ++w) a += rb[w * 32 + lane];
+                const int b = e * 4 + (lane & 3), vi = lane >> 2;
+                const int row_s = b * RB + vi / NT, m = vi % NT;
+                const int c = strm + GU_NS * (row_s >> 3);
+                const int hrow = (c & 3) * GU_CH_ROWS + (row_s & 7);
+                float* dst = c < 4 ? gs : us;
+                dst[(tb * GU_TILE + hrow) * MAX_NT + m] = a * 0.125f;
             }
-            rbuf ^= 1;
+            ebuf ^= 1;
         }
-        if (aborted) break;
-        named_bar_sync(1, GU_CONS);
+        named_bar_sync(1 + GU_NS, GU_CONS);
+        if (*abort_flag) break;                       // every consumer warp sees the same flag here
         // SwiGLU + q8 per 32 rows (this tile), one warp per token
-        for (int m = warp; m < NT; m += GU_CWARPS) {
+        for (int m = warp; m < NT; m += GU_CONS / 32) {
             const int out = p.slot_out[s * NT + m];
-            const float hv = lk_swiglu(gs[lane * MAX_NT + m], us[lane * MAX_NT + m]);
+            const float hv = lk_swiglu(gs[(tb * GU_TILE + lane) * MAX_NT + m], us[(tb * GU_TILE + lane) * MAX_NT + m]);
             float amax = fabsf(hv);
             #pragma unroll
             for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
@@ -185,81 +208,79 @@ __global__ void __launch_bounds__(GU_THREADS, 1) k_gate_up(ExpertParams p) {
 }
 
 // ------------------------------------------------------------------ down
-constexpr int DN_GROUPS = MOE_INTER / 32;            // 64 groups per row
-constexpr int DN_STREAMS = 4;
-constexpr int DN_CONS = DN_GROUPS * DN_STREAMS;      // 256 consumers (8 warps)
-constexpr int DN_CWARPS = DN_CONS / 32;
+constexpr int DN_KG = MOE_INTER / 32;                // 64 groups per row = consumers per stream
+constexpr int DN_NS = 8;
+constexpr int DN_CONS = DN_KG * DN_NS;               // 512
 constexpr int DN_THREADS = DN_CONS + 32;
 constexpr int DN_ROWB = (MOE_INTER / QK) * BLK_IQ2;  // 528
-constexpr int DN_CH_ROWS = 32;
-constexpr int DN_CH_BYTES = DN_CH_ROWS * DN_ROWB;    // 16896
-constexpr int DN_NST = 5;
-constexpr int DN_TILE = 128;
-constexpr int DN_CHUNKS = DN_TILE / DN_CH_ROWS;      // 4
-constexpr int DN_TILES_PER_SLOT = HIDDEN / DN_TILE;  // 56
-constexpr int DN_SROWS = DN_CH_ROWS / DN_STREAMS;    // 8 rows of each chunk per stream
+constexpr int DN_CH_ROWS = 8;
+constexpr int DN_CH_BYTES = DN_CH_ROWS * DN_ROWB;    // 4224
+constexpr int DN_TILE = DN_CH_ROWS * DN_NS;          // 64 rows: chunk c -> stream c
+constexpr int DN_DEPTH = 3;                          // tiles in flight
+constexpr int DN_NST = DN_NS * DN_DEPTH;
+constexpr int DN_TILES_PER_SLOT = HIDDEN / DN_TILE;  // 112
 
-constexpr int DN_OFF_GRID = 0;
-constexpr int DN_OFF_SIGN = DN_OFF_GRID + GRID_TAB_BYTES;
-constexpr int DN_OFF_RING = DN_OFF_SIGN + SIGN_TAB_BYTES;
+constexpr int DN_OFF_TAB = 0;
+constexpr int DN_OFF_RING = DN_OFF_TAB + SEL_TAB_BYTES;
 constexpr int DN_OFF_RED = DN_OFF_RING + DN_NST * DN_CH_BYTES;
-constexpr int DN_OFF_BAR = DN_OFF_RED + 2 * DN_CWARPS * 32 * 4;
+constexpr int DN_OFF_BAR = DN_OFF_RED + DN_NS * 2 * 2 * 8 * 4;
 constexpr int DN_OFF_ABORT = DN_OFF_BAR + 2 * DN_NST * 8;
-constexpr int DN_SMEM = DN_OFF_ABORT + 16;
+constexpr int DN_OFF_LAST = DN_OFF_ABORT + 16;
+constexpr int DN_SMEM = DN_OFF_LAST + DN_NS * 4;
 
 template <int NT>
 __global__ void __launch_bounds__(DN_THREADS, 1) k_down(ExpertParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint2* gtab = (uint2*)(smem + DN_OFF_GRID);
-    uint32_t* stab = (uint32_t*)(smem + DN_OFF_SIGN);
+    const unsigned char* tab = smem + DN_OFF_TAB;
     uint8_t* ring = smem + DN_OFF_RING;
     float* red = (float*)(smem + DN_OFF_RED);
     uint64_t* full = (uint64_t*)(smem + DN_OFF_BAR);
     uint64_t* empty = full + DN_NST;
     volatile int* abort_flag = (volatile int*)(smem + DN_OFF_ABORT);
+    volatile int* lastflag = (volatile int*)(smem + DN_OFF_LAST);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nslots = *p.nslots;
     const int ntiles = nslots * DN_TILES_PER_SLOT;
     if ((int)blockIdx.x >= ntiles) return;
 
-    init_iq2_tables(gtab, stab, tid, DN_THREADS);
+    init_sel_table((uint32_t*)(smem + DN_OFF_TAB), tid, DN_THREADS);
     if (tid == 0) {
         *abort_flag = 0;
-        for (int s = 0; s < DN_NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], DN_CWARPS); }
+        for (int s = 0; s < DN_NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 2); }
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == DN_CWARPS) {                          // ---------------- producer
+    if (warp == DN_CONS / 32) {                       // ---------------- producer
         if (lane == 0) {
-            uint32_t it = 0; bool ok = true;
-            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            uint32_t it = 0;
+            for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
                 const int s = tile % nslots, rt = tile / nslots;
                 const uint8_t* dw = slot_matrix(p, p.slot_expert[s], 2);
-                for (int c = 0; c < DN_CHUNKS; ++c, ++it) {
+                for (int c = 0; c < DN_NS; ++c, ++it) {
                     const int st = it % DN_NST;
-                    if (!mbar_wait(&empty[st], ((it / DN_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { ok = false; break; }
+                    if (*abort_flag || !mbar_wait(&empty[st], ((it / DN_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; goto drain; }
                     const uint8_t* src = dw + (size_t)(rt * DN_TILE + c * DN_CH_ROWS) * DN_ROWB;
                     mbar_arrive_expect_tx(&full[st], DN_CH_BYTES);
                     bulk_g2s(ring + st * DN_CH_BYTES, src, DN_CH_BYTES, &full[st]);
                 }
             }
-            const uint32_t first = it > DN_NST ? it - DN_NST : 0;
-            for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % DN_NST], (j / DN_NST) & 1, p.err, DEV_ERR_TIMEOUT_DRAIN);
+        drain:
+            {
+                const uint32_t first = it > DN_NST ? it - DN_NST : 0;
+                for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % DN_NST], (j / DN_NST) & 1, nullptr, 0);
+            }
         }
         return;
     }
 
-    const int strm = tid / DN_GROUPS, g = tid % DN_GROUPS;
+    const int strm = tid / DN_KG, g = tid % DN_KG, hw = (tid >> 5) & 1;
     const int goff = 2 + BLK_IQ2 * (g >> 3) + 8 * (g & 7);
     const int boff = BLK_IQ2 * (g >> 3);
-    const uint2* gt = gtab + lane;
-    const uint32_t* stl = stab + lane;
-    constexpr int RB = 32 / NT;                       // rows per reduction batch (per stream)
-    constexpr int ROWS_PER_STREAM = DN_TILE / DN_STREAMS;   // 32
-    constexpr int NB = ROWS_PER_STREAM / RB;
-    uint32_t it = 0; int rbuf = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const uint32_t lane4 = (uint32_t)lane << 2;
+    constexpr int RB = 8 / NT;
+    int ebuf = 0; uint32_t ti = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++ti) {
         const int s = tile % nslots, rt = tile / nslots;
         uint32_t xr[NT][8]; float dx[NT]; float wm[NT]; int outm[NT];
         #pragma unroll
@@ -278,43 +299,61 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(ExpertParams p) {
                 dx[m] = 0.0f;
             }
         }
+        const uint32_t it = ti * DN_NS + strm;
+        const int st = it % DN_NST;
+        if (!*abort_flag && !mbar_wait(&full[st], (it / DN_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) *abort_flag = 1;
+        const uint8_t* base = ring + st * DN_CH_BYTES;
         bool aborted = false;
-        for (int b = 0; b < NB; ++b) {
-            float v[32];
+        for (int b = 0; b < NT; ++b) {                // NT batches of RB rows (8 values each)
+            float v[8];
             #pragma unroll
-            for (int rr = 0; rr < RB; ++rr) {
-                const int srow = b * RB + rr;         // 0..31 within this stream's share of the tile
-                const int ri = srow % DN_SROWS;
-                if (ri == 0) { if (!mbar_wait(&full[it % DN_NST], (it / DN_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) *abort_flag = 1; }
-                const uint8_t* row = ring + (it % DN_NST) * DN_CH_BYTES + (strm * DN_SROWS + ri) * DN_ROWB;
-                uint32_t aux0, aux1;
-                load_group_smem(row, goff, aux0, aux1);
-                const float f = load_d_smem(row, boff) * (float)(2 * (int)(aux1 >> 28) + 1);
-                #pragma unroll
-                for (int m = 0; m < NT; ++m) {
-                    const int isum = iq2_group_dot(aux0, aux1, xr[m], gt, stl);
-                    v[rr * NT + m] = (float)isum * (f * dx[m]);
-                }
-                if (ri == DN_SROWS - 1) { __syncwarp(); if (lane == 0) mbar_arrive(&empty[it % DN_NST]); ++it; }
-            }
-            const float tot = warp_transpose_reduce32(v, lane);
-            float* rb_ = red + rbuf * DN_CWARPS * 32;
-            rb_[warp * 32 + lane] = tot;
-            named_bar_sync(1, DN_CONS);
-            if (*abort_flag) { aborted = true; break; }
-            if ((warp & 1) == 0) {                    // first warp of each stream: combine its 2 warps
-                const float a = rb_[warp * 32 + lane] + rb_[(warp + 1) * 32 + lane];
+            for (int rr = 0; rr < RB; ++rr) row_partials<NT>(base + (b * RB + rr) * DN_ROWB, goff, boff, xr, dx, tab, lane4, v + rr * NT);
+            if (b == NT - 1) { __syncwarp(); if (lane == 0) mbar_arrive(&empty[st]); }
+            const float r = warp_reduce8(v, lane);
+            float* rb = red + ((strm * 2 + ebuf) * 2) * 8;
+            if ((lane & 3) == 0) rb[hw * 8 + (lane >> 2)] = r;
+            named_bar_sync(1 + strm, DN_KG);
+            if (*abort_flag) { aborted = true; break; }  // both warps of the stream see the same flag
+            if (hw == 0 && lane < 8) {
+                const float a = rb[lane] + rb[8 + lane];
                 const int rr = lane / NT, m = lane % NT;
-                const int srow = b * RB + rr;
-                const int row = rt * DN_TILE + (srow / DN_SROWS) * DN_CH_ROWS + strm * DN_SROWS + (srow % DN_SROWS);
+                const int row = rt * DN_TILE + strm * DN_CH_ROWS + b * RB + rr;
                 float wv = 0.0f; int ov = -1;
                 #pragma unroll
                 for (int k = 0; k < NT; ++k) if (k == m) { wv = wm[k]; ov = outm[k]; }
                 if (ov >= 0) p.y[(size_t)ov * HIDDEN + row] = wv * (a * 0.125f);
             }
-            rbuf ^= 1;
+            ebuf ^= 1;
         }
         if (aborted) break;
+        if (p.chunk_count) {                          // fused combine: count this slot's chunk in
+            if (hw == 0) {
+                __threadfence();                      // this lane's y stores before the count
+                __syncwarp();
+                if (lane == 0) {
+                    const int old = atomicAdd(&p.chunk_count[rt * DN_NS + strm], 1);
+                    lastflag[strm] = old == nslots - 1;
+                }
+            }
+            named_bar_sync(1 + strm, DN_KG);
+            if (lastflag[strm]) {                     // every slot has written these 8 rows: combine them
+                __threadfence();
+                const int r0 = rt * DN_TILE + strm * DN_CH_ROWS;
+                for (int i = g; i < DN_CH_ROWS * p.T; i += DN_KG) {
+                    const int row = r0 + (i & 7), t = i >> 3;
+                    float m = 0.0f;
+                    for (int k = 0; k < p.keep; ++k) m += __ldcg(p.y + ((size_t)t * p.keep + k) * HIDDEN + row);
+                    if (p.moe) p.moe[(size_t)t * HIDDEN + row] = m;
+                    if (p.h) {
+                        float hv = p.resid[(size_t)t * HIDDEN + row];
+                        if (p.with_shared) hv += __ldcg(p.y + ((size_t)p.T * p.keep + t) * HIDDEN + row);
+                        if (p.shared_sep) hv += p.shared_sep[(size_t)t * HIDDEN + row];
+                        p.h[(size_t)t * HIDDEN + row] = hv + m;
+                    }
+                }
+                if (g == 0) p.chunk_count[rt * DN_NS + strm] = 0;   // ready for the next call
+            }
+        }
     }
 }
 
@@ -330,9 +369,12 @@ template <int NT> static void dn_launch(const ExpertParams& p, int grid, cudaStr
     k_down<NT><<<grid, DN_THREADS, DN_SMEM, st>>>(p);
 }
 
+void launch_gate_up1(const ExpertParams& p, int grid, cudaStream_t st);   // expert_gemv1.cu (one token)
+void launch_down1(const ExpertParams& p, int grid, cudaStream_t st);
+
 void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st) {
     switch (nt) {
-        case 1: gu_launch<1>(p, grid, st); break;
+        case 1: gu_launch<1>(p, grid, st); break;          // (the per-row variant measured slower at one token)
         case 2: gu_launch<2>(p, grid, st); break;
         case 4: gu_launch<4>(p, grid, st); break;
         default: gu_launch<8>(p, grid, st); break;
@@ -340,76 +382,11 @@ void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st) {
 }
 void launch_down(const ExpertParams& p, int nt, int grid, cudaStream_t st) {
     switch (nt) {
-        case 1: dn_launch<1>(p, grid, st); break;
+        case 1: launch_down1(p, grid, st); break;
         case 2: dn_launch<2>(p, grid, st); break;
         case 4: dn_launch<4>(p, grid, st); break;
         default: dn_launch<8>(p, grid, st); break;
     }
-}
-
-// ------------------------------------------------------------------ combine
-__global__ void k_combine(CombineParams p) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;       // float4 index over T x HIDDEN
-    const int per = HIDDEN / 4;
-    if (i >= p.T * per) return;
-    const int t = i / per, c = i % per;
-    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < p.keep; ++k) {
-        const float4 v = ((const float4*)(p.y + ((size_t)t * p.keep + k) * HIDDEN))[c];
-        r.x += v.x; r.y += v.y; r.z += v.z; r.w += v.w;
-    }
-    if (p.moe) ((float4*)(p.moe + (size_t)t * p.ld_out))[c] = r;
-    float4 h = ((const float4*)(p.resid + (size_t)t * p.ld_out))[c];
-    if (p.with_shared) {
-        const float4 v = ((const float4*)(p.y + ((size_t)p.T * p.keep + t) * HIDDEN))[c];
-        h.x += v.x; h.y += v.y; h.z += v.z; h.w += v.w;
-    }
-    if (p.shared) {
-        const float4 v = ((const float4*)(p.shared + (size_t)t * HIDDEN))[c];
-        h.x += v.x; h.y += v.y; h.z += v.z; h.w += v.w;
-    }
-    h.x += r.x; h.y += r.y; h.z += r.z; h.w += r.w;
-    if (p.h) ((float4*)(p.h + (size_t)t * p.ld_out))[c] = h;
-}
-
-void launch_combine(const CombineParams& p, cudaStream_t st) {
-    const int n = p.T * (HIDDEN / 4);
-    k_combine<<<(n + 255) / 256, 256, 0, st>>>(p);
-}
-
-// ------------------------------------------------------------------ seeded weight generation
-// one CTA = 64 consecutive blocks of one expert matrix, staged in shared memory, written as 16-byte words
-__global__ void __launch_bounds__(64) k_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0,
-                                                int rows, int K, int64_t stride) {
-    __shared__ __align__(16) uint8_t buf[64 * BLK_IQ2];
-    const int e = expert0 + blockIdx.y;
-    const uint64_t key = iq2_gen_key(seed, (uint32_t)layer, (uint32_t)matrix, (uint32_t)e);
-    const int64_t nblk = (int64_t)rows * (K / QK);
-    const int64_t b0 = (int64_t)blockIdx.x * 64;
-    const int64_t b = b0 + threadIdx.x;
-    if (b < nblk) iq2_gen_block(key, (uint64_t)b, buf + threadIdx.x * BLK_IQ2);
-    __syncthreads();
-    uint8_t* out = dst + (size_t)blockIdx.y * stride + (size_t)b0 * BLK_IQ2;
-    const int nb = (int)(nblk - b0 < 64 ? nblk - b0 : 64);
-    const int bytes = nb * BLK_IQ2;
-    if (((uintptr_t)out & 15) == 0 && (bytes & 15) == 0) {
-        for (int i = threadIdx.x; i < bytes / 16; i += 64) ((uint4*)out)[i] = ((const uint4*)buf)[i];
-    } else {
-        for (int i = threadIdx.x; i < bytes; i += 64) out[i] = buf[i];
-    }
-}
-
-void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
-                    int64_t stride, cudaStream_t st) {
-    const int64_t nblk = (int64_t)rows * (K / QK);
-    dim3 grid((unsigned)((nblk + 63) / 64), (unsigned)n_exp);
-    k_gen_iq2<<<grid, 64, 0, st>>>(dst, seed, layer, matrix, expert0, rows, K, stride);
-}
-
-int num_sms(int device) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
-    return n;
 }
 
 }  // namespace lk

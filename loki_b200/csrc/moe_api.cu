@@ -20,7 +20,7 @@ struct LkMoeCtx {
     int* slot_expert = nullptr; int* slot_tok = nullptr; int* slot_out = nullptr; float* slot_w = nullptr;
     int* nslots = nullptr; int max_slots = 0;
     int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
-    int* err = nullptr;
+    int* err = nullptr; int* tile_count = nullptr; int* chunk_count = nullptr;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     char msg[256] = {0};
 };
@@ -89,6 +89,10 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LK_CU(dalloc(&c->y, rows * HIDDEN));
     LK_CU(dalloc(&c->err, 1));
     LK_CU(cudaMemset(c->err, 0, sizeof(int)));
+    LK_CU(dalloc(&c->tile_count, (T + 7) / 8));
+    LK_CU(cudaMemset(c->tile_count, 0, (size_t)((T + 7) / 8) * sizeof(int)));
+    LK_CU(dalloc(&c->chunk_count, HIDDEN / 8));
+    LK_CU(cudaMemset(c->chunk_count, 0, (size_t)(HIDDEN / 8) * sizeof(int)));
     LK_CU(cudaMemset(c->y, 0, rows * HIDDEN * sizeof(float)));
     LK_CU(cudaDeviceSynchronize());
     cudaSetDevice(prev);
@@ -99,7 +103,7 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
 void lk_moe_destroy(LkMoeCtx* c) {
     if (!c) return;
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
-                     c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err };
+                     c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->chunk_count };
     for (void* p : ptrs) if (p) cudaFree(p);
     delete c;
 }
@@ -124,7 +128,7 @@ static RouterParams router_params(LkMoeCtx* c, const LkMoeWeights* W, const floa
     RouterParams p{};
     p.x = x; p.T = T; p.ld_x = HIDDEN; p.W = W->router_w; p.w_f16 = W->router_w_f16;
     p.logits_override = logits_override; p.bias = W->router_bias;
-    p.logits = c->logits; p.probs = c->probs; p.sel = sel; p.w = w;
+    p.logits = c->logits; p.probs = c->probs; p.sel = sel; p.w = w; p.tile_count = c->tile_count;
     p.n_experts = c->cfg.n_experts; p.topk = c->cfg.topk; p.keep = c->cfg.keep; p.renorm = c->cfg.renorm;
     p.n_group = c->cfg.n_group; p.topk_group = c->cfg.topk_group; p.scale = c->cfg.scale;
     if (decode_slots) {
@@ -173,18 +177,16 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const
     e.x = x; e.ld_x = HIDDEN;
     e.slot_expert = c->slot_expert; e.slot_tok = c->slot_tok; e.slot_out = c->slot_out; e.slot_w = c->slot_w; e.nslots = c->nslots;
     e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err;
+    if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
+    if (h || moe) {                   // the combine runs inside the down kernel
+        e.chunk_count = c->chunk_count; e.resid = resid; e.shared_sep = nullptr; e.h = h; e.moe = moe;
+        e.T = T; e.keep = keep; e.with_shared = c->cfg.with_shared;
+    }
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
     if (c->ev[1]) LK_CU(record_event(c->ev[1], st));
     launch_down(e, nt, c->nsm, st);
     if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
-    CombineParams cp{};
-    cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared;
-    cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN;
-    if (h || moe) {
-        if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
-        launch_combine(cp, st);
-    }
     if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
     LK_CU(cudaGetLastError());
     return LK_OK;

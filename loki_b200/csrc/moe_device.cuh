@@ -68,54 +68,76 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
 }
 
-// ---- IQ2_XXS tables in shared memory (lane-private layouts)
-//  grid:  uint2 gt[256][32]  (64 KB): entry i, lane l = the 8 magnitudes of grid[i] (x: elements 0-3, y: 4-7)
-//  signs: uint32 st[128][32] (16 KB): byte-permute selectors that pick, per element, the magnitude (nibble j)
-//         or its negation (nibble 4+j) for the 8 sign bits ksigns(i): low 16 bits elements 0-3, high 16 bits 4-7
-constexpr int GRID_TAB_BYTES = 256 * 32 * 8;
-constexpr int SIGN_TAB_BYTES = 128 * 32 * 4;
+// ---- IQ2_XXS decode table in shared memory: 64 KB, lane-private, one 256-byte row per index i:
+//   bytes [0, 128):   grid selector of grid entry i for lanes 0..31 (4 bytes each)
+//   bytes [128, 256): sign selector of sign index i (i < 128) for lanes 0..31
+//   grid selector: nibble j (bits 4j..4j+3, j < 4) = code of element j (0, 1, 2 for magnitude 8, 25, 43);
+//                  bits 16 + 4j the same for element 4 + j.
+//   sign selector: bit 2 of the same nibbles = sign bit of that element (ksigns(i), bit 7 = parity).
+//   (grid | sign) is then a byte-permute selector over the constant pair (POS, NEG): nibble c + 4s picks
+//   magnitude c with sign s, so one prmt yields 4 signed int8 weights.  Lane-private rows make every
+//   data-dependent lookup of a warp hit 32 distinct banks; the lane offset rides in the same prmt that
+//   extracts the grid index (address = idx << 8 | lane << 2).
+constexpr int SEL_TAB_BYTES = 256 * 256;
+constexpr uint32_t IQ2_POS = 0x002B1908u;   // bytes: 8, 25, 43, 0
+constexpr uint32_t IQ2_NEG = 0x00D5E7F8u;   // bytes: -8, -25, -43, 0
 
 static __constant__ uint64_t c_iq2_grid[256] = {
 #include "iq2_grid.inc"
 };
 
-__device__ __forceinline__ uint32_t sign_selectors(uint32_t si) {
-    const uint32_t s = iq2_ksigns(si);
-    uint32_t lo = 0, hi = 0;
+__device__ __forceinline__ uint32_t grid_selector(uint64_t g) {
+    uint32_t s = 0;
     #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        lo |= (uint32_t)(j + 4 * ((s >> j) & 1u)) << (4 * j);
-        hi |= (uint32_t)(j + 4 * ((s >> (4 + j)) & 1u)) << (4 * j);
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t m = (uint32_t)(g >> (8 * j)) & 0xFFu;
+        const uint32_t code = m == 0x08u ? 0u : (m == 0x19u ? 1u : 2u);
+        s |= code << ((j < 4 ? 0 : 16) + 4 * (j & 3));
     }
-    return lo | (hi << 16);
+    return s;
 }
-
-__device__ __forceinline__ void init_iq2_tables(uint2* gt, uint32_t* st, int tid, int nthr) {
-    for (int i = tid; i < 256 * 32; i += nthr) {
-        const uint64_t v = c_iq2_grid[i >> 5];
-        gt[i] = make_uint2((uint32_t)v, (uint32_t)(v >> 32));
+__device__ __forceinline__ uint32_t sign_selector(uint32_t si) {
+    const uint32_t k = iq2_ksigns(si);
+    uint32_t s = 0;
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) s |= ((k >> j) & 1u) << ((j < 4 ? 0 : 16) + 4 * (j & 3) + 2);
+    return s;
+}
+// each selector is computed once (thread t: grid entry t, or sign index t - 256) and written to its 32
+// lane copies with 16-byte stores; a thread starts at chunk t % 8 so the 8 lanes of a store wavefront hit
+// distinct banks
+__device__ __forceinline__ void init_sel_table(uint32_t* tab, int tid, int nthr) {
+    for (int t = tid; t < 256 + 128; t += nthr) {
+        const uint32_t v = t < 256 ? grid_selector(c_iq2_grid[t]) : sign_selector((uint32_t)(t - 256));
+        uint4* row = (uint4*)(tab + (t < 256 ? t * 64 : (t - 256) * 64 + 32));
+        const uint4 q = make_uint4(v, v, v, v);
+        #pragma unroll
+        for (int k = 0; k < 8; ++k) row[(k + t) & 7] = q;
     }
-    for (int i = tid; i < 128 * 32; i += nthr) st[i] = sign_selectors((uint32_t)(i >> 5));
 }
 
-// signed int8 x4 of one half sub-group: magnitudes m (bytes 8/25/43) with per-byte negation chosen by sel
-__device__ __forceinline__ uint32_t apply_signs(uint32_t m, uint32_t sel) {
-    return __byte_perm(m, 0x01010100u - m, sel);   // 0x01010100 - m = bytewise -m (all m bytes are >= 8)
-}
-
-// integer dot of one IQ2_XXS group (aux0 = 4 grid indices, aux1 = 4 sign indices | scale<<28) with the
-// 32 q8 activations x[0..8) (4 bytes per word); gt/st point at this lane's column of the tables
-__device__ __forceinline__ int iq2_group_dot(uint32_t aux0, uint32_t aux1, const uint32_t* x,
-                                             const uint2* gt, const uint32_t* st) {
-    int acc = 0;
+// integer dots of one IQ2_XXS group (aux0 = 4 grid indices, aux1 = 4 sign indices | scale << 28) with
+// the 32 q8 activations of NT tokens (x[t][0..8), 4 int8 per word); tab = the shared table,
+// lane4 = lane << 2.  acc[t] receives the exact int32 sums.
+template <int NT>
+__device__ __forceinline__ void iq2_dot_sel(uint32_t aux0, uint32_t aux1, const uint32_t (&x)[NT][8], int (&acc)[NT],
+                                            const unsigned char* tab, uint32_t lane4) {
+    const uint32_t a1s = aux1 >> 13;
+    const uint32_t so = 128u | lane4;
+    const uint32_t sa[4] = { ((aux1 << 8) & 0x7F00u) | so, ((aux1 << 1) & 0x7F00u) | so,
+                             ((a1s << 7) & 0x7F00u) | so, (a1s & 0x7F00u) | so };
     #pragma unroll
     for (int l = 0; l < 4; ++l) {
-        const uint2 m = gt[((aux0 >> (8 * l)) & 0xFFu) * 32];
-        const uint32_t sel = st[((aux1 >> (7 * l)) & 0x7Fu) * 32];
-        acc = __dp4a((int)apply_signs(m.x, sel), (int)x[2 * l], acc);
-        acc = __dp4a((int)apply_signs(m.y, sel >> 16), (int)x[2 * l + 1], acc);
+        const uint32_t ga = __byte_perm(aux0, lane4, 0x6504u | (uint32_t)(l << 4));
+        const uint32_t sel = *(const uint32_t*)(tab + ga) | *(const uint32_t*)(tab + sa[l]);
+        const uint32_t vlo = __byte_perm(IQ2_POS, IQ2_NEG, sel);
+        const uint32_t vhi = __byte_perm(IQ2_POS, IQ2_NEG, sel >> 16);
+        #pragma unroll
+        for (int t = 0; t < NT; ++t) {
+            acc[t] = __dp4a((int)vlo, (int)x[t][2 * l], acc[t]);
+            acc[t] = __dp4a((int)vhi, (int)x[t][2 * l + 1], acc[t]);
+        }
     }
-    return acc;
 }
 
 // the 8 bytes of IQ2 group `g` of a row staged in shared memory (row start 4-byte aligned): the group
@@ -131,20 +153,24 @@ __device__ __forceinline__ float load_d_smem(const uint8_t* row, int boff) {
     return __half2float(*(const __half*)(row + boff));
 }
 
-// warp transpose-reduction of 32 values per lane: on return v[0] of lane l = sum over the warp's lanes
-// of their v[l] (fixed order: butterfly halves 16, 8, 4, 2, 1)
-__device__ __forceinline__ float warp_transpose_reduce32(float (&v)[32], int lane) {
+// warp reduction of 8 values per lane: on return every lane holds the warp-wide sum of v[i] for
+// i = 4*bit4 + 2*bit3 + bit2 of its lane id (the 4 lanes sharing bits 4..2 hold the same value).
+// Fixed order: halving exchanges over lane offsets 16, 8, 4, then butterflies over 2 and 1.
+__device__ __forceinline__ float warp_reduce8(float (&v)[8], int lane) {
     #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
+    for (int o = 16, h = 4; o >= 4; o >>= 1, h >>= 1) {
         const bool up = (lane & o) != 0;
         #pragma unroll
-        for (int i = 0; i < o; ++i) {
-            const float send = up ? v[i] : v[i + o];
-            const float keep = up ? v[i + o] : v[i];
+        for (int i = 0; i < h; ++i) {
+            const float send = up ? v[i] : v[i + h];
+            const float keep = up ? v[i + h] : v[i];
             v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
         }
     }
-    return v[0];
+    float r = v[0];
+    r += __shfl_xor_sync(0xffffffffu, r, 2);
+    r += __shfl_xor_sync(0xffffffffu, r, 1);
+    return r;
 }
 
 }  // namespace lk

@@ -21,6 +21,7 @@ struct RouterParams {
     int n_experts, topk, keep, renorm, n_group, topk_group; float scale;
     // optional slot table written directly for T == 1 (decode): keep routed slots + shared slot
     int* slot_expert; int* slot_tok; int* slot_out; float* slot_w; int* nslots; int with_shared;
+    int* tile_count;                        // ceil(T/8) zeroed counters (last-CTA-done top-k)
 };
 void launch_router(const RouterParams& p, cudaStream_t st);
 
@@ -48,6 +49,11 @@ struct ExpertParams {
     int8_t* hq; float* hd;                            // SwiGLU output q8: [rows][MOE_INTER], scales [rows][MOE_INTER/32]
     float* y;                                         // weighted expert outputs [rows][HIDDEN]
     int* err;
+    // combine fused into the down kernel (used when chunk_count is set): the last slot to finish an 8-row
+    // chunk of the output writes h = resid + shared + sum_k y[t*keep+k], moe = sum_k y[t*keep+k] for those
+    // rows of all T tokens (shared = y rows T*keep + t when with_shared, and/or the shared_sep rows)
+    int* chunk_count;                                 // HIDDEN/8 zeroed counters (left zeroed)
+    const float* resid; const float* shared_sep; float* h; float* moe; int T; int keep; int with_shared;
 };
 void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st);
 void launch_down(const ExpertParams& p, int nt, int grid, cudaStream_t st);

@@ -1,12 +1,14 @@
 // router.cu -- the DeepSeek-R1 router on sm_100a.
 //
 // k_router_logits: logits[t][e] = W[e] . x[t] (fp32 or fp16 weights), then probs = sigmoid(logits or an
-//   override).  Replaces router_probs (reference src/fused_layer.cu:314-322).  One CTA = 2 experts x a
-//   tile of tokens; 128 threads per expert each own the float4 chunks c = p, p+128, ... of the row
-//   (fmaf over the 4 components in order), then a warp xor-butterfly and (s0+s1)+(s2+s3) across the 4
-//   warps.  The order is fixed and restated by the oracle (orc_router_logits), so probabilities -- and
-//   with them the selected experts -- are bit-identical to it.  Weights are streamed once per token tile.
-// k_router_topk: one warp per token: top-k of p + bias with ties to the lower expert id (reference
+//   override).  Replaces router_probs (reference src/fused_layer.cu:314-322).  One CTA = one expert x a
+//   tile of up to 8 tokens; 256 threads each own the float4 chunks c = tid, tid+256, ... of the row (all
+//   loads in flight at once; fmaf over the 4 components in order), then a warp xor-butterfly and
+//   ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)) across the 8 warps.  The order is fixed and restated by the oracle
+//   (orc_router_logits), so probabilities -- and with them the selected experts -- are bit-identical to it.
+//   The last CTA to finish a token tile (an atomic count after a fence) runs the top-k for it, so the
+//   router is one launch.
+// router_topk_token: one warp per token: top-k of p + bias with ties to the lower expert id (reference
 //   router_topk, src/fused_layer.cu:323-332), or the DeepSeek-V3 grouped mode (n_group groups of 32
 //   experts, group score = sum of the group's top-2, keep topk_group groups); weights p/max(sum, 2^-14)
 //   * scale; then the engine's keep-KE compaction (src/server_core_fused.cpp:793-813: order by weight,
@@ -18,56 +20,72 @@
 
 namespace lk {
 
+__device__ void router_topk_token(const RouterParams& p, int t, int lane);
+
+// one CTA = one expert x a tile of NTT tokens; 256 threads, each owns float4 chunks c = tid + 256 j
 template <int NTT>
 __global__ void __launch_bounds__(256) k_router_logits(RouterParams p) {
-    __shared__ float ws[2][4][NTT];
-    const int half = threadIdx.x >> 7, q = threadIdx.x & 127, warp = q >> 5, lane = q & 31;
-    const int e = blockIdx.x * 2 + half;
+    __shared__ float ws[8][NTT];
+    __shared__ int last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int e = blockIdx.x;
     const int t0 = blockIdx.y * NTT;
     const int nt = min(NTT, p.T - t0);
-    constexpr int NCH = HIDDEN / 4;                 // 1792 float4 chunks
-    float acc[NTT];
+    constexpr int NCH = HIDDEN / 4;                 // 1792 float4 chunks, 7 per thread
+    float4 w[NCH / 256];
     #pragma unroll
-    for (int t = 0; t < NTT; ++t) acc[t] = 0.0f;
-    if (e < p.n_experts) {
-        #pragma unroll 7
-        for (int c = q; c < NCH; c += 128) {
-            float4 w;
-            if (p.w_f16) {
-                const uint2 raw = __ldg((const uint2*)((const __half*)p.W + (size_t)e * HIDDEN) + c);
-                const float2 a = __half22float2(*(const __half2*)&raw.x), b = __half22float2(*(const __half2*)&raw.y);
-                w = make_float4(a.x, a.y, b.x, b.y);
-            } else {
-                w = __ldg((const float4*)((const float*)p.W + (size_t)e * HIDDEN) + c);
-            }
-            #pragma unroll
-            for (int t = 0; t < NTT; ++t) {
-                if (t < nt) {
-                    const float4 xv = *((const float4*)(p.x + (size_t)(t0 + t) * p.ld_x) + c);
-                    acc[t] = fmaf(w.x, xv.x, acc[t]);
-                    acc[t] = fmaf(w.y, xv.y, acc[t]);
-                    acc[t] = fmaf(w.z, xv.z, acc[t]);
-                    acc[t] = fmaf(w.w, xv.w, acc[t]);
-                }
-            }
+    for (int j = 0; j < NCH / 256; ++j) {
+        const int c = tid + 256 * j;
+        if (p.w_f16) {
+            const uint2 raw = __ldg((const uint2*)((const __half*)p.W + (size_t)e * HIDDEN) + c);
+            const float2 a = __half22float2(*(const __half2*)&raw.x), b = __half22float2(*(const __half2*)&raw.y);
+            w[j] = make_float4(a.x, a.y, b.x, b.y);
+        } else {
+            w[j] = __ldg((const float4*)((const float*)p.W + (size_t)e * HIDDEN) + c);
         }
     }
     #pragma unroll
     for (int t = 0; t < NTT; ++t) {
-        float a = acc[t];
+        float a = 0.0f;
+        if (t < nt) {
+            const float4* xr = (const float4*)(p.x + (size_t)(t0 + t) * p.ld_x);
+            #pragma unroll
+            for (int j = 0; j < NCH / 256; ++j) {
+                const float4 xv = xr[tid + 256 * j];
+                a = fmaf(w[j].x, xv.x, a);
+                a = fmaf(w[j].y, xv.y, a);
+                a = fmaf(w[j].z, xv.z, a);
+                a = fmaf(w[j].w, xv.w, a);
+            }
+        }
         #pragma unroll
         for (int o = 16; o > 0; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-        if (lane == 0) ws[half][warp][t] = a;
+        if (lane == 0) ws[warp][t] = a;
     }
     __syncthreads();
-    if (q < nt && e < p.n_experts) {
-        const int t = q;
-        const float lg = __fadd_rn(__fadd_rn(ws[half][0][t], ws[half][1][t]), __fadd_rn(ws[half][2][t], ws[half][3][t]));
+    if (tid < nt) {
+        const int t = tid;
+        const float lg = __fadd_rn(__fadd_rn(__fadd_rn(ws[0][t], ws[1][t]), __fadd_rn(ws[2][t], ws[3][t])),
+                                   __fadd_rn(__fadd_rn(ws[4][t], ws[5][t]), __fadd_rn(ws[6][t], ws[7][t])));
         const size_t o = (size_t)(t0 + t) * p.n_experts + e;
         p.logits[o] = lg;
         const float v = p.logits_override ? p.logits_override[o] : lg;
         p.probs[o] = lk_sigmoid(v);
     }
+    // the last CTA of this token tile runs the top-k for it (probabilities of all experts are visible:
+    // every CTA fences its writes before counting itself in)
+    if (!p.tile_count) return;
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        last = atomicAdd(&p.tile_count[blockIdx.y], 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (warp < nt) router_topk_token(p, t0 + warp, lane);
+    __syncthreads();
+    if (tid == 0) p.tile_count[blockIdx.y] = 0;       // ready for the next call
 }
 
 // warp argmax over (value, index) pairs, ties -> lower index; every lane returns the winner
@@ -80,18 +98,15 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
     }
 }
 
-__global__ void __launch_bounds__(256) k_router_topk(RouterParams p) {
-    const int lane = threadIdx.x & 31;
-    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (t >= p.T) return;
-    const float* pr = p.probs + (size_t)t * p.n_experts;
+__device__ void router_topk_token(const RouterParams& p, int t, int lane) {
+    const float* pr = p.probs + (size_t)t * p.n_experts;   // written by other CTAs: read past L1
     constexpr int PER = N_EXPERTS / 32;             // 8 experts per lane: e = lane + 32*i
     float sc[PER], pv[PER];
     bool allowed[PER];
     #pragma unroll
     for (int i = 0; i < PER; ++i) {
         const int e = lane + 32 * i;
-        pv[i] = pr[e];
+        pv[i] = __ldcg(pr + e);
         sc[i] = __fadd_rn(pv[i], p.bias[e]);
         allowed[i] = true;
     }
@@ -128,7 +143,7 @@ __global__ void __launch_bounds__(256) k_router_topk(RouterParams p) {
         sel[k] = bi;
         #pragma unroll
         for (int i = 0; i < PER; ++i) if (lane + 32 * i == bi) allowed[i] = false;
-        ps[k] = pr[bi];
+        ps[k] = __ldcg(pr + bi);
     }
     float sum = 0.0f;
     for (int k = 0; k < p.topk; ++k) sum = __fadd_rn(sum, ps[k]);
@@ -171,18 +186,18 @@ __global__ void __launch_bounds__(256) k_router_topk(RouterParams p) {
     }
 }
 
+// p.tile_count: ceil(T / 8) zeroed ints (the kernel leaves them zeroed again)
 void launch_router(const RouterParams& p, cudaStream_t st) {
-    const int pairs = (p.n_experts + 1) / 2;
+    const int ne = p.n_experts;
     if (p.T <= 1) {
-        k_router_logits<1><<<dim3(pairs, 1), 256, 0, st>>>(p);
+        k_router_logits<1><<<dim3(ne, 1), 256, 0, st>>>(p);
     } else if (p.T <= 2) {
-        k_router_logits<2><<<dim3(pairs, 1), 256, 0, st>>>(p);
+        k_router_logits<2><<<dim3(ne, 1), 256, 0, st>>>(p);
     } else if (p.T <= 4) {
-        k_router_logits<4><<<dim3(pairs, 1), 256, 0, st>>>(p);
+        k_router_logits<4><<<dim3(ne, 1), 256, 0, st>>>(p);
     } else {
-        k_router_logits<8><<<dim3(pairs, (p.T + 7) / 8), 256, 0, st>>>(p);
+        k_router_logits<8><<<dim3(ne, (p.T + 7) / 8), 256, 0, st>>>(p);
     }
-    k_router_topk<<<(p.T + 7) / 8, 256, 0, st>>>(p);
 }
 
 }  // namespace lk

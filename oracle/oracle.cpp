@@ -84,22 +84,23 @@ void orc_quant_q8(const float* x, int64_t n, int8_t* q, float* d) {
 }
 
 // ------------------------------------------------------------------ router
-// logits[t][e] = W[e] . x[t] in the GPU router kernel's order: 128 partial sums per (t, e); partial p
-// (p = 32*warp + lane) runs over float4 chunks c = p, p+128, ... (14 chunks for 7168) and within a chunk
-// over its 4 components, each step acc = fmaf(w, x, acc); each warp's 32 partials are combined by the
-// xor butterfly (offsets 16, 8, 4, 2, 1: a_l <- a_l + a_(l^o)); the 4 warp sums as (s0 + s1) + (s2 + s3).
+// logits[t][e] = W[e] . x[t] in the GPU router kernel's order: 256 partial sums per (t, e); partial p
+// (p = 32*warp + lane, 8 warps) runs over float4 chunks c = p, p+256, ... (7 chunks for 7168) and within a
+// chunk over its 4 components, each step acc = fmaf(w, x, acc); each warp's 32 partials are combined by the
+// xor butterfly (offsets 16, 8, 4, 2, 1: a_l <- a_l + a_(l^o)); the 8 warp sums as
+// ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)).
 void orc_router_logits(const float* x, int T, const float* W, int n_experts, int K, float* logits) {
     const int NCH = K / 4;
     #pragma omp parallel for collapse(2) schedule(static)
     for (int t = 0; t < T; ++t)
         for (int e = 0; e < n_experts; ++e) {
             const float* xr = x + (size_t)t * K; const float* wr = W + (size_t)e * K;
-            float ws[4];
-            for (int w = 0; w < 4; ++w) {
+            float ws[8];
+            for (int w = 0; w < 8; ++w) {
                 float a[32];
                 for (int l = 0; l < 32; ++l) {
                     float acc = 0.0f;
-                    for (int c = 32 * w + l; c < NCH; c += 128)
+                    for (int c = 32 * w + l; c < NCH; c += 256)
                         for (int j = 0; j < 4; ++j) acc = fmaf(wr[4 * c + j], xr[4 * c + j], acc);
                     a[l] = acc;
                 }
@@ -110,7 +111,7 @@ void orc_router_logits(const float* x, int T, const float* W, int n_experts, int
                 }
                 ws[w] = a[0];
             }
-            logits[(size_t)t * n_experts + e] = (ws[0] + ws[1]) + (ws[2] + ws[3]);
+            logits[(size_t)t * n_experts + e] = ((ws[0] + ws[1]) + (ws[2] + ws[3])) + ((ws[4] + ws[5]) + (ws[6] + ws[7]));
         }
 }
 
