@@ -21,6 +21,9 @@ struct LkMoeCtx {
     int* nslots = nullptr; int max_slots = 0;
     int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
     int* err = nullptr; int* tile_count = nullptr; int* chunk_count = nullptr;
+    // tensor-core path (T >= gemm_min_tokens): 64-token slots and fp16 operand staging
+    int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
+    __half* xh = nullptr; __half* hb = nullptr; int gemm_min_tokens = 64;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     char msg[256] = {0};
 };
@@ -91,6 +94,10 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LK_CU(cudaMemset(c->err, 0, sizeof(int)));
     LK_CU(dalloc(&c->tile_count, (T + 7) / 8));
     LK_CU(cudaMemset(c->tile_count, 0, (size_t)((T + 7) / 8) * sizeof(int)));
+    c->g_max = max_slots_for(T, KE, NE, GEMM_NT, cfg->with_shared);
+    LK_CU(dalloc(&c->g_expert, c->g_max)); LK_CU(dalloc(&c->g_tok, (size_t)c->g_max * GEMM_NT));
+    LK_CU(dalloc(&c->g_out, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_w, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_n, 1));
+    LK_CU(dalloc(&c->xh, (size_t)T * HIDDEN)); LK_CU(dalloc(&c->hb, rows * MOE_INTER));
     LK_CU(dalloc(&c->chunk_count, HIDDEN / 8));
     LK_CU(cudaMemset(c->chunk_count, 0, (size_t)(HIDDEN / 8) * sizeof(int)));
     LK_CU(cudaMemset(c->y, 0, rows * HIDDEN * sizeof(float)));
@@ -103,7 +110,8 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
 void lk_moe_destroy(LkMoeCtx* c) {
     if (!c) return;
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
-                     c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->chunk_count };
+                     c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->chunk_count,
+                     c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->xh, c->hb };
     for (void* p : ptrs) if (p) cudaFree(p);
     delete c;
 }
@@ -192,6 +200,43 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const
     return LK_OK;
 }
 
+// the tensor-core path: 64-token slots, q8->fp16 activations, gate/up GEMM + SwiGLU, down GEMM, combine
+static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, const int* sel,
+                         const float* w, int keep, float* h, float* moe, cudaStream_t st) {
+    SlotParams s{};
+    s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = GEMM_NT; s.with_shared = c->cfg.with_shared;
+    s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
+    s.slot_expert = c->g_expert; s.slot_tok = c->g_tok; s.slot_out = c->g_out; s.slot_w = c->g_w; s.nslots = c->g_n;
+    s.max_slots = c->g_max; s.err = c->err;
+    launch_build_slots(s, st);
+    GemmParams g{};
+    g.gate = (const uint8_t*)W->gate; g.up = (const uint8_t*)W->up; g.down = (const uint8_t*)W->down;
+    g.gate_stride = W->gate_stride; g.up_stride = W->up_stride; g.down_stride = W->down_stride;
+    g.sh_gate = (const uint8_t*)W->sh_gate; g.sh_up = (const uint8_t*)W->sh_up; g.sh_down = (const uint8_t*)W->sh_down;
+    g.x = x; g.ld_x = HIDDEN; g.T = T;
+    g.slot_expert = c->g_expert; g.slot_tok = c->g_tok; g.slot_out = c->g_out; g.slot_w = c->g_w; g.nslots = c->g_n;
+    g.xh = c->xh; g.hb = c->hb; g.y = c->y; g.err = c->err;
+    if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
+    launch_prefill_gemm(g, c->nsm, st);
+    if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
+    if (h || moe) {
+        if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
+        CombineParams cp{};
+        cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
+        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN;
+        launch_combine(cp, st);
+    }
+    if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
+    LK_CU(cudaGetLastError());
+    return LK_OK;
+}
+
+int lk_moe_set_gemm_threshold(LkMoeCtx* c, int min_tokens) {
+    if (!c || min_tokens < 1) return LK_ERR_ARG;
+    c->gemm_min_tokens = min_tokens;
+    return LK_OK;
+}
+
 int lk_moe_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, const int* sel,
                    const float* w, int keep, float* h, float* moe, lk_stream_t stream) {
     if (!c || !x || !sel || !w || T < 0 || keep < 1) return set_err(c, LK_ERR_ARG, "bad argument");
@@ -200,6 +245,7 @@ int lk_moe_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const flo
     if (rc) return rc;
     if (T > c->cfg.max_tokens || keep > c->cfg.keep) return set_err(c, LK_ERR_CAPACITY, "T=%d keep=%d above capacity", T, keep);
     cudaStream_t st = (cudaStream_t)stream;
+    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, resid, T, sel, w, keep, h, moe, st);
     rc = lk_moe_dispatch(c, sel, w, T, keep, nullptr, nullptr, nullptr, stream);
     if (rc) return rc;
     return run_experts(c, W, x, resid, T, keep, h, moe, slot_nt(T), st);
@@ -216,11 +262,15 @@ int lk_moe_forward(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const flo
     const int keep = c->cfg.keep;
     RouterParams p = router_params(c, W, x, T, logits_override, c->sel, c->w, T == 1);
     launch_router(p, st);
-    if (T > 1) {
-        rc = lk_moe_dispatch(c, c->sel, c->w, T, keep, nullptr, nullptr, nullptr, stream);
-        if (rc) return rc;
+    if (T >= c->gemm_min_tokens) {
+        rc = run_gemm_path(c, W, x, resid, T, c->sel, c->w, keep, h, moe, st);
+    } else {
+        if (T > 1) {
+            rc = lk_moe_dispatch(c, c->sel, c->w, T, keep, nullptr, nullptr, nullptr, stream);
+            if (rc) return rc;
+        }
+        rc = run_experts(c, W, x, resid, T, keep, h, moe, slot_nt(T), st);
     }
-    rc = run_experts(c, W, x, resid, T, keep, h, moe, slot_nt(T), st);
     if (rc) return rc;
     if (sel) LK_CU(cudaMemcpyAsync(sel, c->sel, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));
     if (w) LK_CU(cudaMemcpyAsync(w, c->w, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));

@@ -1,6 +1,7 @@
 // moe_internal.h -- kernel parameter blocks and launchers shared by the library's translation units.
 #pragma once
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 #include "moe_format.h"
 
@@ -8,6 +9,7 @@ namespace lk {
 
 constexpr int SHARED_SLOT = -1;      // slot_expert value of the shared expert
 constexpr int MAX_NT = 8;            // tokens per work slot of the grouped matvecs
+constexpr int GEMM_NT = 64;          // tokens per work slot of the tensor-core GEMMs (prefill)
 
 // ---- router
 struct RouterParams {
@@ -66,6 +68,20 @@ struct CombineParams {
     float* h; float* moe; int ld_out;
 };
 void launch_combine(const CombineParams& p, cudaStream_t st);
+
+// ---- tensor-core grouped GEMMs (prefill / batch): slots of up to GEMM_NT tokens
+struct GemmParams {
+    const uint8_t* gate; const uint8_t* up; const uint8_t* down;
+    int64_t gate_stride, up_stride, down_stride;
+    const uint8_t* sh_gate; const uint8_t* sh_up; const uint8_t* sh_down;
+    const float* x; int ld_x; int T;                  // activations [T][HIDDEN] fp32
+    const int* slot_expert; const int* slot_tok; const int* slot_out; const float* slot_w; const int* nslots;  // [slot][GEMM_NT]
+    __half* xh;                                       // [T][HIDDEN] fp16 of the q8-dequantised x (scratch)
+    __half* hb;                                       // [rows][MOE_INTER] fp16 of the q8-dequantised SwiGLU output
+    float* y;                                         // [rows][HIDDEN] weighted expert outputs
+    int* err;
+};
+void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st);
 
 // ---- seeded IQ2_XXS weight generation (moe_format.h generator) for n_experts consecutive experts
 void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,

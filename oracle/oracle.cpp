@@ -236,6 +236,36 @@ static void iq2_matvec_multi(const uint8_t* W, int rows, int K, const int8_t* co
     }
 }
 
+// y = W . h for fp32 activations h (no q8): the tensor-core path's down projection, which consumes the
+// SwiGLU output at 16-bit precision instead of re-quantising it
+static void iq2_matvec_float_multi(const uint8_t* W, int rows, int K, const float* const* h, int ntok, float* const* y) {
+    const int NB = K / QK;
+    #pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t* row = W + (size_t)r * NB * BLK_IQ2;
+        std::vector<double> acc(ntok, 0.0);
+        for (int b = 0; b < NB; ++b) {
+            const uint8_t* blk = row + (size_t)b * BLK_IQ2;
+            uint16_t dh; memcpy(&dh, blk, 2); const float d = half_to_float(dh);
+            for (int g = 0; g < 8; ++g) {
+                uint32_t aux0, aux1; memcpy(&aux0, blk + 2 + 8 * g, 4); memcpy(&aux1, blk + 6 + 8 * g, 4);
+                const double fa = (double)(d * (0.5f + (float)(aux1 >> 28)) * 0.25f);
+                for (int l = 0; l < 4; ++l) {
+                    const uint64_t gv = IQ2_GRID[(aux0 >> (8 * l)) & 0xFF];
+                    const uint32_t sg = iq2_ksigns((aux1 >> (7 * l)) & 127u);
+                    for (int j = 0; j < 8; ++j) {
+                        const int32_t m = (int32_t)((gv >> (8 * j)) & 0xFF);
+                        const int32_t wv = (sg >> j) & 1 ? -m : m;
+                        const int k = b * 256 + g * 32 + l * 8 + j;
+                        for (int t = 0; t < ntok; ++t) acc[t] += fa * (double)wv * (double)h[t][k];
+                    }
+                }
+            }
+        }
+        for (int t = 0; t < ntok; ++t) y[t][r] = (float)acc[t];
+    }
+}
+
 void orc_iq2_matvec(const uint8_t* W, int rows, int K, const int8_t* xq, const float* xd, float* y) {
     iq2_matvec_multi(W, rows, K, &xq, &xd, 1, &y);
 }
@@ -250,8 +280,11 @@ struct OrcLayerW {
     const uint8_t* sh_gate; const uint8_t* sh_up; const uint8_t* sh_down;
 };
 
-int orc_moe_layer(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
-                  int KE, float* h, float* moe, float* y_slot, float* shared_out) {
+// hq8 = 1: the SwiGLU output is re-quantised to q8 per 32 before the down projection (the reference's
+// swiglu_q8, src/fused_layer.cu:334-341: the decode and narrow paths); hq8 = 0: it enters the down
+// projection unquantised (the tensor-core prefill path).
+int orc_moe_layer_ex(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
+                     int KE, float* h, float* moe, float* y_slot, float* shared_out, int hq8) {
     const int E = HIDDEN, H = MOE_INTER;
     // q8 of every token's x
     std::vector<int8_t> xq((size_t)T * E); std::vector<float> xd((size_t)T * E / 32);
@@ -276,15 +309,17 @@ int orc_moe_layer(const float* x, const float* resid, int T, const OrcLayerW* Wl
         iq2_matvec_multi(Wl->gate + m * Wl->gate_stride, H, E, xqp.data(), xdp.data(), n, gp.data());
         iq2_matvec_multi(Wl->up + m * Wl->up_stride, H, E, xqp.data(), xdp.data(), n, up.data());
         std::vector<const int8_t*> hqp(n); std::vector<const float*> hdp(n); std::vector<float*> yp(n);
-        std::vector<std::vector<float>> ytmp(n, std::vector<float>(E));
+        std::vector<std::vector<float>> ytmp(n, std::vector<float>(E)), hf(n, std::vector<float>(H));
+        std::vector<const float*> hfp(n);
         for (int i = 0; i < n; ++i) {
             const int s = perm[off[m] + i];
-            std::vector<float> hv(H);
-            for (int j = 0; j < H; ++j) hv[j] = lk_swiglu(g[(size_t)s * H + j], u[(size_t)s * H + j]);
-            orc_quant_q8(hv.data(), H, hq.data() + (size_t)s * H, hd.data() + (size_t)s * H / 32);
+            for (int j = 0; j < H; ++j) hf[i][j] = lk_swiglu(g[(size_t)s * H + j], u[(size_t)s * H + j]);
+            orc_quant_q8(hf[i].data(), H, hq.data() + (size_t)s * H, hd.data() + (size_t)s * H / 32);
             hqp[i] = hq.data() + (size_t)s * H; hdp[i] = hd.data() + (size_t)s * H / 32; yp[i] = ytmp[i].data();
+            hfp[i] = hf[i].data();
         }
-        iq2_matvec_multi(Wl->down + m * Wl->down_stride, E, H, hqp.data(), hdp.data(), n, yp.data());
+        if (hq8) iq2_matvec_multi(Wl->down + m * Wl->down_stride, E, H, hqp.data(), hdp.data(), n, yp.data());
+        else iq2_matvec_float_multi(Wl->down + m * Wl->down_stride, E, H, hfp.data(), n, yp.data());
         for (int i = 0; i < n; ++i) {
             const int s = perm[off[m] + i];
             for (int j = 0; j < E; ++j) yslot[(size_t)s * E + j] = w[s] * ytmp[i][j];
@@ -301,15 +336,16 @@ int orc_moe_layer(const float* x, const float* resid, int T, const OrcLayerW* Wl
         }
         iq2_matvec_multi(Wl->sh_gate, H, E, xqp.data(), xdp.data(), T, sgp.data());
         iq2_matvec_multi(Wl->sh_up, H, E, xqp.data(), xdp.data(), T, sup.data());
-        std::vector<int8_t> shq((size_t)T * H); std::vector<float> shd((size_t)T * H / 32);
-        std::vector<const int8_t*> hqp(T); std::vector<const float*> hdp(T);
+        std::vector<int8_t> shq((size_t)T * H); std::vector<float> shd((size_t)T * H / 32), shf((size_t)T * H);
+        std::vector<const int8_t*> hqp(T); std::vector<const float*> hdp(T), hfp(T);
         for (int t = 0; t < T; ++t) {
-            std::vector<float> hv(H);
+            float* hv = shf.data() + (size_t)t * H;
             for (int j = 0; j < H; ++j) hv[j] = lk_swiglu(sg[(size_t)t * H + j], su[(size_t)t * H + j]);
-            orc_quant_q8(hv.data(), H, shq.data() + (size_t)t * H, shd.data() + (size_t)t * H / 32);
-            hqp[t] = shq.data() + (size_t)t * H; hdp[t] = shd.data() + (size_t)t * H / 32;
+            orc_quant_q8(hv, H, shq.data() + (size_t)t * H, shd.data() + (size_t)t * H / 32);
+            hqp[t] = shq.data() + (size_t)t * H; hdp[t] = shd.data() + (size_t)t * H / 32; hfp[t] = hv;
         }
-        iq2_matvec_multi(Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
+        if (hq8) iq2_matvec_multi(Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
+        else iq2_matvec_float_multi(Wl->sh_down, E, H, hfp.data(), T, shp.data());
     }
     // combine in fixed k order
     #pragma omp parallel for schedule(static)
@@ -323,6 +359,11 @@ int orc_moe_layer(const float* x, const float* resid, int T, const OrcLayerW* Wl
     if (y_slot) memcpy(y_slot, yslot.data(), yslot.size() * 4);
     if (shared_out) memcpy(shared_out, sh.data(), sh.size() * 4);
     return 0;
+}
+
+int orc_moe_layer(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
+                  int KE, float* h, float* moe, float* y_slot, float* shared_out) {
+    return orc_moe_layer_ex(x, resid, T, Wl, ids, w, KE, h, moe, y_slot, shared_out, 1);
 }
 
 }  // extern "C"

@@ -60,6 +60,8 @@ def lib():
         L.orc_iq2_matvec.argtypes = [P, ctypes.c_int, ctypes.c_int, P, P, P]
         L.orc_moe_layer.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(LayerW), P, P, ctypes.c_int, P, P, P, P]
         L.orc_moe_layer.restype = ctypes.c_int
+        L.orc_moe_layer_ex.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(LayerW), P, P, ctypes.c_int, P, P, P, P, ctypes.c_int]
+        L.orc_moe_layer_ex.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -139,10 +141,12 @@ def iq2_matvec(W, rows, K, xq, xd):
     return y
 
 
-def moe_layer(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None, sh_down=None, want_slots=False):
+def moe_layer(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None, sh_down=None, want_slots=False, hq8=True):
     """Reference MoE layer on arena-layout weights (expert m at m*stride bytes of each arena).
 
-    Returns dict(h, moe[, y_slot, shared]).  ids/w: [T, KE] expert ids (arena slots) and weights."""
+    Returns dict(h, moe[, y_slot, shared]).  ids/w: [T, KE] expert ids (arena slots) and weights.
+    hq8: re-quantise the SwiGLU output to q8 before the down projection (reference semantics; the
+    tensor-core prefill path keeps it at 16-bit precision: hq8=False)."""
     x = np.ascontiguousarray(x, np.float32)
     resid = np.ascontiguousarray(resid, np.float32)
     ids = np.ascontiguousarray(ids, np.int32)
@@ -156,7 +160,8 @@ def moe_layer(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None
     moe = np.empty((T, HIDDEN), np.float32)
     ys = np.empty((T, KE, HIDDEN), np.float32) if want_slots else None
     sh = np.empty((T, HIDDEN), np.float32) if want_slots else None
-    rc = lib().orc_moe_layer(_p(x), _p(resid), T, ctypes.byref(lw), _p(ids), _p(w), KE, _p(h), _p(moe), _p(ys), _p(sh))
+    rc = lib().orc_moe_layer_ex(_p(x), _p(resid), T, ctypes.byref(lw), _p(ids), _p(w), KE, _p(h), _p(moe), _p(ys), _p(sh),
+                                1 if hq8 else 0)
     assert rc == 0
     out = {"h": h, "moe": moe}
     if want_slots:

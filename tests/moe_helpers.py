@@ -23,7 +23,7 @@ def host_arena(oracle, seed, layer, experts):
     return gate, up, down, sh
 
 
-def oracle_layer(oracle, seed, layer, x, resid, sel, w, with_shared=True, tokens=None):
+def oracle_layer(oracle, seed, layer, x, resid, sel, w, with_shared=True, tokens=None, hq8=True):
     """Oracle h/moe for routing (sel, w) with global expert ids, on the given tokens (default: all)."""
     tokens = list(range(x.shape[0])) if tokens is None else list(tokens)
     sel = np.asarray(sel)[tokens]
@@ -32,4 +32,4 @@ def oracle_layer(oracle, seed, layer, x, resid, sel, w, with_shared=True, tokens
     ids = np.vectorize(lambda e: remap[int(e)])(sel).astype(np.int32)
     gate, up, down, sh = host_arena(oracle, seed, layer, used)
     shg, shu, shd = sh if with_shared else (None, None, None)
-    return oracle.moe_layer(x[tokens], resid[tokens], gate, up, down, MAT, ids, np.asarray(w)[tokens], shg, shu, shd)
+    return oracle.moe_layer(x[tokens], resid[tokens], gate, up, down, MAT, ids, np.asarray(w)[tokens], shg, shu, shd, hq8=hq8)

@@ -141,6 +141,38 @@ def test_experts_small_arena(native, moe, oracle, T, keep):
     assert e_moe < RTOL_L2 and e_h < RTOL_L2, (e_moe, e_h)
 
 
+@pytest.mark.parametrize("T,keep", [(2, 8), (40, 8), (70, 2), (130, 8)])
+def test_experts_tensor_core_path(native, moe, oracle, T, keep):
+    """The tcgen05 grouped-GEMM path (forced on for any T) against the oracle on a small arena."""
+    NE = 12
+    layer_id = 13
+    buf = torch.empty(3 * NE * MAT + 3 * MAT, dtype=torch.uint8, device="cuda")
+    base = buf.data_ptr()
+    for m in range(3):
+        rows, K = (INTER, HIDDEN) if m < 2 else (HIDDEN, INTER)
+        moe.gen_iq2(base + m * NE * MAT, SEED, layer_id, m, 0, NE, rows, K, MAT)
+        moe.gen_iq2(base + 3 * NE * MAT + m * MAT, SEED, layer_id, m, 256, 1, rows, K, MAT)
+    ws = native.LkMoeWeights(base, base + NE * MAT, base + 2 * NE * MAT, MAT, MAT, MAT, native.FMT_IQ2,
+                             base + 3 * NE * MAT, base + 3 * NE * MAT + MAT, base + 3 * NE * MAT + 2 * MAT, None, 0, None)
+    rng = np.random.default_rng(T * 7 + keep)
+    sel = np.stack([rng.choice(NE, keep, replace=False) for _ in range(T)]).astype(np.int32)
+    w = rng.uniform(0.05, 1.0, (T, keep)).astype(np.float32)
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    layer = moe.MoeLayer(0, keep=keep, max_tokens=T)
+    layer.set_gemm_threshold(1)
+    h, mo = layer.experts(ws, _dev(x), _dev(r), _dev(sel), _dev(w))
+    layer.device_error()
+    tok = list(range(T)) if T <= 40 else [0, 1, T // 2, T - 2, T - 1]
+    ref = oracle_layer(oracle, SEED, layer_id, x, r, sel, w, tokens=tok, hq8=False)
+    e_moe = rel_l2(mo.cpu().numpy()[tok], ref["moe"])
+    e_h = rel_l2(h.cpu().numpy()[tok], ref["h"])
+    assert e_moe < RTOL_L2 and e_h < RTOL_L2, (e_moe, e_h)
+    # against the q8-re-quantising (reference-semantics) oracle the difference is the q8 noise of h itself
+    ref_q = oracle_layer(oracle, SEED, layer_id, x, r, sel, w, tokens=tok, hq8=True)
+    assert rel_l2(mo.cpu().numpy()[tok], ref_q["moe"]) < 1e-2
+
+
 # ---------------------------------------------------------------- the whole layer (256 experts resident)
 @pytest.fixture(scope="module")
 def layer_weights(moe):
@@ -152,6 +184,7 @@ def layer_weights(moe):
 
 
 def _layer_case(moe, oracle, W, T, keep=8, n_group=1, topk_group=1, logits=None, sample=None, seed=0):
+    hq8 = T < 64                                      # T >= 64 takes the tensor-core path (h kept at 16 bits)
     rng = np.random.default_rng(1000 + T + seed)
     x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
     r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
@@ -165,7 +198,7 @@ def _layer_case(moe, oracle, W, T, keep=8, n_group=1, topk_group=1, logits=None,
     _, osel, ow = oracle.router(x, Wr, bias, cfg, logits=logits)
     np.testing.assert_array_equal(sel, osel)
     np.testing.assert_array_equal(w, ow)
-    ref = oracle_layer(oracle, SEED, 0, x, r, sel, w, tokens=sample)
+    ref = oracle_layer(oracle, SEED, 0, x, r, sel, w, tokens=sample, hq8=hq8)
     tok = list(range(T)) if sample is None else list(sample)
     e_moe = rel_l2(mo.cpu().numpy()[tok], ref["moe"])
     e_h = rel_l2(h.cpu().numpy()[tok], ref["h"])
