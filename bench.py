@@ -347,6 +347,101 @@ def e2e_decode(args, layers, distinct, keep):
             "steps": n, "error": err}
 
 
+def run_prefill(args, ws, rank, local, dist):
+    """one MoE layer, T=512 tokens (bf16 N(0,1) hidden states, fed as fp32), top-8 of 256
+    experts chosen from uniform-random router logits (the router GEMV still runs), IQ2_XXS experts through the
+    tcgen05 grouped GEMMs, combine with the shared expert.  A step = one layer forward."""
+    import torch
+    import ctypes
+    from loki_b200 import moe as M
+    from loki_b200 import native as N
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    T = args.tokens
+    W = M.LayerWeights(dev, SEED, 0)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    x = torch.randn(T, HIDDEN, device=dev, generator=g).to(torch.bfloat16).float()
+    r = torch.randn(T, HIDDEN, device=dev, generator=g).to(torch.bfloat16).float()
+    logits = torch.rand(T, NE, device=dev, generator=g) * 2 - 1
+    h = torch.empty(T, HIDDEN, device=dev)
+    mo = torch.empty(T, HIDDEN, device=dev)
+    ctx = M.MoeLayer(local, keep=args.keep, max_tokens=T)
+    st = W.struct()
+    L = N.lib()
+    stream = torch.cuda.Stream(dev)
+    ev = DriverEvents(4)
+
+    def step(events=False):
+        s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        if events:
+            L.lk_moe_set_events(ctx.ctx, (ctypes.c_void_p * 4)(*[e.value for e in ev.ev]))
+        N.check(L.lk_moe_forward(ctx.ctx, ctypes.byref(st), ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(r.data_ptr()), T,
+                                 ctypes.c_void_p(logits.data_ptr()), ctypes.c_void_p(h.data_ptr()), ctypes.c_void_p(mo.data_ptr()),
+                                 None, None, s), ctx.ctx)
+        if events:
+            L.lk_moe_set_events(ctx.ctx, None)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize(dev)
+    ctx.device_error()
+    barrier(dist)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+    barrier(dist)
+    ms = t0.elapsed_time(t1)
+    gemm_ms = []
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step(events=True)
+            torch.cuda.synchronize(dev)
+            gemm_ms.append(ev.elapsed(0, 2))
+    cl = clocks.stop() if clocks else None
+    ctx.device_error()
+    ms_max = max_over_ranks(dist, ms)
+    value = T * args.steps * ws / (ms_max / 1e3)
+    hbm, bf16, peak_kind = measured_peaks()
+    # routing statistics of the step (distinct experts, tokens per expert)
+    sel = torch.topk(torch.sigmoid(logits) + W.router_bias, 8, dim=1).indices
+    distinct = int(torch.unique(sel).numel())
+    gemm_bytes = (distinct + 1) * 3 * MAT                               # routed + shared gate/up/down, each read once
+    layer_bytes = gemm_bytes + ROUTER_BYTES + T * HIDDEN * 4 * 4
+    flops = 2.0 * T * (args.keep + 1) * 3 * HIDDEN * INTER + 2.0 * T * HIDDEN * NE
+    g_ms = float(np.median(gemm_ms))
+    out = {
+        "metric": "MoE-layer tokens/s (T=512 prefill, one layer)", "value": round(value, 1), "unit": "tokens/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)",
+        "data": "synthetic: seeded IQ2_XXS experts, uniform-random router logits U(-1,1), bf16 N(0,1) hidden states",
+        "config": {"workload": "config2_prefill_T%d" % T, "global_batch": T * ws, "seq_len": T, "layers": 1, "top_k": 8,
+                   "keep": args.keep, "distinct_experts": distinct, "parallelism": "replicas" if ws > 1 else "single",
+                   "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (gemm_bytes / 1e9)},
+        "layer": {"bytes": layer_bytes, "flops": flops, "achieved_gbs": round(layer_bytes / (ms_max / args.steps / 1e3) / 1e9, 1),
+                  "achieved_tflops": round(flops / (ms_max / args.steps / 1e3) / 1e12, 1),
+                  "frac_of_hbm": round(layer_bytes / (ms_max / args.steps / 1e3) / 1e9 / hbm, 4)},
+        "roofline": {"kernel": "k_prefill_gemm (gate/up + down tcgen05 GEMMs, incl. fp16 activation staging)", "bound": "hbm",
+                     "achieved": round(gemm_bytes / (g_ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gemm_bytes / (g_ms / 1e3) / 1e9 / hbm, 4), "traffic": ncu_traffic("k_prefill_gemm", "prefill_T512"),
+                     "algorithmic_bytes_per_launch": gemm_bytes, "peak_source": peak_kind,
+                     "tensor_tflops": round(flops * 0.999 / (g_ms / 1e3) / 1e12, 1), "tensor_peak_tflops": bf16},
+        "gpu_launches": args.steps * 5,
+    }
+    if cl:
+        out["clocks"] = cl
+    return out
+
+
 def reference_arm(args, ws, rank):
     """--impl reference: the CPU oracle (restatement of the reference's path) on the host cores."""
     if rank != 0:
@@ -375,7 +470,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--tokens", type=int, default=512, help="prefill workload: tokens per step")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--keep", type=int, default=8)
     ap.add_argument("--no-e2e", action="store_true")
@@ -391,6 +487,14 @@ def main():
         return
     import torch
     dist = dist_init(ws, local)
+    if args.workload == "prefill":
+        out = run_prefill(args, ws, rank, local, dist)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     out, layers, ctx, structs, xs, rs = run_decode(args, ws, rank, local, dist)
     if not args.no_e2e:
         e2e = e2e_decode(args, layers, len(layers), args.keep)

@@ -1,0 +1,60 @@
+/* loki_ep.h -- expert-parallel MoE layer: 256 routed experts sharded over n_ranks GPUs of one node.
+ *
+ * No counterpart in the reference: its fused_layer.h drives one GPU and streams experts from NVMe
+ * (src/moe_stream_buffer.h).  Here every rank keeps its shard (experts [r*E, (r+1)*E), E = 256/n_ranks)
+ * resident in HBM, tokens stay on their home rank, and two all-to-all exchanges (done by the caller,
+ * e.g. NCCL through torch.distributed) move rows to the experts and partial sums back:
+ *
+ *   home:   lk_moe_route -> lk_ep_pack -> send rows          lk_ep_shared (overlaps the exchange)
+ *   all-to-all #1 (rows)
+ *   expert: lk_ep_experts(received rows) -> partial sums
+ *   all-to-all #2 (partial sums, the transpose of #1)
+ *   home:   lk_ep_combine -> h, moe
+ *
+ * A row is LK_EP_ROW_BYTES: a 64-byte header (int32 sel[8]: the expert id local to the receiving rank or
+ * -1, float w[8]: routing weights) and the token's activations (fp32 [7168]).  Rows for rank d form block
+ * d of the send buffer, tokens ascending; block d starts at row d*cap (fixed capacity, cap >= T: no count
+ * exchange needed, CUDA-graph friendly) or, with cap == 0, right after block d-1 (compact; the caller
+ * exchanges send_counts first to size the transfer).  Unused rows of a fixed-capacity block have all sel
+ * -1 and produce zero partial sums.  All pointers are device pointers; all calls are asynchronous on
+ * `stream`.  Returns LK_OK or an LK_ERR_* code (loki_moe.h). */
+#ifndef LOKI_EP_H
+#define LOKI_EP_H
+#include "loki_moe.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LK_EP_ROW_HDR_BYTES 64
+#define LK_EP_ROW_BYTES (64 + 7168 * 4)
+#define LK_EP_MAX_RANKS 8
+
+/* home side: sel/w [T][keep] (global expert ids, from lk_moe_route) and x [T][7168] -> send rows,
+ * send_counts [n_ranks] (rows per destination) and row_map [T][n_ranks] (the send-buffer row of (t, d),
+ * or -1).  keep <= 8, n_ranks in 1..8 dividing 256.  Ids outside [0, 256) set the context-free error
+ * word `err` (a device int, may be null) and are dropped. */
+LK_API int lk_ep_pack(const int* sel, const float* w, const float* x, int T, int keep, int n_ranks, int cap,
+                      void* send_rows, int* send_counts, int* row_map, int* err, lk_stream_t stream);
+
+/* expert side: R received rows -> out [R][7168] fp32, row r = sum over its entries of w * expert(x) in
+ * entry order (the partial sum of the routed experts this rank owns).  ctx: a context with n_experts = the
+ * shard size, with_shared = 0 and max_tokens >= R; W: the shard's arenas (expert ids local). */
+LK_API int lk_ep_experts(LkMoeCtx* ctx, const LkMoeWeights* W, const void* recv_rows, int R, int keep, float* out,
+                         lk_stream_t stream);
+
+/* home side: the shared expert of the home tokens, h_partial [T][7168] = resid + shared(x).  ctx: a
+ * context with with_shared = 1 (W->sh_* set). */
+LK_API int lk_ep_shared(LkMoeCtx* ctx, const LkMoeWeights* W, const float* x, const float* resid, int T,
+                        float* h_partial, lk_stream_t stream);
+
+/* home side, after the return exchange: ret rows in send-buffer order -> h = h_partial + sum_d ret and
+ * moe = sum_d ret (d ascending) for each of the T tokens; h_partial / h may be null (then h is not
+ * written). */
+LK_API int lk_ep_combine(const float* ret, const int* row_map, int T, int n_ranks, const float* h_partial,
+                         float* h, float* moe, lk_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

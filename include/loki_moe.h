@@ -46,7 +46,7 @@ enum {
 enum { LK_FMT_IQ2 = 4, LK_FMT_Q2K = 5, LK_FMT_Q3K = 6 };   /* numerically equal to FL_IQ2/FL_Q2K/FL_Q3K */
 
 typedef struct LkMoeConfig {
-    int n_experts;      /* routed experts (256) */
+    int n_experts;      /* routed experts: 256, or an expert-parallel shard's count (the router needs 256) */
     int topk;           /* experts chosen by score (8) */
     int keep;           /* experts kept per token after ordering by weight (the engine's --experts; <= topk) */
     int renorm;         /* 1: kept weights rescaled to sum to `scale` (the engine's default) */

@@ -13,10 +13,12 @@ __global__ void k_combine(CombineParams p) {
     const int t = i / per, c = i % per;
     float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < p.keep; ++k) {
+        if (p.sel && p.sel[t * p.keep + k] < 0) continue;
         const float4 v = ((const float4*)(p.y + ((size_t)t * p.keep + k) * HIDDEN))[c];
         r.x += v.x; r.y += v.y; r.z += v.z; r.w += v.w;
     }
     if (p.moe) ((float4*)(p.moe + (size_t)t * p.ld_out))[c] = r;
+    if (!p.h) return;
     float4 h = ((const float4*)(p.resid + (size_t)t * p.ld_out))[c];
     if (p.with_shared) {
         const float4 v = ((const float4*)(p.y + ((size_t)p.T * p.keep + t) * HIDDEN))[c];
@@ -27,7 +29,7 @@ __global__ void k_combine(CombineParams p) {
         h.x += v.x; h.y += v.y; h.z += v.z; h.w += v.w;
     }
     h.x += r.x; h.y += r.y; h.z += r.z; h.w += r.w;
-    if (p.h) ((float4*)(p.h + (size_t)t * p.ld_out))[c] = h;
+    ((float4*)(p.h + (size_t)t * p.ld_out))[c] = h;
 }
 
 void launch_combine(const CombineParams& p, cudaStream_t st) {

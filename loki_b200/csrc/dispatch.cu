@@ -29,11 +29,12 @@ __global__ void __launch_bounds__(DS_THREADS) k_build_slots(SlotParams p) {
     for (int i = tid; i < NE; i += DS_THREADS) { cnt[i] = 0; run[i] = 0; }
     for (int i = tid; i < (DS_THREADS / 32) * N_EXPERTS; i += DS_THREADS) (&wcnt[0][0])[i] = 0;
     __syncthreads();
-    // ids outside [0, n_experts) are reported through the error word and dropped from every table
+    // negative ids mark absent entries (an expert-parallel row's experts that live on another rank) and are
+    // skipped; ids >= n_experts are reported through the error word and dropped from every table
     for (int i = tid; i < entries; i += DS_THREADS) {
         const int e = p.sel[i];
         if (e >= 0 && e < NE) atomicAdd(&cnt[e], 1);
-        else if (p.err) atomicCAS(p.err, 0, DEV_ERR_BAD_SLOT);
+        else if (e >= NE && p.err) atomicCAS(p.err, 0, DEV_ERR_BAD_SLOT);
     }
     __syncthreads();
     if (tid == 0) {

@@ -1,0 +1,179 @@
+// ep.cu -- expert-parallel row exchange kernels (include/loki_ep.h): pack rows for their owner ranks,
+// unpack the received row headers, and the home-side combine of the returned partial sums.
+//
+// No counterpart in the reference (one GPU, experts streamed from NVMe by src/moe_stream_buffer.h).  The
+// arithmetic the rows feed is the single-GPU expert stage; only the order of the final sum differs: the
+// home rank adds the per-rank partial sums (each summed in entry order on its rank) in rank order.
+#include "../../include/loki_ep.h"
+#include "moe_internal.h"
+#include "moe_device.cuh"
+
+namespace lk {
+
+constexpr int EP_PLAN_THREADS = 1024;
+constexpr int EP_ROW_FLOATS = LK_EP_ROW_BYTES / 4;
+static_assert(LK_EP_ROW_BYTES % 16 == 0, "rows must keep 16-byte alignment");
+
+struct EpRowHdr { int sel[8]; float w[8]; };
+static_assert(sizeof(EpRowHdr) == LK_EP_ROW_HDR_BYTES, "header size");
+
+// one CTA: per destination rank the stable (token-ascending) row index of every token that has an entry
+// there, the per-rank counts, block offsets (fixed capacity or compact) and the headers of unused rows
+__global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(const int* __restrict__ sel, int T, int keep, int n_ranks,
+                                                              int cap, int* counts, int* row_map, uint8_t* send, int* err) {
+    __shared__ int wc[LK_EP_MAX_RANKS][32], pre[LK_EP_MAX_RANKS][32], base[LK_EP_MAX_RANKS], off[LK_EP_MAX_RANKS + 1];
+    __shared__ int cnt[LK_EP_MAX_RANKS];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int epr = N_EXPERTS / n_ranks;
+    if (tid < LK_EP_MAX_RANKS) base[tid] = 0;
+    __syncthreads();
+    for (int c0 = 0; c0 < T; c0 += EP_PLAN_THREADS) {
+        const int t = c0 + tid;
+        unsigned mask = 0;
+        if (t < T) {
+            for (int k = 0; k < keep; ++k) {
+                const int e = sel[t * keep + k];
+                if (e >= 0 && e < N_EXPERTS) mask |= 1u << (e / epr);
+                else if (err) atomicCAS(err, 0, DEV_ERR_BAD_SLOT);
+            }
+        }
+        int in_warp[LK_EP_MAX_RANKS];
+        #pragma unroll
+        for (int d = 0; d < LK_EP_MAX_RANKS; ++d) {
+            const unsigned b = __ballot_sync(0xffffffffu, d < n_ranks && ((mask >> d) & 1u));
+            in_warp[d] = __popc(b & ((1u << lane) - 1u));
+            if (lane == 0) wc[d][warp] = __popc(b);
+        }
+        __syncthreads();
+        if (tid < LK_EP_MAX_RANKS * 32) {
+            const int d = tid >> 5, w = tid & 31;
+            int s = 0;
+            for (int i = 0; i < w; ++i) s += wc[d][i];
+            pre[d][w] = s;
+        }
+        __syncthreads();
+        if (t < T) {
+            for (int d = 0; d < n_ranks; ++d)
+                row_map[(size_t)t * n_ranks + d] = ((mask >> d) & 1u) ? base[d] + pre[d][warp] + in_warp[d] : -1;
+        }
+        __syncthreads();
+        if (tid < LK_EP_MAX_RANKS) base[tid] += pre[tid][31] + wc[tid][31];
+        __syncthreads();
+    }
+    if (tid == 0) {
+        off[0] = 0;
+        for (int d = 0; d < n_ranks; ++d) {
+            int n = base[d];
+            if (cap > 0 && n > cap) { if (err) atomicCAS(err, 0, DEV_ERR_BAD_SLOT); n = cap; }
+            counts[d] = n; cnt[d] = n;
+            off[d + 1] = off[d] + (cap > 0 ? cap : n);
+        }
+    }
+    __syncthreads();
+    for (int t = tid; t < T; t += EP_PLAN_THREADS) {           // same tokens as above: own writes are visible
+        for (int d = 0; d < n_ranks; ++d) {
+            int* m = row_map + (size_t)t * n_ranks + d;
+            const int v = *m;
+            if (v >= 0) *m = (cap > 0 && v >= cap) ? -1 : off[d] + v;
+        }
+    }
+    if (cap > 0) {                                             // unused rows of fixed-capacity blocks: no entries
+        for (int d = 0; d < n_ranks; ++d) {
+            for (int r = cnt[d] + (tid >> 4); r < cap; r += EP_PLAN_THREADS / 16) {
+                int* h = (int*)(send + (size_t)(off[d] + r) * LK_EP_ROW_BYTES);
+                h[tid & 15] = (tid & 15) < 8 ? -1 : 0;
+            }
+        }
+    }
+}
+
+// one CTA per token: header and activations of each of its rows (x read once, written to every row)
+__global__ void __launch_bounds__(256) k_ep_copy(const int* __restrict__ sel, const float* __restrict__ w,
+                                                  const float* __restrict__ x, int keep, int n_ranks,
+                                                  const int* __restrict__ row_map, uint8_t* send) {
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const int epr = N_EXPERTS / n_ranks;
+    int rows[LK_EP_MAX_RANKS];
+    #pragma unroll
+    for (int d = 0; d < LK_EP_MAX_RANKS; ++d) rows[d] = d < n_ranks ? row_map[(size_t)t * n_ranks + d] : -1;
+    if (tid < 16 * LK_EP_MAX_RANKS) {
+        const int d = tid >> 4, j = tid & 15, k = j & 7;
+        if (rows[d] >= 0) {
+            int* h = (int*)(send + (size_t)rows[d] * LK_EP_ROW_BYTES);
+            const int e = k < keep ? sel[t * keep + k] : -1;
+            const bool mine = e >= d * epr && e < (d + 1) * epr;
+            if (j < 8) h[j] = mine ? e - d * epr : -1;
+            else ((float*)h)[j] = mine ? w[t * keep + k] : 0.f;
+        }
+    }
+    const float4* src = (const float4*)(x + (size_t)t * HIDDEN);
+    for (int i = tid; i < HIDDEN / 4; i += 256) {
+        const float4 v = src[i];
+        #pragma unroll
+        for (int d = 0; d < LK_EP_MAX_RANKS; ++d)
+            if (rows[d] >= 0) ((float4*)(send + (size_t)rows[d] * LK_EP_ROW_BYTES + LK_EP_ROW_HDR_BYTES))[i] = v;
+    }
+}
+
+__global__ void k_ep_unpack(const uint8_t* __restrict__ recv, int R, int keep, int* sel, float* w) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= R * keep) return;
+    const int r = i / keep, k = i % keep;
+    const EpRowHdr* h = (const EpRowHdr*)(recv + (size_t)r * LK_EP_ROW_BYTES);
+    sel[i] = h->sel[k];
+    w[i] = h->w[k];
+}
+
+__global__ void k_ep_combine(const float* __restrict__ ret, const int* __restrict__ row_map, int T, int n_ranks,
+                             const float* __restrict__ hpart, float* h, float* moe) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;       // float4 index over T x HIDDEN
+    if (i >= T * (HIDDEN / 4)) return;
+    const int t = i / (HIDDEN / 4), c = i % (HIDDEN / 4);
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int d = 0; d < n_ranks; ++d) {
+        const int row = row_map[(size_t)t * n_ranks + d];
+        if (row < 0) continue;
+        const float4 v = ((const float4*)(ret + (size_t)row * HIDDEN))[c];
+        r.x += v.x; r.y += v.y; r.z += v.z; r.w += v.w;
+    }
+    if (moe) ((float4*)(moe + (size_t)t * HIDDEN))[c] = r;
+    if (h && hpart) {
+        const float4 b = ((const float4*)(hpart + (size_t)t * HIDDEN))[c];
+        ((float4*)(h + (size_t)t * HIDDEN))[c] = make_float4(b.x + r.x, b.y + r.y, b.z + r.z, b.w + r.w);
+    }
+}
+
+void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, cudaStream_t st) {
+    const int n = R * keep;
+    k_ep_unpack<<<(n + 255) / 256, 256, 0, st>>>((const uint8_t*)recv, R, keep, sel, w);
+}
+
+}  // namespace lk
+
+using namespace lk;
+
+extern "C" {
+
+int lk_ep_pack(const int* sel, const float* w, const float* x, int T, int keep, int n_ranks, int cap, void* send_rows,
+               int* send_counts, int* row_map, int* err, lk_stream_t stream) {
+    if (T < 0 || keep < 1 || keep > MAX_TOPK || n_ranks < 1 || n_ranks > LK_EP_MAX_RANKS || (N_EXPERTS % n_ranks) ||
+        cap < 0 || (cap > 0 && cap < T) || !send_counts || (T > 0 && (!sel || !w || !x || !send_rows || !row_map)))
+        return LK_ERR_ARG;
+    if (((uintptr_t)send_rows & 15) || ((uintptr_t)x & 15)) return LK_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    k_ep_plan<<<1, EP_PLAN_THREADS, 0, st>>>(sel, T, keep, n_ranks, cap, send_counts, row_map, (uint8_t*)send_rows, err);
+    if (T > 0) k_ep_copy<<<T, 256, 0, st>>>(sel, w, x, keep, n_ranks, row_map, (uint8_t*)send_rows);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+int lk_ep_combine(const float* ret, const int* row_map, int T, int n_ranks, const float* h_partial, float* h, float* moe,
+                  lk_stream_t stream) {
+    if (T < 0 || n_ranks < 1 || n_ranks > LK_EP_MAX_RANKS || (T > 0 && (!row_map || (!ret && n_ranks > 0))))
+        return LK_ERR_ARG;
+    if (T == 0) return LK_OK;
+    const int n = T * (HIDDEN / 4);
+    k_ep_combine<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(ret, row_map, T, n_ranks, h_partial, h, moe);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+}  // extern "C"

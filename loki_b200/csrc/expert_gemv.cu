@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(ExpertParams p) {
                 for (int i = g; i < DN_CH_ROWS * p.T; i += DN_KG) {
                     const int row = r0 + (i & 7), t = i >> 3;
                     float m = 0.0f;
-                    for (int k = 0; k < p.keep; ++k) m += __ldcg(p.y + ((size_t)t * p.keep + k) * HIDDEN + row);
+                    for (int k = 0; k < p.keep; ++k) if (!p.sel || p.sel[t * p.keep + k] >= 0) m += __ldcg(p.y + ((size_t)t * p.keep + k) * HIDDEN + row);
                     if (p.moe) p.moe[(size_t)t * HIDDEN + row] = m;
                     if (p.h) {
                         float hv = p.resid[(size_t)t * HIDDEN + row];

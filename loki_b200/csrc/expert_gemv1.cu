@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
                     for (int i = lane; i < 8 * p.T; i += 32) {
                         const int row = row0 + (i & 7), t = i >> 3;
                         float m = 0.0f;
-                        for (int kk = 0; kk < p.keep; ++kk) m += __ldcg(p.y + ((size_t)t * p.keep + kk) * HIDDEN + row);
+                        for (int kk = 0; kk < p.keep; ++kk) if (!p.sel || p.sel[t * p.keep + kk] >= 0) m += __ldcg(p.y + ((size_t)t * p.keep + kk) * HIDDEN + row);
                         if (p.moe) p.moe[(size_t)t * HIDDEN + row] = m;
                         if (p.h) {
                             float hv = p.resid[(size_t)t * HIDDEN + row];

@@ -7,6 +7,7 @@
 #include <string>
 #include <algorithm>
 #include "../../include/loki_moe.h"
+#include "../../include/loki_ep.h"
 #include "moe_internal.h"
 
 using namespace lk;
@@ -69,7 +70,7 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LkMoeCtx* c = nullptr;
     if (!cfg || !out) return LK_ERR_ARG;
     *out = nullptr;
-    if (cfg->n_experts != N_EXPERTS || cfg->topk < 1 || cfg->topk > MAX_TOPK || cfg->keep < 1 || cfg->keep > cfg->topk ||
+    if (cfg->n_experts < 1 || cfg->n_experts > N_EXPERTS || cfg->topk < 1 || cfg->topk > MAX_TOPK || cfg->keep < 1 || cfg->keep > cfg->topk ||
         cfg->max_tokens < 1 || !(cfg->n_group == 1 || (cfg->n_group * 32 == cfg->n_experts && cfg->topk_group >= 1 &&
         cfg->topk_group <= cfg->n_group)))
         return LK_ERR_UNSUPPORTED;
@@ -152,6 +153,7 @@ int lk_moe_route(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int T, cons
     if (T == 0) return LK_OK;
     if (T > c->cfg.max_tokens) return set_err(c, LK_ERR_CAPACITY, "T=%d > capacity %d", T, c->cfg.max_tokens);
     if (!W || !W->router_w || !W->router_bias) return set_err(c, LK_ERR_ARG, "router weights missing");
+    if (c->cfg.n_experts != N_EXPERTS) return set_err(c, LK_ERR_UNSUPPORTED, "the router needs a 256-expert context");
     cudaStream_t st = (cudaStream_t)stream;
     RouterParams p = router_params(c, W, x, T, logits_override, sel ? sel : c->sel, w ? w : c->w, false);
     launch_router(p, st);
@@ -176,19 +178,20 @@ int lk_moe_dispatch(LkMoeCtx* c, const int* sel, const float* w, int T, int keep
 }
 
 // experts for routing already in c->slot_* (built by the router for T == 1, or by the dispatch kernel)
-static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, int keep,
-                       float* h, float* moe, int nt, cudaStream_t st) {
+// x rows are ld_x floats apart; sel (optional) marks absent entries (negative ids) that the combine skips
+static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, int keep,
+                       const int* sel, float* h, float* moe, int nt, cudaStream_t st) {
     ExpertParams e{};
     e.gate = (const uint8_t*)W->gate; e.up = (const uint8_t*)W->up; e.down = (const uint8_t*)W->down;
     e.gate_stride = W->gate_stride; e.up_stride = W->up_stride; e.down_stride = W->down_stride;
     e.sh_gate = (const uint8_t*)W->sh_gate; e.sh_up = (const uint8_t*)W->sh_up; e.sh_down = (const uint8_t*)W->sh_down;
-    e.x = x; e.ld_x = HIDDEN;
+    e.x = x; e.ld_x = ld_x;
     e.slot_expert = c->slot_expert; e.slot_tok = c->slot_tok; e.slot_out = c->slot_out; e.slot_w = c->slot_w; e.nslots = c->nslots;
     e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err;
     if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
     if (h || moe) {                   // the combine runs inside the down kernel
         e.chunk_count = c->chunk_count; e.resid = resid; e.shared_sep = nullptr; e.h = h; e.moe = moe;
-        e.T = T; e.keep = keep; e.with_shared = c->cfg.with_shared;
+        e.T = T; e.keep = keep; e.with_shared = c->cfg.with_shared; e.sel = sel;
     }
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
@@ -201,7 +204,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const
 }
 
 // the tensor-core path: 64-token slots, q8->fp16 activations, gate/up GEMM + SwiGLU, down GEMM, combine
-static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, const int* sel,
+static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
                          const float* w, int keep, float* h, float* moe, cudaStream_t st) {
     SlotParams s{};
     s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = GEMM_NT; s.with_shared = c->cfg.with_shared;
@@ -213,7 +216,7 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, con
     g.gate = (const uint8_t*)W->gate; g.up = (const uint8_t*)W->up; g.down = (const uint8_t*)W->down;
     g.gate_stride = W->gate_stride; g.up_stride = W->up_stride; g.down_stride = W->down_stride;
     g.sh_gate = (const uint8_t*)W->sh_gate; g.sh_up = (const uint8_t*)W->sh_up; g.sh_down = (const uint8_t*)W->sh_down;
-    g.x = x; g.ld_x = HIDDEN; g.T = T;
+    g.x = x; g.ld_x = ld_x; g.T = T;
     g.slot_expert = c->g_expert; g.slot_tok = c->g_tok; g.slot_out = c->g_out; g.slot_w = c->g_w; g.nslots = c->g_n;
     g.xh = c->xh; g.hb = c->hb; g.y = c->y; g.err = c->err;
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
@@ -223,7 +226,7 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, con
         if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
         CombineParams cp{};
         cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
-        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN;
+        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel;
         launch_combine(cp, st);
     }
     if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
@@ -245,10 +248,10 @@ int lk_moe_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const flo
     if (rc) return rc;
     if (T > c->cfg.max_tokens || keep > c->cfg.keep) return set_err(c, LK_ERR_CAPACITY, "T=%d keep=%d above capacity", T, keep);
     cudaStream_t st = (cudaStream_t)stream;
-    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, resid, T, sel, w, keep, h, moe, st);
+    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, HIDDEN, resid, T, sel, w, keep, h, moe, st);
     rc = lk_moe_dispatch(c, sel, w, T, keep, nullptr, nullptr, nullptr, stream);
     if (rc) return rc;
-    return run_experts(c, W, x, resid, T, keep, h, moe, slot_nt(T), st);
+    return run_experts(c, W, x, HIDDEN, resid, T, keep, sel, h, moe, slot_nt(T), st);
 }
 
 int lk_moe_forward(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T,
@@ -258,23 +261,62 @@ int lk_moe_forward(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const flo
     int rc = check_weights(c, W, true);
     if (rc) return rc;
     if (T > c->cfg.max_tokens) return set_err(c, LK_ERR_CAPACITY, "T=%d > capacity %d", T, c->cfg.max_tokens);
+    if (c->cfg.n_experts != N_EXPERTS) return set_err(c, LK_ERR_UNSUPPORTED, "the router needs a 256-expert context");
     cudaStream_t st = (cudaStream_t)stream;
     const int keep = c->cfg.keep;
     RouterParams p = router_params(c, W, x, T, logits_override, c->sel, c->w, T == 1);
     launch_router(p, st);
     if (T >= c->gemm_min_tokens) {
-        rc = run_gemm_path(c, W, x, resid, T, c->sel, c->w, keep, h, moe, st);
+        rc = run_gemm_path(c, W, x, HIDDEN, resid, T, c->sel, c->w, keep, h, moe, st);
     } else {
         if (T > 1) {
             rc = lk_moe_dispatch(c, c->sel, c->w, T, keep, nullptr, nullptr, nullptr, stream);
             if (rc) return rc;
         }
-        rc = run_experts(c, W, x, resid, T, keep, h, moe, slot_nt(T), st);
+        rc = run_experts(c, W, x, HIDDEN, resid, T, keep, c->sel, h, moe, slot_nt(T), st);
     }
     if (rc) return rc;
     if (sel) LK_CU(cudaMemcpyAsync(sel, c->sel, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));
     if (w) LK_CU(cudaMemcpyAsync(w, c->w, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));
     return LK_OK;
+}
+
+// ---- expert-parallel stages that run on a context (include/loki_ep.h)
+int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int R, int keep, float* out, lk_stream_t stream) {
+    if (!c || !W || R < 0 || keep < 1 || (R > 0 && (!recv_rows || !out))) return set_err(c, LK_ERR_ARG, "bad argument");
+    if (c->cfg.with_shared) return set_err(c, LK_ERR_ARG, "expert-side context must have with_shared = 0");
+    if (R > c->cfg.max_tokens || keep > c->cfg.keep) return set_err(c, LK_ERR_CAPACITY, "R=%d keep=%d above capacity", R, keep);
+    if (R == 0) return LK_OK;
+    if ((uintptr_t)recv_rows & 15) return set_err(c, LK_ERR_ARG, "rows must be 16-byte aligned");
+    int rc = check_weights(c, W, false);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    launch_ep_unpack(recv_rows, R, keep, c->sel, c->w, st);
+    const float* x = (const float*)((const uint8_t*)recv_rows + LK_EP_ROW_HDR_BYTES);
+    const int ld = LK_EP_ROW_BYTES / 4;
+    if (R >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld, nullptr, R, c->sel, c->w, keep, nullptr, out, st);
+    rc = lk_moe_dispatch(c, c->sel, c->w, R, keep, nullptr, nullptr, nullptr, stream);
+    if (rc) return rc;
+    return run_experts(c, W, x, ld, nullptr, R, keep, c->sel, nullptr, out, slot_nt(R), st);
+}
+
+int lk_ep_shared(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, float* h_partial,
+                 lk_stream_t stream) {
+    if (!c || !W || T < 0 || (T > 0 && (!x || !resid || !h_partial))) return set_err(c, LK_ERR_ARG, "bad argument");
+    if (!c->cfg.with_shared || !W->sh_gate || !W->sh_up || !W->sh_down)
+        return set_err(c, LK_ERR_ARG, "the shared expert needs with_shared = 1 and W->sh_*");
+    if (W->down_fmt != LK_FMT_IQ2) return set_err(c, LK_ERR_UNSUPPORTED, "down format %d", W->down_fmt);
+    if (T > c->cfg.max_tokens) return set_err(c, LK_ERR_CAPACITY, "T=%d > capacity %d", T, c->cfg.max_tokens);
+    if (T == 0) return LK_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, HIDDEN, resid, T, nullptr, nullptr, 0, h_partial, nullptr, st);
+    SlotParams s{};                   // keep = 0: shared-expert slots only
+    s.sel = nullptr; s.w = nullptr; s.T = T; s.keep = 0; s.n_experts = c->cfg.n_experts; s.nt = slot_nt(T); s.with_shared = 1;
+    s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
+    s.slot_expert = c->slot_expert; s.slot_tok = c->slot_tok; s.slot_out = c->slot_out; s.slot_w = c->slot_w;
+    s.nslots = c->nslots; s.max_slots = c->max_slots; s.err = c->err;
+    launch_build_slots(s, st);
+    return run_experts(c, W, x, HIDDEN, resid, T, 0, nullptr, h_partial, nullptr, slot_nt(T), st);
 }
 
 const float* lk_moe_slot_outputs(LkMoeCtx* c) { return c ? c->y : nullptr; }

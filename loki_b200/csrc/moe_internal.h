@@ -29,7 +29,7 @@ void launch_router(const RouterParams& p, cudaStream_t st);
 
 // ---- dispatch: per-expert stable token lists and the work-slot table of the grouped matvecs
 struct SlotParams {
-    const int* sel; const float* w; int T; int keep;   // [T][keep]
+    const int* sel; const float* w; int T; int keep;   // [T][keep]; negative ids are absent entries (skipped)
     int n_experts; int nt;                              // tokens per slot (<= MAX_NT)
     int with_shared;
     int* counts; int* offsets; int* perm;               // [n_experts], [n_experts+1], [T*keep]
@@ -56,6 +56,7 @@ struct ExpertParams {
     // rows of all T tokens (shared = y rows T*keep + t when with_shared, and/or the shared_sep rows)
     int* chunk_count;                                 // HIDDEN/8 zeroed counters (left zeroed)
     const float* resid; const float* shared_sep; float* h; float* moe; int T; int keep; int with_shared;
+    const int* sel;                                   // optional [T][keep]: entries with a negative id are not summed
 };
 void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st);
 void launch_down(const ExpertParams& p, int nt, int grid, cudaStream_t st);
@@ -66,6 +67,7 @@ struct CombineParams {
     const float* y; const float* resid; int T; int keep; int with_shared;
     const float* shared;              // optional [T][HIDDEN] shared-expert output added to h
     float* h; float* moe; int ld_out;
+    const int* sel;                   // optional [T][keep]: entries with a negative id are not summed
 };
 void launch_combine(const CombineParams& p, cudaStream_t st);
 
@@ -86,6 +88,9 @@ void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st);
 // ---- seeded IQ2_XXS weight generation (moe_format.h generator) for n_experts consecutive experts
 void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
                     int64_t stride, cudaStream_t st);
+
+// ---- expert-parallel row headers -> sel/w [R][keep]
+void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, cudaStream_t st);
 
 int num_sms(int device);
 

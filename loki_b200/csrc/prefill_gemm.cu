@@ -10,7 +10,7 @@
 //   {08, 19, 2B, F0, CE, AA} and a high byte in {64, 63} -- eight bytes -- so one byte-permute over the
 //   constant pair (0x642B1908, 0x63AACEF0) yields two fp16 values 1024+v; the selectors are the OR of a
 //   per-grid-entry table (codes) and a per-sign-index table (signs), both 64-bit and lane-private.  One
-//   hfma2 (x*m - 1024*m) gives v*m exactly (m = 2*scale+1), one hmul2 by d/8 rounds once.
+//   hfma2 (x*s - 1024*s, 1024*s exact) gives v*s, s = fp16(d*(2*scale+1)/8).
 // B (activations): fp16 of the q8-dequantised values (k_x_q8_f16), gathered per slot token.
 // Pipeline: decode warps fill a 2-stage ring and arrive on full[]; one thread issues 4 K=16 MMAs per
 //   tile per stage and commits to empty[]; after the last stage a commit to accfull[] releases the
@@ -28,6 +28,7 @@ constexpr int PG_M = 128;                    // weight rows per accumulator tile
 constexpr int PG_NMAX = GEMM_NT;             // tokens per slot (64)
 constexpr int PG_KB = 64;                    // K per pipeline stage
 constexpr int PG_NST = 2;
+constexpr int PG_PF = 4;                     // K blocks of global loads in flight per decode thread
 constexpr int PG_DWARPS = 16;                // decode / B-load / epilogue warps
 constexpr int PG_THREADS = (PG_DWARPS + 1) * 32;
 constexpr int PG_A_BYTES = PG_M * PG_KB * 2;             // 16 KB
@@ -88,21 +89,20 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
 // decode one IQ2_XXS group (32 weights) of a row into 4 x 16-byte fp16 core-matrix rows of an A tile
 __device__ __forceinline__ void decode_group_f16(uint32_t aux0, uint32_t aux1, float d, const uint2* gtl, const uint2* stl,
                                                  uint8_t* dst, int k8_stride) {
-    // (1024 + v) * m - 1024 * m = v * m exactly (|v*m| <= 43*31 < 2048), then one rounding by d / 8
-    const uint32_t mi = 2u * (aux1 >> 28) + 1u;
-    const uint32_t m2 = (uint32_t)__half_as_ushort(__uint2half_rn(mi)) * 0x10001u;
-    const uint32_t c2 = (uint32_t)__half_as_ushort(__uint2half_rn(1024u * mi)) * 0x10001u ^ 0x80008000u;   // -1024*m
-    const uint32_t s2 = (uint32_t)__half_as_ushort(__float2half_rn(d * 0.125f)) * 0x10001u;
+    // (1024 + v) * s - 1024 * s = v * s with s = fp16(d * (2*scale+1) / 8); 1024 * s is exact (power of two)
+    const __half hs = __float2half_rn(d * (float)(2u * (aux1 >> 28) + 1u) * 0.125f);
+    const uint32_t s2 = (uint32_t)__half_as_ushort(hs) * 0x10001u;
+    const uint32_t c2 = (uint32_t)__half_as_ushort(__hmul(hs, __float2half_rn(-1024.0f))) * 0x10001u;
     #pragma unroll
     for (int l = 0; l < 4; ++l) {
         const uint2 g = gtl[((aux0 >> (8 * l)) & 0xFFu) * 32];
         const uint2 sg = stl[((aux1 >> (7 * l)) & 0x7Fu) * 32];
         const uint32_t sx = g.x | sg.x, sy = g.y | sg.y;
         uint4 out;
-        out.x = hmul2_u32(hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx), m2, c2), s2);
-        out.y = hmul2_u32(hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx >> 16), m2, c2), s2);
-        out.z = hmul2_u32(hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy), m2, c2), s2);
-        out.w = hmul2_u32(hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy >> 16), m2, c2), s2);
+        out.x = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx), s2, c2);
+        out.y = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx >> 16), s2, c2);
+        out.z = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy), s2, c2);
+        out.w = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy >> 16), s2, c2);
         *(uint4*)(dst + l * k8_stride) = out;
     }
 }
@@ -194,10 +194,10 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
         }
     } else {
         // ---------------------------------------------------------------- decode / B load / epilogue warps
-        const int mat = tid >> 8, row = (tid >> 1) & (PG_M - 1), grp = tid & 1;   // A unit of this thread
+        const int mat = tid >> 8, row = (tid >> 1) & (PG_M - 1), grp = tid & 1;   // A unit: lane pairs share a row (L1 lines)
         const uint2* gtl = gtab + lane;
         const uint2* stl = stab + lane;
-        const int bn = tid >> 3, bk8 = tid & 7;                                       // B chunk of this thread
+        const int bn = tid >> 3, bk8 = tid & 7;                                       // B chunk: 8 lanes read one token's 128 B
         uint32_t it = 0;
         for (int i = 0, item = blockIdx.x; item < nitems; ++i, item += gridDim.x) {
             const int s = item % nslots, rt = item / nslots;
@@ -215,23 +215,41 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
             const int btok = p.slot_tok[s * PG_NMAX + bn];
             const int bsrc = DOWN ? p.slot_out[s * PG_NMAX + bn] : btok;            // B row: h entry (down) / token (gate/up)
             const __half* bbase = DOWN ? p.hb : p.xh;
-            for (int kb = 0; kb < NKB; ++kb, ++it) {
-                const int st = it % PG_NST;
-                if (!*abort_flag && !mbar_wait(&empty[st], ((it / PG_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) *abort_flag = 1;
+            // register prefetch ring: the global loads of K block kb + PG_PF are issued while kb is decoded
+            uint32_t pw[PG_PF][3]; unsigned short pd[PG_PF]; uint4 pb[PG_PF];
+            auto issue = [&](int kb, int j) {
+                const int sb = kb >> 2, gi = (kb & 3) * 2 + grp;
+                const uint32_t off = (uint32_t)sb * BLK_IQ2 + 2u + 8u * (uint32_t)gi;
+                const uint32_t* w = (const uint32_t*)(wrow + (off & ~3u));
+                pw[j][0] = __ldg(w); pw[j][1] = __ldg(w + 1); pw[j][2] = __ldg(w + 2);
+                pd[j] = __ldg((const unsigned short*)(wrow + (size_t)sb * BLK_IQ2));
+                pb[j] = bsrc >= 0 ? __ldg((const uint4*)(bbase + (size_t)bsrc * K + kb * PG_KB + bk8 * 8)) : make_uint4(0u, 0u, 0u, 0u);
+            };
+            #pragma unroll
+            for (int j = 0; j < PG_PF; ++j) issue(j, j);
+            for (int kb0 = 0; kb0 < NKB; kb0 += PG_PF) {
+                #pragma unroll
+                for (int j = 0; j < PG_PF; ++j, ++it) {
+                    const int kb = kb0 + j;
+                    const int st = it % PG_NST;
+                    if (!*abort_flag && !mbar_wait(&empty[st], ((it / PG_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) *abort_flag = 1;
+                    uint8_t* a = ring + st * PG_STAGE + mat * PG_A_BYTES;
+                    uint8_t* b = ring + st * PG_STAGE + 2 * PG_A_BYTES;
+                    // A: group grp of this K block (2 groups per 64 columns) -> k8 blocks 4*grp .. 4*grp+3, row `row`
+                    const int gi = (kb & 3) * 2 + grp;
+                    const uint32_t sh = ((((uint32_t)(kb >> 2) * BLK_IQ2 + 2u + 8u * (uint32_t)gi)) & 3u) * 8u;
+                    const uint32_t aux0 = __funnelshift_r(pw[j][0], pw[j][1], sh), aux1 = __funnelshift_r(pw[j][1], pw[j][2], sh);
+                    const float d = __half2float(__ushort_as_half(pd[j]));
+                    const uint4 bv = pb[j];
+                    if (kb + PG_PF < NKB) issue(kb + PG_PF, j);
+                    decode_group_f16(aux0, aux1, d, gtl, stl, a + (4 * grp) * PG_A_LBO + (row >> 3) * 128 + (row & 7) * 16, PG_A_LBO);
+                    // B: token bn, k8 block bk8 (16 bytes)
+                    *(uint4*)(b + bk8 * PG_B_LBO + (bn >> 3) * 128 + (bn & 7) * 16) = bv;
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full[st]);
+                }
                 if (*abort_flag) break;
-                uint8_t* a = ring + st * PG_STAGE + mat * PG_A_BYTES;
-                uint8_t* b = ring + st * PG_STAGE + 2 * PG_A_BYTES;
-                // A: group grp of this K block (2 groups per 64 columns) -> k8 blocks 4*grp .. 4*grp+3, row `row`
-                uint32_t aux0, aux1; float d;
-                load_group_global(wrow, kb >> 2, (kb & 3) * 2 + grp, aux0, aux1, d);
-                decode_group_f16(aux0, aux1, d, gtl, stl, a + (4 * grp) * PG_A_LBO + (row >> 3) * 128 + (row & 7) * 16, PG_A_LBO);
-                // B: token bn, k8 block bk8 (16 bytes)
-                uint4 bv = make_uint4(0u, 0u, 0u, 0u);
-                if (bsrc >= 0) bv = __ldg((const uint4*)(bbase + (size_t)bsrc * K + kb * PG_KB + bk8 * 8));
-                *(uint4*)(b + bk8 * PG_B_LBO + (bn >> 3) * 128 + (bn & 7) * 16) = bv;
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full[st]);
             }
             if (*abort_flag) break;
             // ------------------------------------------------ epilogue of item i

@@ -1,0 +1,147 @@
+"""Expert-parallel MoE layer: 256 routed experts sharded over the GPUs of one node (include/loki_ep.h).
+
+No counterpart in the reference, which runs one GPU and streams experts from NVMe
+(src/moe_stream_buffer.h).  Rank r keeps experts [r*E, (r+1)*E) (E = 256 / n_ranks) resident, plus
+the router and the shared expert.  Tokens stay on their home rank; one layer is
+
+    home   route -> pack rows per owner rank                 shared expert (overlaps exchange #1)
+    exchange #1: rows (all-to-all)
+    owner  expert stage on the received rows -> per-row partial sums
+    exchange #2: partial sums (all-to-all, the transpose of #1)
+    home   combine: h = resid + shared + sum over ranks, moe = sum over ranks
+
+The exchanges go through a communicator with torch.distributed's all_to_all_single signature (NCCL over
+NVLink on GPUs; gloo in the CPU protocol tests).  Two row layouts: fixed capacity (block d holds up to
+`cap` rows, so no count exchange and no host synchronisation: decode, CUDA-graph friendly) and compact
+(block sizes exchanged first; the host learns them with one device->host copy: batch prefill).
+
+`ops` supplies the per-rank stages.  `NativeEpOps` runs them in libloki_moe.so on one GPU; it is the only
+implementation the package ships.
+"""
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import native as N
+from .moe import MoeLayer, _ptr, _stream
+from .native import HIDDEN, N_EXPERTS, EP_ROW_BYTES, check, lib
+
+
+class TorchComm:
+    """all-to-all over a torch.distributed process group (NCCL on GPUs)."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.size = dist.get_world_size(group)
+
+    def all_to_all(self, out, inp, out_splits=None, in_splits=None, async_op=False):
+        return dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group, async_op=async_op)
+
+
+class NativeEpOps:
+    """The per-rank stages on one GPU: a 256-expert home context (router, shared expert) and an expert
+    context over this rank's shard."""
+
+    def __init__(self, device, n_ranks, max_local_tokens, topk=8, keep=8, renorm=True, n_group=1, topk_group=1,
+                 scale=2.5):
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        self.n_ranks, self.keep = n_ranks, keep
+        self.home = MoeLayer(self.device, topk, keep, renorm, n_group, topk_group, scale, with_shared=True,
+                             max_tokens=max_local_tokens)
+        self.expert = MoeLayer(self.device, topk, keep, renorm, n_group, topk_group, scale, with_shared=False,
+                               max_tokens=max(1, n_ranks * max_local_tokens), n_experts=N_EXPERTS // n_ranks)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def set_gemm_threshold(self, min_tokens):
+        self.home.set_gemm_threshold(min_tokens)
+        self.expert.set_gemm_threshold(min_tokens)
+
+    def route(self, W, x, logits_override=None):
+        _, sel, w = self.home.route(W, x, logits_override=logits_override)
+        return sel, w
+
+    def pack(self, sel, w, x, cap):
+        T = x.shape[0]
+        rows = self.n_ranks * cap if cap else T * self.n_ranks
+        send = torch.empty(max(rows, 1), EP_ROW_BYTES, dtype=torch.uint8, device=self.device)
+        counts = torch.empty(self.n_ranks, dtype=torch.int32, device=self.device)
+        row_map = torch.empty(T, self.n_ranks, dtype=torch.int32, device=self.device)
+        check(lib().lk_ep_pack(_ptr(sel), _ptr(w), _ptr(x), T, sel.shape[1], self.n_ranks, cap, _ptr(send), _ptr(counts),
+                               _ptr(row_map), _ptr(self.err), _stream()))
+        return send, counts, row_map
+
+    def shared(self, W, x, resid):
+        hpart = torch.empty(x.shape[0], HIDDEN, device=self.device)
+        ws = W.struct()
+        self.home._check(lib().lk_ep_shared(self.home.ctx, ctypes.byref(ws), _ptr(x), _ptr(resid), x.shape[0], _ptr(hpart),
+                                            _stream()))
+        return hpart
+
+    def experts(self, W, recv, R, keep):
+        ret = torch.empty(max(R, 1), HIDDEN, device=self.device)
+        ws = W.struct()
+        self.expert._check(lib().lk_ep_experts(self.expert.ctx, ctypes.byref(ws), _ptr(recv), R, keep, _ptr(ret),
+                                               _stream()))
+        return ret[:R]
+
+    def combine(self, ret_home, row_map, hpart):
+        T = row_map.shape[0]
+        h = torch.empty(T, HIDDEN, device=self.device)
+        moe = torch.empty(T, HIDDEN, device=self.device)
+        check(lib().lk_ep_combine(_ptr(ret_home), _ptr(row_map), T, self.n_ranks, _ptr(hpart), _ptr(h), _ptr(moe),
+                                  _stream()))
+        return h, moe
+
+    def device_error(self):
+        self.home.device_error()
+        self.expert.device_error()
+        e = int(self.err.item())
+        if e:
+            self.err.zero_()
+            raise N.NativeError("expert-parallel pack: device error code %d" % e)
+
+
+class EpMoeLayer:
+    """One expert-parallel MoE layer call per rank.
+
+    comm: TorchComm (or any object with its all_to_all); ops: NativeEpOps.  `fixed_cap_max`: calls with at
+    most this many local tokens use the fixed-capacity layout (every rank must then pass the same T)."""
+
+    def __init__(self, comm, ops, fixed_cap_max=8):
+        self.comm, self.ops = comm, ops
+        self.n_ranks = comm.size
+        self.fixed_cap_max = fixed_cap_max
+        self.last_counts = None          # (rows sent per rank, rows received per rank) of the last compact call
+
+    def forward(self, W, x, resid, logits_override=None):
+        """W: this rank's LayerWeights shard (router + shared expert + experts [r*E, (r+1)*E)); x, resid:
+        [T][7168] fp32 home tokens.  Returns h, moe ([T][7168]), sel, w ([T][keep] global ids)."""
+        ops, comm, NR = self.ops, self.comm, self.n_ranks
+        T = x.shape[0]
+        sel, w = ops.route(W, x, logits_override)
+        keep = sel.shape[1]
+        fixed = T <= self.fixed_cap_max
+        cap = T if fixed else 0
+        send, counts, row_map = ops.pack(sel, w, x, cap)
+        if fixed:
+            recv = torch.empty(NR * cap, EP_ROW_BYTES, dtype=torch.uint8, device=send.device)
+            work = comm.all_to_all(recv, send[:NR * cap], async_op=True)
+            sent, got = None, None
+        else:
+            rcounts = torch.empty_like(counts)
+            comm.all_to_all(rcounts, counts)
+            both = torch.cat([counts, rcounts]).cpu().tolist()          # the one host synchronisation
+            sent, got = both[:NR], both[NR:]
+            self.last_counts = (sent, got)
+            recv = torch.empty(sum(got), EP_ROW_BYTES, dtype=torch.uint8, device=send.device)
+            work = comm.all_to_all(recv, send[:sum(sent)], got, sent, async_op=True)
+        hpart = ops.shared(W, x, resid)                                # overlaps exchange #1
+        work.wait()
+        R = recv.shape[0]
+        ret = ops.experts(W, recv, R, keep)
+        ret_home = torch.empty(NR * cap if fixed else sum(sent), HIDDEN, dtype=ret.dtype, device=ret.device)
+        comm.all_to_all(ret_home, ret, sent, got)
+        h, moe = ops.combine(ret_home, row_map, hpart)
+        return h, moe, sel, w

@@ -1,4 +1,4 @@
-"""ctypes binding of libloki_moe.so (include/loki_moe.h and include/loki_fused_moe.h).
+"""ctypes binding of libloki_moe.so (include/loki_moe.h, include/loki_fused_moe.h, include/loki_ep.h).
 
 The library is the product: every call here goes straight to the CUDA kernels.  There is no CPU or
 PyTorch fallback; a missing library raises at first use.
@@ -19,6 +19,9 @@ EXPERT_MATRIX_BYTES = MOE_INTER * (HIDDEN // QK) * BLK_IQ2          # 3 784 704 
 
 LK_OK, LK_ERR_ARG, LK_ERR_CUDA, LK_ERR_UNSUPPORTED, LK_ERR_CAPACITY, LK_ERR_DEVICE = 0, -1, -2, -3, -4, -5
 FMT_IQ2, FMT_Q2K, FMT_Q3K = 4, 5, 6
+EP_ROW_HDR_BYTES = 64
+EP_ROW_BYTES = EP_ROW_HDR_BYTES + HIDDEN * 4      # 28 736
+EP_MAX_RANKS = 8
 
 
 class LkMoeConfig(ctypes.Structure):
@@ -61,6 +64,10 @@ SIGNATURES = {
     "lk_moe_last_error": (ctypes.c_char_p, [_P]),
     "lk_moe_experts_noalloc": (_I, [ctypes.POINTER(LkMoeWeights), _P, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "lk_gen_iq2": (_I, [_P, ctypes.c_uint64, _I, _I, _I, _I, _I, _I, _I64, _P]),
+    "lk_ep_pack": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "lk_ep_experts": (_I, [_P, ctypes.POINTER(LkMoeWeights), _P, _I, _I, _P, _P]),
+    "lk_ep_shared": (_I, [_P, ctypes.POINTER(LkMoeWeights), _P, _P, _I, _P, _P]),
+    "lk_ep_combine": (_I, [_P, _P, _I, _I, _P, _P, _P, _P]),
     "fl_init": (_P, [_I, _I]),
     "fl_wide_init": (_I, [_P, _I, _I]),
     "fl_wide_moe": (None, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _I, _I, _I]),

@@ -7,7 +7,7 @@ import re
 import pytest
 
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADERS = [os.path.join(REPO, "include", h) for h in ("loki_moe.h", "loki_fused_moe.h")]
+HEADERS = [os.path.join(REPO, "include", h) for h in sorted(os.listdir(os.path.join(REPO, "include"))) if h.endswith(".h")]
 
 
 def declared():

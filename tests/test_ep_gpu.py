@@ -1,0 +1,119 @@
+"""Expert-parallel layer on the CUDA path (include/loki_ep.h through loki_b200.ep) against the oracle.
+
+* emulated ranks: 2 or 4 ranks as threads on one GPU (ThreadComm), each with its own 256/N-expert shard
+  and contexts: the pack / expert / shared / combine kernels and the exchange logic, on one device;
+* NCCL: 2 processes on 2 GPUs (skipped with fewer), the real all-to-all over NVLink.
+Routing must match the oracle bit-exactly; h / moe within RTOL_L2 of the single-GPU oracle layer.
+"""
+import os
+import socket
+import threading
+
+import numpy as np
+import pytest
+
+from moe_helpers import SEED, HIDDEN, RTOL_L2, rel_l2, oracle_layer
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _inputs(T_loc, rank):
+    rng = np.random.default_rng(500 + 7 * T_loc + rank)
+    return (rng.standard_normal((T_loc, HIDDEN)).astype(np.float32),
+            rng.standard_normal((T_loc, HIDDEN)).astype(np.float32))
+
+
+def _check_rank(oracle, W, x, r, h, moe, sel, w, keep=8):
+    sel, w = sel.cpu().numpy(), w.cpu().numpy()
+    Wr = W.router_w.float().cpu().numpy()
+    bias = W.router_bias.cpu().numpy()
+    _, osel, ow = oracle.router(x, Wr, bias, oracle.route_cfg(8, keep, 1, 1, 1))
+    np.testing.assert_array_equal(sel, osel)
+    np.testing.assert_array_equal(w, ow)
+    ref = oracle_layer(oracle, SEED, 0, x, r, sel, w)
+    e_moe, e_h = rel_l2(moe.cpu().numpy(), ref["moe"]), rel_l2(h.cpu().numpy(), ref["h"])
+    assert e_moe < RTOL_L2 and e_h < RTOL_L2, (e_moe, e_h)
+
+
+@pytest.mark.parametrize("n_ranks,T_loc,fixed_cap_max", [(2, 1, 8), (2, 5, 8), (4, 3, 8), (2, 12, 4)])
+def test_ep_emulated_ranks_one_gpu(native, oracle, n_ranks, T_loc, fixed_cap_max):
+    from loki_b200.moe import LayerWeights
+    from loki_b200.ep import EpMoeLayer, NativeEpOps
+    from ep_ref import ThreadComm
+    E = 256 // n_ranks
+    comms = ThreadComm.group(n_ranks)
+    shards = [LayerWeights("cuda", SEED, 0, n_experts=E, expert0=r * E) for r in range(n_ranks)]
+    ops = [NativeEpOps(0, n_ranks, T_loc) for _ in range(n_ranks)]
+    for o in ops:
+        o.set_gemm_threshold(1 << 20)              # the matvec path: same q8 scheme as the oracle
+    inputs = [_inputs(T_loc, r) for r in range(n_ranks)]
+    torch.cuda.synchronize()
+    out, errs = [None] * n_ranks, []
+
+    def run(rank):
+        try:
+            layer = EpMoeLayer(comms[rank], ops[rank], fixed_cap_max=fixed_cap_max)
+            x, r = (torch.from_numpy(a).cuda() for a in inputs[rank])
+            out[rank] = layer.forward(shards[rank], x, r)
+        except Exception as e:                     # surfaced below
+            errs.append(e)
+            comms[rank].hub.barrier.abort()
+
+    th = [threading.Thread(target=run, args=(k,)) for k in range(n_ranks)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(timeout=600)
+    assert not errs, errs
+    torch.cuda.synchronize()
+    for rank in range(n_ranks):
+        ops[rank].device_error()
+        _check_rank(oracle, shards[rank], *inputs[rank], *out[rank])
+
+
+def _nccl_worker(rank, port, T_loc, fixed_cap_max, out_dir):
+    import torch.distributed as dist
+    from loki_b200.moe import LayerWeights
+    from loki_b200.ep import EpMoeLayer, NativeEpOps, TorchComm
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=2,
+                            device_id=torch.device("cuda", rank))
+    try:
+        W = LayerWeights("cuda:%d" % rank, SEED, 0, n_experts=128, expert0=rank * 128)
+        ops = NativeEpOps(rank, 2, T_loc)
+        ops.set_gemm_threshold(1 << 20)
+        layer = EpMoeLayer(TorchComm(), ops, fixed_cap_max=fixed_cap_max)
+        x, r = (torch.from_numpy(a).cuda() for a in _inputs(T_loc, rank))
+        h, moe, sel, w = layer.forward(W, x, r)
+        torch.cuda.synchronize()
+        ops.device_error()
+        np.savez(os.path.join(out_dir, "r%d.npz" % rank), h=h.cpu().numpy(), moe=moe.cpu().numpy(),
+                 sel=sel.cpu().numpy(), w=w.cpu().numpy(), Wr=W.router_w.float().cpu().numpy(),
+                 b=W.router_bias.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("T_loc,fixed_cap_max", [(1, 8), (12, 4)])
+def test_ep_nccl_two_gpus(native, oracle, tmp_path, T_loc, fixed_cap_max):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.start_processes(_nccl_worker, args=(port, T_loc, fixed_cap_max, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    for rank in range(2):
+        got = np.load(os.path.join(str(tmp_path), "r%d.npz" % rank))
+        x, r = _inputs(T_loc, rank)
+        _, osel, ow = oracle.router(x, got["Wr"], got["b"], oracle.route_cfg(8, 8, 1, 1, 1))
+        np.testing.assert_array_equal(got["sel"], osel)
+        np.testing.assert_array_equal(got["w"], ow)
+        ref = oracle_layer(oracle, SEED, 0, x, r, osel, ow)
+        assert rel_l2(got["moe"], ref["moe"]) < RTOL_L2
+        assert rel_l2(got["h"], ref["h"]) < RTOL_L2
