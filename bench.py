@@ -9,9 +9,14 @@ captured as one CUDA graph per step.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill|imbalance] [--impl ours|reference]
 
-N > 1 (torchrun): the decode workload runs N independent replicas (one per GPU, each with all 58 layers:
-the weights fit one B200); value = tokens of all ranks / max-over-ranks time.  --impl reference times the
-CPU oracle (the restatement of the reference's CPU path) on the host cores on a bounded sample.
+N > 1 (torchrun): expert parallelism: rank r holds experts [r*256/N, (r+1)*256/N) of
+every layer (plus router and shared expert), and each rank decodes its own token (weak scaling: T=1 per
+GPU); per layer the rows go to the expert owners and the partial sums come back through two all-to-alls
+(the library's NCCL communicator, captured in the step's CUDA graph).  value = tokens of all ranks /
+max-over-ranks time.  `--parallelism replicas` runs N independent single-GPU replicas instead.
+`--workload prefill --tokens 4096` at N > 1 is BASELINE config 3 (expert-parallel batch, T global).
+--impl reference times the CPU oracle (the restatement of the reference's CPU path) on the host cores on a
+bounded sample.
 """
 import argparse
 import json
@@ -309,6 +314,215 @@ def run_decode(args, ws, rank, local, dist):
     return out, layers, ctx, structs, xs, rs
 
 
+def _min_over_ranks(dist, v):
+    import torch
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return float(t.item())
+
+
+def _ep_setup(args, ws, rank, local, dist, max_local_tokens, layers_wanted):
+    import torch
+    from loki_b200 import moe as M
+    from loki_b200.ep import EpMoeLayer, NativeEpOps, NativeComm
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    E = NE // ws
+    free, _ = torch.cuda.mem_get_info(dev)
+    per_layer = (3 * E + 3) * MAT + ROUTER_BYTES
+    distinct = int(_min_over_ranks(dist, max(1, min(layers_wanted, int((free - (10 << 30)) // per_layer)))))
+    shards = [M.LayerWeights(dev, SEED, L, n_experts=E, expert0=rank * E) for L in range(distinct)]
+    comm = NativeComm(local)
+    ops = NativeEpOps(local, ws, max_local_tokens, keep=args.keep)
+    torch.cuda.synchronize(dev)
+    return dev, shards, distinct, comm, ops, EpMoeLayer(comm, ops)
+
+
+def run_ep_decode(args, ws, rank, local, dist):
+    """Expert-parallel decode: T=1 token per rank through the layers, experts sharded 256/N per GPU."""
+    import torch
+    import ctypes
+    from loki_b200 import native as N
+    dev, shards, distinct, comm, ops, layer = _ep_setup(args, ws, rank, local, dist, 1, args.layers)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    xs = torch.randn(args.layers, 1, HIDDEN, device=dev, generator=g)
+    rs = torch.randn(args.layers, 1, HIDDEN, device=dev, generator=g)
+    outs = [None] * args.layers
+    L = N.lib()
+    ev = DriverEvents(4 * args.layers)
+
+    def step(events=False):
+        for i in range(args.layers):
+            if events:
+                L.lk_moe_set_events(ops.expert.ctx, (ctypes.c_void_p * 4)(*[ev.ev[4 * i + j].value for j in range(4)]))
+            outs[i] = layer.forward(shards[i % distinct], xs[i], rs[i])
+        if events:
+            L.lk_moe_set_events(ops.expert.ctx, None)
+
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        step()                                     # eager: kernel attributes, NCCL peer connections
+    torch.cuda.synchronize(dev)
+    ops.device_error()
+    graph, graph_ev = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_ev, stream=stream):
+        step(events=True)
+    with torch.cuda.graph(graph, stream=stream):       # captured last: `outs` are this graph's outputs
+        step()
+    torch.cuda.synchronize(dev)
+    for _ in range(args.warmup):
+        graph.replay()
+    barrier(dist)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        t1.record(stream)
+    barrier(dist)
+    ms = t0.elapsed_time(t1)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph_ev.replay()
+    torch.cuda.synchronize(dev)
+    barrier(dist)
+    # end to end: pinned host inputs in, every layer's h out, inside the timed region
+    hx = torch.empty(args.layers, 2, 1, HIDDEN, pin_memory=True)
+    hx.copy_(torch.stack([xs, rs], 1).cpu())
+    hout = torch.empty(args.layers, 1, HIDDEN, pin_memory=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(2, args.steps // 2)
+    barrier(dist)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(n_e2e):
+            xs.copy_(hx[:, 0], non_blocking=True)
+            rs.copy_(hx[:, 1], non_blocking=True)
+            graph.replay()
+            for i in range(args.layers):
+                hout[i].copy_(outs[i][0], non_blocking=True)
+        e1.record(stream)
+    barrier(dist)
+    e2e_ms = max_over_ranks(dist, e0.elapsed_time(e1))
+    cl = clocks.stop() if clocks else None
+    ops.device_error()
+    gu = np.array([ev.elapsed(4 * i, 4 * i + 1) for i in range(args.layers)])
+    dn = np.array([ev.elapsed(4 * i + 1, 4 * i + 2) for i in range(args.layers)])
+    # distinct local experts each layer's expert stage streamed (all ranks' selections)
+    sel = torch.stack([outs[i][2][0] for i in range(args.layers)])              # [layers][keep] this rank's token
+    if dist is not None:
+        allsel = [torch.empty_like(sel) for _ in range(ws)]
+        dist.all_gather(allsel, sel)
+        allsel = torch.stack(allsel, 1)                                         # [layers][ws][keep]
+    else:
+        allsel = sel[:, None]
+    E = NE // ws
+    loc = [(allsel[i][(allsel[i] // E) == rank]).unique().numel() for i in range(args.layers)]
+    gu_bytes = np.array([2 * MAT * n + 4 * HIDDEN * ws for n in loc], np.float64)
+    achieved = float(np.mean(gu_bytes / (gu / 1e3))) / 1e9
+    ach_all = max_over_ranks(dist, -achieved)
+    achieved_min = -ach_all
+    ms_max = max_over_ranks(dist, ms)
+    value = args.steps * ws / (ms_max / 1e3)
+    hbm, bf16, peak_kind = measured_peaks()
+    graph.reset()
+    graph_ev.reset()
+    comm.close()
+    out = {
+        "metric": "MoE-layer tokens/s (T=1 decode through 58 layers)", "value": round(value, 2), "unit": "tokens/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "iq2_xxs x q8 (int8 dp4a, fp32 accumulate)",
+        "data": "synthetic: seeded IQ2_XXS experts (BASELINE config 0 generator), router W N(0,0.02), bias N(0,0.01), x/resid N(0,1) fp32",
+        "config": {"workload": "config1_decode_T1_58layers_ep", "model": "DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)",
+                   "global_batch": ws, "seq_len": 1, "layers": args.layers, "distinct_layers_resident": distinct,
+                   "top_k": 8, "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": E,
+                   "exchange": "2 all-to-alls per layer (library NCCL communicator, grouped send/recv, in the step's CUDA graph)",
+                   "l2": "no flush: a step streams the selected experts of %d distinct layers (> 126 MB L2)" % distinct},
+        "layer": {"ms_per_layer": round(ms_max / args.steps / args.layers * 1e3, 3), "unit_ms_per_layer": "us",
+                  "expert_stage_us": {"gate_up": round(float(gu.mean()) * 1e3, 2), "down_combine": round(float(dn.mean()) * 1e3, 2)},
+                  "local_experts_per_layer": round(float(np.mean(loc)), 2)},
+        "roofline": {"kernel": "k_gate_up (expert-rank gate/up + SwiGLU + q8 on received rows)", "bound": "hbm",
+                     "achieved": round(achieved_min, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved_min / hbm, 4),
+                     "traffic": None, "algorithmic_bytes_per_launch": float(np.mean(gu_bytes)), "peak_source": peak_kind,
+                     "note": "min over ranks of the mean per-layer achieved bandwidth"},
+        "e2e": {"value": round(n_e2e * ws / (e2e_ms / 1e3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": args.layers * 2 * HIDDEN * 4, "d2h_bytes_per_step": args.layers * HIDDEN * 4,
+                "path": "pinned host x/resid -> CUDA-graph step of EpMoeLayer.forward x58 -> pinned host h (stream events)"},
+        "gpu_launches": args.steps * args.layers * 11,
+    }
+    if cl:
+        out["clocks"] = cl
+    return out
+
+
+def run_ep_prefill(args, ws, rank, local, dist):
+    """expert-parallel batch, T tokens per step in total (T/N per rank), top-8 routing by
+    the router (bf16 N(0,1) hidden states), experts sharded 256/N per GPU; compact row exchange (one count
+    exchange and host read per step); strong scaling."""
+    import torch
+    T = args.tokens
+    assert T % ws == 0
+    Tl = T // ws
+    dev, shards, distinct, comm, ops, layer = _ep_setup(args, ws, rank, local, dist, Tl, 1)
+    W = shards[0]
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    x = torch.randn(Tl, HIDDEN, device=dev, generator=g).to(torch.bfloat16).float()
+    r = torch.randn(Tl, HIDDEN, device=dev, generator=g).to(torch.bfloat16).float()
+    stream = torch.cuda.Stream(dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            out = layer.forward(W, x, r)
+    torch.cuda.synchronize(dev)
+    ops.device_error()
+    barrier(dist)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(args.steps):
+            out = layer.forward(W, x, r)
+        t1.record(stream)
+    barrier(dist)
+    ms = t0.elapsed_time(t1)
+    cl = clocks.stop() if clocks else None
+    ops.device_error()
+    ms_max = max_over_ranks(dist, ms)
+    sent, got = layer.last_counts
+    value = T * args.steps / (ms_max / 1e3)
+    hbm, bf16, peak_kind = measured_peaks()
+    flops = 2.0 * T * (args.keep + 1) * 3 * HIDDEN * INTER + 2.0 * T * HIDDEN * NE
+    comm.close()
+    o = {
+        "metric": "MoE-layer tokens/s (T=%d expert-parallel batch, one layer)" % T, "value": round(value, 1), "unit": "tokens/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)",
+        "data": "synthetic: seeded IQ2_XXS experts, router W N(0,0.02), bias N(0,0.01), bf16 N(0,1) hidden states",
+        "config": {"workload": "config3_ep_batch_T%d" % T, "global_batch": T, "seq_len": T, "layers": 1, "top_k": 8,
+                   "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": NE // ws, "rows_sent": sent,
+                   "rows_received": got, "l2": "no flush: each rank streams its %.2f GB shard" % ((3 * NE // ws + 3) * MAT / 1e9)},
+        "layer": {"flops": flops, "achieved_tflops": round(flops / (ms_max / args.steps / 1e3) / 1e12, 1),
+                  "tensor_frac_of_bf16_peak": round(flops / (ms_max / args.steps / 1e3) / 1e12 / (bf16 * ws), 4)},
+        "gpu_launches": args.steps * 12,
+    }
+    if cl:
+        o["clocks"] = cl
+    return o
+
+
 def e2e_decode(args, layers, distinct, keep):
     """Decode through the engine-facing fl_* ABI with host buffers: per layer fl_moe_prepare (H2D x/resid,
     router, shared expert) -> fl_fetch (D2H sel/wts/ncur/fi) -> host keep pass -> fl_moe (D2H h, moe).
@@ -477,6 +691,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample (profiling runs)")
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU-baseline sample")
+    ap.add_argument("--parallelism", default="ep", choices=["ep", "replicas"], help="N > 1: expert parallel or replicas")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     ws, rank, local = dist_setup(args)
@@ -487,6 +702,13 @@ def main():
         return
     import torch
     dist = dist_init(ws, local)
+    if ws > 1 and args.parallelism == "ep":
+        out = run_ep_prefill(args, ws, rank, local, dist) if args.workload == "prefill" else run_ep_decode(args, ws, rank, local, dist)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     if args.workload == "prefill":
         out = run_prefill(args, ws, rank, local, dist)
         if rank == 0:

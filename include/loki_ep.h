@@ -54,6 +54,22 @@ LK_API int lk_ep_shared(LkMoeCtx* ctx, const LkMoeWeights* W, const float* x, co
 LK_API int lk_ep_combine(const float* ret, const int* row_map, int T, int n_ranks, const float* h_partial,
                          float* h, float* moe, lk_stream_t stream);
 
+/* the exchange: an NCCL communicator over the n_ranks GPUs (libnccl.so.2 bound at run time) and the
+ * all-to-all of byte blocks.  lk_ep_comm_id (one rank) makes the LK_EP_COMM_ID_BYTES id every rank passes
+ * to lk_ep_comm_create (collective: all ranks call it).  lk_ep_all_to_all sends block d of `send` (offset
+ * send_off[d], send_bytes[d] bytes) to rank d and receives block s of `recv` from rank s (recv_off[s],
+ * recv_bytes[s]); the offset / byte arrays are host arrays of n_ranks entries, or all null for equal blocks
+ * of block_bytes at d * block_bytes.  Stream-ordered and CUDA-graph capturable; every rank must call it
+ * with matching sizes. */
+#define LK_EP_COMM_ID_BYTES 128
+typedef struct LkEpComm LkEpComm;
+LK_API int lk_ep_comm_id(void* id_out);
+LK_API int lk_ep_comm_create(const void* id, int n_ranks, int rank, int device, LkEpComm** out);
+LK_API void lk_ep_comm_destroy(LkEpComm* comm);
+LK_API int lk_ep_all_to_all(LkEpComm* comm, const void* send, void* recv, const int64_t* send_off,
+                            const int64_t* send_bytes, const int64_t* recv_off, const int64_t* recv_bytes,
+                            int64_t block_bytes, lk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

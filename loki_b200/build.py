@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libloki_moe.so")
-SOURCES = ["expert_gemv.cu", "expert_gemv1.cu", "aux_kernels.cu", "router.cu", "dispatch.cu", "prefill_gemm.cu", "moe_api.cu", "fl_abi.cu", "noalloc.cu", "ep.cu"]
+SOURCES = ["expert_gemv.cu", "expert_gemv1.cu", "aux_kernels.cu", "router.cu", "dispatch.cu", "prefill_gemm.cu", "moe_api.cu", "fl_abi.cu", "noalloc.cu", "ep.cu", "ep_comm.cu"]
 HEADERS = ["moe_format.h", "moe_device.cuh", "moe_internal.h", "tcgen05.cuh", "iq2_grid.inc",
            os.path.join("..", "..", "include", "loki_moe.h"), os.path.join("..", "..", "include", "loki_fused_moe.h"),
            os.path.join("..", "..", "include", "loki_ep.h")]
@@ -64,7 +64,7 @@ def build(force=False, verbose=False, ptxas_verbose=False):
             if r.returncode != 0:
                 raise RuntimeError("nvcc failed on %s" % src)
     if force or _stale(LIB, objs):
-        cmd = [nv, "-ccbin", host_cxx()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda"]
+        cmd = [nv, "-ccbin", host_cxx()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)

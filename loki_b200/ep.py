@@ -10,8 +10,9 @@ the router and the shared expert.  Tokens stay on their home rank; one layer is
     exchange #2: partial sums (all-to-all, the transpose of #1)
     home   combine: h = resid + shared + sum over ranks, moe = sum over ranks
 
-The exchanges go through a communicator with torch.distributed's all_to_all_single signature (NCCL over
-NVLink on GPUs; gloo in the CPU protocol tests).  Two row layouts: fixed capacity (block d holds up to
+The exchanges go through a communicator with torch.distributed's all_to_all_single signature: NativeComm
+(the library's own NCCL communicator, grouped send/recv over NVLink, capturable in a CUDA graph), TorchComm
+(a torch.distributed process group: NCCL, or gloo in the CPU protocol tests).  Two row layouts: fixed capacity (block d holds up to
 `cap` rows, so no count exchange and no host synchronisation: decode, CUDA-graph friendly) and compact
 (block sizes exchanged first; the host learns them with one device->host copy: batch prefill).
 
@@ -38,6 +39,53 @@ class TorchComm:
 
     def all_to_all(self, out, inp, out_splits=None, in_splits=None, async_op=False):
         return dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group, async_op=async_op)
+
+
+class _Done:
+    def wait(self):
+        pass
+
+
+class NativeComm:
+    """all-to-all through libloki_moe.so's NCCL communicator (include/loki_ep.h lk_ep_all_to_all): stream-ordered
+    on the current CUDA stream, so it can sit inside a captured CUDA graph.  The NCCL id is made on rank 0
+    and broadcast over the default torch.distributed group."""
+
+    def __init__(self, device):
+        self.rank, self.size = dist.get_rank(), dist.get_world_size()
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        idb = ctypes.create_string_buffer(N.EP_COMM_ID_BYTES)
+        if self.rank == 0:
+            check(lib().lk_ep_comm_id(idb))
+        obj = [idb.raw if self.rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0, device=self.device)
+        idb = ctypes.create_string_buffer(obj[0], N.EP_COMM_ID_BYTES)
+        h = ctypes.c_void_p()
+        check(lib().lk_ep_comm_create(idb, self.size, self.rank, self.device.index or 0, ctypes.byref(h)))
+        self.comm = h
+
+    def close(self):
+        if self.comm:
+            lib().lk_ep_comm_destroy(self.comm)
+            self.comm = None
+
+    def all_to_all(self, out, inp, out_splits=None, in_splits=None, async_op=False):
+        n = self.size
+        if in_splits is None and out_splits is None:
+            assert out.numel() * out.element_size() == inp.numel() * inp.element_size()
+            block = inp.numel() * inp.element_size() // n
+            check(lib().lk_ep_all_to_all(self.comm, _ptr(inp), _ptr(out), None, None, None, None, block, _stream()))
+            return _Done()
+        rin = inp[0].numel() * inp.element_size() if inp.dim() > 1 else inp.element_size()
+        rout = out[0].numel() * out.element_size() if out.dim() > 1 else out.element_size()
+        arr = ctypes.c_int64 * n
+        sb = arr(*[s * rin for s in in_splits])
+        so = arr(*[sum(in_splits[:d]) * rin for d in range(n)])
+        rb = arr(*[s * rout for s in out_splits])
+        ro = arr(*[sum(out_splits[:d]) * rout for d in range(n)])
+        check(lib().lk_ep_all_to_all(self.comm, _ptr(inp) if inp.numel() else None, _ptr(out) if out.numel() else None,
+                                     so, sb, ro, rb, 0, _stream()))
+        return _Done()
 
 
 class NativeEpOps:
@@ -114,6 +162,7 @@ class EpMoeLayer:
         self.n_ranks = comm.size
         self.fixed_cap_max = fixed_cap_max
         self.last_counts = None          # (rows sent per rank, rows received per rank) of the last compact call
+        self._side = None                # CUDA stream of the shared expert (overlaps exchange #1)
 
     def forward(self, W, x, resid, logits_override=None):
         """W: this rank's LayerWeights shard (router + shared expert + experts [r*E, (r+1)*E)); x, resid:
@@ -137,11 +186,21 @@ class EpMoeLayer:
             self.last_counts = (sent, got)
             recv = torch.empty(sum(got), EP_ROW_BYTES, dtype=torch.uint8, device=send.device)
             work = comm.all_to_all(recv, send[:sum(sent)], got, sent, async_op=True)
-        hpart = ops.shared(W, x, resid)                                # overlaps exchange #1
+        if x.is_cuda:                                                  # shared expert beside exchange #1
+            main = torch.cuda.current_stream(x.device)
+            if self._side is None:
+                self._side = torch.cuda.Stream(x.device)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                hpart = ops.shared(W, x, resid)
+        else:
+            hpart = ops.shared(W, x, resid)
         work.wait()
         R = recv.shape[0]
         ret = ops.experts(W, recv, R, keep)
         ret_home = torch.empty(NR * cap if fixed else sum(sent), HIDDEN, dtype=ret.dtype, device=ret.device)
         comm.all_to_all(ret_home, ret, sent, got)
+        if x.is_cuda:
+            main.wait_stream(self._side)
         h, moe = ops.combine(ret_home, row_map, hpart)
         return h, moe, sel, w

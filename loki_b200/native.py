@@ -22,6 +22,7 @@ FMT_IQ2, FMT_Q2K, FMT_Q3K = 4, 5, 6
 EP_ROW_HDR_BYTES = 64
 EP_ROW_BYTES = EP_ROW_HDR_BYTES + HIDDEN * 4      # 28 736
 EP_MAX_RANKS = 8
+EP_COMM_ID_BYTES = 128
 
 
 class LkMoeConfig(ctypes.Structure):
@@ -68,6 +69,10 @@ SIGNATURES = {
     "lk_ep_experts": (_I, [_P, ctypes.POINTER(LkMoeWeights), _P, _I, _I, _P, _P]),
     "lk_ep_shared": (_I, [_P, ctypes.POINTER(LkMoeWeights), _P, _P, _I, _P, _P]),
     "lk_ep_combine": (_I, [_P, _P, _I, _I, _P, _P, _P, _P]),
+    "lk_ep_comm_id": (_I, [_P]),
+    "lk_ep_comm_create": (_I, [_P, _I, _I, _I, ctypes.POINTER(_P)]),
+    "lk_ep_comm_destroy": (None, [_P]),
+    "lk_ep_all_to_all": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _P]),
     "fl_init": (_P, [_I, _I]),
     "fl_wide_init": (_I, [_P, _I, _I]),
     "fl_wide_moe": (None, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _I, _I, _I]),

@@ -2,7 +2,8 @@
 
 * emulated ranks: 2 or 4 ranks as threads on one GPU (ThreadComm), each with its own 256/N-expert shard
   and contexts: the pack / expert / shared / combine kernels and the exchange logic, on one device;
-* NCCL: 2 processes on 2 GPUs (skipped with fewer), the real all-to-all over NVLink.
+* NCCL: 2 processes on 2 GPUs (skipped with fewer), the real all-to-all over NVLink, through the library's
+  own communicator (NativeComm, also replayed from a captured CUDA graph) and through torch.distributed.
 Routing must match the oracle bit-exactly; h / moe within RTOL_L2 of the single-GPU oracle layer.
 """
 import os
@@ -72,10 +73,10 @@ def test_ep_emulated_ranks_one_gpu(native, oracle, n_ranks, T_loc, fixed_cap_max
         _check_rank(oracle, shards[rank], *inputs[rank], *out[rank])
 
 
-def _nccl_worker(rank, port, T_loc, fixed_cap_max, out_dir):
+def _nccl_worker(rank, port, T_loc, fixed_cap_max, comm_kind, out_dir):
     import torch.distributed as dist
     from loki_b200.moe import LayerWeights
-    from loki_b200.ep import EpMoeLayer, NativeEpOps, TorchComm
+    from loki_b200.ep import EpMoeLayer, NativeEpOps, TorchComm, NativeComm
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=2,
                             device_id=torch.device("cuda", rank))
@@ -83,10 +84,24 @@ def _nccl_worker(rank, port, T_loc, fixed_cap_max, out_dir):
         W = LayerWeights("cuda:%d" % rank, SEED, 0, n_experts=128, expert0=rank * 128)
         ops = NativeEpOps(rank, 2, T_loc)
         ops.set_gemm_threshold(1 << 20)
-        layer = EpMoeLayer(TorchComm(), ops, fixed_cap_max=fixed_cap_max)
+        comm = NativeComm(rank) if comm_kind == "native" else TorchComm()
+        layer = EpMoeLayer(comm, ops, fixed_cap_max=fixed_cap_max)
         x, r = (torch.from_numpy(a).cuda() for a in _inputs(T_loc, rank))
         h, moe, sel, w = layer.forward(W, x, r)
         torch.cuda.synchronize()
+        if comm_kind == "native" and T_loc <= fixed_cap_max:
+            # the same layer captured in a CUDA graph (exchanges included) and replayed: identical outputs
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                out_g = layer.forward(W, x, r)
+            g.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out_g[0], h) and torch.equal(out_g[1], moe)
+            del g
+        if comm_kind == "native":
+            comm.close()
         ops.device_error()
         np.savez(os.path.join(out_dir, "r%d.npz" % rank), h=h.cpu().numpy(), moe=moe.cpu().numpy(),
                  sel=sel.cpu().numpy(), w=w.cpu().numpy(), Wr=W.router_w.float().cpu().numpy(),
@@ -96,8 +111,9 @@ def _nccl_worker(rank, port, T_loc, fixed_cap_max, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("T_loc,fixed_cap_max", [(1, 8), (12, 4)])
-def test_ep_nccl_two_gpus(native, oracle, tmp_path, T_loc, fixed_cap_max):
+@pytest.mark.parametrize("T_loc,fixed_cap_max,comm_kind", [(1, 8, "native"), (12, 4, "native"), (3, 8, "torch"),
+                                                             (12, 4, "torch")])
+def test_ep_nccl_two_gpus(native, oracle, tmp_path, T_loc, fixed_cap_max, comm_kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -106,7 +122,7 @@ def test_ep_nccl_two_gpus(native, oracle, tmp_path, T_loc, fixed_cap_max):
     port = s.getsockname()[1]
     s.close()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-    mp.start_processes(_nccl_worker, args=(port, T_loc, fixed_cap_max, str(tmp_path)), nprocs=2, join=True,
+    mp.start_processes(_nccl_worker, args=(port, T_loc, fixed_cap_max, comm_kind, str(tmp_path)), nprocs=2, join=True,
                        start_method="spawn")
     for rank in range(2):
         got = np.load(os.path.join(str(tmp_path), "r%d.npz" % rank))
