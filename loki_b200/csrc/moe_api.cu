@@ -24,7 +24,7 @@ struct LkMoeCtx {
     int* err = nullptr; int* tile_count = nullptr; int* chunk_count = nullptr;
     // tensor-core path (T >= gemm_min_tokens): 64-token slots and fp16 operand staging
     int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
-    __half* xh = nullptr; __half* hb = nullptr; int gemm_min_tokens = 64;
+    __half* bt = nullptr; __half* ht = nullptr; int* g_cnt = nullptr; int gemm_min_tokens = 64;
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     char msg[256] = {0};
 };
@@ -98,7 +98,8 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     c->g_max = max_slots_for(T, KE, NE, GEMM_NT, cfg->with_shared);
     LK_CU(dalloc(&c->g_expert, c->g_max)); LK_CU(dalloc(&c->g_tok, (size_t)c->g_max * GEMM_NT));
     LK_CU(dalloc(&c->g_out, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_w, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_n, 1));
-    LK_CU(dalloc(&c->xh, (size_t)T * HIDDEN)); LK_CU(dalloc(&c->hb, rows * MOE_INTER));
+    LK_CU(dalloc(&c->bt, gemm_tile_halfs(c->g_max, false))); LK_CU(dalloc(&c->ht, gemm_tile_halfs(c->g_max, true)));
+    LK_CU(dalloc(&c->g_cnt, c->g_max));
     LK_CU(dalloc(&c->chunk_count, HIDDEN / 8));
     LK_CU(cudaMemset(c->chunk_count, 0, (size_t)(HIDDEN / 8) * sizeof(int)));
     LK_CU(cudaMemset(c->y, 0, rows * HIDDEN * sizeof(float)));
@@ -112,7 +113,7 @@ void lk_moe_destroy(LkMoeCtx* c) {
     if (!c) return;
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
                      c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->chunk_count,
-                     c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->xh, c->hb };
+                     c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt };
     for (void* p : ptrs) if (p) cudaFree(p);
     delete c;
 }
@@ -218,7 +219,7 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int
     g.sh_gate = (const uint8_t*)W->sh_gate; g.sh_up = (const uint8_t*)W->sh_up; g.sh_down = (const uint8_t*)W->sh_down;
     g.x = x; g.ld_x = ld_x; g.T = T;
     g.slot_expert = c->g_expert; g.slot_tok = c->g_tok; g.slot_out = c->g_out; g.slot_w = c->g_w; g.nslots = c->g_n;
-    g.xh = c->xh; g.hb = c->hb; g.y = c->y; g.err = c->err;
+    g.max_slots = c->g_max; g.slot_cnt = c->g_cnt; g.bt = c->bt; g.ht = c->ht; g.y = c->y; g.err = c->err;
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_prefill_gemm(g, c->nsm, st);
     if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
@@ -305,6 +306,8 @@ int lk_ep_shared(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float
     if (!c || !W || T < 0 || (T > 0 && (!x || !resid || !h_partial))) return set_err(c, LK_ERR_ARG, "bad argument");
     if (!c->cfg.with_shared || !W->sh_gate || !W->sh_up || !W->sh_down)
         return set_err(c, LK_ERR_ARG, "the shared expert needs with_shared = 1 and W->sh_*");
+    if (((uintptr_t)W->sh_gate | (uintptr_t)W->sh_up | (uintptr_t)W->sh_down) & 15)
+        return set_err(c, LK_ERR_ARG, "shared expert matrices must be 16-byte aligned");
     if (W->down_fmt != LK_FMT_IQ2) return set_err(c, LK_ERR_UNSUPPORTED, "down format %d", W->down_fmt);
     if (T > c->cfg.max_tokens) return set_err(c, LK_ERR_CAPACITY, "T=%d > capacity %d", T, c->cfg.max_tokens);
     if (T == 0) return LK_OK;

@@ -78,12 +78,15 @@ struct GemmParams {
     const uint8_t* sh_gate; const uint8_t* sh_up; const uint8_t* sh_down;
     const float* x; int ld_x; int T;                  // activations [T][HIDDEN] fp32
     const int* slot_expert; const int* slot_tok; const int* slot_out; const float* slot_w; const int* nslots;  // [slot][GEMM_NT]
-    __half* xh;                                       // [T][HIDDEN] fp16 of the q8-dequantised x (scratch)
-    __half* hb;                                       // [rows][MOE_INTER] fp16 of the q8-dequantised SwiGLU output
+    int max_slots;
+    int* slot_cnt;                                    // [max_slots] tokens per slot (written by the B-tile pre-pass)
+    __half* bt;                                       // gate/up B tiles [max_slots][HIDDEN/64][64x64 fp16]
+    __half* ht;                                       // down B tiles (SwiGLU output) [max_slots][MOE_INTER/64][64x64]
     float* y;                                         // [rows][HIDDEN] weighted expert outputs
     int* err;
 };
 void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st);
+size_t gemm_tile_halfs(int max_slots, bool down);     // size of bt (down = false) / ht (down = true)
 
 // ---- seeded IQ2_XXS weight generation (moe_format.h generator) for n_experts consecutive experts
 void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,

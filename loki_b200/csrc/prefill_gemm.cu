@@ -5,19 +5,27 @@
 //   D[128 weight rows x N tokens] = A[128 x K] . B[N x K]^T   with tcgen05.mma.cta_group::1.kind::f16,
 //   fp32 accumulators in tensor memory (two tiles per item: gate+up rows, or two 128-row halves of down),
 //   N = the slot's token count rounded up to 16.
-// A (weights): IQ2_XXS decoded by 16 warps straight into fp16 in shared memory (UMMA canonical K-major,
-//   no swizzle).  Decode trick: for a weight v in {+-8, +-25, +-43}, fp16(1024 + v) has a low byte in
-//   {08, 19, 2B, F0, CE, AA} and a high byte in {64, 63} -- eight bytes -- so one byte-permute over the
-//   constant pair (0x642B1908, 0x63AACEF0) yields two fp16 values 1024+v; the selectors are the OR of a
-//   per-grid-entry table (codes) and a per-sign-index table (signs), both 64-bit and lane-private.  One
-//   hfma2 (x*s - 1024*s, 1024*s exact) gives v*s, s = fp16(d*(2*scale+1)/8).
-// B (activations): fp16 of the q8-dequantised values (k_x_q8_f16), gathered per slot token.
-// Pipeline: decode warps fill a 2-stage ring and arrive on full[]; one thread issues 4 K=16 MMAs per
-//   tile per stage and commits to empty[]; after the last stage a commit to accfull[] releases the
-//   epilogue (tcgen05.ld of the accumulators), which frees the double-buffered accumulator via accempty[].
-// Epilogues: gate/up -> h = silu(g)*u stored as fp16, the down GEMM's B (unlike the matvec path it is not
-//   re-quantised to q8: with 16-bit operands that step would turn their rounding into q8 boundary flips);
-//   down -> y[entry][row] = w * D (fp32), summed by the combine kernel.
+//
+// A (weights) never touches shared memory as fp16: the IQ2_XXS groups are decoded in registers and
+// written to tensor memory with tcgen05.st (thread = weight row = TMEM lane, 32 weights = 16 columns), and
+// the MMA reads A from tensor memory.  Decode trick: for a weight v in {+-8, +-25, +-43}, fp16(1024 + v)
+// has a low byte in {08, 19, 2B, F0, CE, AA} and a high byte in {64, 63} -- eight bytes -- so one
+// byte-permute over the constant pair (0x642B1908, 0x63AACEF0) yields two fp16 values 1024+v; the selectors
+// are the OR of a per-grid-entry table (codes) and a per-sign-index table (signs), both 64-bit and
+// lane-private in shared memory.  One hfma2 (x*s - 1024*s, 1024*s exact) gives v*s, s = fp16(d*(2*scale+1)/8).
+// B (activations) arrives as pre-tiled K-blocks (UMMA K-major core-matrix layout, N rows, LBO = N/8 * 128
+// bytes): gate/up tiles from k_gate_b_tiles (fp16 of the q8-dequantised x of each slot's tokens), down
+// tiles written by the gate/up epilogue (h = silu(g)*u at fp16: with 16-bit operands a q8 re-quantisation
+// would only turn their rounding into q8 boundary flips).  One bulk copy (1-D TMA) per K-block.
+//
+// Warp roles (576 threads, one CTA per SM, persistent over (slot, tile) items):
+//   warps 0-15  decode: warp w = TMEM lane quarter w&3, tile (w>>2)&1, group-in-K-block w>>3; then epilogue
+//   warp 16     MMA issuer (one thread): 8 MMAs per K-block, commit to empty[], accfull[] per item
+//   warp 17     copies: each weight row's next IQ2 superblock, as the 80-byte 16-aligned window around it,
+//               into a raw ring (16-byte cp.async, 6 rows per instruction, coalesced); B K-block tiles into
+//               the B ring (1-D TMA bulk copies)
+// Barriers: rawfull/rawempty (raw ring), full/empty (A stage in TMEM + B stage in shared memory),
+// accfull/accempty (double-buffered accumulators).  Every wait is bounded (moe_device.cuh).
 #include "moe_internal.h"
 #include "moe_device.cuh"
 #include "tcgen05.cuh"
@@ -27,29 +35,34 @@ namespace lk {
 constexpr int PG_M = 128;                    // weight rows per accumulator tile
 constexpr int PG_NMAX = GEMM_NT;             // tokens per slot (64)
 constexpr int PG_KB = 64;                    // K per pipeline stage
-constexpr int PG_NST = 2;
-constexpr int PG_PF = 4;                     // K blocks of global loads in flight per decode thread
-constexpr int PG_DWARPS = 16;                // decode / B-load / epilogue warps
-constexpr int PG_THREADS = (PG_DWARPS + 1) * 32;
-constexpr int PG_A_BYTES = PG_M * PG_KB * 2;             // 16 KB
-constexpr int PG_B_BYTES = PG_NMAX * PG_KB * 2;          // 8 KB
-constexpr int PG_STAGE = 2 * PG_A_BYTES + PG_B_BYTES;    // 40 KB
-constexpr int PG_A_LBO = (PG_M / 8) * 128;               // K-direction core-matrix stride in A
-constexpr int PG_B_LBO = (PG_NMAX / 8) * 128;            // ... in B
+constexpr int PG_NST = 4;                    // A (TMEM) / B (smem) stages
+constexpr int PG_DWARPS = 16;
+constexpr int PG_MMA_WARP = PG_DWARPS;
+constexpr int PG_COPY_WARP = PG_DWARPS + 1;
+constexpr int PG_THREADS = (PG_DWARPS + 2) * 32;
+constexpr int PG_B_TILE = PG_NMAX * PG_KB * 2;           // 8 KB: one K-block of B at N = 64
+constexpr int PG_RAW_ROWB = 80;                          // one superblock (66 B) in its 16-aligned 80-byte window
+constexpr int PG_RAW_STAGE = 2 * PG_M * PG_RAW_ROWB;     // 256 weight rows: 20 KB
+constexpr int PG_RAW_NST = 3;
 constexpr int PG_GTAB = 256 * 32 * 8;                    // 64 KB grid pair selectors
 constexpr int PG_STAB = 128 * 32 * 8;                    // 32 KB sign pair selectors
 constexpr int PG_OFF_GTAB = 0;
 constexpr int PG_OFF_STAB = PG_OFF_GTAB + PG_GTAB;
-constexpr int PG_OFF_RING = PG_OFF_STAB + PG_STAB;
-constexpr int PG_OFF_BAR = PG_OFF_RING + PG_NST * PG_STAGE;
-constexpr int PG_NBAR = 2 * PG_NST + 2 + 2 + 1;          // full, empty, accfull, accempty, drain
-constexpr int PG_OFF_MISC = PG_OFF_BAR + PG_NBAR * 8;
+constexpr int PG_OFF_B = PG_OFF_STAB + PG_STAB;
+constexpr int PG_OFF_RAW = PG_OFF_B + PG_NST * PG_B_TILE;
+constexpr int PG_OFF_BAR = PG_OFF_RAW + PG_RAW_NST * PG_RAW_STAGE + 64;   // + slack for the last row's over-read
+constexpr int PG_NBAR = 2 * PG_NST + 2 + 2 + 1 + 2 * PG_RAW_NST;
+constexpr int PG_OFF_ROWP = PG_OFF_BAR + PG_NBAR * 8;          // copy warp: the current item's 256 row addresses
+constexpr int PG_OFF_MISC = PG_OFF_ROWP + 2 * PG_M * 8;
 constexpr int PG_SMEM_USED = PG_OFF_MISC + 32;
-// the whole 227 KB is reserved so that every operand read the descriptors can express stays inside this
-// CTA's allocation
+// the whole 227 KB is reserved: one CTA per SM (it allocates all 512 tensor-memory columns), and every
+// operand read the descriptors can express stays inside this CTA's allocation
 constexpr int PG_SMEM = 232448;
 static_assert(PG_SMEM_USED <= PG_SMEM, "shared memory layout exceeds the allocation");
-constexpr uint32_t PG_TMEM_COLS = 256;                   // 2 buffers x (2 tiles x 64 columns)
+constexpr uint32_t PG_TMEM_COLS = 512;
+constexpr uint32_t PG_ACC_COLS = 2 * 2 * PG_NMAX;         // 256: 2 buffers x 2 tiles x 64 fp32 columns
+constexpr uint32_t PG_A_COLS = 2 * (PG_KB / 2);          // 64 per stage: 2 tiles x 32 columns (64 fp16)
+static_assert(PG_ACC_COLS + PG_NST * PG_A_COLS <= PG_TMEM_COLS, "tensor memory layout");
 constexpr uint32_t F16_PAIR_LO = 0x642B1908u;            // bytes 08 19 2B 64
 constexpr uint32_t F16_PAIR_HI = 0x63AACEF0u;            // bytes F0 CE AA 63
 
@@ -82,13 +95,10 @@ __device__ __forceinline__ void init_pair_tables(uint2* gt, uint2* st, int tid, 
 __device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d; asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
 }
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-    uint32_t d; asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b)); return d;
-}
 
-// decode one IQ2_XXS group (32 weights) of a row into 4 x 16-byte fp16 core-matrix rows of an A tile
+// decode one IQ2_XXS group (32 weights) into 16 fp16x2 words in K order (word j = elements 2j, 2j+1)
 __device__ __forceinline__ void decode_group_f16(uint32_t aux0, uint32_t aux1, float d, const uint2* gtl, const uint2* stl,
-                                                 uint8_t* dst, int k8_stride) {
+                                                 uint32_t (&o)[16]) {
     // (1024 + v) * s - 1024 * s = v * s with s = fp16(d * (2*scale+1) / 8); 1024 * s is exact (power of two)
     const __half hs = __float2half_rn(d * (float)(2u * (aux1 >> 28) + 1u) * 0.125f);
     const uint32_t s2 = (uint32_t)__half_as_ushort(hs) * 0x10001u;
@@ -98,24 +108,57 @@ __device__ __forceinline__ void decode_group_f16(uint32_t aux0, uint32_t aux1, f
         const uint2 g = gtl[((aux0 >> (8 * l)) & 0xFFu) * 32];
         const uint2 sg = stl[((aux1 >> (7 * l)) & 0x7Fu) * 32];
         const uint32_t sx = g.x | sg.x, sy = g.y | sg.y;
-        uint4 out;
-        out.x = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx), s2, c2);
-        out.y = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx >> 16), s2, c2);
-        out.z = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy), s2, c2);
-        out.w = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy >> 16), s2, c2);
-        *(uint4*)(dst + l * k8_stride) = out;
+        o[4 * l + 0] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx), s2, c2);
+        o[4 * l + 1] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx >> 16), s2, c2);
+        o[4 * l + 2] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy), s2, c2);
+        o[4 * l + 3] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy >> 16), s2, c2);
     }
 }
 
-// the IQ2 bytes of group `gi` (0..7) of superblock `sb` of a row in global memory
-__device__ __forceinline__ void load_group_global(const uint8_t* row, int sb, int gi, uint32_t& aux0, uint32_t& aux1, float& d) {
-    const uint32_t off = (uint32_t)sb * BLK_IQ2 + 2u + 8u * (uint32_t)gi;
-    const uint32_t* w = (const uint32_t*)(row + (off & ~3u));
-    const uint32_t sh = (off & 3u) * 8u;
-    const uint32_t w0 = __ldg(w), w1 = __ldg(w + 1), w2 = __ldg(w + 2);
-    aux0 = __funnelshift_r(w0, w1, sh);
-    aux1 = __funnelshift_r(w1, w2, sh);
-    d = __half2float(__ushort_as_half(__ldg((const unsigned short*)(row + (size_t)sb * BLK_IQ2))));
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// arrive on `bar` once every cp.async this thread issued so far has landed (counts as one of its arrivals)
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// registers -> tensor memory: 32 lanes x 16 consecutive 32-bit columns (thread i -> lane base + i)
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+                 :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+                    "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// D[tmem] (+)= A[tmem] x B[smem]^T, one 16-deep K step, issued by a single thread
+__device__ __forceinline__ void umma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+                 :: "r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// byte offset of element (n, k) in a B K-block tile of n16 rows (K-major core matrices, LBO = n16/8*128)
+__device__ __forceinline__ uint32_t btile_off(int n, int k, int n16) {
+    return (uint32_t)((k >> 3) * (n16 >> 3) * 128 + (n >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2);
+}
+__device__ __forceinline__ int round16(int c) { return c <= 16 ? 16 : (c + 15) & ~15; }   // MMA N: 16..64
+
+// global weight row `r` (0..255) of work item (slot expert e, row tile rt): gate/up rows 0-127 gate,
+// 128-255 up (tile rows rt*128..); down rows rt*256 + r
+template <bool DOWN>
+__device__ __forceinline__ const uint8_t* item_row(const GemmParams& p, int e, int rt, int r, size_t rowbytes) {
+    const int mat = r >> 7, row = r & (PG_M - 1);
+    const uint8_t* wm;
+    int grow;
+    if (DOWN) {
+        wm = e == SHARED_SLOT ? p.sh_down : p.down + (size_t)e * p.down_stride;
+        grow = rt * 2 * PG_M + mat * PG_M + row;
+    } else {
+        wm = e == SHARED_SLOT ? (mat ? p.sh_up : p.sh_gate) : (mat ? p.up + (size_t)e * p.up_stride : p.gate + (size_t)e * p.gate_stride);
+        grow = rt * PG_M + row;
+    }
+    return wm + (size_t)grow * rowbytes;
 }
 
 template <bool DOWN>
@@ -123,13 +166,17 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const uint2* gtab = (const uint2*)(smem + PG_OFF_GTAB);
     const uint2* stab = (const uint2*)(smem + PG_OFF_STAB);
-    uint8_t* ring = smem + PG_OFF_RING;
+    uint8_t* bring = smem + PG_OFF_B;
+    uint8_t* raw = smem + PG_OFF_RAW;
     uint64_t* bars = (uint64_t*)(smem + PG_OFF_BAR);
     uint64_t* full = bars;
     uint64_t* empty = bars + PG_NST;
     uint64_t* accfull = bars + 2 * PG_NST;
     uint64_t* accempty = accfull + 2;
     uint64_t* drain = accempty + 2;
+    uint64_t* rawfull = drain + 1;
+    uint64_t* rawempty = rawfull + PG_RAW_NST;
+    uintptr_t* rowp = (uintptr_t*)(smem + PG_OFF_ROWP);
     uint32_t* tmem_slot = (uint32_t*)(smem + PG_OFF_MISC);
     volatile int* abort_flag = (volatile int*)(smem + PG_OFF_MISC + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -140,46 +187,94 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
     constexpr int K = DOWN ? MOE_INTER : HIDDEN;
     constexpr int NKB = K / PG_KB;
     const size_t rowbytes = (size_t)(K / QK) * BLK_IQ2;
+    const __half* btiles = DOWN ? p.ht : p.bt;
 
     init_pair_tables((uint2*)(smem + PG_OFF_GTAB), (uint2*)(smem + PG_OFF_STAB), tid, PG_THREADS);
     if (tid == 0) {
         *abort_flag = 0;
-        for (int s = 0; s < PG_NST; ++s) { mbar_init(&full[s], PG_DWARPS); mbar_init(&empty[s], 1); }
+        // full: 16 decode-warp arrivals + the copy warp's expect_tx arrival (B bytes)
+        for (int s = 0; s < PG_NST; ++s) { mbar_init(&full[s], PG_DWARPS + 1); mbar_init(&empty[s], 1); }
         for (int b = 0; b < 2; ++b) { mbar_init(&accfull[b], 1); mbar_init(&accempty[b], PG_DWARPS); }
         mbar_init(drain, 1);
+        for (int s = 0; s < PG_RAW_NST; ++s) { mbar_init(&rawfull[s], 32); mbar_init(&rawempty[s], PG_DWARPS); }
         fence_mbar_init();
     }
-    if (warp == PG_DWARPS) { tmem_alloc(tmem_slot, PG_TMEM_COLS); tmem_relinquish(); }
+    if (warp == PG_MMA_WARP) { tmem_alloc(tmem_slot, PG_TMEM_COLS); tmem_relinquish(); }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t ring_s = smem_u32(ring);
 
-    if (warp == PG_DWARPS) {
+    if (warp == PG_COPY_WARP) {
+        // ---------------------------------------------------------------- raw superblocks + B tiles
+        uint32_t rit = 0, it = 0;
+        for (int item = blockIdx.x; item < nitems && !*abort_flag; item += gridDim.x) {
+            const int s = item % nslots, rt = item / nslots;
+            const int e = p.slot_expert[s];
+            const int n16 = round16(p.slot_cnt[s]);
+            __syncwarp();
+            for (int r = lane; r < 2 * PG_M; r += 32) rowp[r] = (uintptr_t)item_row<DOWN>(p, e, rt, r, rowbytes);
+            __syncwarp();
+            for (int kb = 0; kb < NKB; ++kb, ++it) {
+                if ((kb & 3) == 0) {
+                    const int sb = kb >> 2, rs = rit % PG_RAW_NST;
+                    if (!mbar_wait(&rawempty[rs], ((rit / PG_RAW_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
+                    uint8_t* dst = raw + rs * PG_RAW_STAGE;
+                    const size_t sboff = (size_t)sb * BLK_IQ2;
+                    if (lane < 30) {                  // lane -> (row rsub of 6, 16-byte chunk of 5)
+                        const int rsub = lane / 5, chunk = lane - 5 * rsub;
+                        #pragma unroll 4
+                        for (int r = rsub; r < 2 * PG_M; r += 6) {
+                            const uintptr_t a = (rowp[r] + sboff) & ~(uintptr_t)15;
+                            cp_async16(dst + r * PG_RAW_ROWB + chunk * 16, (const void*)(a + 16 * chunk));
+                        }
+                    }
+                    cp_async_mbar_arrive(&rawfull[rs]);
+                    ++rit;
+                }
+                const int st = it % PG_NST;
+                if (!mbar_wait(&empty[st], ((it / PG_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
+                if (lane == 0) {
+                    const uint32_t bytes = (uint32_t)n16 * PG_KB * 2;
+                    mbar_arrive_expect_tx(&full[st], bytes);
+                    bulk_g2s(bring + st * PG_B_TILE, btiles + ((size_t)s * NKB + kb) * (PG_B_TILE / 2), bytes, &full[st]);
+                }
+            }
+        }
+        {   // every bulk copy issued must land before the CTA may exit
+            __syncwarp();
+            if (lane == 0) {
+                const uint32_t first = it > PG_NST ? it - PG_NST : 0;
+                for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % PG_NST], (j / PG_NST) & 1, nullptr, 0);
+            }
+        }
+        cp_async_wait_all();
+    } else if (warp == PG_MMA_WARP) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
             uint32_t it = 0; int issued = 0;
+            const uint32_t bring_s = smem_u32(bring);
             for (int i = 0, item = blockIdx.x; item < nitems && !*abort_flag; ++i, item += gridDim.x) {
                 const int s = item % nslots;
-                int cnt = 0;
-                while (cnt < PG_NMAX && p.slot_tok[s * PG_NMAX + cnt] >= 0) ++cnt;
-                const int N = cnt <= 16 ? 16 : (cnt <= 32 ? 32 : (cnt <= 48 ? 48 : 64));
+                const int N = round16(p.slot_cnt[s]);
                 const uint32_t idesc = idesc_f16_f32(PG_M, N);
+                const uint32_t lbo = (uint32_t)(N >> 3) * 128;
                 const int buf = i & 1;
                 if (i >= 2 && !mbar_wait(&accempty[buf], ((i >> 1) - 1) & 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
                 tc_fence_after();
                 const uint32_t d0 = tmem + (uint32_t)(buf * 2 * PG_NMAX), d1 = d0 + PG_NMAX;
+                const uint64_t bstep = (uint64_t)((2 * lbo) >> 4);             // one K=16 step along the B tile
                 for (int kb = 0; kb < NKB; ++kb, ++it) {
                     const int st = it % PG_NST;
                     if (!mbar_wait(&full[st], (it / PG_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
                     tc_fence_after();
-                    const uint32_t a0 = ring_s + st * PG_STAGE, a1 = a0 + PG_A_BYTES, b = a1 + PG_A_BYTES;
+                    const uint64_t b0 = umma_desc(bring_s + st * PG_B_TILE, lbo, 128);
+                    const uint32_t a0 = tmem + PG_ACC_COLS + st * PG_A_COLS, a1 = a0 + PG_A_COLS / 2;
                     #pragma unroll
                     for (int ks = 0; ks < PG_KB / 16; ++ks) {
-                        const uint64_t bd = umma_desc(b + ks * 2 * PG_B_LBO, PG_B_LBO, 128);
-                        umma_f16(d0, umma_desc(a0 + ks * 2 * PG_A_LBO, PG_A_LBO, 128), bd, idesc, (kb | ks) != 0);
-                        umma_f16(d1, umma_desc(a1 + ks * 2 * PG_A_LBO, PG_A_LBO, 128), bd, idesc, (kb | ks) != 0);
+                        const uint64_t bd = b0 + (uint64_t)ks * bstep;
+                        umma_f16_ta(d0, a0 + ks * 8, bd, idesc, (kb | ks) != 0);
+                        umma_f16_ta(d1, a1 + ks * 8, bd, idesc, (kb | ks) != 0);
                     }
                     umma_commit(&empty[st]);
                     issued = 1;
@@ -193,62 +288,41 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
             }
         }
     } else {
-        // ---------------------------------------------------------------- decode / B load / epilogue warps
-        const int mat = tid >> 8, row = (tid >> 1) & (PG_M - 1), grp = tid & 1;   // A unit: lane pairs share a row (L1 lines)
+        // ---------------------------------------------------------------- decode warps, then epilogue
+        const int q = warp & 3, mat = (warp >> 2) & 1, grp = warp >> 3;
+        const int row = 32 * q + lane;                                      // weight row in tile `mat` = TMEM lane
         const uint2* gtl = gtab + lane;
         const uint2* stl = stab + lane;
-        const int bn = tid >> 3, bk8 = tid & 7;                                       // B chunk: 8 lanes read one token's 128 B
-        uint32_t it = 0;
+        const uint8_t* rrow0 = raw + (mat * PG_M + row) * PG_RAW_ROWB;
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        uint32_t it = 0, rit = 0;
         for (int i = 0, item = blockIdx.x; item < nitems; ++i, item += gridDim.x) {
             const int s = item % nslots, rt = item / nslots;
             const int e = p.slot_expert[s];
-            const uint8_t* wm;
-            int grow;                                                                  // global weight row of this thread
-            if (DOWN) {
-                wm = e == SHARED_SLOT ? p.sh_down : p.down + (size_t)e * p.down_stride;
-                grow = rt * 2 * PG_M + mat * PG_M + row;
-            } else {
-                wm = e == SHARED_SLOT ? (mat ? p.sh_up : p.sh_gate) : (mat ? p.up + (size_t)e * p.up_stride : p.gate + (size_t)e * p.gate_stride);
-                grow = rt * PG_M + row;
-            }
-            const uint8_t* wrow = wm + (size_t)grow * rowbytes;
-            const int btok = p.slot_tok[s * PG_NMAX + bn];
-            const int bsrc = DOWN ? p.slot_out[s * PG_NMAX + bn] : btok;            // B row: h entry (down) / token (gate/up)
-            const __half* bbase = DOWN ? p.hb : p.xh;
-            // register prefetch ring: the global loads of K block kb + PG_PF are issued while kb is decoded
-            uint32_t pw[PG_PF][3]; unsigned short pd[PG_PF]; uint4 pb[PG_PF];
-            auto issue = [&](int kb, int j) {
-                const int sb = kb >> 2, gi = (kb & 3) * 2 + grp;
-                const uint32_t off = (uint32_t)sb * BLK_IQ2 + 2u + 8u * (uint32_t)gi;
-                const uint32_t* w = (const uint32_t*)(wrow + (off & ~3u));
-                pw[j][0] = __ldg(w); pw[j][1] = __ldg(w + 1); pw[j][2] = __ldg(w + 2);
-                pd[j] = __ldg((const unsigned short*)(wrow + (size_t)sb * BLK_IQ2));
-                pb[j] = bsrc >= 0 ? __ldg((const uint4*)(bbase + (size_t)bsrc * K + kb * PG_KB + bk8 * 8)) : make_uint4(0u, 0u, 0u, 0u);
-            };
-            #pragma unroll
-            for (int j = 0; j < PG_PF; ++j) issue(j, j);
-            for (int kb0 = 0; kb0 < NKB; kb0 += PG_PF) {
-                #pragma unroll
-                for (int j = 0; j < PG_PF; ++j, ++it) {
-                    const int kb = kb0 + j;
-                    const int st = it % PG_NST;
-                    if (!*abort_flag && !mbar_wait(&empty[st], ((it / PG_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) *abort_flag = 1;
-                    uint8_t* a = ring + st * PG_STAGE + mat * PG_A_BYTES;
-                    uint8_t* b = ring + st * PG_STAGE + 2 * PG_A_BYTES;
-                    // A: group grp of this K block (2 groups per 64 columns) -> k8 blocks 4*grp .. 4*grp+3, row `row`
-                    const int gi = (kb & 3) * 2 + grp;
-                    const uint32_t sh = ((((uint32_t)(kb >> 2) * BLK_IQ2 + 2u + 8u * (uint32_t)gi)) & 3u) * 8u;
-                    const uint32_t aux0 = __funnelshift_r(pw[j][0], pw[j][1], sh), aux1 = __funnelshift_r(pw[j][1], pw[j][2], sh);
-                    const float d = __half2float(__ushort_as_half(pd[j]));
-                    const uint4 bv = pb[j];
-                    if (kb + PG_PF < NKB) issue(kb + PG_PF, j);
-                    decode_group_f16(aux0, aux1, d, gtl, stl, a + (4 * grp) * PG_A_LBO + (row >> 3) * 128 + (row & 7) * 16, PG_A_LBO);
-                    // B: token bn, k8 block bk8 (16 bytes)
-                    *(uint4*)(b + bk8 * PG_B_LBO + (bn >> 3) * 128 + (bn & 7) * 16) = bv;
-                    fence_async_smem();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&full[st]);
+            const uintptr_t wrow = (uintptr_t)item_row<DOWN>(p, e, rt, mat * PG_M + row, rowbytes);   // global row
+            for (int kb = 0; kb < NKB; ++kb, ++it) {
+                const int st = it % PG_NST, rs = rit % PG_RAW_NST;
+                if ((kb & 3) == 0 && !*abort_flag && !mbar_wait(&rawfull[rs], (rit / PG_RAW_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))
+                    *abort_flag = 1;
+                // the superblock sits `delta` (0..14) bytes into its staged 16-aligned window
+                const uint8_t* rrow = rrow0 + rs * PG_RAW_STAGE;
+                const int delta = (int)((wrow + (uintptr_t)(kb >> 2) * BLK_IQ2) & 15u);
+                uint32_t aux0, aux1;
+                load_group_smem(rrow, delta + 2 + 8 * ((kb & 3) * 2 + grp), aux0, aux1);
+                const float d = __half2float(*(const __half*)(rrow + delta));
+                uint32_t o[16];
+                decode_group_f16(aux0, aux1, d, gtl, stl, o);
+                if (!*abort_flag && !mbar_wait(&empty[st], ((it / PG_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) *abort_flag = 1;
+                tc_fence_after();
+                tmem_st16(tmem + lane_base + PG_ACC_COLS + st * PG_A_COLS + mat * (PG_A_COLS / 2) + grp * 16, o);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&full[st]);
+                    if ((kb & 3) == 3) mbar_arrive(&rawempty[rs]);
                 }
+                if ((kb & 3) == 3) ++rit;
                 if (*abort_flag) break;
             }
             if (*abort_flag) break;
@@ -256,27 +330,28 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
             const int buf = i & 1;
             if (!mbar_wait(&accfull[buf], (i >> 1) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
             tc_fence_after();
-            const int q = warp & 3, cc = warp >> 2;                // lanes 32q.., tokens 16cc..
-            int cnt = 0;
-            while (cnt < PG_NMAX && p.slot_tok[s * PG_NMAX + cnt] >= 0) ++cnt;
+            const int cc = warp >> 2;                                       // tokens 16cc..16cc+15
+            const int cnt = p.slot_cnt[s], n16 = round16(cnt);
             if (cc * 16 < cnt) {
-                const uint32_t t0 = tmem + (uint32_t)(buf * 2 * PG_NMAX + cc * 16) + ((uint32_t)(32 * q) << 16);
+                const uint32_t t0 = tmem + (uint32_t)(buf * 2 * PG_NMAX + cc * 16) + lane_base;
                 float v0[16], v1[16];
                 tmem_ld16(t0, v0);
                 tmem_ld16(t0 + PG_NMAX, v1);
                 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int n = cc * 16 + j;
-                    const int out = n < cnt ? p.slot_out[s * PG_NMAX + n] : -1;
-                    if (DOWN) {
-                        if (out >= 0) {
+                    if (n < cnt) {
+                        if (DOWN) {
+                            const int out = p.slot_out[s * PG_NMAX + n];
                             const float w = p.slot_w[s * PG_NMAX + n];
-                            const int r0 = rt * 2 * PG_M + 32 * q + lane;
+                            const int r0 = rt * 2 * PG_M + row;
                             p.y[(size_t)out * HIDDEN + r0] = w * v0[j];
                             p.y[(size_t)out * HIDDEN + r0 + PG_M] = w * v1[j];
+                        } else {                          // h = silu(g)*u -> the down GEMM's B tile of this slot
+                            const int hj = rt * PG_M + row;
+                            __half* tile = p.ht + ((size_t)s * (MOE_INTER / PG_KB) + (hj >> 6)) * (PG_B_TILE / 2);
+                            *(__half*)((uint8_t*)tile + btile_off(n, hj & 63, n16)) = __float2half_rn(lk_swiglu(v0[j], v1[j]));
                         }
-                    } else if (out >= 0) {                // h = silu(g)*u enters the down GEMM at fp16
-                        p.hb[(size_t)out * MOE_INTER + rt * PG_M + 32 * q + lane] = __float2half_rn(lk_swiglu(v0[j], v1[j]));
                     }
                 }
             }
@@ -287,23 +362,43 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == PG_DWARPS) { tc_fence_after(); tmem_dealloc(tmem, PG_TMEM_COLS); }
+    if (warp == PG_MMA_WARP) { tc_fence_after(); tmem_dealloc(tmem, PG_TMEM_COLS); }
 }
 
-// x (fp32 [T][HIDDEN]) -> fp16 of its q8-per-32 dequantisation, the B operand of the gate/up GEMM
-__global__ void k_x_q8_f16(const float* __restrict__ x, int ld, int T, __half* __restrict__ xh) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;             // one 32-group per thread
-    if (i >= T * (HIDDEN / 32)) return;
-    const int t = i / (HIDDEN / 32), g = i % (HIDDEN / 32);
+// gate/up B tiles: for slot s and K-block kb, the fp16 of the q8-dequantised x of the slot's tokens in the
+// UMMA K-major core-matrix layout of round16(count) rows (pad rows zero); also the slot's token count
+__global__ void __launch_bounds__(128) k_gate_b_tiles(GemmParams p) {
+    const int s = blockIdx.x, kb = blockIdx.y, tid = threadIdx.x;
+    if (s >= *p.nslots) return;
+    const int n = tid >> 1, g = tid & 1;                 // token row, 32-group within the K-block
+    const int tok = p.slot_tok[s * PG_NMAX + n];
+    const int cnt = __syncthreads_count(tok >= 0) / 2;   // pads are at the end of the slot
+    if (kb == 0 && tid == 0) p.slot_cnt[s] = cnt;
+    const int n16 = round16(cnt);
+    if (n >= n16) return;
     float v[32];
-    const float4* src = (const float4*)(x + (size_t)t * ld + g * 32);
+    if (tok >= 0) {
+        const float4* src = (const float4*)(p.x + (size_t)tok * p.ld_x + kb * PG_KB + g * 32);
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) { const float4 a = src[j]; v[4*j] = a.x; v[4*j+1] = a.y; v[4*j+2] = a.z; v[4*j+3] = a.w; }
+    } else {
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+    }
+    int8_t qv[32];
+    const float d = quant_q8_group(v, qv);
+    uint8_t* tile = (uint8_t*)(p.bt + ((size_t)s * (HIDDEN / PG_KB) + kb) * (PG_B_TILE / 2));
     #pragma unroll
-    for (int j = 0; j < 8; ++j) { const float4 a = src[j]; v[4*j] = a.x; v[4*j+1] = a.y; v[4*j+2] = a.z; v[4*j+3] = a.w; }
-    int8_t q[32];
-    const float d = quant_q8_group(v, q);
-    __half2* dst = (__half2*)(xh + (size_t)t * HIDDEN + g * 32);
-    #pragma unroll
-    for (int j = 0; j < 16; ++j) dst[j] = __halves2half2(__float2half_rn((float)q[2*j] * d), __float2half_rn((float)q[2*j+1] * d));
+    for (int c = 0; c < 4; ++c) {                        // 4 k8 blocks of 8 fp16 (16 bytes) each
+        uint32_t w[4];
+        #pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const int j = c * 8 + 2 * h;
+            w[h] = (uint32_t)__half_as_ushort(__float2half_rn((float)qv[j] * d)) |
+                   ((uint32_t)__half_as_ushort(__float2half_rn((float)qv[j + 1] * d)) << 16);
+        }
+        *(uint4*)(tile + btile_off(n, g * 32 + c * 8, n16)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
 }
 
 template <bool DOWN> static void pg_launch(const GemmParams& p, int grid, cudaStream_t st) {
@@ -313,9 +408,13 @@ template <bool DOWN> static void pg_launch(const GemmParams& p, int grid, cudaSt
 }
 
 void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st) {
-    k_x_q8_f16<<<(p.T * (HIDDEN / 32) + 255) / 256, 256, 0, st>>>(p.x, p.ld_x, p.T, p.xh);
+    k_gate_b_tiles<<<dim3(p.max_slots, HIDDEN / PG_KB), 128, 0, st>>>(p);
     pg_launch<false>(p, grid, st);
     pg_launch<true>(p, grid, st);
+}
+
+size_t gemm_tile_halfs(int max_slots, bool down) {
+    return (size_t)max_slots * ((down ? MOE_INTER : HIDDEN) / PG_KB) * (PG_B_TILE / 2);
 }
 
 }  // namespace lk
