@@ -9,7 +9,7 @@ namespace lk {
 
 constexpr int SHARED_SLOT = -1;      // slot_expert value of the shared expert
 constexpr int MAX_NT = 8;            // tokens per work slot of the grouped matvecs
-constexpr int GEMM_NT = 64;          // tokens per work slot of the tensor-core GEMMs (prefill)
+constexpr int GEMM_NT = 128;         // tokens per work slot of the tensor-core GEMMs (prefill)
 
 // ---- router
 struct RouterParams {

@@ -4,7 +4,8 @@
 // src/fused_layer.cu:540-553) for slots of up to 64 tokens per expert.  Per work item (slot, row tile):
 //   D[128 weight rows x N tokens] = A[128 x K] . B[N x K]^T   with tcgen05.mma.cta_group::1.kind::f16,
 //   fp32 accumulators in tensor memory (two tiles per item: gate+up rows, or two 128-row halves of down),
-//   N = the slot's token count rounded up to 16.
+//   N = the slot's token count rounded up to 16 (up to 128: one tcgen05.mma of M=128, K=16 costs about the
+//   same for any N <= 256, so tokens per instruction are what the tensor pipe's throughput depends on).
 //
 // A (weights) never touches shared memory as fp16: the IQ2_XXS groups are decoded in registers and
 // written to tensor memory with tcgen05.st (thread = weight row = TMEM lane, 32 weights = 16 columns), and
@@ -20,12 +21,13 @@
 //
 // Warp roles (576 threads, one CTA per SM, persistent over (slot, tile) items):
 //   warps 0-15  decode: warp w = TMEM lane quarter w&3, tile (w>>2)&1, group-in-K-block w>>3; then epilogue
-//   warp 16     MMA issuer (one thread): 8 MMAs per K-block, commit to empty[], accfull[] per item
+//   warp 16     MMA issuer (one thread): 8 MMAs per K-block, commit to empty[], accfull per item
 //   warp 17     copies: each weight row's next IQ2 superblock, as the 80-byte 16-aligned window around it,
 //               into a raw ring (16-byte cp.async, 6 rows per instruction, coalesced); B K-block tiles into
 //               the B ring (1-D TMA bulk copies)
 // Barriers: rawfull/rawempty (raw ring), full/empty (A stage in TMEM + B stage in shared memory),
-// accfull/accempty (double-buffered accumulators).  Every wait is bounded (moe_device.cuh).
+// accfull/accempty (the accumulators; the decode warps run the epilogue, so a second accumulator buffer
+// would not let the MMA run ahead).  Every wait is bounded (moe_device.cuh).
 #include "moe_internal.h"
 #include "moe_device.cuh"
 #include "tcgen05.cuh"
@@ -33,14 +35,14 @@
 namespace lk {
 
 constexpr int PG_M = 128;                    // weight rows per accumulator tile
-constexpr int PG_NMAX = GEMM_NT;             // tokens per slot (64)
+constexpr int PG_NMAX = GEMM_NT;             // tokens per slot (128)
 constexpr int PG_KB = 64;                    // K per pipeline stage
 constexpr int PG_NST = 4;                    // A (TMEM) / B (smem) stages
 constexpr int PG_DWARPS = 16;
 constexpr int PG_MMA_WARP = PG_DWARPS;
 constexpr int PG_COPY_WARP = PG_DWARPS + 1;
 constexpr int PG_THREADS = (PG_DWARPS + 2) * 32;
-constexpr int PG_B_TILE = PG_NMAX * PG_KB * 2;           // 8 KB: one K-block of B at N = 64
+constexpr int PG_B_TILE = PG_NMAX * PG_KB * 2;           // 16 KB: one K-block of B at N = 128
 constexpr int PG_RAW_ROWB = 80;                          // one superblock (66 B) in its 16-aligned 80-byte window
 constexpr int PG_RAW_STAGE = 2 * PG_M * PG_RAW_ROWB;     // 256 weight rows: 20 KB
 constexpr int PG_RAW_NST = 3;
@@ -60,7 +62,7 @@ constexpr int PG_SMEM_USED = PG_OFF_MISC + 32;
 constexpr int PG_SMEM = 232448;
 static_assert(PG_SMEM_USED <= PG_SMEM, "shared memory layout exceeds the allocation");
 constexpr uint32_t PG_TMEM_COLS = 512;
-constexpr uint32_t PG_ACC_COLS = 2 * 2 * PG_NMAX;         // 256: 2 buffers x 2 tiles x 64 fp32 columns
+constexpr uint32_t PG_ACC_COLS = 2 * PG_NMAX;             // 256: 2 tiles x 128 fp32 columns
 constexpr uint32_t PG_A_COLS = 2 * (PG_KB / 2);          // 64 per stage: 2 tiles x 32 columns (64 fp16)
 static_assert(PG_ACC_COLS + PG_NST * PG_A_COLS <= PG_TMEM_COLS, "tensor memory layout");
 constexpr uint32_t F16_PAIR_LO = 0x642B1908u;            // bytes 08 19 2B 64
@@ -142,7 +144,7 @@ __device__ __forceinline__ void umma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, ui
 __device__ __forceinline__ uint32_t btile_off(int n, int k, int n16) {
     return (uint32_t)((k >> 3) * (n16 >> 3) * 128 + (n >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2);
 }
-__device__ __forceinline__ int round16(int c) { return c <= 16 ? 16 : (c + 15) & ~15; }   // MMA N: 16..64
+__device__ __forceinline__ int round16(int c) { return c <= 16 ? 16 : (c + 15) & ~15; }   // MMA N: 16..128
 
 // global weight row `r` (0..255) of work item (slot expert e, row tile rt): gate/up rows 0-127 gate,
 // 128-255 up (tile rows rt*128..); down rows rt*256 + r
@@ -194,7 +196,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
         *abort_flag = 0;
         // full: 16 decode-warp arrivals + the copy warp's expect_tx arrival (B bytes)
         for (int s = 0; s < PG_NST; ++s) { mbar_init(&full[s], PG_DWARPS + 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; ++b) { mbar_init(&accfull[b], 1); mbar_init(&accempty[b], PG_DWARPS); }
+        mbar_init(accfull, 1); mbar_init(accempty, PG_DWARPS);
         mbar_init(drain, 1);
         for (int s = 0; s < PG_RAW_NST; ++s) { mbar_init(&rawfull[s], 32); mbar_init(&rawempty[s], PG_DWARPS); }
         fence_mbar_init();
@@ -259,10 +261,9 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
                 const int N = round16(p.slot_cnt[s]);
                 const uint32_t idesc = idesc_f16_f32(PG_M, N);
                 const uint32_t lbo = (uint32_t)(N >> 3) * 128;
-                const int buf = i & 1;
-                if (i >= 2 && !mbar_wait(&accempty[buf], ((i >> 1) - 1) & 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
+                if (i >= 1 && !mbar_wait(accempty, (i - 1) & 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
                 tc_fence_after();
-                const uint32_t d0 = tmem + (uint32_t)(buf * 2 * PG_NMAX), d1 = d0 + PG_NMAX;
+                const uint32_t d0 = tmem, d1 = d0 + PG_NMAX;
                 const uint64_t bstep = (uint64_t)((2 * lbo) >> 4);             // one K=16 step along the B tile
                 for (int kb = 0; kb < NKB; ++kb, ++it) {
                     const int st = it % PG_NST;
@@ -280,7 +281,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
                     issued = 1;
                 }
                 if (*abort_flag) break;
-                umma_commit(&accfull[buf]);
+                umma_commit(accfull);
             }
             if (issued) {                             // every issued MMA has completed before teardown
                 umma_commit(drain);
@@ -327,13 +328,11 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
             }
             if (*abort_flag) break;
             // ------------------------------------------------ epilogue of item i
-            const int buf = i & 1;
-            if (!mbar_wait(&accfull[buf], (i >> 1) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
+            if (!mbar_wait(accfull, i & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
             tc_fence_after();
-            const int cc = warp >> 2;                                       // tokens 16cc..16cc+15
             const int cnt = p.slot_cnt[s], n16 = round16(cnt);
-            if (cc * 16 < cnt) {
-                const uint32_t t0 = tmem + (uint32_t)(buf * 2 * PG_NMAX + cc * 16) + lane_base;
+            for (int cc = warp >> 2; cc * 16 < cnt; cc += 4) {              // tokens 16cc..16cc+15
+                const uint32_t t0 = tmem + (uint32_t)(cc * 16) + lane_base;
                 float v0[16], v1[16];
                 tmem_ld16(t0, v0);
                 tmem_ld16(t0 + PG_NMAX, v1);
@@ -357,7 +356,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&accempty[buf]);
+            if (lane == 0) mbar_arrive(accempty);
         }
     }
     tc_fence_before();
@@ -367,7 +366,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
 
 // gate/up B tiles: for slot s and K-block kb, the fp16 of the q8-dequantised x of the slot's tokens in the
 // UMMA K-major core-matrix layout of round16(count) rows (pad rows zero); also the slot's token count
-__global__ void __launch_bounds__(128) k_gate_b_tiles(GemmParams p) {
+__global__ void __launch_bounds__(2 * PG_NMAX) k_gate_b_tiles(GemmParams p) {
     const int s = blockIdx.x, kb = blockIdx.y, tid = threadIdx.x;
     if (s >= *p.nslots) return;
     const int n = tid >> 1, g = tid & 1;                 // token row, 32-group within the K-block
@@ -408,7 +407,7 @@ template <bool DOWN> static void pg_launch(const GemmParams& p, int grid, cudaSt
 }
 
 void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st) {
-    k_gate_b_tiles<<<dim3(p.max_slots, HIDDEN / PG_KB), 128, 0, st>>>(p);
+    k_gate_b_tiles<<<dim3(p.max_slots, HIDDEN / PG_KB), 2 * PG_NMAX, 0, st>>>(p);
     pg_launch<false>(p, grid, st);
     pg_launch<true>(p, grid, st);
 }
