@@ -225,8 +225,7 @@ constexpr int DN_OFF_RING = DN_OFF_TAB + SEL_TAB_BYTES;
 constexpr int DN_OFF_RED = DN_OFF_RING + DN_NST * DN_CH_BYTES;
 constexpr int DN_OFF_BAR = DN_OFF_RED + DN_NS * 2 * 2 * 8 * 4;
 constexpr int DN_OFF_ABORT = DN_OFF_BAR + 2 * DN_NST * 8;
-constexpr int DN_OFF_LAST = DN_OFF_ABORT + 16;
-constexpr int DN_SMEM = DN_OFF_LAST + DN_NS * 4;
+constexpr int DN_SMEM = DN_OFF_ABORT + 16;
 
 template <int NT>
 __global__ void __launch_bounds__(DN_THREADS, 1) k_down(ExpertParams p) {
@@ -237,7 +236,6 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(ExpertParams p) {
     uint64_t* full = (uint64_t*)(smem + DN_OFF_BAR);
     uint64_t* empty = full + DN_NST;
     volatile int* abort_flag = (volatile int*)(smem + DN_OFF_ABORT);
-    volatile int* lastflag = (volatile int*)(smem + DN_OFF_LAST);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nslots = *p.nslots;
     const int ntiles = nslots * DN_TILES_PER_SLOT;
@@ -326,34 +324,6 @@ __global__ void __launch_bounds__(DN_THREADS, 1) k_down(ExpertParams p) {
             ebuf ^= 1;
         }
         if (aborted) break;
-        if (p.chunk_count) {                          // fused combine: count this slot's chunk in
-            if (hw == 0) {
-                __threadfence();                      // this lane's y stores before the count
-                __syncwarp();
-                if (lane == 0) {
-                    const int old = atomicAdd(&p.chunk_count[rt * DN_NS + strm], 1);
-                    lastflag[strm] = old == nslots - 1;
-                }
-            }
-            named_bar_sync(1 + strm, DN_KG);
-            if (lastflag[strm]) {                     // every slot has written these 8 rows: combine them
-                __threadfence();
-                const int r0 = rt * DN_TILE + strm * DN_CH_ROWS;
-                for (int i = g; i < DN_CH_ROWS * p.T; i += DN_KG) {
-                    const int row = r0 + (i & 7), t = i >> 3;
-                    float m = 0.0f;
-                    for (int k = 0; k < p.keep; ++k) if (!p.sel || p.sel[t * p.keep + k] >= 0) m += __ldcg(p.y + ((size_t)t * p.keep + k) * HIDDEN + row);
-                    if (p.moe) p.moe[(size_t)t * HIDDEN + row] = m;
-                    if (p.h) {
-                        float hv = p.resid[(size_t)t * HIDDEN + row];
-                        if (p.with_shared) hv += __ldcg(p.y + ((size_t)p.T * p.keep + t) * HIDDEN + row);
-                        if (p.shared_sep) hv += p.shared_sep[(size_t)t * HIDDEN + row];
-                        p.h[(size_t)t * HIDDEN + row] = hv + m;
-                    }
-                }
-                if (g == 0) p.chunk_count[rt * DN_NS + strm] = 0;   // ready for the next call
-            }
-        }
     }
 }
 

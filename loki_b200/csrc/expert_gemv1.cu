@@ -1,15 +1,13 @@
 // expert_gemv1.cu -- the single-token (decode, NT = 1) grouped IQ2_XXS matvecs, one warp per row.
 //
-// Same contract as expert_gemv.cu's kernels for NT = 1 (slot tables in, hq/hd and y out, optional fused
-// combine), organised for one token: a warp computes whole row dot products -- lane l owns the K groups
+// Same contract as expert_gemv.cu's kernels for NT = 1 (slot tables in, hq/hd and y out), organised for one token: a warp computes whole row dot products -- lane l owns the K groups
 // l, l+32, ... and holds their q8 activations in registers -- so rows need no cross-warp reduction and
 // no named barriers.  A producer thread streams small row units into a deep shared-memory ring with
 // cp.async.bulk; each unit is consumed by one warp.
 //   gate/up unit = 2 h rows (2 gate rows + 2 up rows, two 3 696-byte copies); the warp writes
 //     h = silu(g)*u for its 2 rows into a per-tile shared buffer, and the last of the 16 units of a
 //     32-row tile (a shared-memory count) quantises the tile to q8 (hq, hd);
-//   down unit = 8 rows (4 224 bytes): 8 row sums by one warp_reduce8, y = w * 0.125 * sum, then the
-//     fused combine as in expert_gemv.cu (the last slot to finish an 8-row chunk writes h / moe).
+//   down unit = 8 rows (4 224 bytes): 8 row sums by one warp_reduce8, y = w * 0.125 * sum.
 // The IQ2 decode is moe_device.cuh's selector-table path (iq2_dot_sel), table at shared offset 0.
 #include "moe_internal.h"
 #include "moe_device.cuh"
@@ -333,29 +331,6 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
             const float sum = warp_reduce8(v, lane);   // lane l: row (l >> 2), 4 replicas
             const int row0 = rt * D1_TILE + k * D1_UROWS;
             if ((lane & 3) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 2)] = wv * (sum * 0.125f);
-            if (p.chunk_count) {                      // fused combine of these 8 rows once every slot wrote them
-                __threadfence();
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) last = atomicAdd(&p.chunk_count[row0 / 8], 1) == nslots - 1;
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    __threadfence();
-                    for (int i = lane; i < 8 * p.T; i += 32) {
-                        const int row = row0 + (i & 7), t = i >> 3;
-                        float m = 0.0f;
-                        for (int kk = 0; kk < p.keep; ++kk) if (!p.sel || p.sel[t * p.keep + kk] >= 0) m += __ldcg(p.y + ((size_t)t * p.keep + kk) * HIDDEN + row);
-                        if (p.moe) p.moe[(size_t)t * HIDDEN + row] = m;
-                        if (p.h) {
-                            float hv = p.resid[(size_t)t * HIDDEN + row];
-                            if (p.with_shared) hv += __ldcg(p.y + ((size_t)p.T * p.keep + t) * HIDDEN + row);
-                            if (p.shared_sep) hv += p.shared_sep[(size_t)t * HIDDEN + row];
-                            p.h[(size_t)t * HIDDEN + row] = hv + m;
-                        }
-                    }
-                    if (lane == 0) p.chunk_count[row0 / 8] = 0;
-                }
-            }
         }
         j += D1_UPT;
         if (*abort_flag) break;

@@ -31,7 +31,7 @@ struct FLCtx {
     int *s_expert = nullptr, *s_tok = nullptr, *s_out = nullptr; float* s_w = nullptr; int* s_n = nullptr;
     int *counts = nullptr, *offsets = nullptr, *perm = nullptr;
     int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
-    int* err = nullptr; int* rcount = nullptr; int* ccount = nullptr;
+    int* err = nullptr; int* rcount = nullptr;
     // host mirrors (pinned)
     int* h_sel = nullptr; float* h_wts = nullptr; float* h_ncur = nullptr; float* h_fi = nullptr; float* h_h = nullptr;
     float* h_moe = nullptr; int* h_tab = nullptr; float* h_tabw = nullptr; float* h_in = nullptr;
@@ -111,7 +111,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
         dz(&c->counts, N_EXPERTS) == cudaSuccess && dz(&c->offsets, N_EXPERTS + 1) == cudaSuccess && dz(&c->perm, NB * MAX_TOPK) == cudaSuccess &&
         dz(&c->hq, rows * MOE_INTER) == cudaSuccess && dz(&c->hd, rows * (MOE_INTER / 32)) == cudaSuccess &&
         dz(&c->y, rows * HIDDEN) == cudaSuccess && dz(&c->err, 1) == cudaSuccess &&
-        dz(&c->rcount, PREP_ROWS / 8) == cudaSuccess && dz(&c->ccount, HIDDEN / 8) == cudaSuccess &&
+        dz(&c->rcount, PREP_ROWS / 8) == cudaSuccess &&
         hz(&c->h_sel, PREP_ROWS * MAX_TOPK) == cudaSuccess && hz(&c->h_wts, PREP_ROWS * MAX_TOPK) == cudaSuccess &&
         hz(&c->h_ncur, R) == cudaSuccess && hz(&c->h_fi, R) == cudaSuccess && hz(&c->h_h, R) == cudaSuccess &&
         hz(&c->h_moe, R) == cudaSuccess && hz(&c->h_tab, (size_t)4 * ms * MAX_NT + 8) == cudaSuccess &&
@@ -127,7 +127,7 @@ void fl_free(FLCtx* c) {
     if (c->st) cudaStreamSynchronize(c->st);
     void* d[] = { c->ncur, c->ffn_inp, c->logits, c->probs, c->sel, c->wts, c->shared_y, c->h, c->moe, c->ids, c->w, c->mo,
                   c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->counts, c->offsets, c->perm, c->hq, c->hd, c->y, c->err,
-                  c->ncur_all, c->base_all, c->out_all, c->whq, c->whd, c->rcount, c->ccount };
+                  c->ncur_all, c->base_all, c->out_all, c->whq, c->whd, c->rcount };
     for (void* p : d) if (p) cudaFree(p);
     for (int p = 0; p < 2; ++p) {
         void* dd[] = { c->w_expert[p], c->w_tok[p], c->w_out[p], c->w_n[p], c->w_w[p] };
@@ -258,10 +258,12 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     launch_build_slots(sp, st);
     const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)EXPERT_DOWN_BYTES;
     ExpertParams e = expert_params(c, gate, up, down, sg, sd, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->hq, c->hd, c->y);
-    e.chunk_count = c->ccount; e.resid = c->ffn_inp; e.shared_sep = c->shared_y; e.h = c->h; e.moe = c->moe;
-    e.T = n; e.keep = KE; e.with_shared = 0;      // h = ffn_inp + shared (from fl_moe_prepare) + routed
     launch_gate_up(e, nt, c->nsm, st);
     launch_down(e, nt, c->nsm, st);
+    CombineParams cp{};                           // h = ffn_inp + shared (from fl_moe_prepare) + routed
+    cp.y = c->y; cp.resid = c->ffn_inp; cp.T = n; cp.keep = KE; cp.with_shared = 0; cp.shared = c->shared_y;
+    cp.h = c->h; cp.moe = c->moe; cp.ld_out = HIDDEN;
+    launch_combine(cp, st);
     FLCK(cudaMemcpyAsync(c->h_h, c->h, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
     FLCK(cudaMemcpyAsync(c->h_moe, c->moe, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
     FLCK(cudaEventRecord(c->em1, st));

@@ -21,7 +21,7 @@ struct LkMoeCtx {
     int* slot_expert = nullptr; int* slot_tok = nullptr; int* slot_out = nullptr; float* slot_w = nullptr;
     int* nslots = nullptr; int max_slots = 0;
     int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
-    int* err = nullptr; int* tile_count = nullptr; int* chunk_count = nullptr;
+    int* err = nullptr; int* tile_count = nullptr;
     // tensor-core path (T >= gemm_min_tokens): 64-token slots and fp16 operand staging
     int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
     __half* bt = nullptr; __half* ht = nullptr; int* g_cnt = nullptr; int gemm_min_tokens = 64;
@@ -100,8 +100,6 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LK_CU(dalloc(&c->g_out, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_w, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_n, 1));
     LK_CU(dalloc(&c->bt, gemm_tile_halfs(c->g_max, false))); LK_CU(dalloc(&c->ht, gemm_tile_halfs(c->g_max, true)));
     LK_CU(dalloc(&c->g_cnt, c->g_max));
-    LK_CU(dalloc(&c->chunk_count, HIDDEN / 8));
-    LK_CU(cudaMemset(c->chunk_count, 0, (size_t)(HIDDEN / 8) * sizeof(int)));
     LK_CU(cudaMemset(c->y, 0, rows * HIDDEN * sizeof(float)));
     LK_CU(cudaDeviceSynchronize());
     cudaSetDevice(prev);
@@ -112,7 +110,7 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
 void lk_moe_destroy(LkMoeCtx* c) {
     if (!c) return;
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
-                     c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->chunk_count,
+                     c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count,
                      c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt };
     for (void* p : ptrs) if (p) cudaFree(p);
     delete c;
@@ -190,15 +188,17 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
     e.slot_expert = c->slot_expert; e.slot_tok = c->slot_tok; e.slot_out = c->slot_out; e.slot_w = c->slot_w; e.nslots = c->nslots;
     e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err;
     if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
-    if (h || moe) {                   // the combine runs inside the down kernel
-        e.chunk_count = c->chunk_count; e.resid = resid; e.shared_sep = nullptr; e.h = h; e.moe = moe;
-        e.T = T; e.keep = keep; e.with_shared = c->cfg.with_shared; e.sel = sel;
-    }
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
     if (c->ev[1]) LK_CU(record_event(c->ev[1], st));
     launch_down(e, nt, c->nsm, st);
     if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
+    if (h || moe) {                   // a separate kernel: fusing it into the down kernel's tail measured slower
+        CombineParams cp{};
+        cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
+        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel;
+        launch_combine(cp, st);
+    }
     if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
     LK_CU(cudaGetLastError());
     return LK_OK;

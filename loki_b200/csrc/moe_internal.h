@@ -51,12 +51,6 @@ struct ExpertParams {
     int8_t* hq; float* hd;                            // SwiGLU output q8: [rows][MOE_INTER], scales [rows][MOE_INTER/32]
     float* y;                                         // weighted expert outputs [rows][HIDDEN]
     int* err;
-    // combine fused into the down kernel (used when chunk_count is set): the last slot to finish an 8-row
-    // chunk of the output writes h = resid + shared + sum_k y[t*keep+k], moe = sum_k y[t*keep+k] for those
-    // rows of all T tokens (shared = y rows T*keep + t when with_shared, and/or the shared_sep rows)
-    int* chunk_count;                                 // HIDDEN/8 zeroed counters (left zeroed)
-    const float* resid; const float* shared_sep; float* h; float* moe; int T; int keep; int with_shared;
-    const int* sel;                                   // optional [T][keep]: entries with a negative id are not summed
 };
 void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st);
 void launch_down(const ExpertParams& p, int nt, int grid, cudaStream_t st);
