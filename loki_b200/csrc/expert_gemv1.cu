@@ -7,7 +7,8 @@
 //   gate/up unit = 2 h rows (2 gate rows + 2 up rows, two 3 696-byte copies); the warp writes
 //     h = silu(g)*u for its 2 rows into a per-tile shared buffer, and the last of the 16 units of a
 //     32-row tile (a shared-memory count) quantises the tile to q8 (hq, hd);
-//   down unit = 8 rows (4 224 bytes): 8 row sums by one warp_reduce8, y = w * 0.125 * sum.
+//   down: copies of 32 rows (16 896 bytes), 4 per 128-row tile; warp w takes 8 rows of copy w/4: 8 row sums
+//     by one warp_reduce8, y = w * 0.125 * sum.
 // The IQ2 decode is moe_device.cuh's selector-table path (iq2_dot_sel), table at shared offset 0.
 #include "moe_internal.h"
 #include "moe_device.cuh"
@@ -227,16 +228,17 @@ __global__ void __launch_bounds__(G1_THREADS, 1) k_gate_up1(ExpertParams p) {
 constexpr int D1_WARPS = 16;
 constexpr int D1_THREADS = (D1_WARPS + 1) * 32;
 constexpr int D1_ROWB = (MOE_INTER / QK) * BLK_IQ2;  // 528
-constexpr int D1_UROWS = 8;
-constexpr int D1_UBYTES = D1_UROWS * D1_ROWB;        // 4224
-constexpr int D1_NST = 32;
-constexpr int D1_TILE = 128;                         // rows per (slot, tile): 16 units
-constexpr int D1_UPT = D1_TILE / D1_UROWS;
+constexpr int D1_UROWS = 8;                          // rows per warp unit
+constexpr int D1_CROWS = 32;                         // rows per bulk copy (16 896 B: copies under ~8 KB
+constexpr int D1_CBYTES = D1_CROWS * D1_ROWB;        //   cannot stream HBM at full rate)
+constexpr int D1_TILE = 128;                         // rows per (slot, tile): 4 copies, 16 warp units
+constexpr int D1_CPT = D1_TILE / D1_CROWS;
+constexpr int D1_NST = 2 * D1_CPT;                   // two tiles: warp w always uses stages w/4 and w/4 + 4
 constexpr int D1_TILES_PER_SLOT = HIDDEN / D1_TILE;  // 56
 
 constexpr int D1_OFF_TAB = 0;
 constexpr int D1_OFF_RING = D1_OFF_TAB + SEL_TAB_BYTES;
-constexpr int D1_OFF_BAR = D1_OFF_RING + D1_NST * D1_UBYTES;
+constexpr int D1_OFF_BAR = D1_OFF_RING + D1_NST * D1_CBYTES;
 constexpr int D1_OFF_ABORT = D1_OFF_BAR + 2 * D1_NST * 8;
 constexpr int D1_SMEM = D1_OFF_ABORT + 16;
 
@@ -253,7 +255,7 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
     init_sel_table((uint32_t*)(smem + D1_OFF_TAB), tid, D1_THREADS);
     if (tid == 0) {
         *abort_flag = 0;
-        for (int s = 0; s < D1_NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < D1_NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], D1_CROWS / D1_UROWS); }
         fence_mbar_init();
     }
     __syncthreads();
@@ -263,11 +265,11 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
             for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
                 const int s = tile % nslots, rt = tile / nslots;
                 const uint8_t* dw = slot_matrix1(p, p.slot_expert[s], 2);
-                for (int k = 0; k < D1_UPT; ++k, ++j) {
+                for (int k = 0; k < D1_CPT; ++k, ++j) {
                     const int st = j % D1_NST;
                     if (*abort_flag || !mbar_wait(&empty[st], ((j / D1_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; goto drain; }
-                    mbar_arrive_expect_tx(&full[st], D1_UBYTES);
-                    bulk_g2s(ring + st * D1_UBYTES, dw + (size_t)(rt * D1_TILE + k * D1_UROWS) * D1_ROWB, D1_UBYTES, &full[st]);
+                    mbar_arrive_expect_tx(&full[st], D1_CBYTES);
+                    bulk_g2s(ring + st * D1_CBYTES, dw + (size_t)(rt * D1_TILE + k * D1_CROWS) * D1_ROWB, D1_CBYTES, &full[st]);
                 }
             }
         drain:
@@ -306,11 +308,12 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
                 dx[q] = 0.0f;
             }
         }
-        for (int k = warp; k < D1_UPT; k += D1_WARPS) {
-            const uint32_t ju = j + (uint32_t)k;
+        {
+            const int k = warp;                       // warp unit: rows 8k..8k+7 of the tile, copy k / 4
+            const uint32_t ju = j + (uint32_t)(k / (D1_CROWS / D1_UROWS));
             const int st = ju % D1_NST;
             if (!*abort_flag && !mbar_wait(&full[st], (ju / D1_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) *abort_flag = 1;
-            const uint32_t ub = ring_s + st * D1_UBYTES;
+            const uint32_t ub = ring_s + st * D1_CBYTES + (k % (D1_CROWS / D1_UROWS)) * D1_UROWS * D1_ROWB;
             const uint32_t ubg = ub + gal, ubd = ub + boff0;
             float v[8];
             #pragma unroll
@@ -332,7 +335,7 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
             const int row0 = rt * D1_TILE + k * D1_UROWS;
             if ((lane & 3) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 2)] = wv * (sum * 0.125f);
         }
-        j += D1_UPT;
+        j += D1_CPT;
         if (*abort_flag) break;
     }
 }
