@@ -523,6 +523,77 @@ def run_ep_prefill(args, ws, rank, local, dist):
     return o
 
 
+def run_imbalance(args, ws, rank, local, dist):
+    """one MoE layer, keep 2 of the top-8 (the reference's --experts 2 mode), T in
+    {1, 8, 64, 512}; the router bias makes expert popularity Zipf(1.2)-like with the hottest expert at ~10x
+    the mean entry count (lam calibrated by loki_b200.synthetic).  Each step runs on a different seeded layer
+    (4 resident) and L2 is flushed (a 256 MB write) between steps outside the timed windows.  N > 1: expert
+    parallel, T tokens per rank (weak scaling)."""
+    import torch
+    from loki_b200 import moe as M
+    from loki_b200 import synthetic as S
+    from loki_b200.ep import EpMoeLayer, NativeEpOps, NativeComm
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lam = S.calibrate_zipf_lambda()
+    bias = torch.from_numpy(S.zipf_bias(lam)).to(dev)
+    E = NE // ws
+    nl = 4
+    layers = [M.LayerWeights(dev, SEED, 100 + L, n_experts=E, expert0=rank * E, router_bias=bias) for L in range(nl)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    comm = NativeComm(local) if ws > 1 else None
+    sweep = {}
+    hbm, bf16, peak_kind = measured_peaks()
+    for T in (1, 8, 64, 512):
+        g = torch.Generator(device=dev).manual_seed(9000 + T + 17 * rank)
+        xs = [torch.randn(T, HIDDEN, device=dev, generator=g) for _ in range(nl)]
+        rs = [torch.randn(T, HIDDEN, device=dev, generator=g) for _ in range(nl)]
+        if ws > 1:
+            ops = NativeEpOps(local, ws, T, keep=2)
+            layer = EpMoeLayer(comm, ops)
+            fwd = lambda i: layer.forward(layers[i % nl], xs[i % nl], rs[i % nl])
+        else:
+            ctx = M.MoeLayer(local, keep=2, max_tokens=T)
+            fwd = lambda i: ctx.forward(layers[i % nl], xs[i % nl], rs[i % nl])
+        for i in range(args.warmup):
+            fwd(i)
+        torch.cuda.synchronize(dev)
+        times, sels = [], []
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            barrier(dist)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            out = fwd(i)
+            b.record()
+            torch.cuda.synchronize(dev)
+            times.append(a.elapsed_time(b))
+            sels.append(out[2].reshape(-1))
+        ms = float(np.mean([max_over_ranks(dist, t) for t in times]))
+        sel = torch.cat(sels)
+        if dist is not None:
+            alls = [torch.empty_like(sel) for _ in range(ws)]
+            dist.all_gather(alls, sel)
+            sel = torch.cat(alls)
+        cnt = torch.bincount(sel.long(), minlength=NE).float() / args.steps
+        sweep[str(T)] = {"tokens_per_s": round(T * ws / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
+                         "hottest_over_mean": round(float(cnt.max() / cnt.mean()), 2),
+                         "experts_used": int((cnt > 0).sum()),
+                         "path": "tcgen05 GEMM" if T >= 64 else "dp4a matvec"}
+    if comm is not None:
+        comm.close()
+    out = {
+        "metric": "MoE-layer tokens/s (load-imbalance sweep: keep 2, Zipf-biased router, T=512 headline)",
+        "value": sweep["512"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sweep["512"]["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "iq2_xxs x q8 (dp4a) / fp16 tcgen05", "data": "synthetic: seeded IQ2_XXS experts, x N(0,1) fp32, Zipf router bias",
+        "config": {"workload": "config4_imbalance", "keep": 2, "top_k": 8, "zipf_s": 1.2, "lambda": round(lam, 5),
+                   "parallelism": "ep%d" % ws if ws > 1 else "single", "l2": "flushed (256 MB write) between steps"},
+        "sweep": sweep,
+    }
+    return out
+
+
 def e2e_decode(args, layers, distinct, keep):
     """Decode through the engine-facing fl_* ABI with host buffers: per layer fl_moe_prepare (H2D x/resid,
     router, shared expert) -> fl_fetch (D2H sel/wts/ncur/fi) -> host keep pass -> fl_moe (D2H h, moe).
@@ -684,7 +755,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "imbalance"])
     ap.add_argument("--tokens", type=int, default=512, help="prefill workload: tokens per step")
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--keep", type=int, default=8)
@@ -702,6 +773,14 @@ def main():
         return
     import torch
     dist = dist_init(ws, local)
+    if args.workload == "imbalance":
+        out = run_imbalance(args, ws, rank, local, dist)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if ws > 1 and args.parallelism == "ep":
         out = run_ep_prefill(args, ws, rank, local, dist) if args.workload == "prefill" else run_ep_decode(args, ws, rank, local, dist)
         if rank == 0:

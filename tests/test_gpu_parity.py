@@ -231,3 +231,33 @@ def test_layer_deterministic(moe, layer_weights):
     h1 = layer.forward(layer_weights, x, r)[0].clone()
     h2 = layer.forward(layer_weights, x, r)[0].clone()
     assert torch.equal(h1, h2)
+
+
+# ---------------------------------------------------------------- load imbalance
+@pytest.mark.parametrize("T", [8, 64, 200])
+def test_layer_zipf_bias_keep2(moe, oracle, T):
+    """keep 2 of top-8 with a Zipf-calibrated router bias (hottest expert ~10x the mean entries): routing
+    bit-exact, outputs within RTOL_L2 (T >= 64 takes the tensor-core path with its hot, multi-slot experts)."""
+    from loki_b200 import synthetic as S
+    bias = S.zipf_bias(S.calibrate_zipf_lambda())
+    W = moe.LayerWeights("cuda", SEED, 0, router_bias=torch.from_numpy(bias))
+    try:
+        rng = np.random.default_rng(4000 + T)
+        x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+        r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+        layer = moe.MoeLayer(0, keep=2, max_tokens=T)
+        h, mo, sel, w = layer.forward(W, _dev(x), _dev(r))
+        layer.device_error()
+        sel, w = sel.cpu().numpy(), w.cpu().numpy()
+        _, osel, ow = oracle.router(x, W.router_w.float().cpu().numpy(), bias, oracle.route_cfg(8, 2, 1, 1, 1))
+        np.testing.assert_array_equal(sel, osel)
+        np.testing.assert_array_equal(w, ow)
+        counts = np.bincount(sel.reshape(-1), minlength=256)
+        assert counts.max() >= 4 * max(counts.mean(), 1e-9)          # the bias does concentrate the routing
+        tok = list(range(T)) if T <= 64 else [0, 1, 50, 99, 150, T - 1]
+        ref = oracle_layer(oracle, SEED, 0, x, r, sel, w, tokens=tok, hq8=T < 64)
+        assert rel_l2(mo.cpu().numpy()[tok], ref["moe"]) < RTOL_L2
+        assert rel_l2(h.cpu().numpy()[tok], ref["h"]) < RTOL_L2
+    finally:
+        del W
+        torch.cuda.empty_cache()
