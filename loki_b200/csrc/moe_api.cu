@@ -48,7 +48,10 @@ static cudaError_t record_event(cudaEvent_t ev, cudaStream_t st) {
     return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal) : cudaEventRecord(ev, st);
 }
 
-static int slot_nt(int T) { return T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8; }
+// tokens per matvec slot below the GEMM threshold: one.  Measured per layer (keep 8): T=2 169 vs 187 us
+// (NT=2), T=8 476 vs 978 us (NT=8), T=32 1658 vs 2664 us -- the single-token kernels' cheaper inner loop
+// outweighs re-reading an expert's weights for each of its (few) tokens.
+static int slot_nt(int) { return 1; }
 
 extern "C" {
 

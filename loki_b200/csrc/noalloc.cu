@@ -51,7 +51,7 @@ std::mutex g_mu;
 unsigned char* g_addr[NA_MAX_DEVICES] = {};
 int g_nsm[NA_MAX_DEVICES] = {};
 
-int slot_nt_na(int T) { return T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8; }
+int slot_nt_na(int) { return 1; }             // as the context path: single-token slots
 
 // device address of the scratch on the current device (looked up once per device)
 int scratch_for_current_device(unsigned char** out, int* nsm) {
