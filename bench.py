@@ -579,14 +579,14 @@ def run_imbalance(args, ws, rank, local, dist):
         sweep[str(T)] = {"tokens_per_s": round(T * ws / (ms / 1e3), 1), "ms_per_step": round(ms, 4),
                          "hottest_over_mean": round(float(cnt.max() / cnt.mean()), 2),
                          "experts_used": int((cnt > 0).sum()),
-                         "path": "tcgen05 GEMM" if T >= 64 else "dp4a matvec"}
+                         "path": "tcgen05 GEMM" if T >= 192 else ("mma.sync register-fed" if T >= 48 else "dp4a matvec")}
     if comm is not None:
         comm.close()
     out = {
         "metric": "MoE-layer tokens/s (load-imbalance sweep: keep 2, Zipf-biased router, T=512 headline)",
         "value": sweep["512"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": sweep["512"]["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "iq2_xxs x q8 (dp4a) / fp16 tcgen05", "data": "synthetic: seeded IQ2_XXS experts, x N(0,1) fp32, Zipf router bias",
+        "dtype": "iq2_xxs x q8 (dp4a) / fp16 mma.sync / fp16 tcgen05", "data": "synthetic: seeded IQ2_XXS experts, x N(0,1) fp32, Zipf router bias",
         "config": {"workload": "config4_imbalance", "keep": 2, "top_k": 8, "zipf_s": 1.2, "lambda": round(lam, 5),
                    "parallelism": "ep%d" % ws if ws > 1 else "single", "l2": "flushed (256 MB write) between steps"},
         "sweep": sweep,

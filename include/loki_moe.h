@@ -94,9 +94,13 @@ LK_API int lk_moe_forward(LkMoeCtx* ctx, const LkMoeWeights* W, const float* x, 
 /* per-slot weighted expert outputs of the last lk_moe_experts/lk_moe_forward call: [T*keep (+T shared)][7168] */
 LK_API const float* lk_moe_slot_outputs(LkMoeCtx* ctx);
 
-/* token count from which lk_moe_forward / lk_moe_experts use the tensor-core GEMM path (tcgen05,
- * slots of up to 64 tokens per expert) instead of the grouped matvecs (default 64) */
+/* token count from which lk_moe_forward / lk_moe_experts (and the expert-parallel stages) use the
+ * tensor-core GEMM path (tcgen05, slots of up to 128 tokens per expert; default 192) */
 LK_API int lk_moe_set_gemm_threshold(LkMoeCtx* ctx, int min_tokens);
+/* below the GEMM threshold (default 192), calls with at least min_tokens tokens (default 48) take the register-fed
+ * mma.sync path (IQ2 decoded into tensor-core fragments, reused by up to 16 tokens per expert slot);
+ * smaller calls take the single-token dp4a matvecs */
+LK_API int lk_moe_set_mma_threshold(LkMoeCtx* ctx, int min_tokens);
 
 /* optional per-kernel timing: events[0..3] (cudaEvent_t) recorded on the launch stream before the gate/up
  * kernel, after it, after the down kernel and after the combine of every following lk_moe_forward /

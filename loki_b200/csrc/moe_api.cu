@@ -24,7 +24,13 @@ struct LkMoeCtx {
     int* err = nullptr; int* tile_count = nullptr;
     // tensor-core path (T >= gemm_min_tokens): 64-token slots and fp16 operand staging
     int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
-    __half* bt = nullptr; __half* ht = nullptr; int* g_cnt = nullptr; int gemm_min_tokens = 64;
+    __half* bt = nullptr; __half* ht = nullptr; int* g_cnt = nullptr; int gemm_min_tokens = 192;
+    // register-fed mma.sync path (mma_min_tokens <= T < gemm_min_tokens): MM_NT-token slots, fp16 activations
+    int* m_expert = nullptr; int* m_tok = nullptr; int* m_out = nullptr; float* m_w = nullptr; int* m_n = nullptr;
+    int* m_cnt = nullptr; int m_max = 0; __half* xh = nullptr; __half* hb = nullptr; int mma_min_tokens = 48;
+    // defaults from a per-layer sweep (keep 8, uniform routing): single-token dp4a matvecs fastest up to ~32
+    // tokens (T=32: 1.67 ms vs 2.03 mma, 2.23 tcgen05), mma.sync from 48 (T=64: 2.65 vs 3.24 / 2.96 ms,
+    // T=128: 3.26 vs 3.56 tcgen05), tcgen05 from 192 (T=256: 3.84 vs 4.13 mma; T=512: 4.31 vs 6.26)
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     char msg[256] = {0};
 };
@@ -103,6 +109,11 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LK_CU(dalloc(&c->g_out, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_w, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_n, 1));
     LK_CU(dalloc(&c->bt, gemm_tile_halfs(c->g_max, false))); LK_CU(dalloc(&c->ht, gemm_tile_halfs(c->g_max, true)));
     LK_CU(dalloc(&c->g_cnt, c->g_max));
+    c->m_max = max_slots_for(T, KE, NE, MM_NT, cfg->with_shared);
+    LK_CU(dalloc(&c->m_expert, c->m_max)); LK_CU(dalloc(&c->m_tok, (size_t)c->m_max * MM_NT));
+    LK_CU(dalloc(&c->m_out, (size_t)c->m_max * MM_NT)); LK_CU(dalloc(&c->m_w, (size_t)c->m_max * MM_NT)); LK_CU(dalloc(&c->m_n, 1));
+    LK_CU(dalloc(&c->m_cnt, c->m_max));
+    LK_CU(dalloc(&c->xh, (size_t)T * HIDDEN)); LK_CU(dalloc(&c->hb, rows * MOE_INTER));
     LK_CU(cudaMemset(c->y, 0, rows * HIDDEN * sizeof(float)));
     LK_CU(cudaDeviceSynchronize());
     cudaSetDevice(prev);
@@ -114,7 +125,8 @@ void lk_moe_destroy(LkMoeCtx* c) {
     if (!c) return;
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
                      c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count,
-                     c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt };
+                     c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt,
+                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->xh, c->hb };
     for (void* p : ptrs) if (p) cudaFree(p);
     delete c;
 }
@@ -238,9 +250,65 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int
     return LK_OK;
 }
 
+// the register-fed mma.sync path: 16-token slots, IQ2 decoded into mma fragments, SwiGLU -> fp16 h, combine
+static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
+                        const float* w, int keep, float* h, float* moe, cudaStream_t st) {
+    if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
+    SlotParams s{};
+    s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = MM_NT; s.with_shared = c->cfg.with_shared;
+    s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
+    s.slot_expert = c->m_expert; s.slot_tok = c->m_tok; s.slot_out = c->m_out; s.slot_w = c->m_w; s.nslots = c->m_n;
+    s.max_slots = c->m_max; s.err = c->err;
+    launch_build_slots(s, st);
+    MmaParams m{};
+    m.gate = (const uint8_t*)W->gate; m.up = (const uint8_t*)W->up; m.down = (const uint8_t*)W->down;
+    m.gate_stride = W->gate_stride; m.up_stride = W->up_stride; m.down_stride = W->down_stride;
+    m.sh_gate = (const uint8_t*)W->sh_gate; m.sh_up = (const uint8_t*)W->sh_up; m.sh_down = (const uint8_t*)W->sh_down;
+    m.x = x; m.ld_x = ld_x; m.T = T;
+    m.slot_expert = c->m_expert; m.slot_tok = c->m_tok; m.slot_out = c->m_out; m.slot_w = c->m_w; m.nslots = c->m_n;
+    m.max_slots = c->m_max; m.slot_cnt = c->m_cnt; m.xh = c->xh; m.hb = c->hb; m.y = c->y; m.err = c->err;
+    if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
+    launch_slot_mma(m, c->nsm, st);
+    if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
+    if (h || moe) {
+        CombineParams cp{};
+        cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
+        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel;
+        launch_combine(cp, st);
+    }
+    if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
+    LK_CU(cudaGetLastError());
+    return LK_OK;
+}
+
+// the expert stage for routing (sel, w) [T][keep], by token count: single-token dp4a matvecs (the slot
+// tables of T == 1 may already have been written by the router: slots_ready), the register-fed mma.sync
+// path, or the tcgen05 GEMMs
+static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
+                     const float* w, int keep, float* h, float* moe, bool slots_ready, cudaStream_t st) {
+    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
+    if (T >= c->mma_min_tokens) return run_mma_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
+    if (!slots_ready) {
+        SlotParams s{};
+        s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = slot_nt(T);
+        s.with_shared = c->cfg.with_shared;
+        s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
+        s.slot_expert = c->slot_expert; s.slot_tok = c->slot_tok; s.slot_out = c->slot_out; s.slot_w = c->slot_w;
+        s.nslots = c->nslots; s.max_slots = c->max_slots; s.err = c->err;
+        launch_build_slots(s, st);
+    }
+    return run_experts(c, W, x, ld_x, resid, T, keep, sel, h, moe, slot_nt(T), st);
+}
+
 int lk_moe_set_gemm_threshold(LkMoeCtx* c, int min_tokens) {
     if (!c || min_tokens < 1) return LK_ERR_ARG;
     c->gemm_min_tokens = min_tokens;
+    return LK_OK;
+}
+
+int lk_moe_set_mma_threshold(LkMoeCtx* c, int min_tokens) {
+    if (!c || min_tokens < 1) return LK_ERR_ARG;
+    c->mma_min_tokens = min_tokens;
     return LK_OK;
 }
 
@@ -251,11 +319,7 @@ int lk_moe_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const flo
     int rc = check_weights(c, W, false);
     if (rc) return rc;
     if (T > c->cfg.max_tokens || keep > c->cfg.keep) return set_err(c, LK_ERR_CAPACITY, "T=%d keep=%d above capacity", T, keep);
-    cudaStream_t st = (cudaStream_t)stream;
-    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, HIDDEN, resid, T, sel, w, keep, h, moe, st);
-    rc = lk_moe_dispatch(c, sel, w, T, keep, nullptr, nullptr, nullptr, stream);
-    if (rc) return rc;
-    return run_experts(c, W, x, HIDDEN, resid, T, keep, sel, h, moe, slot_nt(T), st);
+    return run_stage(c, W, x, HIDDEN, resid, T, sel, w, keep, h, moe, false, (cudaStream_t)stream);
 }
 
 int lk_moe_forward(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T,
@@ -270,15 +334,7 @@ int lk_moe_forward(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const flo
     const int keep = c->cfg.keep;
     RouterParams p = router_params(c, W, x, T, logits_override, c->sel, c->w, T == 1);
     launch_router(p, st);
-    if (T >= c->gemm_min_tokens) {
-        rc = run_gemm_path(c, W, x, HIDDEN, resid, T, c->sel, c->w, keep, h, moe, st);
-    } else {
-        if (T > 1) {
-            rc = lk_moe_dispatch(c, c->sel, c->w, T, keep, nullptr, nullptr, nullptr, stream);
-            if (rc) return rc;
-        }
-        rc = run_experts(c, W, x, HIDDEN, resid, T, keep, c->sel, h, moe, slot_nt(T), st);
-    }
+    rc = run_stage(c, W, x, HIDDEN, resid, T, c->sel, c->w, keep, h, moe, T == 1, st);
     if (rc) return rc;
     if (sel) LK_CU(cudaMemcpyAsync(sel, c->sel, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));
     if (w) LK_CU(cudaMemcpyAsync(w, c->w, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));
@@ -298,10 +354,7 @@ int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int
     launch_ep_unpack(recv_rows, R, keep, c->sel, c->w, st);
     const float* x = (const float*)((const uint8_t*)recv_rows + LK_EP_ROW_HDR_BYTES);
     const int ld = LK_EP_ROW_BYTES / 4;
-    if (R >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld, nullptr, R, c->sel, c->w, keep, nullptr, out, st);
-    rc = lk_moe_dispatch(c, c->sel, c->w, R, keep, nullptr, nullptr, nullptr, stream);
-    if (rc) return rc;
-    return run_experts(c, W, x, ld, nullptr, R, keep, c->sel, nullptr, out, slot_nt(R), st);
+    return run_stage(c, W, x, ld, nullptr, R, c->sel, c->w, keep, nullptr, out, false, st);
 }
 
 int lk_ep_shared(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, float* h_partial,
@@ -314,15 +367,8 @@ int lk_ep_shared(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float
     if (W->down_fmt != LK_FMT_IQ2) return set_err(c, LK_ERR_UNSUPPORTED, "down format %d", W->down_fmt);
     if (T > c->cfg.max_tokens) return set_err(c, LK_ERR_CAPACITY, "T=%d > capacity %d", T, c->cfg.max_tokens);
     if (T == 0) return LK_OK;
-    cudaStream_t st = (cudaStream_t)stream;
-    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, HIDDEN, resid, T, nullptr, nullptr, 0, h_partial, nullptr, st);
-    SlotParams s{};                   // keep = 0: shared-expert slots only
-    s.sel = nullptr; s.w = nullptr; s.T = T; s.keep = 0; s.n_experts = c->cfg.n_experts; s.nt = slot_nt(T); s.with_shared = 1;
-    s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
-    s.slot_expert = c->slot_expert; s.slot_tok = c->slot_tok; s.slot_out = c->slot_out; s.slot_w = c->slot_w;
-    s.nslots = c->nslots; s.max_slots = c->max_slots; s.err = c->err;
-    launch_build_slots(s, st);
-    return run_experts(c, W, x, HIDDEN, resid, T, 0, nullptr, h_partial, nullptr, slot_nt(T), st);
+    // keep = 0: shared-expert slots only
+    return run_stage(c, W, x, HIDDEN, resid, T, nullptr, nullptr, 0, h_partial, nullptr, false, (cudaStream_t)stream);
 }
 
 const float* lk_moe_slot_outputs(LkMoeCtx* c) { return c ? c->y : nullptr; }

@@ -10,6 +10,7 @@ namespace lk {
 constexpr int SHARED_SLOT = -1;      // slot_expert value of the shared expert
 constexpr int MAX_NT = 8;            // tokens per work slot of the grouped matvecs
 constexpr int GEMM_NT = 128;         // tokens per work slot of the tensor-core GEMMs (prefill)
+constexpr int MM_NT = 16;            // tokens per work slot of the register-fed mma.sync products (mid-size T)
 
 // ---- router
 struct RouterParams {
@@ -81,6 +82,22 @@ struct GemmParams {
 };
 void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st);
 size_t gemm_tile_halfs(int max_slots, bool down);     // size of bt (down = false) / ht (down = true)
+
+// ---- register-fed mma.sync grouped products (mid-size T): slots of up to MM_NT tokens
+struct MmaParams {
+    const uint8_t* gate; const uint8_t* up; const uint8_t* down;
+    int64_t gate_stride, up_stride, down_stride;
+    const uint8_t* sh_gate; const uint8_t* sh_up; const uint8_t* sh_down;
+    const float* x; int ld_x; int T;                  // activations [T][HIDDEN] fp32, rows ld_x floats apart
+    const int* slot_expert; const int* slot_tok; const int* slot_out; const float* slot_w; const int* nslots;  // [slot][MM_NT]
+    int max_slots;
+    int* slot_cnt;                                    // [max_slots] tokens per slot (written by the pre-pass)
+    __half* xh;                                       // [T][HIDDEN] fp16 of the q8-dequantised x
+    __half* hb;                                       // [rows][MOE_INTER] fp16 SwiGLU output
+    float* y;                                         // [rows][HIDDEN] weighted expert outputs
+    int* err;
+};
+void launch_slot_mma(const MmaParams& p, int nsm, cudaStream_t st);
 
 // ---- seeded IQ2_XXS weight generation (moe_format.h generator) for n_experts consecutive experts
 void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,

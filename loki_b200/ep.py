@@ -106,6 +106,10 @@ class NativeEpOps:
         self.home.set_gemm_threshold(min_tokens)
         self.expert.set_gemm_threshold(min_tokens)
 
+    def set_mma_threshold(self, min_tokens):
+        self.home.set_mma_threshold(min_tokens)
+        self.expert.set_mma_threshold(min_tokens)
+
     def route(self, W, x, logits_override=None):
         _, sel, w = self.home.route(W, x, logits_override=logits_override)
         return sel, w

@@ -48,6 +48,7 @@ def test_ep_emulated_ranks_one_gpu(native, oracle, n_ranks, T_loc, fixed_cap_max
     ops = [NativeEpOps(0, n_ranks, T_loc) for _ in range(n_ranks)]
     for o in ops:
         o.set_gemm_threshold(1 << 20)              # the matvec path: same q8 scheme as the oracle
+        o.set_mma_threshold(1 << 20)
     inputs = [_inputs(T_loc, r) for r in range(n_ranks)]
     torch.cuda.synchronize()
     out, errs = [None] * n_ranks, []
@@ -84,6 +85,7 @@ def _nccl_worker(rank, port, T_loc, fixed_cap_max, comm_kind, out_dir):
         W = LayerWeights("cuda:%d" % rank, SEED, 0, n_experts=128, expert0=rank * 128)
         ops = NativeEpOps(rank, 2, T_loc)
         ops.set_gemm_threshold(1 << 20)
+        ops.set_mma_threshold(1 << 20)
         comm = NativeComm(rank) if comm_kind == "native" else TorchComm()
         layer = EpMoeLayer(comm, ops, fixed_cap_max=fixed_cap_max)
         x, r = (torch.from_numpy(a).cuda() for a in _inputs(T_loc, rank))

@@ -134,11 +134,43 @@ def test_experts_small_arena(native, moe, oracle, T, keep):
     x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
     r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
     layer = moe.MoeLayer(0, keep=keep, max_tokens=T)
+    layer.set_mma_threshold(1 << 20)                  # the single-token dp4a matvecs (q8 h, as the reference)
     h, mo = layer.experts(ws, _dev(x), _dev(r), _dev(sel), _dev(w))
     layer.device_error()
     ref = oracle_layer(oracle, SEED, layer_id, x, r, sel, w)
     e_moe, e_h = rel_l2(mo.cpu().numpy(), ref["moe"]), rel_l2(h.cpu().numpy(), ref["h"])
     assert e_moe < RTOL_L2 and e_h < RTOL_L2, (e_moe, e_h)
+
+
+@pytest.mark.parametrize("T,keep", [(2, 8), (5, 2), (16, 8), (40, 4), (100, 8)])
+def test_experts_mma_path(native, moe, oracle, T, keep):
+    """The register-fed mma.sync path (fp16 SwiGLU output, as the tcgen05 path) against the oracle."""
+    NE = 12
+    layer_id = 17
+    buf = torch.empty(3 * NE * MAT + 3 * MAT, dtype=torch.uint8, device="cuda")
+    base = buf.data_ptr()
+    for m in range(3):
+        rows, K = (INTER, HIDDEN) if m < 2 else (HIDDEN, INTER)
+        moe.gen_iq2(base + m * NE * MAT, SEED, layer_id, m, 0, NE, rows, K, MAT)
+        moe.gen_iq2(base + 3 * NE * MAT + m * MAT, SEED, layer_id, m, 256, 1, rows, K, MAT)
+    ws = native.LkMoeWeights(base, base + NE * MAT, base + 2 * NE * MAT, MAT, MAT, MAT, native.FMT_IQ2,
+                             base + 3 * NE * MAT, base + 3 * NE * MAT + MAT, base + 3 * NE * MAT + 2 * MAT, None, 0, None)
+    rng = np.random.default_rng(T * 13 + keep)
+    sel = np.stack([rng.choice(NE, keep, replace=False) for _ in range(T)]).astype(np.int32)
+    w = rng.uniform(0.05, 1.0, (T, keep)).astype(np.float32)
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    layer = moe.MoeLayer(0, keep=keep, max_tokens=T)
+    layer.set_mma_threshold(2)
+    layer.set_gemm_threshold(1 << 20)
+    h, mo = layer.experts(ws, _dev(x), _dev(r), _dev(sel), _dev(w))
+    layer.device_error()
+    tok = list(range(T)) if T <= 40 else [0, 1, T // 2, T - 2, T - 1]
+    ref = oracle_layer(oracle, SEED, layer_id, x, r, sel, w, tokens=tok, hq8=False)
+    e_moe, e_h = rel_l2(mo.cpu().numpy()[tok], ref["moe"]), rel_l2(h.cpu().numpy()[tok], ref["h"])
+    assert e_moe < RTOL_L2 and e_h < RTOL_L2, (e_moe, e_h)
+    ref_q = oracle_layer(oracle, SEED, layer_id, x, r, sel, w, tokens=tok, hq8=True)
+    assert rel_l2(mo.cpu().numpy()[tok], ref_q["moe"]) < 1e-2
 
 
 @pytest.mark.parametrize("T,keep", [(2, 8), (40, 8), (70, 2), (130, 8)])
@@ -184,7 +216,7 @@ def layer_weights(moe):
 
 
 def _layer_case(moe, oracle, W, T, keep=8, n_group=1, topk_group=1, logits=None, sample=None, seed=0):
-    hq8 = T < 64                                      # T >= 64 takes the tensor-core path (h kept at 16 bits)
+    hq8 = T < 48                                      # T >= 48 takes the mma / tensor-core paths (h kept at 16 bits)
     rng = np.random.default_rng(1000 + T + seed)
     x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
     r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
@@ -255,9 +287,15 @@ def test_layer_zipf_bias_keep2(moe, oracle, T):
         counts = np.bincount(sel.reshape(-1), minlength=256)
         assert counts.max() >= 4 * max(counts.mean(), 1e-9)          # the bias does concentrate the routing
         tok = list(range(T)) if T <= 64 else [0, 1, 50, 99, 150, T - 1]
-        ref = oracle_layer(oracle, SEED, 0, x, r, sel, w, tokens=tok, hq8=T < 64)
+        ref = oracle_layer(oracle, SEED, 0, x, r, sel, w, tokens=tok, hq8=T < 48)
         assert rel_l2(mo.cpu().numpy()[tok], ref["moe"]) < RTOL_L2
         assert rel_l2(h.cpu().numpy()[tok], ref["h"]) < RTOL_L2
     finally:
         del W
         torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("T", [64, 256])
+def test_layer_default_paths(moe, oracle, layer_weights, T):
+    """The default thresholds route T=64 to the mma.sync path and T=256 to the tcgen05 path."""
+    _layer_case(moe, oracle, layer_weights, T, sample=[0, 1, T // 2, T - 1])

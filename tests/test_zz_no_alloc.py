@@ -64,6 +64,7 @@ def test_noalloc_matches_existing_entry_point_twice(native, arena):
         sel, w, x, r = _case(rng, NE, T, keep)
         h, mo = _noalloc(native, ws, sel, w, x, r)
         ref = M.MoeLayer(0, keep=keep, max_tokens=T)
+        ref.set_mma_threshold(1 << 20)                    # the same single-token matvec path as the no-alloc call
         h_ref, mo_ref = ref.experts(ws, x, r, sel, w)
         ref.device_error()
         e_h = rel_l2(h.cpu().numpy(), h_ref.cpu().numpy())
