@@ -456,7 +456,7 @@ def run_ep_decode(args, ws, rank, local, dist):
         "e2e": {"value": round(n_e2e * ws / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": args.layers * 2 * HIDDEN * 4, "d2h_bytes_per_step": args.layers * HIDDEN * 4,
                 "path": "pinned host x/resid -> CUDA-graph step of EpMoeLayer.forward x58 -> pinned host h (stream events)"},
-        "gpu_launches": args.steps * args.layers * 11,
+        "gpu_launches": args.steps * args.layers * 9,      # router, pack (2), unpack, slots, gate/up, down, combine, EP combine
     }
     if cl:
         out["clocks"] = cl

@@ -5,11 +5,12 @@
  * resident in HBM, tokens stay on their home rank, and two all-to-all exchanges (done by the caller,
  * e.g. NCCL through torch.distributed) move rows to the experts and partial sums back:
  *
- *   home:   lk_moe_route -> lk_ep_pack -> send rows          lk_ep_shared (overlaps the exchange)
+ *   home:   lk_moe_route -> lk_ep_pack -> send rows (every token also to its own rank)
  *   all-to-all #1 (rows)
- *   expert: lk_ep_experts(received rows) -> partial sums
+ *   expert: lk_ep_experts(received rows) -> routed partial sums; the rows from this rank itself also get
+ *           the shared expert in the same launches (a shared-expert-only stage is too small to fill a GPU)
  *   all-to-all #2 (partial sums, the transpose of #1)
- *   home:   lk_ep_combine -> h, moe
+ *   home:   lk_ep_combine -> h = resid + shared + sum of partials, moe = sum of partials
  *
  * A row is LK_EP_ROW_BYTES: a 64-byte header (int32 sel[8]: the expert id local to the receiving rank or
  * -1, float w[8]: routing weights) and the token's activations (fp32 [7168]).  Rows for rank d form block
@@ -32,27 +33,31 @@ extern "C" {
 
 /* home side: sel/w [T][keep] (global expert ids, from lk_moe_route) and x [T][7168] -> send rows,
  * send_counts [n_ranks] (rows per destination) and row_map [T][n_ranks] (the send-buffer row of (t, d),
- * or -1).  keep <= 8, n_ranks in 1..8 dividing 256.  Ids outside [0, 256) set the context-free error
- * word `err` (a device int, may be null) and are dropped. */
-LK_API int lk_ep_pack(const int* sel, const float* w, const float* x, int T, int keep, int n_ranks, int cap,
-                      void* send_rows, int* send_counts, int* row_map, int* err, lk_stream_t stream);
+ * or -1).  self_rank >= 0: every token gets a row in that rank's block even without routed entries there
+ * (its shared expert runs on it); -1: rows only where a token has entries.  keep <= 8, n_ranks in 1..8
+ * dividing 256.  Ids outside [0, 256) set the context-free error word `err` (a device int, may be null)
+ * and are dropped. */
+LK_API int lk_ep_pack(const int* sel, const float* w, const float* x, int T, int keep, int n_ranks, int self_rank,
+                      int cap, void* send_rows, int* send_counts, int* row_map, int* err, lk_stream_t stream);
 
 /* expert side: R received rows -> out [R][7168] fp32, row r = sum over its entries of w * expert(x) in
- * entry order (the partial sum of the routed experts this rank owns).  ctx: a context with n_experts = the
- * shard size, with_shared = 0 and max_tokens >= R; W: the shard's arenas (expert ids local). */
-LK_API int lk_ep_experts(LkMoeCtx* ctx, const LkMoeWeights* W, const void* recv_rows, int R, int keep, float* out,
-                         lk_stream_t stream);
+ * entry order (the partial sum of the routed experts this rank owns); shared_out [shared_rows][7168] =
+ * shared(x) of the rows [shared_row0, shared_row0 + shared_rows) (this rank's own tokens; 0 rows: none,
+ * shared_out may be null).  ctx: a context with n_experts = the shard size, max_tokens >= R and
+ * with_shared = 1 when shared_rows > 0; W: the shard's arenas (expert ids local) and shared expert. */
+LK_API int lk_ep_experts(LkMoeCtx* ctx, const LkMoeWeights* W, const void* recv_rows, int R, int keep,
+                         int shared_row0, int shared_rows, float* out, float* shared_out, lk_stream_t stream);
 
-/* home side: the shared expert of the home tokens, h_partial [T][7168] = resid + shared(x).  ctx: a
- * context with with_shared = 1 (W->sh_* set). */
+/* home side, when the shared expert is not folded into lk_ep_experts: h_partial [T][7168] = resid +
+ * shared(x) of the home tokens.  ctx: a context with with_shared = 1 (W->sh_* set). */
 LK_API int lk_ep_shared(LkMoeCtx* ctx, const LkMoeWeights* W, const float* x, const float* resid, int T,
                         float* h_partial, lk_stream_t stream);
 
-/* home side, after the return exchange: ret rows in send-buffer order -> h = h_partial + sum_d ret and
- * moe = sum_d ret (d ascending) for each of the T tokens; h_partial / h may be null (then h is not
- * written). */
+/* home side, after the return exchange: ret rows in send-buffer order -> h = h_partial (+ shared, when
+ * given) + sum_d ret and moe = sum_d ret (d ascending) for each of the T tokens; h_partial / h may be null
+ * (then h is not written). */
 LK_API int lk_ep_combine(const float* ret, const int* row_map, int T, int n_ranks, const float* h_partial,
-                         float* h, float* moe, lk_stream_t stream);
+                         const float* shared, float* h, float* moe, lk_stream_t stream);
 
 /* the exchange: an NCCL communicator over the n_ranks GPUs (libnccl.so.2 bound at run time) and the
  * all-to-all of byte blocks.  lk_ep_comm_id (one rank) makes the LK_EP_COMM_ID_BYTES id every rank passes

@@ -19,9 +19,10 @@ __global__ void k_combine(CombineParams p) {
     }
     if (p.moe) ((float4*)(p.moe + (size_t)t * p.ld_out))[c] = r;
     if (!p.h) return;
-    float4 h = ((const float4*)(p.resid + (size_t)t * p.ld_out))[c];
-    if (p.with_shared) {
-        const float4 v = ((const float4*)(p.y + ((size_t)p.T * p.keep + t) * HIDDEN))[c];
+    float4 h = p.resid ? ((const float4*)(p.resid + (size_t)t * p.ld_out))[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    const int nsh = p.sh_n < 0 ? 0 : (p.sh_n > 0 ? p.sh_n : p.T), j = t - p.sh_t0;
+    if (p.with_shared && j >= 0 && j < nsh) {
+        const float4 v = ((const float4*)(p.y + ((size_t)p.T * p.keep + j) * HIDDEN))[c];
         h.x += v.x; h.y += v.y; h.z += v.z; h.w += v.w;
     }
     if (p.shared) {

@@ -7,7 +7,8 @@
 //   stable by (t, k) -- a counting sort whose in-chunk ranks come from warp match masks;
 //   the work-slot table of the grouped matvecs: expert e's list cut into slots of `nt` entries
 //   (slot_tok = token, slot_out = entry row of the hq/y buffers, slot_w = routing weight; -1/0 pads),
-//   experts in ascending order, then ceil(T/nt) shared-expert slots (entry rows T*keep + t, weight 1).
+//   experts in ascending order, then the shared-expert slots (tokens sh_t0.. of SlotParams, entry rows
+//   T*keep + j, weight 1).
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
@@ -87,16 +88,17 @@ __global__ void __launch_bounds__(DS_THREADS) k_build_slots(SlotParams p) {
         }
     }
     const int nrs = soff[NE];
-    const int nss = p.with_shared ? (p.T + nt - 1) / nt : 0;
+    const int nsh = !p.with_shared || p.sh_n < 0 ? 0 : (p.sh_n > 0 ? p.sh_n : p.T);
+    const int nss = (nsh + nt - 1) / nt;
     for (int j = tid; j < nss; j += DS_THREADS) {
         const int s = nrs + j;
         if (s >= p.max_slots) continue;
         p.slot_expert[s] = SHARED_SLOT;
         for (int m = 0; m < nt; ++m) {
             const int t = j * nt + m;
-            p.slot_tok[s * nt + m] = t < p.T ? t : -1;
-            p.slot_out[s * nt + m] = t < p.T ? entries + t : -1;
-            p.slot_w[s * nt + m] = t < p.T ? 1.0f : 0.0f;
+            p.slot_tok[s * nt + m] = t < nsh ? p.sh_t0 + t : -1;
+            p.slot_out[s * nt + m] = t < nsh ? entries + t : -1;
+            p.slot_w[s * nt + m] = t < nsh ? 1.0f : 0.0f;
         }
     }
     if (tid == 0) { p.offsets[NE] = off[NE]; *p.nslots = min(nrs + nss, p.max_slots); }

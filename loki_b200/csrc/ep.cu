@@ -20,7 +20,8 @@ static_assert(sizeof(EpRowHdr) == LK_EP_ROW_HDR_BYTES, "header size");
 // one CTA: per destination rank the stable (token-ascending) row index of every token that has an entry
 // there, the per-rank counts, block offsets (fixed capacity or compact) and the headers of unused rows
 __global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(const int* __restrict__ sel, int T, int keep, int n_ranks,
-                                                              int cap, int* counts, int* row_map, uint8_t* send, int* err) {
+                                                              int self_rank, int cap, int* counts, int* row_map, uint8_t* send,
+                                                              int* err) {
     __shared__ int wc[LK_EP_MAX_RANKS][32], pre[LK_EP_MAX_RANKS][32], base[LK_EP_MAX_RANKS], off[LK_EP_MAX_RANKS + 1];
     __shared__ int cnt[LK_EP_MAX_RANKS];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -31,6 +32,7 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(const int* __restri
         const int t = c0 + tid;
         unsigned mask = 0;
         if (t < T) {
+            if (self_rank >= 0) mask |= 1u << self_rank;     // every token's row to its own rank (shared expert)
             for (int k = 0; k < keep; ++k) {
                 const int e = sel[t * keep + k];
                 if (e >= 0 && e < N_EXPERTS) mask |= 1u << (e / epr);
@@ -125,7 +127,7 @@ __global__ void k_ep_unpack(const uint8_t* __restrict__ recv, int R, int keep, i
 }
 
 __global__ void k_ep_combine(const float* __restrict__ ret, const int* __restrict__ row_map, int T, int n_ranks,
-                             const float* __restrict__ hpart, float* h, float* moe) {
+                             const float* __restrict__ hpart, const float* __restrict__ shared, float* h, float* moe) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;       // float4 index over T x HIDDEN
     if (i >= T * (HIDDEN / 4)) return;
     const int t = i / (HIDDEN / 4), c = i % (HIDDEN / 4);
@@ -138,7 +140,11 @@ __global__ void k_ep_combine(const float* __restrict__ ret, const int* __restric
     }
     if (moe) ((float4*)(moe + (size_t)t * HIDDEN))[c] = r;
     if (h && hpart) {
-        const float4 b = ((const float4*)(hpart + (size_t)t * HIDDEN))[c];
+        float4 b = ((const float4*)(hpart + (size_t)t * HIDDEN))[c];
+        if (shared) {
+            const float4 v = ((const float4*)(shared + (size_t)t * HIDDEN))[c];
+            b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
+        }
         ((float4*)(h + (size_t)t * HIDDEN))[c] = make_float4(b.x + r.x, b.y + r.y, b.z + r.z, b.w + r.w);
     }
 }
@@ -154,25 +160,26 @@ using namespace lk;
 
 extern "C" {
 
-int lk_ep_pack(const int* sel, const float* w, const float* x, int T, int keep, int n_ranks, int cap, void* send_rows,
-               int* send_counts, int* row_map, int* err, lk_stream_t stream) {
+int lk_ep_pack(const int* sel, const float* w, const float* x, int T, int keep, int n_ranks, int self_rank, int cap,
+               void* send_rows, int* send_counts, int* row_map, int* err, lk_stream_t stream) {
     if (T < 0 || keep < 1 || keep > MAX_TOPK || n_ranks < 1 || n_ranks > LK_EP_MAX_RANKS || (N_EXPERTS % n_ranks) ||
+        self_rank < -1 || self_rank >= n_ranks ||
         cap < 0 || (cap > 0 && cap < T) || !send_counts || (T > 0 && (!sel || !w || !x || !send_rows || !row_map)))
         return LK_ERR_ARG;
     if (((uintptr_t)send_rows & 15) || ((uintptr_t)x & 15)) return LK_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
-    k_ep_plan<<<1, EP_PLAN_THREADS, 0, st>>>(sel, T, keep, n_ranks, cap, send_counts, row_map, (uint8_t*)send_rows, err);
+    k_ep_plan<<<1, EP_PLAN_THREADS, 0, st>>>(sel, T, keep, n_ranks, self_rank, cap, send_counts, row_map, (uint8_t*)send_rows, err);
     if (T > 0) k_ep_copy<<<T, 256, 0, st>>>(sel, w, x, keep, n_ranks, row_map, (uint8_t*)send_rows);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
-int lk_ep_combine(const float* ret, const int* row_map, int T, int n_ranks, const float* h_partial, float* h, float* moe,
-                  lk_stream_t stream) {
+int lk_ep_combine(const float* ret, const int* row_map, int T, int n_ranks, const float* h_partial, const float* shared,
+                  float* h, float* moe, lk_stream_t stream) {
     if (T < 0 || n_ranks < 1 || n_ranks > LK_EP_MAX_RANKS || (T > 0 && (!row_map || (!ret && n_ranks > 0))))
         return LK_ERR_ARG;
     if (T == 0) return LK_OK;
     const int n = T * (HIDDEN / 4);
-    k_ep_combine<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(ret, row_map, T, n_ranks, h_partial, h, moe);
+    k_ep_combine<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(ret, row_map, T, n_ranks, h_partial, shared, h, moe);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 

@@ -22,6 +22,7 @@ struct LkMoeCtx {
     int* nslots = nullptr; int max_slots = 0;
     int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
     int* err = nullptr; int* tile_count = nullptr;
+    int sh_t0 = 0, sh_n = 0;          // shared-expert token range of the next expert stage (SlotParams semantics)
     // tensor-core path (T >= gemm_min_tokens): 64-token slots and fp16 operand staging
     int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
     __half* bt = nullptr; __half* ht = nullptr; int* g_cnt = nullptr; int gemm_min_tokens = 192;
@@ -185,7 +186,7 @@ int lk_moe_dispatch(LkMoeCtx* c, const int* sel, const float* w, int T, int keep
     s.with_shared = c->cfg.with_shared;
     s.counts = counts ? counts : c->counts; s.offsets = offsets ? offsets : c->offsets; s.perm = perm ? perm : c->perm;
     s.slot_expert = c->slot_expert; s.slot_tok = c->slot_tok; s.slot_out = c->slot_out; s.slot_w = c->slot_w;
-    s.nslots = c->nslots; s.max_slots = c->max_slots; s.err = c->err;
+    s.nslots = c->nslots; s.max_slots = c->max_slots; s.err = c->err; s.sh_t0 = c->sh_t0; s.sh_n = c->sh_n;
     launch_build_slots(s, (cudaStream_t)stream);
     LK_CU(cudaGetLastError());
     return LK_OK;
@@ -202,7 +203,6 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
     e.x = x; e.ld_x = ld_x;
     e.slot_expert = c->slot_expert; e.slot_tok = c->slot_tok; e.slot_out = c->slot_out; e.slot_w = c->slot_w; e.nslots = c->nslots;
     e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err;
-    if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
     if (c->ev[1]) LK_CU(record_event(c->ev[1], st));
@@ -211,7 +211,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
     if (h || moe) {                   // a separate kernel: fusing it into the down kernel's tail measured slower
         CombineParams cp{};
         cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
-        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel;
+        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel; cp.sh_t0 = c->sh_t0; cp.sh_n = c->sh_n;
         launch_combine(cp, st);
     }
     if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
@@ -226,7 +226,7 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int
     s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = GEMM_NT; s.with_shared = c->cfg.with_shared;
     s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
     s.slot_expert = c->g_expert; s.slot_tok = c->g_tok; s.slot_out = c->g_out; s.slot_w = c->g_w; s.nslots = c->g_n;
-    s.max_slots = c->g_max; s.err = c->err;
+    s.max_slots = c->g_max; s.err = c->err; s.sh_t0 = c->sh_t0; s.sh_n = c->sh_n;
     launch_build_slots(s, st);
     GemmParams g{};
     g.gate = (const uint8_t*)W->gate; g.up = (const uint8_t*)W->up; g.down = (const uint8_t*)W->down;
@@ -239,10 +239,9 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int
     launch_prefill_gemm(g, c->nsm, st);
     if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
     if (h || moe) {
-        if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
-        CombineParams cp{};
+            CombineParams cp{};
         cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
-        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel;
+        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel; cp.sh_t0 = c->sh_t0; cp.sh_n = c->sh_n;
         launch_combine(cp, st);
     }
     if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
@@ -253,12 +252,11 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int
 // the register-fed mma.sync path: 16-token slots, IQ2 decoded into mma fragments, SwiGLU -> fp16 h, combine
 static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
                         const float* w, int keep, float* h, float* moe, cudaStream_t st) {
-    if (h && !resid) return set_err(c, LK_ERR_ARG, "h requested without resid");
     SlotParams s{};
     s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = MM_NT; s.with_shared = c->cfg.with_shared;
     s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
     s.slot_expert = c->m_expert; s.slot_tok = c->m_tok; s.slot_out = c->m_out; s.slot_w = c->m_w; s.nslots = c->m_n;
-    s.max_slots = c->m_max; s.err = c->err;
+    s.max_slots = c->m_max; s.err = c->err; s.sh_t0 = c->sh_t0; s.sh_n = c->sh_n;
     launch_build_slots(s, st);
     MmaParams m{};
     m.gate = (const uint8_t*)W->gate; m.up = (const uint8_t*)W->up; m.down = (const uint8_t*)W->down;
@@ -273,7 +271,7 @@ static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int 
     if (h || moe) {
         CombineParams cp{};
         cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
-        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel;
+        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel; cp.sh_t0 = c->sh_t0; cp.sh_n = c->sh_n;
         launch_combine(cp, st);
     }
     if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
@@ -294,7 +292,7 @@ static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_
         s.with_shared = c->cfg.with_shared;
         s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
         s.slot_expert = c->slot_expert; s.slot_tok = c->slot_tok; s.slot_out = c->slot_out; s.slot_w = c->slot_w;
-        s.nslots = c->nslots; s.max_slots = c->max_slots; s.err = c->err;
+        s.nslots = c->nslots; s.max_slots = c->max_slots; s.err = c->err; s.sh_t0 = c->sh_t0; s.sh_n = c->sh_n;
         launch_build_slots(s, st);
     }
     return run_experts(c, W, x, ld_x, resid, T, keep, sel, h, moe, slot_nt(T), st);
@@ -342,9 +340,13 @@ int lk_moe_forward(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const flo
 }
 
 // ---- expert-parallel stages that run on a context (include/loki_ep.h)
-int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int R, int keep, float* out, lk_stream_t stream) {
-    if (!c || !W || R < 0 || keep < 1 || (R > 0 && (!recv_rows || !out))) return set_err(c, LK_ERR_ARG, "bad argument");
-    if (c->cfg.with_shared) return set_err(c, LK_ERR_ARG, "expert-side context must have with_shared = 0");
+int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int R, int keep, int shared_row0,
+                  int shared_rows, float* out, float* shared_out, lk_stream_t stream) {
+    if (!c || !W || R < 0 || keep < 1 || (R > 0 && (!recv_rows || !out)) || (shared_rows > 0 && !shared_out))
+        return set_err(c, LK_ERR_ARG, "bad argument");
+    if (shared_rows < 0 || shared_row0 < 0 || shared_row0 + shared_rows > R)
+        return set_err(c, LK_ERR_ARG, "shared rows [%d, +%d) outside the %d received rows", shared_row0, shared_rows, R);
+    if (shared_rows > 0 && !c->cfg.with_shared) return set_err(c, LK_ERR_ARG, "shared rows need a with_shared context");
     if (R > c->cfg.max_tokens || keep > c->cfg.keep) return set_err(c, LK_ERR_CAPACITY, "R=%d keep=%d above capacity", R, keep);
     if (R == 0) return LK_OK;
     if ((uintptr_t)recv_rows & 15) return set_err(c, LK_ERR_ARG, "rows must be 16-byte aligned");
@@ -354,7 +356,16 @@ int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int
     launch_ep_unpack(recv_rows, R, keep, c->sel, c->w, st);
     const float* x = (const float*)((const uint8_t*)recv_rows + LK_EP_ROW_HDR_BYTES);
     const int ld = LK_EP_ROW_BYTES / 4;
-    return run_stage(c, W, x, ld, nullptr, R, c->sel, c->w, keep, nullptr, out, false, st);
+    // out = the routed partial sums; the shared expert runs in the same launches on the rows
+    // [shared_row0, +shared_rows), and its outputs (entry rows R*keep + j) are copied to shared_out
+    c->sh_t0 = shared_row0; c->sh_n = shared_rows > 0 ? shared_rows : -1;
+    rc = run_stage(c, W, x, ld, nullptr, R, c->sel, c->w, keep, nullptr, out, false, st);
+    c->sh_t0 = 0; c->sh_n = 0;
+    if (rc) return rc;
+    if (shared_rows > 0)
+        LK_CU(cudaMemcpyAsync(shared_out, c->y + (size_t)R * keep * HIDDEN, (size_t)shared_rows * HIDDEN * sizeof(float),
+                              cudaMemcpyDeviceToDevice, st));
+    return LK_OK;
 }
 
 int lk_ep_shared(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, float* h_partial,

@@ -37,6 +37,9 @@ struct SlotParams {
     int* slot_expert; int* slot_tok; int* slot_out; float* slot_w; int* nslots;   // slot tables
     int max_slots;
     int* err;                                           // device error word (bad expert ids)
+    // shared-expert slots (with_shared) cover tokens [sh_t0, sh_t0 + sh_n) -- sh_n = 0: all T tokens from 0,
+    // sh_n < 0: none; their entry rows are T*keep + (t - sh_t0)
+    int sh_t0, sh_n;
 };
 void launch_build_slots(const SlotParams& p, cudaStream_t st);
 int max_slots_for(int T, int keep, int n_experts, int nt, int with_shared);
@@ -63,6 +66,7 @@ struct CombineParams {
     const float* shared;              // optional [T][HIDDEN] shared-expert output added to h
     float* h; float* moe; int ld_out;
     const int* sel;                   // optional [T][keep]: entries with a negative id are not summed
+    int sh_t0, sh_n;                  // shared-expert rows as in SlotParams; resid may be null (zero)
 };
 void launch_combine(const CombineParams& p, cudaStream_t st);
 

@@ -4,9 +4,10 @@ No counterpart in the reference, which runs one GPU and streams experts from NVM
 (src/moe_stream_buffer.h).  Rank r keeps experts [r*E, (r+1)*E) (E = 256 / n_ranks) resident, plus
 the router and the shared expert.  Tokens stay on their home rank; one layer is
 
-    home   route -> pack rows per owner rank                 shared expert (overlaps exchange #1)
+    home   route -> pack rows per owner rank (every token also gets a row to its own rank)
     exchange #1: rows (all-to-all)
-    owner  expert stage on the received rows -> per-row partial sums
+    owner  expert stage on the received rows -> per-row partial sums; the rows from this rank itself also
+           get the shared expert, in the same launches
     exchange #2: partial sums (all-to-all, the transpose of #1)
     home   combine: h = resid + shared + sum over ranks, moe = sum over ranks
 
@@ -98,7 +99,7 @@ class NativeEpOps:
         self.n_ranks, self.keep = n_ranks, keep
         self.home = MoeLayer(self.device, topk, keep, renorm, n_group, topk_group, scale, with_shared=True,
                              max_tokens=max_local_tokens)
-        self.expert = MoeLayer(self.device, topk, keep, renorm, n_group, topk_group, scale, with_shared=False,
+        self.expert = MoeLayer(self.device, topk, keep, renorm, n_group, topk_group, scale, with_shared=True,
                                max_tokens=max(1, n_ranks * max_local_tokens), n_experts=N_EXPERTS // n_ranks)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
 
@@ -114,14 +115,14 @@ class NativeEpOps:
         _, sel, w = self.home.route(W, x, logits_override=logits_override)
         return sel, w
 
-    def pack(self, sel, w, x, cap):
+    def pack(self, sel, w, x, cap, self_rank):
         T = x.shape[0]
         rows = self.n_ranks * cap if cap else T * self.n_ranks
         send = torch.empty(max(rows, 1), EP_ROW_BYTES, dtype=torch.uint8, device=self.device)
         counts = torch.empty(self.n_ranks, dtype=torch.int32, device=self.device)
         row_map = torch.empty(T, self.n_ranks, dtype=torch.int32, device=self.device)
-        check(lib().lk_ep_pack(_ptr(sel), _ptr(w), _ptr(x), T, sel.shape[1], self.n_ranks, cap, _ptr(send), _ptr(counts),
-                               _ptr(row_map), _ptr(self.err), _stream()))
+        check(lib().lk_ep_pack(_ptr(sel), _ptr(w), _ptr(x), T, sel.shape[1], self.n_ranks, self_rank, cap, _ptr(send),
+                               _ptr(counts), _ptr(row_map), _ptr(self.err), _stream()))
         return send, counts, row_map
 
     def shared(self, W, x, resid):
@@ -131,19 +132,21 @@ class NativeEpOps:
                                             _stream()))
         return hpart
 
-    def experts(self, W, recv, R, keep):
+    def experts(self, W, recv, R, keep, shared_row0=0, shared_rows=0):
+        """Routed partial sums of the R received rows, and the shared expert of rows [shared_row0, +shared_rows)."""
         ret = torch.empty(max(R, 1), HIDDEN, device=self.device)
+        shared = torch.empty(max(shared_rows, 1), HIDDEN, device=self.device)
         ws = W.struct()
-        self.expert._check(lib().lk_ep_experts(self.expert.ctx, ctypes.byref(ws), _ptr(recv), R, keep, _ptr(ret),
-                                               _stream()))
-        return ret[:R]
+        self.expert._check(lib().lk_ep_experts(self.expert.ctx, ctypes.byref(ws), _ptr(recv), R, keep, shared_row0,
+                                               shared_rows, _ptr(ret), _ptr(shared), _stream()))
+        return ret[:R], shared[:shared_rows]
 
-    def combine(self, ret_home, row_map, hpart):
+    def combine(self, ret_home, row_map, hpart, shared=None):
         T = row_map.shape[0]
         h = torch.empty(T, HIDDEN, device=self.device)
         moe = torch.empty(T, HIDDEN, device=self.device)
-        check(lib().lk_ep_combine(_ptr(ret_home), _ptr(row_map), T, self.n_ranks, _ptr(hpart), _ptr(h), _ptr(moe),
-                                  _stream()))
+        check(lib().lk_ep_combine(_ptr(ret_home), _ptr(row_map), T, self.n_ranks, _ptr(hpart), _ptr(shared), _ptr(h),
+                                  _ptr(moe), _stream()))
         return h, moe
 
     def device_error(self):
@@ -166,22 +169,23 @@ class EpMoeLayer:
         self.n_ranks = comm.size
         self.fixed_cap_max = fixed_cap_max
         self.last_counts = None          # (rows sent per rank, rows received per rank) of the last compact call
-        self._side = None                # CUDA stream of the shared expert (overlaps exchange #1)
 
     def forward(self, W, x, resid, logits_override=None):
         """W: this rank's LayerWeights shard (router + shared expert + experts [r*E, (r+1)*E)); x, resid:
         [T][7168] fp32 home tokens.  Returns h, moe ([T][7168]), sel, w ([T][keep] global ids)."""
         ops, comm, NR = self.ops, self.comm, self.n_ranks
         T = x.shape[0]
+        me = comm.rank
         sel, w = ops.route(W, x, logits_override)
         keep = sel.shape[1]
         fixed = T <= self.fixed_cap_max
         cap = T if fixed else 0
-        send, counts, row_map = ops.pack(sel, w, x, cap)
+        send, counts, row_map = ops.pack(sel, w, x, cap, me)
         if fixed:
             recv = torch.empty(NR * cap, EP_ROW_BYTES, dtype=torch.uint8, device=send.device)
-            work = comm.all_to_all(recv, send[:NR * cap], async_op=True)
+            comm.all_to_all(recv, send[:NR * cap])
             sent, got = None, None
+            own0 = me * cap                                            # this rank's own rows in the receive buffer
         else:
             rcounts = torch.empty_like(counts)
             comm.all_to_all(rcounts, counts)
@@ -189,22 +193,11 @@ class EpMoeLayer:
             sent, got = both[:NR], both[NR:]
             self.last_counts = (sent, got)
             recv = torch.empty(sum(got), EP_ROW_BYTES, dtype=torch.uint8, device=send.device)
-            work = comm.all_to_all(recv, send[:sum(sent)], got, sent, async_op=True)
-        if x.is_cuda:                                                  # shared expert beside exchange #1
-            main = torch.cuda.current_stream(x.device)
-            if self._side is None:
-                self._side = torch.cuda.Stream(x.device)
-            self._side.wait_stream(main)
-            with torch.cuda.stream(self._side):
-                hpart = ops.shared(W, x, resid)
-        else:
-            hpart = ops.shared(W, x, resid)
-        work.wait()
+            comm.all_to_all(recv, send[:sum(sent)], got, sent)
+            own0 = sum(got[:me])
         R = recv.shape[0]
-        ret = ops.experts(W, recv, R, keep)
+        ret, shared = ops.experts(W, recv, R, keep, own0, T)           # + the shared expert of the own T rows
         ret_home = torch.empty(NR * cap if fixed else sum(sent), HIDDEN, dtype=ret.dtype, device=ret.device)
         comm.all_to_all(ret_home, ret, sent, got)
-        if x.is_cuda:
-            main.wait_stream(self._side)
-        h, moe = ops.combine(ret_home, row_map, hpart)
+        h, moe = ops.combine(ret_home, row_map, resid, shared)
         return h, moe, sel, w

@@ -66,10 +66,10 @@ SIGNATURES = {
     "lk_moe_last_error": (ctypes.c_char_p, [_P]),
     "lk_moe_experts_noalloc": (_I, [ctypes.POINTER(LkMoeWeights), _P, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "lk_gen_iq2": (_I, [_P, ctypes.c_uint64, _I, _I, _I, _I, _I, _I, _I64, _P]),
-    "lk_ep_pack": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
-    "lk_ep_experts": (_I, [_P, ctypes.POINTER(LkMoeWeights), _P, _I, _I, _P, _P]),
+    "lk_ep_pack": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "lk_ep_experts": (_I, [_P, ctypes.POINTER(LkMoeWeights), _P, _I, _I, _I, _I, _P, _P, _P]),
     "lk_ep_shared": (_I, [_P, ctypes.POINTER(LkMoeWeights), _P, _P, _I, _P, _P]),
-    "lk_ep_combine": (_I, [_P, _P, _I, _I, _P, _P, _P, _P]),
+    "lk_ep_combine": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
     "lk_ep_comm_id": (_I, [_P]),
     "lk_ep_comm_create": (_I, [_P, _I, _I, _I, ctypes.POINTER(_P)]),
     "lk_ep_comm_destroy": (None, [_P]),

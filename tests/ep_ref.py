@@ -46,12 +46,12 @@ class RefEpOps:
         _, sel, w = self.oracle.router(x.numpy(), W.router_w, W.router_bias, self.cfg, logits=lo)
         return torch.from_numpy(sel), torch.from_numpy(w)
 
-    def pack(self, sel, w, x, cap):
+    def pack(self, sel, w, x, cap, self_rank):
         sel, w, x = sel.numpy(), w.numpy(), x.numpy()
         T, keep = sel.shape
         NR, epr = self.n_ranks, N_EXPERTS // self.n_ranks
         owner = sel // epr
-        lists = [[t for t in range(T) if (owner[t] == d).any()] for d in range(NR)]
+        lists = [[t for t in range(T) if d == self_rank or (owner[t] == d).any()] for d in range(NR)]
         counts = np.array([len(l) for l in lists], np.int32)
         offs = np.concatenate([[0], np.cumsum([cap if cap else c for c in counts])]).astype(np.int64)
         rows = NR * cap if cap else T * NR
@@ -74,18 +74,25 @@ class RefEpOps:
                 send[row, 64:] = x[t].view(np.uint8)
         return torch.from_numpy(send), torch.from_numpy(counts), torch.from_numpy(row_map)
 
-    def shared(self, W, x, resid):
-        x, resid = x.numpy(), resid.numpy()
+    def _shared(self, W, x):
         T = x.shape[0]
         g, u, dn = W.matrices(W.expert0)
         sg, su, sd = W.matrices(N_EXPERTS)
-        out = self.oracle.moe_layer(x, resid, g, u, dn, MAT, np.zeros((T, 1), np.int32), np.zeros((T, 1), np.float32),
-                                    sg, su, sd)
-        return torch.from_numpy(out["h"])
+        out = self.oracle.moe_layer(x, np.zeros_like(x), g, u, dn, MAT, np.zeros((T, 1), np.int32),
+                                    np.zeros((T, 1), np.float32), sg, su, sd)
+        return out["h"]
 
-    def experts(self, W, recv, R, keep):
+    def experts(self, W, recv, R, keep, shared_row0=0, shared_rows=0):
         recv = recv.numpy()
         ret = np.zeros((R, HIDDEN), np.float32)
+        shared = np.zeros((shared_rows, HIDDEN), np.float32)
+        if shared_rows:
+            xs = recv[shared_row0:shared_row0 + shared_rows, 64:].copy().view(np.float32)
+            shared = self._shared(W, xs)
+        ret, shared = self._routed(W, recv, R, keep, ret), torch.from_numpy(shared)
+        return ret, shared
+
+    def _routed(self, W, recv, R, keep, ret):
         if R == 0:
             return torch.from_numpy(ret)
         sel = recv[:, :32].copy().view(np.int32)[:, :keep]
@@ -104,7 +111,7 @@ class RefEpOps:
         ret[live] = out["moe"]
         return torch.from_numpy(ret)
 
-    def combine(self, ret_home, row_map, hpart):
+    def combine(self, ret_home, row_map, hpart, shared=None):
         ret_home, row_map, hpart = ret_home.numpy(), row_map.numpy(), hpart.numpy()
         T = row_map.shape[0]
         acc = np.zeros((T, HIDDEN), np.float32)
@@ -112,7 +119,8 @@ class RefEpOps:
             for t in range(T):
                 if row_map[t, d] >= 0:
                     acc[t] += ret_home[row_map[t, d]]
-        return torch.from_numpy(hpart + acc), torch.from_numpy(acc)
+        base = hpart if shared is None else hpart + shared.numpy()
+        return torch.from_numpy(base + acc), torch.from_numpy(acc)
 
 
 class _Done:

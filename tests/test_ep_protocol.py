@@ -73,10 +73,10 @@ def test_ep_protocol_gloo(oracle, tmp_path, T_loc, fixed_cap_max, n_group):
         ref = oracle_layer(oracle, SEED, 0, x, r, osel, ow)
         assert rel_l2(got["moe"], ref["moe"]) < 1e-5
         assert rel_l2(got["h"], ref["h"]) < 1e-5
-        if T_loc > fixed_cap_max:                  # compact layout: counts are the tokens with an expert there
+        if T_loc > fixed_cap_max:                  # compact layout: tokens with an expert there, all to the own rank
             sent = got["counts"][0]
             owners = osel // 128
-            assert list(sent) == [int((owners == d).any(axis=1).sum()) for d in range(WORLD)]
+            assert list(sent) == [T_loc if d == rank else int((owners == d).any(axis=1).sum()) for d in range(WORLD)]
             total_sent += int(np.sum(sent))
     if T_loc > fixed_cap_max:
         assert total_sent > 0
