@@ -323,10 +323,10 @@ def _min_over_ranks(dist, v):
     return float(t.item())
 
 
-def _ep_setup(args, ws, rank, local, dist, max_local_tokens, layers_wanted):
+def _ep_setup(args, ws, rank, local, dist, max_local_tokens, layers_wanted, p2p_cap=0):
     import torch
     from loki_b200 import moe as M
-    from loki_b200.ep import EpMoeLayer, NativeEpOps, NativeComm
+    from loki_b200.ep import EpMoeLayer, NativeEpOps, NativeComm, P2PExchange
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     E = NE // ws
@@ -336,8 +336,9 @@ def _ep_setup(args, ws, rank, local, dist, max_local_tokens, layers_wanted):
     shards = [M.LayerWeights(dev, SEED, L, n_experts=E, expert0=rank * E) for L in range(distinct)]
     comm = NativeComm(local)
     ops = NativeEpOps(local, ws, max_local_tokens, keep=args.keep)
+    p2p = P2PExchange(local, p2p_cap) if p2p_cap else None
     torch.cuda.synchronize(dev)
-    return dev, shards, distinct, comm, ops, EpMoeLayer(comm, ops)
+    return dev, shards, distinct, comm, ops, EpMoeLayer(comm, ops, p2p=p2p)
 
 
 def run_ep_decode(args, ws, rank, local, dist):
@@ -345,7 +346,8 @@ def run_ep_decode(args, ws, rank, local, dist):
     import torch
     import ctypes
     from loki_b200 import native as N
-    dev, shards, distinct, comm, ops, layer = _ep_setup(args, ws, rank, local, dist, 1, args.layers)
+    dev, shards, distinct, comm, ops, layer = _ep_setup(args, ws, rank, local, dist, 1, args.layers,
+                                                        p2p_cap=1 if args.exchange == "p2p" else 0)
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     xs = torch.randn(args.layers, 1, HIDDEN, device=dev, generator=g)
     rs = torch.randn(args.layers, 1, HIDDEN, device=dev, generator=g)
@@ -435,6 +437,8 @@ def run_ep_decode(args, ws, rank, local, dist):
     hbm, bf16, peak_kind = measured_peaks()
     graph.reset()
     graph_ev.reset()
+    if layer.p2p is not None:
+        layer.p2p.close()
     comm.close()
     out = {
         "metric": "MoE-layer tokens/s (T=1 decode through 58 layers)", "value": round(value, 2), "unit": "tokens/s",
@@ -444,7 +448,9 @@ def run_ep_decode(args, ws, rank, local, dist):
         "config": {"workload": "config1_decode_T1_58layers_ep", "model": "DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)",
                    "global_batch": ws, "seq_len": 1, "layers": args.layers, "distinct_layers_resident": distinct,
                    "top_k": 8, "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": E,
-                   "exchange": "2 all-to-alls per layer (library NCCL communicator, grouped send/recv, in the step's CUDA graph)",
+                   "exchange": ("peer-memory mailboxes over NVLink (CUDA IPC, flag + bounded wait), in the step's CUDA graph"
+                                if args.exchange == "p2p" else
+                                "2 all-to-alls per layer (library NCCL communicator, grouped send/recv, in the step's CUDA graph)"),
                    "l2": "no flush: a step streams the selected experts of %d distinct layers (> 126 MB L2)" % distinct},
         "layer": {"ms_per_layer": round(ms_max / args.steps / args.layers * 1e3, 3), "unit_ms_per_layer": "us",
                   "expert_stage_us": {"gate_up": round(float(gu.mean()) * 1e3, 2), "down_combine": round(float(dn.mean()) * 1e3, 2)},
@@ -456,7 +462,8 @@ def run_ep_decode(args, ws, rank, local, dist):
         "e2e": {"value": round(n_e2e * ws / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": args.layers * 2 * HIDDEN * 4, "d2h_bytes_per_step": args.layers * HIDDEN * 4,
                 "path": "pinned host x/resid -> CUDA-graph step of EpMoeLayer.forward x58 -> pinned host h (stream events)"},
-        "gpu_launches": args.steps * args.layers * 9,      # router, pack (2), unpack, slots, gate/up, down, combine, EP combine
+        "gpu_launches": args.steps * args.layers * 11,     # router, plan, send/pack, wait, unpack, slots, gate/up, down,
+                                                           # combine, return, wait + EP combine
     }
     if cl:
         out["clocks"] = cl
@@ -763,6 +770,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample (profiling runs)")
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU-baseline sample")
     ap.add_argument("--parallelism", default="ep", choices=["ep", "replicas"], help="N > 1: expert parallel or replicas")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"], help="EP decode row exchange")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     ws, rank, local = dist_setup(args)

@@ -75,6 +75,30 @@ LK_API int lk_ep_all_to_all(LkEpComm* comm, const void* send, void* recv, const 
                             const int64_t* send_bytes, const int64_t* recv_off, const int64_t* recv_bytes,
                             int64_t block_bytes, lk_stream_t stream);
 
+/* the peer-memory exchange for fixed-capacity (decode) layers: every rank owns a mailbox in its HBM (rows
+ * received from each rank, partial sums returned by each owner, flags), exported by CUDA IPC and mapped by
+ * every peer; senders store over NVLink and publish a flag, receivers poll their local flags with a
+ * bounded wait (a timeout sets `err`).  Setup: lk_ep_mailbox_create on every rank (cap = the largest
+ * per-rank token count, <= 64) gives an IPC handle; gather all n_ranks handles (LK_EP_IPC_HANDLE_BYTES
+ * each, rank order) and pass them to lk_ep_mailbox_connect.  Per layer, on one stream:
+ *   lk_ep_p2p_dispatch (plan + rows into the owners' mailboxes; every token also to itself)
+ *   lk_ep_p2p_rows (wait for all ranks' rows; *rows = n_ranks*cap rows in fixed-capacity order)
+ *   lk_ep_experts(rows, n_ranks*cap, ..., own rows rank*cap .. +T, partial, shared)
+ *   lk_ep_p2p_return(partial)  (each block of cap partial sums to its home rank)
+ *   lk_ep_p2p_combine (wait for all returns; h = resid + shared + sum, moe = sum)
+ * All kernels are capturable; the flags carry an epoch that advances per layer on the device. */
+#define LK_EP_IPC_HANDLE_BYTES 64
+typedef struct LkEpMailbox LkEpMailbox;
+LK_API int lk_ep_mailbox_create(int n_ranks, int rank, int cap, int device, LkEpMailbox** out, void* ipc_handle_out);
+LK_API int lk_ep_mailbox_connect(LkEpMailbox* mb, const void* handles);
+LK_API void lk_ep_mailbox_destroy(LkEpMailbox* mb);
+LK_API int lk_ep_p2p_dispatch(LkEpMailbox* mb, const int* sel, const float* w, const float* x, int T, int keep,
+                              int* row_map, int* err, lk_stream_t stream);
+LK_API int lk_ep_p2p_rows(LkEpMailbox* mb, const void** rows, int* err, lk_stream_t stream);
+LK_API int lk_ep_p2p_return(LkEpMailbox* mb, const float* partial, lk_stream_t stream);
+LK_API int lk_ep_p2p_combine(LkEpMailbox* mb, const int* row_map, int T, const float* resid, const float* shared,
+                             float* h, float* moe, int* err, lk_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

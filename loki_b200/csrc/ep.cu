@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(const int* __restri
             if (v >= 0) *m = (cap > 0 && v >= cap) ? -1 : off[d] + v;
         }
     }
-    if (cap > 0) {                                             // unused rows of fixed-capacity blocks: no entries
+    if (cap > 0 && send) {                                     // unused rows of fixed-capacity blocks: no entries
         for (int d = 0; d < n_ranks; ++d) {
             for (int r = cnt[d] + (tid >> 4); r < cap; r += EP_PLAN_THREADS / 16) {
                 int* h = (int*)(send + (size_t)(off[d] + r) * LK_EP_ROW_BYTES);
@@ -149,6 +149,12 @@ __global__ void k_ep_combine(const float* __restrict__ ret, const int* __restric
     }
 }
 
+int ep_plan(const int* sel, int T, int keep, int n_ranks, int self_rank, int cap, int* counts, int* row_map, uint8_t* send,
+            int* err, cudaStream_t st) {
+    k_ep_plan<<<1, EP_PLAN_THREADS, 0, st>>>(sel, T, keep, n_ranks, self_rank, cap, counts, row_map, send, err);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
 void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, cudaStream_t st) {
     const int n = R * keep;
     k_ep_unpack<<<(n + 255) / 256, 256, 0, st>>>((const uint8_t*)recv, R, keep, sel, w);
@@ -168,7 +174,7 @@ int lk_ep_pack(const int* sel, const float* w, const float* x, int T, int keep, 
         return LK_ERR_ARG;
     if (((uintptr_t)send_rows & 15) || ((uintptr_t)x & 15)) return LK_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
-    k_ep_plan<<<1, EP_PLAN_THREADS, 0, st>>>(sel, T, keep, n_ranks, self_rank, cap, send_counts, row_map, (uint8_t*)send_rows, err);
+    if (ep_plan(sel, T, keep, n_ranks, self_rank, cap, send_counts, row_map, (uint8_t*)send_rows, err, st)) return LK_ERR_CUDA;
     if (T > 0) k_ep_copy<<<T, 256, 0, st>>>(sel, w, x, keep, n_ranks, row_map, (uint8_t*)send_rows);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }

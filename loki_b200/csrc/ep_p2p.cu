@@ -1,0 +1,216 @@
+// ep_p2p.cu -- the expert-parallel decode exchange over NVLink peer memory (include/loki_ep.h).
+//
+// For small per-layer messages (decode: a few 28 KB rows per rank pair) a collective library's launch and
+// protocol latency dominates.  Here every rank owns a mailbox in its HBM -- rows received from each
+// source rank, partial sums returned by each owner rank, and two flag arrays -- exported with CUDA IPC and
+// mapped by every peer.  Senders store straight into the destination's mailbox over NVLink, then publish
+// a flag (fence + release store, system scope); receivers poll their local flags (acquire loads, system
+// scope) with a bounded wait before reading.  Flags carry a per-rank epoch that the last wait of a layer
+// advances, so the same kernels replay correctly inside a captured CUDA graph.  No rank can run a layer
+// ahead: each layer ends with a wait for every owner's return.
+//
+// Layout of one mailbox (bytes): [flags: 2 x LK_EP_MAX_RANKS u32, epoch u32, pad to 256]
+//   [rows: n_ranks x cap x LK_EP_ROW_BYTES] [rets: n_ranks x cap x 7168 fp32]
+// Row (s, r) is source rank s's r-th row for this rank; ret (d, r) is owner d's partial sum for this rank's
+// r-th row sent to d -- the same indices as the fixed-capacity send buffer, so row_map indexes rets.
+#include <cstring>
+#include "../../include/loki_ep.h"
+#include "moe_internal.h"
+#include "moe_device.cuh"
+
+namespace lk {
+
+constexpr int P2P_HDR = 256;
+constexpr int P2P_THREADS = 256;
+
+struct P2PPeers {
+    uint8_t* mb[LK_EP_MAX_RANKS];     // every rank's mailbox base, as mapped in this process
+};
+
+__device__ __forceinline__ uint32_t* mb_flags(uint8_t* mb, int which) { return (uint32_t*)mb + which * LK_EP_MAX_RANKS; }
+__device__ __forceinline__ uint32_t* mb_epoch(uint8_t* mb) { return (uint32_t*)mb + 2 * LK_EP_MAX_RANKS; }
+__device__ __forceinline__ uint8_t* mb_rows(uint8_t* mb) { return mb + P2P_HDR; }
+__device__ __forceinline__ float* mb_rets(uint8_t* mb, int n_ranks, int cap) {
+    return (float*)(mb + P2P_HDR + (size_t)n_ranks * cap * LK_EP_ROW_BYTES);
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v; asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory"); return v;
+}
+
+// one CTA per destination rank d: this rank's rows for d (tokens with an entry on d, and every token to
+// itself) into d's mailbox block `self`, unused rows with empty headers, then the dispatch flag
+__global__ void __launch_bounds__(P2P_THREADS) k_p2p_send(const int* __restrict__ sel, const float* __restrict__ w,
+                                                           const float* __restrict__ x, int T, int keep, int n_ranks,
+                                                           int self, int cap, P2PPeers peers) {
+    const int d = blockIdx.x, tid = threadIdx.x;
+    const int epr = N_EXPERTS / n_ranks;
+    const uint32_t epoch = *mb_epoch(peers.mb[self]) + 1u;
+    uint8_t* block = mb_rows(peers.mb[d]) + (size_t)self * cap * LK_EP_ROW_BYTES;
+    int r = 0;
+    for (int t = 0; t < T; ++t) {
+        bool has = d == self;
+        for (int k = 0; k < keep && !has; ++k) { const int e = sel[t * keep + k]; has = e >= d * epr && e < (d + 1) * epr; }
+        if (!has) continue;                            // uniform across the CTA
+        uint8_t* row = block + (size_t)r * LK_EP_ROW_BYTES;
+        if (tid < 16) {
+            const int k = tid & 7;
+            const int e = k < keep ? sel[t * keep + k] : -1;
+            const bool mine = e >= d * epr && e < (d + 1) * epr;
+            if (tid < 8) ((int*)row)[tid] = mine ? e - d * epr : -1;
+            else ((float*)row)[tid] = mine ? w[t * keep + k] : 0.f;
+        }
+        const float4* src = (const float4*)(x + (size_t)t * HIDDEN);
+        float4* dst = (float4*)(row + LK_EP_ROW_HDR_BYTES);
+        for (int i = tid; i < HIDDEN / 4; i += P2P_THREADS) dst[i] = src[i];
+        ++r;
+    }
+    for (int rr = r; rr < cap; ++rr)
+        if (tid < 16) ((int*)(block + (size_t)rr * LK_EP_ROW_BYTES))[tid] = tid < 8 ? -1 : 0;
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        st_release_sys(mb_flags(peers.mb[d], 0) + self, epoch);
+    }
+}
+
+// one CTA per source rank s: this rank's partial sums for s's rows into s's mailbox block `self`
+__global__ void __launch_bounds__(P2P_THREADS) k_p2p_return(const float* __restrict__ partial, int n_ranks, int self,
+                                                             int cap, P2PPeers peers) {
+    const int s = blockIdx.x, tid = threadIdx.x;
+    const uint32_t epoch = *mb_epoch(peers.mb[self]) + 1u;
+    const float4* src = (const float4*)(partial + (size_t)s * cap * HIDDEN);
+    float4* dst = (float4*)(mb_rets(peers.mb[s], n_ranks, cap) + (size_t)self * cap * HIDDEN);
+    for (int i = tid; i < cap * HIDDEN / 4; i += P2P_THREADS) dst[i] = src[i];
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        st_release_sys(mb_flags(peers.mb[s], 1) + self, epoch);
+    }
+}
+
+// lane s waits (bounded) until flag `which` of source s reaches this layer's epoch; `advance`: then the
+// epoch moves on (the layer's last wait)
+__global__ void k_p2p_wait(uint8_t* mb, int which, int n_ranks, int advance, int* err) {
+    const int s = threadIdx.x;
+    const uint32_t want = *mb_epoch(mb) + 1u;
+    bool ok = true;
+    if (s < n_ranks) {
+        const uint32_t* f = mb_flags(mb, which) + s;
+        if ((int)(ld_acquire_sys(f) - want) < 0) {
+            const unsigned long long t0 = globaltimer_ns();
+            while ((int)(ld_acquire_sys(f) - want) < 0) {
+                if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) { ok = false; break; }
+            }
+        }
+        if (!ok && err) atomicCAS(err, 0, which ? DEV_ERR_TIMEOUT_EMPTY : DEV_ERR_TIMEOUT_FULL);
+    }
+    __syncwarp();
+    if (advance && s == 0) *mb_epoch(mb) = want;
+}
+
+}  // namespace lk
+
+using namespace lk;
+
+struct LkEpMailbox {
+    int n_ranks = 0, rank = 0, cap = 0, device = 0;
+    size_t bytes = 0;
+    uint8_t* local = nullptr;
+    P2PPeers peers{};
+    bool opened[LK_EP_MAX_RANKS] = {};
+};
+
+static size_t mailbox_bytes(int n_ranks, int cap) {
+    return (size_t)P2P_HDR + (size_t)n_ranks * cap * LK_EP_ROW_BYTES + (size_t)n_ranks * cap * HIDDEN * sizeof(float);
+}
+
+extern "C" {
+
+int lk_ep_mailbox_create(int n_ranks, int rank, int cap, int device, LkEpMailbox** out, void* ipc_handle_out) {
+    if (!out || !ipc_handle_out || n_ranks < 1 || n_ranks > LK_EP_MAX_RANKS || rank < 0 || rank >= n_ranks || cap < 1 ||
+        cap > 64)
+        return LK_ERR_ARG;
+    *out = nullptr;
+    if (cudaSetDevice(device) != cudaSuccess) return LK_ERR_CUDA;
+    LkEpMailbox* m = new LkEpMailbox();
+    m->n_ranks = n_ranks; m->rank = rank; m->cap = cap; m->device = device;
+    m->bytes = mailbox_bytes(n_ranks, cap);
+    if (cudaMalloc((void**)&m->local, m->bytes) != cudaSuccess || cudaMemset(m->local, 0, m->bytes) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) {
+        if (m->local) cudaFree(m->local);
+        delete m;
+        return LK_ERR_CUDA;
+    }
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, m->local) != cudaSuccess) { cudaFree(m->local); delete m; return LK_ERR_CUDA; }
+    memcpy(ipc_handle_out, &h, sizeof(h));
+    m->peers.mb[rank] = m->local;
+    *out = m;
+    return LK_OK;
+}
+
+int lk_ep_mailbox_connect(LkEpMailbox* m, const void* handles) {
+    if (!m || !handles) return LK_ERR_ARG;
+    if (cudaSetDevice(m->device) != cudaSuccess) return LK_ERR_CUDA;
+    for (int r = 0; r < m->n_ranks; ++r) {
+        if (r == m->rank || m->opened[r]) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t*)handles + (size_t)r * LK_EP_IPC_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return LK_ERR_CUDA;
+        m->peers.mb[r] = (uint8_t*)p;
+        m->opened[r] = true;
+    }
+    return LK_OK;
+}
+
+void lk_ep_mailbox_destroy(LkEpMailbox* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    cudaDeviceSynchronize();
+    for (int r = 0; r < m->n_ranks; ++r)
+        if (m->opened[r]) cudaIpcCloseMemHandle(m->peers.mb[r]);
+    if (m->local) cudaFree(m->local);
+    delete m;
+}
+
+int lk_ep_p2p_dispatch(LkEpMailbox* m, const int* sel, const float* w, const float* x, int T, int keep, int* row_map,
+                       int* err, lk_stream_t stream) {
+    if (!m || T < 1 || T > m->cap || keep < 1 || keep > MAX_TOPK || !sel || !w || !x || !row_map) return LK_ERR_ARG;
+    for (int r = 0; r < m->n_ranks; ++r) if (!m->peers.mb[r]) return LK_ERR_ARG;   // not connected
+    cudaStream_t st = (cudaStream_t)stream;
+    // row_map and counts as the fixed-capacity pack computes them (rows ordered by token per destination)
+    int* counts = (int*)(m->local + 2 * LK_EP_MAX_RANKS * 4 + 4);   // scratch in the mailbox header (8 ints)
+    int rc = ep_plan(sel, T, keep, m->n_ranks, m->rank, m->cap, counts, row_map, nullptr, err, st);
+    if (rc) return rc;
+    k_p2p_send<<<m->n_ranks, P2P_THREADS, 0, st>>>(sel, w, x, T, keep, m->n_ranks, m->rank, m->cap, m->peers);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+int lk_ep_p2p_rows(LkEpMailbox* m, const void** rows, int* err, lk_stream_t stream) {
+    if (!m || !rows) return LK_ERR_ARG;
+    k_p2p_wait<<<1, 32, 0, (cudaStream_t)stream>>>(m->local, 0, m->n_ranks, 0, err);
+    *rows = m->local + P2P_HDR;
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+int lk_ep_p2p_return(LkEpMailbox* m, const float* partial, lk_stream_t stream) {
+    if (!m || !partial) return LK_ERR_ARG;
+    k_p2p_return<<<m->n_ranks, P2P_THREADS, 0, (cudaStream_t)stream>>>(partial, m->n_ranks, m->rank, m->cap, m->peers);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+int lk_ep_p2p_combine(LkEpMailbox* m, const int* row_map, int T, const float* resid, const float* shared, float* h,
+                      float* moe, int* err, lk_stream_t stream) {
+    if (!m || T < 1 || T > m->cap || !row_map) return LK_ERR_ARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    k_p2p_wait<<<1, 32, 0, st>>>(m->local, 1, m->n_ranks, 1, err);
+    if (cudaGetLastError() != cudaSuccess) return LK_ERR_CUDA;
+    const float* rets = (const float*)(m->local + P2P_HDR + (size_t)m->n_ranks * m->cap * LK_EP_ROW_BYTES);
+    return lk_ep_combine(rets, row_map, T, m->n_ranks, resid, shared, h, moe, stream);
+}
+
+}  // extern "C"

@@ -109,6 +109,10 @@ void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expe
 
 // ---- expert-parallel row headers -> sel/w [R][keep]
 void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, cudaStream_t st);
+// ---- expert-parallel row plan only: counts [n_ranks], row_map [T][n_ranks] (and, with `send`, the
+//      headers of unused fixed-capacity rows)
+int ep_plan(const int* sel, int T, int keep, int n_ranks, int self_rank, int cap, int* counts, int* row_map, uint8_t* send,
+            int* err, cudaStream_t st);
 
 int num_sms(int device);
 

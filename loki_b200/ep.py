@@ -27,7 +27,7 @@ import torch.distributed as dist
 
 from . import native as N
 from .moe import MoeLayer, _ptr, _stream
-from .native import HIDDEN, N_EXPERTS, EP_ROW_BYTES, check, lib
+from .native import HIDDEN, N_EXPERTS, EP_ROW_BYTES, EP_IPC_HANDLE_BYTES, check, lib
 
 
 class TorchComm:
@@ -89,6 +89,32 @@ class NativeComm:
         return _Done()
 
 
+class P2PExchange:
+    """The peer-memory exchange of fixed-capacity (decode) layers: a mailbox per rank in HBM, exported with
+    CUDA IPC and mapped by every peer (include/loki_ep.h lk_ep_mailbox_* / lk_ep_p2p_*).  `cap`: the largest
+    per-rank token count it serves.  Collective: every rank of the default group constructs it."""
+
+    def __init__(self, device, cap):
+        self.rank, self.size = dist.get_rank(), dist.get_world_size()
+        self.cap = cap
+        dev = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        h = ctypes.create_string_buffer(EP_IPC_HANDLE_BYTES)
+        mb = ctypes.c_void_p()
+        check(lib().lk_ep_mailbox_create(self.size, self.rank, cap, dev.index or 0, ctypes.byref(mb), h))
+        self.mb = mb
+        handles = [None] * self.size
+        dist.all_gather_object(handles, h.raw)
+        check(lib().lk_ep_mailbox_connect(self.mb, b"".join(handles)))
+        dist.barrier()                                  # every mailbox mapped everywhere before any traffic
+
+    def close(self):
+        if self.mb:
+            torch.cuda.synchronize()
+            dist.barrier()                              # no peer still writes into our mailbox
+            lib().lk_ep_mailbox_destroy(self.mb)
+            self.mb = None
+
+
 class NativeEpOps:
     """The per-rank stages on one GPU: a 256-expert home context (router, shared expert) and an expert
     context over this rank's shard."""
@@ -133,13 +159,31 @@ class NativeEpOps:
         return hpart
 
     def experts(self, W, recv, R, keep, shared_row0=0, shared_rows=0):
-        """Routed partial sums of the R received rows, and the shared expert of rows [shared_row0, +shared_rows)."""
+        """Routed partial sums of the R received rows (a tensor or a device address), and the shared expert
+        of rows [shared_row0, +shared_rows)."""
         ret = torch.empty(max(R, 1), HIDDEN, device=self.device)
         shared = torch.empty(max(shared_rows, 1), HIDDEN, device=self.device)
         ws = W.struct()
-        self.expert._check(lib().lk_ep_experts(self.expert.ctx, ctypes.byref(ws), _ptr(recv), R, keep, shared_row0,
+        rows = recv if isinstance(recv, ctypes.c_void_p) else _ptr(recv)
+        self.expert._check(lib().lk_ep_experts(self.expert.ctx, ctypes.byref(ws), rows, R, keep, shared_row0,
                                                shared_rows, _ptr(ret), _ptr(shared), _stream()))
         return ret[:R], shared[:shared_rows]
+
+    def p2p_layer(self, p2p, W, x, resid, sel, w):
+        """One fixed-capacity layer over the peer-memory exchange (after routing): h, moe."""
+        T, keep, NR = x.shape[0], sel.shape[1], self.n_ranks
+        row_map = torch.empty(T, NR, dtype=torch.int32, device=self.device)
+        check(lib().lk_ep_p2p_dispatch(p2p.mb, _ptr(sel), _ptr(w), _ptr(x), T, keep, _ptr(row_map), _ptr(self.err),
+                                       _stream()))
+        rows = ctypes.c_void_p()
+        check(lib().lk_ep_p2p_rows(p2p.mb, ctypes.byref(rows), _ptr(self.err), _stream()))
+        partial, shared = self.experts(W, rows, NR * p2p.cap, keep, p2p.rank * p2p.cap, T)
+        check(lib().lk_ep_p2p_return(p2p.mb, _ptr(partial), _stream()))
+        h = torch.empty(T, HIDDEN, device=self.device)
+        moe = torch.empty(T, HIDDEN, device=self.device)
+        check(lib().lk_ep_p2p_combine(p2p.mb, _ptr(row_map), T, _ptr(resid), _ptr(shared), _ptr(h), _ptr(moe),
+                                      _ptr(self.err), _stream()))
+        return h, moe
 
     def combine(self, ret_home, row_map, hpart, shared=None):
         T = row_map.shape[0]
@@ -162,10 +206,12 @@ class EpMoeLayer:
     """One expert-parallel MoE layer call per rank.
 
     comm: TorchComm (or any object with its all_to_all); ops: NativeEpOps.  `fixed_cap_max`: calls with at
-    most this many local tokens use the fixed-capacity layout (every rank must then pass the same T)."""
+    most this many local tokens use the fixed-capacity layout (every rank must then pass the same T).
+    `p2p`: a P2PExchange -- fixed-capacity calls of at most p2p.cap tokens then use the peer-memory exchange
+    instead of the communicator."""
 
-    def __init__(self, comm, ops, fixed_cap_max=8):
-        self.comm, self.ops = comm, ops
+    def __init__(self, comm, ops, fixed_cap_max=8, p2p=None):
+        self.comm, self.ops, self.p2p = comm, ops, p2p
         self.n_ranks = comm.size
         self.fixed_cap_max = fixed_cap_max
         self.last_counts = None          # (rows sent per rank, rows received per rank) of the last compact call
@@ -178,6 +224,9 @@ class EpMoeLayer:
         me = comm.rank
         sel, w = ops.route(W, x, logits_override)
         keep = sel.shape[1]
+        if self.p2p is not None and T <= self.p2p.cap:
+            h, moe = ops.p2p_layer(self.p2p, W, x, resid, sel, w)
+            return h, moe, sel, w
         fixed = T <= self.fixed_cap_max
         cap = T if fixed else 0
         send, counts, row_map = ops.pack(sel, w, x, cap, me)

@@ -23,6 +23,7 @@ EP_ROW_HDR_BYTES = 64
 EP_ROW_BYTES = EP_ROW_HDR_BYTES + HIDDEN * 4      # 28 736
 EP_MAX_RANKS = 8
 EP_COMM_ID_BYTES = 128
+EP_IPC_HANDLE_BYTES = 64
 
 
 class LkMoeConfig(ctypes.Structure):
@@ -74,6 +75,13 @@ SIGNATURES = {
     "lk_ep_comm_create": (_I, [_P, _I, _I, _I, ctypes.POINTER(_P)]),
     "lk_ep_comm_destroy": (None, [_P]),
     "lk_ep_all_to_all": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _P]),
+    "lk_ep_mailbox_create": (_I, [_I, _I, _I, _I, ctypes.POINTER(_P), _P]),
+    "lk_ep_mailbox_connect": (_I, [_P, _P]),
+    "lk_ep_mailbox_destroy": (None, [_P]),
+    "lk_ep_p2p_dispatch": (_I, [_P, _P, _P, _P, _I, _I, _P, _P, _P]),
+    "lk_ep_p2p_rows": (_I, [_P, ctypes.POINTER(_P), _P, _P]),
+    "lk_ep_p2p_return": (_I, [_P, _P, _P]),
+    "lk_ep_p2p_combine": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P]),
     "fl_init": (_P, [_I, _I]),
     "fl_wide_init": (_I, [_P, _I, _I]),
     "fl_wide_moe": (None, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _I, _I, _I]),

@@ -77,7 +77,7 @@ def test_ep_emulated_ranks_one_gpu(native, oracle, n_ranks, T_loc, fixed_cap_max
 def _nccl_worker(rank, port, T_loc, fixed_cap_max, comm_kind, out_dir):
     import torch.distributed as dist
     from loki_b200.moe import LayerWeights
-    from loki_b200.ep import EpMoeLayer, NativeEpOps, TorchComm, NativeComm
+    from loki_b200.ep import EpMoeLayer, NativeEpOps, TorchComm, NativeComm, P2PExchange
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=2,
                             device_id=torch.device("cuda", rank))
@@ -86,12 +86,13 @@ def _nccl_worker(rank, port, T_loc, fixed_cap_max, comm_kind, out_dir):
         ops = NativeEpOps(rank, 2, T_loc)
         ops.set_gemm_threshold(1 << 20)
         ops.set_mma_threshold(1 << 20)
-        comm = NativeComm(rank) if comm_kind == "native" else TorchComm()
-        layer = EpMoeLayer(comm, ops, fixed_cap_max=fixed_cap_max)
+        comm = NativeComm(rank) if comm_kind in ("native", "p2p") else TorchComm()
+        p2p = P2PExchange(rank, T_loc) if comm_kind == "p2p" else None
+        layer = EpMoeLayer(comm, ops, fixed_cap_max=fixed_cap_max, p2p=p2p)
         x, r = (torch.from_numpy(a).cuda() for a in _inputs(T_loc, rank))
         h, moe, sel, w = layer.forward(W, x, r)
         torch.cuda.synchronize()
-        if comm_kind == "native" and T_loc <= fixed_cap_max:
+        if comm_kind in ("native", "p2p") and T_loc <= fixed_cap_max:
             # the same layer captured in a CUDA graph (exchanges included) and replayed: identical outputs
             s = torch.cuda.Stream()
             s.wait_stream(torch.cuda.current_stream())
@@ -102,7 +103,9 @@ def _nccl_worker(rank, port, T_loc, fixed_cap_max, comm_kind, out_dir):
             torch.cuda.synchronize()
             assert torch.equal(out_g[0], h) and torch.equal(out_g[1], moe)
             del g
-        if comm_kind == "native":
+        if p2p is not None:
+            p2p.close()
+        if comm_kind in ("native", "p2p"):
             comm.close()
         ops.device_error()
         np.savez(os.path.join(out_dir, "r%d.npz" % rank), h=h.cpu().numpy(), moe=moe.cpu().numpy(),
@@ -114,7 +117,7 @@ def _nccl_worker(rank, port, T_loc, fixed_cap_max, comm_kind, out_dir):
 
 
 @pytest.mark.parametrize("T_loc,fixed_cap_max,comm_kind", [(1, 8, "native"), (12, 4, "native"), (3, 8, "torch"),
-                                                             (12, 4, "torch")])
+                                                             (12, 4, "torch"), (1, 8, "p2p"), (5, 8, "p2p")])
 def test_ep_nccl_two_gpus(native, oracle, tmp_path, T_loc, fixed_cap_max, comm_kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
