@@ -141,9 +141,10 @@ __device__ void router_topk_token(const RouterParams& p, int t, int lane) {
             if (allowed[i] && (bi == 0x7fffffff || sc[i] > bv)) { bv = sc[i]; bi = lane + 32 * i; }
         warp_argmax(bv, bi);
         sel[k] = bi;
+        float mine = 0.0f;                          // the winner's probability, from its lane's registers
         #pragma unroll
-        for (int i = 0; i < PER; ++i) if (lane + 32 * i == bi) allowed[i] = false;
-        ps[k] = __ldcg(pr + bi);
+        for (int i = 0; i < PER; ++i) if (lane + 32 * i == bi) { allowed[i] = false; mine = pv[i]; }
+        ps[k] = __shfl_sync(0xffffffffu, mine, bi & 31);
     }
     float sum = 0.0f;
     for (int k = 0; k < p.topk; ++k) sum = __fadd_rn(sum, ps[k]);
