@@ -344,7 +344,7 @@ void launch_down1(const ExpertParams& p, int grid, cudaStream_t st);
 
 void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st) {
     switch (nt) {
-        case 1: gu_launch<1>(p, grid, st); break;          // (the per-row variant measured slower at one token)
+        case 1: launch_gate_up1(p, grid, st); break;
         case 2: gu_launch<2>(p, grid, st); break;
         case 4: gu_launch<4>(p, grid, st); break;
         default: gu_launch<8>(p, grid, st); break;

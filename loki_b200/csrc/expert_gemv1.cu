@@ -1,15 +1,14 @@
-// expert_gemv1.cu -- the single-token (decode, NT = 1) grouped IQ2_XXS matvecs, one warp per row.
+// expert_gemv1.cu -- the single-token (decode, NT = 1) grouped IQ2_XXS matvecs.
 //
-// Same contract as expert_gemv.cu's kernels for NT = 1 (slot tables in, hq/hd and y out), organised for one token: a warp computes whole row dot products -- lane l owns the K groups
-// l, l+32, ... and holds their q8 activations in registers -- so rows need no cross-warp reduction and
-// no named barriers.  A producer thread streams small row units into a deep shared-memory ring with
-// cp.async.bulk; each unit is consumed by one warp.
-//   gate/up unit = 2 h rows (2 gate rows + 2 up rows, two 3 696-byte copies); the warp writes
-//     h = silu(g)*u for its 2 rows into a per-tile shared buffer, and the last of the 16 units of a
-//     32-row tile (a shared-memory count) quantises the tile to q8 (hq, hd);
-//   down: copies of 32 rows (16 896 bytes), 4 per 128-row tile; warp w takes 8 rows of copy w/4: 8 row sums
-//     by one warp_reduce8, y = w * 0.125 * sum.
-// The IQ2 decode is moe_device.cuh's selector-table path (iq2_dot_sel), table at shared offset 0.
+// Same contract as expert_gemv.cu's kernels for NT = 1 (slot tables in, hq/hd and y out).  Both kernels
+// stream weight rows into a shared-memory ring with cp.async.bulk from one producer thread.
+//   gate/up (k_gate_up1): one 32-weight K group per consumer thread, 4 streams of 224 threads, decode
+//     with the signs applied to the activations (moe_device.cuh, iq2_dot_xs); SwiGLU and the q8 of h are
+//     fused in;
+//   down (k_down1): a warp computes whole row dot products -- lane l owns the K groups l and l + 32 --
+//     over copies of 32 rows (16 896 bytes), 4 per 128-row tile; warp w takes 8 rows of copy w/4: 8 row
+//     sums by one warp_reduce8, y = w * 0.125 * sum.  Decode: the selector table (iq2_dot1), which
+//     measured faster here than the sign-on-activation core.
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
@@ -68,159 +67,143 @@ __device__ __forceinline__ const uint8_t* slot_matrix1(const ExpertParams& p, in
          : which == 1 ? p.up + (size_t)e * p.up_stride : p.down + (size_t)e * p.down_stride;
 }
 
-// ------------------------------------------------------------------ gate / up, one token
-constexpr int G1_WARPS = 16;
-constexpr int G1_THREADS = (G1_WARPS + 1) * 32;
+// ------------------------------------------------------------------ gate / up, one token per slot
+// 4 consumer streams x 224 threads (one 32-weight K group each) + a producer warp.  A tile is 32 h rows
+// = 8 chunks of 8 rows (chunks 0-3 gate, 4-7 up), each chunk one 14 784-byte bulk copy into stage c.
+// Stream k takes chunk k (gate rows 8k..8k+7) and then chunk k + 4 (the same up rows).  Per chunk a
+// warp sums its 8 row partials with warp_reduce8.  At the end of the tile every consumer leaves one
+// value in a double-buffered shared array, and after one barrier warp 0 adds the 7 warps of each row
+// (fixed order), applies SwiGLU and quantises the tile's 32 h values to q8.
+// A CTA walks a contiguous range of (slot, row tile) pairs, so the activations are re-quantised only
+// when the slot's token changes.
+constexpr int G1_NS = 4;
+constexpr int G1_KG = HIDDEN / 32;                   // 224 consumers per stream
+constexpr int G1_SW = G1_KG / 32;                    // 7 warps per stream
+constexpr int G1_CONS = G1_NS * G1_KG;               // 896
+constexpr int G1_THREADS = G1_CONS + 32;             // + producer warp
 constexpr int G1_ROWB = (HIDDEN / QK) * BLK_IQ2;     // 1848
-constexpr int G1_UROWS = 2;                          // h rows per unit
-constexpr int G1_UBYTES = 2 * G1_UROWS * G1_ROWB;    // 7392: gate rows then up rows
-constexpr int G1_NST = 20;
-constexpr int G1_TILE = 32;                          // h rows per q8 tile
-constexpr int G1_UPT = G1_TILE / G1_UROWS;           // 16 units per tile
-constexpr int G1_TILES_PER_SLOT = MOE_INTER / G1_TILE;
-constexpr int G1_GPL = HIDDEN / 32 / 32;             // 7 groups per lane
-constexpr int G1_NBUF = 4;                           // tiles in flight per CTA (<= NST/UPT + 2)
+constexpr int G1_CROWS = 8;
+constexpr int G1_CBYTES = G1_CROWS * G1_ROWB;        // 14784
+constexpr int G1_TILE = 32;                          // h rows per tile
+constexpr int G1_CPT = 2 * G1_TILE / G1_CROWS;       // 8 chunks per tile; chunk c always uses stage c
+constexpr int G1_TILES_PER_SLOT = MOE_INTER / G1_TILE;   // 64
+static_assert(G1_CPT == 2 * G1_NS, "each stream takes one gate and one up chunk per tile");
 
 constexpr int G1_OFF_TAB = 0;
-constexpr int G1_OFF_RING = G1_OFF_TAB + SEL_TAB_BYTES;
-constexpr int G1_OFF_H = G1_OFF_RING + G1_NST * G1_UBYTES;
-constexpr int G1_OFF_CNT = G1_OFF_H + G1_NBUF * G1_TILE * 4;
-constexpr int G1_OFF_BAR = G1_OFF_CNT + G1_NBUF * 4;
-constexpr int G1_OFF_ABORT = G1_OFF_BAR + 2 * G1_NST * 8;
+constexpr int G1_OFF_RING = G1_OFF_TAB + XS_TAB_BYTES;
+constexpr int G1_OFF_RED = G1_OFF_RING + G1_CPT * G1_CBYTES;
+constexpr int G1_OFF_BAR = G1_OFF_RED + 2 * G1_NS * G1_SW * 32 * 4;
+constexpr int G1_OFF_ABORT = G1_OFF_BAR + 2 * G1_CPT * 8;
 constexpr int G1_SMEM = G1_OFF_ABORT + 16;
 
 __global__ void __launch_bounds__(G1_THREADS, 1) k_gate_up1(ExpertParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
+    const unsigned char* tab = smem + G1_OFF_TAB;
     uint8_t* ring = smem + G1_OFF_RING;
-    float* hbuf = (float*)(smem + G1_OFF_H);
-    int* hcnt = (int*)(smem + G1_OFF_CNT);
+    float* red = (float*)(smem + G1_OFF_RED);
     uint64_t* full = (uint64_t*)(smem + G1_OFF_BAR);
-    uint64_t* empty = full + G1_NST;
+    uint64_t* empty = full + G1_CPT;
     volatile int* abort_flag = (volatile int*)(smem + G1_OFF_ABORT);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nslots = *p.nslots;
     const int ntiles = nslots * G1_TILES_PER_SLOT;
-    if ((int)blockIdx.x >= ntiles) return;
-    init_sel_table((uint32_t*)(smem + G1_OFF_TAB), tid, G1_THREADS);
-    if (tid < G1_NBUF) hcnt[tid] = 0;
+    const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x);
+    const int t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+    if (t0 >= t1) return;
+
+    init_xs_table(smem + G1_OFF_TAB, tid, G1_THREADS);
     if (tid == 0) {
         *abort_flag = 0;
-        for (int s = 0; s < G1_NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int c = 0; c < G1_CPT; ++c) { mbar_init(&full[c], 1); mbar_init(&empty[c], G1_SW); }
         fence_mbar_init();
     }
     __syncthreads();
-    // unit sequence of this CTA: tiles blockIdx.x + k*gridDim.x, each as 16 units; unit j -> stage j % NST,
-    // consumed by warp j % G1_WARPS
-    if (warp == G1_WARPS) {                           // ---------------- producer
+
+    if (warp == G1_CONS / 32) {                       // ---------------- producer
         if (lane == 0) {
-            uint32_t j = 0;
-            for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-                const int s = tile % nslots, rt = tile / nslots;
+            uint32_t it = 0;                          // copies issued; copy it uses stage it % 8, phase it / 8
+            for (int tile = t0; tile < t1; ++tile) {
+                const int s = tile / G1_TILES_PER_SLOT, rt = tile % G1_TILES_PER_SLOT;
                 const int e = p.slot_expert[s];
                 const uint8_t* g = slot_matrix1(p, e, 0);
                 const uint8_t* u = slot_matrix1(p, e, 1);
-                for (int k = 0; k < G1_UPT; ++k, ++j) {
-                    const int st = j % G1_NST;
-                    if (*abort_flag || !mbar_wait(&empty[st], ((j / G1_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; goto drain; }
-                    const size_t roff = (size_t)(rt * G1_TILE + k * G1_UROWS) * G1_ROWB;
-                    mbar_arrive_expect_tx(&full[st], G1_UBYTES);
-                    bulk_g2s(ring + st * G1_UBYTES, g + roff, G1_UBYTES / 2, &full[st]);
-                    bulk_g2s(ring + st * G1_UBYTES + G1_UBYTES / 2, u + roff, G1_UBYTES / 2, &full[st]);
+                for (int c = 0; c < G1_CPT; ++c, ++it) {
+                    if (*abort_flag || !mbar_wait(&empty[c], ((it / G1_CPT) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; goto drain; }
+                    const uint8_t* src = (c < G1_NS ? g : u) + (size_t)(rt * G1_TILE + (c % G1_NS) * G1_CROWS) * G1_ROWB;
+                    mbar_arrive_expect_tx(&full[c], G1_CBYTES);
+                    bulk_g2s(ring + c * G1_CBYTES, src, G1_CBYTES, &full[c]);
                 }
             }
         drain:
-            {
-                const uint32_t first = j > G1_NST ? j - G1_NST : 0;
-                for (uint32_t i = first; i < j; ++i) mbar_wait(&full[i % G1_NST], (i / G1_NST) & 1, nullptr, 0);
+            {   // every issued copy must land before the CTA may exit
+                const uint32_t first = it > G1_CPT ? it - G1_CPT : 0;
+                for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % G1_CPT], (j / G1_CPT) & 1, nullptr, 0);
             }
         }
         return;
     }
 
-    const uint32_t tab_s = smem_u32(smem + G1_OFF_TAB);
-    const uint32_t ring_s = smem_u32(ring);
-    const uint32_t lane4 = (uint32_t)lane << 2;
-    const uint32_t goff0 = 2u + BLK_IQ2 * (lane >> 3) + 8u * (lane & 7);   // group `lane`; +264 per 32 groups
-    const uint32_t gal = goff0 & ~3u, gsh = (goff0 & 3u) * 8u;
-    const uint32_t boff0 = BLK_IQ2 * (lane >> 3);
-    uint32_t xr[G1_GPL][8]; float dx[G1_GPL]; int xtok = -2;
-    uint32_t j = 0; int tseq = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tseq) {
-        const int s = tile % nslots, rt = tile / nslots;
+    // ---------------------------------------------------------------- consumers
+    const int strm = tid / G1_KG, g = tid % G1_KG, sw = g >> 5;
+    const int goff = 2 + BLK_IQ2 * (g >> 3) + 8 * (g & 7);
+    const int boff = BLK_IQ2 * (g >> 3);
+    const uint32_t lane4 = (uint32_t)lane << 2, lane8 = (uint32_t)lane << 3;
+    uint32_t xr[8], nx[8];
+    float dx = 0.0f;
+    int xtok = -2;
+    bool aborted = false;
+    uint32_t ti = 0;
+    for (int tile = t0; tile < t1; ++tile, ++ti) {
+        const int s = tile / G1_TILES_PER_SLOT, rt = tile % G1_TILES_PER_SLOT;
         const int tok = p.slot_tok[s];
         if (tok != xtok) {
+            if (tok >= 0) dx = q8_group_global(p.x + (size_t)tok * p.ld_x, g, xr);
+            else { dx = 0.0f; for (int j = 0; j < 8; ++j) xr[j] = 0u; }
             #pragma unroll
-            for (int q = 0; q < G1_GPL; ++q) {
-                if (tok >= 0) dx[q] = q8_group_global(p.x + (size_t)tok * p.ld_x, lane + 32 * q, xr[q]);
-                else { dx[q] = 0.0f; for (int w = 0; w < 8; ++w) xr[q][w] = 0u; }
-            }
+            for (int j = 0; j < 8; ++j) nx[j] = neg_i8x4(xr[j]);
             xtok = tok;
         }
-        const int hb = tseq % G1_NBUF;
-        for (int k = warp; k < G1_UPT; k += G1_WARPS) {   // this warp's units of the tile
-            const uint32_t ju = j + (uint32_t)k;
-            const int st = ju % G1_NST;
-            if (!*abort_flag && !mbar_wait(&full[st], (ju / G1_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) *abort_flag = 1;
-            const uint32_t ub = ring_s + st * G1_UBYTES;
-            const uint32_t ubg = ub + gal, ubd = ub + boff0;
-            float v[4];                               // g(row0), g(row1), u(row0), u(row1)
+        float kept = 0.0f;
+        #pragma unroll
+        for (int bb = 0; bb < 2; ++bb) {
+            const int c = strm + G1_NS * bb;
+            if (!aborted && !mbar_wait(&full[c], ti & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { aborted = true; *abort_flag = 1; }
+            const uint8_t* base = ring + c * G1_CBYTES;
+            float v[8];
             #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                float a = 0.0f;
-                #pragma unroll
-                for (int q = 0; q < G1_GPL; ++q) {
-                    uint32_t aux0, aux1;
-                    lds_group(ubg + r * G1_ROWB + 264u * q, gsh, aux0, aux1);
-                    const float d = __half2float(__ushort_as_half(lds_u16(ubd + r * G1_ROWB + 264u * q)));
-                    const int isum = iq2_dot1(aux0, aux1, xr[q], tab_s, lane4);
-                    a = fmaf((float)(isum * ((int)((aux1 >> 27) & 0x1Eu) + 1)), d * dx[q], a);
-                }
-                v[r] = a;
+            for (int rr = 0; rr < G1_CROWS; ++rr) {
+                const uint8_t* row = base + rr * G1_ROWB;
+                uint32_t aux0, aux1;
+                load_group_smem(row, goff, aux0, aux1);
+                const float d = load_d_smem(row, boff);
+                const int acc = iq2_dot_xs(aux0, aux1, xr, nx, tab, lane4, lane8);
+                const int mult = (int)((aux1 >> 27) & 0x1Eu) + 1;          // 2*scale + 1
+                v[rr] = (float)(acc * mult) * (d * dx);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
-            // 4 values over the warp: halving over 16, 8, then butterflies 4, 2, 1 -> lane l holds v[(l >> 3) & 3]
+            if (lane == 0) mbar_arrive(&empty[c]);
+            const float r = warp_reduce8(v, lane);    // lane l: row l >> 2 of the chunk
+            if ((lane & 3) == bb) kept = r;
+        }
+        float* rb = red + (ti & 1) * (G1_NS * G1_SW * 32);
+        rb[(strm * G1_SW + sw) * 32 + lane] = kept;
+        if (named_bar_or(1, G1_CONS, aborted)) break;   // uniform: every consumer leaves here together
+        if (warp == 0) {                              // h row `lane` of the tile: stream lane/8, chunk row lane%8
+            const float* q = rb + (lane >> 3) * G1_SW * 32 + (lane & 7) * 4;
+            float ga = q[0], ua = q[1];
             #pragma unroll
-            for (int o = 16, h = 2; o >= 8; o >>= 1, h >>= 1) {
-                const bool up = (lane & o) != 0;
-                #pragma unroll
-                for (int i = 0; i < h; ++i) {
-                    const float send = up ? v[i] : v[i + h];
-                    const float keep = up ? v[i + h] : v[i];
-                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-                }
-            }
-            float r0 = v[0];
-            r0 += __shfl_xor_sync(0xffffffffu, r0, 4);
-            r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
-            r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
-            // lanes 0-7: g row0, 8-15: g row1, 16-23: u row0, 24-31: u row1
-            const float uo = __shfl_xor_sync(0xffffffffu, r0, 16);
-            if (lane == 0 || lane == 8) {
-                const int hr = k * G1_UROWS + (lane >> 3);
-                hbuf[hb * G1_TILE + hr] = lk_swiglu(r0 * 0.125f, uo * 0.125f);
-            }
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) { __threadfence_block(); last = atomicAdd(&hcnt[hb], 1) == G1_UPT - 1; }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {                               // all 32 h rows of the tile are in hbuf: q8 them
-                __threadfence_block();
-                const float hv = ((volatile float*)hbuf)[hb * G1_TILE + lane];
-                float amax = fabsf(hv);
-                #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-                const float d = amax / 127.0f, id = d > 0.0f ? 1.0f / d : 0.0f;
-                const int out = p.slot_out[s];
-                if (out >= 0) {
-                    p.hq[(size_t)out * MOE_INTER + rt * G1_TILE + lane] = (int8_t)(int)rintf(hv * id);
-                    if (lane == 0) p.hd[(size_t)out * (MOE_INTER / 32) + rt] = d;
-                }
-                if (lane == 0) hcnt[hb] = 0;
+            for (int w = 1; w < G1_SW; ++w) { ga += q[w * 32]; ua += q[w * 32 + 1]; }
+            const float hv = lk_swiglu(ga * 0.125f, ua * 0.125f);
+            float amax = fabsf(hv);
+            #pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float d = amax / 127.0f, id = d > 0.0f ? 1.0f / d : 0.0f;
+            const int out = p.slot_out[s];
+            if (out >= 0) {
+                p.hq[(size_t)out * MOE_INTER + rt * G1_TILE + lane] = (int8_t)(int)rintf(hv * id);
+                if (lane == 0) p.hd[(size_t)out * (MOE_INTER / 32) + rt] = d;
             }
         }
-        j += G1_UPT;
-        if (*abort_flag) break;
     }
 }
 

@@ -44,12 +44,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
                  : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
+// try_wait with a suspend-time hint: the warp sleeps until the phase completes or about `ns` pass,
+// instead of re-issuing the test (a spinning warp takes issue slots from the compute warps of its SMSP)
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(ns) : "memory");
+    return ok != 0;
+}
+constexpr uint32_t WAIT_SLEEP_NS = 20000;
 // wait for the phase of `parity` to complete; false (after recording `code`) once the deadline passes
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer_ns();
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, WAIT_SLEEP_NS)) return true;
         if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) { if (err) atomicCAS(err, 0, code); return false; }
     }
 }
@@ -66,6 +75,14 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
+}
+// named barrier that also ORs a predicate over the participating threads: every thread gets the same
+// answer, so decisions taken on it (an abort) are uniform
+__device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+                 : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(nthreads) : "memory");
+    return r != 0;
 }
 
 // ---- IQ2_XXS decode table in shared memory: 64 KB, lane-private, one 256-byte row per index i:
@@ -138,6 +155,67 @@ __device__ __forceinline__ void iq2_dot_sel(uint32_t aux0, uint32_t aux1, const 
             acc[t] = __dp4a((int)vhi, (int)x[t][2 * l + 1], acc[t]);
         }
     }
+}
+
+// ---- IQ2_XXS decode with the signs applied to the activations (one token per thread): 80 KB,
+// lane-private rows again.
+//   [0, 64 KB):      grid magnitudes: entry i at i*256 + lane*8 = the 8 magnitude bytes of grid entry i
+//   [64 KB, 80 KB):  sign selectors: entry s (7-bit sign index) at 64 KB + s*128 + lane*4; nibble j (bits
+//                    4j..4j+3) = j + 4*sign_j, nibble 4 + j (bits 16 + 4j) = j + 4*sign_{4+j}
+// A thread keeps its activations x (int8, 4 per word) and their negations nx.  Per 8 weights:
+// prmt(x, nx, selector) gives the signed activations, and dp4a multiplies them by the unsigned magnitudes.
+// Compared with the selector table: no OR of two lookups, and the sign index needs only mask (and shift)
+// at stride 128.
+constexpr int XS_TAB_BYTES = 80 * 1024;
+constexpr int XS_SGN_OFF = 64 * 1024;
+
+__device__ __forceinline__ uint32_t xs_sign_selector(uint32_t si) {
+    const uint32_t k = iq2_ksigns(si);
+    uint32_t s = 0;
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) s |= ((uint32_t)(j & 3) + 4u * ((k >> j) & 1u)) << ((j < 4 ? 0 : 16) + 4 * (j & 3));
+    return s;
+}
+__device__ __forceinline__ void init_xs_table(uint8_t* tab, int tid, int nthr) {
+    for (int i = tid; i < 256 * 4; i += nthr) {           // 4 lanes' copies (32 B) per store pair
+        const int e = i >> 2, l0 = (i & 3) * 8;
+        const uint64_t g = c_iq2_grid[e];
+        uint4* row = (uint4*)(tab + e * 256 + l0 * 8);
+        const uint4 q = make_uint4((uint32_t)g, (uint32_t)(g >> 32), (uint32_t)g, (uint32_t)(g >> 32));
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) row[k] = q;
+    }
+    for (int i = tid; i < 128 * 2; i += nthr) {
+        const int s = i >> 1, l0 = (i & 1) * 16;
+        const uint32_t v = xs_sign_selector((uint32_t)s);
+        uint4* row = (uint4*)(tab + XS_SGN_OFF + s * 128 + l0 * 4);
+        const uint4 q = make_uint4(v, v, v, v);
+        #pragma unroll
+        for (int k = 0; k < 4; ++k) row[k] = q;
+    }
+}
+// bytewise negation of 4 int8 values in [-127, 127] (q8 never holds -128)
+__device__ __forceinline__ uint32_t neg_i8x4(uint32_t v) {
+    uint32_t r = 0;
+    #pragma unroll
+    for (int j = 0; j < 4; ++j) r |= (uint32_t)(uint8_t)(-(int8_t)(v >> (8 * j))) << (8 * j);
+    return r;
+}
+// exact int32 dot of one IQ2_XXS group (aux0, aux1) with 32 q8 activations x (nx = their negations);
+// tab = the xs table, lane4 / lane8 = lane << 2 / lane << 3
+__device__ __forceinline__ int iq2_dot_xs(uint32_t aux0, uint32_t aux1, const uint32_t (&x)[8], const uint32_t (&nx)[8],
+                                          const unsigned char* tab, uint32_t lane4, uint32_t lane8) {
+    int acc = 0;
+    #pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const uint32_t ga = __byte_perm(aux0, lane8, 0x5504u | (uint32_t)(l << 4));   // idx << 8 | lane << 3
+        const uint2 g = *(const uint2*)(tab + ga);
+        const uint32_t sa = (l == 0 ? (aux1 << 7) : l == 1 ? aux1 : l == 2 ? (aux1 >> 7) : (aux1 >> 14)) & 0x3F80u;
+        const uint32_t s = *(const uint32_t*)(tab + XS_SGN_OFF + (sa | lane4));
+        acc = __dp4a((int)g.x, (int)__byte_perm(x[2 * l], nx[2 * l], s), acc);
+        acc = __dp4a((int)g.y, (int)__byte_perm(x[2 * l + 1], nx[2 * l + 1], s >> 16), acc);
+    }
+    return acc;
 }
 
 // the 8 bytes of IQ2 group `g` of a row staged in shared memory (row start 4-byte aligned): the group
