@@ -7,6 +7,8 @@ namespace lk {
 
 // ------------------------------------------------------------------ combine
 __global__ void k_combine(CombineParams p) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;       // float4 index over T x HIDDEN
     const int per = HIDDEN / 4;
     if (i >= p.T * per) return;
@@ -35,7 +37,7 @@ __global__ void k_combine(CombineParams p) {
 
 void launch_combine(const CombineParams& p, cudaStream_t st) {
     const int n = p.T * (HIDDEN / 4);
-    k_combine<<<(n + 255) / 256, 256, 0, st>>>(p);
+    launch_pdl(k_combine, dim3((n + 255) / 256), dim3(256), 0, st, p);
 }
 
 // ------------------------------------------------------------------ seeded weight generation

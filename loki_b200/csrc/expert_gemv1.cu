@@ -105,12 +105,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) k_gate_up1(ExpertParams p) {
     uint64_t* empty = full + G1_CPT;
     volatile int* abort_flag = (volatile int*)(smem + G1_OFF_ABORT);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nslots = *p.nslots;
-    const int ntiles = nslots * G1_TILES_PER_SLOT;
-    const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x);
-    const int t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
-    if (t0 >= t1) return;
-
+    // shared-memory setup overlaps the previous kernel; everything it produced is read after pdl_wait
     init_xs_table(smem + G1_OFF_TAB, tid, G1_THREADS);
     if (tid == 0) {
         *abort_flag = 0;
@@ -118,6 +113,13 @@ __global__ void __launch_bounds__(G1_THREADS, 1) k_gate_up1(ExpertParams p) {
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_trigger();
+    pdl_wait();
+    const int nslots = *p.nslots;
+    const int ntiles = nslots * G1_TILES_PER_SLOT;
+    const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x);
+    const int t1 = (int)((long long)(blockIdx.x + 1) * ntiles / gridDim.x);
+    if (t0 >= t1) return;
 
     if (warp == G1_CONS / 32) {                       // ---------------- producer
         if (lane == 0) {
@@ -232,9 +234,6 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
     uint64_t* empty = full + D1_NST;
     volatile int* abort_flag = (volatile int*)(smem + D1_OFF_ABORT);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nslots = *p.nslots;
-    const int ntiles = nslots * D1_TILES_PER_SLOT;
-    if ((int)blockIdx.x >= ntiles) return;
     init_sel_table((uint32_t*)(smem + D1_OFF_TAB), tid, D1_THREADS);
     if (tid == 0) {
         *abort_flag = 0;
@@ -242,6 +241,11 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_trigger();
+    pdl_wait();
+    const int nslots = *p.nslots;
+    const int ntiles = nslots * D1_TILES_PER_SLOT;
+    if ((int)blockIdx.x >= ntiles) return;
     if (warp == D1_WARPS) {                           // ---------------- producer
         if (lane == 0) {
             uint32_t j = 0;
@@ -326,12 +330,12 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
 void launch_gate_up1(const ExpertParams& p, int grid, cudaStream_t st) {
     static bool attr = false;
     if (!attr) { cudaFuncSetAttribute(k_gate_up1, cudaFuncAttributeMaxDynamicSharedMemorySize, G1_SMEM); attr = true; }
-    k_gate_up1<<<grid, G1_THREADS, G1_SMEM, st>>>(p);
+    launch_pdl(k_gate_up1, dim3(grid), dim3(G1_THREADS), G1_SMEM, st, p);
 }
 void launch_down1(const ExpertParams& p, int grid, cudaStream_t st) {
     static bool attr = false;
     if (!attr) { cudaFuncSetAttribute(k_down1, cudaFuncAttributeMaxDynamicSharedMemorySize, D1_SMEM); attr = true; }
-    k_down1<<<grid, D1_THREADS, D1_SMEM, st>>>(p);
+    launch_pdl(k_down1, dim3(grid), dim3(D1_THREADS), D1_SMEM, st, p);
 }
 
 }  // namespace lk

@@ -76,6 +76,11 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(nthreads) : "memory");
 }
+// programmatic dependent launch: let the next kernel in the stream be scheduled (its CTAs still wait in
+// pdl_wait for this grid to complete), and wait for the previous kernel's completion and memory
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // named barrier that also ORs a predicate over the participating threads: every thread gets the same
 // answer, so decisions taken on it (an abort) are uniform
 __device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool pred) {

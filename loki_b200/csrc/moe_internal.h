@@ -28,6 +28,22 @@ struct RouterParams {
 };
 void launch_router(const RouterParams& p, cudaStream_t st);
 
+// Programmatic dependent launch for the decode chain (router -> gate/up -> down -> combine -> next router):
+// the kernel may start while its predecessor still runs.  Each such kernel only sets up shared memory (and
+// reads never-written inputs such as weights) before griddepcontrol.wait, and triggers its own
+// dependents once its CTAs are running, so a dependent grid is only scheduled after every CTA of its
+// predecessor is resident (no SM starvation).
+template <typename P>
+inline cudaError_t launch_pdl(void (*kernel)(P), dim3 grid, dim3 block, size_t smem, cudaStream_t st, const P& params) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid; cfg.blockDim = block; cfg.dynamicSmemBytes = smem; cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
 // ---- dispatch: per-expert stable token lists and the work-slot table of the grouped matvecs
 struct SlotParams {
     const int* sel; const float* w; int T; int keep;   // [T][keep]; negative ids are absent entries (skipped)

@@ -44,6 +44,10 @@ __global__ void __launch_bounds__(256) k_router_logits(RouterParams p) {
             w[j] = __ldg((const float4*)((const float*)p.W + (size_t)e * HIDDEN) + c);
         }
     }
+    // the router weights are never written by a kernel: their loads are in flight before the wait for
+    // the previous kernel (which may still be producing x)
+    pdl_trigger();
+    pdl_wait();
     #pragma unroll
     for (int t = 0; t < NTT; ++t) {
         float a = 0.0f;
@@ -190,15 +194,10 @@ __device__ void router_topk_token(const RouterParams& p, int t, int lane) {
 // p.tile_count: ceil(T / 8) zeroed ints (the kernel leaves them zeroed again)
 void launch_router(const RouterParams& p, cudaStream_t st) {
     const int ne = p.n_experts;
-    if (p.T <= 1) {
-        k_router_logits<1><<<dim3(ne, 1), 256, 0, st>>>(p);
-    } else if (p.T <= 2) {
-        k_router_logits<2><<<dim3(ne, 1), 256, 0, st>>>(p);
-    } else if (p.T <= 4) {
-        k_router_logits<4><<<dim3(ne, 1), 256, 0, st>>>(p);
-    } else {
-        k_router_logits<8><<<dim3(ne, (p.T + 7) / 8), 256, 0, st>>>(p);
-    }
+    if (p.T <= 1) launch_pdl(k_router_logits<1>, dim3(ne, 1), dim3(256), 0, st, p);
+    else if (p.T <= 2) launch_pdl(k_router_logits<2>, dim3(ne, 1), dim3(256), 0, st, p);
+    else if (p.T <= 4) launch_pdl(k_router_logits<4>, dim3(ne, 1), dim3(256), 0, st, p);
+    else launch_pdl(k_router_logits<8>, dim3(ne, (p.T + 7) / 8), dim3(256), 0, st, p);
 }
 
 }  // namespace lk
