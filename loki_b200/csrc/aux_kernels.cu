@@ -13,12 +13,18 @@ __global__ void k_combine(CombineParams p) {
     const int per = HIDDEN / 4;
     if (i >= p.T * per) return;
     const int t = i / per, c = i % per;
-    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < p.keep; ++k) {
-        if (p.sel && p.sel[t * p.keep + k] < 0) continue;
-        const float4 v = ((const float4*)(p.y + ((size_t)t * p.keep + k) * HIDDEN))[c];
-        r.x += v.x; r.y += v.y; r.z += v.z; r.w += v.w;
+    // all loads first (independent), then the sums in entry order: the chain is one memory round trip
+    float4 v[MAX_TOPK];
+    bool use[MAX_TOPK];
+    #pragma unroll
+    for (int k = 0; k < MAX_TOPK; ++k) {
+        use[k] = k < p.keep && !(p.sel && p.sel[t * p.keep + k] < 0);
+        v[k] = k < p.keep ? ((const float4*)(p.y + ((size_t)t * p.keep + k) * HIDDEN))[c] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    #pragma unroll
+    for (int k = 0; k < MAX_TOPK; ++k)
+        if (use[k]) { r.x += v[k].x; r.y += v[k].y; r.z += v[k].z; r.w += v[k].w; }
     if (p.moe) ((float4*)(p.moe + (size_t)t * p.ld_out))[c] = r;
     if (!p.h) return;
     float4 h = p.resid ? ((const float4*)(p.resid + (size_t)t * p.ld_out))[c] : make_float4(0.f, 0.f, 0.f, 0.f);

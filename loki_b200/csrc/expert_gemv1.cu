@@ -6,7 +6,7 @@
 //     with the signs applied to the activations (moe_device.cuh, iq2_dot_xs); SwiGLU and the q8 of h are
 //     fused in;
 //   down (k_down1): a warp computes whole row dot products -- lane l owns the K groups l and l + 32 --
-//     over copies of 32 rows (16 896 bytes), 4 per 128-row tile; warp w takes 8 rows of copy w/4: 8 row
+//     over units of 32 rows (one 16 896-byte copy each), 4 warps per unit, each warp 8 rows: 8 row
 //     sums by one warp_reduce8, y = w * 0.125 * sum.  Decode: the selector table (iq2_dot1), which
 //     measured faster here than the sign-on-activation core.
 #include "moe_internal.h"
@@ -213,13 +213,12 @@ __global__ void __launch_bounds__(G1_THREADS, 1) k_gate_up1(ExpertParams p) {
 constexpr int D1_WARPS = 16;
 constexpr int D1_THREADS = (D1_WARPS + 1) * 32;
 constexpr int D1_ROWB = (MOE_INTER / QK) * BLK_IQ2;  // 528
-constexpr int D1_UROWS = 8;                          // rows per warp unit
-constexpr int D1_CROWS = 32;                         // rows per bulk copy (16 896 B: copies under ~8 KB
-constexpr int D1_CBYTES = D1_CROWS * D1_ROWB;        //   cannot stream HBM at full rate)
-constexpr int D1_TILE = 128;                         // rows per (slot, tile): 4 copies, 16 warp units
-constexpr int D1_CPT = D1_TILE / D1_CROWS;
-constexpr int D1_NST = 2 * D1_CPT;                   // two tiles: warp w always uses stages w/4 and w/4 + 4
-constexpr int D1_TILES_PER_SLOT = HIDDEN / D1_TILE;  // 56
+constexpr int D1_UROWS = 8;                          // rows per warp
+constexpr int D1_CROWS = 32;                         // rows per unit = one bulk copy (16 896 B: copies under
+constexpr int D1_CBYTES = D1_CROWS * D1_ROWB;        //   ~8 KB cannot stream HBM at full rate)
+constexpr int D1_GROUPS = D1_WARPS / (D1_CROWS / D1_UROWS);   // 4 groups of 4 warps, one unit each at a time
+constexpr int D1_NST = 2 * D1_GROUPS;                // group g always uses stages g and g + 4
+constexpr int D1_UNITS_PER_SLOT = HIDDEN / D1_CROWS; // 224
 
 constexpr int D1_OFF_TAB = 0;
 constexpr int D1_OFF_RING = D1_OFF_TAB + SEL_TAB_BYTES;
@@ -227,6 +226,8 @@ constexpr int D1_OFF_BAR = D1_OFF_RING + D1_NST * D1_CBYTES;
 constexpr int D1_OFF_ABORT = D1_OFF_BAR + 2 * D1_NST * 8;
 constexpr int D1_SMEM = D1_OFF_ABORT + 16;
 
+// A CTA takes a contiguous range of units (32 output rows of one slot): 9 slots x 224 units over 148 CTAs
+// is 13 or 14 units each.  Local unit j goes to stage j % 8 and to warp group j % 4.
 __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem + D1_OFF_RING;
@@ -244,25 +245,24 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
     pdl_trigger();
     pdl_wait();
     const int nslots = *p.nslots;
-    const int ntiles = nslots * D1_TILES_PER_SLOT;
-    if ((int)blockIdx.x >= ntiles) return;
+    const int nunits = nslots * D1_UNITS_PER_SLOT;
+    const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x);
+    const int nu = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x) - u0;
+    if (nu <= 0) return;
     if (warp == D1_WARPS) {                           // ---------------- producer
         if (lane == 0) {
-            uint32_t j = 0;
-            for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-                const int s = tile % nslots, rt = tile / nslots;
+            int j = 0;
+            for (; j < nu; ++j) {
+                const int u = u0 + j, s = u / D1_UNITS_PER_SLOT, cu = u % D1_UNITS_PER_SLOT;
+                const int st = j % D1_NST;
+                if (*abort_flag || !mbar_wait(&empty[st], ((j / D1_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
                 const uint8_t* dw = slot_matrix1(p, p.slot_expert[s], 2);
-                for (int k = 0; k < D1_CPT; ++k, ++j) {
-                    const int st = j % D1_NST;
-                    if (*abort_flag || !mbar_wait(&empty[st], ((j / D1_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; goto drain; }
-                    mbar_arrive_expect_tx(&full[st], D1_CBYTES);
-                    bulk_g2s(ring + st * D1_CBYTES, dw + (size_t)(rt * D1_TILE + k * D1_CROWS) * D1_ROWB, D1_CBYTES, &full[st]);
-                }
+                mbar_arrive_expect_tx(&full[st], D1_CBYTES);
+                bulk_g2s(ring + st * D1_CBYTES, dw + (size_t)cu * D1_CBYTES, D1_CBYTES, &full[st]);
             }
-        drain:
-            {
-                const uint32_t first = j > D1_NST ? j - D1_NST : 0;
-                for (uint32_t i = first; i < j; ++i) mbar_wait(&full[i % D1_NST], (i / D1_NST) & 1, nullptr, 0);
+            {   // every issued copy must land before the CTA may exit
+                const int first = j > D1_NST ? j - D1_NST : 0;
+                for (int i = first; i < j; ++i) mbar_wait(&full[i % D1_NST], (i / D1_NST) & 1, nullptr, 0);
             }
         }
         return;
@@ -274,55 +274,53 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
     const uint32_t goff0 = 2u + BLK_IQ2 * (lane >> 3) + 8u * (lane & 7);   // groups lane, lane + 32 (+264)
     const uint32_t gal = goff0 & ~3u, gsh = (goff0 & 3u) * 8u;
     const uint32_t boff0 = BLK_IQ2 * (lane >> 3);
-    uint32_t j = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const int s = tile % nslots, rt = tile / nslots;
-        const int out = p.slot_out[s];
-        const float wv = p.slot_w[s];
-        uint32_t xr[2][8]; float dx[2];
-        #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const int g = lane + 32 * q;
-            if (out >= 0) {
-                const uint4* src = (const uint4*)(p.hq + (size_t)out * MOE_INTER + g * 32);
-                const uint4 a = src[0], c = src[1];
-                xr[q][0] = a.x; xr[q][1] = a.y; xr[q][2] = a.z; xr[q][3] = a.w;
-                xr[q][4] = c.x; xr[q][5] = c.y; xr[q][6] = c.z; xr[q][7] = c.w;
-                dx[q] = p.hd[(size_t)out * (MOE_INTER / 32) + g];
-            } else {
-                #pragma unroll
-                for (int w = 0; w < 8; ++w) xr[q][w] = 0u;
-                dx[q] = 0.0f;
-            }
-        }
-        {
-            const int k = warp;                       // warp unit: rows 8k..8k+7 of the tile, copy k / 4
-            const uint32_t ju = j + (uint32_t)(k / (D1_CROWS / D1_UROWS));
-            const int st = ju % D1_NST;
-            if (!*abort_flag && !mbar_wait(&full[st], (ju / D1_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) *abort_flag = 1;
-            const uint32_t ub = ring_s + st * D1_CBYTES + (k % (D1_CROWS / D1_UROWS)) * D1_UROWS * D1_ROWB;
-            const uint32_t ubg = ub + gal, ubd = ub + boff0;
-            float v[8];
+    const int grp = warp / (D1_CROWS / D1_UROWS), sub = warp % (D1_CROWS / D1_UROWS);
+    uint32_t xr[2][8]; float dx[2] = {0.0f, 0.0f};
+    int xslot = -1, out = -1;
+    float wv = 0.0f;
+    for (int j = grp; j < nu; j += D1_GROUPS) {
+        const int u = u0 + j, s = u / D1_UNITS_PER_SLOT, cu = u % D1_UNITS_PER_SLOT;
+        if (s != xslot) {                             // this slot's h (q8) as the activations
+            xslot = s; out = p.slot_out[s]; wv = p.slot_w[s];
             #pragma unroll
-            for (int r = 0; r < D1_UROWS; ++r) {
-                float a = 0.0f;
-                #pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    uint32_t aux0, aux1;
-                    lds_group(ubg + r * D1_ROWB + 264u * q, gsh, aux0, aux1);
-                    const float d = __half2float(__ushort_as_half(lds_u16(ubd + r * D1_ROWB + 264u * q)));
-                    const int isum = iq2_dot1(aux0, aux1, xr[q], tab_s, lane4);
-                    a = fmaf((float)(isum * ((int)((aux1 >> 27) & 0x1Eu) + 1)), d * dx[q], a);
+            for (int q = 0; q < 2; ++q) {
+                const int g = lane + 32 * q;
+                if (out >= 0) {
+                    const uint4* src = (const uint4*)(p.hq + (size_t)out * MOE_INTER + g * 32);
+                    const uint4 a = src[0], c = src[1];
+                    xr[q][0] = a.x; xr[q][1] = a.y; xr[q][2] = a.z; xr[q][3] = a.w;
+                    xr[q][4] = c.x; xr[q][5] = c.y; xr[q][6] = c.z; xr[q][7] = c.w;
+                    dx[q] = p.hd[(size_t)out * (MOE_INTER / 32) + g];
+                } else {
+                    #pragma unroll
+                    for (int w = 0; w < 8; ++w) xr[q][w] = 0u;
+                    dx[q] = 0.0f;
                 }
-                v[r] = a;
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
-            const float sum = warp_reduce8(v, lane);   // lane l: row (l >> 2), 4 replicas
-            const int row0 = rt * D1_TILE + k * D1_UROWS;
-            if ((lane & 3) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 2)] = wv * (sum * 0.125f);
         }
-        j += D1_CPT;
+        const int st = j % D1_NST;
+        if (!mbar_wait(&full[st], (j / D1_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
+        const uint32_t ub = ring_s + st * D1_CBYTES + sub * D1_UROWS * D1_ROWB;
+        const uint32_t ubg = ub + gal, ubd = ub + boff0;
+        float v[8];
+        #pragma unroll
+        for (int r = 0; r < D1_UROWS; ++r) {
+            float a = 0.0f;
+            #pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                uint32_t aux0, aux1;
+                lds_group(ubg + r * D1_ROWB + 264u * q, gsh, aux0, aux1);
+                const float d = __half2float(__ushort_as_half(lds_u16(ubd + r * D1_ROWB + 264u * q)));
+                const int isum = iq2_dot1(aux0, aux1, xr[q], tab_s, lane4);
+                a = fmaf((float)(isum * ((int)((aux1 >> 27) & 0x1Eu) + 1)), d * dx[q], a);
+            }
+            v[r] = a;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        const float sum = warp_reduce8(v, lane);   // lane l: row (l >> 2), 4 replicas
+        const int row0 = cu * D1_CROWS + sub * D1_UROWS;
+        if ((lane & 3) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 2)] = wv * (sum * 0.125f);
         if (*abort_flag) break;
     }
 }
