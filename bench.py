@@ -38,6 +38,10 @@ MAT = INTER * (HIDDEN // 256) * 66                       # 3 784 704 bytes per e
 ROUTER_BYTES = NE * HIDDEN * 4
 
 
+# DeepSeek-R1 routing (inherited by configs 1-4): 8 groups of 32 experts, top 4 groups
+N_GROUP, TOPK_GROUP = 8, 4
+
+
 def measured_peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -174,7 +178,7 @@ def cpu_decode_sample(n_layers, keep=8, seed=SEED):
         r = rng.standard_normal((1, HIDDEN)).astype(np.float32)
         W = (rng.standard_normal((NE, HIDDEN)) * 0.02).astype(np.float32)
         bias = (rng.standard_normal(NE) * 0.01).astype(np.float32)
-        cfg = O.route_cfg(8, keep)
+        cfg = O.route_cfg(8, keep, 1, N_GROUP, TOPK_GROUP)
         _, sel, w = O.router(x, W, bias, cfg)
         used = sorted(set(int(e) for e in sel[0]))
         remap = {e: i for i, e in enumerate(used)}
@@ -218,7 +222,7 @@ def run_decode(args, ws, rank, local, dist):
     rs = torch.randn(args.layers, 1, HIDDEN, device=dev, generator=g)
     hs = torch.empty(args.layers, 1, HIDDEN, device=dev)
     mos = torch.empty(args.layers, 1, HIDDEN, device=dev)
-    ctx = M.MoeLayer(local, keep=args.keep, max_tokens=1)
+    ctx = M.MoeLayer(local, keep=args.keep, max_tokens=1, n_group=N_GROUP, topk_group=TOPK_GROUP)
     structs = [l.struct() for l in layers]
     L = N.lib()
     stream = torch.cuda.Stream(dev)
@@ -295,7 +299,7 @@ def run_decode(args, ws, rank, local, dist):
         "data": "synthetic: seeded IQ2_XXS experts (BASELINE config 0 generator), router W N(0,0.02), bias N(0,0.01), x/resid N(0,1) fp32",
         "config": {"workload": "config1_decode_T1_58layers", "model": "DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)",
                    "global_batch": ws, "seq_len": 1, "layers": args.layers, "distinct_layers_resident": distinct,
-                   "top_k": 8, "keep": args.keep, "parallelism": "replicas" if ws > 1 else "single",
+                   "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP, "keep": args.keep, "parallelism": "replicas" if ws > 1 else "single",
                    "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (args.layers * layer_bytes / 1e9)},
         "layer": {"ms_per_layer": round(ms_max / args.steps / args.layers * 1e3, 3), "unit_ms_per_layer": "us",
                   "bytes_per_layer": layer_bytes,
@@ -338,7 +342,7 @@ def _ep_setup(args, ws, rank, local, dist, max_local_tokens, layers_wanted, p2p_
     distinct = int(_min_over_ranks(dist, max(1, min(layers_wanted, int((free - (10 << 30)) // per_layer)))))
     shards = [M.LayerWeights(dev, SEED, L, n_experts=E, expert0=rank * E) for L in range(distinct)]
     comm = NativeComm(local)
-    ops = NativeEpOps(local, ws, max_local_tokens, keep=args.keep)
+    ops = NativeEpOps(local, ws, max_local_tokens, keep=args.keep, n_group=N_GROUP, topk_group=TOPK_GROUP)
     p2p = P2PExchange(local, p2p_cap) if p2p_cap else None
     torch.cuda.synchronize(dev)
     return dev, shards, distinct, comm, ops, EpMoeLayer(comm, ops, p2p=p2p)
@@ -450,7 +454,7 @@ def run_ep_decode(args, ws, rank, local, dist):
         "data": "synthetic: seeded IQ2_XXS experts (BASELINE config 0 generator), router W N(0,0.02), bias N(0,0.01), x/resid N(0,1) fp32",
         "config": {"workload": "config1_decode_T1_58layers_ep", "model": "DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)",
                    "global_batch": ws, "seq_len": 1, "layers": args.layers, "distinct_layers_resident": distinct,
-                   "top_k": 8, "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": E,
+                   "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP, "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": E,
                    "exchange": ("peer-memory mailboxes over NVLink (CUDA IPC, flag + bounded wait), in the step's CUDA graph"
                                 if args.exchange == "p2p" else
                                 "2 all-to-alls per layer (library NCCL communicator, grouped send/recv, in the step's CUDA graph)"),
@@ -521,7 +525,7 @@ def run_ep_prefill(args, ws, rank, local, dist):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)",
         "data": "synthetic: seeded IQ2_XXS experts, router W N(0,0.02), bias N(0,0.01), bf16 N(0,1) hidden states",
-        "config": {"workload": "config3_ep_batch_T%d" % T, "global_batch": T, "seq_len": T, "layers": 1, "top_k": 8,
+        "config": {"workload": "config3_ep_batch_T%d" % T, "global_batch": T, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,
                    "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": NE // ws, "rows_sent": sent,
                    "rows_received": got, "l2": "no flush: each rank streams its %.2f GB shard" % ((3 * NE // ws + 3) * MAT / 1e9)},
         "layer": {"flops": flops, "achieved_tflops": round(flops / (ms_max / args.steps / 1e3) / 1e12, 1),
@@ -545,7 +549,7 @@ def run_imbalance(args, ws, rank, local, dist):
     from loki_b200.ep import EpMoeLayer, NativeEpOps, NativeComm
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    lam = S.calibrate_zipf_lambda()
+    lam = S.calibrate_zipf_lambda(n_group=N_GROUP, topk_group=TOPK_GROUP)
     bias = torch.from_numpy(S.zipf_bias(lam)).to(dev)
     E = NE // ws
     nl = 4
@@ -559,11 +563,11 @@ def run_imbalance(args, ws, rank, local, dist):
         xs = [torch.randn(T, HIDDEN, device=dev, generator=g) for _ in range(nl)]
         rs = [torch.randn(T, HIDDEN, device=dev, generator=g) for _ in range(nl)]
         if ws > 1:
-            ops = NativeEpOps(local, ws, T, keep=2)
+            ops = NativeEpOps(local, ws, T, keep=2, n_group=N_GROUP, topk_group=TOPK_GROUP)
             layer = EpMoeLayer(comm, ops)
             fwd = lambda i: layer.forward(layers[i % nl], xs[i % nl], rs[i % nl])
         else:
-            ctx = M.MoeLayer(local, keep=2, max_tokens=T)
+            ctx = M.MoeLayer(local, keep=2, max_tokens=T, n_group=N_GROUP, topk_group=TOPK_GROUP)
             fwd = lambda i: ctx.forward(layers[i % nl], xs[i % nl], rs[i % nl])
         for i in range(args.warmup):
             fwd(i)
@@ -597,7 +601,7 @@ def run_imbalance(args, ws, rank, local, dist):
         "value": sweep["512"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": sweep["512"]["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "iq2_xxs x q8 (dp4a) / fp16 mma.sync / fp16 tcgen05", "data": "synthetic: seeded IQ2_XXS experts, x N(0,1) fp32, Zipf router bias",
-        "config": {"workload": "config4_imbalance", "keep": 2, "top_k": 8, "zipf_s": 1.2, "lambda": round(lam, 5),
+        "config": {"workload": "config4_imbalance", "keep": 2, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP, "zipf_s": 1.2, "lambda": round(lam, 5),
                    "parallelism": "ep%d" % ws if ws > 1 else "single", "l2": "flushed (256 MB write) between steps"},
         "sweep": sweep,
     }
@@ -660,7 +664,7 @@ def run_prefill(args, ws, rank, local, dist):
     logits = torch.rand(T, NE, device=dev, generator=g) * 2 - 1
     h = torch.empty(T, HIDDEN, device=dev)
     mo = torch.empty(T, HIDDEN, device=dev)
-    ctx = M.MoeLayer(local, keep=args.keep, max_tokens=T)
+    ctx = M.MoeLayer(local, keep=args.keep, max_tokens=T, n_group=N_GROUP, topk_group=TOPK_GROUP)
     st = W.struct()
     L = N.lib()
     stream = torch.cuda.Stream(dev)
@@ -719,7 +723,7 @@ def run_prefill(args, ws, rank, local, dist):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)",
         "data": "synthetic: seeded IQ2_XXS experts, uniform-random router logits U(-1,1), bf16 N(0,1) hidden states",
-        "config": {"workload": "config2_prefill_T%d" % T, "global_batch": T * ws, "seq_len": T, "layers": 1, "top_k": 8,
+        "config": {"workload": "config2_prefill_T%d" % T, "global_batch": T * ws, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,
                    "keep": args.keep, "distinct_experts": distinct, "parallelism": "replicas" if ws > 1 else "single",
                    "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (gemm_bytes / 1e9)},
         "layer": {"bytes": layer_bytes, "flops": flops, "achieved_gbs": round(layer_bytes / (ms_max / args.steps / 1e3) / 1e9, 1),
@@ -754,7 +758,7 @@ def reference_arm(args, ws, rank):
             "ms_per_step": round(t_layer * args.layers * 1e3, 2), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "iq2_xxs x q8 (int32 dot, fp64 accumulate)", "data": "synthetic",
             "config": {"workload": "config1_decode_T1_58layers", "global_batch": 1, "seq_len": 1, "layers": args.layers,
-                       "keep": args.keep, "parallelism": "cpu"},
+                       "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP, "keep": args.keep, "parallelism": "cpu"},
             "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 

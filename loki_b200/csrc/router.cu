@@ -21,6 +21,13 @@
 namespace lk {
 
 __device__ void router_topk_token(const RouterParams& p, int t, int lane);
+__device__ void router_topk_cta(const RouterParams& p, int t);
+
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* a, int v) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
+    return old;
+}
 
 // one CTA = one expert x a tile of NTT tokens; 256 threads, each owns float4 chunks c = tid + 256 j
 template <int NTT>
@@ -76,18 +83,16 @@ __global__ void __launch_bounds__(256) k_router_logits(RouterParams p) {
         const float v = p.logits_override ? p.logits_override[o] : lg;
         p.probs[o] = lk_sigmoid(v);
     }
-    // the last CTA of this token tile runs the top-k for it (probabilities of all experts are visible:
-    // every CTA fences its writes before counting itself in)
+    // the last CTA of this token tile runs the top-k for it.  The count is an acquire-release atomic:
+    // each CTA releases its probabilities (ordered before it by the barrier), and the last one acquires
+    // everyone's before its barrier hands them to its other threads.
     if (!p.tile_count) return;
     __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        last = atomicAdd(&p.tile_count[blockIdx.y], 1) == (int)gridDim.x - 1;
-    }
+    if (tid == 0) last = atom_add_acq_rel_gpu(&p.tile_count[blockIdx.y], 1) == (int)gridDim.x - 1;
     __syncthreads();
     if (!last) return;
-    __threadfence();
-    if (warp < nt) router_topk_token(p, t0 + warp, lane);
+    if (nt == 1) router_topk_cta(p, t0);          // one token: all 8 warps
+    else if (warp < nt) router_topk_token(p, t0 + warp, lane);
     __syncthreads();
     if (tid == 0) p.tile_count[blockIdx.y] = 0;       // ready for the next call
 }
@@ -101,6 +106,8 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
         if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
     }
 }
+
+__device__ void router_finish(const RouterParams& p, int t, int lane, const int (&sel)[MAX_TOPK], const float (&ps)[MAX_TOPK]);
 
 __device__ void router_topk_token(const RouterParams& p, int t, int lane) {
     const float* pr = p.probs + (size_t)t * p.n_experts;   // written by other CTAs: read past L1
@@ -150,6 +157,12 @@ __device__ void router_topk_token(const RouterParams& p, int t, int lane) {
         for (int i = 0; i < PER; ++i) if (lane + 32 * i == bi) { allowed[i] = false; mine = pv[i]; }
         ps[k] = __shfl_sync(0xffffffffu, mine, bi & 31);
     }
+    router_finish(p, t, lane, sel, ps);
+}
+
+// weights of the selected experts (normalised, scaled), the engine's keep pass, and the outputs;
+// sel / ps: the topk selected experts and their probabilities in selection order (all lanes alike)
+__device__ void router_finish(const RouterParams& p, int t, int lane, const int (&sel)[MAX_TOPK], const float (&ps)[MAX_TOPK]) {
     float sum = 0.0f;
     for (int k = 0; k < p.topk; ++k) sum = __fadd_rn(sum, ps[k]);
     sum = fmaxf(sum, 6.103515625e-5f);
@@ -188,6 +201,68 @@ __device__ void router_topk_token(const RouterParams& p, int t, int lane) {
             p.slot_expert[keep] = SHARED_SLOT; p.slot_tok[keep] = 0; p.slot_out[keep] = keep; p.slot_w[keep] = 1.0f;
         }
         *p.nslots = keep + (p.with_shared ? 1 : 0);
+    }
+}
+
+// One token's top-k with the whole CTA (256 threads = 256 experts, group g = warp g).  Each warp sorts its
+// 32 (score, id) pairs by a bitonic network over shuffles (descending score, ties to the lower id): a
+// group's score is then lanes 0 + 1, and its best topk are lanes 0..topk-1.  The allowed groups' best
+// topk are the candidates; each candidate's rank among them is its position in the selection.  The
+// result (order included) is that of topk rounds of argmax over the allowed experts.
+__device__ void router_topk_cta(const RouterParams& p, int t) {
+    __shared__ float s_p[N_EXPERTS];
+    __shared__ float s_gs[8];
+    __shared__ float s_cv[8 * MAX_TOPK];
+    __shared__ int s_ci[8 * MAX_TOPK];
+    __shared__ int s_sel[MAX_TOPK];
+    __shared__ float s_ps[MAX_TOPK];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float pv = __ldcg(p.probs + (size_t)t * p.n_experts + tid);
+    s_p[tid] = pv;
+    float v = __fadd_rn(pv, p.bias[tid]);
+    int i = tid;
+    #pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+        #pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v, j);
+            const int oi = __shfl_xor_sync(0xffffffffu, i, j);
+            const bool mine_better = v > ov || (v == ov && i < oi);
+            const bool keep_mine = (((lane & j) == 0) == ((lane & k) == 0)) ? mine_better : !mine_better;
+            if (!keep_mine) { v = ov; i = oi; }
+        }
+    }
+    const float second = __shfl_sync(0xffffffffu, v, 1);
+    if (lane == 0) s_gs[warp] = __fadd_rn(v, second);
+    __syncthreads();
+    unsigned allowed = 0xFFu;
+    if (p.n_group > 1) {                              // top topk_group groups, ties -> lower group
+        allowed = 0u;
+        for (int r = 0; r < p.topk_group; ++r) {
+            int bg = -1; float bv = 0.0f;
+            #pragma unroll
+            for (int g = 0; g < 8; ++g) if (!((allowed >> g) & 1u) && (bg < 0 || s_gs[g] > bv)) { bg = g; bv = s_gs[g]; }
+            allowed |= 1u << bg;
+        }
+    }
+    const int nc = __popc(allowed) * p.topk;
+    if (((allowed >> warp) & 1u) && lane < p.topk) {
+        const int pos = __popc(allowed & ((1u << warp) - 1u)) * p.topk + lane;
+        s_cv[pos] = v; s_ci[pos] = i;
+    }
+    __syncthreads();
+    if (tid < nc) {
+        const float cv = s_cv[tid]; const int ci = s_ci[tid];
+        int rank = 0;
+        for (int c = 0; c < nc; ++c) { const float ov = s_cv[c]; const int oi = s_ci[c]; rank += (ov > cv || (ov == cv && oi < ci)) ? 1 : 0; }
+        if (rank < p.topk) { s_sel[rank] = ci; s_ps[rank] = s_p[ci]; }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int sel[MAX_TOPK]; float ps[MAX_TOPK];
+        #pragma unroll
+        for (int k = 0; k < MAX_TOPK; ++k) { sel[k] = k < p.topk ? s_sel[k] : 0; ps[k] = k < p.topk ? s_ps[k] : 0.0f; }
+        router_finish(p, t, lane, sel, ps);
     }
 }
 

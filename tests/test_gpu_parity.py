@@ -92,6 +92,25 @@ def test_router_logits_override(native, moe, oracle):
     np.testing.assert_array_equal(w.cpu().numpy(), ow)
 
 
+@pytest.mark.parametrize("T", [1, 3])
+@pytest.mark.parametrize("grouped", [False, True])
+def test_router_ties(native, moe, oracle, T, grouped):
+    """Logits on a 5-value grid and a zero bias: many experts (and groups) score exactly alike, so the
+    order of the selection rests on the lower-id tie rule (one-token CTA path and per-warp path)."""
+    rng = np.random.default_rng(11 + T)
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    W = (rng.standard_normal((256, HIDDEN)) * 0.02).astype(np.float32)
+    bias = np.zeros(256, np.float32)
+    logits = rng.integers(-2, 3, (T, 256)).astype(np.float32) * 0.5
+    ng, tg = (8, 4) if grouped else (1, 1)
+    layer = moe.MoeLayer(0, n_group=ng, topk_group=tg, max_tokens=T)
+    Wd, bd, xd, ld = _dev(W), _dev(bias), _dev(x), _dev(logits)
+    probs, sel, w = layer.route(router_only_weights(native, Wd, bd), xd, logits_override=ld)
+    op, osel, ow = oracle.router(None, None, bias, oracle.route_cfg(8, 8, 1, ng, tg), logits=logits)
+    np.testing.assert_array_equal(sel.cpu().numpy(), osel)
+    np.testing.assert_array_equal(w.cpu().numpy(), ow)
+
+
 # ---------------------------------------------------------------- dispatch
 def zipf_sel(rng, T, keep, s=1.2):
     p = 1.0 / np.arange(1, 257) ** s
