@@ -107,7 +107,8 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
     }
 }
 
-__device__ void router_finish(const RouterParams& p, int t, int lane, const int (&sel)[MAX_TOPK], const float (&ps)[MAX_TOPK]);
+__device__ __forceinline__ void router_finish(const RouterParams& p, int t, int lane, const int (&sel)[MAX_TOPK],
+                                              const float (&ps)[MAX_TOPK]);
 
 __device__ void router_topk_token(const RouterParams& p, int t, int lane) {
     const float* pr = p.probs + (size_t)t * p.n_experts;   // written by other CTAs: read past L1
@@ -145,7 +146,10 @@ __device__ void router_topk_token(const RouterParams& p, int t, int lane) {
         for (int i = 0; i < PER; ++i) allowed[i] = keepg[i];
     }
     int sel[MAX_TOPK]; float ps[MAX_TOPK];
-    for (int k = 0; k < p.topk; ++k) {
+    #pragma unroll
+    for (int k = 0; k < MAX_TOPK; ++k) {
+        sel[k] = 0; ps[k] = 0.0f;
+        if (k >= p.topk) continue;
         float bv = -INFINITY; int bi = 0x7fffffff;
         #pragma unroll
         for (int i = 0; i < PER; ++i)
@@ -162,33 +166,51 @@ __device__ void router_topk_token(const RouterParams& p, int t, int lane) {
 
 // weights of the selected experts (normalised, scaled), the engine's keep pass, and the outputs;
 // sel / ps: the topk selected experts and their probabilities in selection order (all lanes alike)
-__device__ void router_finish(const RouterParams& p, int t, int lane, const int (&sel)[MAX_TOPK], const float (&ps)[MAX_TOPK]) {
+__device__ __forceinline__ void router_finish(const RouterParams& p, int t, int lane, const int (&sel)[MAX_TOPK],
+                                              const float (&ps)[MAX_TOPK]) {
+    // every loop runs over the constant MAX_TOPK with predicates, so the arrays stay in registers
     float sum = 0.0f;
-    for (int k = 0; k < p.topk; ++k) sum = __fadd_rn(sum, ps[k]);
+    #pragma unroll
+    for (int k = 0; k < MAX_TOPK; ++k) if (k < p.topk) sum = __fadd_rn(sum, ps[k]);
     sum = fmaxf(sum, 6.103515625e-5f);
+    float pk = 0.0f;                                  // lane k divides entry k's probability, then all gather
+    #pragma unroll
+    for (int k = 0; k < MAX_TOPK; ++k) if (k == lane) pk = ps[k];
+    const float mine = __fmul_rn(__fdiv_rn(pk, sum), p.scale);
     float wt[MAX_TOPK];
-    for (int k = 0; k < p.topk; ++k) wt[k] = __fmul_rn(__fdiv_rn(ps[k], sum), p.scale);
+    #pragma unroll
+    for (int k = 0; k < MAX_TOPK; ++k) wt[k] = __shfl_sync(0xffffffffu, mine, k);
     int osel[MAX_TOPK]; float ow[MAX_TOPK];
     const int keep = p.keep;
     if (keep >= p.topk) {
-        for (int k = 0; k < p.topk; ++k) { osel[k] = sel[k]; ow[k] = wt[k]; }
+        #pragma unroll
+        for (int k = 0; k < MAX_TOPK; ++k) { osel[k] = sel[k]; ow[k] = wt[k]; }
     } else {
-        int ord[MAX_TOPK];
-        for (int k = 0; k < p.topk; ++k) ord[k] = k;
-        for (int a = 1; a < p.topk; ++a) {          // stable insertion sort by weight, descending
-            const int v = ord[a]; int b = a - 1;
-            while (b >= 0 && wt[ord[b]] < wt[v]) { ord[b + 1] = ord[b]; --b; }
-            ord[b + 1] = v;
+        // the engine's stable sort by weight, descending: entry a goes to position
+        // #{b : wt[b] > wt[a]} + #{b < a : wt[b] == wt[a]}
+        #pragma unroll
+        for (int r = 0; r < MAX_TOPK; ++r) { osel[r] = 0; ow[r] = 0.0f; }
+        #pragma unroll
+        for (int a = 0; a < MAX_TOPK; ++a) {
+            int r = 0;
+            #pragma unroll
+            for (int b = 0; b < MAX_TOPK; ++b)
+                if (b < p.topk && b != a && (wt[b] > wt[a] || (wt[b] == wt[a] && b < a))) ++r;
+            #pragma unroll
+            for (int q = 0; q < MAX_TOPK; ++q) if (a < p.topk && r == q) { osel[q] = sel[a]; ow[q] = wt[a]; }
         }
         float sw = 0.0f;
-        for (int k = 0; k < keep; ++k) { osel[k] = sel[ord[k]]; ow[k] = wt[ord[k]]; sw = __fadd_rn(sw, ow[k]); }
+        #pragma unroll
+        for (int k = 0; k < MAX_TOPK; ++k) if (k < keep) sw = __fadd_rn(sw, ow[k]);
         if (p.renorm && sw > 1e-6f) {
             const float f = __fdiv_rn(p.scale, sw);
-            for (int k = 0; k < keep; ++k) ow[k] = __fmul_rn(ow[k], f);
+            #pragma unroll
+            for (int k = 0; k < MAX_TOPK; ++k) if (k < keep) ow[k] = __fmul_rn(ow[k], f);
         }
     }
     if (lane < keep) {
         int sv = 0; float wv = 0.0f;
+        #pragma unroll
         for (int k = 0; k < MAX_TOPK; ++k) if (k == lane) { sv = osel[k]; wv = ow[k]; }
         p.sel[(size_t)t * keep + lane] = sv;
         p.w[(size_t)t * keep + lane] = wv;
