@@ -6,44 +6,43 @@
 namespace lk {
 
 // ------------------------------------------------------------------ combine
-__global__ void k_combine(CombineParams p) {
+__global__ void __launch_bounds__(64) k_combine(CombineParams p) {
     pdl_trigger();
     pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;       // float4 index over T x HIDDEN
     const int per = HIDDEN / 4;
     if (i >= p.T * per) return;
     const int t = i / per, c = i % per;
-    // all loads first (independent), then the sums in entry order: the chain is one memory round trip
+    // every load is issued before any sum (one memory round trip); the sums keep entry order
     float4 v[MAX_TOPK];
     bool use[MAX_TOPK];
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
     #pragma unroll
     for (int k = 0; k < MAX_TOPK; ++k) {
         use[k] = k < p.keep && !(p.sel && p.sel[t * p.keep + k] < 0);
-        v[k] = k < p.keep ? ((const float4*)(p.y + ((size_t)t * p.keep + k) * HIDDEN))[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[k] = k < p.keep ? ((const float4*)(p.y + ((size_t)t * p.keep + k) * HIDDEN))[c] : zero;
     }
-    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int nsh = p.sh_n < 0 ? 0 : (p.sh_n > 0 ? p.sh_n : p.T), j = t - p.sh_t0;
+    const bool has_sh = p.h && p.with_shared && j >= 0 && j < nsh;
+    const float4 hr = p.h && p.resid ? ((const float4*)(p.resid + (size_t)t * p.ld_out))[c] : zero;
+    const float4 hs = has_sh ? ((const float4*)(p.y + ((size_t)p.T * p.keep + j) * HIDDEN))[c] : zero;
+    const float4 he = p.h && p.shared ? ((const float4*)(p.shared + (size_t)t * HIDDEN))[c] : zero;
+    float4 r = zero;
     #pragma unroll
     for (int k = 0; k < MAX_TOPK; ++k)
         if (use[k]) { r.x += v[k].x; r.y += v[k].y; r.z += v[k].z; r.w += v[k].w; }
     if (p.moe) ((float4*)(p.moe + (size_t)t * p.ld_out))[c] = r;
     if (!p.h) return;
-    float4 h = p.resid ? ((const float4*)(p.resid + (size_t)t * p.ld_out))[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-    const int nsh = p.sh_n < 0 ? 0 : (p.sh_n > 0 ? p.sh_n : p.T), j = t - p.sh_t0;
-    if (p.with_shared && j >= 0 && j < nsh) {
-        const float4 v = ((const float4*)(p.y + ((size_t)p.T * p.keep + j) * HIDDEN))[c];
-        h.x += v.x; h.y += v.y; h.z += v.z; h.w += v.w;
-    }
-    if (p.shared) {
-        const float4 v = ((const float4*)(p.shared + (size_t)t * HIDDEN))[c];
-        h.x += v.x; h.y += v.y; h.z += v.z; h.w += v.w;
-    }
+    float4 h = hr;
+    if (has_sh) { h.x += hs.x; h.y += hs.y; h.z += hs.z; h.w += hs.w; }
+    if (p.shared) { h.x += he.x; h.y += he.y; h.z += he.z; h.w += he.w; }
     h.x += r.x; h.y += r.y; h.z += r.z; h.w += r.w;
     ((float4*)(p.h + (size_t)t * p.ld_out))[c] = h;
 }
 
 void launch_combine(const CombineParams& p, cudaStream_t st) {
     const int n = p.T * (HIDDEN / 4);
-    launch_pdl(k_combine, dim3((n + 255) / 256), dim3(256), 0, st, p);
+    launch_pdl(k_combine, dim3((n + 63) / 64), dim3(64), 0, st, p);
 }
 
 // ------------------------------------------------------------------ seeded weight generation
