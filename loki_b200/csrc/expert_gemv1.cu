@@ -159,10 +159,18 @@ __global__ void __launch_bounds__(G1_THREADS, 1) k_gate_up1(ExpertParams p) {
         const int s = tile / G1_TILES_PER_SLOT, rt = tile % G1_TILES_PER_SLOT;
         const int tok = p.slot_tok[s];
         if (tok != xtok) {
-            if (tok >= 0) dx = q8_group_global(p.x + (size_t)tok * p.ld_x, g, xr);
-            else { dx = 0.0f; for (int j = 0; j < 8; ++j) xr[j] = 0u; }
-            #pragma unroll
-            for (int j = 0; j < 8; ++j) nx[j] = neg_i8x4(xr[j]);
+            if (tok == 0 && p.xq) {                  // quantised by the router (one-token forward)
+                const uint4 a0 = ((const uint4*)(p.xq + g * 32))[0], a1 = ((const uint4*)(p.xq + g * 32))[1];
+                const uint4 b0 = ((const uint4*)(p.xqn + g * 32))[0], b1 = ((const uint4*)(p.xqn + g * 32))[1];
+                xr[0] = a0.x; xr[1] = a0.y; xr[2] = a0.z; xr[3] = a0.w; xr[4] = a1.x; xr[5] = a1.y; xr[6] = a1.z; xr[7] = a1.w;
+                nx[0] = b0.x; nx[1] = b0.y; nx[2] = b0.z; nx[3] = b0.w; nx[4] = b1.x; nx[5] = b1.y; nx[6] = b1.z; nx[7] = b1.w;
+                dx = p.xd[g];
+            } else {
+                if (tok >= 0) dx = q8_group_global(p.x + (size_t)tok * p.ld_x, g, xr);
+                else { dx = 0.0f; for (int j = 0; j < 8; ++j) xr[j] = 0u; }
+                #pragma unroll
+                for (int j = 0; j < 8; ++j) nx[j] = neg_i8x4(xr[j]);
+            }
             xtok = tok;
         }
         float kept = 0.0f;

@@ -22,6 +22,9 @@ struct LkMoeCtx {
     int* nslots = nullptr; int max_slots = 0;
     int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
     int* err = nullptr; int* tile_count = nullptr;
+    int8_t* xq = nullptr; int8_t* xqn = nullptr; float* xd = nullptr;   // token 0's q8 x from the router (T == 1)
+    bool xq_ready = false;            // set while a one-token forward's expert stage runs, for x == xq_src
+    const float* xq_src = nullptr;
     int sh_t0 = 0, sh_n = 0;          // shared-expert token range of the next expert stage (SlotParams semantics)
     // tensor-core path (T >= gemm_min_tokens): 64-token slots and fp16 operand staging
     int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
@@ -103,6 +106,7 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LK_CU(dalloc(&c->y, rows * HIDDEN));
     LK_CU(dalloc(&c->err, 1));
     LK_CU(cudaMemset(c->err, 0, sizeof(int)));
+    LK_CU(dalloc(&c->xq, HIDDEN)); LK_CU(dalloc(&c->xqn, HIDDEN)); LK_CU(dalloc(&c->xd, HIDDEN / 32));
     LK_CU(dalloc(&c->tile_count, (T + 7) / 8));
     LK_CU(cudaMemset(c->tile_count, 0, (size_t)((T + 7) / 8) * sizeof(int)));
     c->g_max = max_slots_for(T, KE, NE, GEMM_NT, cfg->with_shared);
@@ -125,7 +129,7 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
 void lk_moe_destroy(LkMoeCtx* c) {
     if (!c) return;
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
-                     c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count,
+                     c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->xq, c->xqn, c->xd,
                      c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt,
                      c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->xh, c->hb };
     for (void* p : ptrs) if (p) cudaFree(p);
@@ -203,6 +207,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
     e.x = x; e.ld_x = ld_x;
     e.slot_expert = c->slot_expert; e.slot_tok = c->slot_tok; e.slot_out = c->slot_out; e.slot_w = c->slot_w; e.nslots = c->nslots;
     e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err;
+    if (c->xq_ready && x == c->xq_src) { e.xq = c->xq; e.xqn = c->xqn; e.xd = c->xd; }
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
     if (c->ev[1]) LK_CU(record_event(c->ev[1], st));
@@ -331,8 +336,11 @@ int lk_moe_forward(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const flo
     cudaStream_t st = (cudaStream_t)stream;
     const int keep = c->cfg.keep;
     RouterParams p = router_params(c, W, x, T, logits_override, c->sel, c->w, T == 1);
+    if (T == 1) { p.xq = c->xq; p.xqn = c->xqn; p.xd = c->xd; }
     launch_router(p, st);
+    c->xq_ready = T == 1; c->xq_src = x;
     rc = run_stage(c, W, x, HIDDEN, resid, T, c->sel, c->w, keep, h, moe, T == 1, st);
+    c->xq_ready = false; c->xq_src = nullptr;
     if (rc) return rc;
     if (sel) LK_CU(cudaMemcpyAsync(sel, c->sel, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));
     if (w) LK_CU(cudaMemcpyAsync(w, c->w, (size_t)T * keep * 4, cudaMemcpyDeviceToDevice, st));

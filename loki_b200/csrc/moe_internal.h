@@ -25,6 +25,9 @@ struct RouterParams {
     // optional slot table written directly for T == 1 (decode): keep routed slots + shared slot
     int* slot_expert; int* slot_tok; int* slot_out; float* slot_w; int* nslots; int with_shared;
     int* tile_count;                        // ceil(T/8) zeroed counters (last-CTA-done top-k)
+    // optional, T == 1: the q8 of x for the expert kernels -- CTA e < HIDDEN/32 writes group e: int8 values
+    // xq, their negations xqn (HIDDEN bytes each) and the scale xd[e] (quant_q8_group, bit for bit)
+    int8_t* xq; int8_t* xqn; float* xd;
 };
 void launch_router(const RouterParams& p, cudaStream_t st);
 
@@ -68,6 +71,7 @@ struct ExpertParams {
     const uint8_t* sh_gate; const uint8_t* sh_up; const uint8_t* sh_down;
     const float* x; int ld_x;                         // activations [T][HIDDEN] (fp32; quantised to q8 in-kernel)
     const int* slot_expert; const int* slot_tok; const int* slot_out; const float* slot_w; const int* nslots;
+    const int8_t* xq; const int8_t* xqn; const float* xd;   // optional: token 0's q8 activations from the router
     int8_t* hq; float* hd;                            // SwiGLU output q8: [rows][MOE_INTER], scales [rows][MOE_INTER/32]
     float* y;                                         // weighted expert outputs [rows][HIDDEN]
     int* err;

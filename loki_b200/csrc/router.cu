@@ -55,6 +55,21 @@ __global__ void __launch_bounds__(256) k_router_logits(RouterParams p) {
     // the previous kernel (which may still be producing x)
     pdl_trigger();
     pdl_wait();
+    if (NTT == 1 && p.xq && e < HIDDEN / 32 && warp == 0) {   // one token: q8 group e of x for the experts
+        const float4 xv = lane < 8 ? ((const float4*)p.x)[e * 8 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float amax = fmaxf(fmaxf(fabsf(xv.x), fabsf(xv.y)), fmaxf(fabsf(xv.z), fabsf(xv.w)));
+        #pragma unroll
+        for (int o = 4; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float d = amax / 127.0f, id = d > 0.0f ? 1.0f / d : 0.0f;      // as quant_q8_group
+        if (lane < 8) {
+            const int q0 = (int)rintf(xv.x * id), q1 = (int)rintf(xv.y * id), q2 = (int)rintf(xv.z * id), q3 = (int)rintf(xv.w * id);
+            ((uint32_t*)p.xq)[e * 8 + lane] = (uint32_t)(uint8_t)q0 | (uint32_t)(uint8_t)q1 << 8 |
+                                              (uint32_t)(uint8_t)q2 << 16 | (uint32_t)(uint8_t)q3 << 24;
+            ((uint32_t*)p.xqn)[e * 8 + lane] = (uint32_t)(uint8_t)-q0 | (uint32_t)(uint8_t)-q1 << 8 |
+                                               (uint32_t)(uint8_t)-q2 << 16 | (uint32_t)(uint8_t)-q3 << 24;
+            if (lane == 0) p.xd[e] = d;
+        }
+    }
     #pragma unroll
     for (int t = 0; t < NTT; ++t) {
         float a = 0.0f;
