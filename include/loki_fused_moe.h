@@ -27,8 +27,11 @@
  * returns; FLOut points into library-owned pinned mirrors valid until the next call on the context;
  * fl_moe, fl_fetch, fl_wide_finish, fl_skip, fl_wide_skip block the host until their results are in
  * the mirrors.  Differences: errors are printed and recorded (fl_moe_error) instead of exit(7); the
- * down projection format must be FL_IQ2 (Q2_K / Q3_K downs return LK_ERR_UNSUPPORTED through
- * fl_moe_error); with HBM-resident shards, ids may be global expert ids into the full 256-expert arena.
+ * down projection format is FL_IQ2, FL_Q2K or FL_Q3K (the real model's downs; other formats return
+ * LK_ERR_UNSUPPORTED through fl_moe_error), with the routed arena's expert stride
+ * ggml_row_size(down_fmt, 2048) * 7168 as in the engine's load_experts; the shared expert passed to
+ * fl_moe_prepare is IQ2_XXS; with HBM-resident shards, ids may be global expert ids into the full
+ * 256-expert arena.
  */
 #ifndef LOKI_FUSED_MOE_H
 #define LOKI_FUSED_MOE_H

@@ -61,8 +61,10 @@ typedef struct LkMoeWeights {
     /* routed experts in the engine's arena layout: expert e's matrix at base + e * stride (bytes) */
     const void* gate; const void* up; const void* down;
     int64_t gate_stride, up_stride, down_stride;
-    int down_fmt;                 /* LK_FMT_IQ2 */
-    /* shared expert (IQ2_XXS, same shapes as one routed expert); null when with_shared == 0 */
+    int down_fmt;                 /* format of every down matrix, routed and shared: LK_FMT_IQ2, or the real model's
+                                     LK_FMT_Q2K / LK_FMT_Q3K (fl_moe's down_fmt, src/fused_layer.h:45); the K-quants
+                                     run the single-token matvec path at every T (q8 SwiGLU output, as the reference) */
+    /* shared expert (IQ2_XXS gate/up, down in down_fmt, same shapes as one routed expert); null when with_shared == 0 */
     const void* sh_gate; const void* sh_up; const void* sh_down;
     /* router: weights [n_experts][7168] fp32 (router_w_f16 = 0) or fp16 (1); bias [n_experts] fp32 */
     const void* router_w; int router_w_f16;
@@ -134,6 +136,10 @@ LK_API int lk_moe_experts_noalloc(const LkMoeWeights* W, const float* x, const f
  * / 2 down), expert expert0+i written at dst + i * stride; the same bytes as the CPU generator. */
 LK_API int lk_gen_iq2(void* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
                int64_t stride, lk_stream_t stream);
+/* the same for any format: fmt LK_FMT_IQ2 (identical to lk_gen_iq2), LK_FMT_Q2K or LK_FMT_Q3K (every byte but the
+ * fp16 scales uniform, d and dmin = fp16(|N(0,1)|*1e-3)); the same bytes as the CPU generator */
+LK_API int lk_gen_weights(int fmt, void* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
+                          int64_t stride, lk_stream_t stream);
 
 #ifdef __cplusplus
 }

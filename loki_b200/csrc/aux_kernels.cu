@@ -48,18 +48,22 @@ void launch_combine(const CombineParams& p, cudaStream_t st) {
 // ------------------------------------------------------------------ seeded weight generation
 // one CTA = 64 consecutive blocks of one expert matrix, staged in shared memory, written as 16-byte words
 __global__ void __launch_bounds__(64) k_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0,
-                                                int rows, int K, int64_t stride) {
-    __shared__ __align__(16) uint8_t buf[64 * BLK_IQ2];
+                                                int rows, int K, int64_t stride, int fmt) {
+    __shared__ __align__(16) uint8_t buf[64 * BLK_Q3K];
     const int e = expert0 + blockIdx.y;
+    const int nbytes = fmt_block_bytes(fmt);
     const uint64_t key = iq2_gen_key(seed, (uint32_t)layer, (uint32_t)matrix, (uint32_t)e);
     const int64_t nblk = (int64_t)rows * (K / QK);
     const int64_t b0 = (int64_t)blockIdx.x * 64;
     const int64_t b = b0 + threadIdx.x;
-    if (b < nblk) iq2_gen_block(key, (uint64_t)b, buf + threadIdx.x * BLK_IQ2);
+    if (b < nblk) {
+        if (fmt == FMT_IQ2) iq2_gen_block(key, (uint64_t)b, buf + threadIdx.x * BLK_IQ2);
+        else kq_gen_block(fmt, key, (uint64_t)b, buf + threadIdx.x * nbytes);
+    }
     __syncthreads();
-    uint8_t* out = dst + (size_t)blockIdx.y * stride + (size_t)b0 * BLK_IQ2;
+    uint8_t* out = dst + (size_t)blockIdx.y * stride + (size_t)b0 * nbytes;
     const int nb = (int)(nblk - b0 < 64 ? nblk - b0 : 64);
-    const int bytes = nb * BLK_IQ2;
+    const int bytes = nb * nbytes;
     if (((uintptr_t)out & 15) == 0 && (bytes & 15) == 0) {
         for (int i = threadIdx.x; i < bytes / 16; i += 64) ((uint4*)out)[i] = ((const uint4*)buf)[i];
     } else {
@@ -71,7 +75,14 @@ void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expe
                     int64_t stride, cudaStream_t st) {
     const int64_t nblk = (int64_t)rows * (K / QK);
     dim3 grid((unsigned)((nblk + 63) / 64), (unsigned)n_exp);
-    k_gen_iq2<<<grid, 64, 0, st>>>(dst, seed, layer, matrix, expert0, rows, K, stride);
+    k_gen_iq2<<<grid, 64, 0, st>>>(dst, seed, layer, matrix, expert0, rows, K, stride, FMT_IQ2);
+}
+
+void launch_gen_weights(int fmt, uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
+                        int64_t stride, cudaStream_t st) {
+    const int64_t nblk = (int64_t)rows * (K / QK);
+    dim3 grid((unsigned)((nblk + 63) / 64), (unsigned)n_exp);
+    k_gen_iq2<<<grid, 64, 0, st>>>(dst, seed, layer, matrix, expert0, rows, K, stride, fmt);
 }
 
 int num_sms(int device) {

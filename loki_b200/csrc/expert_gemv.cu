@@ -351,6 +351,7 @@ void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st) {
     }
 }
 void launch_down(const ExpertParams& p, int nt, int grid, cudaStream_t st) {
+    if (p.down_fmt == FMT_Q2K || p.down_fmt == FMT_Q3K) { launch_down1_kq(p, grid, st); return; }   // single-token slots only
     switch (nt) {
         case 1: launch_down1(p, grid, st); break;
         case 2: dn_launch<2>(p, grid, st); break;

@@ -78,6 +78,8 @@ static void check_dev(FLCtx* c) {
     }
 }
 
+static bool down_fmt_ok(int f) { return f == FL_IQ2 || f == FL_Q2K || f == FL_Q3K; }
+
 static ExpertParams expert_params(FLCtx* c, const void* gate, const void* up, const void* down, int64_t sg, int64_t sd,
                                   const float* x, int* se, int* stok, int* sout, float* sw, int* sn,
                                   int8_t* hq, float* hd, float* y) {
@@ -238,7 +240,7 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
             int KE, int n, FLOut* out) {
     if (!c || !out) return;
     std::memset(out, 0, sizeof(FLOut));
-    if (down_fmt != FL_IQ2) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe: down format must be FL_IQ2 in this build"); return; }
+    if (!down_fmt_ok(down_fmt)) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe: down format must be FL_IQ2, FL_Q2K or FL_Q3K"); return; }
     if (n < 1 || n > NB || KE < 1 || KE > MAX_TOPK || nexp < 1 || nexp > N_EXPERTS || !ids || !w) { fl_fail(c, LK_ERR_ARG, "fl_moe: bad argument"); return; }
     if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_moe: arena not 16-byte aligned"); return; }
     for (int i = 0; i < n * KE; ++i) if (ids[i] < 0 || ids[i] >= nexp) { fl_fail(c, LK_ERR_ARG, "fl_moe: slot id out of range"); return; }
@@ -249,15 +251,16 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     FLCK(cudaMemcpyAsync(c->ids, hi, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
     FLCK(cudaMemcpyAsync(c->w, hw, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
     c->last_ids.assign(ids, ids + n * KE); c->last_w.assign(w, w + n * KE); c->last_n = n; c->last_ke = KE;
-    const int nt = nt_for(n);
+    const int nt = down_fmt == FL_IQ2 ? nt_for(n) : 1;      // the K-quant down kernel takes single-token slots
     SlotParams sp{};
     sp.sel = c->ids; sp.w = c->w; sp.T = n; sp.keep = KE; sp.n_experts = N_EXPERTS; sp.nt = nt; sp.with_shared = 0;
     sp.counts = c->counts; sp.offsets = c->offsets; sp.perm = c->perm;
     sp.slot_expert = c->s_expert; sp.slot_tok = c->s_tok; sp.slot_out = c->s_out; sp.slot_w = c->s_w; sp.nslots = c->s_n;
     sp.max_slots = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1); sp.err = c->err;
     launch_build_slots(sp, st);
-    const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)EXPERT_DOWN_BYTES;
+    const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)down_matrix_bytes(down_fmt);
     ExpertParams e = expert_params(c, gate, up, down, sg, sd, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->hq, c->hd, c->y);
+    e.down_fmt = down_fmt;
     launch_gate_up(e, nt, c->nsm, st);
     launch_down(e, nt, c->nsm, st);
     CombineParams cp{};                           // h = ffn_inp + shared (from fl_moe_prepare) + routed
@@ -311,8 +314,9 @@ int fl_wide_init(FLCtx* c, int wmax, int KE) {
     if (dz(&c->ncur_all, R) || dz(&c->base_all, R) || dz(&c->out_all, ent * HIDDEN) || dz(&c->whq, ent * MOE_INTER) ||
         dz(&c->whd, ent * (MOE_INTER / 32)) || hz(&c->h_wh, R) || hz(&c->h_wmoe, R)) { fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0; }
     for (int p = 0; p < 2; ++p) {
-        if (dz(&c->w_expert[p], WIDE_SLOTS) || dz(&c->w_tok[p], WIDE_SLOTS * NB) || dz(&c->w_out[p], WIDE_SLOTS * NB) ||
-            dz(&c->w_w[p], WIDE_SLOTS * NB) || dz(&c->w_n[p], 1) || hz(&c->hw_tab[p], WIDE_SLOTS * (1 + 2 * NB) + 1) ||
+        // room for WIDE_SLOTS x NB single-token slots (the K-quant downs split every wide slot into its rows)
+        if (dz(&c->w_expert[p], WIDE_SLOTS * NB) || dz(&c->w_tok[p], WIDE_SLOTS * NB) || dz(&c->w_out[p], WIDE_SLOTS * NB) ||
+            dz(&c->w_w[p], WIDE_SLOTS * NB) || dz(&c->w_n[p], 1) || hz(&c->hw_tab[p], 3 * WIDE_SLOTS * NB + 1) ||
             hz(&c->hw_w[p], WIDE_SLOTS * NB) || cudaEventCreateWithFlags(&c->wev[p], cudaEventDisableTiming)) {
             fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0;
         }
@@ -323,36 +327,43 @@ int fl_wide_init(FLCtx* c, int wmax, int KE) {
 void fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int nexp, const int* midx, const int* rows,
                  const int* kidx, const float* wk, int nslots, int KE, int par) {
     if (!c || !c->ncur_all) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: fl_wide_init first"); return; }
-    if (down_fmt != FL_IQ2) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_wide_moe: down format must be FL_IQ2 in this build"); return; }
+    if (!down_fmt_ok(down_fmt)) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_wide_moe: down format must be FL_IQ2, FL_Q2K or FL_Q3K"); return; }
     if (KE != c->wke || nslots < 0 || nexp < 1) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: bad argument"); return; }
     if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: arena not 16-byte aligned"); return; }
     par &= 1;
     cudaStream_t st = c->st;
-    const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)EXPERT_DOWN_BYTES;
+    const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)down_matrix_bytes(down_fmt);
+    // slots as given (NB rows each), or, for the K-quant downs, one single-token slot per live row
+    const int snt = down_fmt == FL_IQ2 ? NB : 1;
     for (int s0 = 0; s0 < nslots; s0 += WIDE_SLOTS) {
         const int ns = std::min(WIDE_SLOTS, nslots - s0);
         if (s0 > 0) FLCK(cudaStreamSynchronize(st));          // the tables of this parity are reused
-        int* he = c->hw_tab[par]; int* ht = he + WIDE_SLOTS; int* ho = ht + WIDE_SLOTS * NB; float* hw = c->hw_w[par];
+        int* he = c->hw_tab[par]; int* ht = he + WIDE_SLOTS * NB; int* ho = ht + WIDE_SLOTS * NB; float* hw = c->hw_w[par];
+        int nout = 0;                                          // slots written
         for (int s = 0; s < ns; ++s) {
             const int m = midx[s0 + s];
             if (m < 0 || m >= nexp) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: slot expert out of range"); return; }
-            he[s] = m;
+            if (snt == NB) he[nout] = m;
             for (int i = 0; i < NB; ++i) {
                 const int r = rows[(size_t)(s0 + s) * NB + i], k = kidx[(size_t)(s0 + s) * NB + i];
                 const bool live = r >= 0 && r < c->wmax && k >= 0 && k < KE;
-                ht[s * NB + i] = live ? r : -1; ho[s * NB + i] = live ? r * KE + k : -1; hw[s * NB + i] = live ? wk[(size_t)(s0 + s) * NB + i] : 0.f;
+                const float wv = live ? wk[(size_t)(s0 + s) * NB + i] : 0.f;
+                if (snt == NB) { ht[nout * NB + i] = live ? r : -1; ho[nout * NB + i] = live ? r * KE + k : -1; hw[nout * NB + i] = wv; }
+                else if (live) { he[nout] = m; ht[nout] = r; ho[nout] = r * KE + k; hw[nout] = wv; ++nout; }
             }
+            if (snt == NB) ++nout;
         }
-        ho[ns * NB] = ns;
-        FLCK(cudaMemcpyAsync(c->w_expert[par], he, ns * 4, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->w_tok[par], ht, (size_t)ns * NB * 4, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->w_out[par], ho, (size_t)ns * NB * 4, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->w_w[par], hw, (size_t)ns * NB * 4, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->w_n[par], ho + ns * NB, 4, cudaMemcpyHostToDevice, st));
+        ho[nout * snt] = nout;
+        FLCK(cudaMemcpyAsync(c->w_expert[par], he, (size_t)nout * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_tok[par], ht, (size_t)nout * snt * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_out[par], ho, (size_t)nout * snt * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_w[par], hw, (size_t)nout * snt * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_n[par], ho + nout * snt, 4, cudaMemcpyHostToDevice, st));
         ExpertParams e = expert_params(c, gate, up, down, sg, sd, c->ncur_all, c->w_expert[par], c->w_tok[par], c->w_out[par],
                                        c->w_w[par], c->w_n[par], c->whq, c->whd, c->out_all);
-        launch_gate_up(e, NB, c->nsm, st);
-        launch_down(e, NB, c->nsm, st);
+        e.down_fmt = down_fmt;
+        launch_gate_up(e, snt, c->nsm, st);
+        launch_down(e, snt, c->nsm, st);
     }
     FLCK(cudaGetLastError());
 }

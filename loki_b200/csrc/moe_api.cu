@@ -138,7 +138,8 @@ void lk_moe_destroy(LkMoeCtx* c) {
 
 static int check_weights(LkMoeCtx* c, const LkMoeWeights* W, bool need_router) {
     if (!W) return set_err(c, LK_ERR_ARG, "null weights");
-    if (W->down_fmt != LK_FMT_IQ2) return set_err(c, LK_ERR_UNSUPPORTED, "down format %d: only IQ2_XXS (4) is implemented", W->down_fmt);
+    if (W->down_fmt != LK_FMT_IQ2 && W->down_fmt != LK_FMT_Q2K && W->down_fmt != LK_FMT_Q3K)
+        return set_err(c, LK_ERR_UNSUPPORTED, "down format %d: IQ2_XXS (4), Q2_K (5) or Q3_K (6)", W->down_fmt);
     const void* mats[] = { W->gate, W->up, W->down };
     for (const void* m : mats) if (!m || ((uintptr_t)m & 15)) return set_err(c, LK_ERR_ARG, "expert arena null or not 16-byte aligned");
     if ((W->gate_stride & 15) || (W->up_stride & 15) || (W->down_stride & 15))
@@ -206,7 +207,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
     e.sh_gate = (const uint8_t*)W->sh_gate; e.sh_up = (const uint8_t*)W->sh_up; e.sh_down = (const uint8_t*)W->sh_down;
     e.x = x; e.ld_x = ld_x;
     e.slot_expert = c->slot_expert; e.slot_tok = c->slot_tok; e.slot_out = c->slot_out; e.slot_w = c->slot_w; e.nslots = c->nslots;
-    e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err;
+    e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err; e.down_fmt = W->down_fmt;
     if (c->xq_ready && x == c->xq_src) { e.xq = c->xq; e.xqn = c->xqn; e.xd = c->xd; }
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
@@ -286,11 +287,13 @@ static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int 
 
 // the expert stage for routing (sel, w) [T][keep], by token count: single-token dp4a matvecs (the slot
 // tables of T == 1 may already have been written by the router: slots_ready), the register-fed mma.sync
-// path, or the tcgen05 GEMMs
+// path, or the tcgen05 GEMMs.  K-quant (Q2_K / Q3_K) downs take the dp4a matvecs at every T: their down
+// kernel consumes the q8 SwiGLU output, the reference's numerics for those formats.
 static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
                      const float* w, int keep, float* h, float* moe, bool slots_ready, cudaStream_t st) {
-    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
-    if (T >= c->mma_min_tokens) return run_mma_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
+    const bool iq2_down = W->down_fmt == LK_FMT_IQ2;
+    if (iq2_down && T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
+    if (iq2_down && T >= c->mma_min_tokens) return run_mma_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
     if (!slots_ready) {
         SlotParams s{};
         s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = slot_nt(T);
@@ -383,7 +386,8 @@ int lk_ep_shared(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float
         return set_err(c, LK_ERR_ARG, "the shared expert needs with_shared = 1 and W->sh_*");
     if (((uintptr_t)W->sh_gate | (uintptr_t)W->sh_up | (uintptr_t)W->sh_down) & 15)
         return set_err(c, LK_ERR_ARG, "shared expert matrices must be 16-byte aligned");
-    if (W->down_fmt != LK_FMT_IQ2) return set_err(c, LK_ERR_UNSUPPORTED, "down format %d", W->down_fmt);
+    if (W->down_fmt != LK_FMT_IQ2 && W->down_fmt != LK_FMT_Q2K && W->down_fmt != LK_FMT_Q3K)
+        return set_err(c, LK_ERR_UNSUPPORTED, "down format %d", W->down_fmt);
     if (T > c->cfg.max_tokens) return set_err(c, LK_ERR_CAPACITY, "T=%d > capacity %d", T, c->cfg.max_tokens);
     if (T == 0) return LK_OK;
     // keep = 0: shared-expert slots only
@@ -411,6 +415,14 @@ int lk_gen_iq2(void* dst, uint64_t seed, int layer, int matrix, int expert0, int
                lk_stream_t stream) {
     if (!dst || rows < 1 || K < QK || (K % QK) || n_exp < 1) return LK_ERR_ARG;
     launch_gen_iq2((uint8_t*)dst, seed, layer, matrix, expert0, n_exp, rows, K, stride, (cudaStream_t)stream);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+int lk_gen_weights(int fmt, void* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K, int64_t stride,
+                   lk_stream_t stream) {
+    if (fmt != LK_FMT_IQ2 && fmt != LK_FMT_Q2K && fmt != LK_FMT_Q3K) return LK_ERR_UNSUPPORTED;
+    if (!dst || rows < 1 || K < QK || (K % QK) || n_exp < 1) return LK_ERR_ARG;
+    launch_gen_weights(fmt, (uint8_t*)dst, seed, layer, matrix, expert0, n_exp, rows, K, stride, (cudaStream_t)stream);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 

@@ -40,6 +40,31 @@ constexpr size_t EXPERT_DOWN_BYTES = (size_t)HIDDEN * (MOE_INTER / QK) * BLK_IQ2
 // ---- format ids, numerically equal to the reference's FL_IQ2 / FL_Q2K / FL_Q3K
 enum { FMT_IQ2 = 4, FMT_Q2K = 5, FMT_Q3K = 6 };
 
+// ---- the K-quant down formats (GGUF / ggml block layouts; the reference's BLK_Q2 / BLK_Q3,
+//  fused_layer.cu:19).  256 weights per block; weight i = 128n + 32j + 16s + l (n < 2, j < 4, s < 2,
+//  l < 16) sits in byte 32n + 16s + l of qs at bits 2j..2j+1, and its 16-weight sub-block has scale
+//  index 8n + 2j + s.
+//   Q2_K (84 B): scales[16] (bits 0-3 scale, 4-7 min), qs[64], fp16 d, fp16 dmin;
+//                w = d*(sc & 15)*q - dmin*(sc >> 4), q in 0..3
+//   Q3_K (110 B): hmask[32], qs[64], scales[12] (16 x 6 bits, stored + 32), fp16 d;
+//                w = d*(scale - 32)*(q - (hmask[16s + l] bit (4n + j) ? 0 : 4)), q in 0..3
+constexpr int BLK_Q2K = 84;
+constexpr int BLK_Q3K = 110;
+constexpr int Q2K_QS = 16, Q2K_D = 80, Q2K_DMIN = 82;
+constexpr int Q3K_QS = 32, Q3K_SC = 96, Q3K_D = 108;
+LK_HD constexpr int fmt_block_bytes(int fmt) { return fmt == FMT_Q2K ? BLK_Q2K : fmt == FMT_Q3K ? BLK_Q3K : BLK_IQ2; }
+// one expert's down matrix [HIDDEN rows][MOE_INTER] in format fmt: 3 784 704 / 4 816 896 / 6 307 840 B
+LK_HD constexpr size_t down_matrix_bytes(int fmt) { return (size_t)HIDDEN * (MOE_INTER / QK) * fmt_block_bytes(fmt); }
+
+// Q3_K's 6-bit scale i (0..15) from the 12 packed bytes: low 4 bits in byte i (i < 8) or the high
+// nibble of byte i - 8, high 2 bits at bits 2*(i/4) of byte 8 + i%4 (ggml dequantize_row_q3_K's
+// kmask unpacking; the reference's q3_scales, fused_layer.cu:34-37).  Returns scale - 32.
+LK_HD int q3k_scale(const uint8_t* sc, int i) {
+    const int lo = i < 8 ? (sc[i] & 15) : (sc[i - 8] >> 4);
+    const int hi = (sc[8 + (i & 3)] >> (2 * (i >> 2))) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
 // ---- fp16 <-> fp32 in software (IEEE binary16, round to nearest even), identical on host and device
 LK_HD uint32_t f32_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 LK_HD float bits_f32(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
@@ -163,6 +188,24 @@ LK_HD void iq2_gen_block(uint64_t key, uint64_t block, uint8_t* out) {
     for (int g = 0; g < 8; ++g) {
         const uint64_t v = iq2_gen_group(key, block, g);
         for (int j = 0; j < 8; ++j) out[2 + 8 * g + j] = (uint8_t)(v >> (8 * j));
+    }
+}
+
+// seeded synthetic K-quant blocks (Q2_K / Q3_K down matrices): every byte except the fp16 scales is
+// uniform (splitmix64 draws 0..13 of the block's counter range), d = fp16(|N(0,1)|*1e-3) from draws
+// 16.., Q2_K's dmin likewise from draws 24..  Keys as for IQ2_XXS, so a layer's down matrix in any
+// format comes from the same (seed, layer, matrix, expert) chain.
+LK_HD void kq_gen_block(int fmt, uint64_t key, uint64_t block, uint8_t* out) {
+    const int nu = fmt == FMT_Q2K ? Q2K_D : Q3K_D;          // uniform bytes before the fp16 scale(s)
+    for (int g = 0; 8 * g < nu; ++g) {
+        const uint64_t v = splitmix64(key ^ (block * 32ull + (uint64_t)g));
+        for (int j = 0; j < 8 && 8 * g + j < nu; ++j) out[8 * g + j] = (uint8_t)(v >> (8 * j));
+    }
+    const uint16_t d = iq2_gen_d(key, block * 2ull + (1ull << 40));
+    out[nu] = (uint8_t)(d & 0xFF); out[nu + 1] = (uint8_t)(d >> 8);
+    if (fmt == FMT_Q2K) {
+        const uint16_t m = iq2_gen_d(key, block * 2ull + 1ull + (1ull << 40));
+        out[Q2K_DMIN] = (uint8_t)(m & 0xFF); out[Q2K_DMIN + 1] = (uint8_t)(m >> 8);
     }
 }
 

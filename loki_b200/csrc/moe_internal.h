@@ -75,9 +75,12 @@ struct ExpertParams {
     int8_t* hq; float* hd;                            // SwiGLU output q8: [rows][MOE_INTER], scales [rows][MOE_INTER/32]
     float* y;                                         // weighted expert outputs [rows][HIDDEN]
     int* err;
+    int down_fmt;                                     // FMT_IQ2 (default, 0 reads as IQ2), FMT_Q2K or FMT_Q3K: every down matrix
 };
 void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st);
 void launch_down(const ExpertParams& p, int nt, int grid, cudaStream_t st);
+// single-token down projection of K-quant (Q2_K / Q3_K) experts (expert_kq.cu)
+void launch_down1_kq(const ExpertParams& p, int grid, cudaStream_t st);
 
 // ---- combine: h = resid + shared + sum_k y[t*keep+k], moe = sum_k y[t*keep+k]
 //      (shared = the y rows T*keep + t when with_shared, and/or the separate `shared` rows)
@@ -126,6 +129,9 @@ void launch_slot_mma(const MmaParams& p, int nsm, cudaStream_t st);
 // ---- seeded IQ2_XXS weight generation (moe_format.h generator) for n_experts consecutive experts
 void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
                     int64_t stride, cudaStream_t st);
+// ---- the same for any down format (FMT_IQ2, or the K-quants' kq_gen_block)
+void launch_gen_weights(int fmt, uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
+                        int64_t stride, cudaStream_t st);
 
 // ---- expert-parallel row headers -> sel/w [R][keep]
 void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, cudaStream_t st);

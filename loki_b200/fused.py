@@ -11,7 +11,7 @@ import numpy as np
 from . import native as N
 from .native import HIDDEN, lib
 
-FL_IQ2 = 4
+FL_IQ2, FL_Q2K, FL_Q3K = 4, 5, 6      # down formats (src/fused_layer.h:11)
 
 
 def _p(a):

@@ -19,6 +19,9 @@ EXPERT_MATRIX_BYTES = MOE_INTER * (HIDDEN // QK) * BLK_IQ2          # 3 784 704 
 
 LK_OK, LK_ERR_ARG, LK_ERR_CUDA, LK_ERR_UNSUPPORTED, LK_ERR_CAPACITY, LK_ERR_DEVICE = 0, -1, -2, -3, -4, -5
 FMT_IQ2, FMT_Q2K, FMT_Q3K = 4, 5, 6
+BLOCK_BYTES = {FMT_IQ2: 66, FMT_Q2K: 84, FMT_Q3K: 110}
+# one expert's down matrix [7168 rows][2048] per format: 3 784 704 / 4 816 896 / 6 307 840 bytes
+DOWN_MATRIX_BYTES = {f: HIDDEN * (MOE_INTER // QK) * b for f, b in BLOCK_BYTES.items()}
 EP_ROW_HDR_BYTES = 64
 EP_ROW_BYTES = EP_ROW_HDR_BYTES + HIDDEN * 4      # 28 736
 EP_MAX_RANKS = 8
@@ -67,6 +70,7 @@ SIGNATURES = {
     "lk_moe_last_error": (ctypes.c_char_p, [_P]),
     "lk_moe_experts_noalloc": (_I, [ctypes.POINTER(LkMoeWeights), _P, _P, _I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "lk_gen_iq2": (_I, [_P, ctypes.c_uint64, _I, _I, _I, _I, _I, _I, _I64, _P]),
+    "lk_gen_weights": (_I, [_I, _P, ctypes.c_uint64, _I, _I, _I, _I, _I, _I, _I64, _P]),
     "lk_ep_pack": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "lk_ep_experts": (_I, [_P, ctypes.POINTER(LkMoeWeights), _P, _I, _I, _I, _I, _P, _P, _P]),
     "lk_ep_shared": (_I, [_P, ctypes.POINTER(LkMoeWeights), _P, _P, _I, _P, _P]),

@@ -13,6 +13,9 @@
 //   keep-KE + renorm ...... src/server_core_fused.cpp:793-813 (sort by w desc, keep KE, scale to sum 2.5)
 //   SwiGLU + q8 ........... src/fused_layer.cu:334-341 (h = g/(1+exp(-g))*u, re-quantised per 32)
 //   expert products ....... src/fused_layer.cu:178-202 (IQ2 gate/up/down: sum_g fa_g * dx_g * isum_g)
+//   K-quant downs ......... src/fused_layer.cu:203-227 (Q2_K: per 16 weights fa*dx*isum - dmin*m*s16),
+//                           :228-254 (Q3_K: fa = d*(scale-32), q = low2 - 4 where the high bit is clear);
+//                           block decode cross-checked against gguf-py 0.19.0 Q2_K / Q3_K dequantize
 //   combine ............... src/fused_layer.cu:366-373 and 354-360 (routed = sum_k w_k y_k; h = routed +
 //                           shared + ffn_inp; moe = routed)
 //   permute ............... src/server_core_fused.cpp:937 (byexp: per expert, (row, k) pairs in row-major
@@ -72,6 +75,43 @@ void orc_gen_iq2(uint64_t seed, int layer, int matrix, int expert, int rows, int
 void orc_gen_d_only(uint64_t seed, int layer, int matrix, int expert, int64_t nblk, uint16_t* out) {
     const uint64_t key = iq2_gen_key(seed, (uint32_t)layer, (uint32_t)matrix, (uint32_t)expert);
     for (int64_t b = 0; b < nblk; ++b) out[b] = iq2_gen_d(key, (uint64_t)b);
+}
+
+// out[nblk*256] = dequantised Q2_K (fmt 5) or Q3_K (fmt 6) blocks (gguf-py dequantize_blocks semantics:
+// Q2_K d*(sc&15)*q - dmin*(sc>>4); Q3_K d*(scale-32)*q3, each product in fp32 as written)
+void orc_kq_dequant(int fmt, const uint8_t* blocks, int64_t nblk, float* out) {
+    const int nb = fmt_block_bytes(fmt);
+    #pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nblk; ++b) {
+        const uint8_t* blk = blocks + b * nb;
+        for (int i = 0; i < QK; ++i) {
+            const int n = i >> 7, j = (i >> 5) & 3, s = (i >> 4) & 1, l = i & 15;
+            const int is = 8 * n + 2 * j + s;
+            float v;
+            if (fmt == FMT_Q2K) {
+                uint16_t dh, mh; memcpy(&dh, blk + Q2K_D, 2); memcpy(&mh, blk + Q2K_DMIN, 2);
+                const int q = (blk[Q2K_QS + 32 * n + 16 * s + l] >> (2 * j)) & 3;
+                const float dl = half_to_float(dh) * (float)(blk[is] & 15), ml = half_to_float(mh) * (float)(blk[is] >> 4);
+                v = dl * (float)q - ml;
+            } else {
+                uint16_t dh; memcpy(&dh, blk + Q3K_D, 2);
+                const int lo = (blk[Q3K_QS + 32 * n + 16 * s + l] >> (2 * j)) & 3;
+                const int hb = (blk[16 * s + l] >> (4 * n + j)) & 1;
+                const float dl = half_to_float(dh) * (float)q3k_scale(blk + Q3K_SC, is);
+                v = dl * (float)(lo - (hb ? 0 : 4));
+            }
+            out[b * QK + i] = v;
+        }
+    }
+}
+
+// seeded K-quant matrix (moe_format.h kq_gen_block): rows x K in format fmt of (layer, matrix, expert)
+void orc_gen_kq(int fmt, uint64_t seed, int layer, int matrix, int expert, int rows, int K, uint8_t* out) {
+    const uint64_t key = iq2_gen_key(seed, (uint32_t)layer, (uint32_t)matrix, (uint32_t)expert);
+    const int64_t nblk = (int64_t)rows * (K / QK);
+    const int nb = fmt_block_bytes(fmt);
+    #pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nblk; ++b) kq_gen_block(fmt, key, (uint64_t)b, out + b * nb);
 }
 
 float orc_expf(float x) { return lk_expf(x); }
@@ -266,6 +306,52 @@ static void iq2_matvec_float_multi(const uint8_t* W, int rows, int K, const floa
     }
 }
 
+// y = W . dequant(xq, xd) for a K-quant matrix (Q2_K / Q3_K) and `ntok` q8 activation rows, in the
+// reference's per-16 arithmetic (src/fused_layer.cu:203-254): per 16-weight sub-block an exact integer
+// sum isum = sum q_w * q_x; Q2_K adds fa*dx*isum - mla*dx*sum(q_x) with fa = d*(sc&15), mla = dmin*(sc>>4)
+// (the reference's s16 term); Q3_K adds fa*dx*isum with fa = d*(scale-32) and q_w = low2 - 4 where the
+// high bit is clear.  Evaluated in double: the ideal value of the q8 scheme.
+static void kq_matvec_multi(int fmt, const uint8_t* W, int rows, int K, const int8_t* const* xq, const float* const* xd,
+                            int ntok, float* const* y) {
+    const int NB = K / QK, nb = fmt_block_bytes(fmt);
+    const int qs = fmt == FMT_Q2K ? Q2K_QS : Q3K_QS;
+    #pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t* row = W + (size_t)r * NB * nb;
+        std::vector<double> acc(ntok, 0.0);
+        for (int b = 0; b < NB; ++b) {
+            const uint8_t* blk = row + (size_t)b * nb;
+            uint16_t dh, mh = 0;
+            memcpy(&dh, blk + (fmt == FMT_Q2K ? Q2K_D : Q3K_D), 2);
+            if (fmt == FMT_Q2K) memcpy(&mh, blk + Q2K_DMIN, 2);
+            const float d = half_to_float(dh), dmin = half_to_float(mh);
+            for (int is = 0; is < 16; ++is) {                     // sub-block 8n + 2j + s
+                const int n = is >> 3, j = (is >> 1) & 3, s = is & 1;
+                const int k0 = b * QK + 128 * n + 32 * j + 16 * s;
+                int32_t qw[16];
+                for (int l = 0; l < 16; ++l) {
+                    const int lo = (blk[qs + 32 * n + 16 * s + l] >> (2 * j)) & 3;
+                    qw[l] = fmt == FMT_Q2K ? lo : lo - (((blk[16 * s + l] >> (4 * n + j)) & 1) ? 0 : 4);
+                }
+                const double fa = fmt == FMT_Q2K ? (double)(d * (float)(blk[is] & 15)) : (double)(d * (float)q3k_scale(blk + Q3K_SC, is));
+                const double mla = fmt == FMT_Q2K ? (double)(dmin * (float)(blk[is] >> 4)) : 0.0;
+                for (int t = 0; t < ntok; ++t) {
+                    int32_t isum = 0, xs = 0;
+                    for (int l = 0; l < 16; ++l) { isum += qw[l] * (int32_t)xq[t][k0 + l]; xs += xq[t][k0 + l]; }
+                    const double dx = (double)xd[t][k0 / 32];
+                    acc[t] += fa * dx * (double)isum - mla * dx * (double)xs;
+                }
+            }
+        }
+        for (int t = 0; t < ntok; ++t) y[t][r] = (float)acc[t];
+    }
+}
+
+// one activation row through a K-quant matrix (tests)
+void orc_kq_matvec(int fmt, const uint8_t* W, int rows, int K, const int8_t* xq, const float* xd, float* y) {
+    kq_matvec_multi(fmt, W, rows, K, &xq, &xd, 1, &y);
+}
+
 void orc_iq2_matvec(const uint8_t* W, int rows, int K, const int8_t* xq, const float* xd, float* y) {
     iq2_matvec_multi(W, rows, K, &xq, &xd, 1, &y);
 }
@@ -283,8 +369,11 @@ struct OrcLayerW {
 // hq8 = 1: the SwiGLU output is re-quantised to q8 per 32 before the down projection (the reference's
 // swiglu_q8, src/fused_layer.cu:334-341: the decode and narrow paths); hq8 = 0: it enters the down
 // projection unquantised (the tensor-core prefill path).
-int orc_moe_layer_ex(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
-                     int KE, float* h, float* moe, float* y_slot, float* shared_out, int hq8) {
+// down_fmt: format of every down matrix, routed and shared (FMT_IQ2, FMT_Q2K or FMT_Q3K; the K-quants
+// need hq8 = 1, the reference's narrow and wide passes)
+int orc_moe_layer_fmt(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
+                      int KE, float* h, float* moe, float* y_slot, float* shared_out, int hq8, int down_fmt) {
+    if (down_fmt != FMT_IQ2 && (!hq8 || (down_fmt != FMT_Q2K && down_fmt != FMT_Q3K))) return 1;
     const int E = HIDDEN, H = MOE_INTER;
     // q8 of every token's x
     std::vector<int8_t> xq((size_t)T * E); std::vector<float> xd((size_t)T * E / 32);
@@ -318,7 +407,8 @@ int orc_moe_layer_ex(const float* x, const float* resid, int T, const OrcLayerW*
             hqp[i] = hq.data() + (size_t)s * H; hdp[i] = hd.data() + (size_t)s * H / 32; yp[i] = ytmp[i].data();
             hfp[i] = hf[i].data();
         }
-        if (hq8) iq2_matvec_multi(Wl->down + m * Wl->down_stride, E, H, hqp.data(), hdp.data(), n, yp.data());
+        if (down_fmt != FMT_IQ2) kq_matvec_multi(down_fmt, Wl->down + m * Wl->down_stride, E, H, hqp.data(), hdp.data(), n, yp.data());
+        else if (hq8) iq2_matvec_multi(Wl->down + m * Wl->down_stride, E, H, hqp.data(), hdp.data(), n, yp.data());
         else iq2_matvec_float_multi(Wl->down + m * Wl->down_stride, E, H, hfp.data(), n, yp.data());
         for (int i = 0; i < n; ++i) {
             const int s = perm[off[m] + i];
@@ -344,7 +434,8 @@ int orc_moe_layer_ex(const float* x, const float* resid, int T, const OrcLayerW*
             orc_quant_q8(hv, H, shq.data() + (size_t)t * H, shd.data() + (size_t)t * H / 32);
             hqp[t] = shq.data() + (size_t)t * H; hdp[t] = shd.data() + (size_t)t * H / 32; hfp[t] = hv;
         }
-        if (hq8) iq2_matvec_multi(Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
+        if (down_fmt != FMT_IQ2) kq_matvec_multi(down_fmt, Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
+        else if (hq8) iq2_matvec_multi(Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
         else iq2_matvec_float_multi(Wl->sh_down, E, H, hfp.data(), T, shp.data());
     }
     // combine in fixed k order
@@ -359,6 +450,11 @@ int orc_moe_layer_ex(const float* x, const float* resid, int T, const OrcLayerW*
     if (y_slot) memcpy(y_slot, yslot.data(), yslot.size() * 4);
     if (shared_out) memcpy(shared_out, sh.data(), sh.size() * 4);
     return 0;
+}
+
+int orc_moe_layer_ex(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
+                     int KE, float* h, float* moe, float* y_slot, float* shared_out, int hq8) {
+    return orc_moe_layer_fmt(x, resid, T, Wl, ids, w, KE, h, moe, y_slot, shared_out, hq8, FMT_IQ2);
 }
 
 int orc_moe_layer(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,

@@ -17,6 +17,8 @@ MOE_INTER = 2048
 N_EXPERTS = 256
 QK = 256
 BLK_IQ2 = 66
+FMT_IQ2, FMT_Q2K, FMT_Q3K = 4, 5, 6
+BLOCK_BYTES = {FMT_IQ2: 66, FMT_Q2K: 84, FMT_Q3K: 110}
 
 
 def build(force=False):
@@ -62,6 +64,13 @@ def lib():
         L.orc_moe_layer.restype = ctypes.c_int
         L.orc_moe_layer_ex.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(LayerW), P, P, ctypes.c_int, P, P, P, P, ctypes.c_int]
         L.orc_moe_layer_ex.restype = ctypes.c_int
+        L.orc_moe_layer_fmt.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(LayerW), P, P, ctypes.c_int, P, P, P, P, ctypes.c_int,
+                                        ctypes.c_int]
+        L.orc_moe_layer_fmt.restype = ctypes.c_int
+        L.orc_kq_dequant.argtypes = [ctypes.c_int, P, ctypes.c_int64, P]
+        L.orc_gen_kq.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                 ctypes.c_int, P]
+        L.orc_kq_matvec.argtypes = [ctypes.c_int, P, ctypes.c_int, ctypes.c_int, P, P, P]
         _lib = L
     return _lib
 
@@ -82,6 +91,33 @@ def gen_iq2(seed, layer, matrix, expert, rows, K):
     out = np.empty(rows * (K // QK) * BLK_IQ2, np.uint8)
     lib().orc_gen_iq2(seed, layer, matrix, expert, rows, K, _p(out))
     return out
+
+
+def kq_dequant(fmt, blocks):
+    """Q2_K (fmt 5) / Q3_K (fmt 6) blocks -> fp32 weights (gguf-py dequantize semantics)."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    nblk = blocks.size // BLOCK_BYTES[fmt]
+    out = np.empty(nblk * QK, np.float32)
+    lib().orc_kq_dequant(fmt, _p(blocks), nblk, _p(out))
+    return out
+
+
+def gen_kq(fmt, seed, layer, matrix, expert, rows, K):
+    out = np.empty(rows * (K // QK) * BLOCK_BYTES[fmt], np.uint8)
+    lib().orc_gen_kq(fmt, seed, layer, matrix, expert, rows, K, _p(out))
+    return out
+
+
+def gen_matrix(fmt, seed, layer, matrix, expert, rows, K):
+    """Seeded matrix in any of the three formats (IQ2_XXS uses the IQ2 generator)."""
+    return gen_iq2(seed, layer, matrix, expert, rows, K) if fmt == FMT_IQ2 else gen_kq(fmt, seed, layer, matrix, expert, rows, K)
+
+
+def kq_matvec(fmt, W, rows, K, xq, xd):
+    y = np.empty(rows, np.float32)
+    lib().orc_kq_matvec(fmt, _p(np.ascontiguousarray(W, np.uint8)), rows, K, _p(np.ascontiguousarray(xq, np.int8)),
+                        _p(np.ascontiguousarray(xd, np.float32)), _p(y))
+    return y
 
 
 def quant_q8(x):
@@ -141,18 +177,20 @@ def iq2_matvec(W, rows, K, xq, xd):
     return y
 
 
-def moe_layer(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None, sh_down=None, want_slots=False, hq8=True):
+def moe_layer(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None, sh_down=None, want_slots=False, hq8=True,
+              down_fmt=FMT_IQ2, down_stride=None):
     """Reference MoE layer on arena-layout weights (expert m at m*stride bytes of each arena).
 
     Returns dict(h, moe[, y_slot, shared]).  ids/w: [T, KE] expert ids (arena slots) and weights.
     hq8: re-quantise the SwiGLU output to q8 before the down projection (reference semantics; the
-    tensor-core prefill path keeps it at 16-bit precision: hq8=False)."""
+    tensor-core prefill path keeps it at 16-bit precision: hq8=False).  down_fmt: format of every down
+    matrix (routed and shared); down_stride: the down arena's expert stride (default `stride`)."""
     x = np.ascontiguousarray(x, np.float32)
     resid = np.ascontiguousarray(resid, np.float32)
     ids = np.ascontiguousarray(ids, np.int32)
     w = np.ascontiguousarray(w, np.float32)
     T, KE = ids.shape
-    lw = LayerW(_p(gate).value, _p(up).value, _p(down).value, stride, stride, stride,
+    lw = LayerW(_p(gate).value, _p(up).value, _p(down).value, stride, stride, stride if down_stride is None else down_stride,
                 None if sh_gate is None else _p(sh_gate).value,
                 None if sh_up is None else _p(sh_up).value,
                 None if sh_down is None else _p(sh_down).value)
@@ -160,8 +198,8 @@ def moe_layer(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None
     moe = np.empty((T, HIDDEN), np.float32)
     ys = np.empty((T, KE, HIDDEN), np.float32) if want_slots else None
     sh = np.empty((T, HIDDEN), np.float32) if want_slots else None
-    rc = lib().orc_moe_layer_ex(_p(x), _p(resid), T, ctypes.byref(lw), _p(ids), _p(w), KE, _p(h), _p(moe), _p(ys), _p(sh),
-                                1 if hq8 else 0)
+    rc = lib().orc_moe_layer_fmt(_p(x), _p(resid), T, ctypes.byref(lw), _p(ids), _p(w), KE, _p(h), _p(moe), _p(ys), _p(sh),
+                                 1 if hq8 else 0, down_fmt)
     assert rc == 0
     out = {"h": h, "moe": moe}
     if want_slots:

@@ -12,8 +12,12 @@ independent implementation of the same format and against itself over time:
   router_kat.npz     router outputs (probs, top-8 ids/weights; keep-2 ids/weights; grouped mode) of the
                      oracle on numpy-seeded inputs -- pins routing semantics.
   moe_layer_kat.npz  h / moe of the oracle layer on a small arena (6 experts, T=3) -- pins the layer math.
+  kquant_gguf.npz    Q2_K and Q3_K blocks (seeded, uniform random bytes, and edge blocks with zero /
+                     subnormal / negative / large d and dmin) and their dequantisation by gguf-py 0.19.0
+                     (the Python port of ggml's dequantize_row_q2_K / q3_K), plus the oracle layer with
+                     each K-quant down format on a small arena (4 experts, T=2).
 
-Run from the repository root:  python tests/golden/make_golden.py
+Run from the repository root:  python tests/golden/make_golden.py [name ...]   (no name: every fixture)
 """
 import os
 import sys
@@ -52,9 +56,59 @@ def edge_blocks():
     return np.frombuffer(b"".join(blocks), np.uint8)
 
 
-def main():
+def kquant_blocks(fmt, nb):
+    """Uniform random blocks whose fp16 scale fields walk the edge values (finite only)."""
+    rng = np.random.default_rng(11 + fmt)
+    blocks = rng.integers(0, 256, (48, nb), dtype=np.uint8)
+    ds = [0.0, 1e-3, -2.5e-3, 6.0e-8, 1.0, 65504.0, 3.0517578125e-05, 0.5, -0.75]
+    off = nb - 4 if fmt == O.FMT_Q2K else nb - 2
+    for b in range(48):
+        d = np.float16(ds[b % len(ds)]) if b < 2 * len(ds) else np.float16(rng.standard_normal() * 1e-3)
+        blocks[b, off:off + 2] = np.frombuffer(np.array([d], np.float16).tobytes(), np.uint8)
+        if fmt == O.FMT_Q2K:
+            m = np.float16(ds[(b + 3) % len(ds)]) if b < 2 * len(ds) else np.float16(abs(rng.standard_normal()) * 1e-3)
+            blocks[b, nb - 2:nb] = np.frombuffer(np.array([m], np.float16).tobytes(), np.uint8)
+    return blocks.reshape(-1)
+
+
+def make_kquant():
     from gguf.quants import dequantize
     from gguf import GGMLQuantizationType as QT
+    out = {}
+    for fmt, qt, tag in ((O.FMT_Q2K, QT.Q2_K, "q2k"), (O.FMT_Q3K, QT.Q3_K, "q3k")):
+        nb = O.BLOCK_BYTES[fmt]
+        seeded = O.gen_kq(fmt, SEED, 0, 2, 3, 8, 2048)              # 8 rows x 8 blocks
+        blocks = np.concatenate([kquant_blocks(fmt, nb), seeded])
+        out[tag + "_blocks"] = blocks
+        out[tag + "_dequant"] = dequantize(blocks, qt).reshape(-1).astype(np.float32)
+        NE = 4
+        S = 2048 * 28 * 66
+        DS = 7168 * 8 * nb
+        gate = np.concatenate([O.gen_iq2(SEED, 11, 0, e, 2048, 7168) for e in range(NE)])
+        up = np.concatenate([O.gen_iq2(SEED, 11, 1, e, 2048, 7168) for e in range(NE)])
+        down = np.concatenate([O.gen_kq(fmt, SEED, 11, 2, e, 7168, 2048) for e in range(NE)])
+        shg, shu = O.gen_iq2(SEED, 11, 0, 256, 2048, 7168), O.gen_iq2(SEED, 11, 1, 256, 2048, 7168)
+        shd = O.gen_kq(fmt, SEED, 11, 2, 256, 7168, 2048)
+        rng = np.random.default_rng(77)
+        xs = rng.standard_normal((2, 7168)).astype(np.float32)
+        rs = rng.standard_normal((2, 7168)).astype(np.float32)
+        ids = np.array([[0, 3, 1], [2, 0, 3]], np.int32)
+        wk = rng.uniform(0.1, 1.0, (2, 3)).astype(np.float32)
+        lay = O.moe_layer(xs, rs, gate, up, down, S, ids, wk, shg, shu, shd, down_fmt=fmt, down_stride=DS)
+        out[tag + "_layer_ids"] = ids
+        out[tag + "_layer_w"] = wk
+        out[tag + "_layer_h"] = lay["h"]
+        out[tag + "_layer_moe"] = lay["moe"]
+    np.savez_compressed(os.path.join(HERE, "kquant_gguf.npz"), **out)
+
+
+def main(names):
+    from gguf.quants import dequantize
+    from gguf import GGMLQuantizationType as QT
+    if names == ["kquant"]:
+        make_kquant()
+        print("kquant_gguf.npz written to", HERE)
+        return
 
     seeded = O.gen_iq2(SEED, 0, 0, 3, 8, 7168)            # 8 rows x 28 blocks
     blocks = np.concatenate([edge_blocks(), seeded[: 66 * 64]])
@@ -90,8 +144,9 @@ def main():
     wk = rng.uniform(0.1, 1.0, (T, KE)).astype(np.float32)
     out = O.moe_layer(xs, rs, gate, up, down, S, ids, wk, shg, shu, shd)
     np.savez_compressed(os.path.join(HERE, "moe_layer_kat.npz"), ids=ids, w=wk, h=out["h"], moe=out["moe"])
+    make_kquant()
     print("fixtures written to", HERE)
 
 
 if __name__ == "__main__":
-    main()
+    main(sys.argv[1:])

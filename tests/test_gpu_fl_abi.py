@@ -1,0 +1,88 @@
+"""GPU parity of the engine-facing fused-layer ABI (include/loki_fused_moe.h), driven the way
+src/server_core_fused.cpp drives src/fused_layer.h: fl_moe_prepare -> fl_fetch -> host keep pass ->
+fl_moe (narrow, n <= 8 rows), and fl_moe_prepare(wrow) per group -> fl_wide_moe per arena batch ->
+fl_wide_finish (wide pass).  Host buffers in and out; every down format the ABI accepts."""
+import numpy as np
+import pytest
+
+from moe_helpers import SEED, HIDDEN, RTOL_L2, rel_l2, oracle_layer
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", params=[4, 5, 6], ids=["iq2", "q2k", "q3k"])
+def fl_layer(request, native):
+    from loki_b200 import moe as M
+    fmt = request.param
+    W = M.LayerWeights("cuda", SEED, 5, down_fmt=fmt)
+    torch.cuda.synchronize()
+    yield fmt, W
+    del W
+    torch.cuda.empty_cache()
+
+
+def _mw(native, W, fmt):
+    # fl_moe_prepare's shared expert is IQ2_XXS: with K-quant layers the test runs without it
+    sh = (W.sh_gate, W.sh_up, W.sh_down) if fmt == 4 else (None, None, None)
+    return native.FLMoeW(W.router_w.data_ptr(), 0, W.router_bias.data_ptr(), *sh)
+
+
+@pytest.mark.parametrize("n,KE", [(1, 8), (3, 2), (8, 8)])
+def test_fl_narrow(native, oracle, fl_layer, n, KE):
+    from loki_b200 import fused as F
+    fmt, W = fl_layer
+    rng = np.random.default_rng(n * 10 + KE)
+    x = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    fc = F.FusedCtx()
+    try:
+        fc.prepare(_mw(native, W, fmt), x, r)
+        got = fc.fetch(n, 1)
+        _, osel, ow = oracle.router(x, W.router_w.float().cpu().numpy(), W.router_bias.cpu().numpy(),
+                                    oracle.route_cfg(8, 8, 0))
+        np.testing.assert_array_equal(got["sel"], osel)
+        np.testing.assert_array_equal(got["wts"], ow)
+        ids, w = F.keep_pass(got["sel"], got["wts"], KE)
+        h, mo = fc.moe(W.gate, W.up, W.down, 256, ids, w, down_fmt=fmt)
+        assert fc.error() == 0
+        ref = oracle_layer(oracle, SEED, 5, x, r, ids, w, with_shared=fmt == 4, down_fmt=fmt)
+        assert rel_l2(mo, ref["moe"]) < RTOL_L2
+        assert rel_l2(h, ref["h"]) < RTOL_L2
+    finally:
+        fc.close()
+
+
+def test_fl_wide(native, oracle, fl_layer):
+    from loki_b200 import fused as F
+    fmt, W = fl_layer
+    n, KE = 20, 4
+    rng = np.random.default_rng(2020 + fmt)
+    x = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    fc = F.FusedCtx()
+    try:
+        assert fc.wide_init(32, KE) == 1
+        sel = np.empty((n, 8), np.int32)
+        wts = np.empty((n, 8), np.float32)
+        for g0 in range(0, n, 8):
+            g1 = min(n, g0 + 8)
+            fc.prepare(_mw(native, W, fmt), x[g0:g1], r[g0:g1], wrow=g0)
+            got = fc.fetch(g1 - g0, 1)
+            sel[g0:g1], wts[g0:g1] = got["sel"], got["wts"]
+        ids, w = F.keep_pass(sel, wts, KE)
+        used = sorted(set(int(e) for e in ids.reshape(-1)))
+        for i, (batch, midx, rows, kidx, wk) in enumerate(F.wide_slots(ids, w, KE, used, eb=4)):
+            par = i & 1
+            if i >= 2:
+                fc.wide_wait(par)                     # the engine's order: this parity's tables are free again
+            gmidx = [batch[u] for u in midx]          # resident arenas: global expert ids
+            fc.wide_moe(W.gate, W.up, W.down, 256, gmidx, rows, kidx, wk, KE, par, down_fmt=fmt)
+            fc.wide_mark(par)
+        h, mo = fc.wide_finish(n, KE)
+        assert fc.error() == 0
+        ref = oracle_layer(oracle, SEED, 5, x, r, ids, w, with_shared=fmt == 4, down_fmt=fmt)
+        assert rel_l2(mo, ref["moe"]) < RTOL_L2
+        assert rel_l2(h, ref["h"]) < RTOL_L2
+    finally:
+        fc.close()

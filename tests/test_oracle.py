@@ -246,3 +246,74 @@ def test_moe_layer_kat(oracle):
     out = oracle.moe_layer(xs, rs, gate, up, down, S, f["ids"], f["w"], shg, shu, shd)
     np.testing.assert_array_equal(out["h"], f["h"])
     np.testing.assert_array_equal(out["moe"], f["moe"])
+
+
+# ---------------------------------------------------------------- K-quant down formats (Q2_K, Q3_K)
+KQ = [(5, "q2k", "Q2_K"), (6, "q3k", "Q3_K")]
+
+
+@pytest.mark.parametrize("fmt,tag,name", KQ)
+def test_kq_dequant_matches_gguf_fixture(oracle, fmt, tag, name):
+    f = np.load(os.path.join(GOLD, "kquant_gguf.npz"))
+    out = oracle.kq_dequant(fmt, f[tag + "_blocks"])
+    np.testing.assert_array_equal(out, f[tag + "_dequant"])
+
+
+@pytest.mark.parametrize("fmt,tag,name", KQ)
+def test_kq_dequant_matches_gguf_live(oracle, fmt, tag, name):
+    gguf = pytest.importorskip("gguf")
+    from gguf.quants import dequantize
+    blk = oracle.gen_kq(fmt, SEED, 7, 2, 100, 32, 2048)
+    np.testing.assert_array_equal(oracle.kq_dequant(fmt, blk), dequantize(blk, getattr(gguf.GGMLQuantizationType, name)).reshape(-1))
+
+
+def test_q3k_scale_unpack_matches_kmask_restatement(oracle):
+    """The 6-bit scale unpacking against a word-level restatement of ggml's kmask1/kmask2 shuffle
+    (dequantize_row_q3_K; the reference's q3_scales, fused_layer.cu:34-37)."""
+    rng = np.random.default_rng(21)
+    blk = rng.integers(0, 256, (64, 110), dtype=np.uint8)
+    blk[:, 108:110] = np.frombuffer(np.array([1.0] * 64, np.float16).tobytes(), np.uint8).reshape(64, 2)
+    blk[:, 32:96] = 0x55                        # every low 2-bit field = 1
+    blk[:, 0:32] = 0xFF                         # every high bit set: q = 1
+    deq = oracle.kq_dequant(6, blk.reshape(-1)).reshape(64, 16, 16)
+    for b in range(64):
+        a0, a1, tmp = (int.from_bytes(bytes(blk[b, 96 + 4 * i: 100 + 4 * i]), "little") for i in range(3))
+        aux = [(a0 & 0x0F0F0F0F) | (((tmp >> 0) & 0x03030303) << 4), (a1 & 0x0F0F0F0F) | (((tmp >> 2) & 0x03030303) << 4),
+               ((a0 >> 4) & 0x0F0F0F0F) | (((tmp >> 4) & 0x03030303) << 4), ((a1 >> 4) & 0x0F0F0F0F) | (((tmp >> 6) & 0x03030303) << 4)]
+        sc = [((aux[i // 4] >> (8 * (i % 4))) & 0xFF) - 32 for i in range(16)]
+        np.testing.assert_array_equal(deq[b, :, 0], np.array(sc, np.float32))
+
+
+@pytest.mark.parametrize("fmt,tag,name", KQ)
+def test_kq_matvec_vs_float64(oracle, fmt, tag, name):
+    rng = np.random.default_rng(9)
+    rows, K = 96, 2048
+    W = oracle.gen_kq(fmt, SEED, 2, 2, 9, rows, K)
+    x = rng.standard_normal(K).astype(np.float32)
+    q, d = oracle.quant_q8(x)
+    y = oracle.kq_matvec(fmt, W, rows, K, q, d)
+    Wd = oracle.kq_dequant(fmt, W).reshape(rows, K).astype(np.float64)
+    ref = Wd @ _q8_dequant(oracle, x)
+    assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < 1e-6
+
+
+@pytest.mark.parametrize("fmt,tag,name", KQ)
+def test_kq_moe_layer_kat(oracle, fmt, tag, name):
+    f = np.load(os.path.join(GOLD, "kquant_gguf.npz"))
+    NE, nb = 4, oracle.BLOCK_BYTES[fmt]
+    S, DS = 2048 * 28 * 66, 7168 * 8 * nb
+    gate = np.concatenate([oracle.gen_iq2(SEED, 11, 0, e, 2048, 7168) for e in range(NE)])
+    up = np.concatenate([oracle.gen_iq2(SEED, 11, 1, e, 2048, 7168) for e in range(NE)])
+    down = np.concatenate([oracle.gen_kq(fmt, SEED, 11, 2, e, 7168, 2048) for e in range(NE)])
+    shg, shu = oracle.gen_iq2(SEED, 11, 0, 256, 2048, 7168), oracle.gen_iq2(SEED, 11, 1, 256, 2048, 7168)
+    shd = oracle.gen_kq(fmt, SEED, 11, 2, 256, 7168, 2048)
+    rng = np.random.default_rng(77)
+    xs = rng.standard_normal((2, 7168)).astype(np.float32)
+    rs = rng.standard_normal((2, 7168)).astype(np.float32)
+    out = oracle.moe_layer(xs, rs, gate, up, down, S, f[tag + "_layer_ids"], f[tag + "_layer_w"], shg, shu, shd,
+                           down_fmt=fmt, down_stride=DS)
+    np.testing.assert_array_equal(out["h"], f[tag + "_layer_h"])
+    np.testing.assert_array_equal(out["moe"], f[tag + "_layer_moe"])
+    # the layer's down projection against the dequantised K-quant matrix (float64 restatement)
+    D = oracle.kq_dequant(fmt, down[:DS]).reshape(7168, 2048).astype(np.float64)
+    assert np.isfinite(D).all() and np.abs(D).max() > 0
