@@ -63,6 +63,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     }
 }
 
+// the same wait for roles whose waits are long (a warp that waits hundreds of cycles for another role):
+// between tests the warp sleeps (__nanosleep, doubling from ns0 to 256 ns) instead of re-issuing, so the
+// compute warps of its SM sub-partition keep the issue slots
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, int* err, int code, uint32_t ns0 = 32) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    uint32_t ns = ns0;
+    while (true) {
+        __nanosleep(ns);
+        if (mbar_try_wait(bar, parity)) return true;
+        ns = ns < 256u ? 2u * ns : 256u;
+        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) { if (err) atomicCAS(err, 0, code); return false; }
+    }
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` (src/dst 16-byte aligned, bytes % 16 == 0)
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"

@@ -1,11 +1,12 @@
 // prefill_gemm.cu -- the prefill / batch regime: grouped expert GEMMs on the 5th-generation tensor cores.
 //
 // Replaces the wide pass's tc_matvec<F_IQ2> (mma.sync int8, 8 rows per slot; reference
-// src/fused_layer.cu:540-553) for slots of up to 64 tokens per expert.  Per work item (slot, row tile):
+// src/fused_layer.cu:540-553) for slots of up to 128 tokens per expert.  Per work item (slot, row tile):
 //   D[128 weight rows x N tokens] = A[128 x K] . B[N x K]^T   with tcgen05.mma.cta_group::1.kind::f16,
 //   fp32 accumulators in tensor memory (two tiles per item: gate+up rows, or two 128-row halves of down),
-//   N = the slot's token count rounded up to 16 (up to 128: one tcgen05.mma of M=128, K=16 costs about the
-//   same for any N <= 256, so tokens per instruction are what the tensor pipe's throughput depends on).
+//   N = the slot's token count rounded up to 16 (up to 128).  Measured per tcgen05.mma (M=128, K=16, issued
+//   warp-uniformly): 39 cycles at N=16, 64 at N=128, 128 at N=256 -- the decode of A, not the tensor pipe,
+//   sets the pace for the token counts of a prefill chunk.
 //
 // A (weights) never touches shared memory as fp16: the IQ2_XXS groups are decoded in registers and
 // written to tensor memory with tcgen05.st (thread = weight row = TMEM lane, 32 weights = 16 columns), and
@@ -19,15 +20,20 @@
 // tiles written by the gate/up epilogue (h = silu(g)*u at fp16: with 16-bit operands a q8 re-quantisation
 // would only turn their rounding into q8 boundary flips).  One bulk copy (1-D TMA) per K-block.
 //
-// Warp roles (576 threads, one CTA per SM, persistent over (slot, tile) items):
-//   warps 0-15  decode: warp w = TMEM lane quarter w&3, tile (w>>2)&1, group-in-K-block w>>3; then epilogue
-//   warp 16     MMA issuer (one thread): 8 MMAs per K-block, commit to empty[], accfull per item
-//   warp 17     copies: each weight row's next IQ2 superblock, as the 80-byte 16-aligned window around it,
-//               into a raw ring (16-byte cp.async, 6 rows per instruction, coalesced); B K-block tiles into
-//               the B ring (1-D TMA bulk copies)
+// Warp roles (608 threads, one CTA per SM, persistent over (slot, tile) items); one pipeline stage is a
+// 128-deep K-block (4 IQ2 groups), two stages in flight:
+//   warps 0-15  decode: warp w = TMEM lane quarter w&3, tile (w>>2)&1, groups 2(w>>3), 2(w>>3)+1 of each
+//               K-block (two independent decode chains per thread); then the epilogue
+//   warp 16     MMA issuer (the whole warp on warp-uniform operands, elect.sync issues): 16 MMAs per K-block,
+//               commit to empty[], accfull per item
+//   warp 17     B K-block tiles into the B ring (1-D TMA bulk copies), one thread
+//   warp 18     raw superblocks: each weight row's next IQ2 superblock, as the 80-byte 16-aligned window around
+//               it, into a 3-stage raw ring (16-byte cp.async, 6 rows per instruction, coalesced), up to three
+//               superblocks ahead of the decode warps whatever the B stages do
 // Barriers: rawfull/rawempty (raw ring), full/empty (A stage in TMEM + B stage in shared memory),
 // accfull/accempty (the accumulators; the decode warps run the epilogue, so a second accumulator buffer
-// would not let the MMA run ahead).  Every wait is bounded (moe_device.cuh).
+// would not let the MMA run ahead).  Every wait is bounded (moe_device.cuh); the waits of every role back
+// off with __nanosleep so a waiting warp leaves the issue slots to the decode warps.
 #include "moe_internal.h"
 #include "moe_device.cuh"
 #include "tcgen05.cuh"
@@ -36,13 +42,14 @@ namespace lk {
 
 constexpr int PG_M = 128;                    // weight rows per accumulator tile
 constexpr int PG_NMAX = GEMM_NT;             // tokens per slot (128)
-constexpr int PG_KB = 64;                    // K per pipeline stage
-constexpr int PG_NST = 4;                    // A (TMEM) / B (smem) stages
+constexpr int PG_KB = 128;                   // K per pipeline stage: 4 IQ2 groups, half a superblock
+constexpr int PG_NST = 2;                    // A (TMEM) / B (smem) stages
 constexpr int PG_DWARPS = 16;
 constexpr int PG_MMA_WARP = PG_DWARPS;
-constexpr int PG_COPY_WARP = PG_DWARPS + 1;
-constexpr int PG_THREADS = (PG_DWARPS + 2) * 32;
-constexpr int PG_B_TILE = PG_NMAX * PG_KB * 2;           // 16 KB: one K-block of B at N = 128
+constexpr int PG_COPY_WARP = PG_DWARPS + 1;  // B tiles
+constexpr int PG_RAW_WARP = PG_DWARPS + 2;   // raw superblocks
+constexpr int PG_THREADS = (PG_DWARPS + 3) * 32;
+constexpr int PG_B_TILE = PG_NMAX * PG_KB * 2;           // 32 KB: one K-block of B at N = 128
 constexpr int PG_RAW_ROWB = 80;                          // one superblock (66 B) in its 16-aligned 80-byte window
 constexpr int PG_RAW_STAGE = 2 * PG_M * PG_RAW_ROWB;     // 256 weight rows: 20 KB
 constexpr int PG_RAW_NST = 3;
@@ -54,7 +61,7 @@ constexpr int PG_OFF_B = PG_OFF_STAB + PG_STAB;
 constexpr int PG_OFF_RAW = PG_OFF_B + PG_NST * PG_B_TILE;
 constexpr int PG_OFF_BAR = PG_OFF_RAW + PG_RAW_NST * PG_RAW_STAGE + 64;   // + slack for the last row's over-read
 constexpr int PG_NBAR = 2 * PG_NST + 2 + 2 + 1 + 2 * PG_RAW_NST;
-constexpr int PG_OFF_ROWP = PG_OFF_BAR + PG_NBAR * 8;          // copy warp: the current item's 256 row addresses
+constexpr int PG_OFF_ROWP = PG_OFF_BAR + PG_NBAR * 8;          // raw copy warp: the current item's 256 row addresses
 constexpr int PG_OFF_MISC = PG_OFF_ROWP + 2 * PG_M * 8;
 constexpr int PG_SMEM_USED = PG_OFF_MISC + 32;
 // the whole 227 KB is reserved: one CTA per SM (it allocates all 512 tensor-memory columns), and every
@@ -63,7 +70,7 @@ constexpr int PG_SMEM = 232448;
 static_assert(PG_SMEM_USED <= PG_SMEM, "shared memory layout exceeds the allocation");
 constexpr uint32_t PG_TMEM_COLS = 512;
 constexpr uint32_t PG_ACC_COLS = 2 * PG_NMAX;             // 256: 2 tiles x 128 fp32 columns
-constexpr uint32_t PG_A_COLS = 2 * (PG_KB / 2);          // 64 per stage: 2 tiles x 32 columns (64 fp16)
+constexpr uint32_t PG_A_COLS = 2 * (PG_KB / 2);          // 128 per stage: 2 tiles x 64 columns (128 fp16)
 static_assert(PG_ACC_COLS + PG_NST * PG_A_COLS <= PG_TMEM_COLS, "tensor memory layout");
 constexpr uint32_t F16_PAIR_LO = 0x642B1908u;            // bytes 08 19 2B 64
 constexpr uint32_t F16_PAIR_HI = 0x63AACEF0u;            // bytes F0 CE AA 63
@@ -207,90 +214,98 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == PG_COPY_WARP) {
-        // ---------------------------------------------------------------- raw superblocks + B tiles
-        uint32_t rit = 0, it = 0;
+    if (warp == PG_RAW_WARP) {
+        // ---------------------------------------------------------------- raw superblocks (2 stages of K each)
+        // runs up to PG_RAW_NST superblocks ahead of the decode warps, independently of the B stages
+        uint32_t rit = 0;
         for (int item = blockIdx.x; item < nitems && !*abort_flag; item += gridDim.x) {
             const int s = item % nslots, rt = item / nslots;
             const int e = p.slot_expert[s];
-            const int n16 = round16(p.slot_cnt[s]);
             __syncwarp();
             for (int r = lane; r < 2 * PG_M; r += 32) rowp[r] = (uintptr_t)item_row<DOWN>(p, e, rt, r, rowbytes);
             __syncwarp();
-            for (int kb = 0; kb < NKB; ++kb, ++it) {
-                if ((kb & 3) == 0) {
-                    const int sb = kb >> 2, rs = rit % PG_RAW_NST;
-                    if (!mbar_wait(&rawempty[rs], ((rit / PG_RAW_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
-                    uint8_t* dst = raw + rs * PG_RAW_STAGE;
-                    const size_t sboff = (size_t)sb * BLK_IQ2;
-                    if (lane < 30) {                  // lane -> (row rsub of 6, 16-byte chunk of 5)
-                        const int rsub = lane / 5, chunk = lane - 5 * rsub;
-                        #pragma unroll 4
-                        for (int r = rsub; r < 2 * PG_M; r += 6) {
-                            const uintptr_t a = (rowp[r] + sboff) & ~(uintptr_t)15;
-                            cp_async16(dst + r * PG_RAW_ROWB + chunk * 16, (const void*)(a + 16 * chunk));
-                        }
+            for (int sb = 0; sb < K / QK; ++sb, ++rit) {
+                const int rs = rit % PG_RAW_NST;
+                if (!mbar_wait_backoff(&rawempty[rs], ((rit / PG_RAW_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
+                uint8_t* dst = raw + rs * PG_RAW_STAGE;
+                const size_t sboff = (size_t)sb * BLK_IQ2;
+                if (lane < 30) {                      // lane -> (row rsub of 6, 16-byte chunk of 5)
+                    const int rsub = lane / 5, chunk = lane - 5 * rsub;
+                    #pragma unroll 4
+                    for (int r = rsub; r < 2 * PG_M; r += 6) {
+                        const uintptr_t a = (rowp[r] + sboff) & ~(uintptr_t)15;
+                        cp_async16(dst + r * PG_RAW_ROWB + chunk * 16, (const void*)(a + 16 * chunk));
                     }
-                    cp_async_mbar_arrive(&rawfull[rs]);
-                    ++rit;
                 }
-                const int st = it % PG_NST;
-                if (!mbar_wait(&empty[st], ((it / PG_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
-                if (lane == 0) {
+                cp_async_mbar_arrive(&rawfull[rs]);
+            }
+        }
+        cp_async_wait_all();
+    } else if (warp == PG_COPY_WARP) {
+        // ---------------------------------------------------------------- B tiles (one bulk copy per K-block)
+        uint32_t it = 0;
+        if (lane == 0) {
+            for (int item = blockIdx.x; item < nitems && !*abort_flag; item += gridDim.x) {
+                const int s = item % nslots;
+                const int n16 = round16(p.slot_cnt[s]);
+                for (int kb = 0; kb < NKB; ++kb, ++it) {
+                    const int st = it % PG_NST;
+                    if (!mbar_wait_backoff(&empty[st], ((it / PG_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
                     const uint32_t bytes = (uint32_t)n16 * PG_KB * 2;
                     mbar_arrive_expect_tx(&full[st], bytes);
                     bulk_g2s(bring + st * PG_B_TILE, btiles + ((size_t)s * NKB + kb) * (PG_B_TILE / 2), bytes, &full[st]);
                 }
             }
+            // every bulk copy issued must land before the CTA may exit
+            const uint32_t first = it > PG_NST ? it - PG_NST : 0;
+            for (uint32_t j = first; j < it; ++j) mbar_wait_backoff(&full[j % PG_NST], (j / PG_NST) & 1, nullptr, 0);
         }
-        {   // every bulk copy issued must land before the CTA may exit
-            __syncwarp();
-            if (lane == 0) {
-                const uint32_t first = it > PG_NST ? it - PG_NST : 0;
-                for (uint32_t j = first; j < it; ++j) mbar_wait(&full[j % PG_NST], (j / PG_NST) & 1, nullptr, 0);
-            }
-        }
-        cp_async_wait_all();
     } else if (warp == PG_MMA_WARP) {
-        // ---------------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            uint32_t it = 0; int issued = 0;
-            const uint32_t bring_s = smem_u32(bring);
-            for (int i = 0, item = blockIdx.x; item < nitems && !*abort_flag; ++i, item += gridDim.x) {
-                const int s = item % nslots;
-                const int N = round16(p.slot_cnt[s]);
-                const uint32_t idesc = idesc_f16_f32(PG_M, N);
-                const uint32_t lbo = (uint32_t)(N >> 3) * 128;
-                if (i >= 1 && !mbar_wait(accempty, (i - 1) & 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
+        // ---------------------------------------------------------------- MMA issuer (the whole warp, elect.sync)
+        // every lane runs the loop on the same values (broadcast from lane 0 where they come from memory), so
+        // the operands are warp-uniform; each decision after a bounded wait is taken by the whole warp
+        uint32_t it = 0; int issued = 0;
+        const uint32_t bring_s = smem_u32(bring);
+        for (int i = 0, item = blockIdx.x; item < nitems; ++i, item += gridDim.x) {
+            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
+            const int s = item % nslots;
+            const int N = __shfl_sync(0xffffffffu, round16(p.slot_cnt[s]), 0);
+            const uint32_t idesc = idesc_f16_f32(PG_M, N);
+            const uint32_t lbo = (uint32_t)(N >> 3) * 128;
+            if (i >= 1 && !__all_sync(0xffffffffu, mbar_wait_backoff(accempty, (i - 1) & 1, p.err, DEV_ERR_TIMEOUT_EMPTY))) {
+                if (lane == 0) *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d0 = tmem, d1 = d0 + PG_NMAX;
+            const uint64_t bstep = (uint64_t)((2 * lbo) >> 4);             // one K=16 step along the B tile
+            bool ok = true;
+            for (int kb = 0; kb < NKB; ++kb, ++it) {
+                const int st = it % PG_NST;
+                if (!__all_sync(0xffffffffu, mbar_wait_backoff(&full[st], (it / PG_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d0 = tmem, d1 = d0 + PG_NMAX;
-                const uint64_t bstep = (uint64_t)((2 * lbo) >> 4);             // one K=16 step along the B tile
-                for (int kb = 0; kb < NKB; ++kb, ++it) {
-                    const int st = it % PG_NST;
-                    if (!mbar_wait(&full[st], (it / PG_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
-                    tc_fence_after();
-                    const uint64_t b0 = umma_desc(bring_s + st * PG_B_TILE, lbo, 128);
-                    const uint32_t a0 = tmem + PG_ACC_COLS + st * PG_A_COLS, a1 = a0 + PG_A_COLS / 2;
-                    #pragma unroll
-                    for (int ks = 0; ks < PG_KB / 16; ++ks) {
-                        const uint64_t bd = b0 + (uint64_t)ks * bstep;
-                        umma_f16_ta(d0, a0 + ks * 8, bd, idesc, (kb | ks) != 0);
-                        umma_f16_ta(d1, a1 + ks * 8, bd, idesc, (kb | ks) != 0);
-                    }
-                    umma_commit(&empty[st]);
-                    issued = 1;
+                const uint64_t b0 = umma_desc(bring_s + st * PG_B_TILE, lbo, 128);
+                const uint32_t a0 = tmem + PG_ACC_COLS + st * PG_A_COLS, a1 = a0 + PG_A_COLS / 2;
+                #pragma unroll
+                for (int ks = 0; ks < PG_KB / 16; ++ks) {
+                    const uint64_t bd = b0 + (uint64_t)ks * bstep;
+                    umma_f16_ta_warp(d0, a0 + ks * 8, bd, idesc, (kb | ks) != 0);
+                    umma_f16_ta_warp(d1, a1 + ks * 8, bd, idesc, (kb | ks) != 0);
                 }
-                if (*abort_flag) break;
-                umma_commit(accfull);
+                umma_commit_warp(&empty[st]);
+                issued = 1;
             }
-            if (issued) {                             // every issued MMA has completed before teardown
-                umma_commit(drain);
-                mbar_wait(drain, 0, nullptr, 0);
-            }
+            if (!ok) { if (lane == 0) *abort_flag = 1; break; }
+            umma_commit_warp(accfull);
+        }
+        if (issued) {                                 // every issued MMA has completed before teardown
+            umma_commit_warp(drain);
+            mbar_wait_backoff(drain, 0, nullptr, 0);
         }
     } else {
         // ---------------------------------------------------------------- decode warps, then epilogue
-        const int q = warp & 3, mat = (warp >> 2) & 1, grp = warp >> 3;
+        // warp w: TMEM lane quarter q = w & 3 (its rows), tile mat, groups 2gp, 2gp + 1 of every K-block
+        const int q = warp & 3, mat = (warp >> 2) & 1, gp = warp >> 3;
         const int row = 32 * q + lane;                                      // weight row in tile `mat` = TMEM lane
         const uint2* gtl = gtab + lane;
         const uint2* stl = stab + lane;
@@ -303,32 +318,37 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
             const uintptr_t wrow = (uintptr_t)item_row<DOWN>(p, e, rt, mat * PG_M + row, rowbytes);   // global row
             for (int kb = 0; kb < NKB; ++kb, ++it) {
                 const int st = it % PG_NST, rs = rit % PG_RAW_NST;
-                if ((kb & 3) == 0 && !*abort_flag && !mbar_wait(&rawfull[rs], (rit / PG_RAW_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))
+                if ((kb & 1) == 0 && !*abort_flag && !mbar_wait_backoff(&rawfull[rs], (rit / PG_RAW_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))
                     *abort_flag = 1;
                 // the superblock sits `delta` (0..14) bytes into its staged 16-aligned window
                 const uint8_t* rrow = rrow0 + rs * PG_RAW_STAGE;
-                const int delta = (int)((wrow + (uintptr_t)(kb >> 2) * BLK_IQ2) & 15u);
-                uint32_t aux0, aux1;
-                load_group_smem(rrow, delta + 2 + 8 * ((kb & 3) * 2 + grp), aux0, aux1);
+                const int delta = (int)((wrow + (uintptr_t)(kb >> 1) * BLK_IQ2) & 15u);
+                const int g0 = (kb & 1) * 4 + 2 * gp;                      // first of this thread's groups in the superblock
+                uint32_t aux0a, aux1a, aux0b, aux1b;
+                load_group_smem(rrow, delta + 2 + 8 * g0, aux0a, aux1a);
+                load_group_smem(rrow, delta + 10 + 8 * g0, aux0b, aux1b);
                 const float d = __half2float(*(const __half*)(rrow + delta));
-                uint32_t o[16];
-                decode_group_f16(aux0, aux1, d, gtl, stl, o);
-                if (!*abort_flag && !mbar_wait(&empty[st], ((it / PG_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) *abort_flag = 1;
+                uint32_t oa[16], ob[16];
+                decode_group_f16(aux0a, aux1a, d, gtl, stl, oa);
+                decode_group_f16(aux0b, aux1b, d, gtl, stl, ob);
+                if (!*abort_flag && !mbar_wait_backoff(&empty[st], ((it / PG_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) *abort_flag = 1;
                 tc_fence_after();
-                tmem_st16(tmem + lane_base + PG_ACC_COLS + st * PG_A_COLS + mat * (PG_A_COLS / 2) + grp * 16, o);
+                const uint32_t ta = tmem + lane_base + PG_ACC_COLS + st * PG_A_COLS + mat * (PG_A_COLS / 2) + gp * 32;
+                tmem_st16(ta, oa);
+                tmem_st16(ta + 16, ob);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&full[st]);
-                    if ((kb & 3) == 3) mbar_arrive(&rawempty[rs]);
+                    if (kb & 1) mbar_arrive(&rawempty[rs]);
                 }
-                if ((kb & 3) == 3) ++rit;
+                if (kb & 1) ++rit;
                 if (*abort_flag) break;
             }
             if (*abort_flag) break;
             // ------------------------------------------------ epilogue of item i
-            if (!mbar_wait(accfull, i & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
+            if (!mbar_wait_backoff(accfull, i & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
             tc_fence_after();
             const int cnt = p.slot_cnt[s], n16 = round16(cnt);
             for (int cc = warp >> 2; cc * 16 < cnt; cc += 4) {              // tokens 16cc..16cc+15
@@ -348,8 +368,8 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
                             p.y[(size_t)out * HIDDEN + r0 + PG_M] = w * v1[j];
                         } else {                          // h = silu(g)*u -> the down GEMM's B tile of this slot
                             const int hj = rt * PG_M + row;
-                            __half* tile = p.ht + ((size_t)s * (MOE_INTER / PG_KB) + (hj >> 6)) * (PG_B_TILE / 2);
-                            *(__half*)((uint8_t*)tile + btile_off(n, hj & 63, n16)) = __float2half_rn(lk_swiglu(v0[j], v1[j]));
+                            __half* tile = p.ht + ((size_t)s * (MOE_INTER / PG_KB) + hj / PG_KB) * (PG_B_TILE / 2);
+                            *(__half*)((uint8_t*)tile + btile_off(n, hj % PG_KB, n16)) = __float2half_rn(lk_swiglu(v0[j], v1[j]));
                         }
                     }
                 }
@@ -366,12 +386,13 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
 
 // gate/up B tiles: for slot s and K-block kb, the fp16 of the q8-dequantised x of the slot's tokens in the
 // UMMA K-major core-matrix layout of round16(count) rows (pad rows zero); also the slot's token count
-__global__ void __launch_bounds__(2 * PG_NMAX) k_gate_b_tiles(GemmParams p) {
+constexpr int PG_BT_THREADS = PG_NMAX * (PG_KB / 32);   // one thread per (token row, 32-group of the K-block)
+__global__ void __launch_bounds__(PG_BT_THREADS) k_gate_b_tiles(GemmParams p) {
     const int s = blockIdx.x, kb = blockIdx.y, tid = threadIdx.x;
     if (s >= *p.nslots) return;
-    const int n = tid >> 1, g = tid & 1;                 // token row, 32-group within the K-block
+    const int n = tid / (PG_KB / 32), g = tid % (PG_KB / 32);   // token row, 32-group within the K-block
     const int tok = p.slot_tok[s * PG_NMAX + n];
-    const int cnt = __syncthreads_count(tok >= 0) / 2;   // pads are at the end of the slot
+    const int cnt = __syncthreads_count(tok >= 0) / (PG_KB / 32);   // pads are at the end of the slot
     if (kb == 0 && tid == 0) p.slot_cnt[s] = cnt;
     const int n16 = round16(cnt);
     if (n >= n16) return;
@@ -407,7 +428,7 @@ template <bool DOWN> static void pg_launch(const GemmParams& p, int grid, cudaSt
 }
 
 void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st) {
-    k_gate_b_tiles<<<dim3(p.max_slots, HIDDEN / PG_KB), 2 * PG_NMAX, 0, st>>>(p);
+    k_gate_b_tiles<<<dim3(p.max_slots, HIDDEN / PG_KB), PG_BT_THREADS, 0, st>>>(p);
     pg_launch<false>(p, grid, st);
     pg_launch<true>(p, grid, st);
 }

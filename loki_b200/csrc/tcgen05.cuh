@@ -52,6 +52,22 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  :: "r"(smem_u32(bar)) : "memory");
 }
 
+// ---- warp-level issue: the whole (converged) warp executes these with identical operands and elect.sync
+// lets one lane issue.  Measured on B200: a lone thread issuing with operands in ordinary registers pays
+// ~110-200 cycles per tcgen05.mma whatever the shape, while warp-uniform issue runs at the tensor pipe's
+// rate (M=128: 39 cycles at N=16, 64 at N=128, 128 at N=256 for kind::f16).
+// D[tmem] (+)= A[tmem] x B[smem]^T, one 16-deep K step
+__device__ __forceinline__ void umma_f16_ta_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\telect.sync _|e, 0xffffffff;\n\t"
+                 "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+                 :: "r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void umma_commit_warp(uint64_t* bar) {
+    asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+                 "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+                 :: "r"(smem_u32(bar)) : "memory");
+}
+
 // ---- tensor memory -> registers: 32 lanes x 16 consecutive 32-bit columns (thread i <- lane base+i)
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
