@@ -95,6 +95,7 @@ constexpr int G1_OFF_RED = G1_OFF_RING + G1_CPT * G1_CBYTES;
 constexpr int G1_OFF_BAR = G1_OFF_RED + 2 * G1_NS * G1_SW * 32 * 4;
 constexpr int G1_OFF_ABORT = G1_OFF_BAR + 2 * G1_CPT * 8;
 constexpr int G1_SMEM = G1_OFF_ABORT + 16;
+static_assert(G1_SMEM <= 232448, "gate/up shared-memory layout exceeds the 227 KB a CTA can have");
 
 __global__ void __launch_bounds__(G1_THREADS, 1) k_gate_up1(ExpertParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
