@@ -25,13 +25,45 @@ def _view(addr, n, dtype):
     return np.ctypeslib.as_array(ctypes.cast(addr, ctypes.POINTER(ct)), shape=(n,))
 
 
-def keep_pass(sel, wts, KE, renorm=True, scale=2.5):
-    """The engine's keep-KE compaction (src/server_core_fused.cpp:793-813) on host arrays [n][8]."""
+def keep_pass(sel, wts, KE, renorm=True, scale=2.5, share=False, n_pad_from=None):
+    """The engine's keep-KE compaction (src/server_core_fused.cpp:793-813) on host arrays [n][8]: each row's
+    experts ordered by weight (descending; equal weights keep their position), the first KE kept, and with
+    renorm their weights rescaled to sum to `scale`.
+
+    share: the engine's --share-experts variant (server_core_fused.cpp:799-807), for n > 1 rows: every row
+    keeps its own top min(2, KE); its remaining slots take, in weight order, experts that the set U already
+    holds, then the highest-weight rest, each of which joins U.  U starts as the own top experts of the rows
+    before n_pad_from (the engine's N_PAD_FROM; default every row).  The choice of a row depends on the rows
+    beside it, so the engine turns it off for fixed-width passes; callers decide likewise."""
+    sel = np.asarray(sel)
+    wts = np.asarray(wts, np.float32)
+    n = sel.shape[0]
     if KE >= sel.shape[1]:
         return sel.astype(np.int32), wts.astype(np.float32)
-    order = np.argsort(-wts, axis=1, kind="stable")[:, :KE]
-    s = np.take_along_axis(sel, order, 1).astype(np.int32)
-    w = np.take_along_axis(wts, order, 1).astype(np.float32)
+    order = np.argsort(-wts, axis=1, kind="stable")
+    if share and n > 1:
+        own = min(2, KE)
+        npf = n if n_pad_from is None else min(n, n_pad_from)
+        U = {int(sel[i, order[i, k]]) for i in range(npf) for k in range(own)}
+        idx = np.empty((n, KE), np.int64)
+        for i in range(n):
+            pick = [int(order[i, k]) for k in range(own)]
+            for k in range(own, sel.shape[1]):
+                if len(pick) >= KE:
+                    break
+                if int(sel[i, order[i, k]]) in U:
+                    pick.append(int(order[i, k]))
+            for k in range(own, sel.shape[1]):
+                if len(pick) >= KE:
+                    break
+                if int(order[i, k]) not in pick:
+                    pick.append(int(order[i, k]))
+                    U.add(int(sel[i, order[i, k]]))
+            idx[i] = pick
+    else:
+        idx = order[:, :KE]
+    s = np.take_along_axis(sel, idx, 1).astype(np.int32)
+    w = np.take_along_axis(wts, idx, 1).astype(np.float32)
     if renorm:
         sw = np.zeros(w.shape[0], np.float32)
         for k in range(KE):
@@ -39,6 +71,26 @@ def keep_pass(sel, wts, KE, renorm=True, scale=2.5):
         f = np.where(sw > 1e-6, np.float32(scale) / np.where(sw > 1e-6, sw, 1), 1).astype(np.float32)
         w = (w * f[:, None]).astype(np.float32)
     return s, w
+
+
+def pad_rows(sel, w, n_pad_from):
+    """The engine's pad rows (src/server_core_fused.cpp:815): rows from n_pad_from on take row 0's experts at
+    weight 0, so a fixed-width pass computes them without changing any output."""
+    sel = np.array(sel, np.int32, copy=True)
+    w = np.array(w, np.float32, copy=True)
+    sel[n_pad_from:] = sel[0]
+    w[n_pad_from:] = 0.0
+    return sel, w
+
+
+def union_remap(sel):
+    """The engine's expert union and slot remap (src/server_core_fused.cpp:816-818): the sorted distinct
+    expert ids of the pass (the arena's load list) and every entry's index into it (fl_moe's ids)."""
+    sel = np.asarray(sel, np.int32)
+    used = np.unique(sel)
+    remap = np.full(256, -1, np.int32)
+    remap[used] = np.arange(len(used), dtype=np.int32)
+    return used.astype(np.int32), remap[sel]
 
 
 class FusedCtx:

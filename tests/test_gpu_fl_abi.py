@@ -28,8 +28,8 @@ def _mw(native, W, fmt):
     return native.FLMoeW(W.router_w.data_ptr(), 0, W.router_bias.data_ptr(), *sh)
 
 
-@pytest.mark.parametrize("n,KE", [(1, 8), (3, 2), (8, 8)])
-def test_fl_narrow(native, oracle, fl_layer, n, KE):
+@pytest.mark.parametrize("n,KE,share", [(1, 8, False), (3, 2, False), (8, 8, False), (8, 3, True)])
+def test_fl_narrow(native, oracle, fl_layer, n, KE, share):
     from loki_b200 import fused as F
     fmt, W = fl_layer
     rng = np.random.default_rng(n * 10 + KE)
@@ -43,7 +43,7 @@ def test_fl_narrow(native, oracle, fl_layer, n, KE):
                                     oracle.route_cfg(8, 8, 0))
         np.testing.assert_array_equal(got["sel"], osel)
         np.testing.assert_array_equal(got["wts"], ow)
-        ids, w = F.keep_pass(got["sel"], got["wts"], KE)
+        ids, w = F.keep_pass(got["sel"], got["wts"], KE, share=share)
         h, mo = fc.moe(W.gate, W.up, W.down, 256, ids, w, down_fmt=fmt)
         assert fc.error() == 0
         ref = oracle_layer(oracle, SEED, 5, x, r, ids, w, with_shared=fmt == 4, down_fmt=fmt)
