@@ -609,41 +609,36 @@ def run_imbalance(args, ws, rank, local, dist):
 
 
 def e2e_decode(args, layers, distinct, keep):
-    """Decode through the engine-facing fl_* ABI with host buffers: per layer fl_moe_prepare (H2D x/resid,
-    router, shared expert) -> fl_fetch (D2H sel/wts/ncur/fi) -> host keep pass -> fl_moe (D2H h, moe).
-    Wall clock; every copy and host synchronisation is inside the timed region."""
+    """Decode through the engine-facing fl_* ABI with host buffers, driven from C++ the way the engine drives
+    it (libloki_replay.so lkr_decode): per layer fl_moe_prepare (H2D x/resid, router, shared expert) ->
+    fl_moe_auto (keep pass on the device, experts, combine, D2H h/moe).  The engine's unchanged sequence
+    (fl_fetch -> host keep pass -> fl_moe) is timed beside it.  Wall clock; every copy and host
+    synchronisation is inside the timed region."""
     from loki_b200 import fused as F
-    from loki_b200 import native as N
-    fc = F.FusedCtx()
     rng = np.random.default_rng(77)
     xs = rng.standard_normal((args.layers, 1, HIDDEN)).astype(np.float32)
     rs = rng.standard_normal((args.layers, 1, HIDDEN)).astype(np.float32)
-    mws = []
-    for l in layers:
-        mws.append(N.FLMoeW(l.router_w.data_ptr(), 0, l.router_bias.data_ptr(), l.sh_gate, l.sh_up, l.sh_down))
-
-    def one_step():
-        for i in range(args.layers):
-            lw = layers[i % distinct]
-            fc.prepare(mws[i % distinct], xs[i], rs[i])
-            r = fc.fetch(1, 1)
-            ids, w = F.keep_pass(r["sel"], r["wts"], keep)
-            fc.moe(lw.gate, lw.up, lw.down, NE, ids, w)
-
-    for _ in range(max(1, args.warmup)):
-        one_step()
+    per_layer = [layers[i % distinct] for i in range(args.layers)]
     n = max(1, args.steps // 2)
-    t0 = time.perf_counter()
-    for _ in range(n):
-        one_step()
-    dt = time.perf_counter() - t0
-    err = fc.error()
-    fc.close()
-    h2d = args.layers * (2 * HIDDEN * 4 + keep * 8)
-    d2h = args.layers * (8 * 8 + 2 * HIDDEN * 4 + 2 * HIDDEN * 4)
-    return {"value": round(n / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "path": "fl_moe_prepare -> fl_fetch -> host keep pass -> fl_moe (pinned host mirrors, wall clock)",
-            "steps": n, "error": err}
+    out = {}
+    for device_keep in (True, False):
+        fc = F.FusedCtx()
+        try:
+            sec, _ = F.replay_decode(fc, per_layer, xs, rs, keep, max(1, args.warmup), n, device_keep=device_keep)
+            out[device_keep] = (round(n / sec, 2), fc.error())
+        finally:
+            fc.close()
+    h2d = args.layers * (2 * HIDDEN * 4)
+    d2h = args.layers * (2 * HIDDEN * 4 + keep * 8)
+    return {"value": out[True][0], "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "C++ engine replay (libloki_replay.so): fl_moe_prepare -> fl_moe_auto per layer (pinned host mirrors, "
+                    "wall clock)",
+            "engine_sequence": {"value": out[False][0], "unit": "tokens/s",
+                                "path": "fl_moe_prepare -> fl_fetch -> host keep pass -> fl_moe per layer (the engine's calls "
+                                        "unchanged)",
+                                "h2d_bytes_per_step": args.layers * (2 * HIDDEN * 4 + keep * 8),
+                                "d2h_bytes_per_step": args.layers * (8 * 8 + 2 * HIDDEN * 4 + 2 * HIDDEN * 4)},
+            "steps": n, "error": out[True][1] | out[False][1]}
 
 
 def run_prefill(args, ws, rank, local, dist):

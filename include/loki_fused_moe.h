@@ -22,6 +22,9 @@
  * Additive (no counterpart: it is the MoE half of fl_attn, src/fused_layer.cu:506-525):
  *   fl_moe_prepare   router + shared expert on the rows' normalised hidden state `ncur` with residual
  *                    `ffn_inp`; leaves the context as fl_attn does for the MoE calls that follow.
+ * Additive (no counterpart: the engine's host routing post-pass, src/server_core_fused.cpp:793-818, done on
+ * the device):
+ *   fl_moe_auto      fl_fetch + host keep pass + fl_moe in one call, without the routing round trip.
  *
  * Behaviour kept from the reference: host arrays (ids, w, slot tables) are copied before the call
  * returns; FLOut points into library-owned pinned mirrors valid until the next call on the context;
@@ -90,6 +93,17 @@ LK_API double fl_gpu_ms(FLCtx* c, int which);
  * device pointers (host = 0).  wrow >= 0: these rows are rows wrow.. of a wide pass (their ncur and
  * ffn_inp + shared output go to the pass-wide buffers, as fl_attn's wrow does). */
 LK_API void   fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow);
+/* additive: the narrow pass for the first n <= 8 rows of the last fl_moe_prepare, routed on the device from
+ * that call's router output: each row's KE highest-weight experts (equal weights in position order; renorm = 1
+ * rescales them to sum to 2.5), as global expert ids into a 256-expert resident arena.  Results as fl_moe (h,
+ * moe; fl_moe_outs sees this routing).  The engine's --share-experts choice depends on the rows beside each
+ * other and stays on the host path (fl_fetch + keep pass + fl_moe). */
+LK_API void   fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int renorm, int n,
+                          FLOut* out);
+/* additive: fl_moe_prepare, fl_moe and fl_moe_auto replay a CUDA graph for every call shape (weights, row
+ * count, KE, format) seen before -- captured on its second occurrence -- instead of issuing their launches and
+ * copies one by one (default on; enable = 0 issues them directly).  The results are the same either way. */
+LK_API void   fl_use_graphs(FLCtx* c, int enable);
 /* additive: last error recorded on the context (0 = none), cleared by the call */
 LK_API int    fl_moe_error(FLCtx* c);
 LK_API void   fl_free(FLCtx* c);

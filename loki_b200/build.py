@@ -16,6 +16,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libloki_moe.so")
+# the engine-side replay harness (csrc/fl_replay.cpp): plain C++ against the fl_* ABI of LIB
+REPLAY_SRC = os.path.join(CSRC, "fl_replay.cpp")
+REPLAY_LIB = os.path.join(HERE, "libloki_replay.so")
 SOURCES = ["expert_gemv.cu", "expert_gemv1.cu", "aux_kernels.cu", "router.cu", "dispatch.cu", "prefill_gemm.cu", "moe_api.cu", "fl_abi.cu", "noalloc.cu", "ep.cu", "ep_comm.cu", "slot_mma.cu", "ep_p2p.cu", "expert_kq.cu"]
 HEADERS = ["moe_format.h", "moe_device.cuh", "moe_internal.h", "tcgen05.cuh", "iq2_grid.inc",
            os.path.join("..", "..", "include", "loki_moe.h"), os.path.join("..", "..", "include", "loki_fused_moe.h"),
@@ -69,6 +72,13 @@ def build(force=False, verbose=False, ptxas_verbose=False):
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)
             raise RuntimeError("link failed")
+    if force or _stale(REPLAY_LIB, [REPLAY_SRC, LIB, os.path.join(CSRC, "..", "..", "include", "loki_fused_moe.h")]):
+        cmd = [host_cxx(), "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden", "-o", REPLAY_LIB, REPLAY_SRC,
+               "-L" + HERE, "-lloki_moe", "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise RuntimeError("replay harness build failed")
     return LIB
 
 

@@ -9,6 +9,7 @@
 #include <cstdlib>
 #include <vector>
 #include <algorithm>
+#include <functional>
 #include "../../include/loki_fused_moe.h"
 #include "../../include/loki_moe.h"
 #include "moe_internal.h"
@@ -31,7 +32,7 @@ struct FLCtx {
     int *s_expert = nullptr, *s_tok = nullptr, *s_out = nullptr; float* s_w = nullptr; int* s_n = nullptr;
     int *counts = nullptr, *offsets = nullptr, *perm = nullptr;
     int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
-    int* err = nullptr; int* rcount = nullptr;
+    int* err = nullptr; int* rcount = nullptr; int* h_err = nullptr;   // device error word and its pinned mirror
     // host mirrors (pinned)
     int* h_sel = nullptr; float* h_wts = nullptr; float* h_ncur = nullptr; float* h_fi = nullptr; float* h_h = nullptr;
     float* h_moe = nullptr; int* h_tab = nullptr; float* h_tabw = nullptr; float* h_in = nullptr;
@@ -46,7 +47,13 @@ struct FLCtx {
     // last narrow call (for fl_moe_outs)
     int last_n = 0, last_ke = 0; std::vector<int> last_ids; std::vector<float> last_w;
     int last_err = 0; int prep_n = 0;
+    // CUDA graphs of repeated call shapes (fl_moe_prepare, fl_moe, fl_moe_auto): one replay instead of a
+    // dozen launches and copies.  A shape is captured on its second occurrence (the first runs directly).
+    struct GraphKey { int kind, a, b, c, d; const void* p[8]; };
+    struct GraphEntry { GraphKey k; int seen; cudaGraphExec_t exec; };
+    std::vector<GraphEntry> graphs; bool use_graphs = true;
 };
+constexpr size_t FL_MAX_GRAPHS = 1024;
 
 static int fl_fail(FLCtx* c, int code, const char* what, cudaError_t e = cudaSuccess) {
     std::fprintf(stderr, "[loki_moe] %s%s%s\n", what, e != cudaSuccess ? ": " : "", e != cudaSuccess ? cudaGetErrorString(e) : "");
@@ -69,11 +76,15 @@ template <class T> static cudaError_t hz(T** p, size_t n) {
 
 static int nt_for(int n) { return n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8; }
 
-// device error word -> recorded error (called after a stream synchronisation)
+// the device error word rides with a blocking call's result copies: queue_err before the stream
+// synchronisation, check_dev after it (no separate synchronous copy per call)
+static void queue_err(FLCtx* c) {
+    if (cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess) fl_fail(c, LK_ERR_CUDA, "error-word copy");
+}
 static void check_dev(FLCtx* c) {
-    int e = 0;
-    if (cudaMemcpy(&e, c->err, 4, cudaMemcpyDeviceToHost) == cudaSuccess && e) {
-        cudaMemset(c->err, 0, 4);
+    if (*c->h_err) {
+        *c->h_err = 0;
+        cudaMemsetAsync(c->err, 0, 4, c->st);
         fl_fail(c, LK_ERR_DEVICE, "device-side error recorded by a kernel");
     }
 }
@@ -113,7 +124,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
         dz(&c->counts, N_EXPERTS) == cudaSuccess && dz(&c->offsets, N_EXPERTS + 1) == cudaSuccess && dz(&c->perm, NB * MAX_TOPK) == cudaSuccess &&
         dz(&c->hq, rows * MOE_INTER) == cudaSuccess && dz(&c->hd, rows * (MOE_INTER / 32)) == cudaSuccess &&
         dz(&c->y, rows * HIDDEN) == cudaSuccess && dz(&c->err, 1) == cudaSuccess &&
-        dz(&c->rcount, PREP_ROWS / 8) == cudaSuccess &&
+        dz(&c->rcount, PREP_ROWS / 8) == cudaSuccess && hz(&c->h_err, 1) == cudaSuccess &&
         hz(&c->h_sel, PREP_ROWS * MAX_TOPK) == cudaSuccess && hz(&c->h_wts, PREP_ROWS * MAX_TOPK) == cudaSuccess &&
         hz(&c->h_ncur, R) == cudaSuccess && hz(&c->h_fi, R) == cudaSuccess && hz(&c->h_h, R) == cudaSuccess &&
         hz(&c->h_moe, R) == cudaSuccess && hz(&c->h_tab, (size_t)4 * ms * MAX_NT + 8) == cudaSuccess &&
@@ -138,8 +149,9 @@ void fl_free(FLCtx* c) {
         if (c->hw_w[p]) cudaFreeHost(c->hw_w[p]);
         if (c->wev[p]) cudaEventDestroy(c->wev[p]);
     }
-    void* h[] = { c->h_sel, c->h_wts, c->h_ncur, c->h_fi, c->h_h, c->h_moe, c->h_tab, c->h_tabw, c->h_in, c->h_wh, c->h_wmoe };
+    void* h[] = { c->h_sel, c->h_wts, c->h_ncur, c->h_fi, c->h_h, c->h_moe, c->h_tab, c->h_tabw, c->h_in, c->h_wh, c->h_wmoe, c->h_err };
     for (void* p : h) if (p) cudaFreeHost(p);
+    for (auto& g : c->graphs) if (g.exec) cudaGraphExecDestroy(g.exec);
     cudaEvent_t ev[] = { c->em0, c->em1, c->ep0, c->ep1 };
     for (cudaEvent_t e : ev) if (e) cudaEventDestroy(e);
     if (c->st) cudaStreamDestroy(c->st);
@@ -157,37 +169,81 @@ void fl_wait_event(FLCtx* c, fl_event_t ev) { if (c) FLCK(cudaStreamWaitEvent(c-
 
 double fl_gpu_ms(FLCtx* c, int which) { return !c ? 0.0 : which == 1 ? c->ms_moe : c->ms_prep; }
 
-// shared-expert-only slot table for rows [0, n): written on the host, copied on the stream
-static void shared_slots(FLCtx* c, int n, int nt) {
-    const int ns = (n + nt - 1) / nt;
-    int* he = c->h_tab; int* ht = he + ns; int* ho = ht + ns * nt; float* hw = c->h_tabw;
-    for (int j = 0; j < ns; ++j) {
-        he[j] = SHARED_SLOT;
-        for (int m = 0; m < nt; ++m) { const int t = j * nt + m; ht[j * nt + m] = t < n ? t : -1; ho[j * nt + m] = t < n ? t : -1; hw[j * nt + m] = t < n ? 1.f : 0.f; }
+// event record that is also a graph node while the stream is being captured
+static cudaError_t rec(cudaEvent_t ev, cudaStream_t st) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(st, &cs);
+    if (e != cudaSuccess) return e;
+    return cs == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(ev, st, cudaEventRecordExternal) : cudaEventRecord(ev, st);
+}
+
+// run `enqueue` (stream work only, with fixed pointers for a given key) directly, or as a replay of the CUDA
+// graph captured for that key: a key is captured on its second occurrence; if capturing fails the work runs
+// directly and the key is not tried again
+static void run_graph(FLCtx* c, const FLCtx::GraphKey& k, const std::function<void()>& enqueue) {
+    if (!c->use_graphs) { enqueue(); return; }
+    FLCtx::GraphEntry* g = nullptr;
+    for (auto& e : c->graphs)
+        if (!std::memcmp(&e.k, &k, sizeof(k))) { g = &e; break; }
+    if (!g) {
+        if (c->graphs.size() < FL_MAX_GRAPHS) c->graphs.push_back({k, 1, nullptr});
+        enqueue();
+        return;
     }
-    ho[ns * nt] = ns;
-    FLCK(cudaMemcpyAsync(c->s_expert, he, ns * 4, cudaMemcpyHostToDevice, c->st));
-    FLCK(cudaMemcpyAsync(c->s_tok, ht, (size_t)ns * nt * 4, cudaMemcpyHostToDevice, c->st));
-    FLCK(cudaMemcpyAsync(c->s_out, ho, (size_t)ns * nt * 4, cudaMemcpyHostToDevice, c->st));
-    FLCK(cudaMemcpyAsync(c->s_w, hw, (size_t)ns * nt * 4, cudaMemcpyHostToDevice, c->st));
-    FLCK(cudaMemcpyAsync(c->s_n, ho + ns * nt, 4, cudaMemcpyHostToDevice, c->st));
+    if (g->exec) { FLCK(cudaGraphLaunch(g->exec, c->st)); return; }
+    if (g->seen < 0) { enqueue(); return; }           // capture failed before
+    cudaGraph_t graph = nullptr;
+    bool ok = cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+    if (ok) {
+        enqueue();
+        ok = cudaStreamEndCapture(c->st, &graph) == cudaSuccess && graph;
+        if (ok) ok = cudaGraphInstantiate(&g->exec, graph, 0) == cudaSuccess;
+        if (graph) cudaGraphDestroy(graph);
+    }
+    if (!ok) {
+        cudaGetLastError();
+        g->exec = nullptr; g->seen = -1;
+        enqueue();
+        return;
+    }
+    FLCK(cudaGraphLaunch(g->exec, c->st));
+}
+
+// shared-expert-only slot table for rows [0, n) (slots of nt tokens), written on the device
+__global__ void k_shared_slots(int n, int nt, int* se, int* stok, int* sout, float* sw, int* sn) {
+    const int ns = (n + nt - 1) / nt;
+    for (int i = threadIdx.x; i < ns * nt; i += blockDim.x) {
+        const int t = i < n ? i : -1;
+        if (i % nt == 0) se[i / nt] = SHARED_SLOT;
+        stok[i] = t; sout[i] = t; sw[i] = t >= 0 ? 1.0f : 0.0f;
+    }
+    if (threadIdx.x == 0) *sn = ns;
+}
+static void shared_slots(FLCtx* c, int n, int nt) {
+    k_shared_slots<<<1, 64, 0, c->st>>>(n, nt, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n);
 }
 
 void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
     if (!c || !W || !ncur || !ffn_inp || N < 1 || N > PREP_ROWS) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: bad argument"); return; }
     if (wrow >= 0 && (!c->ncur_all || wrow + N > c->wmax)) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: wide rows outside fl_wide_init capacity"); return; }
     cudaStream_t st = c->st;
-    FLCK(cudaEventRecord(c->ep0, st));
     const size_t bytes = (size_t)N * HIDDEN * 4;
+    if (host) { std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes); }
+    c->prep_n = N;
+    FLCtx::GraphKey key;
+    std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
+    key.kind = 1; key.a = N; key.b = host; key.c = wrow; key.d = W->gate_f16;
+    const void* kp[8] = { W->gate_inp, W->probs_b, W->sh_gate, W->sh_up, W->sh_down, host ? nullptr : ncur, host ? nullptr : ffn_inp, nullptr };
+    std::memcpy(key.p, kp, sizeof(kp));
+    run_graph(c, key, [&]() {
+    FLCK(rec(c->ep0, st));
     if (host) {
-        std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes);
         FLCK(cudaMemcpyAsync(c->ncur, c->h_ncur, bytes, cudaMemcpyHostToDevice, st));
         FLCK(cudaMemcpyAsync(c->ffn_inp, c->h_fi, bytes, cudaMemcpyHostToDevice, st));
     } else {
         FLCK(cudaMemcpyAsync(c->ncur, ncur, bytes, cudaMemcpyDeviceToDevice, st));
         FLCK(cudaMemcpyAsync(c->ffn_inp, ffn_inp, bytes, cudaMemcpyDeviceToDevice, st));
     }
-    c->prep_n = N;
     // router: full top-8 (the engine applies its keep-KE pass on the fetched rows)
     RouterParams rp{};
     rp.x = c->ncur; rp.T = N; rp.ld_x = HIDDEN; rp.W = W->gate_inp; rp.w_f16 = W->gate_f16; rp.bias = W->probs_b;
@@ -213,7 +269,8 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
         cp.h = c->base_all + (size_t)wrow * HIDDEN; cp.moe = nullptr; cp.ld_out = HIDDEN;
         launch_combine(cp, st);
     }
-    FLCK(cudaEventRecord(c->ep1, st));
+    FLCK(rec(c->ep1, st));
+    });
     FLCK(cudaGetLastError());
 }
 
@@ -230,27 +287,17 @@ void fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
         out->sel = c->h_sel; out->wts = c->h_wts; out->ncur = c->h_ncur; out->fi = c->h_fi;
     }
     if (what & 32) { FLCK(cudaMemcpyAsync(c->h_h, c->h, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st)); out->h = c->h_h; }
+    queue_err(c);
     FLCK(cudaStreamSynchronize(st));
     float ms = 0.f;
     if (cudaEventElapsedTime(&ms, c->ep0, c->ep1) == cudaSuccess) c->ms_prep += ms;
     check_dev(c);
 }
 
-void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int nexp, int down_fmt, const int* ids, const float* w,
-            int KE, int n, FLOut* out) {
-    if (!c || !out) return;
-    std::memset(out, 0, sizeof(FLOut));
-    if (!down_fmt_ok(down_fmt)) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe: down format must be FL_IQ2, FL_Q2K or FL_Q3K"); return; }
-    if (n < 1 || n > NB || KE < 1 || KE > MAX_TOPK || nexp < 1 || nexp > N_EXPERTS || !ids || !w) { fl_fail(c, LK_ERR_ARG, "fl_moe: bad argument"); return; }
-    if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_moe: arena not 16-byte aligned"); return; }
-    for (int i = 0; i < n * KE; ++i) if (ids[i] < 0 || ids[i] >= nexp) { fl_fail(c, LK_ERR_ARG, "fl_moe: slot id out of range"); return; }
+// the narrow pass from routing already on the device (c->ids, c->w [n][KE]): slots, experts, combine, and the
+// result copies into the pinned mirrors (h, moe; with ids_back also the routing), then the stream sync
+static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int n, bool ids_back) {
     cudaStream_t st = c->st;
-    FLCK(cudaEventRecord(c->em0, st));
-    int* hi = c->h_tab; float* hw = c->h_tabw;
-    std::memcpy(hi, ids, (size_t)n * KE * 4); std::memcpy(hw, w, (size_t)n * KE * 4);
-    FLCK(cudaMemcpyAsync(c->ids, hi, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
-    FLCK(cudaMemcpyAsync(c->w, hw, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
-    c->last_ids.assign(ids, ids + n * KE); c->last_w.assign(w, w + n * KE); c->last_n = n; c->last_ke = KE;
     const int nt = down_fmt == FL_IQ2 ? nt_for(n) : 1;      // the K-quant down kernel takes single-token slots
     SlotParams sp{};
     sp.sel = c->ids; sp.w = c->w; sp.T = n; sp.keep = KE; sp.n_experts = N_EXPERTS; sp.nt = nt; sp.with_shared = 0;
@@ -269,13 +316,110 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     launch_combine(cp, st);
     FLCK(cudaMemcpyAsync(c->h_h, c->h, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
     FLCK(cudaMemcpyAsync(c->h_moe, c->moe, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
-    FLCK(cudaEventRecord(c->em1, st));
-    FLCK(cudaStreamSynchronize(st));
+    if (ids_back) {
+        FLCK(cudaMemcpyAsync(c->h_tab, c->ids, (size_t)n * KE * 4, cudaMemcpyDeviceToHost, st));
+        FLCK(cudaMemcpyAsync(c->h_tabw, c->w, (size_t)n * KE * 4, cudaMemcpyDeviceToHost, st));
+    }
+    FLCK(rec(c->em1, st));
+    queue_err(c);
+}
+
+// after the enqueued narrow pass: wait for it, account its time, read the error word and the routing back
+static void finish_narrow(FLCtx* c, int KE, int n, bool ids_back, FLOut* out) {
+    FLCK(cudaStreamSynchronize(c->st));
     float ms = 0.f;
     if (cudaEventElapsedTime(&ms, c->em0, c->em1) == cudaSuccess) c->ms_moe += ms;
     check_dev(c);
+    if (ids_back) { c->last_ids.assign(c->h_tab, c->h_tab + n * KE); c->last_w.assign(c->h_tabw, c->h_tabw + n * KE); }
+    c->last_n = n; c->last_ke = KE;
     out->h = c->h_h; out->moe = c->h_moe;
 }
+
+void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int nexp, int down_fmt, const int* ids, const float* w,
+            int KE, int n, FLOut* out) {
+    if (!c || !out) return;
+    std::memset(out, 0, sizeof(FLOut));
+    if (!down_fmt_ok(down_fmt)) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe: down format must be FL_IQ2, FL_Q2K or FL_Q3K"); return; }
+    if (n < 1 || n > NB || KE < 1 || KE > MAX_TOPK || nexp < 1 || nexp > N_EXPERTS || !ids || !w) { fl_fail(c, LK_ERR_ARG, "fl_moe: bad argument"); return; }
+    if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_moe: arena not 16-byte aligned"); return; }
+    for (int i = 0; i < n * KE; ++i) if (ids[i] < 0 || ids[i] >= nexp) { fl_fail(c, LK_ERR_ARG, "fl_moe: slot id out of range"); return; }
+    cudaStream_t st = c->st;
+    int* hi = c->h_tab; float* hw = c->h_tabw;
+    std::memcpy(hi, ids, (size_t)n * KE * 4); std::memcpy(hw, w, (size_t)n * KE * 4);
+    c->last_ids.assign(ids, ids + n * KE); c->last_w.assign(w, w + n * KE);
+    FLCtx::GraphKey key;
+    std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
+    key.kind = 2; key.a = n; key.b = KE; key.c = down_fmt;
+    key.p[0] = gate; key.p[1] = up; key.p[2] = down;
+    run_graph(c, key, [&]() {
+        FLCK(rec(c->em0, st));
+        FLCK(cudaMemcpyAsync(c->ids, hi, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w, hw, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
+        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, false);
+    });
+    finish_narrow(c, KE, n, false, out);
+}
+
+}  // extern "C"
+
+// the engine's keep-KE pass (src/server_core_fused.cpp:793-813, without --share-experts) on the device: row i
+// of the router output (sel8 / w8 [n][8], top-8 by score) -> its KE highest-weight experts (equal weights in
+// position order) and, with renorm, their weights scaled to sum to 2.5, in the host pass's float order
+__global__ void k_fl_keep(const int* sel8, const float* w8, int n, int KE, int renorm, int* ids, float* w) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float wv[8]; int sv[8], rank[8];
+    #pragma unroll
+    for (int k = 0; k < 8; ++k) { wv[k] = w8[i * 8 + k]; sv[k] = sel8[i * 8 + k]; }
+    if (KE >= 8) {                                // the engine compacts only for KE < 8
+        #pragma unroll
+        for (int k = 0; k < 8; ++k) { ids[i * 8 + k] = sv[k]; w[i * 8 + k] = wv[k]; }
+        return;
+    }
+    #pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        int r = 0;
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) r += (wv[j] > wv[k]) || (wv[j] == wv[k] && j < k);
+        rank[k] = r;
+    }
+    float kw[8]; int ks[8];
+    #pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        kw[r] = 0.0f; ks[r] = 0;
+        #pragma unroll
+        for (int k = 0; k < 8; ++k) if (rank[k] == r) { kw[r] = wv[k]; ks[r] = sv[k]; }
+    }
+    float sw = 0.0f;
+    #pragma unroll
+    for (int r = 0; r < 8; ++r) if (r < KE) sw += kw[r];
+    const float f = (renorm && sw > 1e-6f) ? 2.5f / sw : 1.0f;
+    #pragma unroll
+    for (int r = 0; r < 8; ++r) if (r < KE) { ids[i * KE + r] = ks[r]; w[i * KE + r] = renorm && sw > 1e-6f ? kw[r] * f : kw[r]; }
+}
+
+extern "C" {
+
+void fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int renorm, int n, FLOut* out) {
+    if (!c || !out) return;
+    std::memset(out, 0, sizeof(FLOut));
+    if (!down_fmt_ok(down_fmt)) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe_auto: down format must be FL_IQ2, FL_Q2K or FL_Q3K"); return; }
+    if (n < 1 || n > NB || n > c->prep_n || KE < 1 || KE > MAX_TOPK) { fl_fail(c, LK_ERR_ARG, "fl_moe_auto: bad argument (n <= 8 rows of the last fl_moe_prepare)"); return; }
+    if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_moe_auto: arena not 16-byte aligned"); return; }
+    cudaStream_t st = c->st;
+    FLCtx::GraphKey key;
+    std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
+    key.kind = 3; key.a = n; key.b = KE; key.c = down_fmt; key.d = renorm;
+    key.p[0] = gate; key.p[1] = up; key.p[2] = down;
+    run_graph(c, key, [&]() {
+        FLCK(rec(c->em0, st));
+        k_fl_keep<<<1, 64, 0, st>>>(c->sel, c->wts, n, KE, renorm, c->ids, c->w);
+        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, true);
+    });
+    finish_narrow(c, KE, n, true, out);
+}
+
+void fl_use_graphs(FLCtx* c, int enable) { if (c) c->use_graphs = enable != 0; }
 
 void fl_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
     if (!c || !out || !mo || n < 1 || n > PREP_ROWS) return;
@@ -386,6 +530,7 @@ void fl_wide_finish(FLCtx* c, int n, int KE, FLOut* out) {
     launch_combine(cp, st);
     FLCK(cudaMemcpyAsync(c->h_wh, hbuf, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
     FLCK(cudaMemcpyAsync(c->h_wmoe, hbuf + (size_t)n * HIDDEN, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+    queue_err(c);
     FLCK(cudaStreamSynchronize(st));
     cudaFree(hbuf);
     check_dev(c);

@@ -5,6 +5,7 @@ fl_moe_prepare (the MoE half of fl_attn) -> fl_fetch(what=1) -> host keep-KE pas
 (prefill) pass fl_moe_prepare(wrow=...) per group -> fl_wide_moe per arena batch -> fl_wide_finish.
 """
 import ctypes
+import os
 
 import numpy as np
 
@@ -93,6 +94,57 @@ def union_remap(sel):
     return used.astype(np.int32), remap[sel]
 
 
+_replay = None
+
+
+def replay_lib():
+    """libloki_replay.so: the engine-side C++ harness (keep pass, per-token call sequence) over this ABI."""
+    global _replay
+    if _replay is None:
+        lib()
+        L = ctypes.CDLL(os.path.join(os.path.dirname(N.LIB_PATH), "libloki_replay.so"))
+        P, I = ctypes.c_void_p, ctypes.c_int
+        L.lkr_keep.argtypes = [P, P, I, I, I, I, I, P, P]
+        L.lkr_keep.restype = I
+        L.lkr_decode.argtypes = [P, I, P, P, P, P, I, P, P, I, I, I, I, P, I]
+        L.lkr_decode.restype = ctypes.c_double
+        _replay = L
+    return _replay
+
+
+def keep_pass_native(sel, wts, KE, renorm=True, share=False, n_pad_from=None):
+    """lkr_keep (the C++ keep pass the replay harness uses) on host arrays [n][8]."""
+    sel = np.ascontiguousarray(sel, np.int32)
+    wts = np.ascontiguousarray(wts, np.float32)
+    n = sel.shape[0]
+    s = np.empty((n, KE), np.int32)
+    w = np.empty((n, KE), np.float32)
+    rc = replay_lib().lkr_keep(_p(sel), _p(wts), n, KE, int(renorm), int(share), n if n_pad_from is None else n_pad_from,
+                               _p(s), _p(w))
+    assert rc == 0
+    return s, w
+
+
+def replay_decode(fc, layers, x, resid, KE, warmup, steps, down_fmt=FL_IQ2, device_keep=False):
+    """The engine's per-token MoE call sequence over `layers` (LayerWeights with 256-expert arenas), driven
+    from C++ (lkr_decode): fl_moe_prepare -> fl_fetch -> host keep pass -> fl_moe per layer, or with
+    device_keep fl_moe_prepare -> fl_moe_auto.  x, resid: [L][n][7168] host arrays.  Returns (seconds of the
+    timed steps, the last layer's h of the last step)."""
+    L = len(layers)
+    x = np.ascontiguousarray(x, np.float32)
+    resid = np.ascontiguousarray(resid, np.float32)
+    n = x.shape[1]
+    mw = (N.FLMoeW * L)(*[N.FLMoeW(l.router_w.data_ptr(), 0, l.router_bias.data_ptr(), l.sh_gate, l.sh_up, l.sh_down)
+                          for l in layers])
+    ptrs = lambda attr: (ctypes.c_void_p * L)(*[getattr(l, attr) for l in layers])
+    h = np.empty((n, HIDDEN), np.float32)
+    sec = replay_lib().lkr_decode(fc.c, L, mw, ptrs("gate"), ptrs("up"), ptrs("down"), down_fmt, _p(x), _p(resid), n, KE,
+                                  warmup, steps, _p(h), 1 if device_keep else 0)
+    if sec < 0:
+        raise N.NativeError("lkr_decode failed (%g): fl_moe_error %d" % (sec, fc.error()))
+    return sec, h
+
+
 class FusedCtx:
     def __init__(self, kvp=512, sc_cap=64):
         self.c = lib().fl_init(kvp, sc_cap)
@@ -113,6 +165,9 @@ class FusedCtx:
 
     def error(self):
         return lib().fl_moe_error(self.c)
+
+    def use_graphs(self, enable):
+        lib().fl_use_graphs(self.c, int(enable))
 
     def prepare(self, mw, ncur, ffn_inp, wrow=-1):
         ncur = np.ascontiguousarray(ncur, np.float32)
@@ -141,6 +196,14 @@ class FusedCtx:
         n, KE = ids.shape
         lib().fl_moe(self.c, ctypes.c_void_p(gate), ctypes.c_void_p(up), ctypes.c_void_p(down), nexp, down_fmt, _p(ids), _p(w),
                      KE, n, ctypes.byref(self.out))
+        o = self.out
+        return (_view(o.h, n * HIDDEN, np.float32).reshape(n, HIDDEN) if o.h else None,
+                _view(o.moe, n * HIDDEN, np.float32).reshape(n, HIDDEN) if o.moe else None)
+
+    def moe_auto(self, gate, up, down, n, KE, renorm=True, down_fmt=FL_IQ2):
+        """fl_moe_auto: the narrow pass routed on the device from the last prepare's router output."""
+        lib().fl_moe_auto(self.c, ctypes.c_void_p(gate), ctypes.c_void_p(up), ctypes.c_void_p(down), down_fmt, KE, int(renorm), n,
+                          ctypes.byref(self.out))
         o = self.out
         return (_view(o.h, n * HIDDEN, np.float32).reshape(n, HIDDEN) if o.h else None,
                 _view(o.moe, n * HIDDEN, np.float32).reshape(n, HIDDEN) if o.moe else None)

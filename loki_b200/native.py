@@ -103,6 +103,8 @@ SIGNATURES = {
     "fl_gpu_ms": (_D, [_P, _I]),
     "fl_moe_prepare": (None, [_P, ctypes.POINTER(FLMoeW), _P, _P, _I, _I, _I]),
     "fl_moe_error": (_I, [_P]),
+    "fl_moe_auto": (None, [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(FLOut)]),
+    "fl_use_graphs": (None, [_P, _I]),
     "fl_free": (None, [_P]),
 }
 

@@ -86,3 +86,93 @@ def test_fl_wide(native, oracle, fl_layer):
         assert rel_l2(h, ref["h"]) < RTOL_L2
     finally:
         fc.close()
+
+
+def test_fl_replay_decode(native, oracle, fl_layer):
+    """The C++ engine replay (lkr_decode) over two layers: the last layer's h equals the oracle's."""
+    from loki_b200 import fused as F
+    fmt, W = fl_layer
+    if fmt != 4:
+        pytest.skip("the replay drives fl_moe_prepare's IQ2_XXS shared expert")
+    rng = np.random.default_rng(31)
+    x = rng.standard_normal((2, 1, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((2, 1, HIDDEN)).astype(np.float32)
+    fc = F.FusedCtx()
+    try:
+        sec, h = F.replay_decode(fc, [W, W], x, r, 8, 1, 2, down_fmt=fmt)
+        assert sec > 0 and fc.error() == 0
+    finally:
+        fc.close()
+    _, osel, ow = oracle.router(x[1], W.router_w.float().cpu().numpy(), W.router_bias.cpu().numpy(), oracle.route_cfg(8, 8, 0))
+    ref = oracle_layer(oracle, SEED, 5, x[1], r[1], osel, ow, down_fmt=fmt)
+    assert rel_l2(h, ref["h"]) < RTOL_L2
+
+
+@pytest.mark.parametrize("n,KE", [(1, 8), (3, 2), (8, 3)])
+def test_fl_moe_auto_equals_host_keep_path(native, oracle, fl_layer, n, KE):
+    """fl_moe_auto (routing post-pass on the device) gives exactly the outputs of fl_fetch + host keep pass +
+    fl_moe, and fl_moe_outs sees its routing."""
+    from loki_b200 import fused as F
+    fmt, W = fl_layer
+    rng = np.random.default_rng(700 + n * 10 + KE)
+    x = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    fc = F.FusedCtx()
+    try:
+        fc.prepare(_mw(native, W, fmt), x, r)
+        got = fc.fetch(n, 1)
+        ids, w = F.keep_pass(got["sel"], got["wts"], KE)
+        h1, m1 = [a.copy() for a in fc.moe(W.gate, W.up, W.down, 256, ids, w, down_fmt=fmt)]
+        outs1 = fc.moe_outs(0, ids[0], w[0]).copy()
+        fc.prepare(_mw(native, W, fmt), x, r)
+        h2, m2 = [a.copy() for a in fc.moe_auto(W.gate, W.up, W.down, n, KE, down_fmt=fmt)]
+        outs2 = fc.moe_outs(0, ids[0], w[0])
+        assert fc.error() == 0
+        np.testing.assert_array_equal(h1, h2)
+        np.testing.assert_array_equal(m1, m2)
+        np.testing.assert_array_equal(outs1, outs2)
+    finally:
+        fc.close()
+
+
+def test_fl_replay_decode_device_keep(native, oracle, fl_layer):
+    """The C++ replay through fl_moe_auto: the last layer's h equals the oracle's (keep 2 of 8, renormalised)."""
+    from loki_b200 import fused as F
+    fmt, W = fl_layer
+    if fmt != 4:
+        pytest.skip("the replay drives fl_moe_prepare's IQ2_XXS shared expert")
+    rng = np.random.default_rng(32)
+    x = rng.standard_normal((2, 1, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((2, 1, HIDDEN)).astype(np.float32)
+    fc = F.FusedCtx()
+    try:
+        sec, h = F.replay_decode(fc, [W, W], x, r, 2, 1, 2, down_fmt=fmt, device_keep=True)
+        assert sec > 0 and fc.error() == 0
+    finally:
+        fc.close()
+    _, osel, ow = oracle.router(x[1], W.router_w.float().cpu().numpy(), W.router_bias.cpu().numpy(), oracle.route_cfg(8, 2, 1))
+    ref = oracle_layer(oracle, SEED, 5, x[1], r[1], osel, ow, down_fmt=fmt)
+    assert rel_l2(h, ref["h"]) < RTOL_L2
+
+
+@pytest.mark.parametrize("device_keep", [False, True])
+def test_fl_graphs_match_direct_launches(native, fl_layer, device_keep):
+    """Repeated call shapes replay captured CUDA graphs: the same h as issuing every launch directly."""
+    from loki_b200 import fused as F
+    fmt, W = fl_layer
+    if fmt != 4:
+        pytest.skip("the replay drives fl_moe_prepare's IQ2_XXS shared expert")
+    rng = np.random.default_rng(33)
+    x = rng.standard_normal((3, 2, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((3, 2, HIDDEN)).astype(np.float32)
+    hs = []
+    for graphs in (False, True):
+        fc = F.FusedCtx()
+        try:
+            fc.use_graphs(graphs)
+            _, h = F.replay_decode(fc, [W, W, W], x, r, 4, 2, 3, device_keep=device_keep)   # shapes repeat
+            assert fc.error() == 0
+            hs.append(h)
+        finally:
+            fc.close()
+    np.testing.assert_array_equal(hs[0], hs[1])

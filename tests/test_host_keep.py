@@ -97,3 +97,16 @@ def test_pad_rows_and_union_remap():
     used, idsc = F.union_remap(ps)
     assert list(used) == [5, 7, 9]
     np.testing.assert_array_equal(used[idsc], ps)
+
+
+@pytest.mark.parametrize("share", [False, True])
+def test_native_keep_matches_python(share):
+    """lkr_keep (the C++ keep pass of the engine-replay harness) equals keep_pass."""
+    rng = np.random.default_rng(5 + share)
+    for KE in (1, 2, 3, 5, 8):
+        for pool in (10, 256):
+            sel, w = _rows(rng, 7, pool)
+            a = F.keep_pass(sel, w, KE, share=share)
+            b = F.keep_pass_native(sel, w, KE, share=share)
+            np.testing.assert_array_equal(a[0], b[0])
+            np.testing.assert_array_equal(a[1], b[1])
