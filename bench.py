@@ -36,6 +36,12 @@ SEED = 0x10C1
 HIDDEN, INTER, NE = 7168, 2048, 256
 MAT = INTER * (HIDDEN // 256) * 66                       # 3 784 704 bytes per expert matrix
 ROUTER_BYTES = NE * HIDDEN * 4
+DOWN_FMTS = {"iq2": (4, 66), "q2k": (5, 84), "q3k": (6, 110)}   # --down-fmt: format id, bytes per 256-weight block
+
+
+def down_bytes(args):
+    """Bytes of one expert's down matrix in the decode workload's down format."""
+    return HIDDEN * (INTER // 256) * DOWN_FMTS[args.down_fmt][1]
 
 
 # DeepSeek-R1 routing (BASELINE config 0, inherited by configs 1-4): 8 groups of 32 experts, top 4 groups
@@ -196,14 +202,14 @@ def cpu_decode_sample(n_layers, keep=8, seed=SEED):
 
 
 # ------------------------------------------------------------------ decode workload (config 1)
-def build_decode(dev, n_layers, keep):
+def build_decode(dev, n_layers, keep, fmt=4, ds=MAT):
     import torch
     from loki_b200 import moe as M
     free, total = torch.cuda.mem_get_info(dev)
-    per_layer = (3 * NE + 3) * MAT + ROUTER_BYTES
+    per_layer = (2 * NE + 2) * MAT + (NE + 1) * ds + ROUTER_BYTES
     fit = int((free - (6 << 30)) // per_layer)
     distinct = max(1, min(n_layers, fit))
-    layers = [M.LayerWeights(dev, SEED, L) for L in range(distinct)]
+    layers = [M.LayerWeights(dev, SEED, L, down_fmt=fmt) for L in range(distinct)]
     torch.cuda.synchronize(dev)
     return layers, distinct
 
@@ -215,7 +221,8 @@ def run_decode(args, ws, rank, local, dist):
     from loki_b200 import native as N
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    layers, distinct = build_decode(dev, args.layers, args.keep)
+    fmt, DS = DOWN_FMTS[args.down_fmt][0], down_bytes(args)
+    layers, distinct = build_decode(dev, args.layers, args.keep, fmt, DS)
     layer_of = [L % distinct for L in range(args.layers)]
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     xs = torch.randn(args.layers, 1, HIDDEN, device=dev, generator=g)
@@ -287,17 +294,20 @@ def run_decode(args, ws, rank, local, dist):
     hbm, bf16, peak_kind = measured_peaks()
     n_slots = args.keep + 1
     gu_bytes = n_slots * 2 * MAT + 4 * HIDDEN                       # 8 routed + shared gate/up rows, x in
-    dn_bytes = n_slots * MAT + n_slots * (INTER + INTER // 32 * 4) + n_slots * HIDDEN * 4
-    layer_bytes = n_slots * 3 * MAT + ROUTER_BYTES + 3 * 4 * HIDDEN
+    dn_bytes = n_slots * DS + n_slots * (INTER + INTER // 32 * 4) + n_slots * HIDDEN * 4
+    layer_bytes = n_slots * (2 * MAT + DS) + ROUTER_BYTES + 3 * 4 * HIDDEN
     gu_ms = float(gu.mean())
     achieved = gu_bytes / (gu_ms / 1e3) / 1e9
     traffic = ncu_traffic("k_gate_up", "decode_T1")
     out = {
         "metric": "MoE-layer tokens/s (T=1 decode through 58 layers)", "value": round(value, 2), "unit": "tokens/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "iq2_xxs x q8 (int8 dp4a, fp32 accumulate)",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "iq2_xxs x q8 (int8 dp4a, fp32 accumulate)" if fmt == 4 else "iq2_xxs gate/up, %s down x q8 (int8 dp4a, fp32 accumulate)" % args.down_fmt,
         "data": "synthetic: seeded IQ2_XXS experts (BASELINE config 0 generator), router W N(0,0.02), bias N(0,0.01), x/resid N(0,1) fp32",
-        "config": {"workload": "config1_decode_T1_58layers", "model": "DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)",
+        "config": {"workload": "config1_decode_T1_58layers" if fmt == 4 else "decode_T1_58layers_%s_down" % args.down_fmt,
+                   "model": "DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)" if fmt == 4 else
+                            "DeepSeek-R1 MoE layer (IQ2_XXS gate/up, %s down as in the real model, 256 experts + shared)" % args.down_fmt,
                    "global_batch": ws, "seq_len": 1, "layers": args.layers, "distinct_layers_resident": distinct,
                    "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP, "keep": args.keep, "parallelism": "replicas" if ws > 1 else "single",
                    "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (args.layers * layer_bytes / 1e9)},
@@ -314,7 +324,7 @@ def run_decode(args, ws, rank, local, dist):
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "traffic": traffic, "algorithmic_bytes_per_launch": gu_bytes, "peak_source": peak_kind,
                      "down_kernel_frac": round(dn_bytes / (float(dn.mean()) / 1e3) / 1e9 / hbm, 4)},
-        "gpu_launches": args.steps * args.layers * 3,      # per layer: router (+top-k), gate/up, down (+combine)
+        "gpu_launches": args.steps * args.layers * 4,      # per layer: router (+top-k), gate/up, down, combine
     }
     if cl:
         out["clocks"] = cl
@@ -769,6 +779,8 @@ def main():
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--keep", type=int, default=8)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--down-fmt", default="iq2", choices=sorted(DOWN_FMTS),
+                    help="decode workload: format of the down matrices (q2k / q3k: the real model's; no e2e or CPU leg)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample (profiling runs)")
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU-baseline sample")
     ap.add_argument("--parallelism", default="ep", choices=["ep", "replicas"], help="N > 1: expert parallel or replicas")
@@ -807,6 +819,8 @@ def main():
             dist.destroy_process_group()
         return
     out, layers, ctx, structs, xs, rs = run_decode(args, ws, rank, local, dist)
+    if args.down_fmt != "iq2":
+        args.no_e2e = args.no_cpu = True            # fl_moe_prepare's shared expert and the CPU sample are IQ2_XXS
     if not args.no_e2e:
         e2e = e2e_decode(args, layers, len(layers), args.keep)
         e2e_v = max_over_ranks(dist, 1.0 / e2e["value"])

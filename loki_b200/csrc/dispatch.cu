@@ -54,10 +54,13 @@ __global__ void __launch_bounds__(DS_THREADS) k_build_slots(SlotParams p) {
         const int rank_w = __popc(peers & ((1u << lane) - 1u));
         if (live && rank_w == 0) wcnt[warp][e] = (unsigned short)__popc(peers);
         __syncthreads();
-        if (live) {
+        if (live) {                                   // rank r of the entry in expert e's stable list
             int before = 0;
             for (int w = 0; w < warp; ++w) before += wcnt[w][e];
-            p.perm[off[e] + run[e] + before + rank_w] = i;
+            const int r = run[e] + before + rank_w;
+            p.perm[off[e] + r] = i;
+            const int s = soff[e] + r / nt, m = r % nt;   // its slot and position: written here, in parallel
+            if (s < p.max_slots) { p.slot_tok[s * nt + m] = i / p.keep; p.slot_out[s * nt + m] = i; p.slot_w[s * nt + m] = p.w[i]; }
         }
         __syncthreads();
         for (int x = tid; x < NE; x += DS_THREADS) {
@@ -67,25 +70,19 @@ __global__ void __launch_bounds__(DS_THREADS) k_build_slots(SlotParams p) {
         }
         __syncthreads();
     }
-    // slot tables
+    // slot tables: the entries were placed by the rank pass; here each slot's expert and the pads that
+    // fill the last slot of every expert (positions cnt % nt .. nt-1), over (expert, position) pairs
     for (int e = tid; e < NE; e += DS_THREADS) {
-        if (tid < NE) p.counts[e] = cnt[e];
+        p.counts[e] = cnt[e];
         p.offsets[e] = off[e];
-        const int ns = (cnt[e] + nt - 1) / nt;
-        for (int j = 0; j < ns; ++j) {
-            const int s = soff[e] + j;
-            if (s >= p.max_slots) break;
-            p.slot_expert[s] = e;
-            for (int m = 0; m < nt; ++m) {
-                const int li = j * nt + m;
-                if (li < cnt[e]) {
-                    const int ent = p.perm[off[e] + li];
-                    p.slot_tok[s * nt + m] = ent / p.keep; p.slot_out[s * nt + m] = ent; p.slot_w[s * nt + m] = p.w[ent];
-                } else {
-                    p.slot_tok[s * nt + m] = -1; p.slot_out[s * nt + m] = -1; p.slot_w[s * nt + m] = 0.0f;
-                }
-            }
-        }
+        for (int s = soff[e]; s < soff[e + 1] && s < p.max_slots; ++s) p.slot_expert[s] = e;
+    }
+    for (int x = tid; x < NE * nt; x += DS_THREADS) {
+        const int e = x / nt, m = x % nt;
+        if (cnt[e] % nt == 0 || m < cnt[e] % nt) continue;
+        const int s = soff[e + 1] - 1;
+        if (s >= p.max_slots) continue;
+        p.slot_tok[s * nt + m] = -1; p.slot_out[s * nt + m] = -1; p.slot_w[s * nt + m] = 0.0f;
     }
     const int nrs = soff[NE];
     const int nsh = !p.with_shared || p.sh_n < 0 ? 0 : (p.sh_n > 0 ? p.sh_n : p.T);
