@@ -124,7 +124,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
         dz(&c->counts, N_EXPERTS) == cudaSuccess && dz(&c->offsets, N_EXPERTS + 1) == cudaSuccess && dz(&c->perm, NB * MAX_TOPK) == cudaSuccess &&
         dz(&c->hq, rows * MOE_INTER) == cudaSuccess && dz(&c->hd, rows * (MOE_INTER / 32)) == cudaSuccess &&
         dz(&c->y, rows * HIDDEN) == cudaSuccess && dz(&c->err, 1) == cudaSuccess &&
-        dz(&c->rcount, PREP_ROWS / 8) == cudaSuccess && hz(&c->h_err, 1) == cudaSuccess &&
+        dz(&c->rcount, PREP_ROWS) == cudaSuccess && hz(&c->h_err, 1) == cudaSuccess &&
         hz(&c->h_sel, PREP_ROWS * MAX_TOPK) == cudaSuccess && hz(&c->h_wts, PREP_ROWS * MAX_TOPK) == cudaSuccess &&
         hz(&c->h_ncur, R) == cudaSuccess && hz(&c->h_fi, R) == cudaSuccess && hz(&c->h_h, R) == cudaSuccess &&
         hz(&c->h_moe, R) == cudaSuccess && hz(&c->h_tab, (size_t)4 * ms * MAX_NT + 8) == cudaSuccess &&

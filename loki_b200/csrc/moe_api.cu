@@ -107,8 +107,8 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LK_CU(dalloc(&c->err, 1));
     LK_CU(cudaMemset(c->err, 0, sizeof(int)));
     LK_CU(dalloc(&c->xq, HIDDEN)); LK_CU(dalloc(&c->xqn, HIDDEN)); LK_CU(dalloc(&c->xd, HIDDEN / 32));
-    LK_CU(dalloc(&c->tile_count, (T + 7) / 8));
-    LK_CU(cudaMemset(c->tile_count, 0, (size_t)((T + 7) / 8) * sizeof(int)));
+    LK_CU(dalloc(&c->tile_count, T));
+    LK_CU(cudaMemset(c->tile_count, 0, (size_t)T * sizeof(int)));
     c->g_max = max_slots_for(T, KE, NE, GEMM_NT, cfg->with_shared);
     LK_CU(dalloc(&c->g_expert, c->g_max)); LK_CU(dalloc(&c->g_tok, (size_t)c->g_max * GEMM_NT));
     LK_CU(dalloc(&c->g_out, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_w, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_n, 1));

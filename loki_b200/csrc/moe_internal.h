@@ -24,10 +24,11 @@ struct RouterParams {
     int n_experts, topk, keep, renorm, n_group, topk_group; float scale;
     // optional slot table written directly for T == 1 (decode): keep routed slots + shared slot
     int* slot_expert; int* slot_tok; int* slot_out; float* slot_w; int* nslots; int with_shared;
-    int* tile_count;                        // ceil(T/8) zeroed counters (last-CTA-done top-k)
+    int* tile_count;                        // T zeroed counters (last-CTA-done top-k; one per token tile)
     // optional, T == 1: the q8 of x for the expert kernels -- CTA e < HIDDEN/32 writes group e: int8 values
     // xq, their negations xqn (HIDDEN bytes each) and the scale xd[e] (quant_q8_group, bit for bit)
     int8_t* xq; int8_t* xqn; float* xd;
+    int esplit;                             // set by launch_router: expert splits of the batch kernel
 };
 void launch_router(const RouterParams& p, cudaStream_t st);
 

@@ -8,6 +8,11 @@
 //   (orc_router_logits), so probabilities -- and with them the selected experts -- are bit-identical to it.
 //   The last CTA to finish a token tile (an atomic count after a fence) runs the top-k for it, so the
 //   router is one launch.
+// k_router_batch (T >= 64): the same logits in the same order, with the data movement turned around: a CTA
+//   keeps a tile of 4 tokens' rows in shared memory and streams expert rows past it, so each (token,
+//   expert) pair costs ~7 KB of L2 traffic instead of the 31.5 KB of one expert x 8 tokens per CTA.  Thread
+//   p still owns partial p (chunks p + 256 j of every row, fmaf in the same order, the same butterfly and
+//   warp tree), so the results are bit-identical to k_router_logits and the oracle.
 // router_topk_token: one warp per token: top-k of p + bias with ties to the lower expert id (reference
 //   router_topk, src/fused_layer.cu:323-332), or the DeepSeek-V3 grouped mode (n_group groups of 32
 //   experts, group score = sum of the group's top-2, keep topk_group groups); weights p/max(sum, 2^-14)
@@ -110,6 +115,103 @@ __global__ void __launch_bounds__(256) k_router_logits(RouterParams p) {
     else if (warp < nt) router_topk_token(p, t0 + warp, lane);
     __syncthreads();
     if (tid == 0) p.tile_count[blockIdx.y] = 0;       // ready for the next call
+}
+
+constexpr int RB_TT = 4;                          // tokens per CTA tile
+constexpr int RB_EB = 8;                          // experts per barrier round (the 8 warp sums per pair)
+constexpr int RB_SMEM = RB_TT * HIDDEN * 4;       // the token tile: 112 KB, two CTAs per SM
+
+__device__ __forceinline__ void rb_load_w(const RouterParams& p, int e, int tid, float4 (&w)[HIDDEN / 1024]) {
+    #pragma unroll
+    for (int j = 0; j < HIDDEN / 1024; ++j) {
+        const int c = tid + 256 * j;
+        if (p.w_f16) {
+            const uint2 raw = __ldg((const uint2*)((const __half*)p.W + (size_t)e * HIDDEN) + c);
+            const float2 a = __half22float2(*(const __half2*)&raw.x), b = __half22float2(*(const __half2*)&raw.y);
+            w[j] = make_float4(a.x, a.y, b.x, b.y);
+        } else {
+            w[j] = __ldg((const float4*)((const float*)p.W + (size_t)e * HIDDEN) + c);
+        }
+    }
+}
+
+// one CTA = RB_TT tokens x experts [e0, e0 + n_experts / esplit); the top-k of a token tile runs in the
+// CTA that finishes it (its only CTA when esplit == 1)
+__global__ void __launch_bounds__(256) k_router_batch(RouterParams p) {
+    const int esplit = p.esplit;
+    extern __shared__ __align__(16) float4 xt[];  // [RB_TT][HIDDEN / 4]; thread tid only touches chunks tid + 256 j
+    __shared__ float ws[8][RB_TT][RB_EB];
+    __shared__ int last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int NCH = HIDDEN / 4, J = NCH / 256;
+    const int t0 = blockIdx.x * RB_TT, nt = min(RB_TT, p.T - t0);
+    const int per = p.n_experts / esplit, e0 = blockIdx.y * per;
+    float4 w[J];
+    rb_load_w(p, e0, tid, w);                     // router weights are never written by a kernel
+    pdl_trigger();
+    pdl_wait();
+    #pragma unroll
+    for (int t = 0; t < RB_TT; ++t)
+        #pragma unroll
+        for (int j = 0; j < J; ++j)
+            xt[t * NCH + tid + 256 * j] = t < nt ? ((const float4*)(p.x + (size_t)(t0 + t) * p.ld_x))[tid + 256 * j]
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int eb = e0; eb < e0 + per; eb += RB_EB) {
+        #pragma unroll 1
+        for (int k = 0; k < RB_EB; ++k) {
+            const int e = eb + k;
+            const bool more = e + 1 < e0 + per;
+            float4 wn[J];
+            if (more) rb_load_w(p, e + 1, tid, wn);   // the next row is in flight during this one's sums
+            float a[RB_TT];
+            #pragma unroll
+            for (int t = 0; t < RB_TT; ++t) {
+                a[t] = 0.0f;
+                #pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    const float4 xv = xt[t * NCH + tid + 256 * j];
+                    a[t] = fmaf(w[j].x, xv.x, a[t]);
+                    a[t] = fmaf(w[j].y, xv.y, a[t]);
+                    a[t] = fmaf(w[j].z, xv.z, a[t]);
+                    a[t] = fmaf(w[j].w, xv.w, a[t]);
+                }
+            }
+            #pragma unroll
+            for (int t = 0; t < RB_TT; ++t) {
+                #pragma unroll
+                for (int o = 16; o > 0; o >>= 1) a[t] = __fadd_rn(a[t], __shfl_xor_sync(0xffffffffu, a[t], o));
+                if (lane == 0) ws[warp][t][k] = a[t];
+            }
+            if (more) {
+                #pragma unroll
+                for (int j = 0; j < J; ++j) w[j] = wn[j];
+            }
+        }
+        __syncthreads();
+        if (tid < RB_TT * RB_EB) {
+            const int t = tid / RB_EB, k = tid % RB_EB;
+            if (t < nt) {
+                const float lg = __fadd_rn(__fadd_rn(__fadd_rn(ws[0][t][k], ws[1][t][k]), __fadd_rn(ws[2][t][k], ws[3][t][k])),
+                                           __fadd_rn(__fadd_rn(ws[4][t][k], ws[5][t][k]), __fadd_rn(ws[6][t][k], ws[7][t][k])));
+                const size_t o = (size_t)(t0 + t) * p.n_experts + eb + k;
+                p.logits[o] = lg;
+                const float v = p.logits_override ? p.logits_override[o] : lg;
+                p.probs[o] = lk_sigmoid(v);
+            }
+        }
+        __syncthreads();
+    }
+    if (!p.tile_count) return;
+    if (esplit > 1) {                             // as k_router_logits: acquire-release count per token tile
+        if (tid == 0) last = atom_add_acq_rel_gpu(&p.tile_count[blockIdx.x], 1) == esplit - 1;
+        __syncthreads();
+        if (!last) return;
+    }
+    if (warp < nt) router_topk_token(p, t0 + warp, lane);
+    if (esplit > 1) {
+        __syncthreads();
+        if (tid == 0) p.tile_count[blockIdx.x] = 0;   // ready for the next call
+    }
 }
 
 // warp argmax over (value, index) pairs, ties -> lower index; every lane returns the winner
@@ -303,13 +405,24 @@ __device__ void router_topk_cta(const RouterParams& p, int t) {
     }
 }
 
-// p.tile_count: ceil(T / 8) zeroed ints (the kernel leaves them zeroed again)
+// p.tile_count: T zeroed ints (one per token tile of 8, or of 4 for the batch kernel; left zeroed again)
 void launch_router(const RouterParams& p, cudaStream_t st) {
     const int ne = p.n_experts;
     if (p.T <= 1) launch_pdl(k_router_logits<1>, dim3(ne, 1), dim3(256), 0, st, p);
     else if (p.T <= 2) launch_pdl(k_router_logits<2>, dim3(ne, 1), dim3(256), 0, st, p);
     else if (p.T <= 4) launch_pdl(k_router_logits<4>, dim3(ne, 1), dim3(256), 0, st, p);
-    else launch_pdl(k_router_logits<8>, dim3(ne, (p.T + 7) / 8), dim3(256), 0, st, p);
+    else if (p.T < 64) launch_pdl(k_router_logits<8>, dim3(ne, (p.T + 7) / 8), dim3(256), 0, st, p);
+    else {                                        // batches: token tiles in shared memory, expert rows streamed
+        static bool attr = false;
+        if (!attr) { cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, RB_SMEM); attr = true; }
+        int dev = 0; cudaGetDevice(&dev);
+        const int tiles = (p.T + RB_TT - 1) / RB_TT, target = 2 * num_sms(dev);
+        int esplit = 1;                           // split the experts until there are ~2 CTAs per SM
+        while (tiles * esplit < target && (ne / (2 * esplit)) % RB_EB == 0) esplit *= 2;
+        RouterParams q = p;
+        q.esplit = esplit;
+        launch_pdl(k_router_batch, dim3(tiles, esplit), dim3(256), RB_SMEM, st, q);
+    }
 }
 
 }  // namespace lk
