@@ -125,7 +125,9 @@ class NativeEpOps:
         self.n_ranks, self.keep = n_ranks, keep
         self.home = MoeLayer(self.device, topk, keep, renorm, n_group, topk_group, scale, with_shared=True,
                              max_tokens=max_local_tokens)
-        self.expert = MoeLayer(self.device, topk, keep, renorm, n_group, topk_group, scale, with_shared=True,
+        # the shard context never routes (rows arrive with their experts chosen), so it takes the plain
+        # routing configuration whatever the home context's grouped mode
+        self.expert = MoeLayer(self.device, topk, keep, renorm, 1, 1, scale, with_shared=True,
                                max_tokens=max(1, n_ranks * max_local_tokens), n_experts=N_EXPERTS // n_ranks)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
 

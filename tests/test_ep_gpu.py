@@ -25,11 +25,11 @@ def _inputs(T_loc, rank):
             rng.standard_normal((T_loc, HIDDEN)).astype(np.float32))
 
 
-def _check_rank(oracle, W, x, r, h, moe, sel, w, keep=8):
+def _check_rank(oracle, W, x, r, h, moe, sel, w, keep=8, n_group=1):
     sel, w = sel.cpu().numpy(), w.cpu().numpy()
     Wr = W.router_w.float().cpu().numpy()
     bias = W.router_bias.cpu().numpy()
-    _, osel, ow = oracle.router(x, Wr, bias, oracle.route_cfg(8, keep, 1, 1, 1))
+    _, osel, ow = oracle.router(x, Wr, bias, oracle.route_cfg(8, keep, 1, n_group, 4 if n_group > 1 else 1))
     np.testing.assert_array_equal(sel, osel)
     np.testing.assert_array_equal(w, ow)
     ref = oracle_layer(oracle, SEED, 0, x, r, sel, w)
@@ -37,15 +37,17 @@ def _check_rank(oracle, W, x, r, h, moe, sel, w, keep=8):
     assert e_moe < RTOL_L2 and e_h < RTOL_L2, (e_moe, e_h)
 
 
-@pytest.mark.parametrize("n_ranks,T_loc,fixed_cap_max", [(2, 1, 8), (2, 5, 8), (4, 3, 8), (2, 12, 4)])
-def test_ep_emulated_ranks_one_gpu(native, oracle, n_ranks, T_loc, fixed_cap_max):
+@pytest.mark.parametrize("n_ranks,T_loc,fixed_cap_max,n_group", [(2, 1, 8, 1), (2, 5, 8, 1), (4, 3, 8, 1), (2, 12, 4, 1),
+                                                                 (2, 5, 8, 8), (4, 1, 8, 8)])
+def test_ep_emulated_ranks_one_gpu(native, oracle, n_ranks, T_loc, fixed_cap_max, n_group):
+    """n_group = 8: the DeepSeek-V3 grouped routing on the home rank (the shard contexts never route)."""
     from loki_b200.moe import LayerWeights
     from loki_b200.ep import EpMoeLayer, NativeEpOps
     from ep_ref import ThreadComm
     E = 256 // n_ranks
     comms = ThreadComm.group(n_ranks)
     shards = [LayerWeights("cuda", SEED, 0, n_experts=E, expert0=r * E) for r in range(n_ranks)]
-    ops = [NativeEpOps(0, n_ranks, T_loc) for _ in range(n_ranks)]
+    ops = [NativeEpOps(0, n_ranks, T_loc, n_group=n_group, topk_group=4 if n_group > 1 else 1) for _ in range(n_ranks)]
     for o in ops:
         o.set_gemm_threshold(1 << 20)              # the matvec path: same q8 scheme as the oracle
         o.set_mma_threshold(1 << 20)
@@ -71,7 +73,7 @@ def test_ep_emulated_ranks_one_gpu(native, oracle, n_ranks, T_loc, fixed_cap_max
     torch.cuda.synchronize()
     for rank in range(n_ranks):
         ops[rank].device_error()
-        _check_rank(oracle, shards[rank], *inputs[rank], *out[rank])
+        _check_rank(oracle, shards[rank], *inputs[rank], *out[rank], n_group=n_group)
 
 
 def _nccl_worker(rank, port, T_loc, fixed_cap_max, comm_kind, out_dir):
