@@ -47,6 +47,9 @@ struct FLCtx {
     // last narrow call (for fl_moe_outs)
     int last_n = 0, last_ke = 0; std::vector<int> last_ids; std::vector<float> last_w;
     int last_err = 0; int prep_n = 0;
+    // the shared expert of the last fl_moe_prepare, not yet computed: fl_moe_auto folds it into its own
+    // expert launches; fl_moe / fl_skip compute it first (ensure_shared)
+    bool sh_pending = false; const void* sh_w[3] = {nullptr, nullptr, nullptr};
     // CUDA graphs of repeated call shapes (fl_moe_prepare, fl_moe, fl_moe_auto): one replay instead of a
     // dozen launches and copies.  A shape is captured on its second occurrence (the first runs directly).
     struct GraphKey { int kind, a, b, c, d; const void* p[8]; };
@@ -110,7 +113,8 @@ FLCtx* fl_init(int kvp, int sc_cap) {
     cudaGetDevice(&c->dev);
     c->nsm = num_sms(c->dev);
     const size_t R = (size_t)PREP_ROWS * HIDDEN;
-    const size_t rows = (size_t)std::max(NARROW_SLOTS, PREP_ROWS);    // hq / y rows of a narrow or prepare launch
+    // hq / y rows of a narrow launch (n*KE routed + n shared entries) or a prepare launch
+    const size_t rows = (size_t)std::max(NARROW_SLOTS + NB, PREP_ROWS);
     const int ms = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1);
     bool ok =
         cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) == cudaSuccess &&
@@ -223,6 +227,22 @@ static void shared_slots(FLCtx* c, int n, int nt) {
     k_shared_slots<<<1, 64, 0, c->st>>>(n, nt, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n);
 }
 
+// the shared expert (IQ2_XXS) of rows [0, n) of ncur into shared_y, as its own launches
+static void enqueue_shared(FLCtx* c, const void* g, const void* u, const void* d, int n) {
+    const int nt = nt_for(n);
+    shared_slots(c, n, nt);
+    ExpertParams e = expert_params(c, nullptr, nullptr, nullptr, 0, 0, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n,
+                                   c->hq, c->hd, c->shared_y);
+    e.sh_gate = (const uint8_t*)g; e.sh_up = (const uint8_t*)u; e.sh_down = (const uint8_t*)d;
+    launch_gate_up(e, nt, c->nsm, c->st);
+    launch_down(e, nt, c->nsm, c->st);
+}
+static void ensure_shared(FLCtx* c) {
+    if (!c->sh_pending) return;
+    enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], c->prep_n);
+    c->sh_pending = false;
+}
+
 void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
     if (!c || !W || !ncur || !ffn_inp || N < 1 || N > PREP_ROWS) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: bad argument"); return; }
     if (wrow >= 0 && (!c->ncur_all || wrow + N > c->wmax)) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: wide rows outside fl_wide_init capacity"); return; }
@@ -230,6 +250,8 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     const size_t bytes = (size_t)N * HIDDEN * 4;
     if (host) { std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes); }
     c->prep_n = N;
+    c->sh_pending = W->sh_gate && W->sh_up && W->sh_down && wrow < 0;
+    c->sh_w[0] = W->sh_gate; c->sh_w[1] = W->sh_up; c->sh_w[2] = W->sh_down;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
     key.kind = 1; key.a = N; key.b = host; key.c = wrow; key.d = W->gate_f16;
@@ -250,16 +272,10 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     rp.logits = c->logits; rp.probs = c->probs; rp.sel = c->sel; rp.w = c->wts; rp.tile_count = c->rcount;
     rp.n_experts = N_EXPERTS; rp.topk = MAX_TOPK; rp.keep = MAX_TOPK; rp.renorm = 0; rp.n_group = 1; rp.topk_group = 1; rp.scale = 2.5f;
     launch_router(rp, st);
-    // shared expert on all rows
-    if (W->sh_gate && W->sh_up && W->sh_down) {
-        const int nt = nt_for(N);
-        shared_slots(c, N, nt);
-        ExpertParams e = expert_params(c, nullptr, nullptr, nullptr, 0, 0, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n,
-                                       c->hq, c->hd, c->shared_y);
-        e.sh_gate = (const uint8_t*)W->sh_gate; e.sh_up = (const uint8_t*)W->sh_up; e.sh_down = (const uint8_t*)W->sh_down;
-        launch_gate_up(e, nt, c->nsm, st);
-        launch_down(e, nt, c->nsm, st);
-    } else {
+    // shared expert on all rows: now for a wide pass (its base rows need it), else when first needed
+    if (W->sh_gate && W->sh_up && W->sh_down && wrow >= 0) {
+        enqueue_shared(c, W->sh_gate, W->sh_up, W->sh_down, N);
+    } else if (!(W->sh_gate && W->sh_up && W->sh_down)) {
         FLCK(cudaMemsetAsync(c->shared_y, 0, bytes, st));
     }
     if (wrow >= 0) {                  // wide pass: this group's ncur and base = ffn_inp + shared
@@ -296,11 +312,12 @@ void fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
 
 // the narrow pass from routing already on the device (c->ids, c->w [n][KE]): slots, experts, combine, and the
 // result copies into the pinned mirrors (h, moe; with ids_back also the routing), then the stream sync
-static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int n, bool ids_back) {
+static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int n, bool ids_back,
+                           bool fold_shared = false) {
     cudaStream_t st = c->st;
     const int nt = down_fmt == FL_IQ2 ? nt_for(n) : 1;      // the K-quant down kernel takes single-token slots
     SlotParams sp{};
-    sp.sel = c->ids; sp.w = c->w; sp.T = n; sp.keep = KE; sp.n_experts = N_EXPERTS; sp.nt = nt; sp.with_shared = 0;
+    sp.sel = c->ids; sp.w = c->w; sp.T = n; sp.keep = KE; sp.n_experts = N_EXPERTS; sp.nt = nt; sp.with_shared = fold_shared ? 1 : 0;
     sp.counts = c->counts; sp.offsets = c->offsets; sp.perm = c->perm;
     sp.slot_expert = c->s_expert; sp.slot_tok = c->s_tok; sp.slot_out = c->s_out; sp.slot_w = c->s_w; sp.nslots = c->s_n;
     sp.max_slots = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1); sp.err = c->err;
@@ -308,12 +325,18 @@ static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const voi
     const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)down_matrix_bytes(down_fmt);
     ExpertParams e = expert_params(c, gate, up, down, sg, sd, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->hq, c->hd, c->y);
     e.down_fmt = down_fmt;
+    if (fold_shared) {                            // the shared expert as n more slots of the same launches
+        e.sh_gate = (const uint8_t*)c->sh_w[0]; e.sh_up = (const uint8_t*)c->sh_w[1]; e.sh_down = (const uint8_t*)c->sh_w[2];
+    }
     launch_gate_up(e, nt, c->nsm, st);
     launch_down(e, nt, c->nsm, st);
-    CombineParams cp{};                           // h = ffn_inp + shared (from fl_moe_prepare) + routed
-    cp.y = c->y; cp.resid = c->ffn_inp; cp.T = n; cp.keep = KE; cp.with_shared = 0; cp.shared = c->shared_y;
+    CombineParams cp{};                           // h = ffn_inp + shared + routed
+    cp.y = c->y; cp.resid = c->ffn_inp; cp.T = n; cp.keep = KE; cp.with_shared = fold_shared ? 1 : 0;
+    cp.shared = fold_shared ? nullptr : c->shared_y;
     cp.h = c->h; cp.moe = c->moe; cp.ld_out = HIDDEN;
     launch_combine(cp, st);
+    if (fold_shared)                              // keep shared_y what fl_moe_prepare would have left
+        FLCK(cudaMemcpyAsync(c->shared_y, c->y + (size_t)n * KE * HIDDEN, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToDevice, st));
     FLCK(cudaMemcpyAsync(c->h_h, c->h, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
     FLCK(cudaMemcpyAsync(c->h_moe, c->moe, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
     if (ids_back) {
@@ -347,11 +370,16 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     int* hi = c->h_tab; float* hw = c->h_tabw;
     std::memcpy(hi, ids, (size_t)n * KE * 4); std::memcpy(hw, w, (size_t)n * KE * 4);
     c->last_ids.assign(ids, ids + n * KE); c->last_w.assign(w, w + n * KE);
+    const bool pend = c->sh_pending;              // the prepare's shared expert, in this call's launches
+    const int pn = c->prep_n;
+    c->sh_pending = false;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
-    key.kind = 2; key.a = n; key.b = KE; key.c = down_fmt;
+    key.kind = 2; key.a = n; key.b = KE; key.c = down_fmt; key.d = pend ? pn : 0;
     key.p[0] = gate; key.p[1] = up; key.p[2] = down;
+    if (pend) { key.p[3] = c->sh_w[0]; key.p[4] = c->sh_w[1]; key.p[5] = c->sh_w[2]; }
     run_graph(c, key, [&]() {
+        if (pend) enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], pn);
         FLCK(rec(c->em0, st));
         FLCK(cudaMemcpyAsync(c->ids, hi, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
         FLCK(cudaMemcpyAsync(c->w, hw, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
@@ -407,14 +435,20 @@ void fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, i
     if (n < 1 || n > NB || n > c->prep_n || KE < 1 || KE > MAX_TOPK) { fl_fail(c, LK_ERR_ARG, "fl_moe_auto: bad argument (n <= 8 rows of the last fl_moe_prepare)"); return; }
     if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_moe_auto: arena not 16-byte aligned"); return; }
     cudaStream_t st = c->st;
+    // the pending shared expert (IQ2_XXS) joins the routed launches when the downs are IQ2_XXS too; with a
+    // K-quant down format it runs on its own first
+    const bool fold = c->sh_pending && down_fmt == FL_IQ2 && n == c->prep_n;
+    if (!fold) ensure_shared(c);
+    c->sh_pending = false;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
-    key.kind = 3; key.a = n; key.b = KE; key.c = down_fmt; key.d = renorm;
+    key.kind = 3; key.a = n; key.b = KE; key.c = down_fmt; key.d = renorm | (fold ? 2 : 0);
     key.p[0] = gate; key.p[1] = up; key.p[2] = down;
+    if (fold) { key.p[3] = c->sh_w[0]; key.p[4] = c->sh_w[1]; key.p[5] = c->sh_w[2]; }
     run_graph(c, key, [&]() {
         FLCK(rec(c->em0, st));
         k_fl_keep<<<1, 64, 0, st>>>(c->sel, c->wts, n, KE, renorm, c->ids, c->w);
-        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, true);
+        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, true, fold);
     });
     finish_narrow(c, KE, n, true, out);
 }
@@ -425,6 +459,7 @@ void fl_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
     if (!c || !out || !mo || n < 1 || n > PREP_ROWS) return;
     std::memset(out, 0, sizeof(FLOut));
     cudaStream_t st = c->st;
+    ensure_shared(c);
     std::memcpy(c->h_in, mo, (size_t)n * HIDDEN * 4);
     FLCK(cudaMemcpyAsync(c->mo, c->h_in, (size_t)n * HIDDEN * 4, cudaMemcpyHostToDevice, st));
     CombineParams cp{};
