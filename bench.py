@@ -44,6 +44,15 @@ def down_bytes(args):
     return HIDDEN * (INTER // 256) * DOWN_FMTS[args.down_fmt][1]
 
 
+FMT_Q5K = 3                                              # --shared-fmt q5k: Q5_K gate/up + Q6_K down (the real model's)
+SH_MODEL_BYTES = 2 * INTER * (HIDDEN // 256) * 176 + HIDDEN * (INTER // 256) * 210   # 32 227 328
+
+
+def shared_bytes(args):
+    """Bytes of the shared expert's three matrices in the decode workload."""
+    return SH_MODEL_BYTES if args.shared_fmt == "q5k" else 2 * MAT + down_bytes(args)
+
+
 # DeepSeek-R1 routing (BASELINE config 0, inherited by configs 1-4): 8 groups of 32 experts, top 4 groups
 N_GROUP, TOPK_GROUP = 8, 4
 
@@ -202,14 +211,14 @@ def cpu_decode_sample(n_layers, keep=8, seed=SEED):
 
 
 # ------------------------------------------------------------------ decode workload (config 1)
-def build_decode(dev, n_layers, keep, fmt=4, ds=MAT):
+def build_decode(dev, n_layers, keep, fmt=4, ds=MAT, sh_fmt=4, sh_bytes=None):
     import torch
     from loki_b200 import moe as M
     free, total = torch.cuda.mem_get_info(dev)
-    per_layer = (2 * NE + 2) * MAT + (NE + 1) * ds + ROUTER_BYTES
+    per_layer = 2 * NE * MAT + NE * ds + (2 * MAT + ds if sh_bytes is None else sh_bytes) + ROUTER_BYTES
     fit = int((free - (6 << 30)) // per_layer)
     distinct = max(1, min(n_layers, fit))
-    layers = [M.LayerWeights(dev, SEED, L, down_fmt=fmt) for L in range(distinct)]
+    layers = [M.LayerWeights(dev, SEED, L, down_fmt=fmt, sh_fmt=sh_fmt) for L in range(distinct)]
     torch.cuda.synchronize(dev)
     return layers, distinct
 
@@ -222,7 +231,9 @@ def run_decode(args, ws, rank, local, dist):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     fmt, DS = DOWN_FMTS[args.down_fmt][0], down_bytes(args)
-    layers, distinct = build_decode(dev, args.layers, args.keep, fmt, DS)
+    model_sh = args.shared_fmt == "q5k"
+    SHB = shared_bytes(args)
+    layers, distinct = build_decode(dev, args.layers, args.keep, fmt, DS, FMT_Q5K if model_sh else 4, SHB)
     layer_of = [L % distinct for L in range(args.layers)]
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     xs = torch.randn(args.layers, 1, HIDDEN, device=dev, generator=g)
@@ -292,10 +303,10 @@ def run_decode(args, ws, rank, local, dist):
     tokens = args.steps * ws
     value = tokens / (ms_max / 1e3)
     hbm, bf16, peak_kind = measured_peaks()
-    n_slots = args.keep + 1
-    gu_bytes = n_slots * 2 * MAT + 4 * HIDDEN                       # 8 routed + shared gate/up rows, x in
+    n_slots = args.keep + (0 if model_sh else 1)                     # the model-format shared expert has own launches
+    gu_bytes = n_slots * 2 * MAT + 4 * HIDDEN                       # routed (+ IQ2_XXS shared) gate/up rows, x in
     dn_bytes = n_slots * DS + n_slots * (INTER + INTER // 32 * 4) + n_slots * HIDDEN * 4
-    layer_bytes = n_slots * (2 * MAT + DS) + ROUTER_BYTES + 3 * 4 * HIDDEN
+    layer_bytes = args.keep * (2 * MAT + DS) + SHB + ROUTER_BYTES + 3 * 4 * HIDDEN
     gu_ms = float(gu.mean())
     achieved = gu_bytes / (gu_ms / 1e3) / 1e9
     traffic = ncu_traffic("k_gate_up", "decode_T1")
@@ -303,11 +314,15 @@ def run_decode(args, ws, rank, local, dist):
         "metric": "MoE-layer tokens/s (T=1 decode through 58 layers)", "value": round(value, 2), "unit": "tokens/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "iq2_xxs x q8 (int8 dp4a, fp32 accumulate)" if fmt == 4 else "iq2_xxs gate/up, %s down x q8 (int8 dp4a, fp32 accumulate)" % args.down_fmt,
+        "dtype": ("iq2_xxs x q8 (int8 dp4a, fp32 accumulate)" if fmt == 4 else
+                  "iq2_xxs gate/up, %s down x q8 (int8 dp4a, fp32 accumulate)" % args.down_fmt) +
+                 ("; shared expert q5_k/q6_k x q8" if model_sh else ""),
         "data": "synthetic: seeded IQ2_XXS experts (BASELINE config 0 generator), router W N(0,0.02), bias N(0,0.01), x/resid N(0,1) fp32",
-        "config": {"workload": "config1_decode_T1_58layers" if fmt == 4 else "decode_T1_58layers_%s_down" % args.down_fmt,
-                   "model": "DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)" if fmt == 4 else
-                            "DeepSeek-R1 MoE layer (IQ2_XXS gate/up, %s down as in the real model, 256 experts + shared)" % args.down_fmt,
+        "config": {"workload": ("config1_decode_T1_58layers" if fmt == 4 else "decode_T1_58layers_%s_down" % args.down_fmt) +
+                               ("_q5k_q6k_shared" if model_sh else ""),
+                   "model": ("DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)" if fmt == 4 else
+                             "DeepSeek-R1 MoE layer (IQ2_XXS gate/up, %s down as in the real model, 256 experts + shared)" % args.down_fmt) +
+                            ("; shared expert Q5_K gate/up + Q6_K down as in the real model" if model_sh else ""),
                    "global_batch": ws, "seq_len": 1, "layers": args.layers, "distinct_layers_resident": distinct,
                    "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP, "keep": args.keep, "parallelism": "replicas" if ws > 1 else "single",
                    "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (args.layers * layer_bytes / 1e9)},
@@ -317,14 +332,17 @@ def run_decode(args, ws, rank, local, dist):
                   "frac_of_hbm": round(layer_bytes * args.layers * args.steps / (ms_max / 1e3) / 1e9 / hbm, 4),
                   # per-kernel times come from a second capture with event nodes between the kernels, which
                   # serialise them; in the timed graph each kernel's prologue overlaps its predecessor
-                  # (programmatic dependent launch), so "rest" (layer minus the two) can be negative
+                  # (programmatic dependent launch), so "rest" (layer minus the two) can be negative.  With the
+                  # model-format shared expert its two launches (before the routed ones) fall into "rest".
                   "kernel_us_event_graph": {"gate_up": round(gu_ms * 1e3, 2), "down_combine": round(float(dn.mean()) * 1e3, 2),
                                             "rest": round(ms_max / args.steps / args.layers * 1e3 - gu_ms * 1e3 - float(dn.mean()) * 1e3, 2)}},
-        "roofline": {"kernel": "k_gate_up<1> (routed + shared gate/up + SwiGLU + q8)", "bound": "hbm",
+        "roofline": {"kernel": "k_gate_up<1> (routed + shared gate/up + SwiGLU + q8)" if not model_sh else
+                               "k_gate_up<1> (routed gate/up + SwiGLU + q8)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "traffic": traffic, "algorithmic_bytes_per_launch": gu_bytes, "peak_source": peak_kind,
                      "down_kernel_frac": round(dn_bytes / (float(dn.mean()) / 1e3) / 1e9 / hbm, 4)},
-        "gpu_launches": args.steps * args.layers * 4,      # per layer: router (+top-k), gate/up, down, combine
+        # per layer: router (+top-k), gate/up, down, combine (+ the model-format shared expert's gate/up and down)
+        "gpu_launches": args.steps * args.layers * (6 if model_sh else 4),
     }
     if cl:
         out["clocks"] = cl
@@ -634,7 +652,8 @@ def e2e_decode(args, layers, distinct, keep):
     for device_keep in (True, False):
         fc = F.FusedCtx()
         try:
-            sec, _ = F.replay_decode(fc, per_layer, xs, rs, keep, max(1, args.warmup), n, device_keep=device_keep)
+            sec, _ = F.replay_decode(fc, per_layer, xs, rs, keep, max(1, args.warmup), n, down_fmt=DOWN_FMTS[args.down_fmt][0],
+                                     device_keep=device_keep)
             out[device_keep] = (round(n / sec, 2), fc.error())
         finally:
             fc.close()
@@ -781,6 +800,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--down-fmt", default="iq2", choices=sorted(DOWN_FMTS),
                     help="decode workload: format of the down matrices (q2k / q3k: the real model's; no e2e or CPU leg)")
+    ap.add_argument("--shared-fmt", default="iq2", choices=["iq2", "q5k"],
+                    help="decode workload: the shared expert's formats (q5k: the real model's Q5_K gate/up + Q6_K down)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample (profiling runs)")
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU-baseline sample")
     ap.add_argument("--parallelism", default="ep", choices=["ep", "replicas"], help="N > 1: expert parallel or replicas")
@@ -819,8 +840,10 @@ def main():
             dist.destroy_process_group()
         return
     out, layers, ctx, structs, xs, rs = run_decode(args, ws, rank, local, dist)
-    if args.down_fmt != "iq2":
-        args.no_e2e = args.no_cpu = True            # fl_moe_prepare's shared expert and the CPU sample are IQ2_XXS
+    if args.down_fmt != "iq2" or args.shared_fmt != "iq2":
+        args.no_cpu = True                          # the CPU sample is the IQ2_XXS layer
+    if args.down_fmt != "iq2" and args.shared_fmt == "iq2":
+        args.no_e2e = True                          # fl_moe_prepare's IQ2_XXS shared expert has IQ2_XXS downs
     if not args.no_e2e:
         e2e = e2e_decode(args, layers, len(layers), args.keep)
         e2e_v = max_over_ranks(dist, 1.0 / e2e["value"])

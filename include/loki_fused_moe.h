@@ -69,6 +69,7 @@ typedef struct FLOut {
 typedef struct FLMoeW {
     const void* gate_inp; int gate_f16; const float* probs_b;
     const void* sh_gate; const void* sh_up; const void* sh_down;
+    int sh_fmt;     /* 0 / FL_IQ2: IQ2_XXS shared expert (IQ2_XXS down); FL_Q5K: the real model's Q5_K gate/up + Q6_K down */
 } FLMoeW;
 
 LK_API FLCtx* fl_init(int kvp, int sc_cap);

@@ -43,7 +43,7 @@ enum {
     LK_ERR_DEVICE = -5        /* a kernel recorded an error (bounded wait expired, bad slot) */
 };
 
-enum { LK_FMT_IQ2 = 4, LK_FMT_Q2K = 5, LK_FMT_Q3K = 6 };   /* numerically equal to FL_IQ2/FL_Q2K/FL_Q3K */
+enum { LK_FMT_Q6K = 1, LK_FMT_Q5K = 3, LK_FMT_IQ2 = 4, LK_FMT_Q2K = 5, LK_FMT_Q3K = 6 };   /* numerically equal to FL_* */
 
 typedef struct LkMoeConfig {
     int n_experts;      /* routed experts: 256, or an expert-parallel shard's count (the router needs 256) */
@@ -61,14 +61,18 @@ typedef struct LkMoeWeights {
     /* routed experts in the engine's arena layout: expert e's matrix at base + e * stride (bytes) */
     const void* gate; const void* up; const void* down;
     int64_t gate_stride, up_stride, down_stride;
-    int down_fmt;                 /* format of every down matrix, routed and shared: LK_FMT_IQ2, or the real model's
+    int down_fmt;                 /* format of every routed down matrix: LK_FMT_IQ2, or the real model's
                                      LK_FMT_Q2K / LK_FMT_Q3K (fl_moe's down_fmt, src/fused_layer.h:45); the K-quants
                                      run the single-token matvec path at every T (q8 SwiGLU output, as the reference) */
-    /* shared expert (IQ2_XXS gate/up, down in down_fmt, same shapes as one routed expert); null when with_shared == 0 */
+    /* shared expert, same shapes as one routed expert; null when with_shared == 0.  Formats: sh_fmt 0 or
+     * LK_FMT_IQ2 = IQ2_XXS gate/up with a down in down_fmt (run as extra slots of the routed launches);
+     * LK_FMT_Q5K = the real model's Q5_K gate/up and Q6_K down (src/fused_layer.h:14; own launches, the
+     * reference's shared-expert numerics: q8 x, per-32 / per-16 integer sums, q8 SwiGLU output) */
     const void* sh_gate; const void* sh_up; const void* sh_down;
     /* router: weights [n_experts][7168] fp32 (router_w_f16 = 0) or fp16 (1); bias [n_experts] fp32 */
     const void* router_w; int router_w_f16;
     const float* router_bias;
+    int sh_fmt;
 } LkMoeWeights;
 
 LK_API int  lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out);

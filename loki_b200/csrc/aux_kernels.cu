@@ -49,7 +49,7 @@ void launch_combine(const CombineParams& p, cudaStream_t st) {
 // one CTA = 64 consecutive blocks of one expert matrix, staged in shared memory, written as 16-byte words
 __global__ void __launch_bounds__(64) k_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0,
                                                 int rows, int K, int64_t stride, int fmt) {
-    __shared__ __align__(16) uint8_t buf[64 * BLK_Q3K];
+    __shared__ __align__(16) uint8_t buf[64 * BLK_Q6K];        // the largest block (210 B)
     const int e = expert0 + blockIdx.y;
     const int nbytes = fmt_block_bytes(fmt);
     const uint64_t key = iq2_gen_key(seed, (uint32_t)layer, (uint32_t)matrix, (uint32_t)e);

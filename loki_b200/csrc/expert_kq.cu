@@ -1,5 +1,5 @@
-// expert_kq.cu -- the down projection for K-quant experts (Q2_K, Q3_K): the real DeepSeek-R1
-// IQ2_XXS model's down matrices (the reference's tc_matvec<F_Q2K / F_Q3K>, src/fused_layer.cu:203-254,
+// expert_kq.cu -- the down projection for K-quant experts (Q2_K, Q3_K, Q6_K): the real DeepSeek-R1
+// IQ2_XXS model's routed down matrices and its shared expert's down (the reference's tc_matvec<F_Q2K / F_Q3K>, src/fused_layer.cu:203-254,
 // launched at :608 and :550).
 //
 // Contract as k_down1 (expert_gemv1.cu): single-token slots, the slot's SwiGLU output as q8 (hq, hd),
@@ -14,8 +14,14 @@
 //   Q2_K: isum = sum q_w * q_x (dp4a over 2-bit fields), v += dx * (d*sc*isum - dmin*m*sum q_x)
 //   Q3_K: w3 = low2 | hbit << 2 (0..7, value w3 - 4), isum = dp4a(w3, x) - 4 * sum q_x,
 //         v += dx * d * (scale - 32) * isum
-// the reference's per-16 arithmetic with exact integer sums.  Q3_K blocks (110 B) are only 2-byte aligned
-// in shared memory, so their words are read as aligned pairs and funnel-shifted.
+//   Q6_K (the real model's shared down, :131-158): q6 = low4 | high2 << 4 (0..63, value q6 - 32),
+//         isum = dp4a(q6, x) - 32 * sum q_x, v += dx * d * scale * isum (int8 scales, one word per quarter)
+// the reference's per-16 arithmetic with exact integer sums.  Q3_K (110 B) and Q6_K (210 B) blocks are only
+// 2-byte aligned in shared memory, so their words are read as aligned pairs and funnel-shifted.  Q6_K units
+// are 53 760 B, so its ring has one stage per group (4) instead of two.
+// Shared-only mode (slot_expert == null, launch_shared_kq): slot j is the shared expert of token j, written to
+// y row sh_row0 + j with weight 1; with sh_gu set, each lane forms SwiGLU and the q8 of its own 64 h values
+// (two whole q8 groups) from the fp32 gate/up rows.
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
@@ -33,21 +39,24 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
 template <int FMT> struct KqFmt;
 template <> struct KqFmt<FMT_Q2K> { static constexpr int BLK = BLK_Q2K; };
 template <> struct KqFmt<FMT_Q3K> { static constexpr int BLK = BLK_Q3K; };
+template <> struct KqFmt<FMT_Q6K> { static constexpr int BLK = BLK_Q6K; };
 
 constexpr int KQ_WARPS = 16;
 constexpr int KQ_THREADS = (KQ_WARPS + 1) * 32;
 constexpr int KQ_WROWS = 8;                          // rows per warp
 constexpr int KQ_UROWS = 32;                         // rows per unit (one bulk copy)
 constexpr int KQ_GROUPS = KQ_WARPS / (KQ_UROWS / KQ_WROWS);   // 4 groups of 4 warps
-constexpr int KQ_NST = 2 * KQ_GROUPS;                // group g uses stages g and g + 4
 constexpr int KQ_UNITS_PER_SLOT = HIDDEN / KQ_UROWS; // 224
 
-template <int FMT> constexpr int kq_rowb() { return (MOE_INTER / QK) * KqFmt<FMT>::BLK; }     // 672 / 880
+template <int FMT> constexpr int kq_rowb() { return (MOE_INTER / QK) * KqFmt<FMT>::BLK; }     // 672 / 880 / 1680
 template <int FMT> constexpr int kq_ubytes() { return KQ_UROWS * kq_rowb<FMT>(); }
-template <int FMT> constexpr int kq_off_bar() { return KQ_NST * kq_ubytes<FMT>(); }
-template <int FMT> constexpr int kq_smem() { return kq_off_bar<FMT>() + 2 * KQ_NST * 8 + 16; }
-static_assert(kq_smem<FMT_Q3K>() <= 232448, "Q3_K ring exceeds shared memory");
-static_assert(kq_rowb<FMT_Q2K>() % 16 == 0 && kq_rowb<FMT_Q3K>() % 16 == 0, "bulk copies need 16-byte rows");
+// ring stages: group g uses stages g and g + 4; Q6_K's 53 760-byte units allow one stage per group
+template <int FMT> constexpr int kq_nst() { return FMT == FMT_Q6K ? KQ_GROUPS : 2 * KQ_GROUPS; }
+template <int FMT> constexpr int kq_off_bar() { return kq_nst<FMT>() * kq_ubytes<FMT>(); }
+template <int FMT> constexpr int kq_smem() { return kq_off_bar<FMT>() + 2 * kq_nst<FMT>() * 8 + 16; }
+static_assert(kq_smem<FMT_Q3K>() <= 232448 && kq_smem<FMT_Q6K>() <= 232448, "K-quant ring exceeds shared memory");
+static_assert(kq_rowb<FMT_Q2K>() % 16 == 0 && kq_rowb<FMT_Q3K>() % 16 == 0 && kq_rowb<FMT_Q6K>() % 16 == 0,
+              "bulk copies need 16-byte rows");
 
 __device__ __forceinline__ const uint8_t* kq_down_matrix(const ExpertParams& p, int e) {
     return e == SHARED_SLOT ? p.sh_down : p.down + (size_t)e * p.down_stride;
@@ -79,6 +88,37 @@ __device__ __forceinline__ float kq_row_dot(uint32_t blk, uint32_t sh, int q, co
                 const float t = fmaf(d * (float)(scb & 15u), (float)isum, -(dmin * (float)(scb >> 4)) * (float)xs[2 * jj + s]);
                 v = fmaf(dx[jj], t, v);
             }
+        }
+    } else if (FMT == FMT_Q6K) {                         // block 2-byte aligned: blk = aligned base, sh = 0 or 16
+        // quarter q: ql bytes 64n..64n+63 at nibble q & 1, qh bytes 128+32n.. at bit pairs 4(q&1) + 2(s16>>1),
+        // int8 scales 4q..4q+3 (one word), 16-weight sub-block s16 = weights 64q + 16 s16 ..
+        const int hs = q & 1;
+        uint32_t ql[16], qh[8];
+        {
+            uint32_t a[17];
+            #pragma unroll
+            for (int w = 0; w < 17; ++w) a[w] = lds_u32(blk + 64 * n + 4 * w);
+            #pragma unroll
+            for (int w = 0; w < 16; ++w) ql[w] = __funnelshift_r(a[w], a[w + 1], sh);
+            #pragma unroll
+            for (int w = 0; w < 9; ++w) a[w] = lds_u32(blk + Q6K_QH + 32 * n + 4 * w);
+            #pragma unroll
+            for (int w = 0; w < 8; ++w) qh[w] = __funnelshift_r(a[w], a[w + 1], sh);
+        }
+        const uint32_t scw = __funnelshift_r(lds_u32(blk + Q6K_SC + 4 * q), lds_u32(blk + Q6K_SC + 4 * q + 4), sh);
+        const float d = __half2float(__ushort_as_half((uint16_t)lds_u16(blk + Q6K_D + (sh >> 3))));
+        #pragma unroll
+        for (int s16 = 0; s16 < 4; ++s16) {
+            int isum = 0;
+            #pragma unroll
+            for (int w = 0; w < 4; ++w) {
+                const uint32_t q6 = ((ql[4 * s16 + w] >> (4 * hs)) & 0x0F0F0F0Fu) |
+                                    (((qh[4 * (s16 & 1) + w] >> (4 * hs + 2 * (s16 >> 1))) & 0x03030303u) << 4);
+                isum = __dp4a((int)q6, (int)xr[4 * s16 + w], isum);
+            }
+            isum -= 32 * xs[s16];
+            const int scale = (int)(int8_t)(uint8_t)((scw >> (8 * s16)) & 0xFFu);
+            v = fmaf(dx[s16 >> 1] * (d * (float)scale), (float)isum, v);
         }
     } else {                                             // block 2-byte aligned: blk = aligned base, sh = 0 or 16
         uint32_t hm[8], qs[8];
@@ -125,7 +165,7 @@ __device__ __forceinline__ float kq_row_dot(uint32_t blk, uint32_t sh, int q, co
 
 template <int FMT>
 __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
-    constexpr int RB = kq_rowb<FMT>(), UB = kq_ubytes<FMT>();
+    constexpr int RB = kq_rowb<FMT>(), UB = kq_ubytes<FMT>(), KQ_NST = kq_nst<FMT>();
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem;
     uint64_t* full = (uint64_t*)(smem + kq_off_bar<FMT>());
@@ -140,7 +180,8 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
     __syncthreads();
     pdl_trigger();
     pdl_wait();
-    const int nslots = *p.nslots;
+    const bool sh_only = p.slot_expert == nullptr;   // shared-only slots (launch_shared_kq)
+    const int nslots = sh_only ? p.sh_count : *p.nslots;
     const int nunits = nslots * KQ_UNITS_PER_SLOT;
     const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x);
     const int nu = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x) - u0;
@@ -152,7 +193,7 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
                 const int u = u0 + j, s = u / KQ_UNITS_PER_SLOT, cu = u % KQ_UNITS_PER_SLOT;
                 const int st = j % KQ_NST;
                 if (*abort_flag || !mbar_wait(&empty[st], ((j / KQ_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
-                const uint8_t* dw = kq_down_matrix(p, p.slot_expert[s]);
+                const uint8_t* dw = kq_down_matrix(p, sh_only ? SHARED_SLOT : p.slot_expert[s]);
                 mbar_arrive_expect_tx(&full[st], UB);
                 bulk_g2s(ring + st * UB, dw + (size_t)cu * UB, UB, &full[st]);
             }
@@ -175,8 +216,26 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
     for (int j = grp; j < nu; j += KQ_GROUPS) {
         const int u = u0 + j, s = u / KQ_UNITS_PER_SLOT, cu = u % KQ_UNITS_PER_SLOT;
         if (s != xslot) {                             // this slot's h (q8): K [256b + 64q, +64)
-            xslot = s; out = p.slot_out[s]; wv = p.slot_w[s];
-            if (out >= 0) {
+            xslot = s; out = sh_only ? p.sh_row0 + s : p.slot_out[s]; wv = sh_only ? 1.0f : p.slot_w[s];
+            if (sh_only && p.sh_gu) {                 // SwiGLU + q8 of this lane's two h groups from fp32 gate/up
+                const float* gr = p.sh_gu + (size_t)s * 2 * MOE_INTER + b * QK + 64 * q;
+                #pragma unroll
+                for (int hg = 0; hg < 2; ++hg) {
+                    float hv[32];
+                    #pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float4 gv = ((const float4*)(gr + 32 * hg))[i], uv = ((const float4*)(gr + MOE_INTER + 32 * hg))[i];
+                        hv[4*i] = lk_swiglu(gv.x, uv.x); hv[4*i+1] = lk_swiglu(gv.y, uv.y);
+                        hv[4*i+2] = lk_swiglu(gv.z, uv.z); hv[4*i+3] = lk_swiglu(gv.w, uv.w);
+                    }
+                    int8_t qv[32];
+                    dx[hg] = quant_q8_group(hv, qv);
+                    #pragma unroll
+                    for (int w = 0; w < 8; ++w)
+                        xr[8 * hg + w] = (uint32_t)(uint8_t)qv[4*w] | ((uint32_t)(uint8_t)qv[4*w+1] << 8) |
+                                         ((uint32_t)(uint8_t)qv[4*w+2] << 16) | ((uint32_t)(uint8_t)qv[4*w+3] << 24);
+                }
+            } else if (out >= 0) {
                 const uint4* src = (const uint4*)(p.hq + (size_t)out * MOE_INTER + b * QK + 64 * q);
                 #pragma unroll
                 for (int c = 0; c < 4; ++c) { const uint4 a = src[c]; xr[4*c] = a.x; xr[4*c+1] = a.y; xr[4*c+2] = a.z; xr[4*c+3] = a.w; }
@@ -220,6 +279,7 @@ template <int FMT> void kq_launch(const ExpertParams& p, int grid, cudaStream_t 
 
 void launch_down1_kq(const ExpertParams& p, int grid, cudaStream_t st) {
     if (p.down_fmt == FMT_Q2K) kq_launch<FMT_Q2K>(p, grid, st);
+    else if (p.down_fmt == FMT_Q6K) kq_launch<FMT_Q6K>(p, grid, st);
     else kq_launch<FMT_Q3K>(p, grid, st);
 }
 

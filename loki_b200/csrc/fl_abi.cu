@@ -49,7 +49,8 @@ struct FLCtx {
     int last_err = 0; int prep_n = 0;
     // the shared expert of the last fl_moe_prepare, not yet computed: fl_moe_auto folds it into its own
     // expert launches; fl_moe / fl_skip compute it first (ensure_shared)
-    bool sh_pending = false; const void* sh_w[3] = {nullptr, nullptr, nullptr};
+    bool sh_pending = false; const void* sh_w[3] = {nullptr, nullptr, nullptr}; int sh_fmt = 0;
+    float* sh_gu = nullptr;           // fp32 gate/up rows of the real model's shared expert (shared_kq.cu)
     // CUDA graphs of repeated call shapes (fl_moe_prepare, fl_moe, fl_moe_auto): one replay instead of a
     // dozen launches and copies.  A shape is captured on its second occurrence (the first runs directly).
     struct GraphKey { int kind, a, b, c, d; const void* p[8]; };
@@ -121,6 +122,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
         dz(&c->ncur, R) == cudaSuccess && dz(&c->ffn_inp, R) == cudaSuccess && dz(&c->logits, PREP_ROWS * N_EXPERTS) == cudaSuccess &&
         dz(&c->probs, PREP_ROWS * N_EXPERTS) == cudaSuccess && dz(&c->sel, PREP_ROWS * MAX_TOPK) == cudaSuccess &&
         dz(&c->wts, PREP_ROWS * MAX_TOPK) == cudaSuccess && dz(&c->shared_y, R) == cudaSuccess && dz(&c->h, R) == cudaSuccess &&
+        dz(&c->sh_gu, (size_t)PREP_ROWS * 2 * MOE_INTER) == cudaSuccess &&
         dz(&c->moe, R) == cudaSuccess && dz(&c->ids, NB * MAX_TOPK) == cudaSuccess && dz(&c->w, NB * MAX_TOPK) == cudaSuccess &&
         dz(&c->mo, R) == cudaSuccess &&
         dz(&c->s_expert, ms) == cudaSuccess && dz(&c->s_tok, (size_t)ms * MAX_NT) == cudaSuccess &&
@@ -142,7 +144,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
 void fl_free(FLCtx* c) {
     if (!c) return;
     if (c->st) cudaStreamSynchronize(c->st);
-    void* d[] = { c->ncur, c->ffn_inp, c->logits, c->probs, c->sel, c->wts, c->shared_y, c->h, c->moe, c->ids, c->w, c->mo,
+    void* d[] = { c->ncur, c->ffn_inp, c->logits, c->probs, c->sel, c->wts, c->shared_y, c->sh_gu, c->h, c->moe, c->ids, c->w, c->mo,
                   c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->counts, c->offsets, c->perm, c->hq, c->hd, c->y, c->err,
                   c->ncur_all, c->base_all, c->out_all, c->whq, c->whd, c->rcount };
     for (void* p : d) if (p) cudaFree(p);
@@ -227,8 +229,17 @@ static void shared_slots(FLCtx* c, int n, int nt) {
     k_shared_slots<<<1, 64, 0, c->st>>>(n, nt, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n);
 }
 
-// the shared expert (IQ2_XXS) of rows [0, n) of ncur into shared_y, as its own launches
-static void enqueue_shared(FLCtx* c, const void* g, const void* u, const void* d, int n) {
+// the shared expert of rows [0, n) of ncur into shared_y, as its own launches: IQ2_XXS (sh_fmt 0 / FL_IQ2)
+// through the routed kernels with shared-only slots, the real model's Q5_K / Q6_K (FL_Q5K) through shared_kq.cu
+static void enqueue_shared(FLCtx* c, const void* g, const void* u, const void* d, int n, int sh_fmt) {
+    if (sh_fmt == FL_Q5K) {
+        SharedKqParams sp{};
+        sp.gate = (const uint8_t*)g; sp.up = (const uint8_t*)u; sp.down = (const uint8_t*)d;
+        sp.x = c->ncur; sp.ld_x = HIDDEN; sp.t0 = 0; sp.n = n; sp.row0 = 0;
+        sp.gu = c->sh_gu; sp.y = c->shared_y; sp.err = c->err;
+        launch_shared_kq(sp, c->nsm, c->st);
+        return;
+    }
     const int nt = nt_for(n);
     shared_slots(c, n, nt);
     ExpertParams e = expert_params(c, nullptr, nullptr, nullptr, 0, 0, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n,
@@ -239,22 +250,23 @@ static void enqueue_shared(FLCtx* c, const void* g, const void* u, const void* d
 }
 static void ensure_shared(FLCtx* c) {
     if (!c->sh_pending) return;
-    enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], c->prep_n);
+    enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], c->prep_n, c->sh_fmt);
     c->sh_pending = false;
 }
 
 void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
     if (!c || !W || !ncur || !ffn_inp || N < 1 || N > PREP_ROWS) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: bad argument"); return; }
     if (wrow >= 0 && (!c->ncur_all || wrow + N > c->wmax)) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: wide rows outside fl_wide_init capacity"); return; }
+    if (W->sh_fmt != 0 && W->sh_fmt != FL_IQ2 && W->sh_fmt != FL_Q5K) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe_prepare: shared-expert format must be FL_IQ2 or FL_Q5K"); return; }
     cudaStream_t st = c->st;
     const size_t bytes = (size_t)N * HIDDEN * 4;
     if (host) { std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes); }
     c->prep_n = N;
     c->sh_pending = W->sh_gate && W->sh_up && W->sh_down && wrow < 0;
-    c->sh_w[0] = W->sh_gate; c->sh_w[1] = W->sh_up; c->sh_w[2] = W->sh_down;
+    c->sh_w[0] = W->sh_gate; c->sh_w[1] = W->sh_up; c->sh_w[2] = W->sh_down; c->sh_fmt = W->sh_fmt == FL_Q5K ? FL_Q5K : 0;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
-    key.kind = 1; key.a = N; key.b = host; key.c = wrow; key.d = W->gate_f16;
+    key.kind = 1; key.a = N; key.b = host; key.c = wrow; key.d = W->gate_f16 | (c->sh_fmt << 4);
     const void* kp[8] = { W->gate_inp, W->probs_b, W->sh_gate, W->sh_up, W->sh_down, host ? nullptr : ncur, host ? nullptr : ffn_inp, nullptr };
     std::memcpy(key.p, kp, sizeof(kp));
     run_graph(c, key, [&]() {
@@ -274,7 +286,7 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     launch_router(rp, st);
     // shared expert on all rows: now for a wide pass (its base rows need it), else when first needed
     if (W->sh_gate && W->sh_up && W->sh_down && wrow >= 0) {
-        enqueue_shared(c, W->sh_gate, W->sh_up, W->sh_down, N);
+        enqueue_shared(c, W->sh_gate, W->sh_up, W->sh_down, N, c->sh_fmt);
     } else if (!(W->sh_gate && W->sh_up && W->sh_down)) {
         FLCK(cudaMemsetAsync(c->shared_y, 0, bytes, st));
     }
@@ -375,11 +387,11 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     c->sh_pending = false;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
-    key.kind = 2; key.a = n; key.b = KE; key.c = down_fmt; key.d = pend ? pn : 0;
+    key.kind = 2; key.a = n; key.b = KE; key.c = down_fmt; key.d = pend ? pn | (c->sh_fmt << 16) : 0;
     key.p[0] = gate; key.p[1] = up; key.p[2] = down;
     if (pend) { key.p[3] = c->sh_w[0]; key.p[4] = c->sh_w[1]; key.p[5] = c->sh_w[2]; }
     run_graph(c, key, [&]() {
-        if (pend) enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], pn);
+        if (pend) enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], pn, c->sh_fmt);
         FLCK(rec(c->em0, st));
         FLCK(cudaMemcpyAsync(c->ids, hi, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
         FLCK(cudaMemcpyAsync(c->w, hw, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
@@ -436,8 +448,8 @@ void fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, i
     if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_moe_auto: arena not 16-byte aligned"); return; }
     cudaStream_t st = c->st;
     // the pending shared expert (IQ2_XXS) joins the routed launches when the downs are IQ2_XXS too; with a
-    // K-quant down format it runs on its own first
-    const bool fold = c->sh_pending && down_fmt == FL_IQ2 && n == c->prep_n;
+    // K-quant down format, or in the real model's Q5_K / Q6_K formats, it runs on its own first
+    const bool fold = c->sh_pending && c->sh_fmt == 0 && down_fmt == FL_IQ2 && n == c->prep_n;
     if (!fold) ensure_shared(c);
     c->sh_pending = false;
     FLCtx::GraphKey key;

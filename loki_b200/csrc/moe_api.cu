@@ -26,6 +26,9 @@ struct LkMoeCtx {
     bool xq_ready = false;            // set while a one-token forward's expert stage runs, for x == xq_src
     const float* xq_src = nullptr;
     int sh_t0 = 0, sh_n = 0;          // shared-expert token range of the next expert stage (SlotParams semantics)
+    // the shared expert in the real model's formats (W->sh_fmt == LK_FMT_Q5K) runs as its own launches
+    // (shared_kq.cu); the routed slot tables then carry no shared slots (rs = 0).  shgu: its fp32 gate/up rows
+    int rs = 0; float* shgu = nullptr;
     // tensor-core path (T >= gemm_min_tokens): 64-token slots and fp16 operand staging
     int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
     __half* bt = nullptr; __half* ht = nullptr; int* g_cnt = nullptr; int gemm_min_tokens = 192;
@@ -119,6 +122,7 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LK_CU(dalloc(&c->m_out, (size_t)c->m_max * MM_NT)); LK_CU(dalloc(&c->m_w, (size_t)c->m_max * MM_NT)); LK_CU(dalloc(&c->m_n, 1));
     LK_CU(dalloc(&c->m_cnt, c->m_max));
     LK_CU(dalloc(&c->xh, (size_t)T * HIDDEN)); LK_CU(dalloc(&c->hb, rows * MOE_INTER));
+    if (cfg->with_shared) LK_CU(dalloc(&c->shgu, (size_t)T * 2 * MOE_INTER));
     LK_CU(cudaMemset(c->y, 0, rows * HIDDEN * sizeof(float)));
     LK_CU(cudaDeviceSynchronize());
     cudaSetDevice(prev);
@@ -131,7 +135,7 @@ void lk_moe_destroy(LkMoeCtx* c) {
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
                      c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->xq, c->xqn, c->xd,
                      c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt,
-                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->xh, c->hb };
+                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->xh, c->hb, c->shgu };
     for (void* p : ptrs) if (p) cudaFree(p);
     delete c;
 }
@@ -148,6 +152,9 @@ static int check_weights(LkMoeCtx* c, const LkMoeWeights* W, bool need_router) {
         const void* sm[] = { W->sh_gate, W->sh_up, W->sh_down };
         for (const void* m : sm) if (!m || ((uintptr_t)m & 15)) return set_err(c, LK_ERR_ARG, "shared expert null or not 16-byte aligned");
     }
+    if (W->sh_fmt != 0 && W->sh_fmt != LK_FMT_IQ2 && W->sh_fmt != LK_FMT_Q5K)
+        return set_err(c, LK_ERR_UNSUPPORTED, "shared-expert format %d: IQ2_XXS (4) or Q5_K/Q6_K (3)", W->sh_fmt);
+    c->rs = c->cfg.with_shared && W->sh_fmt != LK_FMT_Q5K;
     if (need_router && (!W->router_w || !W->router_bias)) return set_err(c, LK_ERR_ARG, "router weights missing");
     return LK_OK;
 }
@@ -162,7 +169,7 @@ static RouterParams router_params(LkMoeCtx* c, const LkMoeWeights* W, const floa
     p.n_group = c->cfg.n_group; p.topk_group = c->cfg.topk_group; p.scale = c->cfg.scale;
     if (decode_slots) {
         p.slot_expert = c->slot_expert; p.slot_tok = c->slot_tok; p.slot_out = c->slot_out; p.slot_w = c->slot_w;
-        p.nslots = c->nslots; p.with_shared = c->cfg.with_shared;
+        p.nslots = c->nslots; p.with_shared = c->rs;
     }
     return p;
 }
@@ -229,7 +236,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
 static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
                          const float* w, int keep, float* h, float* moe, cudaStream_t st) {
     SlotParams s{};
-    s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = GEMM_NT; s.with_shared = c->cfg.with_shared;
+    s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = GEMM_NT; s.with_shared = c->rs;
     s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
     s.slot_expert = c->g_expert; s.slot_tok = c->g_tok; s.slot_out = c->g_out; s.slot_w = c->g_w; s.nslots = c->g_n;
     s.max_slots = c->g_max; s.err = c->err; s.sh_t0 = c->sh_t0; s.sh_n = c->sh_n;
@@ -259,7 +266,7 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int
 static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
                         const float* w, int keep, float* h, float* moe, cudaStream_t st) {
     SlotParams s{};
-    s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = MM_NT; s.with_shared = c->cfg.with_shared;
+    s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = MM_NT; s.with_shared = c->rs;
     s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
     s.slot_expert = c->m_expert; s.slot_tok = c->m_tok; s.slot_out = c->m_out; s.slot_w = c->m_w; s.nslots = c->m_n;
     s.max_slots = c->m_max; s.err = c->err; s.sh_t0 = c->sh_t0; s.sh_n = c->sh_n;
@@ -292,12 +299,31 @@ static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int 
 static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
                      const float* w, int keep, float* h, float* moe, bool slots_ready, cudaStream_t st) {
     const bool iq2_down = W->down_fmt == LK_FMT_IQ2;
+    if (c->cfg.with_shared && !c->rs) {               // the real model's shared expert: its own launches first
+        SharedKqParams sp{};
+        sp.gate = (const uint8_t*)W->sh_gate; sp.up = (const uint8_t*)W->sh_up; sp.down = (const uint8_t*)W->sh_down;
+        sp.x = x; sp.ld_x = ld_x;
+        sp.n = c->sh_n < 0 ? 0 : (c->sh_n > 0 ? c->sh_n : T); sp.t0 = c->sh_n > 0 ? c->sh_t0 : 0; sp.row0 = T * keep;
+        if (c->xq_ready && x == c->xq_src) { sp.xq = c->xq; sp.xd = c->xd; }
+        sp.gu = c->shgu; sp.y = c->y; sp.err = c->err;
+        launch_shared_kq(sp, c->nsm, st);
+        if (keep == 0) {                              // shared expert only (lk_ep_shared)
+            if (h || moe) {
+                CombineParams cp{};
+                cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = 0; cp.with_shared = 1; cp.shared = nullptr;
+                cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = nullptr; cp.sh_t0 = c->sh_t0; cp.sh_n = c->sh_n;
+                launch_combine(cp, st);
+            }
+            LK_CU(cudaGetLastError());
+            return LK_OK;
+        }
+    }
     if (iq2_down && T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
     if (iq2_down && T >= c->mma_min_tokens) return run_mma_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
     if (!slots_ready) {
         SlotParams s{};
         s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = slot_nt(T);
-        s.with_shared = c->cfg.with_shared;
+        s.with_shared = c->rs;
         s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
         s.slot_expert = c->slot_expert; s.slot_tok = c->slot_tok; s.slot_out = c->slot_out; s.slot_w = c->slot_w;
         s.nslots = c->nslots; s.max_slots = c->max_slots; s.err = c->err; s.sh_t0 = c->sh_t0; s.sh_n = c->sh_n;
@@ -388,6 +414,9 @@ int lk_ep_shared(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float
         return set_err(c, LK_ERR_ARG, "shared expert matrices must be 16-byte aligned");
     if (W->down_fmt != LK_FMT_IQ2 && W->down_fmt != LK_FMT_Q2K && W->down_fmt != LK_FMT_Q3K)
         return set_err(c, LK_ERR_UNSUPPORTED, "down format %d", W->down_fmt);
+    if (W->sh_fmt != 0 && W->sh_fmt != LK_FMT_IQ2 && W->sh_fmt != LK_FMT_Q5K)
+        return set_err(c, LK_ERR_UNSUPPORTED, "shared-expert format %d", W->sh_fmt);
+    c->rs = W->sh_fmt != LK_FMT_Q5K;
     if (T > c->cfg.max_tokens) return set_err(c, LK_ERR_CAPACITY, "T=%d > capacity %d", T, c->cfg.max_tokens);
     if (T == 0) return LK_OK;
     // keep = 0: shared-expert slots only
@@ -420,7 +449,7 @@ int lk_gen_iq2(void* dst, uint64_t seed, int layer, int matrix, int expert0, int
 
 int lk_gen_weights(int fmt, void* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K, int64_t stride,
                    lk_stream_t stream) {
-    if (fmt != LK_FMT_IQ2 && fmt != LK_FMT_Q2K && fmt != LK_FMT_Q3K) return LK_ERR_UNSUPPORTED;
+    if (fmt != LK_FMT_IQ2 && fmt != LK_FMT_Q2K && fmt != LK_FMT_Q3K && fmt != LK_FMT_Q5K && fmt != LK_FMT_Q6K) return LK_ERR_UNSUPPORTED;
     if (!dst || rows < 1 || K < QK || (K % QK) || n_exp < 1) return LK_ERR_ARG;
     launch_gen_weights(fmt, (uint8_t*)dst, seed, layer, matrix, expert0, n_exp, rows, K, stride, (cudaStream_t)stream);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;

@@ -37,8 +37,9 @@ LK_HD constexpr size_t iq2_matrix_bytes(int rows, int K) { return (size_t)rows *
 constexpr size_t EXPERT_GU_BYTES = (size_t)MOE_INTER * (HIDDEN / QK) * BLK_IQ2;
 constexpr size_t EXPERT_DOWN_BYTES = (size_t)HIDDEN * (MOE_INTER / QK) * BLK_IQ2;
 
-// ---- format ids, numerically equal to the reference's FL_IQ2 / FL_Q2K / FL_Q3K
-enum { FMT_IQ2 = 4, FMT_Q2K = 5, FMT_Q3K = 6 };
+// ---- format ids, numerically equal to the reference's FL_Q6K / FL_Q5K / FL_IQ2 / FL_Q2K / FL_Q3K
+//      (src/fused_layer.h:11)
+enum { FMT_Q6K = 1, FMT_Q5K = 3, FMT_IQ2 = 4, FMT_Q2K = 5, FMT_Q3K = 6 };
 
 // ---- the K-quant down formats (GGUF / ggml block layouts; the reference's BLK_Q2 / BLK_Q3,
 //  fused_layer.cu:19).  256 weights per block; weight i = 128n + 32j + 16s + l (n < 2, j < 4, s < 2,
@@ -52,9 +53,26 @@ constexpr int BLK_Q2K = 84;
 constexpr int BLK_Q3K = 110;
 constexpr int Q2K_QS = 16, Q2K_D = 80, Q2K_DMIN = 82;
 constexpr int Q3K_QS = 32, Q3K_SC = 96, Q3K_D = 108;
-LK_HD constexpr int fmt_block_bytes(int fmt) { return fmt == FMT_Q2K ? BLK_Q2K : fmt == FMT_Q3K ? BLK_Q3K : BLK_IQ2; }
+// ---- the shared expert's formats in the real model (the reference's BLK_Q5 / BLK_Q6; W->sh_gate / sh_up
+//  Q5_K, sh_down Q6_K, src/fused_layer.h:14).  256 weights per block.
+//   Q5_K (176 B): fp16 d, fp16 dmin, scales[12] (8 x (6-bit scale, 6-bit min)), qh[32], qs[128].  Weight
+//                i = 64j + 32u + l (j < 4, u < 2, l < 32): q = ((qs[32j + l] >> 4u) & 15) | (qh[l] bit
+//                2j + u) << 4, in 0..31; its 32-weight sub-block is 2j + u with (scale, min) from
+//                q5k_scale_min; w = d*scale*q - dmin*min.
+//   Q6_K (210 B): ql[128], qh[64], scales[16] (int8), fp16 d.  Weight i = 128n + 32c + l (n < 2, c < 4,
+//                l < 32): q = ((ql[64n + 32(c & 1) + l] >> 4(c >> 1)) & 15) | ((qh[32n + l] >> 2c) & 3) << 4,
+//                value q - 32; its 16-weight sub-block is i / 16; w = d*scales[i / 16]*(q - 32).
+constexpr int BLK_Q5K = 176;
+constexpr int BLK_Q6K = 210;
+constexpr int Q5K_SC = 4, Q5K_QH = 16, Q5K_QS = 48;
+constexpr int Q6K_QH = 128, Q6K_SC = 192, Q6K_D = 208;
+LK_HD constexpr int fmt_block_bytes(int fmt) {
+    return fmt == FMT_Q2K ? BLK_Q2K : fmt == FMT_Q3K ? BLK_Q3K : fmt == FMT_Q5K ? BLK_Q5K : fmt == FMT_Q6K ? BLK_Q6K : BLK_IQ2;
+}
 // one expert's down matrix [HIDDEN rows][MOE_INTER] in format fmt: 3 784 704 / 4 816 896 / 6 307 840 B
 LK_HD constexpr size_t down_matrix_bytes(int fmt) { return (size_t)HIDDEN * (MOE_INTER / QK) * fmt_block_bytes(fmt); }
+// one gate (or up) matrix [MOE_INTER rows][HIDDEN] in format fmt: 3 784 704 (IQ2_XXS) / 10 092 544 (Q5_K) B
+LK_HD constexpr size_t gu_matrix_bytes(int fmt) { return (size_t)MOE_INTER * (HIDDEN / QK) * fmt_block_bytes(fmt); }
 
 // Q3_K's 6-bit scale i (0..15) from the 12 packed bytes: low 4 bits in byte i (i < 8) or the high
 // nibble of byte i - 8, high 2 bits at bits 2*(i/4) of byte 8 + i%4 (ggml dequantize_row_q3_K's
@@ -63,6 +81,14 @@ LK_HD int q3k_scale(const uint8_t* sc, int i) {
     const int lo = i < 8 ? (sc[i] & 15) : (sc[i - 8] >> 4);
     const int hi = (sc[8 + (i & 3)] >> (2 * (i >> 2))) & 3;
     return (lo | (hi << 4)) - 32;
+}
+
+// Q5_K's (scale, min) of 32-weight sub-block j (0..7) from the 12 packed bytes (ggml get_scale_min_k4; the
+// reference's scale_min, fused_layer.cu:25-26): j < 4: low 6 bits of bytes j and j + 4; else the nibbles
+// of byte j + 4 with the top 2 bits of bytes j - 4 (scale) and j (min) as bits 4-5.
+LK_HD void q5k_scale_min(const uint8_t* sc, int j, int& scale, int& mn) {
+    if (j < 4) { scale = sc[j] & 63; mn = sc[j + 4] & 63; }
+    else { scale = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4); mn = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4); }
 }
 
 // ---- fp16 <-> fp32 in software (IEEE binary16, round to nearest even), identical on host and device
@@ -167,7 +193,8 @@ LK_HD uint64_t iq2_gen_key(uint64_t seed, uint32_t layer, uint32_t matrix, uint3
     h = splitmix64(h ^ ((uint64_t)matrix << 32));
     return splitmix64(h ^ ((uint64_t)expert << 16));
 }
-LK_HD uint16_t iq2_gen_d(uint64_t key, uint64_t block) {
+// fp16(|N(0,1)| * scale) from the draws at block*16 + 8..10
+LK_HD uint16_t gen_abs_normal_half(uint64_t key, uint64_t block, float scale) {
     int32_t s = 0;
     for (int w = 0; w < 3; ++w) {
         const uint64_t r = splitmix64(key ^ (block * 16ull + 8ull + (uint64_t)w));
@@ -175,9 +202,10 @@ LK_HD uint16_t iq2_gen_d(uint64_t key, uint64_t block) {
     }
     const int32_t c = 2 * s - 12 * 65535;            // 2 * (sum - 12 * 65535/2): exact integer
     const float n = (float)c * (1.0f / 131072.0f);   // / 2^17: unit-variance Irwin-Hall(12), exact
-    const float a = fabsf(n) * 1.0e-3f;
+    const float a = fabsf(n) * scale;
     return float_to_half_rne(a);
 }
+LK_HD uint16_t iq2_gen_d(uint64_t key, uint64_t block) { return gen_abs_normal_half(key, block, 1.0e-3f); }
 LK_HD uint64_t iq2_gen_group(uint64_t key, uint64_t block, int g) {
     return splitmix64(key ^ (block * 16ull + (uint64_t)g));
 }
@@ -191,21 +219,26 @@ LK_HD void iq2_gen_block(uint64_t key, uint64_t block, uint8_t* out) {
     }
 }
 
-// seeded synthetic K-quant blocks (Q2_K / Q3_K down matrices): every byte except the fp16 scales is
-// uniform (splitmix64 draws 0..13 of the block's counter range), d = fp16(|N(0,1)|*1e-3) from draws
-// 16.., Q2_K's dmin likewise from draws 24..  Keys as for IQ2_XXS, so a layer's down matrix in any
-// format comes from the same (seed, layer, matrix, expert) chain.
+// seeded synthetic K-quant blocks (Q2_K / Q3_K downs, Q5_K / Q6_K shared expert): every byte except the
+// fp16 scales is uniform (splitmix64 draws 0..26 of the block's counter range, 8 bytes each), d =
+// fp16(|N(0,1)|*c) from the draws at block*2 + 2^40, dmin (Q2_K, Q5_K) from block*2 + 1 + 2^40; c = 1e-3
+// (Q2_K, Q3_K) or 4e-5 (Q5_K, Q6_K, whose 5- and 6-bit values and 6- and 8-bit scales are ~30-100x wider),
+// so every format's weights have the IQ2_XXS experts' magnitude.  Keys as for IQ2_XXS, so a layer's matrix
+// in any format comes from the same (seed, layer, matrix, expert) chain.
 LK_HD void kq_gen_block(int fmt, uint64_t key, uint64_t block, uint8_t* out) {
-    const int nu = fmt == FMT_Q2K ? Q2K_D : Q3K_D;          // uniform bytes before the fp16 scale(s)
-    for (int g = 0; 8 * g < nu; ++g) {
+    const int nb = fmt_block_bytes(fmt);
+    for (int g = 0; 8 * g < nb; ++g) {
         const uint64_t v = splitmix64(key ^ (block * 32ull + (uint64_t)g));
-        for (int j = 0; j < 8 && 8 * g + j < nu; ++j) out[8 * g + j] = (uint8_t)(v >> (8 * j));
+        for (int j = 0; j < 8 && 8 * g + j < nb; ++j) out[8 * g + j] = (uint8_t)(v >> (8 * j));
     }
-    const uint16_t d = iq2_gen_d(key, block * 2ull + (1ull << 40));
-    out[nu] = (uint8_t)(d & 0xFF); out[nu + 1] = (uint8_t)(d >> 8);
-    if (fmt == FMT_Q2K) {
-        const uint16_t m = iq2_gen_d(key, block * 2ull + 1ull + (1ull << 40));
-        out[Q2K_DMIN] = (uint8_t)(m & 0xFF); out[Q2K_DMIN + 1] = (uint8_t)(m >> 8);
+    const int doff = fmt == FMT_Q2K ? Q2K_D : fmt == FMT_Q3K ? Q3K_D : fmt == FMT_Q6K ? Q6K_D : 0;
+    const float c = (fmt == FMT_Q5K || fmt == FMT_Q6K) ? 4.0e-5f : 1.0e-3f;
+    const uint16_t d = gen_abs_normal_half(key, block * 2ull + (1ull << 40), c);
+    out[doff] = (uint8_t)(d & 0xFF); out[doff + 1] = (uint8_t)(d >> 8);
+    if (fmt == FMT_Q2K || fmt == FMT_Q5K) {
+        const int moff = fmt == FMT_Q2K ? Q2K_DMIN : 2;
+        const uint16_t m = gen_abs_normal_half(key, block * 2ull + 1ull + (1ull << 40), c);
+        out[moff] = (uint8_t)(m & 0xFF); out[moff + 1] = (uint8_t)(m >> 8);
     }
 }
 

@@ -85,6 +85,7 @@ extern "C" int lk_moe_experts_noalloc(const LkMoeWeights* W, const float* x, con
     }
     if (!W || !x || !sel || !w || (h && !resid)) return LK_ERR_ARG;
     if (W->down_fmt != LK_FMT_IQ2) return LK_ERR_UNSUPPORTED;
+    if (with_shared && W->sh_fmt != 0 && W->sh_fmt != LK_FMT_IQ2) return LK_ERR_UNSUPPORTED;   // IQ2_XXS shared expert only
     const void* mats[] = { W->gate, W->up, W->down };
     for (const void* m : mats) if (!m || ((uintptr_t)m & 15)) return LK_ERR_ARG;
     if ((W->gate_stride & 15) || (W->up_stride & 15) || (W->down_stride & 15)) return LK_ERR_ARG;

@@ -134,7 +134,8 @@ def replay_decode(fc, layers, x, resid, KE, warmup, steps, down_fmt=FL_IQ2, devi
     x = np.ascontiguousarray(x, np.float32)
     resid = np.ascontiguousarray(resid, np.float32)
     n = x.shape[1]
-    mw = (N.FLMoeW * L)(*[N.FLMoeW(l.router_w.data_ptr(), 0, l.router_bias.data_ptr(), l.sh_gate, l.sh_up, l.sh_down)
+    mw = (N.FLMoeW * L)(*[N.FLMoeW(l.router_w.data_ptr(), 0, l.router_bias.data_ptr(), l.sh_gate, l.sh_up, l.sh_down,
+                                   N.FMT_Q5K if getattr(l, "sh_fmt", N.FMT_IQ2) == N.FMT_Q5K else 0)
                           for l in layers])
     ptrs = lambda attr: (ctypes.c_void_p * L)(*[getattr(l, attr) for l in layers])
     h = np.empty((n, HIDDEN), np.float32)

@@ -24,7 +24,7 @@ import numpy as np
 import torch
 
 from . import native as N
-from .native import HIDDEN, MOE_INTER, N_EXPERTS, FMT_IQ2, FMT_Q2K, FMT_Q3K
+from .native import HIDDEN, MOE_INTER, N_EXPERTS, FMT_IQ2, FMT_Q2K, FMT_Q3K, FMT_Q5K
 
 GGML_F32, GGML_F16, GGML_Q2_K, GGML_Q3_K, GGML_Q5_K, GGML_Q6_K, GGML_IQ2_XXS = 0, 1, 10, 11, 13, 14, 16
 # ggml type -> (weights per block, bytes per block)
@@ -101,11 +101,11 @@ class GgufFile:
         return self.tensors[name]
 
     def bytes(self, name):
-        """The tensor's data as a read-only uint8 memmap."""
+        """The tensor's data as a uint8 memmap (copy-on-write: the file is never modified)."""
         ttype, ne, off, nbytes = self.info(name)
         if nbytes is None:
             raise GgufError("%s: ggml type %d is not one this loader reads" % (name, ttype))
-        return np.memmap(self.path, dtype=np.uint8, mode="r", offset=off, shape=(nbytes,))
+        return np.memmap(self.path, dtype=np.uint8, mode="c", offset=off, shape=(nbytes,))   # copy-on-write: never written back
 
 
 def _expect(g, name, types, ne):
@@ -121,9 +121,9 @@ class GgufLayer:
     """One MoE layer of a GGUF file resident in HBM, with the interface of moe.LayerWeights (arenas,
     strides, down format, shared expert, router) for lk_moe_* calls.
 
-    The shared expert is loaded when its gate/up are IQ2_XXS and its down has the routed down's format (the
-    lk_* expert stage takes one down format); otherwise (the real model's Q5_K / Q6_K) `shared_types` records
-    its ggml types and `sh_gate` is None, so the context must run with_shared = 0."""
+    The shared expert is loaded in the real model's formats (Q5_K gate/up, Q6_K down: sh_fmt = FMT_Q5K), or as
+    IQ2_XXS gate/up with a down in the routed down's format (sh_fmt = FMT_IQ2).  Any other combination is not
+    loaded: `shared_types` records its ggml types and `sh_gate` is None, so the context must run with_shared = 0."""
 
     def __init__(self, gguf, layer, device="cuda"):
         g = gguf if isinstance(gguf, GgufFile) else GgufFile(gguf)
@@ -146,9 +146,14 @@ class GgufLayer:
         self.shared_types = tuple(g.info(n)[0] for n in sh) if all(n in g.tensors for n in sh) else None
         self.sh_gate = self.sh_up = self.sh_down = None
         self.shared = None
-        if self.shared_types == (GGML_IQ2_XXS, GGML_IQ2_XXS, dtype_):
+        self.sh_fmt = FMT_IQ2
+        if self.shared_types in ((GGML_IQ2_XXS, GGML_IQ2_XXS, dtype_), (GGML_Q5_K, GGML_Q5_K, GGML_Q6_K)):
+            model = self.shared_types[0] == GGML_Q5_K
+            for n, ne in zip(sh, ([HIDDEN, MOE_INTER], [HIDDEN, MOE_INTER], [MOE_INTER, HIDDEN])):
+                _expect(g, n, {self.shared_types[0] if "down" not in n else self.shared_types[2]}, ne)
             self.shared = [self._upload(g.bytes(n)) for n in sh]
             self.sh_gate, self.sh_up, self.sh_down = (a.data_ptr() for a in self.shared)
+            self.sh_fmt = FMT_Q5K if model else FMT_IQ2
         # router: F32 [256][7168], or the F16 copy of the engine's trimmed file
         if p + "ffn_gate_inp_f16.weight" in g.tensors:
             _expect(g, p + "ffn_gate_inp_f16.weight", {GGML_F16}, [HIDDEN, N_EXPERTS])
@@ -173,4 +178,5 @@ class GgufLayer:
     def struct(self):
         return N.LkMoeWeights(self.gate, self.up, self.down, self.stride, self.stride, self.down_stride, self.down_fmt,
                               self.sh_gate, self.sh_up, self.sh_down, self.router_w.data_ptr(),
-                              1 if self.router_w.dtype == torch.float16 else 0, self.router_bias.data_ptr())
+                              1 if self.router_w.dtype == torch.float16 else 0, self.router_bias.data_ptr(),
+                              FMT_Q5K if self.sh_fmt == FMT_Q5K else 0)

@@ -31,7 +31,7 @@ def gen_iq2(dst, seed, layer, matrix, expert0, n_exp, rows, K, stride, stream=No
 
 
 def gen_weights(fmt, dst, seed, layer, matrix, expert0, n_exp, rows, K, stride, stream=None):
-    """Seeded matrices in any supported format (IQ2_XXS, Q2_K, Q3_K); the CPU generator's bytes."""
+    """Seeded matrices in any supported format (IQ2_XXS, Q2_K, Q3_K, Q5_K, Q6_K); the CPU generator's bytes."""
     addr = dst if isinstance(dst, int) else dst.data_ptr()
     check(lib().lk_gen_weights(fmt, ctypes.c_void_p(addr), seed, layer, matrix, expert0, n_exp, rows, K, stride, _stream(stream)))
 
@@ -42,18 +42,23 @@ class LayerWeights:
     buf layout (bytes): [gate x n_experts][up x n_experts][down x n_experts][shared gate][shared up][shared down],
     each gate/up matrix EXPERT_MATRIX_BYTES (3 784 704, a multiple of 256) of seeded IQ2_XXS, each down matrix
     DOWN_MATRIX_BYTES[down_fmt] in down_fmt (IQ2_XXS, or the real model's Q2_K / Q3_K), all from the seeded
-    generators (matrix ids 0/1/2, shared expert id 256).  An expert-parallel shard holds the n_experts
+    generators (matrix ids 0/1/2, shared expert id 256).  The shared expert is IQ2_XXS with a down in down_fmt
+    (sh_fmt = FMT_IQ2), or in the real model's formats (sh_fmt = FMT_Q5K: Q5_K gate/up, Q6_K down).
+    An expert-parallel shard holds the n_experts
     consecutive global experts starting at expert0 (arena slot i = global expert expert0 + i).  Router weights/bias are given or drawn from
     torch's generator: W ~ N(0, 0.02) [n_experts][7168] fp32 (or fp16), bias ~ N(0, 0.01)."""
 
     def __init__(self, device, seed, layer, n_experts=N_EXPERTS, with_shared=True, router_w=None, router_bias=None,
-                 router_f16=False, stream=None, buf=None, expert0=0, down_fmt=FMT_IQ2):
+                 router_f16=False, stream=None, buf=None, expert0=0, down_fmt=FMT_IQ2, sh_fmt=FMT_IQ2):
         self.device = torch.device(device)
         self.seed, self.layer, self.n_experts, self.with_shared = seed, layer, n_experts, with_shared
         self.expert0 = expert0
         self.down_fmt = down_fmt
+        self.sh_fmt = sh_fmt
         S, DS = EXPERT_MATRIX_BYTES, N.DOWN_MATRIX_BYTES[down_fmt]
-        self.nbytes = (2 * S + DS) * (n_experts + (1 if with_shared else 0))
+        sh_gu_fmt, sh_dn_fmt = (N.FMT_Q5K, N.FMT_Q6K) if sh_fmt == N.FMT_Q5K else (FMT_IQ2, down_fmt)
+        self.sh_sizes = (N.GU_MATRIX_BYTES[sh_gu_fmt], N.GU_MATRIX_BYTES[sh_gu_fmt], N.DOWN_MATRIX_BYTES[sh_dn_fmt])
+        self.nbytes = (2 * S + DS) * n_experts + (sum(self.sh_sizes) if with_shared else 0)
         self.buf = buf if buf is not None else torch.empty(self.nbytes, dtype=torch.uint8, device=self.device)
         base = self.buf.data_ptr()
         self.gate, self.up, self.down = base, base + n_experts * S, base + 2 * n_experts * S
@@ -63,10 +68,11 @@ class LayerWeights:
         gen_weights(down_fmt, self.down, seed, layer, 2, expert0, n_experts, HIDDEN, MOE_INTER, DS, stream)
         if with_shared:
             sh = base + n_experts * (2 * S + DS)
-            self.sh_gate, self.sh_up, self.sh_down = sh, sh + S, sh + 2 * S
-            gen_iq2(self.sh_gate, seed, layer, 0, N_EXPERTS, 1, MOE_INTER, HIDDEN, S, stream)
-            gen_iq2(self.sh_up, seed, layer, 1, N_EXPERTS, 1, MOE_INTER, HIDDEN, S, stream)
-            gen_weights(down_fmt, self.sh_down, seed, layer, 2, N_EXPERTS, 1, HIDDEN, MOE_INTER, DS, stream)
+            SG = self.sh_sizes[0]
+            self.sh_gate, self.sh_up, self.sh_down = sh, sh + SG, sh + 2 * SG
+            gen_weights(sh_gu_fmt, self.sh_gate, seed, layer, 0, N_EXPERTS, 1, MOE_INTER, HIDDEN, SG, stream)
+            gen_weights(sh_gu_fmt, self.sh_up, seed, layer, 1, N_EXPERTS, 1, MOE_INTER, HIDDEN, SG, stream)
+            gen_weights(sh_dn_fmt, self.sh_down, seed, layer, 2, N_EXPERTS, 1, HIDDEN, MOE_INTER, self.sh_sizes[2], stream)
         else:
             self.sh_gate = self.sh_up = self.sh_down = None
         if router_w is None:
@@ -82,13 +88,15 @@ class LayerWeights:
     def struct(self):
         return N.LkMoeWeights(self.gate, self.up, self.down, self.stride, self.stride, self.down_stride, self.down_fmt,
                               self.sh_gate, self.sh_up, self.sh_down, self.router_w.data_ptr(),
-                              1 if self.router_w.dtype == torch.float16 else 0, self.router_bias.data_ptr())
+                              1 if self.router_w.dtype == torch.float16 else 0, self.router_bias.data_ptr(),
+                              self.sh_fmt if self.sh_fmt == N.FMT_Q5K else 0)
 
     def expert_bytes(self, expert, matrix):
         """Host copy of one expert matrix (matrix 0 gate, 1 up, 2 down; expert == n_experts: shared)."""
         size = self.down_stride if matrix == 2 else self.stride
         if expert == self.n_experts:
-            off = self.n_experts * (2 * self.stride + self.down_stride) + matrix * self.stride
+            off = self.n_experts * (2 * self.stride + self.down_stride) + sum(self.sh_sizes[:matrix])
+            size = self.sh_sizes[matrix]
         else:
             off = matrix * self.n_experts * self.stride + expert * size
         return self.buf[off:off + size].cpu().numpy()

@@ -18,10 +18,12 @@ BLK_IQ2 = 66
 EXPERT_MATRIX_BYTES = MOE_INTER * (HIDDEN // QK) * BLK_IQ2          # 3 784 704 (gate, up and down alike)
 
 LK_OK, LK_ERR_ARG, LK_ERR_CUDA, LK_ERR_UNSUPPORTED, LK_ERR_CAPACITY, LK_ERR_DEVICE = 0, -1, -2, -3, -4, -5
-FMT_IQ2, FMT_Q2K, FMT_Q3K = 4, 5, 6
-BLOCK_BYTES = {FMT_IQ2: 66, FMT_Q2K: 84, FMT_Q3K: 110}
+FMT_Q6K, FMT_Q5K, FMT_IQ2, FMT_Q2K, FMT_Q3K = 1, 3, 4, 5, 6
+BLOCK_BYTES = {FMT_IQ2: 66, FMT_Q2K: 84, FMT_Q3K: 110, FMT_Q5K: 176, FMT_Q6K: 210}
 # one expert's down matrix [7168 rows][2048] per format: 3 784 704 / 4 816 896 / 6 307 840 bytes
 DOWN_MATRIX_BYTES = {f: HIDDEN * (MOE_INTER // QK) * b for f, b in BLOCK_BYTES.items()}
+# bytes of one gate (or up) matrix [MOE_INTER][HIDDEN] per format
+GU_MATRIX_BYTES = {f: MOE_INTER * (HIDDEN // QK) * b for f, b in BLOCK_BYTES.items()}
 EP_ROW_HDR_BYTES = 64
 EP_ROW_BYTES = EP_ROW_HDR_BYTES + HIDDEN * 4      # 28 736
 EP_MAX_RANKS = 8
@@ -40,7 +42,8 @@ class LkMoeWeights(ctypes.Structure):
                 ("gate_stride", ctypes.c_int64), ("up_stride", ctypes.c_int64), ("down_stride", ctypes.c_int64),
                 ("down_fmt", ctypes.c_int),
                 ("sh_gate", ctypes.c_void_p), ("sh_up", ctypes.c_void_p), ("sh_down", ctypes.c_void_p),
-                ("router_w", ctypes.c_void_p), ("router_w_f16", ctypes.c_int), ("router_bias", ctypes.c_void_p)]
+                ("router_w", ctypes.c_void_p), ("router_w_f16", ctypes.c_int), ("router_bias", ctypes.c_void_p),
+                ("sh_fmt", ctypes.c_int)]
 
 
 class FLOut(ctypes.Structure):
@@ -49,7 +52,7 @@ class FLOut(ctypes.Structure):
 
 class FLMoeW(ctypes.Structure):
     _fields_ = [("gate_inp", ctypes.c_void_p), ("gate_f16", ctypes.c_int), ("probs_b", ctypes.c_void_p),
-                ("sh_gate", ctypes.c_void_p), ("sh_up", ctypes.c_void_p), ("sh_down", ctypes.c_void_p)]
+                ("sh_gate", ctypes.c_void_p), ("sh_up", ctypes.c_void_p), ("sh_down", ctypes.c_void_p), ("sh_fmt", ctypes.c_int)]
 
 
 # exported symbol -> (restype, argtypes)

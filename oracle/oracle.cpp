@@ -77,13 +77,35 @@ void orc_gen_d_only(uint64_t seed, int layer, int matrix, int expert, int64_t nb
     for (int64_t b = 0; b < nblk; ++b) out[b] = iq2_gen_d(key, (uint64_t)b);
 }
 
-// out[nblk*256] = dequantised Q2_K (fmt 5) or Q3_K (fmt 6) blocks (gguf-py dequantize_blocks semantics:
-// Q2_K d*(sc&15)*q - dmin*(sc>>4); Q3_K d*(scale-32)*q3, each product in fp32 as written)
+// out[nblk*256] = dequantised Q2_K (fmt 5), Q3_K (6), Q5_K (3) or Q6_K (1) blocks (gguf-py
+// dequantize_blocks semantics: Q2_K d*(sc&15)*q - dmin*(sc>>4); Q3_K d*(scale-32)*q3; Q5_K
+// (d*scale)*q - dmin*min; Q6_K (d*scale)*(q-32); each product in fp32 as written)
 void orc_kq_dequant(int fmt, const uint8_t* blocks, int64_t nblk, float* out) {
     const int nb = fmt_block_bytes(fmt);
     #pragma omp parallel for schedule(static)
     for (int64_t b = 0; b < nblk; ++b) {
         const uint8_t* blk = blocks + b * nb;
+        if (fmt == FMT_Q5K) {
+            uint16_t dh, mh; memcpy(&dh, blk, 2); memcpy(&mh, blk + 2, 2);
+            const float d = half_to_float(dh), dmin = half_to_float(mh);
+            for (int i = 0; i < QK; ++i) {
+                const int j = i >> 6, u = (i >> 5) & 1, l = i & 31;
+                const int q = ((blk[Q5K_QS + 32 * j + l] >> (4 * u)) & 15) | (((blk[Q5K_QH + l] >> (2 * j + u)) & 1) << 4);
+                int sc, mn; q5k_scale_min(blk + Q5K_SC, 2 * j + u, sc, mn);
+                out[b * QK + i] = (d * (float)sc) * (float)q - dmin * (float)mn;
+            }
+            continue;
+        }
+        if (fmt == FMT_Q6K) {
+            uint16_t dh; memcpy(&dh, blk + Q6K_D, 2);
+            const float d = half_to_float(dh);
+            for (int i = 0; i < QK; ++i) {
+                const int n = i >> 7, c = (i >> 5) & 3, l = i & 31;
+                const int q = ((blk[64 * n + 32 * (c & 1) + l] >> (4 * (c >> 1))) & 15) | (((blk[Q6K_QH + 32 * n + l] >> (2 * c)) & 3) << 4);
+                out[b * QK + i] = (d * (float)(int8_t)blk[Q6K_SC + i / 16]) * (float)(q - 32);
+            }
+            continue;
+        }
         for (int i = 0; i < QK; ++i) {
             const int n = i >> 7, j = (i >> 5) & 3, s = (i >> 4) & 1, l = i & 15;
             const int is = 8 * n + 2 * j + s;
@@ -311,8 +333,61 @@ static void iq2_matvec_float_multi(const uint8_t* W, int rows, int K, const floa
 // sum isum = sum q_w * q_x; Q2_K adds fa*dx*isum - mla*dx*sum(q_x) with fa = d*(sc&15), mla = dmin*(sc>>4)
 // (the reference's s16 term); Q3_K adds fa*dx*isum with fa = d*(scale-32) and q_w = low2 - 4 where the
 // high bit is clear.  Evaluated in double: the ideal value of the q8 scheme.
+//
+// Q5_K (the shared expert's gate/up, src/fused_layer.cu:102-130): per 32-weight sub-block isum = sum q_w * q_x
+// (q_w in 0..31), acc += dx * (d*scale*isum - dmin*min*sum q_x).  Q6_K (the shared down, :131-158): per
+// 16-weight sub-block isum = sum (q_w - 32) * q_x, acc += d*scales[i/16]*dx*isum.
+static void q56_matvec_multi(int fmt, const uint8_t* W, int rows, int K, const int8_t* const* xq, const float* const* xd,
+                             int ntok, float* const* y) {
+    const int NB = K / QK, nb = fmt_block_bytes(fmt);
+    #pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t* row = W + (size_t)r * NB * nb;
+        std::vector<double> acc(ntok, 0.0);
+        for (int b = 0; b < NB; ++b) {
+            const uint8_t* blk = row + (size_t)b * nb;
+            if (fmt == FMT_Q5K) {
+                uint16_t dh, mh; memcpy(&dh, blk, 2); memcpy(&mh, blk + 2, 2);
+                const double d = half_to_float(dh), dmin = half_to_float(mh);
+                for (int sb = 0; sb < 8; ++sb) {
+                    const int j = sb >> 1, u = sb & 1, k0 = b * QK + 32 * sb;
+                    int sc, mn; q5k_scale_min(blk + Q5K_SC, sb, sc, mn);
+                    int32_t qw[32];
+                    for (int l = 0; l < 32; ++l)
+                        qw[l] = ((blk[Q5K_QS + 32 * j + l] >> (4 * u)) & 15) | (((blk[Q5K_QH + l] >> (2 * j + u)) & 1) << 4);
+                    for (int t = 0; t < ntok; ++t) {
+                        int32_t isum = 0, xs = 0;
+                        for (int l = 0; l < 32; ++l) { isum += qw[l] * (int32_t)xq[t][k0 + l]; xs += xq[t][k0 + l]; }
+                        acc[t] += (double)xd[t][k0 / 32] * (d * sc * (double)isum - dmin * mn * (double)xs);
+                    }
+                }
+            } else {
+                uint16_t dh; memcpy(&dh, blk + Q6K_D, 2);
+                const double d = half_to_float(dh);
+                for (int s16 = 0; s16 < 16; ++s16) {
+                    const int k0 = b * QK + 16 * s16;
+                    int32_t qw[16];
+                    for (int l = 0; l < 16; ++l) {
+                        const int i = 16 * s16 + l, n = i >> 7, c = (i >> 5) & 3, ll = i & 31;
+                        qw[l] = (((blk[64 * n + 32 * (c & 1) + ll] >> (4 * (c >> 1))) & 15) |
+                                 (((blk[Q6K_QH + 32 * n + ll] >> (2 * c)) & 3) << 4)) - 32;
+                    }
+                    const double fa = d * (double)(int8_t)blk[Q6K_SC + s16];
+                    for (int t = 0; t < ntok; ++t) {
+                        int32_t isum = 0;
+                        for (int l = 0; l < 16; ++l) isum += qw[l] * (int32_t)xq[t][k0 + l];
+                        acc[t] += fa * (double)xd[t][k0 / 32] * (double)isum;
+                    }
+                }
+            }
+        }
+        for (int t = 0; t < ntok; ++t) y[t][r] = (float)acc[t];
+    }
+}
+
 static void kq_matvec_multi(int fmt, const uint8_t* W, int rows, int K, const int8_t* const* xq, const float* const* xd,
                             int ntok, float* const* y) {
+    if (fmt == FMT_Q5K || fmt == FMT_Q6K) { q56_matvec_multi(fmt, W, rows, K, xq, xd, ntok, y); return; }
     const int NB = K / QK, nb = fmt_block_bytes(fmt);
     const int qs = fmt == FMT_Q2K ? Q2K_QS : Q3K_QS;
     #pragma omp parallel for schedule(static)
@@ -369,11 +444,15 @@ struct OrcLayerW {
 // hq8 = 1: the SwiGLU output is re-quantised to q8 per 32 before the down projection (the reference's
 // swiglu_q8, src/fused_layer.cu:334-341: the decode and narrow paths); hq8 = 0: it enters the down
 // projection unquantised (the tensor-core prefill path).
-// down_fmt: format of every down matrix, routed and shared (FMT_IQ2, FMT_Q2K or FMT_Q3K; the K-quants
-// need hq8 = 1, the reference's narrow and wide passes)
-int orc_moe_layer_fmt(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
-                      int KE, float* h, float* moe, float* y_slot, float* shared_out, int hq8, int down_fmt) {
+// down_fmt: format of every routed down matrix (FMT_IQ2, FMT_Q2K or FMT_Q3K; the K-quants need hq8 = 1,
+// the reference's narrow and wide passes).  The shared expert's gate/up are in sh_gu_fmt (FMT_IQ2, or the
+// real model's FMT_Q5K) and its down in sh_down_fmt (down_fmt, or FMT_Q6K); its SwiGLU output is always
+// re-quantised to q8 when either is a K-quant (the reference's shared path, fused_layer.cu:521-524).
+int orc_moe_layer_fmt2(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
+                       int KE, float* h, float* moe, float* y_slot, float* shared_out, int hq8, int down_fmt,
+                       int sh_gu_fmt, int sh_down_fmt) {
     if (down_fmt != FMT_IQ2 && (!hq8 || (down_fmt != FMT_Q2K && down_fmt != FMT_Q3K))) return 1;
+    if ((sh_gu_fmt != FMT_IQ2 && sh_gu_fmt != FMT_Q5K) || (sh_down_fmt != down_fmt && sh_down_fmt != FMT_Q6K)) return 1;
     const int E = HIDDEN, H = MOE_INTER;
     // q8 of every token's x
     std::vector<int8_t> xq((size_t)T * E); std::vector<float> xd((size_t)T * E / 32);
@@ -424,8 +503,13 @@ int orc_moe_layer_fmt(const float* x, const float* resid, int T, const OrcLayerW
             xqp[t] = xq.data() + (size_t)t * E; xdp[t] = xd.data() + (size_t)t * E / 32;
             sgp[t] = sg.data() + (size_t)t * H; sup[t] = su.data() + (size_t)t * H; shp[t] = sh.data() + (size_t)t * E;
         }
-        iq2_matvec_multi(Wl->sh_gate, H, E, xqp.data(), xdp.data(), T, sgp.data());
-        iq2_matvec_multi(Wl->sh_up, H, E, xqp.data(), xdp.data(), T, sup.data());
+        if (sh_gu_fmt == FMT_Q5K) {
+            kq_matvec_multi(FMT_Q5K, Wl->sh_gate, H, E, xqp.data(), xdp.data(), T, sgp.data());
+            kq_matvec_multi(FMT_Q5K, Wl->sh_up, H, E, xqp.data(), xdp.data(), T, sup.data());
+        } else {
+            iq2_matvec_multi(Wl->sh_gate, H, E, xqp.data(), xdp.data(), T, sgp.data());
+            iq2_matvec_multi(Wl->sh_up, H, E, xqp.data(), xdp.data(), T, sup.data());
+        }
         std::vector<int8_t> shq((size_t)T * H); std::vector<float> shd((size_t)T * H / 32), shf((size_t)T * H);
         std::vector<const int8_t*> hqp(T); std::vector<const float*> hdp(T), hfp(T);
         for (int t = 0; t < T; ++t) {
@@ -434,8 +518,8 @@ int orc_moe_layer_fmt(const float* x, const float* resid, int T, const OrcLayerW
             orc_quant_q8(hv, H, shq.data() + (size_t)t * H, shd.data() + (size_t)t * H / 32);
             hqp[t] = shq.data() + (size_t)t * H; hdp[t] = shd.data() + (size_t)t * H / 32; hfp[t] = hv;
         }
-        if (down_fmt != FMT_IQ2) kq_matvec_multi(down_fmt, Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
-        else if (hq8) iq2_matvec_multi(Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
+        if (sh_down_fmt != FMT_IQ2) kq_matvec_multi(sh_down_fmt, Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
+        else if (hq8 || sh_gu_fmt != FMT_IQ2) iq2_matvec_multi(Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
         else iq2_matvec_float_multi(Wl->sh_down, E, H, hfp.data(), T, shp.data());
     }
     // combine in fixed k order
@@ -450,6 +534,11 @@ int orc_moe_layer_fmt(const float* x, const float* resid, int T, const OrcLayerW
     if (y_slot) memcpy(y_slot, yslot.data(), yslot.size() * 4);
     if (shared_out) memcpy(shared_out, sh.data(), sh.size() * 4);
     return 0;
+}
+
+int orc_moe_layer_fmt(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
+                      int KE, float* h, float* moe, float* y_slot, float* shared_out, int hq8, int down_fmt) {
+    return orc_moe_layer_fmt2(x, resid, T, Wl, ids, w, KE, h, moe, y_slot, shared_out, hq8, down_fmt, FMT_IQ2, down_fmt);
 }
 
 int orc_moe_layer_ex(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,

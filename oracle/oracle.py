@@ -17,8 +17,8 @@ MOE_INTER = 2048
 N_EXPERTS = 256
 QK = 256
 BLK_IQ2 = 66
-FMT_IQ2, FMT_Q2K, FMT_Q3K = 4, 5, 6
-BLOCK_BYTES = {FMT_IQ2: 66, FMT_Q2K: 84, FMT_Q3K: 110}
+FMT_Q6K, FMT_Q5K, FMT_IQ2, FMT_Q2K, FMT_Q3K = 1, 3, 4, 5, 6
+BLOCK_BYTES = {FMT_IQ2: 66, FMT_Q2K: 84, FMT_Q3K: 110, FMT_Q5K: 176, FMT_Q6K: 210}
 
 
 def build(force=False):
@@ -67,6 +67,8 @@ def lib():
         L.orc_moe_layer_fmt.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(LayerW), P, P, ctypes.c_int, P, P, P, P, ctypes.c_int,
                                         ctypes.c_int]
         L.orc_moe_layer_fmt.restype = ctypes.c_int
+        L.orc_moe_layer_fmt2.argtypes = L.orc_moe_layer_fmt.argtypes + [ctypes.c_int, ctypes.c_int]
+        L.orc_moe_layer_fmt2.restype = ctypes.c_int
         L.orc_kq_dequant.argtypes = [ctypes.c_int, P, ctypes.c_int64, P]
         L.orc_gen_kq.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                  ctypes.c_int, P]
@@ -94,7 +96,7 @@ def gen_iq2(seed, layer, matrix, expert, rows, K):
 
 
 def kq_dequant(fmt, blocks):
-    """Q2_K (fmt 5) / Q3_K (fmt 6) blocks -> fp32 weights (gguf-py dequantize semantics)."""
+    """Q2_K (fmt 5), Q3_K (6), Q5_K (3) or Q6_K (1) blocks -> fp32 weights (gguf-py dequantize semantics)."""
     blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
     nblk = blocks.size // BLOCK_BYTES[fmt]
     out = np.empty(nblk * QK, np.float32)
@@ -109,7 +111,7 @@ def gen_kq(fmt, seed, layer, matrix, expert, rows, K):
 
 
 def gen_matrix(fmt, seed, layer, matrix, expert, rows, K):
-    """Seeded matrix in any of the three formats (IQ2_XXS uses the IQ2 generator)."""
+    """Seeded matrix in any supported format (IQ2_XXS uses the IQ2 generator)."""
     return gen_iq2(seed, layer, matrix, expert, rows, K) if fmt == FMT_IQ2 else gen_kq(fmt, seed, layer, matrix, expert, rows, K)
 
 
@@ -178,13 +180,15 @@ def iq2_matvec(W, rows, K, xq, xd):
 
 
 def moe_layer(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None, sh_down=None, want_slots=False, hq8=True,
-              down_fmt=FMT_IQ2, down_stride=None):
+              down_fmt=FMT_IQ2, down_stride=None, sh_gu_fmt=FMT_IQ2, sh_down_fmt=None):
     """Reference MoE layer on arena-layout weights (expert m at m*stride bytes of each arena).
 
     Returns dict(h, moe[, y_slot, shared]).  ids/w: [T, KE] expert ids (arena slots) and weights.
     hq8: re-quantise the SwiGLU output to q8 before the down projection (reference semantics; the
     tensor-core prefill path keeps it at 16-bit precision: hq8=False).  down_fmt: format of every down
-    matrix (routed and shared); down_stride: the down arena's expert stride (default `stride`)."""
+    matrix (routed and shared); down_stride: the down arena's expert stride (default `stride`).
+    sh_gu_fmt / sh_down_fmt: the shared expert's formats (default IQ2_XXS and down_fmt; the real model's are
+    FMT_Q5K and FMT_Q6K)."""
     x = np.ascontiguousarray(x, np.float32)
     resid = np.ascontiguousarray(resid, np.float32)
     ids = np.ascontiguousarray(ids, np.int32)
@@ -198,8 +202,8 @@ def moe_layer(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None
     moe = np.empty((T, HIDDEN), np.float32)
     ys = np.empty((T, KE, HIDDEN), np.float32) if want_slots else None
     sh = np.empty((T, HIDDEN), np.float32) if want_slots else None
-    rc = lib().orc_moe_layer_fmt(_p(x), _p(resid), T, ctypes.byref(lw), _p(ids), _p(w), KE, _p(h), _p(moe), _p(ys), _p(sh),
-                                 1 if hq8 else 0, down_fmt)
+    rc = lib().orc_moe_layer_fmt2(_p(x), _p(resid), T, ctypes.byref(lw), _p(ids), _p(w), KE, _p(h), _p(moe), _p(ys), _p(sh),
+                                  1 if hq8 else 0, down_fmt, sh_gu_fmt, down_fmt if sh_down_fmt is None else sh_down_fmt)
     assert rc == 0
     out = {"h": h, "moe": moe}
     if want_slots:

@@ -16,6 +16,9 @@ independent implementation of the same format and against itself over time:
                      subnormal / negative / large d and dmin) and their dequantisation by gguf-py 0.19.0
                      (the Python port of ggml's dequantize_row_q2_K / q3_K), plus the oracle layer with
                      each K-quant down format on a small arena (4 experts, T=2).
+  shared_kq_gguf.npz Q5_K and Q6_K blocks (the real model's shared-expert formats; seeded and edge blocks)
+                     and their dequantisation by gguf-py 0.19.0, plus the oracle layer with IQ2_XXS routed
+                     gate/up, Q3_K routed downs and a Q5_K / Q6_K shared expert (3 experts, T=2).
 
 Run from the repository root:  python tests/golden/make_golden.py [name ...]   (no name: every fixture)
 """
@@ -102,12 +105,67 @@ def make_kquant():
     np.savez_compressed(os.path.join(HERE, "kquant_gguf.npz"), **out)
 
 
+def shared_kq_blocks(fmt, nb):
+    """Uniform random Q5_K / Q6_K blocks whose fp16 d (and Q5_K dmin) walk the edge values (finite only)."""
+    rng = np.random.default_rng(31 + fmt)
+    blocks = rng.integers(0, 256, (48, nb), dtype=np.uint8)
+    ds = [0.0, 1e-3, -2.5e-3, 6.0e-8, 1.0, 65504.0, 3.0517578125e-05, 0.5, -0.75]
+    doff = 0 if fmt == O.FMT_Q5K else nb - 2
+    for b in range(48):
+        d = np.float16(ds[b % len(ds)]) if b < 2 * len(ds) else np.float16(rng.standard_normal() * 4e-5)
+        blocks[b, doff:doff + 2] = np.frombuffer(np.array([d], np.float16).tobytes(), np.uint8)
+        if fmt == O.FMT_Q5K:
+            m = np.float16(ds[(b + 3) % len(ds)]) if b < 2 * len(ds) else np.float16(abs(rng.standard_normal()) * 4e-5)
+            blocks[b, 2:4] = np.frombuffer(np.array([m], np.float16).tobytes(), np.uint8)
+    return blocks.reshape(-1)
+
+
+def make_shared_kq():
+    """The real model's shared-expert formats: Q5_K (gate/up) and Q6_K (down) blocks dequantised by gguf-py,
+    and a layer KAT with IQ2_XXS routed gate/up, Q3_K routed downs and a Q5_K / Q6_K shared expert."""
+    from gguf.quants import dequantize
+    from gguf import GGMLQuantizationType as QT
+    out = {}
+    for fmt, qt, tag in ((O.FMT_Q5K, QT.Q5_K, "q5k"), (O.FMT_Q6K, QT.Q6_K, "q6k")):
+        seeded = O.gen_kq(fmt, SEED, 0, 0 if fmt == O.FMT_Q5K else 2, 256, 8, 2048)
+        blocks = np.concatenate([shared_kq_blocks(fmt, O.BLOCK_BYTES[fmt]), seeded])
+        out[tag + "_blocks"] = blocks
+        out[tag + "_dequant"] = dequantize(blocks, qt).reshape(-1).astype(np.float32)
+    lay = shared_kq_layer()
+    out.update({"layer_" + k: v for k, v in lay.items()})
+    np.savez_compressed(os.path.join(HERE, "shared_kq_gguf.npz"), **out)
+
+
+def shared_kq_layer():
+    """The layer KAT's inputs and outputs (the test rebuilds the weights from the same seeds)."""
+    NE = 3
+    S, DS = 2048 * 28 * 66, 7168 * 8 * O.BLOCK_BYTES[O.FMT_Q3K]
+    gate = np.concatenate([O.gen_iq2(SEED, 12, 0, e, 2048, 7168) for e in range(NE)])
+    up = np.concatenate([O.gen_iq2(SEED, 12, 1, e, 2048, 7168) for e in range(NE)])
+    down = np.concatenate([O.gen_kq(O.FMT_Q3K, SEED, 12, 2, e, 7168, 2048) for e in range(NE)])
+    shg = O.gen_kq(O.FMT_Q5K, SEED, 12, 0, 256, 2048, 7168)
+    shu = O.gen_kq(O.FMT_Q5K, SEED, 12, 1, 256, 2048, 7168)
+    shd = O.gen_kq(O.FMT_Q6K, SEED, 12, 2, 256, 7168, 2048)
+    rng = np.random.default_rng(78)
+    xs = rng.standard_normal((2, 7168)).astype(np.float32)
+    rs = rng.standard_normal((2, 7168)).astype(np.float32)
+    ids = np.array([[0, 2], [1, 0]], np.int32)
+    wk = rng.uniform(0.1, 1.0, (2, 2)).astype(np.float32)
+    lay = O.moe_layer(xs, rs, gate, up, down, S, ids, wk, shg, shu, shd, want_slots=True, down_fmt=O.FMT_Q3K, down_stride=DS,
+                      sh_gu_fmt=O.FMT_Q5K, sh_down_fmt=O.FMT_Q6K)
+    return {"ids": ids, "w": wk, "h": lay["h"], "moe": lay["moe"], "shared": lay["shared"]}
+
+
 def main(names):
     from gguf.quants import dequantize
     from gguf import GGMLQuantizationType as QT
     if names == ["kquant"]:
         make_kquant()
         print("kquant_gguf.npz written to", HERE)
+        return
+    if names == ["sharedkq"]:
+        make_shared_kq()
+        print("shared_kq_gguf.npz written to", HERE)
         return
 
     seeded = O.gen_iq2(SEED, 0, 0, 3, 8, 7168)            # 8 rows x 28 blocks
@@ -145,6 +203,7 @@ def main(names):
     out = O.moe_layer(xs, rs, gate, up, down, S, ids, wk, shg, shu, shd)
     np.savez_compressed(os.path.join(HERE, "moe_layer_kat.npz"), ids=ids, w=wk, h=out["h"], moe=out["moe"])
     make_kquant()
+    make_shared_kq()
     print("fixtures written to", HERE)
 
 

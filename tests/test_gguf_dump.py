@@ -138,12 +138,13 @@ def test_gguf_layer_on_gpu(native, oracle, tmp_path, down_fmt, f16_router):
 
 
 @pytest.mark.gpu
-def test_gguf_model_shared_expert_types_reported(native, oracle, tmp_path):
+def test_gguf_model_shared_expert_loaded(native, oracle, tmp_path):
+    """The real model's shared-expert types (Q5_K gate/up, Q6_K down) load as the model-format shared expert."""
     from loki_b200.gguf_experts import GgufLayer, GGML_Q5_K, GGML_Q6_K
     path = str(tmp_path / "layer.gguf")
     _write_layer_file(path, oracle, 5, model_shared=True)
     L = GgufLayer(path, 0)
-    assert L.down_fmt == 5 and not L.with_shared and L.shared_types == (GGML_Q5_K, GGML_Q5_K, GGML_Q6_K)
+    assert L.down_fmt == 5 and L.with_shared and L.sh_fmt == 3 and L.shared_types == (GGML_Q5_K, GGML_Q5_K, GGML_Q6_K)
 
 
 @pytest.mark.gpu

@@ -317,3 +317,84 @@ def test_kq_moe_layer_kat(oracle, fmt, tag, name):
     # the layer's down projection against the dequantised K-quant matrix (float64 restatement)
     D = oracle.kq_dequant(fmt, down[:DS]).reshape(7168, 2048).astype(np.float64)
     assert np.isfinite(D).all() and np.abs(D).max() > 0
+
+
+# ---------------------------------------------------------------- the shared expert's formats (Q5_K, Q6_K)
+SKQ = [(3, "q5k", "Q5_K", 7168), (1, "q6k", "Q6_K", 2048)]
+
+
+@pytest.mark.parametrize("fmt,tag,name,K", SKQ)
+def test_shared_kq_dequant_matches_gguf_fixture(oracle, fmt, tag, name, K):
+    f = np.load(os.path.join(GOLD, "shared_kq_gguf.npz"))
+    np.testing.assert_array_equal(oracle.kq_dequant(fmt, f[tag + "_blocks"]), f[tag + "_dequant"])
+
+
+@pytest.mark.parametrize("fmt,tag,name,K", SKQ)
+def test_shared_kq_dequant_matches_gguf_live(oracle, fmt, tag, name, K):
+    gguf = pytest.importorskip("gguf")
+    from gguf.quants import dequantize
+    blk = oracle.gen_kq(fmt, SEED, 7, 0, 256, 16, K)
+    np.testing.assert_array_equal(oracle.kq_dequant(fmt, blk), dequantize(blk, getattr(gguf.GGMLQuantizationType, name)).reshape(-1))
+
+
+@pytest.mark.parametrize("fmt,tag,name,K", SKQ)
+def test_shared_kq_matvec_vs_float64(oracle, fmt, tag, name, K):
+    """The reference's per-sub-block integer arithmetic (Q5_K per 32 with the min term, Q6_K per 16) equals
+    the dequantised matrix times the q8 activations."""
+    rng = np.random.default_rng(10)
+    rows = 64
+    W = oracle.gen_kq(fmt, SEED, 2, 0, 256, rows, K)
+    x = rng.standard_normal(K).astype(np.float32)
+    q, d = oracle.quant_q8(x)
+    y = oracle.kq_matvec(fmt, W, rows, K, q, d)
+    ref = oracle.kq_dequant(fmt, W).reshape(rows, K).astype(np.float64) @ _q8_dequant(oracle, x)
+    assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < 1e-6
+
+
+def test_q5k_scale_min_matches_restatement(oracle):
+    """Q5_K's packed (scale, min) pairs against a bit-level restatement of ggml's get_scale_min_k4: with q = 1
+    everywhere (qs nibbles 1, qh bits 0), d = 1 and dmin = 0 each sub-block's weights equal its scale."""
+    rng = np.random.default_rng(22)
+    blk = rng.integers(0, 256, (64, 176), dtype=np.uint8)
+    blk[:, 0:2] = np.frombuffer(np.array([1.0] * 64, np.float16).tobytes(), np.uint8).reshape(64, 2)
+    blk[:, 2:4] = 0
+    blk[:, 16:48] = 0
+    blk[:, 48:176] = 0x11
+    deq = oracle.kq_dequant(3, blk.reshape(-1)).reshape(64, 8, 32)
+    for b in range(64):
+        q = blk[b, 4:16].astype(int)
+        sc = [q[j] & 63 if j < 4 else (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4) for j in range(8)]
+        np.testing.assert_array_equal(deq[b, :, 0], np.array(sc, np.float32))
+
+
+def test_shared_kq_moe_layer_kat(oracle):
+    """IQ2_XXS routed gate/up, Q3_K routed downs and the real model's Q5_K / Q6_K shared expert."""
+    f = np.load(os.path.join(GOLD, "shared_kq_gguf.npz"))
+    NE = 3
+    S, DS = 2048 * 28 * 66, 7168 * 8 * 110
+    gate = np.concatenate([oracle.gen_iq2(SEED, 12, 0, e, 2048, 7168) for e in range(NE)])
+    up = np.concatenate([oracle.gen_iq2(SEED, 12, 1, e, 2048, 7168) for e in range(NE)])
+    down = np.concatenate([oracle.gen_kq(6, SEED, 12, 2, e, 7168, 2048) for e in range(NE)])
+    shg = oracle.gen_kq(3, SEED, 12, 0, 256, 2048, 7168)
+    shu = oracle.gen_kq(3, SEED, 12, 1, 256, 2048, 7168)
+    shd = oracle.gen_kq(1, SEED, 12, 2, 256, 7168, 2048)
+    rng = np.random.default_rng(78)
+    xs = rng.standard_normal((2, 7168)).astype(np.float32)
+    rs = rng.standard_normal((2, 7168)).astype(np.float32)
+    out = oracle.moe_layer(xs, rs, gate, up, down, S, f["layer_ids"], f["layer_w"], shg, shu, shd, want_slots=True,
+                           down_fmt=6, down_stride=DS, sh_gu_fmt=3, sh_down_fmt=1)
+    np.testing.assert_array_equal(out["h"], f["layer_h"])
+    np.testing.assert_array_equal(out["moe"], f["layer_moe"])
+    np.testing.assert_array_equal(out["shared"], f["layer_shared"])
+    # the shared part against a float64 restatement from the gguf-py-pinned dequantisation
+    G = oracle.kq_dequant(3, shg).reshape(2048, 7168).astype(np.float64)
+    U = oracle.kq_dequant(3, shu).reshape(2048, 7168).astype(np.float64)
+    D = oracle.kq_dequant(1, shd).reshape(7168, 2048).astype(np.float64)
+    xq = _q8_dequant(oracle, xs[0])
+    g, u = G @ xq, U @ xq
+    hsw = (g / (1 + np.exp(-g))) * u
+    ref = D @ _q8_dequant(oracle, hsw.astype(np.float32))
+    assert np.linalg.norm(out["shared"][0] - ref) / np.linalg.norm(ref) < 1e-3
+    # shared and routed parts have comparable magnitudes with the generator's scales
+    r = np.linalg.norm(out["shared"]) / np.linalg.norm(out["moe"])
+    assert 0.05 < r < 20
