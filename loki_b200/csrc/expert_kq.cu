@@ -18,10 +18,9 @@
 //         isum = dp4a(q6, x) - 32 * sum q_x, v += dx * d * scale * isum (int8 scales, one word per quarter)
 // the reference's per-16 arithmetic with exact integer sums.  Q3_K (110 B) and Q6_K (210 B) blocks are only
 // 2-byte aligned in shared memory, so their words are read as aligned pairs and funnel-shifted.  Q6_K units
-// are 53 760 B, so its ring has one stage per group (4) instead of two.
-// Shared-only mode (slot_expert == null, launch_shared_kq): slot j is the shared expert of token j, written to
-// y row sh_row0 + j with weight 1; with sh_gu set, each lane forms SwiGLU and the q8 of its own 64 h values
-// (two whole q8 groups) from the fp32 gate/up rows.
+// rows are 1 680 B, so its warps take 4 rows each (units of 16 rows, 26 880 B).
+// Shared-only mode (slot_expert == null, launch_shared_kq): slot j is the shared expert of token j: h from
+// hq/hd row sh_row0 + j, written to y row sh_row0 + j with weight 1.
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
@@ -43,15 +42,18 @@ template <> struct KqFmt<FMT_Q6K> { static constexpr int BLK = BLK_Q6K; };
 
 constexpr int KQ_WARPS = 16;
 constexpr int KQ_THREADS = (KQ_WARPS + 1) * 32;
-constexpr int KQ_WROWS = 8;                          // rows per warp
-constexpr int KQ_UROWS = 32;                         // rows per unit (one bulk copy)
-constexpr int KQ_GROUPS = KQ_WARPS / (KQ_UROWS / KQ_WROWS);   // 4 groups of 4 warps
-constexpr int KQ_UNITS_PER_SLOT = HIDDEN / KQ_UROWS; // 224
+constexpr int KQ_GWARPS = 4;                         // warps per group: a unit is 4 warps x kq_wrows rows
+constexpr int KQ_GROUPS = KQ_WARPS / KQ_GWARPS;      // 4 groups
 
+// rows per warp: 8, or 4 for Q6_K (the shared expert's down: one matrix per token, so at T = 1 each SM
+// has ~48 rows and shorter units keep more warps busy)
+template <int FMT> constexpr int kq_wrows() { return FMT == FMT_Q6K ? 4 : 8; }
+template <int FMT> constexpr int kq_urows() { return KQ_GWARPS * kq_wrows<FMT>(); }          // 32 / 16 rows per unit
+template <int FMT> constexpr int kq_units_per_slot() { return HIDDEN / kq_urows<FMT>(); }    // 224 / 448
 template <int FMT> constexpr int kq_rowb() { return (MOE_INTER / QK) * KqFmt<FMT>::BLK; }     // 672 / 880 / 1680
-template <int FMT> constexpr int kq_ubytes() { return KQ_UROWS * kq_rowb<FMT>(); }
-// ring stages: group g uses stages g and g + 4; Q6_K's 53 760-byte units allow one stage per group
-template <int FMT> constexpr int kq_nst() { return FMT == FMT_Q6K ? KQ_GROUPS : 2 * KQ_GROUPS; }
+template <int FMT> constexpr int kq_ubytes() { return kq_urows<FMT>() * kq_rowb<FMT>(); }
+// ring stages: group g uses stages g and g + 4
+template <int FMT> constexpr int kq_nst() { return 2 * KQ_GROUPS; }
 template <int FMT> constexpr int kq_off_bar() { return kq_nst<FMT>() * kq_ubytes<FMT>(); }
 template <int FMT> constexpr int kq_smem() { return kq_off_bar<FMT>() + 2 * kq_nst<FMT>() * 8 + 16; }
 static_assert(kq_smem<FMT_Q3K>() <= 232448 && kq_smem<FMT_Q6K>() <= 232448, "K-quant ring exceeds shared memory");
@@ -166,6 +168,7 @@ __device__ __forceinline__ float kq_row_dot(uint32_t blk, uint32_t sh, int q, co
 template <int FMT>
 __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
     constexpr int RB = kq_rowb<FMT>(), UB = kq_ubytes<FMT>(), KQ_NST = kq_nst<FMT>();
+    constexpr int WROWS = kq_wrows<FMT>(), UROWS = kq_urows<FMT>(), UPS = kq_units_per_slot<FMT>();
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* ring = smem;
     uint64_t* full = (uint64_t*)(smem + kq_off_bar<FMT>());
@@ -174,7 +177,7 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         *abort_flag = 0;
-        for (int s = 0; s < KQ_NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], KQ_UROWS / KQ_WROWS); }
+        for (int s = 0; s < KQ_NST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], KQ_GWARPS); }
         fence_mbar_init();
     }
     __syncthreads();
@@ -182,7 +185,7 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
     pdl_wait();
     const bool sh_only = p.slot_expert == nullptr;   // shared-only slots (launch_shared_kq)
     const int nslots = sh_only ? p.sh_count : *p.nslots;
-    const int nunits = nslots * KQ_UNITS_PER_SLOT;
+    const int nunits = nslots * UPS;
     const int u0 = (int)((long long)blockIdx.x * nunits / gridDim.x);
     const int nu = (int)((long long)(blockIdx.x + 1) * nunits / gridDim.x) - u0;
     if (nu <= 0) return;
@@ -190,7 +193,7 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
         if (lane == 0) {
             int j = 0;
             for (; j < nu; ++j) {
-                const int u = u0 + j, s = u / KQ_UNITS_PER_SLOT, cu = u % KQ_UNITS_PER_SLOT;
+                const int u = u0 + j, s = u / UPS, cu = u % UPS;
                 const int st = j % KQ_NST;
                 if (*abort_flag || !mbar_wait(&empty[st], ((j / KQ_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
                 const uint8_t* dw = kq_down_matrix(p, sh_only ? SHARED_SLOT : p.slot_expert[s]);
@@ -209,33 +212,15 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
     const int b = lane >> 2, q = lane & 3;
     const uint32_t boff = (uint32_t)(b * KqFmt<FMT>::BLK);
     const uint32_t balign = boff & ~3u, bsh = (boff & 3u) * 8u;          // Q3_K: odd blocks sit 2 bytes past a word
-    const int grp = warp / (KQ_UROWS / KQ_WROWS), sub = warp % (KQ_UROWS / KQ_WROWS);
+    const int grp = warp / KQ_GWARPS, sub = warp % KQ_GWARPS;
     uint32_t xr[16]; float dx[2] = {0.0f, 0.0f}; int xs[4] = {0, 0, 0, 0};
     int xslot = -1, out = -1;
     float wv = 0.0f;
     for (int j = grp; j < nu; j += KQ_GROUPS) {
-        const int u = u0 + j, s = u / KQ_UNITS_PER_SLOT, cu = u % KQ_UNITS_PER_SLOT;
+        const int u = u0 + j, s = u / UPS, cu = u % UPS;
         if (s != xslot) {                             // this slot's h (q8): K [256b + 64q, +64)
             xslot = s; out = sh_only ? p.sh_row0 + s : p.slot_out[s]; wv = sh_only ? 1.0f : p.slot_w[s];
-            if (sh_only && p.sh_gu) {                 // SwiGLU + q8 of this lane's two h groups from fp32 gate/up
-                const float* gr = p.sh_gu + (size_t)s * 2 * MOE_INTER + b * QK + 64 * q;
-                #pragma unroll
-                for (int hg = 0; hg < 2; ++hg) {
-                    float hv[32];
-                    #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float4 gv = ((const float4*)(gr + 32 * hg))[i], uv = ((const float4*)(gr + MOE_INTER + 32 * hg))[i];
-                        hv[4*i] = lk_swiglu(gv.x, uv.x); hv[4*i+1] = lk_swiglu(gv.y, uv.y);
-                        hv[4*i+2] = lk_swiglu(gv.z, uv.z); hv[4*i+3] = lk_swiglu(gv.w, uv.w);
-                    }
-                    int8_t qv[32];
-                    dx[hg] = quant_q8_group(hv, qv);
-                    #pragma unroll
-                    for (int w = 0; w < 8; ++w)
-                        xr[8 * hg + w] = (uint32_t)(uint8_t)qv[4*w] | ((uint32_t)(uint8_t)qv[4*w+1] << 8) |
-                                         ((uint32_t)(uint8_t)qv[4*w+2] << 16) | ((uint32_t)(uint8_t)qv[4*w+3] << 24);
-                }
-            } else if (out >= 0) {
+            if (out >= 0) {
                 const uint4* src = (const uint4*)(p.hq + (size_t)out * MOE_INTER + b * QK + 64 * q);
                 #pragma unroll
                 for (int c = 0; c < 4; ++c) { const uint4 a = src[c]; xr[4*c] = a.x; xr[4*c+1] = a.y; xr[4*c+2] = a.z; xr[4*c+3] = a.w; }
@@ -256,15 +241,20 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
         }
         const int st = j % KQ_NST;
         if (!mbar_wait(&full[st], (j / KQ_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
-        const uint32_t ub = ring_s + st * UB + sub * KQ_WROWS * RB;
-        float v[8];
+        const uint32_t ub = ring_s + st * UB + sub * WROWS * RB;
+        float v[WROWS];
         #pragma unroll
-        for (int r = 0; r < KQ_WROWS; ++r) v[r] = kq_row_dot<FMT>(ub + r * RB + (FMT == FMT_Q2K ? boff : balign), bsh, q, xr, dx, xs);
+        for (int r = 0; r < WROWS; ++r) v[r] = kq_row_dot<FMT>(ub + r * RB + (FMT == FMT_Q2K ? boff : balign), bsh, q, xr, dx, xs);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
-        const float sum = warp_reduce8(v, lane);      // lane l: row (l >> 2), 4 replicas
-        const int row0 = cu * KQ_UROWS + sub * KQ_WROWS;
-        if ((lane & 3) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 2)] = wv * sum;
+        const int row0 = cu * UROWS + sub * WROWS;
+        if constexpr (WROWS == 8) {
+            const float sum = warp_reduce8(*reinterpret_cast<float(*)[8]>(v), lane);   // lane l: row l >> 2, 4 replicas
+            if ((lane & 3) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 2)] = wv * sum;
+        } else {
+            const float sum = warp_reduce4(*reinterpret_cast<float(*)[4]>(v), lane);   // lane l: row l >> 3, 8 replicas
+            if ((lane & 7) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 3)] = wv * sum;
+        }
         if (*abort_flag) break;
     }
 }

@@ -51,6 +51,7 @@ struct FLCtx {
     // expert launches; fl_moe / fl_skip compute it first (ensure_shared)
     bool sh_pending = false; const void* sh_w[3] = {nullptr, nullptr, nullptr}; int sh_fmt = 0;
     float* sh_gu = nullptr;           // fp32 gate/up rows of the real model's shared expert (shared_kq.cu)
+    int* sh_pair = nullptr;           // its gate/up pairing counters (zeroed)
     // CUDA graphs of repeated call shapes (fl_moe_prepare, fl_moe, fl_moe_auto): one replay instead of a
     // dozen launches and copies.  A shape is captured on its second occurrence (the first runs directly).
     struct GraphKey { int kind, a, b, c, d; const void* p[8]; };
@@ -122,7 +123,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
         dz(&c->ncur, R) == cudaSuccess && dz(&c->ffn_inp, R) == cudaSuccess && dz(&c->logits, PREP_ROWS * N_EXPERTS) == cudaSuccess &&
         dz(&c->probs, PREP_ROWS * N_EXPERTS) == cudaSuccess && dz(&c->sel, PREP_ROWS * MAX_TOPK) == cudaSuccess &&
         dz(&c->wts, PREP_ROWS * MAX_TOPK) == cudaSuccess && dz(&c->shared_y, R) == cudaSuccess && dz(&c->h, R) == cudaSuccess &&
-        dz(&c->sh_gu, (size_t)PREP_ROWS * 2 * MOE_INTER) == cudaSuccess &&
+        dz(&c->sh_gu, (size_t)PREP_ROWS * 2 * MOE_INTER) == cudaSuccess && dz(&c->sh_pair, (size_t)PREP_ROWS * (MOE_INTER / 32)) == cudaSuccess &&
         dz(&c->moe, R) == cudaSuccess && dz(&c->ids, NB * MAX_TOPK) == cudaSuccess && dz(&c->w, NB * MAX_TOPK) == cudaSuccess &&
         dz(&c->mo, R) == cudaSuccess &&
         dz(&c->s_expert, ms) == cudaSuccess && dz(&c->s_tok, (size_t)ms * MAX_NT) == cudaSuccess &&
@@ -144,7 +145,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
 void fl_free(FLCtx* c) {
     if (!c) return;
     if (c->st) cudaStreamSynchronize(c->st);
-    void* d[] = { c->ncur, c->ffn_inp, c->logits, c->probs, c->sel, c->wts, c->shared_y, c->sh_gu, c->h, c->moe, c->ids, c->w, c->mo,
+    void* d[] = { c->ncur, c->ffn_inp, c->logits, c->probs, c->sel, c->wts, c->shared_y, c->sh_gu, c->sh_pair, c->h, c->moe, c->ids, c->w, c->mo,
                   c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->counts, c->offsets, c->perm, c->hq, c->hd, c->y, c->err,
                   c->ncur_all, c->base_all, c->out_all, c->whq, c->whd, c->rcount };
     for (void* p : d) if (p) cudaFree(p);
@@ -236,7 +237,7 @@ static void enqueue_shared(FLCtx* c, const void* g, const void* u, const void* d
         SharedKqParams sp{};
         sp.gate = (const uint8_t*)g; sp.up = (const uint8_t*)u; sp.down = (const uint8_t*)d;
         sp.x = c->ncur; sp.ld_x = HIDDEN; sp.t0 = 0; sp.n = n; sp.row0 = 0;
-        sp.gu = c->sh_gu; sp.y = c->shared_y; sp.err = c->err;
+        sp.gu = c->sh_gu; sp.hq = c->hq; sp.hd = c->hd; sp.pair = c->sh_pair; sp.y = c->shared_y; sp.err = c->err;
         launch_shared_kq(sp, c->nsm, c->st);
         return;
     }

@@ -28,7 +28,7 @@ struct LkMoeCtx {
     int sh_t0 = 0, sh_n = 0;          // shared-expert token range of the next expert stage (SlotParams semantics)
     // the shared expert in the real model's formats (W->sh_fmt == LK_FMT_Q5K) runs as its own launches
     // (shared_kq.cu); the routed slot tables then carry no shared slots (rs = 0).  shgu: its fp32 gate/up rows
-    int rs = 0; float* shgu = nullptr;
+    int rs = 0; float* shgu = nullptr; int* shpair = nullptr;
     // tensor-core path (T >= gemm_min_tokens): 64-token slots and fp16 operand staging
     int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
     __half* bt = nullptr; __half* ht = nullptr; int* g_cnt = nullptr; int gemm_min_tokens = 192;
@@ -122,7 +122,11 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LK_CU(dalloc(&c->m_out, (size_t)c->m_max * MM_NT)); LK_CU(dalloc(&c->m_w, (size_t)c->m_max * MM_NT)); LK_CU(dalloc(&c->m_n, 1));
     LK_CU(dalloc(&c->m_cnt, c->m_max));
     LK_CU(dalloc(&c->xh, (size_t)T * HIDDEN)); LK_CU(dalloc(&c->hb, rows * MOE_INTER));
-    if (cfg->with_shared) LK_CU(dalloc(&c->shgu, (size_t)T * 2 * MOE_INTER));
+    if (cfg->with_shared) {
+        LK_CU(dalloc(&c->shgu, (size_t)T * 2 * MOE_INTER));
+        LK_CU(dalloc(&c->shpair, (size_t)T * (MOE_INTER / 32)));
+        LK_CU(cudaMemset(c->shpair, 0, (size_t)T * (MOE_INTER / 32) * sizeof(int)));
+    }
     LK_CU(cudaMemset(c->y, 0, rows * HIDDEN * sizeof(float)));
     LK_CU(cudaDeviceSynchronize());
     cudaSetDevice(prev);
@@ -135,7 +139,7 @@ void lk_moe_destroy(LkMoeCtx* c) {
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
                      c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->xq, c->xqn, c->xd,
                      c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt,
-                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->xh, c->hb, c->shgu };
+                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->xh, c->hb, c->shgu, c->shpair };
     for (void* p : ptrs) if (p) cudaFree(p);
     delete c;
 }
@@ -305,7 +309,7 @@ static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_
         sp.x = x; sp.ld_x = ld_x;
         sp.n = c->sh_n < 0 ? 0 : (c->sh_n > 0 ? c->sh_n : T); sp.t0 = c->sh_n > 0 ? c->sh_t0 : 0; sp.row0 = T * keep;
         if (c->xq_ready && x == c->xq_src) { sp.xq = c->xq; sp.xd = c->xd; }
-        sp.gu = c->shgu; sp.y = c->y; sp.err = c->err;
+        sp.gu = c->shgu; sp.hq = c->hq; sp.hd = c->hd; sp.pair = c->shpair; sp.y = c->y; sp.err = c->err;
         launch_shared_kq(sp, c->nsm, st);
         if (keep == 0) {                              // shared expert only (lk_ep_shared)
             if (h || moe) {

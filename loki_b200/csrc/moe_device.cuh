@@ -271,4 +271,24 @@ __device__ __forceinline__ float warp_reduce8(float (&v)[8], int lane) {
     return r;
 }
 
+// warp reduction of 4 values per lane: every lane ends with the warp-wide sum of v[2*bit4 + bit3] of its
+// lane id (8 lanes share each).  Fixed order: halving exchanges over offsets 16 and 8, butterflies 4, 2, 1.
+__device__ __forceinline__ float warp_reduce4(float (&v)[4], int lane) {
+    #pragma unroll
+    for (int o = 16, h = 2; o >= 8; o >>= 1, h >>= 1) {
+        const bool up = (lane & o) != 0;
+        #pragma unroll
+        for (int i = 0; i < h; ++i) {
+            const float send = up ? v[i] : v[i + h];
+            const float keep = up ? v[i + h] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    float r = v[0];
+    r += __shfl_xor_sync(0xffffffffu, r, 4);
+    r += __shfl_xor_sync(0xffffffffu, r, 2);
+    r += __shfl_xor_sync(0xffffffffu, r, 1);
+    return r;
+}
+
 }  // namespace lk

@@ -78,10 +78,8 @@ struct ExpertParams {
     int* err;
     int down_fmt;                                     // FMT_IQ2 (default, 0 reads as IQ2), FMT_Q2K or FMT_Q3K: every down matrix
     // shared-only launches of launch_down1_kq (slot_expert == null): sh_count single-token slots, slot j
-    // reading sh_down into y row sh_row0 + j (weight 1); the slot's h from sh_gu (fp32 [j][gate 2048 | up
-    // 2048], SwiGLU and q8 formed per lane) when set, else from hq/hd rows sh_row0 + j
+    // reading sh_down and the q8 h of hq/hd row sh_row0 + j into y row sh_row0 + j (weight 1)
     int sh_count, sh_row0;
-    const float* sh_gu;
 };
 void launch_gate_up(const ExpertParams& p, int nt, int grid, cudaStream_t st);
 void launch_down(const ExpertParams& p, int nt, int grid, cudaStream_t st);
@@ -89,13 +87,14 @@ void launch_down(const ExpertParams& p, int nt, int grid, cudaStream_t st);
 void launch_down1_kq(const ExpertParams& p, int grid, cudaStream_t st);
 
 // the real model's shared expert (Q5_K gate/up, Q6_K down; shared_kq.cu) of tokens [t0, t0 + n) of x as its
-// own launches: gate/up rows into gu (fp32 [n][2][MOE_INTER]), the down into y rows row0 + j (weight 1)
+// own launches: gate/up rows into gu (fp32 [n][2][MOE_INTER]), SwiGLU q8 into hq/hd rows row0 + j, the down
+// into y rows row0 + j (weight 1).  pair: n * 64 zeroed counters (left zeroed)
 struct SharedKqParams {
     const uint8_t* gate; const uint8_t* up; const uint8_t* down;
     const float* x; int ld_x;
     int t0, n, row0;
     const int8_t* xq; const float* xd;                // optional: token 0's q8 x from the router
-    float* gu; float* y; int* err;
+    float* gu; int8_t* hq; float* hd; int* pair; float* y; int* err;
 };
 void launch_shared_kq(const SharedKqParams& p, int grid, cudaStream_t st);
 

@@ -12,9 +12,11 @@
 //   v = dx * (d*scale*isum - dmin*min*sum q_x)
 // -- the reference's per-32 integer arithmetic.  A block's header (d, dmin, 12 scale bytes), its 32 qh bytes
 // and the thread's 32 qs bytes are five 16-byte shared loads (Q5_K blocks are 176 B: 16-byte aligned).  The
-// tile's row sums (7 warps per row, fixed order) go to `gu` as fp32 [token][gate 2048 | up 2048].
-// down: k_down1_kq<FMT_Q6K> (expert_kq.cu) in its shared-only mode: each lane forms SwiGLU and the q8 of its
-// own 64 h values from `gu` (two whole q8 groups), the reference's swiglu_q8.
+// tile's row sums (7 warps per row, fixed order) go to `gu` as fp32 [token][gate 2048 | up 2048].  The gate
+// and up tiles of the same rows run on different CTAs: a per-(token, row tile) counter (fence, then atomic
+// add) tells the CTA that finishes second, which forms SwiGLU and the q8 of those 32 h values (one q8 group,
+// the reference's swiglu_q8) from its own sums and the partner's, and resets the counter.
+// down: k_down1_kq<FMT_Q6K> (expert_kq.cu) in its shared-only mode, reading those q8 rows.
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
@@ -47,26 +49,6 @@ __device__ __forceinline__ uint4 lds_v4(uint32_t a) {
     uint4 v;
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
-}
-
-// warp reduction of 4 values per lane: every lane ends with the warp-wide sum of v[2*bit4 + bit3] of its
-// lane id (8 lanes share each).  Fixed order: halving exchanges over offsets 16 and 8, butterflies 4, 2, 1.
-__device__ __forceinline__ float warp_reduce4(float (&v)[4], int lane) {
-    #pragma unroll
-    for (int o = 16, h = 2; o >= 8; o >>= 1, h >>= 1) {
-        const bool up = (lane & o) != 0;
-        #pragma unroll
-        for (int i = 0; i < h; ++i) {
-            const float send = up ? v[i] : v[i + h];
-            const float keep = up ? v[i + h] : v[i];
-            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-    }
-    float r = v[0];
-    r += __shfl_xor_sync(0xffffffffu, r, 4);
-    r += __shfl_xor_sync(0xffffffffu, r, 2);
-    r += __shfl_xor_sync(0xffffffffu, r, 1);
-    return r;
 }
 
 // q8 of the 32-wide group g of an fp32 row (global): 8 packed words, returns the scale
@@ -202,6 +184,25 @@ __global__ void __launch_bounds__(S5_THREADS, 1) k_sh_gate_up_q5k(SharedKqParams
             #pragma unroll
             for (int w = 1; w < S5_SW; ++w) acc += q[w * 32];
             p.gu[(size_t)jm * MOE_INTER + rt * S5_TILE + lane] = acc;
+            __threadfence();                          // this half visible before the count
+            __syncwarp();
+            const int j = jm >> 1;
+            int* cnt = p.pair + (size_t)j * S5_TILES_PER_MAT + rt;
+            int old = 0;
+            if (lane == 0) old = atomicAdd(cnt, 1);
+            old = __shfl_sync(0xffffffffu, old, 0);
+            if (old == 1) {                           // the partner's half is done: SwiGLU + q8 of these 32 rows
+                __threadfence();
+                const float other = __ldcg(p.gu + (size_t)(jm ^ 1) * MOE_INTER + rt * S5_TILE + lane);
+                const float hv = (jm & 1) ? lk_swiglu(other, acc) : lk_swiglu(acc, other);
+                float amax = fabsf(hv);
+                #pragma unroll
+                for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                const float d = amax / 127.0f, id = d > 0.0f ? 1.0f / d : 0.0f;
+                const size_t out = (size_t)(p.row0 + j);
+                p.hq[out * MOE_INTER + rt * S5_TILE + lane] = (int8_t)(int)rintf(hv * id);
+                if (lane == 0) { p.hd[out * (MOE_INTER / 32) + rt] = d; *cnt = 0; }
+            }
         }
     }
 }
@@ -215,8 +216,8 @@ void launch_shared_kq(const SharedKqParams& p, int grid, cudaStream_t st) {
     const int tiles = p.n * 2 * S5_TILES_PER_MAT;
     launch_pdl(k_sh_gate_up_q5k, dim3(grid < tiles ? grid : tiles), dim3(S5_THREADS), S5_SMEM, st, p);
     ExpertParams e{};                                 // the down: k_down1_kq<Q6_K>, shared-only slots
-    e.sh_down = p.down; e.y = p.y; e.err = p.err; e.down_fmt = FMT_Q6K;
-    e.slot_expert = nullptr; e.sh_count = p.n; e.sh_row0 = p.row0; e.sh_gu = p.gu;
+    e.sh_down = p.down; e.hq = p.hq; e.hd = p.hd; e.y = p.y; e.err = p.err; e.down_fmt = FMT_Q6K;
+    e.slot_expert = nullptr; e.sh_count = p.n; e.sh_row0 = p.row0;
     launch_down1_kq(e, grid, st);
 }
 
