@@ -13,6 +13,7 @@
 #include "../../include/loki_fused_moe.h"
 #include "../../include/loki_moe.h"
 #include "moe_internal.h"
+#include "moe_device.cuh"
 
 using namespace lk;
 
@@ -21,6 +22,7 @@ constexpr int NB = 8;                 // narrow pass rows (fl_moe's n <= 8)
 constexpr int PREP_ROWS = 64;         // rows per fl_moe_prepare call (fl_attn's 8 groups of 8)
 constexpr int WIDE_SLOTS = 72;        // slots per wide launch set (the reference's XH_SLOTS)
 constexpr int NARROW_SLOTS = NB * MAX_TOPK;
+constexpr int P8 = PREP_ROWS * MAX_TOPK;           // router outputs of a prepare launch
 }
 
 struct FLCtx {
@@ -33,6 +35,13 @@ struct FLCtx {
     int *counts = nullptr, *offsets = nullptr, *perm = nullptr;
     int8_t* hq = nullptr; float* hd = nullptr; float* y = nullptr;
     int* err = nullptr; int* rcount = nullptr; int* h_err = nullptr;   // device error word and its pinned mirror
+    // paired buffers are allocated as one block each, so each pair crosses the bus in one 2-D copy:
+    // [ncur | ffn_inp], [h | moe] (rows PREP_ROWS * HIDDEN apart), [ids | w | err] (NARROW_SLOTS apart),
+    // [sel | wts] (P8 apart), and the same for their pinned host mirrors
+    void* blk[4] = {}; void* hblk[4] = {};
+    // the folded shared expert's rows of the last fl_moe_auto are still in y (rows n*KE..): copied into
+    // shared_y only when a later call needs it (materialize_shared)
+    int sh_in_y_n = 0, sh_in_y_ke = 0;
     // host mirrors (pinned)
     int* h_sel = nullptr; float* h_wts = nullptr; float* h_ncur = nullptr; float* h_fi = nullptr; float* h_h = nullptr;
     float* h_moe = nullptr; int* h_tab = nullptr; float* h_tabw = nullptr; float* h_in = nullptr;
@@ -79,7 +88,14 @@ template <class T> static cudaError_t hz(T** p, size_t n) {
     return e;
 }
 
-static int nt_for(int n) { return n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8; }
+// tokens per expert slot: one.  The single-token kernels' cheaper inner loop outruns the multi-token ones
+// at every narrow size (the device API's sweep: T=2 169 vs 187 us per layer, T=8 476 vs 978 us)
+static int nt_for(int) { return 1; }
+
+// rows [0, n) of two row-major buffers `pitch` bytes apart, in one copy
+static cudaError_t copy_pair(void* dst, const void* src, size_t pitch, size_t bytes, cudaMemcpyKind kind, cudaStream_t st) {
+    return cudaMemcpy2DAsync(dst, pitch, src, pitch, bytes, 2, kind, st);
+}
 
 // the device error word rides with a blocking call's result copies: queue_err before the stream
 // synchronisation, check_dev after it (no separate synchronous copy per call)
@@ -118,35 +134,42 @@ FLCtx* fl_init(int kvp, int sc_cap) {
     // hq / y rows of a narrow launch (n*KE routed + n shared entries) or a prepare launch
     const size_t rows = (size_t)std::max(NARROW_SLOTS + NB, PREP_ROWS);
     const int ms = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1);
+    float *io = nullptr, *ho = nullptr, *h_io = nullptr, *h_ho = nullptr;
+    int *iwe = nullptr, *sw = nullptr, *h_iwe = nullptr, *h_sw = nullptr;
     bool ok =
         cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) == cudaSuccess &&
-        dz(&c->ncur, R) == cudaSuccess && dz(&c->ffn_inp, R) == cudaSuccess && dz(&c->logits, PREP_ROWS * N_EXPERTS) == cudaSuccess &&
-        dz(&c->probs, PREP_ROWS * N_EXPERTS) == cudaSuccess && dz(&c->sel, PREP_ROWS * MAX_TOPK) == cudaSuccess &&
-        dz(&c->wts, PREP_ROWS * MAX_TOPK) == cudaSuccess && dz(&c->shared_y, R) == cudaSuccess && dz(&c->h, R) == cudaSuccess &&
+        dz(&io, 2 * R) == cudaSuccess && dz(&ho, 2 * R) == cudaSuccess && dz(&iwe, 3 * NARROW_SLOTS) == cudaSuccess &&
+        dz(&sw, 2 * P8) == cudaSuccess && hz(&h_io, 2 * R) == cudaSuccess && hz(&h_ho, 2 * R) == cudaSuccess &&
+        hz(&h_iwe, 3 * NARROW_SLOTS) == cudaSuccess && hz(&h_sw, 2 * P8) == cudaSuccess &&
+        dz(&c->logits, PREP_ROWS * N_EXPERTS) == cudaSuccess &&
+        dz(&c->probs, PREP_ROWS * N_EXPERTS) == cudaSuccess && dz(&c->shared_y, R) == cudaSuccess &&
         dz(&c->sh_gu, (size_t)PREP_ROWS * 2 * MOE_INTER) == cudaSuccess && dz(&c->sh_pair, (size_t)PREP_ROWS * (MOE_INTER / 32)) == cudaSuccess &&
-        dz(&c->moe, R) == cudaSuccess && dz(&c->ids, NB * MAX_TOPK) == cudaSuccess && dz(&c->w, NB * MAX_TOPK) == cudaSuccess &&
         dz(&c->mo, R) == cudaSuccess &&
         dz(&c->s_expert, ms) == cudaSuccess && dz(&c->s_tok, (size_t)ms * MAX_NT) == cudaSuccess &&
         dz(&c->s_out, (size_t)ms * MAX_NT) == cudaSuccess && dz(&c->s_w, (size_t)ms * MAX_NT) == cudaSuccess && dz(&c->s_n, 1) == cudaSuccess &&
         dz(&c->counts, N_EXPERTS) == cudaSuccess && dz(&c->offsets, N_EXPERTS + 1) == cudaSuccess && dz(&c->perm, NB * MAX_TOPK) == cudaSuccess &&
         dz(&c->hq, rows * MOE_INTER) == cudaSuccess && dz(&c->hd, rows * (MOE_INTER / 32)) == cudaSuccess &&
-        dz(&c->y, rows * HIDDEN) == cudaSuccess && dz(&c->err, 1) == cudaSuccess &&
-        dz(&c->rcount, PREP_ROWS) == cudaSuccess && hz(&c->h_err, 1) == cudaSuccess &&
-        hz(&c->h_sel, PREP_ROWS * MAX_TOPK) == cudaSuccess && hz(&c->h_wts, PREP_ROWS * MAX_TOPK) == cudaSuccess &&
-        hz(&c->h_ncur, R) == cudaSuccess && hz(&c->h_fi, R) == cudaSuccess && hz(&c->h_h, R) == cudaSuccess &&
-        hz(&c->h_moe, R) == cudaSuccess && hz(&c->h_tab, (size_t)4 * ms * MAX_NT + 8) == cudaSuccess &&
-        hz(&c->h_tabw, (size_t)ms * MAX_NT) == cudaSuccess && hz(&c->h_in, R) == cudaSuccess &&
+        dz(&c->y, rows * HIDDEN) == cudaSuccess &&
+        dz(&c->rcount, PREP_ROWS) == cudaSuccess && hz(&c->h_in, R) == cudaSuccess &&
         cudaEventCreate(&c->em0) == cudaSuccess && cudaEventCreate(&c->em1) == cudaSuccess &&
         cudaEventCreate(&c->ep0) == cudaSuccess && cudaEventCreate(&c->ep1) == cudaSuccess;
+    c->blk[0] = io; c->blk[1] = ho; c->blk[2] = iwe; c->blk[3] = sw;
+    c->hblk[0] = h_io; c->hblk[1] = h_ho; c->hblk[2] = h_iwe; c->hblk[3] = h_sw;
     if (!ok) { fl_fail(c, LK_ERR_CUDA, "fl_init: allocation failed", cudaGetLastError()); fl_free(c); return nullptr; }
+    c->ncur = io; c->ffn_inp = io + R; c->h = ho; c->moe = ho + R;
+    c->ids = iwe; c->w = (float*)(iwe + NARROW_SLOTS); c->err = iwe + 2 * NARROW_SLOTS;
+    c->sel = sw; c->wts = (float*)(sw + P8);
+    c->h_ncur = h_io; c->h_fi = h_io + R; c->h_h = h_ho; c->h_moe = h_ho + R;
+    c->h_tab = h_iwe; c->h_tabw = (float*)(h_iwe + NARROW_SLOTS); c->h_err = h_iwe + 2 * NARROW_SLOTS;
+    c->h_sel = h_sw; c->h_wts = (float*)(h_sw + P8);
     return c;
 }
 
 void fl_free(FLCtx* c) {
     if (!c) return;
     if (c->st) cudaStreamSynchronize(c->st);
-    void* d[] = { c->ncur, c->ffn_inp, c->logits, c->probs, c->sel, c->wts, c->shared_y, c->sh_gu, c->sh_pair, c->h, c->moe, c->ids, c->w, c->mo,
-                  c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->counts, c->offsets, c->perm, c->hq, c->hd, c->y, c->err,
+    void* d[] = { c->blk[0], c->blk[1], c->blk[2], c->blk[3], c->logits, c->probs, c->shared_y, c->sh_gu, c->sh_pair, c->mo,
+                  c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->counts, c->offsets, c->perm, c->hq, c->hd, c->y,
                   c->ncur_all, c->base_all, c->out_all, c->whq, c->whd, c->rcount };
     for (void* p : d) if (p) cudaFree(p);
     for (int p = 0; p < 2; ++p) {
@@ -156,7 +179,7 @@ void fl_free(FLCtx* c) {
         if (c->hw_w[p]) cudaFreeHost(c->hw_w[p]);
         if (c->wev[p]) cudaEventDestroy(c->wev[p]);
     }
-    void* h[] = { c->h_sel, c->h_wts, c->h_ncur, c->h_fi, c->h_h, c->h_moe, c->h_tab, c->h_tabw, c->h_in, c->h_wh, c->h_wmoe, c->h_err };
+    void* h[] = { c->hblk[0], c->hblk[1], c->hblk[2], c->hblk[3], c->h_in, c->h_wh, c->h_wmoe };
     for (void* p : h) if (p) cudaFreeHost(p);
     for (auto& g : c->graphs) if (g.exec) cudaGraphExecDestroy(g.exec);
     cudaEvent_t ev[] = { c->em0, c->em1, c->ep0, c->ep1 };
@@ -249,6 +272,14 @@ static void enqueue_shared(FLCtx* c, const void* g, const void* u, const void* d
     launch_gate_up(e, nt, c->nsm, c->st);
     launch_down(e, nt, c->nsm, c->st);
 }
+// shared_y as fl_moe_prepare leaves it, after an fl_moe_auto that folded the shared expert into its launches
+static void materialize_shared(FLCtx* c) {
+    if (!c->sh_in_y_n) return;
+    FLCK(cudaMemcpyAsync(c->shared_y, c->y + (size_t)c->sh_in_y_n * c->sh_in_y_ke * HIDDEN, (size_t)c->sh_in_y_n * HIDDEN * 4,
+                         cudaMemcpyDeviceToDevice, c->st));
+    c->sh_in_y_n = 0;
+}
+
 static void ensure_shared(FLCtx* c) {
     if (!c->sh_pending) return;
     enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], c->prep_n, c->sh_fmt);
@@ -264,6 +295,7 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     if (host) { std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes); }
     c->prep_n = N;
     c->sh_pending = W->sh_gate && W->sh_up && W->sh_down && wrow < 0;
+    c->sh_in_y_n = 0;                             // this prepare's shared expert supersedes the last one
     c->sh_w[0] = W->sh_gate; c->sh_w[1] = W->sh_up; c->sh_w[2] = W->sh_down; c->sh_fmt = W->sh_fmt == FL_Q5K ? FL_Q5K : 0;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
@@ -273,8 +305,7 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     run_graph(c, key, [&]() {
     FLCK(rec(c->ep0, st));
     if (host) {
-        FLCK(cudaMemcpyAsync(c->ncur, c->h_ncur, bytes, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->ffn_inp, c->h_fi, bytes, cudaMemcpyHostToDevice, st));
+        FLCK(copy_pair(c->ncur, c->h_ncur, (size_t)PREP_ROWS * HIDDEN * 4, bytes, cudaMemcpyHostToDevice, st));
     } else {
         FLCK(cudaMemcpyAsync(c->ncur, ncur, bytes, cudaMemcpyDeviceToDevice, st));
         FLCK(cudaMemcpyAsync(c->ffn_inp, ffn_inp, bytes, cudaMemcpyDeviceToDevice, st));
@@ -309,10 +340,8 @@ void fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
     n = std::min(n, c->prep_n > 0 ? c->prep_n : n);
     cudaStream_t st = c->st;
     if (what & 1) {
-        FLCK(cudaMemcpyAsync(c->h_sel, c->sel, (size_t)n * MAX_TOPK * 4, cudaMemcpyDeviceToHost, st));
-        FLCK(cudaMemcpyAsync(c->h_wts, c->wts, (size_t)n * MAX_TOPK * 4, cudaMemcpyDeviceToHost, st));
-        FLCK(cudaMemcpyAsync(c->h_ncur, c->ncur, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
-        FLCK(cudaMemcpyAsync(c->h_fi, c->ffn_inp, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+        FLCK(copy_pair(c->h_sel, c->sel, (size_t)P8 * 4, (size_t)n * MAX_TOPK * 4, cudaMemcpyDeviceToHost, st));
+        FLCK(copy_pair(c->h_ncur, c->ncur, (size_t)PREP_ROWS * HIDDEN * 4, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
         out->sel = c->h_sel; out->wts = c->h_wts; out->ncur = c->h_ncur; out->fi = c->h_fi;
     }
     if (what & 32) { FLCK(cudaMemcpyAsync(c->h_h, c->h, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st)); out->h = c->h_h; }
@@ -326,15 +355,17 @@ void fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
 // the narrow pass from routing already on the device (c->ids, c->w [n][KE]): slots, experts, combine, and the
 // result copies into the pinned mirrors (h, moe; with ids_back also the routing), then the stream sync
 static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int n, bool ids_back,
-                           bool fold_shared = false) {
+                           bool fold_shared = false, bool slots_ready = false) {
     cudaStream_t st = c->st;
-    const int nt = down_fmt == FL_IQ2 ? nt_for(n) : 1;      // the K-quant down kernel takes single-token slots
-    SlotParams sp{};
-    sp.sel = c->ids; sp.w = c->w; sp.T = n; sp.keep = KE; sp.n_experts = N_EXPERTS; sp.nt = nt; sp.with_shared = fold_shared ? 1 : 0;
-    sp.counts = c->counts; sp.offsets = c->offsets; sp.perm = c->perm;
-    sp.slot_expert = c->s_expert; sp.slot_tok = c->s_tok; sp.slot_out = c->s_out; sp.slot_w = c->s_w; sp.nslots = c->s_n;
-    sp.max_slots = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1); sp.err = c->err;
-    launch_build_slots(sp, st);
+    const int nt = nt_for(n);
+    if (!slots_ready) {                           // slot tables from the device routing (k_fl_keep1 writes them for n == 1)
+        SlotParams sp{};
+        sp.sel = c->ids; sp.w = c->w; sp.T = n; sp.keep = KE; sp.n_experts = N_EXPERTS; sp.nt = nt; sp.with_shared = fold_shared ? 1 : 0;
+        sp.counts = c->counts; sp.offsets = c->offsets; sp.perm = c->perm;
+        sp.slot_expert = c->s_expert; sp.slot_tok = c->s_tok; sp.slot_out = c->s_out; sp.slot_w = c->s_w; sp.nslots = c->s_n;
+        sp.max_slots = max_slots_for(PREP_ROWS, MAX_TOPK, N_EXPERTS, 1, 1); sp.err = c->err;
+        launch_build_slots(sp, st);
+    }
     const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)down_matrix_bytes(down_fmt);
     ExpertParams e = expert_params(c, gate, up, down, sg, sd, c->ncur, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->hq, c->hd, c->y);
     e.down_fmt = down_fmt;
@@ -348,16 +379,13 @@ static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const voi
     cp.shared = fold_shared ? nullptr : c->shared_y;
     cp.h = c->h; cp.moe = c->moe; cp.ld_out = HIDDEN;
     launch_combine(cp, st);
-    if (fold_shared)                              // keep shared_y what fl_moe_prepare would have left
-        FLCK(cudaMemcpyAsync(c->shared_y, c->y + (size_t)n * KE * HIDDEN, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToDevice, st));
-    FLCK(cudaMemcpyAsync(c->h_h, c->h, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
-    FLCK(cudaMemcpyAsync(c->h_moe, c->moe, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
-    if (ids_back) {
-        FLCK(cudaMemcpyAsync(c->h_tab, c->ids, (size_t)n * KE * 4, cudaMemcpyDeviceToHost, st));
-        FLCK(cudaMemcpyAsync(c->h_tabw, c->w, (size_t)n * KE * 4, cudaMemcpyDeviceToHost, st));
-    }
+    // the folded shared rows stay in y until a later call needs shared_y (materialize_shared)
+    FLCK(copy_pair(c->h_h, c->h, (size_t)PREP_ROWS * HIDDEN * 4, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+    if (ids_back)                                 // ids, w and the error word: three rows of one block
+        FLCK(cudaMemcpy2DAsync(c->h_tab, (size_t)NARROW_SLOTS * 4, c->ids, (size_t)NARROW_SLOTS * 4, (size_t)n * KE * 4, 3,
+                               cudaMemcpyDeviceToHost, st));
     FLCK(rec(c->em1, st));
-    queue_err(c);
+    if (!ids_back) queue_err(c);
 }
 
 // after the enqueued narrow pass: wait for it, account its time, read the error word and the routing back
@@ -383,6 +411,7 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     int* hi = c->h_tab; float* hw = c->h_tabw;
     std::memcpy(hi, ids, (size_t)n * KE * 4); std::memcpy(hw, w, (size_t)n * KE * 4);
     c->last_ids.assign(ids, ids + n * KE); c->last_w.assign(w, w + n * KE);
+    materialize_shared(c);
     const bool pend = c->sh_pending;              // the prepare's shared expert, in this call's launches
     const int pn = c->prep_n;
     c->sh_pending = false;
@@ -394,8 +423,7 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     run_graph(c, key, [&]() {
         if (pend) enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], pn, c->sh_fmt);
         FLCK(rec(c->em0, st));
-        FLCK(cudaMemcpyAsync(c->ids, hi, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->w, hw, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));
+        FLCK(copy_pair(c->ids, hi, (size_t)NARROW_SLOTS * 4, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));   // ids, w
         enqueue_narrow(c, gate, up, down, down_fmt, KE, n, false);
     });
     finish_narrow(c, KE, n, false, out);
@@ -406,9 +434,7 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
 // the engine's keep-KE pass (src/server_core_fused.cpp:793-813, without --share-experts) on the device: row i
 // of the router output (sel8 / w8 [n][8], top-8 by score) -> its KE highest-weight experts (equal weights in
 // position order) and, with renorm, their weights scaled to sum to 2.5, in the host pass's float order
-__global__ void k_fl_keep(const int* sel8, const float* w8, int n, int KE, int renorm, int* ids, float* w) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
+__device__ __forceinline__ void keep_row(const int* sel8, const float* w8, int i, int KE, int renorm, int* ids, float* w) {
     float wv[8]; int sv[8], rank[8];
     #pragma unroll
     for (int k = 0; k < 8; ++k) { wv[k] = w8[i * 8 + k]; sv[k] = sel8[i * 8 + k]; }
@@ -439,6 +465,27 @@ __global__ void k_fl_keep(const int* sel8, const float* w8, int n, int KE, int r
     for (int r = 0; r < 8; ++r) if (r < KE) { ids[i * KE + r] = ks[r]; w[i * KE + r] = renorm && sw > 1e-6f ? kw[r] * f : kw[r]; }
 }
 
+__global__ void k_fl_keep(const int* sel8, const float* w8, int n, int KE, int renorm, int* ids, float* w) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) keep_row(sel8, w8, i, KE, renorm, ids, w);
+}
+
+// one row (the decode case): the keep pass and the expert stage's single-token slot tables -- the KE kept
+// experts in rank order, then the folded shared expert -- so no dispatch kernel runs
+struct Keep1Params {
+    const int* sel8; const float* w8; int KE, renorm, fold;
+    int* ids; float* w; int* se; int* stok; int* sout; float* sw; int* sn;
+};
+__global__ void k_fl_keep1(Keep1Params p) {
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x != 0) return;
+    keep_row(p.sel8, p.w8, 0, p.KE, p.renorm, p.ids, p.w);
+    for (int k = 0; k < p.KE; ++k) { p.se[k] = p.ids[k]; p.stok[k] = 0; p.sout[k] = k; p.sw[k] = p.w[k]; }
+    if (p.fold) { p.se[p.KE] = SHARED_SLOT; p.stok[p.KE] = 0; p.sout[p.KE] = p.KE; p.sw[p.KE] = 1.0f; }
+    *p.sn = p.KE + (p.fold ? 1 : 0);
+}
+
 extern "C" {
 
 void fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int renorm, int n, FLOut* out) {
@@ -450,6 +497,7 @@ void fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, i
     cudaStream_t st = c->st;
     // the pending shared expert (IQ2_XXS) joins the routed launches when the downs are IQ2_XXS too; with a
     // K-quant down format, or in the real model's Q5_K / Q6_K formats, it runs on its own first
+    materialize_shared(c);
     const bool fold = c->sh_pending && c->sh_fmt == 0 && down_fmt == FL_IQ2 && n == c->prep_n;
     if (!fold) ensure_shared(c);
     c->sh_pending = false;
@@ -460,9 +508,15 @@ void fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, i
     if (fold) { key.p[3] = c->sh_w[0]; key.p[4] = c->sh_w[1]; key.p[5] = c->sh_w[2]; }
     run_graph(c, key, [&]() {
         FLCK(rec(c->em0, st));
-        k_fl_keep<<<1, 64, 0, st>>>(c->sel, c->wts, n, KE, renorm, c->ids, c->w);
-        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, true, fold);
+        if (n == 1) {
+            const Keep1Params kp{ c->sel, c->wts, KE, renorm, fold ? 1 : 0, c->ids, c->w, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n };
+            FLCK(launch_pdl(k_fl_keep1, dim3(1), dim3(32), 0, st, kp));
+        } else {
+            k_fl_keep<<<1, 64, 0, st>>>(c->sel, c->wts, n, KE, renorm, c->ids, c->w);
+        }
+        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, true, fold, n == 1);
     });
+    if (fold) { c->sh_in_y_n = n; c->sh_in_y_ke = KE; }
     finish_narrow(c, KE, n, true, out);
 }
 
@@ -472,6 +526,7 @@ void fl_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
     if (!c || !out || !mo || n < 1 || n > PREP_ROWS) return;
     std::memset(out, 0, sizeof(FLOut));
     cudaStream_t st = c->st;
+    materialize_shared(c);
     ensure_shared(c);
     std::memcpy(c->h_in, mo, (size_t)n * HIDDEN * 4);
     FLCK(cudaMemcpyAsync(c->mo, c->h_in, (size_t)n * HIDDEN * 4, cudaMemcpyHostToDevice, st));
@@ -524,6 +579,7 @@ void fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, i
     if ((((uintptr_t)gate | (uintptr_t)up | (uintptr_t)down) & 15)) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: arena not 16-byte aligned"); return; }
     par &= 1;
     cudaStream_t st = c->st;
+    materialize_shared(c);
     const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)down_matrix_bytes(down_fmt);
     // slots as given (NB rows each), or, for the K-quant downs, one single-token slot per live row
     const int snt = down_fmt == FL_IQ2 ? NB : 1;
