@@ -414,18 +414,21 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     materialize_shared(c);
     const bool pend = c->sh_pending;              // the prepare's shared expert, in this call's launches
     const int pn = c->prep_n;
+    // as in fl_moe_auto: an IQ2_XXS shared expert over all prepared rows joins the routed launches
+    const bool fold = pend && c->sh_fmt == 0 && down_fmt == FL_IQ2 && n == pn;
     c->sh_pending = false;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
-    key.kind = 2; key.a = n; key.b = KE; key.c = down_fmt; key.d = pend ? pn | (c->sh_fmt << 16) : 0;
+    key.kind = 2; key.a = n; key.b = KE; key.c = down_fmt; key.d = pend ? pn | (c->sh_fmt << 16) | (fold ? 1 << 24 : 0) : 0;
     key.p[0] = gate; key.p[1] = up; key.p[2] = down;
     if (pend) { key.p[3] = c->sh_w[0]; key.p[4] = c->sh_w[1]; key.p[5] = c->sh_w[2]; }
     run_graph(c, key, [&]() {
-        if (pend) enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], pn, c->sh_fmt);
+        if (pend && !fold) enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], pn, c->sh_fmt);
         FLCK(rec(c->em0, st));
         FLCK(copy_pair(c->ids, hi, (size_t)NARROW_SLOTS * 4, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));   // ids, w
-        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, false);
+        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, false, fold);
     });
+    if (fold) { c->sh_in_y_n = n; c->sh_in_y_ke = KE; }
     finish_narrow(c, KE, n, false, out);
 }
 
