@@ -551,7 +551,9 @@ def run_ep_prefill(args, ws, rank, local, dist):
         "metric": "MoE-layer tokens/s (T=%d expert-parallel batch, one layer)" % T, "value": round(value, 1), "unit": "tokens/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)",
+        "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)" if not model_fmt else
+                 "the real model's formats (%s down, %s shared) x q8, int8 dp4a matvecs at every T, fp32 accumulate"
+                 % (args.down_fmt, args.shared_fmt),
         "data": "synthetic: seeded IQ2_XXS experts, router W N(0,0.02), bias N(0,0.01), bf16 N(0,1) hidden states",
         "config": {"workload": "config3_ep_batch_T%d" % T, "global_batch": T, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,
                    "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": NE // ws, "rows_sent": sent,
@@ -681,7 +683,9 @@ def run_prefill(args, ws, rank, local, dist):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     T = args.tokens
-    W = M.LayerWeights(dev, SEED, 0)
+    fmt, DS = DOWN_FMTS[args.down_fmt][0], down_bytes(args)
+    model_fmt = fmt != 4 or args.shared_fmt == "q5k"
+    W = M.LayerWeights(dev, SEED, 0, down_fmt=fmt, sh_fmt=FMT_Q5K if args.shared_fmt == "q5k" else 4)
     g = torch.Generator(device=dev).manual_seed(4321 + rank)
     x = torch.randn(T, HIDDEN, device=dev, generator=g).to(torch.bfloat16).float()
     r = torch.randn(T, HIDDEN, device=dev, generator=g).to(torch.bfloat16).float()
@@ -737,7 +741,7 @@ def run_prefill(args, ws, rank, local, dist):
     # routing statistics of the step (distinct experts, tokens per expert)
     sel = torch.topk(torch.sigmoid(logits) + W.router_bias, 8, dim=1).indices
     distinct = int(torch.unique(sel).numel())
-    gemm_bytes = (distinct + 1) * 3 * MAT                               # routed + shared gate/up/down, each read once
+    gemm_bytes = distinct * (2 * MAT + DS) + shared_bytes(args)         # routed + shared gate/up/down, each read once
     layer_bytes = gemm_bytes + ROUTER_BYTES + T * HIDDEN * 4 * 4
     flops = 2.0 * T * (args.keep + 1) * 3 * HIDDEN * INTER + 2.0 * T * HIDDEN * NE
     g_ms = float(np.median(gemm_ms))
@@ -745,9 +749,12 @@ def run_prefill(args, ws, rank, local, dist):
         "metric": "MoE-layer tokens/s (T=512 prefill, one layer)", "value": round(value, 1), "unit": "tokens/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)",
+        "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)" if not model_fmt else
+                 "the real model's formats (%s down, %s shared) x q8, int8 dp4a matvecs at every T, fp32 accumulate"
+                 % (args.down_fmt, args.shared_fmt),
         "data": "synthetic: seeded IQ2_XXS experts, uniform-random router logits U(-1,1), bf16 N(0,1) hidden states",
-        "config": {"workload": "config2_prefill_T%d" % T, "global_batch": T * ws, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,
+        "config": {"workload": "config2_prefill_T%d" % T + ("" if not model_fmt else "_%s_down_%s_shared" % (args.down_fmt, args.shared_fmt)),
+                   "global_batch": T * ws, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,
                    "keep": args.keep, "distinct_experts": distinct, "parallelism": "replicas" if ws > 1 else "single",
                    "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (gemm_bytes / 1e9)},
         "layer": {"bytes": layer_bytes, "flops": flops, "achieved_gbs": round(layer_bytes / (ms_max / args.steps / 1e3) / 1e9, 1),

@@ -67,7 +67,9 @@ def build(force=False, verbose=False, ptxas_verbose=False):
             if r.returncode != 0:
                 raise RuntimeError("nvcc failed on %s" % src)
     if force or _stale(LIB, objs):
-        cmd = [nv, "-ccbin", host_cxx()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda", "-ldl"]
+        cuda_lib = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "lib64")
+        cmd = [nv, "-ccbin", host_cxx()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda", "-ldl", "-lcublas",
+                                                                                "-Xlinker", "-rpath=" + cuda_lib]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)

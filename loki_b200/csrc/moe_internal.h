@@ -98,6 +98,18 @@ struct SharedKqParams {
 };
 void launch_shared_kq(const SharedKqParams& p, int grid, cudaStream_t st);
 
+// the same shared expert for many tokens as dense GEMMs: its three matrices dequantised to fp16 (w16:
+// [gate 2048 | up 2048][7168] then down [7168][2048]), x rows to fp16 (x16 [n][7168]), gate/up = cuBLAS fp16
+// GEMM with fp32 accumulation into gu, SwiGLU in fp32 rounded to fp16 (h16 [n][2048]), the down GEMM into y
+// rows row0 + j.  blas: a cublasHandle_t with its workspace set.  Returns a cublasStatus_t.
+struct SharedGemmParams {
+    const uint8_t* gate; const uint8_t* up; const uint8_t* down;
+    const float* x; int ld_x; int t0, n, row0;
+    __half* w16; __half* x16; __half* h16; float* gu; float* y;
+    void* blas;
+};
+int launch_shared_gemm(const SharedGemmParams& p, cudaStream_t st);
+
 // ---- combine: h = resid + shared + sum_k y[t*keep+k], moe = sum_k y[t*keep+k]
 //      (shared = the y rows T*keep + t when with_shared, and/or the separate `shared` rows)
 struct CombineParams {

@@ -178,6 +178,10 @@ class MoeLayer:
         """Below the GEMM threshold, use the register-fed mma.sync path for calls with >= min_tokens tokens."""
         self._check(lib().lk_moe_set_mma_threshold(self.ctx, min_tokens))
 
+    def set_shared_gemm_threshold(self, min_tokens):
+        """Run a Q5_K/Q6_K shared expert as dense fp16 GEMMs for calls with >= min_tokens tokens (default 16)."""
+        self._check(lib().lk_moe_set_shared_gemm_threshold(self.ctx, min_tokens))
+
     def device_error(self, stream=None):
         """Synchronise and return the device error status (0 = none); raises on a recorded error."""
         return self._check(lib().lk_moe_get_error(self.ctx, _stream(stream)))

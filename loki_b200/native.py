@@ -68,6 +68,7 @@ SIGNATURES = {
     "lk_moe_set_events": (_I, [_P, _P]),
     "lk_moe_set_gemm_threshold": (_I, [_P, _I]),
     "lk_moe_set_mma_threshold": (_I, [_P, _I]),
+    "lk_moe_set_shared_gemm_threshold": (_I, [_P, _I]),
     "lk_moe_get_error": (_I, [_P, _P]),
     "lk_moe_strerror": (ctypes.c_char_p, [_I]),
     "lk_moe_last_error": (ctypes.c_char_p, [_P]),

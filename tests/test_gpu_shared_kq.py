@@ -39,9 +39,20 @@ def small_layer(request, native):
     torch.cuda.empty_cache()
 
 
+def _shared_float_ref(oracle, W, x):
+    """The shared expert on fp32 x with the gguf-py-pinned dequantised weights, in float64 (the dense path's
+    reference: no q8 of x or of the SwiGLU output)."""
+    G = oracle.kq_dequant(FMT_Q5K, W.expert_bytes(W.n_experts, 0)).reshape(INTER, HIDDEN).astype(np.float64)
+    U = oracle.kq_dequant(FMT_Q5K, W.expert_bytes(W.n_experts, 1)).reshape(INTER, HIDDEN).astype(np.float64)
+    D = oracle.kq_dequant(FMT_Q6K, W.expert_bytes(W.n_experts, 2)).reshape(HIDDEN, INTER).astype(np.float64)
+    g, u = x.astype(np.float64) @ G.T, x.astype(np.float64) @ U.T
+    return ((g / (1.0 + np.exp(-g))) * u) @ D.T
+
+
 @pytest.mark.parametrize("T,keep", [(1, 8), (1, 2), (3, 4), (8, 8), (20, 3)])
 def test_shared_model_fmt_experts(native, oracle, small_layer, T, keep):
-    """lk_moe_experts with the routed experts in the single-token regime and the Q5_K/Q6_K shared expert."""
+    """lk_moe_experts with the routed experts in the single-token regime and the Q5_K/Q6_K shared expert on
+    its per-token q8 kernels (the dense path held off)."""
     from loki_b200 import moe as M
     fmt, W = small_layer
     rng = np.random.default_rng(T * 13 + keep + fmt)
@@ -50,6 +61,7 @@ def test_shared_model_fmt_experts(native, oracle, small_layer, T, keep):
     x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
     r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
     layer = M.MoeLayer(0, keep=keep, max_tokens=T)
+    layer.set_shared_gemm_threshold(1 << 20)
     h, mo = layer.experts(W, _dev(x), _dev(r), _dev(sel), _dev(w))
     layer.device_error()
     tok = list(range(T)) if T <= 8 else [0, 7, T - 1]
@@ -85,9 +97,36 @@ def test_shared_model_fmt_tensor_core_regimes(native, oracle, small_layer, T, re
     tok = [0, 1, T // 2, T - 1]
     ref = oracle_layer(oracle, SEED, 23, x, r, sel, w, tokens=tok, hq8=False, sh_fmt=FMT_Q5K)
     hn, mn = h.cpu().numpy()[tok], mo.cpu().numpy()[tok]
-    e_moe, e_h = rel_l2(mn, ref["moe"]), rel_l2(hn, ref["h"])
-    e_sh = rel_l2(hn - mn - r[tok], ref["h"] - ref["moe"] - r[tok])
-    assert e_moe < RTOL_L2 and e_h < RTOL_L2 and e_sh < RTOL_L2, (e_moe, e_h, e_sh)
+    e_moe = rel_l2(mn, ref["moe"])
+    # the shared expert took the dense fp16 path (>= 16 tokens): against the float restatement
+    e_sh = rel_l2(hn - mn - r[tok], _shared_float_ref(oracle, W, x[tok]))
+    assert e_moe < RTOL_L2 and e_sh < RTOL_L2, (e_moe, e_sh)
+
+
+@pytest.mark.parametrize("T", [16, 40])
+def test_shared_model_fmt_dense_path(native, oracle, small_layer, T):
+    """Calls of >= 16 tokens: the Q5_K/Q6_K shared expert dequantised to fp16 once and run as two cuBLAS GEMMs
+    (fp32 accumulation), the routed experts on their usual regime; twice, the second call reusing the buffers."""
+    from loki_b200 import moe as M
+    fmt, W = small_layer
+    keep = 2
+    rng = np.random.default_rng(T * 3 + fmt)
+    sel = np.stack([rng.choice(10, keep, replace=False) for _ in range(T)]).astype(np.int32)
+    w = rng.uniform(0.05, 1.0, (T, keep)).astype(np.float32)
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    layer = M.MoeLayer(0, keep=keep, max_tokens=T)
+    layer.set_mma_threshold(1 << 20)
+    for _ in range(2):
+        h, mo = layer.experts(W, _dev(x), _dev(r), _dev(sel), _dev(w))
+        layer.device_error()
+    tok = [0, T // 3, T - 1]
+    ref = oracle_layer(oracle, SEED, 23, x, r, sel, w, tokens=tok, down_fmt=fmt, sh_fmt=FMT_Q5K)
+    hn, mn = h.cpu().numpy()[tok], mo.cpu().numpy()[tok]
+    e_moe = rel_l2(mn, ref["moe"])
+    e_sh = rel_l2(hn - mn - r[tok], _shared_float_ref(oracle, W, x[tok]))
+    e_q8 = rel_l2(hn - mn - r[tok], ref["h"] - ref["moe"] - r[tok])       # against the q8 numerics, for scale
+    assert e_moe < RTOL_L2 and e_sh < RTOL_L2, (e_moe, e_sh, e_q8)
 
 
 def test_shared_model_fmt_forward_T1(native, oracle):
