@@ -73,7 +73,8 @@ __device__ __forceinline__ float q8_group_row(const float* row, int g, uint32_t 
 }
 
 // one row's sub-block s (0..7) of the block at shared address bb: the partial dot product with this thread's
-// 32 q8 activations (xr, their sum xs, scale dx)
+// 32 q8 activations (xr, their sum xs, scale dx).  Per 4 weights: the qs nibbles shifted down, qh bit s
+// rotated into bit 4 of each byte (one funnel shift), the two merged by one LOP3; then dp4a.
 __device__ __forceinline__ float q5k_dot(uint32_t bb, int s, const uint32_t (&xr)[8], int xs, float dx) {
     const uint4 hdr = lds_v4(bb);                    // d | dmin, scales[0..3], scales[4..7], scales[8..11]
     const uint4 h0 = lds_v4(bb + Q5K_QH), h1 = lds_v4(bb + Q5K_QH + 16);
@@ -81,20 +82,20 @@ __device__ __forceinline__ float q5k_dot(uint32_t bb, int s, const uint32_t (&xr
     const uint4 q0 = lds_v4(qo), q1 = lds_v4(qo + 16);
     const uint32_t qs[8] = { q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w };
     const uint32_t qh[8] = { h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w };
-    const int nsh = 4 * (s & 1);
+    const uint32_t nsh = 4u * (uint32_t)(s & 1), rot = (uint32_t)(4 - s) & 31u;
     int isum = 0;
     #pragma unroll
     for (int w = 0; w < 8; ++w) {
-        const uint32_t q5 = ((qs[w] >> nsh) & 0x0F0F0F0Fu) | (((qh[w] >> s) & 0x01010101u) << 4);
+        const uint32_t hi = __funnelshift_l(qh[w], qh[w], rot) & 0x10101010u;
+        const uint32_t q5 = ((qs[w] >> nsh) & 0x0F0F0F0Fu) | hi;
         isum = __dp4a((int)q5, (int)xr[w], isum);
     }
-    const int k8 = 8 * (s & 3);
-    const uint32_t A = (hdr.y >> k8) & 0xFFu, B = (hdr.z >> k8) & 0xFFu, C = (hdr.w >> k8) & 0xFFu;
-    const uint32_t sc = s < 4 ? (A & 63u) : ((C & 15u) | ((A >> 6) << 4));
-    const uint32_t mn = s < 4 ? (B & 63u) : ((C >> 4) | ((B >> 6) << 4));
-    const float d = __half2float(__ushort_as_half((uint16_t)(hdr.x & 0xFFFFu)));
-    const float dmin = __half2float(__ushort_as_half((uint16_t)(hdr.x >> 16)));
-    return dx * fmaf(d * (float)sc, (float)isum, -(dmin * (float)mn) * (float)xs);
+    const uint32_t selk = 0x4440u | (uint32_t)(s & 3);     // byte s & 3 of a word, zero-extended
+    const uint32_t A = __byte_perm(hdr.y, 0u, selk), B = __byte_perm(hdr.z, 0u, selk), C = __byte_perm(hdr.w, 0u, selk);
+    const uint32_t sc = s < 4 ? (A & 63u) : ((C & 15u) | ((A >> 2) & 48u));
+    const uint32_t mn = s < 4 ? (B & 63u) : ((C >> 4) | ((B >> 2) & 48u));
+    const float2 dd = __half22float2(*reinterpret_cast<const __half2*>(&hdr.x));   // (d, dmin)
+    return dx * fmaf(dd.x * (float)sc, (float)isum, -(dd.y * (float)mn) * (float)xs);
 }
 
 __global__ void __launch_bounds__(S5_THREADS, 1) k_sh_gate_up_q5k(SharedKqParams p) {
