@@ -1,0 +1,97 @@
+// ref_harness.cu -- TEST INFRASTRUCTURE, not product.  Builds the reference's own MoE code
+// (src/fused_layer.cu of the reference checkout, included from where it lies by `make -C oracle ref`; nothing
+// of it is copied here) into oracle/_ref/libref_moe.so with the reference's own flags (nvcc -O3 -arch=sm_89,
+// build.bat:13; the sm_89 PTX is JIT-compiled for the B200), and exposes entry points that run ITS kernels:
+//   refh_router  router_probs + router_topk as attn_block launches them (fused_layer.cu:506)
+//   refh_moe     the shared expert as fl_attn runs it (quant_x, Q5_K gate/up, swiglu_q8, Q6_K down;
+//                fused_layer.cu:521-524), then the narrow MoE pass fl_moe (:599-612) with its combine
+// The GPU tests compare these with the CPU oracle: they pin the oracle's routing and layer arithmetic
+// against the reference itself.  Every call is synchronous; inputs and outputs are host arrays.
+#include "fused_layer.cu"
+
+namespace {
+
+FLCtx* g_ctx = nullptr;
+FLCtx* ref_ctx() {
+    if (!g_ctx) g_ctx = fl_init(64, 64);          // attention-side sizes kept small: only the MoE buffers are used
+    return g_ctx;
+}
+
+// device copy of a host array, with 4 KB of zeroed slack after it (no read of the reference's staging loops
+// can leave the allocation)
+template <class T> T* upload(const void* host, size_t bytes) {
+    T* d = nullptr;
+    CK(cudaMalloc((void**)&d, bytes + 4096));
+    CK(cudaMemset(d, 0, bytes + 4096));
+    if (bytes) CK(cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice));
+    return d;
+}
+
+}  // namespace
+
+extern "C" {
+
+// x [n][7168] fp32, gate_inp [256][7168] fp32 (f16 = 0) or fp16 (f16 = 1), bias [256] -> probs [n][256],
+// sel [n][8], wts [n][8]; n <= 64
+int refh_router(const float* x, int n, const void* gate_inp, int f16, const float* bias, float* probs, int* sel, float* wts) {
+    if (n < 1 || n > RMAX) return 1;
+    FLCtx* c = ref_ctx();
+    cudaStream_t st = c->st;
+    float* xd = upload<float>(x, (size_t)n * E * 4);
+    void* wd = upload<uint8_t>(gate_inp, (size_t)256 * E * (f16 ? 2 : 4));
+    float* bd = upload<float>(bias, 256 * 4);
+    float *pd = nullptr, *wtd = nullptr; int* sd = nullptr;
+    CK(cudaMalloc((void**)&pd, (size_t)n * 256 * 4)); CK(cudaMalloc((void**)&sd, (size_t)n * 8 * 4)); CK(cudaMalloc((void**)&wtd, (size_t)n * 8 * 4));
+    router_probs<<<blocks_for((size_t)n * 256 * 32), 256, 0, st>>>(xd, wd, f16, pd, n);
+    router_topk<<<n, 256, 0, st>>>(pd, bd, sd, wtd);
+    CK(cudaStreamSynchronize(st));
+    CK(cudaMemcpy(probs, pd, (size_t)n * 256 * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(sel, sd, (size_t)n * 8 * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(wts, wtd, (size_t)n * 8 * 4, cudaMemcpyDeviceToHost));
+    void* fr[] = { xd, wd, bd, pd, sd, wtd };
+    for (void* p : fr) cudaFree(p);
+    return 0;
+}
+
+// One narrow MoE pass of n <= 8 rows through the reference: x (ncur) and resid (ffn_inp) [n][7168]; arenas
+// of nexp experts (gate/up IQ2_XXS, down Q2_K (down_fmt 5) or Q3_K (6)), slot ids / weights [n][KE];
+// optional shared expert (Q5_K gate, Q5_K up, Q6_K down; all three null = none) -> h, moe [n][7168]
+int refh_moe(const float* x, const float* resid, int n, const uint8_t* gate, const uint8_t* up, const uint8_t* down, int nexp,
+             int down_fmt, const int* ids, const float* w, int KE, const uint8_t* sh_gate, const uint8_t* sh_up,
+             const uint8_t* sh_down, float* h, float* moe) {
+    if (n < 1 || n > NB || nexp < 1 || KE < 1 || KE > 8 || (down_fmt != FL_Q2K && down_fmt != FL_Q3K)) return 1;
+    FLCtx* c = ref_ctx();
+    cudaStream_t st = c->st;
+    const size_t wsg = (size_t)HSH * (E / QK) * BLK_IQ2;
+    const size_t wsd = (size_t)E * (HSH / QK) * (down_fmt == FL_Q3K ? BLK_Q3 : BLK_Q2);
+    uint8_t* gd = upload<uint8_t>(gate, nexp * wsg);
+    uint8_t* ud = upload<uint8_t>(up, nexp * wsg);
+    uint8_t* dd = upload<uint8_t>(down, nexp * wsd);
+    CK(cudaMemset(c->ncur, 0, (size_t)NB * E * 4));
+    CK(cudaMemset(c->ffn_inp, 0, (size_t)NB * E * 4));
+    CK(cudaMemcpy(c->ncur, x, (size_t)n * E * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->ffn_inp, resid, (size_t)n * E * 4, cudaMemcpyHostToDevice));
+    uint8_t *sg = nullptr, *su = nullptr, *sdn = nullptr;
+    if (sh_gate && sh_up && sh_down) {            // fl_attn's shared expert on ncur, one row-block (G = 1, R = NB)
+        sg = upload<uint8_t>(sh_gate, (size_t)HSH * (E / QK) * BLK_Q5);
+        su = upload<uint8_t>(sh_up, (size_t)HSH * (E / QK) * BLK_Q5);
+        sdn = upload<uint8_t>(sh_down, (size_t)E * (HSH / QK) * BLK_Q6);
+        const int G = 1;
+        quant_x<<<blocks_for((size_t)NB * (E / 32)), 256, 0, st>>>(c->ncur, E, G, E, NB * E, c->xcur);
+        mvg(c, F_Q5K, sg, 0, HSH, E, 1, c->xcur, 7, c->partS, G);
+        mvg(c, F_Q5K, su, 0, HSH, E, 1, c->xcur, 7, c->partS + (size_t)7 * NB * HSH, G);
+        swiglu_q8<<<blocks_for((size_t)NB * (HSH / 32)), 256, 0, st>>>(c->partS, c->partS + (size_t)7 * NB * HSH, 7, G, HSH, c->xh);
+        mvg(c, F_Q6K, sdn, 0, E, HSH, 1, c->xh, 2, c->partSD, G);
+    } else {
+        CK(cudaMemsetAsync(c->partSD, 0, (size_t)2 * NB * E * 4, st));
+    }
+    FLOut out;
+    fl_moe(c, gd, ud, dd, nexp, down_fmt, ids, w, KE, n, &out);
+    std::memcpy(h, out.h, (size_t)n * E * 4);
+    std::memcpy(moe, out.moe, (size_t)n * E * 4);
+    void* fr[] = { gd, ud, dd, sg, su, sdn };
+    for (void* p : fr) if (p) cudaFree(p);
+    return 0;
+}
+
+}  // extern "C"

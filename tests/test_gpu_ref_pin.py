@@ -1,0 +1,95 @@
+"""The CPU oracle pinned against the reference's OWN kernels on the GPU.
+
+oracle/_ref/libref_moe.so is src/fused_layer.cu of the reference, built from its sources with its own flags
+(nvcc -O3 -arch=sm_89; `make -C oracle ref`, oracle/ref_harness.cu) and JIT-compiled for the B200.  It runs the
+reference's router (router_probs / router_topk, fused_layer.cu:314-332), its shared expert as fl_attn runs it
+(Q5_K gate/up, swiglu_q8, Q6_K down; :521-524) and its narrow MoE pass fl_moe (IQ2_XXS gate/up, Q2_K / Q3_K
+down, moe_combine; :599-612).  The oracle must agree with it, and so must this library's GPU path."""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from moe_helpers import SEED, HIDDEN, INTER, MAT, RTOL_L2, rel_l2, FMT_Q5K, FMT_Q6K
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+REF_LIB = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref", "libref_moe.so")
+P = ctypes.c_void_p
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not os.path.exists(REF_LIB):
+        pytest.skip("oracle/_ref/libref_moe.so not built (make -C oracle ref needs the reference checkout)")
+    L = ctypes.CDLL(REF_LIB)
+    L.refh_router.argtypes = [P, ctypes.c_int, P, ctypes.c_int, P, P, P, P]
+    L.refh_moe.argtypes = [P, P, ctypes.c_int, P, P, P, ctypes.c_int, ctypes.c_int, P, P, ctypes.c_int, P, P, P, P, P]
+    return L
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(P)
+
+
+@pytest.mark.parametrize("f16", [False, True])
+def test_router_matches_reference_kernels(native, oracle, ref, f16):
+    rng = np.random.default_rng(501 + f16)
+    T = 6
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    W = (rng.standard_normal((256, HIDDEN)) * 0.02).astype(np.float32)
+    if f16:
+        W = W.astype(np.float16)
+    bias = (rng.standard_normal(256) * 0.01).astype(np.float32)
+    probs, sel, wts = np.empty((T, 256), np.float32), np.empty((T, 8), np.int32), np.empty((T, 8), np.float32)
+    assert ref.refh_router(_p(x), T, _p(np.ascontiguousarray(W)), int(f16), _p(bias), _p(probs), _p(sel), _p(wts)) == 0
+    op, osel, ow = oracle.router(x, W.astype(np.float32), bias, oracle.route_cfg(8, 8))
+    np.testing.assert_allclose(probs, op, rtol=2e-6, atol=1e-7)
+    np.testing.assert_array_equal(sel, osel)
+    np.testing.assert_allclose(wts, ow, rtol=2e-6)
+
+
+def _arena(oracle, down_fmt, NE):
+    gate = np.concatenate([oracle.gen_iq2(SEED, 14, 0, e, INTER, HIDDEN) for e in range(NE)])
+    up = np.concatenate([oracle.gen_iq2(SEED, 14, 1, e, INTER, HIDDEN) for e in range(NE)])
+    down = np.concatenate([oracle.gen_kq(down_fmt, SEED, 14, 2, e, HIDDEN, INTER) for e in range(NE)])
+    sh = (oracle.gen_kq(FMT_Q5K, SEED, 14, 0, 256, INTER, HIDDEN), oracle.gen_kq(FMT_Q5K, SEED, 14, 1, 256, INTER, HIDDEN),
+          oracle.gen_kq(FMT_Q6K, SEED, 14, 2, 256, HIDDEN, INTER))
+    return gate, up, down, sh
+
+
+@pytest.mark.parametrize("down_fmt,n,KE,shared", [(5, 1, 4, True), (6, 3, 4, True), (5, 8, 2, False), (6, 2, 6, False)])
+def test_moe_layer_matches_reference_kernels(native, oracle, ref, down_fmt, n, KE, shared):
+    """fl_moe of the reference (with fl_attn's Q5_K/Q6_K shared expert) vs the oracle and vs this library."""
+    from loki_b200 import moe as M
+    NE = 6
+    gate, up, down, sh = _arena(oracle, down_fmt, NE)
+    DS = HIDDEN * 8 * oracle.BLOCK_BYTES[down_fmt]
+    rng = np.random.default_rng(100 * down_fmt + n)
+    x = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    ids = np.stack([rng.choice(NE, KE, replace=False) for _ in range(n)]).astype(np.int32)
+    w = rng.uniform(0.1, 1.0, (n, KE)).astype(np.float32)
+    h_ref, moe_ref = np.empty((n, HIDDEN), np.float32), np.empty((n, HIDDEN), np.float32)
+    shp = sh if shared else (None, None, None)
+    assert ref.refh_moe(_p(x), _p(r), n, _p(gate), _p(up), _p(down), NE, down_fmt, _p(ids), _p(w), KE,
+                        _p(shp[0]), _p(shp[1]), _p(shp[2]), _p(h_ref), _p(moe_ref)) == 0
+    # the oracle (the reference's q8 scheme and per-sub-block integer sums)
+    o = oracle.moe_layer(x, r, gate, up, down, MAT, ids, w, *shp, down_fmt=down_fmt, down_stride=DS,
+                         sh_gu_fmt=FMT_Q5K, sh_down_fmt=FMT_Q6K)
+    e_moe, e_h = rel_l2(o["moe"], moe_ref), rel_l2(o["h"], h_ref)
+    e_sh = rel_l2(o["h"] - o["moe"] - r, h_ref - moe_ref - r) if shared else 0.0
+    print("oracle vs reference kernels: moe %.2e  h %.2e  shared %.2e" % (e_moe, e_h, e_sh))
+    assert e_moe < 1e-4 and e_h < 1e-4 and e_sh < 1e-4, (e_moe, e_h, e_sh)
+    # this library's expert stage on the same arenas
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    g_d, u_d, d_d = dev(gate), dev(up), dev(down)
+    s_d = [dev(m) for m in sh] if shared else [None, None, None]
+    ws = native.LkMoeWeights(g_d.data_ptr(), u_d.data_ptr(), d_d.data_ptr(), MAT, MAT, DS, down_fmt,
+                             *(m.data_ptr() if m is not None else None for m in s_d), None, 0, None, FMT_Q5K if shared else 0)
+    layer = M.MoeLayer(0, topk=KE, keep=KE, max_tokens=n, n_experts=NE, with_shared=shared)
+    h, mo = layer.experts(ws, dev(x), dev(r), dev(ids), dev(w))
+    layer.device_error()
+    assert rel_l2(mo.cpu().numpy(), moe_ref) < RTOL_L2 and rel_l2(h.cpu().numpy(), h_ref) < RTOL_L2
