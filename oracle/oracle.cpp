@@ -16,8 +16,16 @@
 //   K-quant downs ......... src/fused_layer.cu:203-227 (Q2_K: per 16 weights fa*dx*isum - dmin*m*s16),
 //                           :228-254 (Q3_K: fa = d*(scale-32), q = low2 - 4 where the high bit is clear);
 //                           block decode cross-checked against gguf-py 0.19.0 Q2_K / Q3_K dequantize
+//   shared expert ......... src/fused_layer.cu:521-524 with tc_matvec's Q5_K (:102-130, per 32 weights
+//                           fa*dx*isum - dmin*m*sx) and Q6_K (:131-158, per 16 weights) arithmetic; block
+//                           decode cross-checked against gguf-py 0.19.0 Q5_K / Q6_K dequantize
 //   combine ............... src/fused_layer.cu:366-373 and 354-360 (routed = sum_k w_k y_k; h = routed +
 //                           shared + ffn_inp; moe = routed)
+//
+// Pinned against the reference's own kernels: oracle/_ref/libref_moe.so (src/fused_layer.cu built from its
+// sources by `make ref`) runs the router, the Q5_K/Q6_K shared expert and fl_moe on the GPU, and
+// tests/test_gpu_ref_pin.py holds this file's router (ids equal, weights within 2e-6) and layer outputs
+// (within 1e-4 relative L2; measured ~2.3e-7) to them.
 //   permute ............... src/server_core_fused.cpp:937 (byexp: per expert, (row, k) pairs in row-major
 //                           order) -- the per-expert token lists, stable by (token, k)
 //
