@@ -7,6 +7,7 @@
 //                fused_layer.cu:521-524), then the narrow MoE pass fl_moe (:599-612) with its combine
 // The GPU tests compare these with the CPU oracle: they pin the oracle's routing and layer arithmetic
 // against the reference itself.  Every call is synchronous; inputs and outputs are host arrays.
+#include <chrono>
 #include "fused_layer.cu"
 
 namespace {
@@ -91,6 +92,65 @@ int refh_moe(const float* x, const float* resid, int n, const uint8_t* gate, con
     std::memcpy(moe, out.moe, (size_t)n * E * 4);
     void* fr[] = { gd, ud, dd, sg, su, sdn };
     for (void* p : fr) if (p) cudaFree(p);
+    return 0;
+}
+
+// Device time of the reference on one decode layer's MoE work, per call, over `iters` calls after 3 warm-up
+// calls, with every input resident: the shared expert as fl_attn launches it (events around its four
+// launches) and fl_moe (its own em0/em1 events, fl_gpu_ms(c, 1)).  Before each call `flush` (device,
+// flush_bytes) is overwritten so no weight is served from L2.  Returns 0; *moe_us / *shared_us / *wall_us
+// receive the mean per call (wall: fl_moe's host call, which includes its synchronisation).
+int refh_bench(const float* x, const float* resid, int n, const uint8_t* gate, const uint8_t* up, const uint8_t* down, int nexp,
+               int down_fmt, const int* ids, const float* w, int KE, const uint8_t* sh_gate, const uint8_t* sh_up,
+               const uint8_t* sh_down, void* flush, size_t flush_bytes, int iters, double* moe_us, double* shared_us, double* wall_us) {
+    if (n < 1 || n > NB || nexp < 1 || KE < 1 || KE > 8 || iters < 1 || (down_fmt != FL_Q2K && down_fmt != FL_Q3K)) return 1;
+    FLCtx* c = ref_ctx();
+    cudaStream_t st = c->st;
+    const size_t wsg = (size_t)HSH * (E / QK) * BLK_IQ2;
+    const size_t wsd = (size_t)E * (HSH / QK) * (down_fmt == FL_Q3K ? BLK_Q3 : BLK_Q2);
+    uint8_t* gd = upload<uint8_t>(gate, nexp * wsg);
+    uint8_t* ud = upload<uint8_t>(up, nexp * wsg);
+    uint8_t* dd = upload<uint8_t>(down, nexp * wsd);
+    uint8_t* sg = upload<uint8_t>(sh_gate, (size_t)HSH * (E / QK) * BLK_Q5);
+    uint8_t* su = upload<uint8_t>(sh_up, (size_t)HSH * (E / QK) * BLK_Q5);
+    uint8_t* sdn = upload<uint8_t>(sh_down, (size_t)E * (HSH / QK) * BLK_Q6);
+    CK(cudaMemset(c->ncur, 0, (size_t)NB * E * 4));
+    CK(cudaMemset(c->ffn_inp, 0, (size_t)NB * E * 4));
+    CK(cudaMemcpy(c->ncur, x, (size_t)n * E * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->ffn_inp, resid, (size_t)n * E * 4, cudaMemcpyHostToDevice));
+    cudaEvent_t s0, s1;
+    CK(cudaEventCreate(&s0)); CK(cudaEventCreate(&s1));
+    double sh_ms = 0.0, wall = 0.0;
+    const double moe0 = c->ms_moe;
+    FLOut out;
+    for (int it = -3; it < iters; ++it) {
+        if (it == 0) { sh_ms = 0.0; wall = 0.0; }
+        const double m_before = c->ms_moe;
+        if (flush) CK(cudaMemsetAsync(flush, it & 0xFF, flush_bytes, st));
+        CK(cudaEventRecord(s0, st));
+        const int G = 1;
+        quant_x<<<blocks_for((size_t)NB * (E / 32)), 256, 0, st>>>(c->ncur, E, G, E, NB * E, c->xcur);
+        mvg(c, F_Q5K, sg, 0, HSH, E, 1, c->xcur, 7, c->partS, G);
+        mvg(c, F_Q5K, su, 0, HSH, E, 1, c->xcur, 7, c->partS + (size_t)7 * NB * HSH, G);
+        swiglu_q8<<<blocks_for((size_t)NB * (HSH / 32)), 256, 0, st>>>(c->partS, c->partS + (size_t)7 * NB * HSH, 7, G, HSH, c->xh);
+        mvg(c, F_Q6K, sdn, 0, E, HSH, 1, c->xh, 2, c->partSD, G);
+        CK(cudaEventRecord(s1, st));
+        if (flush) CK(cudaMemsetAsync(flush, (it + 1) & 0xFF, flush_bytes, st));
+        const auto t0 = std::chrono::steady_clock::now();
+        fl_moe(c, gd, ud, dd, nexp, down_fmt, ids, w, KE, n, &out);
+        const auto t1 = std::chrono::steady_clock::now();
+        float ms = 0.f;
+        CK(cudaEventElapsedTime(&ms, s0, s1));
+        if (it >= 0) { sh_ms += ms; wall += std::chrono::duration<double, std::micro>(t1 - t0).count(); }
+        if (it < 0) c->ms_moe = m_before;         // warm-up calls do not count
+        (void)moe0;
+    }
+    *moe_us = (c->ms_moe - moe0) * 1e3 / iters;
+    *shared_us = sh_ms * 1e3 / iters;
+    *wall_us = wall / iters;
+    CK(cudaEventDestroy(s0)); CK(cudaEventDestroy(s1));
+    void* fr[] = { gd, ud, dd, sg, su, sdn };
+    for (void* p : fr) cudaFree(p);
     return 0;
 }
 

@@ -93,3 +93,48 @@ def test_moe_layer_matches_reference_kernels(native, oracle, ref, down_fmt, n, K
     h, mo = layer.experts(ws, dev(x), dev(r), dev(ids), dev(w))
     layer.device_error()
     assert rel_l2(mo.cpu().numpy(), moe_ref) < RTOL_L2 and rel_l2(h.cpu().numpy(), h_ref) < RTOL_L2
+
+
+def test_reference_kernels_timing(native, oracle, ref):
+    """Timing beside the pin: the reference's own kernels (fl_attn's shared expert + fl_moe) and this library's
+    expert stage on the same decode-layer work -- the real model's formats (IQ2_XXS gate/up, Q2_K downs,
+    Q5_K/Q6_K shared expert), one row, 8 experts -- with every input resident and L2 overwritten (256 MB)
+    before each call.  Device time per call from CUDA events on each side; printed, not asserted."""
+    from loki_b200 import moe as M
+    NE, KE, n, iters = 8, 8, 1, 20
+    gate, up, down, sh = _arena(oracle, 5, NE)
+    DS = HIDDEN * 8 * 84
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    ids = np.arange(KE, dtype=np.int32).reshape(1, KE)
+    w = rng.uniform(0.1, 1.0, (1, KE)).astype(np.float32)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    moe_us, sh_us, wall_us = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+    assert ref.refh_bench(_p(x), _p(r), n, _p(gate), _p(up), _p(down), NE, 5, _p(ids), _p(w), KE, _p(sh[0]), _p(sh[1]), _p(sh[2]),
+                          P(flush.data_ptr()), ctypes.c_size_t(flush.numel()), iters, ctypes.byref(moe_us), ctypes.byref(sh_us),
+                          ctypes.byref(wall_us)) == 0
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    g_d, u_d, d_d = dev(gate), dev(up), dev(down)
+    s_d = [dev(m) for m in sh]
+    ws = native.LkMoeWeights(g_d.data_ptr(), u_d.data_ptr(), d_d.data_ptr(), MAT, MAT, DS, 5, *(m.data_ptr() for m in s_d),
+                             None, 0, None, FMT_Q5K)
+    layer = M.MoeLayer(0, topk=KE, keep=KE, max_tokens=n, n_experts=NE)
+    xd, rd, idd, wd = dev(x), dev(r), dev(ids), dev(w)
+    h = torch.empty(n, HIDDEN, device="cuda")
+    mo = torch.empty(n, HIDDEN, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for it in range(3 + iters):
+        flush.fill_(it & 0xFF)
+        e0.record()
+        layer.experts(ws, xd, rd, idd, wd, h=h, moe=mo)
+        e1.record()
+        torch.cuda.synchronize()
+        if it >= 3:
+            times.append(e0.elapsed_time(e1) * 1e3)
+    layer.device_error()
+    ours = float(np.mean(times))
+    refs = moe_us.value + sh_us.value
+    print("reference kernels on B200: fl_moe %.1f us + shared expert %.1f us = %.1f us (fl_moe wall %.1f us); "
+          "this library: %.1f us (%.2fx)" % (moe_us.value, sh_us.value, refs, wall_us.value, ours, refs / ours))
