@@ -5,6 +5,8 @@
 //   refh_router  router_probs + router_topk as attn_block launches them (fused_layer.cu:506)
 //   refh_moe     the shared expert as fl_attn runs it (quant_x, Q5_K gate/up, swiglu_q8, Q6_K down;
 //                fused_layer.cu:521-524), then the narrow MoE pass fl_moe (:599-612) with its combine
+//   refh_ctx / refh_wide_rows   the context and the rows fl_attn leaves for the exported wide pass
+//   refh_bench   the device time of the first two, for the timing beside the pin
 // The GPU tests compare these with the CPU oracle: they pin the oracle's routing and layer arithmetic
 // against the reference itself.  Every call is synchronous; inputs and outputs are host arrays.
 #include <chrono>
@@ -92,6 +94,20 @@ int refh_moe(const float* x, const float* resid, int n, const uint8_t* gate, con
     std::memcpy(moe, out.moe, (size_t)n * E * 4);
     void* fr[] = { gd, ud, dd, sg, su, sdn };
     for (void* p : fr) if (p) cudaFree(p);
+    return 0;
+}
+
+// The reference's context, for driving its exported wide pass (fl_wide_init / fl_wide_moe / fl_wide_mark /
+// fl_wide_wait / fl_wide_finish, fused_layer.cu:528-561) the way the engine does (engine:930-950)
+void* refh_ctx() { return ref_ctx(); }
+
+// What fl_attn(wrow = 0) leaves for a wide pass of n rows without a shared expert: ncur_all = x and
+// base_all = resid (fused_layer.cu:525, base_rows with zero shared partials).  Call after fl_wide_init.
+int refh_wide_rows(const float* x, const float* resid, int n) {
+    FLCtx* c = ref_ctx();
+    if (!c->ncur_all || n < 1 || n > c->wmax) return 1;
+    CK(cudaMemcpy(c->ncur_all, x, (size_t)n * E * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->base_all, resid, (size_t)n * E * 4, cudaMemcpyHostToDevice));
     return 0;
 }
 

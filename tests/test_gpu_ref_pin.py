@@ -138,3 +138,123 @@ def test_reference_kernels_timing(native, oracle, ref):
     refs = moe_us.value + sh_us.value
     print("reference kernels on B200: fl_moe %.1f us + shared expert %.1f us = %.1f us (fl_moe wall %.1f us); "
           "this library: %.1f us (%.2fx)" % (moe_us.value, sh_us.value, refs, wall_us.value, ours, refs / ours))
+
+
+def _wide_lib(ref, native):
+    ref.refh_ctx.restype = P
+    ref.refh_wide_rows.argtypes = [P, P, ctypes.c_int]
+    ref.fl_wide_init.argtypes = [P, ctypes.c_int, ctypes.c_int]
+    ref.fl_wide_moe.argtypes = [P, P, P, P, ctypes.c_int, ctypes.c_int, P, P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    ref.fl_wide_mark.argtypes = [P, ctypes.c_int]
+    ref.fl_wide_wait.argtypes = [P, ctypes.c_int]
+    ref.fl_wide_finish.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(native.FLOut)]
+    return ref.refh_ctx()
+
+
+def _run_reference_wide(ref, native, c, gate, up, down, down_fmt, nexp, ids, w, KE, n, eb):
+    """The engine's wide-pass driver (src/server_core_fused.cpp:930-950) over the reference's exported calls."""
+    from loki_b200 import fused as F
+    used = sorted(set(int(e) for e in ids.reshape(-1)))
+    plan = []
+    for batch, midx, rows, kidx, wk in F.wide_slots(ids, w, KE, used, eb=eb):
+        plan.append((np.array([batch[u] for u in midx], np.int32), np.array(rows, np.int32), np.array(kidx, np.int32),
+                     np.array(wk, np.float32)))
+    for i, (gm, rows, kidx, wk) in enumerate(plan):
+        par = i & 1
+        if i >= 2:
+            ref.fl_wide_wait(c, par)
+        ref.fl_wide_moe(c, P(gate), P(up), P(down), down_fmt, nexp, _p(gm), _p(rows), _p(kidx), _p(wk), len(gm), KE, par)
+        ref.fl_wide_mark(c, par)
+    out = native.FLOut()
+    ref.fl_wide_finish(c, n, KE, ctypes.byref(out))
+    h = np.ctypeslib.as_array(ctypes.cast(out.h, ctypes.POINTER(ctypes.c_float)), (n * HIDDEN,)).reshape(n, HIDDEN).copy()
+    moe = np.ctypeslib.as_array(ctypes.cast(out.moe, ctypes.POINTER(ctypes.c_float)), (n * HIDDEN,)).reshape(n, HIDDEN).copy()
+    return h, moe
+
+
+@pytest.mark.parametrize("down_fmt,n,KE", [(5, 20, 4), (6, 13, 3)])
+def test_wide_pass_matches_reference_kernels(native, oracle, ref, down_fmt, n, KE):
+    """The reference's wide (prefill) pass -- slots of <= 8 (row, k) pairs per expert, arena batches of <= 4
+    experts, double-buffered parities, wide_finish -- against the oracle and this library."""
+    from loki_b200 import moe as M
+    NE = 12
+    gate, up, down, _ = _arena(oracle, down_fmt, NE)
+    DS = HIDDEN * 8 * oracle.BLOCK_BYTES[down_fmt]
+    rng = np.random.default_rng(900 + n)
+    x = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    ids = np.stack([rng.choice(NE, KE, replace=False) for _ in range(n)]).astype(np.int32)
+    w = rng.uniform(0.1, 1.0, (n, KE)).astype(np.float32)
+    c = _wide_lib(ref, native)
+    assert ref.fl_wide_init(c, 64, KE) == 1
+    assert ref.refh_wide_rows(_p(x), _p(r), n) == 0
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    g_d, u_d, d_d = dev(gate), dev(up), dev(down)
+    h_ref, moe_ref = _run_reference_wide(ref, native, c, g_d.data_ptr(), u_d.data_ptr(), d_d.data_ptr(), down_fmt, NE, ids, w, KE, n, 4)
+    o = oracle.moe_layer(x, r, gate, up, down, MAT, ids, w, down_fmt=down_fmt, down_stride=DS)
+    e_moe, e_h = rel_l2(o["moe"], moe_ref), rel_l2(o["h"], h_ref)
+    print("oracle vs reference wide pass: moe %.2e  h %.2e" % (e_moe, e_h))
+    assert e_moe < 1e-4 and e_h < 1e-4, (e_moe, e_h)
+    ws = native.LkMoeWeights(g_d.data_ptr(), u_d.data_ptr(), d_d.data_ptr(), MAT, MAT, DS, down_fmt, None, None, None, None, 0, None, 0)
+    layer = M.MoeLayer(0, topk=KE, keep=KE, max_tokens=n, n_experts=NE, with_shared=False)
+    h, mo = layer.experts(ws, dev(x), dev(r), dev(ids), dev(w))
+    layer.device_error()
+    assert rel_l2(mo.cpu().numpy(), moe_ref) < RTOL_L2 and rel_l2(h.cpu().numpy(), h_ref) < RTOL_L2
+
+
+def test_reference_wide_pass_timing(native, oracle, ref):
+    """Timing beside the pin, prefill: the reference's wide pass (the engine's driver over fl_wide_moe, arena
+    batches of 16 experts) and this library's expert stage, T=512 rows, top-8 of 256 experts, Q2_K downs (the
+    reference's wide pass takes only K-quant downs), no shared expert; host wall time of one pass each."""
+    import time
+    from loki_b200 import fused as F
+    from loki_b200 import moe as M
+    T, KE = 512, 8
+    W = M.LayerWeights("cuda", SEED, 40, down_fmt=5, with_shared=False)
+    rng = np.random.default_rng(512)
+    x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((T, HIDDEN)).astype(np.float32)
+    ids = np.argsort(-rng.uniform(-1, 1, (T, 256)), axis=1)[:, :KE].astype(np.int32)
+    w = rng.uniform(0.1, 1.0, (T, KE)).astype(np.float32)
+    c = _wide_lib(ref, native)
+    assert ref.fl_wide_init(c, T, KE) == 1
+    assert ref.refh_wide_rows(_p(x), _p(r), T) == 0
+    used = sorted(set(int(e) for e in ids.reshape(-1)))
+    plan = [(np.array([b[u] for u in mi], np.int32), np.array(ro, np.int32), np.array(ki, np.int32), np.array(wk, np.float32))
+            for b, mi, ro, ki, wk in F.wide_slots(ids, w, KE, used, eb=16)]
+    out = native.FLOut()
+
+    def ref_pass():
+        for i, (gm, rows, kidx, wk) in enumerate(plan):
+            par = i & 1
+            if i >= 2:
+                ref.fl_wide_wait(c, par)
+            ref.fl_wide_moe(c, P(W.gate), P(W.up), P(W.down), 5, 256, _p(gm), _p(rows), _p(kidx), _p(wk), len(gm), KE, par)
+            ref.fl_wide_mark(c, par)
+        ref.fl_wide_finish(c, T, KE, ctypes.byref(out))
+
+    layer = M.MoeLayer(0, keep=KE, max_tokens=T, with_shared=False)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    xd, rd, idd, wd = dev(x), dev(r), dev(ids), dev(w)
+    h = torch.empty(T, HIDDEN, device="cuda")
+    mo = torch.empty(T, HIDDEN, device="cuda")
+
+    def our_pass():
+        layer.experts(W, xd, rd, idd, wd, h=h, moe=mo)
+        torch.cuda.synchronize()
+
+    res = {}
+    for name, fn in (("reference", ref_pass), ("ours", our_pass)):
+        fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        res[name] = (time.perf_counter() - t0) / 3 * 1e3
+    layer.device_error()
+    h_ref = np.ctypeslib.as_array(ctypes.cast(out.h, ctypes.POINTER(ctypes.c_float)), (T * HIDDEN,)).reshape(T, HIDDEN)
+    err = rel_l2(h.cpu().numpy(), h_ref)
+    print("wide pass T=512, Q2_K downs: reference %.2f ms, this library %.2f ms (%.2fx), h rel L2 %.1e"
+          % (res["reference"], res["ours"], res["reference"] / res["ours"], err))
+    assert err < RTOL_L2
