@@ -314,7 +314,12 @@ static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int 
     m.slot_expert = c->m_expert; m.slot_tok = c->m_tok; m.slot_out = c->m_out; m.slot_w = c->m_w; m.nslots = c->m_n;
     m.max_slots = c->m_max; m.slot_cnt = c->m_cnt; m.xh = c->xh; m.hb = c->hb; m.y = c->y; m.err = c->err;
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
-    launch_slot_mma(m, c->nsm, st);
+    if (W->down_fmt == LK_FMT_IQ2) {
+        launch_slot_mma(m, c->nsm, st);
+    } else {                                          // K-quant downs: IQ2_XXS gate/up phase, then the K-quant mma down
+        launch_slot_mma_gate_up(m, c->nsm, st);
+        launch_kq_mma_down(m, W->down_fmt, c->nsm, st);
+    }
     if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
     if (h || moe) {
         CombineParams cp{};
@@ -329,8 +334,9 @@ static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int 
 
 // the expert stage for routing (sel, w) [T][keep], by token count: single-token dp4a matvecs (the slot
 // tables of T == 1 may already have been written by the router: slots_ready), the register-fed mma.sync
-// path, or the tcgen05 GEMMs.  K-quant (Q2_K / Q3_K) downs take the dp4a matvecs at every T: their down
-// kernel consumes the q8 SwiGLU output, the reference's numerics for those formats.
+// path, or the tcgen05 GEMMs.  K-quant (Q2_K / Q3_K) downs take the dp4a matvecs below the mma threshold
+// (q8 SwiGLU output, the reference's numerics) and the mma.sync path (IQ2_XXS gate/up, then kq_mma.cu's
+// down, fp16 h) from there at every larger T.
 static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
                      const float* w, int keep, float* h, float* moe, bool slots_ready, cudaStream_t st) {
     const bool iq2_down = W->down_fmt == LK_FMT_IQ2;
@@ -362,7 +368,7 @@ static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_
         }
     }
     if (iq2_down && T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
-    if (iq2_down && T >= c->mma_min_tokens) return run_mma_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
+    if (T >= c->mma_min_tokens) return run_mma_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
     if (!slots_ready) {
         SlotParams s{};
         s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = slot_nt(T);

@@ -153,6 +153,9 @@ struct MmaParams {
     int* err;
 };
 void launch_slot_mma(const MmaParams& p, int nsm, cudaStream_t st);
+// the gate/up phase alone (SwiGLU output as fp16 rows hb), then the Q2_K / Q3_K down on mma.sync (kq_mma.cu)
+void launch_slot_mma_gate_up(const MmaParams& p, int nsm, cudaStream_t st);
+void launch_kq_mma_down(const MmaParams& p, int down_fmt, int nsm, cudaStream_t st);
 
 // ---- seeded IQ2_XXS weight generation (moe_format.h generator) for n_experts consecutive experts
 void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,

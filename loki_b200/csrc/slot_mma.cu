@@ -318,10 +318,14 @@ template <bool DOWN> static void mm_launch(const MmaParams& p, int grid, cudaStr
     k_slot_mma<DOWN><<<grid, MM_THREADS, MM_SMEM, st>>>(p);
 }
 
-void launch_slot_mma(const MmaParams& p, int nsm, cudaStream_t st) {
+void launch_slot_mma_gate_up(const MmaParams& p, int nsm, cudaStream_t st) {
     const int n = p.T * (HIDDEN / 32) > p.max_slots ? p.T * (HIDDEN / 32) : p.max_slots;
     k_mma_prep<<<(n + 255) / 256, 256, 0, st>>>(p);
     mm_launch<false>(p, 2 * nsm, st);
+}
+
+void launch_slot_mma(const MmaParams& p, int nsm, cudaStream_t st) {
+    launch_slot_mma_gate_up(p, nsm, st);
     mm_launch<true>(p, 2 * nsm, st);
 }
 

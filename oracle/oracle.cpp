@@ -430,6 +430,23 @@ static void kq_matvec_multi(int fmt, const uint8_t* W, int rows, int K, const in
     }
 }
 
+// y = W . h for a K-quant matrix and `ntok` unquantised activation rows: every row dequantised as gguf-py
+// does (orc_kq_dequant), the dot products in double.  The reference for the kernels that keep the SwiGLU
+// output at 16-bit precision (the mma.sync K-quant down).
+static void kq_matvec_float_multi(int fmt, const uint8_t* W, int rows, int K, const float* const* h, int ntok, float* const* y) {
+    const int NB = K / QK, nb = fmt_block_bytes(fmt);
+    #pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) {
+        std::vector<float> wr((size_t)K);
+        for (int b = 0; b < NB; ++b) orc_kq_dequant(fmt, W + ((size_t)r * NB + b) * nb, 1, wr.data() + (size_t)b * QK);
+        for (int t = 0; t < ntok; ++t) {
+            double acc = 0.0;
+            for (int k = 0; k < K; ++k) acc += (double)wr[k] * (double)h[t][k];
+            y[t][r] = (float)acc;
+        }
+    }
+}
+
 // one activation row through a K-quant matrix (tests)
 void orc_kq_matvec(int fmt, const uint8_t* W, int rows, int K, const int8_t* xq, const float* xd, float* y) {
     kq_matvec_multi(fmt, W, rows, K, &xq, &xd, 1, &y);
@@ -452,14 +469,14 @@ struct OrcLayerW {
 // hq8 = 1: the SwiGLU output is re-quantised to q8 per 32 before the down projection (the reference's
 // swiglu_q8, src/fused_layer.cu:334-341: the decode and narrow paths); hq8 = 0: it enters the down
 // projection unquantised (the tensor-core prefill path).
-// down_fmt: format of every routed down matrix (FMT_IQ2, FMT_Q2K or FMT_Q3K; the K-quants need hq8 = 1,
-// the reference's narrow and wide passes).  The shared expert's gate/up are in sh_gu_fmt (FMT_IQ2, or the
+// down_fmt: format of every routed down matrix (FMT_IQ2, FMT_Q2K or FMT_Q3K; with hq8 = 1 the K-quants use
+// the reference's per-16 q8 arithmetic, with hq8 = 0 the unquantised h against the dequantised rows).  The shared expert's gate/up are in sh_gu_fmt (FMT_IQ2, or the
 // real model's FMT_Q5K) and its down in sh_down_fmt (down_fmt, or FMT_Q6K); its SwiGLU output is always
 // re-quantised to q8 when either is a K-quant (the reference's shared path, fused_layer.cu:521-524).
 int orc_moe_layer_fmt2(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
                        int KE, float* h, float* moe, float* y_slot, float* shared_out, int hq8, int down_fmt,
                        int sh_gu_fmt, int sh_down_fmt) {
-    if (down_fmt != FMT_IQ2 && (!hq8 || (down_fmt != FMT_Q2K && down_fmt != FMT_Q3K))) return 1;
+    if (down_fmt != FMT_IQ2 && down_fmt != FMT_Q2K && down_fmt != FMT_Q3K) return 1;
     if ((sh_gu_fmt != FMT_IQ2 && sh_gu_fmt != FMT_Q5K) || (sh_down_fmt != down_fmt && sh_down_fmt != FMT_Q6K)) return 1;
     const int E = HIDDEN, H = MOE_INTER;
     // q8 of every token's x
@@ -494,7 +511,8 @@ int orc_moe_layer_fmt2(const float* x, const float* resid, int T, const OrcLayer
             hqp[i] = hq.data() + (size_t)s * H; hdp[i] = hd.data() + (size_t)s * H / 32; yp[i] = ytmp[i].data();
             hfp[i] = hf[i].data();
         }
-        if (down_fmt != FMT_IQ2) kq_matvec_multi(down_fmt, Wl->down + m * Wl->down_stride, E, H, hqp.data(), hdp.data(), n, yp.data());
+        if (down_fmt != FMT_IQ2 && hq8) kq_matvec_multi(down_fmt, Wl->down + m * Wl->down_stride, E, H, hqp.data(), hdp.data(), n, yp.data());
+        else if (down_fmt != FMT_IQ2) kq_matvec_float_multi(down_fmt, Wl->down + m * Wl->down_stride, E, H, hfp.data(), n, yp.data());
         else if (hq8) iq2_matvec_multi(Wl->down + m * Wl->down_stride, E, H, hqp.data(), hdp.data(), n, yp.data());
         else iq2_matvec_float_multi(Wl->down + m * Wl->down_stride, E, H, hfp.data(), n, yp.data());
         for (int i = 0; i < n; ++i) {
@@ -526,7 +544,9 @@ int orc_moe_layer_fmt2(const float* x, const float* resid, int T, const OrcLayer
             orc_quant_q8(hv, H, shq.data() + (size_t)t * H, shd.data() + (size_t)t * H / 32);
             hqp[t] = shq.data() + (size_t)t * H; hdp[t] = shd.data() + (size_t)t * H / 32; hfp[t] = hv;
         }
-        if (sh_down_fmt != FMT_IQ2) kq_matvec_multi(sh_down_fmt, Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
+        if (sh_down_fmt != FMT_IQ2 && (hq8 || sh_gu_fmt != FMT_IQ2))
+            kq_matvec_multi(sh_down_fmt, Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
+        else if (sh_down_fmt != FMT_IQ2) kq_matvec_float_multi(sh_down_fmt, Wl->sh_down, E, H, hfp.data(), T, shp.data());
         else if (hq8 || sh_gu_fmt != FMT_IQ2) iq2_matvec_multi(Wl->sh_down, E, H, hqp.data(), hdp.data(), T, shp.data());
         else iq2_matvec_float_multi(Wl->sh_down, E, H, hfp.data(), T, shp.data());
     }

@@ -254,7 +254,16 @@ def test_reference_wide_pass_timing(native, oracle, ref):
         res[name] = (time.perf_counter() - t0) / 3 * 1e3
     layer.device_error()
     h_ref = np.ctypeslib.as_array(ctypes.cast(out.h, ctypes.POINTER(ctypes.c_float)), (T * HIDDEN,)).reshape(T, HIDDEN)
-    err = rel_l2(h.cpu().numpy(), h_ref)
-    print("wide pass T=512, Q2_K downs: reference %.2f ms, this library %.2f ms (%.2fx), h rel L2 %.1e"
-          % (res["reference"], res["ours"], res["reference"] / res["ours"], err))
-    assert err < RTOL_L2
+    hn = h.cpu().numpy()
+    err = rel_l2(hn, h_ref)
+    # this library at T=512 keeps h at fp16 (the mma.sync K-quant down); the reference re-quantises it to q8.
+    # Each side against the oracle of its own numerics, on sampled rows:
+    from moe_helpers import oracle_layer
+    tok = [0, 1, 255, 511]
+    o16 = oracle_layer(oracle, SEED, 40, x, r, ids, w, with_shared=False, tokens=tok, hq8=False, down_fmt=5)
+    o8 = oracle_layer(oracle, SEED, 40, x, r, ids, w, with_shared=False, tokens=tok, hq8=True, down_fmt=5)
+    e_ours, e_ref = rel_l2(hn[tok], o16["h"]), rel_l2(h_ref[tok], o8["h"])
+    print("wide pass T=512, Q2_K downs: reference %.2f ms, this library %.2f ms (%.2fx); vs own-numerics oracle: "
+          "ours %.1e, reference %.1e; ours vs reference %.1e"
+          % (res["reference"], res["ours"], res["reference"] / res["ours"], e_ours, e_ref, err))
+    assert e_ours < RTOL_L2 and e_ref < 1e-4
