@@ -1,5 +1,6 @@
 // kq_mma.cu -- the K-quant (Q2_K / Q3_K) down projection for batches, on mma.sync: the real model's routed
-// downs at T >= the mma threshold, after the register-fed IQ2_XXS gate/up phase of slot_mma.cu.
+// downs at T >= the mma threshold, after an IQ2_XXS gate/up phase that writes fp16 SwiGLU rows -- the
+// register-fed one of slot_mma.cu, or from the GEMM threshold the tcgen05 one of prefill_gemm.cu.
 //
 // The single-token dp4a kernel (expert_kq.cu) decodes a down matrix once per (token, expert) entry; at T=512
 // that makes the layer instruction-bound.  Here one warp owns 16 weight rows of one slot's expert (<= MM_NT =
@@ -84,7 +85,9 @@ __global__ void __launch_bounds__(KM_WARPS * 32) k_kq_mma_down(MmaParams p) {
     const int nitems = *p.nslots * KM_ITEMS_PER_SLOT;
     for (int item = blockIdx.x * KM_WARPS + warp; item < nitems; item += gridDim.x * KM_WARPS) {
         const int s = item / KM_ITEMS_PER_SLOT, rb = item % KM_ITEMS_PER_SLOT;
-        const int cnt = p.slot_cnt[s];
+        int cnt = 0;                                  // the slot's tokens (counted here when no pre-pass ran)
+        if (p.slot_cnt) cnt = p.slot_cnt[s];
+        else while (cnt < MM_NT && p.slot_tok[s * MM_NT + cnt] >= 0) ++cnt;
         if (cnt <= 0) continue;
         const int e = p.slot_expert[s];
         const uint8_t* W = (e == SHARED_SLOT ? p.sh_down : p.down + (size_t)e * p.down_stride) + (size_t)rb * 16 * ROWB;

@@ -284,7 +284,23 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int
     g.slot_expert = c->g_expert; g.slot_tok = c->g_tok; g.slot_out = c->g_out; g.slot_w = c->g_w; g.nslots = c->g_n;
     g.max_slots = c->g_max; g.slot_cnt = c->g_cnt; g.bt = c->bt; g.ht = c->ht; g.y = c->y; g.err = c->err;
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
-    launch_prefill_gemm(g, c->nsm, st);
+    if (W->down_fmt == LK_FMT_IQ2) {
+        launch_prefill_gemm(g, c->nsm, st);
+    } else {   // K-quant downs: the tcgen05 gate/up GEMM writes fp16 SwiGLU rows, the mma.sync K-quant down reads them
+        g.hb = c->hb;
+        launch_prefill_gemm_gate_up(g, c->nsm, st);
+        SlotParams ms{};
+        ms.sel = sel; ms.w = w; ms.T = T; ms.keep = keep; ms.n_experts = c->cfg.n_experts; ms.nt = MM_NT; ms.with_shared = c->rs;
+        ms.counts = c->counts; ms.offsets = c->offsets; ms.perm = c->perm;
+        ms.slot_expert = c->m_expert; ms.slot_tok = c->m_tok; ms.slot_out = c->m_out; ms.slot_w = c->m_w; ms.nslots = c->m_n;
+        ms.max_slots = c->m_max; ms.err = c->err; ms.sh_t0 = c->sh_t0; ms.sh_n = c->sh_n;
+        launch_build_slots(ms, st);
+        MmaParams m{};
+        m.down = (const uint8_t*)W->down; m.down_stride = W->down_stride; m.sh_down = (const uint8_t*)W->sh_down;
+        m.T = T; m.slot_expert = c->m_expert; m.slot_tok = c->m_tok; m.slot_out = c->m_out; m.slot_w = c->m_w; m.nslots = c->m_n;
+        m.max_slots = c->m_max; m.slot_cnt = nullptr; m.hb = c->hb; m.y = c->y; m.err = c->err;
+        launch_kq_mma_down(m, W->down_fmt, c->nsm, st);
+    }
     if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
     if (h || moe) {
             CombineParams cp{};
@@ -335,8 +351,8 @@ static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int 
 // the expert stage for routing (sel, w) [T][keep], by token count: single-token dp4a matvecs (the slot
 // tables of T == 1 may already have been written by the router: slots_ready), the register-fed mma.sync
 // path, or the tcgen05 GEMMs.  K-quant (Q2_K / Q3_K) downs take the dp4a matvecs below the mma threshold
-// (q8 SwiGLU output, the reference's numerics) and the mma.sync path (IQ2_XXS gate/up, then kq_mma.cu's
-// down, fp16 h) from there at every larger T.
+// (q8 SwiGLU output, the reference's numerics); above it their gate/up is the mma.sync or (from the GEMM
+// threshold) tcgen05 IQ2_XXS phase writing fp16 SwiGLU rows, and their down kq_mma.cu's mma.sync kernel.
 static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
                      const float* w, int keep, float* h, float* moe, bool slots_ready, cudaStream_t st) {
     const bool iq2_down = W->down_fmt == LK_FMT_IQ2;
@@ -367,7 +383,7 @@ static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_
             return LK_OK;
         }
     }
-    if (iq2_down && T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
+    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
     if (T >= c->mma_min_tokens) return run_mma_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
     if (!slots_ready) {
         SlotParams s{};

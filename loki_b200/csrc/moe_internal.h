@@ -134,8 +134,11 @@ struct GemmParams {
     __half* ht;                                       // down B tiles (SwiGLU output) [max_slots][MOE_INTER/64][64x64]
     float* y;                                         // [rows][HIDDEN] weighted expert outputs
     int* err;
+    __half* hb;                                       // optional: the SwiGLU output as fp16 rows [entry][MOE_INTER]
+                                                      //   instead of the down B tiles (launch_prefill_gemm_gate_up)
 };
 void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st);
+void launch_prefill_gemm_gate_up(const GemmParams& p, int grid, cudaStream_t st);   // the gate/up GEMM alone
 size_t gemm_tile_halfs(int max_slots, bool down);     // size of bt (down = false) / ht (down = true)
 
 // ---- register-fed mma.sync grouped products (mid-size T): slots of up to MM_NT tokens

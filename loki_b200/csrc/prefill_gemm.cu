@@ -369,7 +369,13 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
                         } else {                          // h = silu(g)*u -> the down GEMM's B tile of this slot
                             const int hj = rt * PG_M + row;
                             __half* tile = p.ht + ((size_t)s * (MOE_INTER / PG_KB) + hj / PG_KB) * (PG_B_TILE / 2);
-                            *(__half*)((uint8_t*)tile + btile_off(n, hj % PG_KB, n16)) = __float2half_rn(lk_swiglu(v0[j], v1[j]));
+                            const __half hv = __float2half_rn(lk_swiglu(v0[j], v1[j]));
+                            if (p.hb) {                   // fp16 rows for a down kernel of its own (K-quant downs)
+                                const int out = p.slot_out[s * PG_NMAX + n];
+                                if (out >= 0) p.hb[(size_t)out * MOE_INTER + hj] = hv;
+                            } else {
+                                *(__half*)((uint8_t*)tile + btile_off(n, hj % PG_KB, n16)) = hv;
+                            }
                         }
                     }
                 }
@@ -427,9 +433,13 @@ template <bool DOWN> static void pg_launch(const GemmParams& p, int grid, cudaSt
     k_prefill_gemm<DOWN><<<grid, PG_THREADS, PG_SMEM, st>>>(p);
 }
 
-void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st) {
+void launch_prefill_gemm_gate_up(const GemmParams& p, int grid, cudaStream_t st) {
     k_gate_b_tiles<<<dim3(p.max_slots, HIDDEN / PG_KB), PG_BT_THREADS, 0, st>>>(p);
     pg_launch<false>(p, grid, st);
+}
+
+void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st) {
+    launch_prefill_gemm_gate_up(p, grid, st);
     pg_launch<true>(p, grid, st);
 }
 
