@@ -47,8 +47,10 @@ struct FLCtx {
     float* h_moe = nullptr; int* h_tab = nullptr; float* h_tabw = nullptr; float* h_in = nullptr;
     // wide pass
     int wmax = 0, wke = 0;
-    float* ncur_all = nullptr; float* base_all = nullptr; float* out_all = nullptr; int8_t* whq = nullptr; float* whd = nullptr;
-    int *w_expert[2] = {}, *w_tok[2] = {}, *w_out[2] = {}, *w_n[2] = {}; float* w_w[2] = {};
+    float* ncur_all = nullptr; float* base_all = nullptr; float* out_all = nullptr;
+    __half* wxh = nullptr; __half* whb = nullptr;   // the pass's rows and SwiGLU outputs in fp16 (mma.sync path)
+    int wxh_rows = 0;                               // rows of ncur_all already converted into wxh for this pass
+    int *w_expert[2] = {}, *w_tok[2] = {}, *w_out[2] = {}, *w_n[2] = {}, *w_cnt[2] = {}; float* w_w[2] = {};
     int* hw_tab[2] = {}; float* hw_w[2] = {};
     float* h_wh = nullptr; float* h_wmoe = nullptr;
     cudaEvent_t wev[2] = {}, em0 = nullptr, em1 = nullptr, ep0 = nullptr, ep1 = nullptr;
@@ -170,10 +172,10 @@ void fl_free(FLCtx* c) {
     if (c->st) cudaStreamSynchronize(c->st);
     void* d[] = { c->blk[0], c->blk[1], c->blk[2], c->blk[3], c->logits, c->probs, c->shared_y, c->sh_gu, c->sh_pair, c->mo,
                   c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->counts, c->offsets, c->perm, c->hq, c->hd, c->y,
-                  c->ncur_all, c->base_all, c->out_all, c->whq, c->whd, c->rcount };
+                  c->ncur_all, c->base_all, c->out_all, c->wxh, c->whb, c->rcount };
     for (void* p : d) if (p) cudaFree(p);
     for (int p = 0; p < 2; ++p) {
-        void* dd[] = { c->w_expert[p], c->w_tok[p], c->w_out[p], c->w_n[p], c->w_w[p] };
+        void* dd[] = { c->w_expert[p], c->w_tok[p], c->w_out[p], c->w_n[p], c->w_cnt[p], c->w_w[p] };
         for (void* q : dd) if (q) cudaFree(q);
         if (c->hw_tab[p]) cudaFreeHost(c->hw_tab[p]);
         if (c->hw_w[p]) cudaFreeHost(c->hw_w[p]);
@@ -296,6 +298,7 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     c->prep_n = N;
     c->sh_pending = W->sh_gate && W->sh_up && W->sh_down && wrow < 0;
     c->sh_in_y_n = 0;                             // this prepare's shared expert supersedes the last one
+    if (wrow >= 0) c->wxh_rows = 0;               // rows of a wide pass change: their fp16 copy is redone
     c->sh_w[0] = W->sh_gate; c->sh_w[1] = W->sh_up; c->sh_w[2] = W->sh_down; c->sh_fmt = W->sh_fmt == FL_Q5K ? FL_Q5K : 0;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
@@ -561,13 +564,15 @@ int fl_wide_init(FLCtx* c, int wmax, int KE) {
     c->wmax = wmax; c->wke = KE;
     const size_t R = (size_t)wmax * HIDDEN;
     const size_t ent = (size_t)wmax * KE;
-    if (dz(&c->ncur_all, R) || dz(&c->base_all, R) || dz(&c->out_all, ent * HIDDEN) || dz(&c->whq, ent * MOE_INTER) ||
-        dz(&c->whd, ent * (MOE_INTER / 32)) || hz(&c->h_wh, R) || hz(&c->h_wmoe, R)) { fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0; }
+    if (dz(&c->ncur_all, R) || dz(&c->base_all, R) || dz(&c->out_all, ent * HIDDEN) || dz(&c->wxh, R) ||
+        dz(&c->whb, ent * MOE_INTER) || hz(&c->h_wh, R) || hz(&c->h_wmoe, R)) { fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0; }
+    c->wxh_rows = 0;
     for (int p = 0; p < 2; ++p) {
-        // room for WIDE_SLOTS x NB single-token slots (the K-quant downs split every wide slot into its rows)
-        if (dz(&c->w_expert[p], WIDE_SLOTS * NB) || dz(&c->w_tok[p], WIDE_SLOTS * NB) || dz(&c->w_out[p], WIDE_SLOTS * NB) ||
-            dz(&c->w_w[p], WIDE_SLOTS * NB) || dz(&c->w_n[p], 1) || hz(&c->hw_tab[p], 3 * WIDE_SLOTS * NB + 1) ||
-            hz(&c->hw_w[p], WIDE_SLOTS * NB) || cudaEventCreateWithFlags(&c->wev[p], cudaEventDisableTiming)) {
+        // room for WIDE_SLOTS slots of MM_NT tokens (the mma.sync path's layout)
+        const int e = WIDE_SLOTS * MM_NT;
+        if (dz(&c->w_expert[p], WIDE_SLOTS) || dz(&c->w_tok[p], e) || dz(&c->w_out[p], e) || dz(&c->w_w[p], e) ||
+            dz(&c->w_n[p], 1) || dz(&c->w_cnt[p], WIDE_SLOTS) || hz(&c->hw_tab[p], WIDE_SLOTS + 2 * e + 1) ||
+            hz(&c->hw_w[p], e) || cudaEventCreateWithFlags(&c->wev[p], cudaEventDisableTiming)) {
             fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0;
         }
     }
@@ -584,37 +589,58 @@ void fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, i
     cudaStream_t st = c->st;
     materialize_shared(c);
     const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)down_matrix_bytes(down_fmt);
-    // slots as given (NB rows each), or, for the K-quant downs, one single-token slot per live row
-    const int snt = down_fmt == FL_IQ2 ? NB : 1;
+    // The engine's slots (<= NB (row, k) pairs of one expert each) merged, consecutive same-expert slots
+    // together, into the mma.sync path's slots of up to MM_NT tokens: IQ2_XXS gate/up decoded once per slot
+    // (slot_mma.cu), then the IQ2_XXS or K-quant (kq_mma.cu) down; h stays fp16.
     for (int s0 = 0; s0 < nslots; s0 += WIDE_SLOTS) {
         const int ns = std::min(WIDE_SLOTS, nslots - s0);
         if (s0 > 0) FLCK(cudaStreamSynchronize(st));          // the tables of this parity are reused
-        int* he = c->hw_tab[par]; int* ht = he + WIDE_SLOTS * NB; int* ho = ht + WIDE_SLOTS * NB; float* hw = c->hw_w[par];
-        int nout = 0;                                          // slots written
+        int* he = c->hw_tab[par]; int* ht = he + WIDE_SLOTS; int* ho = ht + WIDE_SLOTS * MM_NT; float* hw = c->hw_w[par];
+        int nout = 0, fill = 0, cur = -1, maxr = -1;
         for (int s = 0; s < ns; ++s) {
             const int m = midx[s0 + s];
             if (m < 0 || m >= nexp) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: slot expert out of range"); return; }
-            if (snt == NB) he[nout] = m;
+            int live = 0;
             for (int i = 0; i < NB; ++i) {
                 const int r = rows[(size_t)(s0 + s) * NB + i], k = kidx[(size_t)(s0 + s) * NB + i];
-                const bool live = r >= 0 && r < c->wmax && k >= 0 && k < KE;
-                const float wv = live ? wk[(size_t)(s0 + s) * NB + i] : 0.f;
-                if (snt == NB) { ht[nout * NB + i] = live ? r : -1; ho[nout * NB + i] = live ? r * KE + k : -1; hw[nout * NB + i] = wv; }
-                else if (live) { he[nout] = m; ht[nout] = r; ho[nout] = r * KE + k; hw[nout] = wv; ++nout; }
+                live += (r >= 0 && r < c->wmax && k >= 0 && k < KE) ? 1 : 0;
             }
-            if (snt == NB) ++nout;
+            if (live == 0) continue;
+            if (m != cur || fill + live > MM_NT) {             // a new mma slot
+                he[nout] = m; cur = m; fill = 0;
+                for (int i = 0; i < MM_NT; ++i) { ht[nout * MM_NT + i] = -1; ho[nout * MM_NT + i] = -1; hw[nout * MM_NT + i] = 0.f; }
+                ++nout;
+            }
+            for (int i = 0; i < NB; ++i) {
+                const int r = rows[(size_t)(s0 + s) * NB + i], k = kidx[(size_t)(s0 + s) * NB + i];
+                if (!(r >= 0 && r < c->wmax && k >= 0 && k < KE)) continue;
+                const int q = (nout - 1) * MM_NT + fill++;
+                ht[q] = r; ho[q] = r * KE + k; hw[q] = wk[(size_t)(s0 + s) * NB + i];
+                maxr = std::max(maxr, r);
+            }
         }
-        ho[nout * snt] = nout;
+        if (nout == 0) continue;
+        ho[nout * MM_NT] = nout;
         FLCK(cudaMemcpyAsync(c->w_expert[par], he, (size_t)nout * 4, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->w_tok[par], ht, (size_t)nout * snt * 4, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->w_out[par], ho, (size_t)nout * snt * 4, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->w_w[par], hw, (size_t)nout * snt * 4, cudaMemcpyHostToDevice, st));
-        FLCK(cudaMemcpyAsync(c->w_n[par], ho + nout * snt, 4, cudaMemcpyHostToDevice, st));
-        ExpertParams e = expert_params(c, gate, up, down, sg, sd, c->ncur_all, c->w_expert[par], c->w_tok[par], c->w_out[par],
-                                       c->w_w[par], c->w_n[par], c->whq, c->whd, c->out_all);
-        e.down_fmt = down_fmt;
-        launch_gate_up(e, snt, c->nsm, st);
-        launch_down(e, snt, c->nsm, st);
+        FLCK(cudaMemcpyAsync(c->w_tok[par], ht, (size_t)nout * MM_NT * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_out[par], ho, (size_t)nout * MM_NT * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_w[par], hw, (size_t)nout * MM_NT * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->w_n[par], ho + nout * MM_NT, 4, cudaMemcpyHostToDevice, st));
+        MmaParams m{};
+        m.gate = (const uint8_t*)gate; m.up = (const uint8_t*)up; m.down = (const uint8_t*)down;
+        m.gate_stride = sg; m.up_stride = sg; m.down_stride = sd;
+        m.x = c->ncur_all; m.ld_x = HIDDEN;
+        m.T = maxr + 1 > c->wxh_rows ? maxr + 1 : 0;          // the pass's rows into fp16 once (the prep kernel)
+        m.slot_expert = c->w_expert[par]; m.slot_tok = c->w_tok[par]; m.slot_out = c->w_out[par]; m.slot_w = c->w_w[par];
+        m.nslots = c->w_n[par]; m.max_slots = WIDE_SLOTS; m.slot_cnt = c->w_cnt[par];
+        m.xh = c->wxh; m.hb = c->whb; m.y = c->out_all; m.err = c->err;
+        if (m.T) c->wxh_rows = m.T;
+        if (down_fmt == FL_IQ2) {
+            launch_slot_mma(m, c->nsm, st);
+        } else {
+            launch_slot_mma_gate_up(m, c->nsm, st);
+            launch_kq_mma_down(m, down_fmt, c->nsm, st);
+        }
     }
     FLCK(cudaGetLastError());
 }

@@ -243,8 +243,25 @@ def test_reference_wide_pass_timing(native, oracle, ref):
         layer.experts(W, xd, rd, idd, wd, h=h, moe=mo)
         torch.cuda.synchronize()
 
+    # this library's engine-facing wide pass: the same plan through fl_wide_moe / fl_wide_finish
+    fc = F.FusedCtx()
+    assert fc.wide_init(T, KE) == 1
+    mw = native.FLMoeW(W.router_w.data_ptr(), 0, W.router_bias.data_ptr(), None, None, None, 0)
+    for g0 in range(0, T, 8):
+        fc.prepare(mw, x[g0:g0 + 8], r[g0:g0 + 8], wrow=g0)
+    fl_out = {}
+
+    def fl_pass():
+        for i, (gm, rows, kidx, wk) in enumerate(plan):
+            par = i & 1
+            if i >= 2:
+                fc.wide_wait(par)
+            fc.wide_moe(W.gate, W.up, W.down, 256, gm, rows, kidx, wk, KE, par, down_fmt=5)
+            fc.wide_mark(par)
+        fl_out["h"], fl_out["moe"] = fc.wide_finish(T, KE)
+
     res = {}
-    for name, fn in (("reference", ref_pass), ("ours", our_pass)):
+    for name, fn in (("reference", ref_pass), ("ours", our_pass), ("ours_fl", fl_pass)):
         fn()
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -263,7 +280,11 @@ def test_reference_wide_pass_timing(native, oracle, ref):
     o16 = oracle_layer(oracle, SEED, 40, x, r, ids, w, with_shared=False, tokens=tok, hq8=False, down_fmt=5)
     o8 = oracle_layer(oracle, SEED, 40, x, r, ids, w, with_shared=False, tokens=tok, hq8=True, down_fmt=5)
     e_ours, e_ref = rel_l2(hn[tok], o16["h"]), rel_l2(h_ref[tok], o8["h"])
-    print("wide pass T=512, Q2_K downs: reference %.2f ms, this library %.2f ms (%.2fx); vs own-numerics oracle: "
-          "ours %.1e, reference %.1e; ours vs reference %.1e"
-          % (res["reference"], res["ours"], res["reference"] / res["ours"], e_ours, e_ref, err))
-    assert e_ours < RTOL_L2 and e_ref < 1e-4
+    e_fl = rel_l2(fl_out["h"][tok], o16["h"])
+    assert fc.error() == 0
+    fc.close()
+    print("wide pass T=512, Q2_K downs: reference %.2f ms, this library %.2f ms (%.2fx), through its fl_wide_* ABI "
+          "%.2f ms (%.2fx); vs own-numerics oracle: ours %.1e, fl %.1e, reference %.1e; ours vs reference %.1e"
+          % (res["reference"], res["ours"], res["reference"] / res["ours"], res["ours_fl"], res["reference"] / res["ours_fl"],
+             e_ours, e_fl, e_ref, err))
+    assert e_ours < RTOL_L2 and e_fl < RTOL_L2 and e_ref < 1e-4
