@@ -54,6 +54,7 @@ struct FLCtx {
     int* hw_tab[2] = {}; float* hw_w[2] = {};
     float* h_wh = nullptr; float* h_wmoe = nullptr;
     cudaEvent_t wev[2] = {}, em0 = nullptr, em1 = nullptr, ep0 = nullptr, ep1 = nullptr;
+    cudaEvent_t eh2d = nullptr;       // after the last copy out of the pinned row mirrors (h_ncur / h_fi)
     double ms_moe = 0, ms_prep = 0;
     // last narrow call (for fl_moe_outs)
     int last_n = 0, last_ke = 0; std::vector<int> last_ids; std::vector<float> last_w;
@@ -154,7 +155,8 @@ FLCtx* fl_init(int kvp, int sc_cap) {
         dz(&c->y, rows * HIDDEN) == cudaSuccess &&
         dz(&c->rcount, PREP_ROWS) == cudaSuccess && hz(&c->h_in, R) == cudaSuccess &&
         cudaEventCreate(&c->em0) == cudaSuccess && cudaEventCreate(&c->em1) == cudaSuccess &&
-        cudaEventCreate(&c->ep0) == cudaSuccess && cudaEventCreate(&c->ep1) == cudaSuccess;
+        cudaEventCreate(&c->ep0) == cudaSuccess && cudaEventCreate(&c->ep1) == cudaSuccess &&
+        cudaEventCreateWithFlags(&c->eh2d, cudaEventDisableTiming) == cudaSuccess;
     c->blk[0] = io; c->blk[1] = ho; c->blk[2] = iwe; c->blk[3] = sw;
     c->hblk[0] = h_io; c->hblk[1] = h_ho; c->hblk[2] = h_iwe; c->hblk[3] = h_sw;
     if (!ok) { fl_fail(c, LK_ERR_CUDA, "fl_init: allocation failed", cudaGetLastError()); fl_free(c); return nullptr; }
@@ -184,7 +186,7 @@ void fl_free(FLCtx* c) {
     void* h[] = { c->hblk[0], c->hblk[1], c->hblk[2], c->hblk[3], c->h_in, c->h_wh, c->h_wmoe };
     for (void* p : h) if (p) cudaFreeHost(p);
     for (auto& g : c->graphs) if (g.exec) cudaGraphExecDestroy(g.exec);
-    cudaEvent_t ev[] = { c->em0, c->em1, c->ep0, c->ep1 };
+    cudaEvent_t ev[] = { c->em0, c->em1, c->ep0, c->ep1, c->eh2d };
     for (cudaEvent_t e : ev) if (e) cudaEventDestroy(e);
     if (c->st) cudaStreamDestroy(c->st);
     delete c;
@@ -294,7 +296,10 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     if (W->sh_fmt != 0 && W->sh_fmt != FL_IQ2 && W->sh_fmt != FL_Q5K) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe_prepare: shared-expert format must be FL_IQ2 or FL_Q5K"); return; }
     cudaStream_t st = c->st;
     const size_t bytes = (size_t)N * HIDDEN * 4;
-    if (host) { std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes); }
+    if (host) {                                   // the mirrors may still feed the previous call's queued copy
+        FLCK(cudaEventSynchronize(c->eh2d));
+        std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes);
+    }
     c->prep_n = N;
     c->sh_pending = W->sh_gate && W->sh_up && W->sh_down && wrow < 0;
     c->sh_in_y_n = 0;                             // this prepare's shared expert supersedes the last one
@@ -309,6 +314,7 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     FLCK(rec(c->ep0, st));
     if (host) {
         FLCK(copy_pair(c->ncur, c->h_ncur, (size_t)PREP_ROWS * HIDDEN * 4, bytes, cudaMemcpyHostToDevice, st));
+        FLCK(rec(c->eh2d, st));
     } else {
         FLCK(cudaMemcpyAsync(c->ncur, ncur, bytes, cudaMemcpyDeviceToDevice, st));
         FLCK(cudaMemcpyAsync(c->ffn_inp, ffn_inp, bytes, cudaMemcpyDeviceToDevice, st));
