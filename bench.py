@@ -552,8 +552,8 @@ def run_ep_prefill(args, ws, rank, local, dist):
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)" if not model_fmt else
-                 "the real model's formats (%s down, %s shared) x q8, int8 dp4a matvecs at every T, fp32 accumulate"
-                 % (args.down_fmt, args.shared_fmt),
+                 "the real model's formats (%s down, %s shared): IQ2_XXS gate/up tcgen05 fp16 x fp16, K-quant down mma.sync "
+                 "fp16 x fp16(h), Q5_K/Q6_K shared dequantised to fp16 + cuBLAS; fp32 accumulate" % (args.down_fmt, args.shared_fmt),
         "data": "synthetic: seeded IQ2_XXS experts, router W N(0,0.02), bias N(0,0.01), bf16 N(0,1) hidden states",
         "config": {"workload": "config3_ep_batch_T%d" % T, "global_batch": T, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,
                    "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": NE // ws, "rows_sent": sent,
@@ -750,8 +750,8 @@ def run_prefill(args, ws, rank, local, dist):
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)" if not model_fmt else
-                 "the real model's formats (%s down, %s shared) x q8, int8 dp4a matvecs at every T, fp32 accumulate"
-                 % (args.down_fmt, args.shared_fmt),
+                 "the real model's formats (%s down, %s shared): IQ2_XXS gate/up tcgen05 fp16 x fp16, K-quant down mma.sync "
+                 "fp16 x fp16(h), Q5_K/Q6_K shared dequantised to fp16 + cuBLAS; fp32 accumulate" % (args.down_fmt, args.shared_fmt),
         "data": "synthetic: seeded IQ2_XXS experts, uniform-random router logits U(-1,1), bf16 N(0,1) hidden states",
         "config": {"workload": "config2_prefill_T%d" % T + ("" if not model_fmt else "_%s_down_%s_shared" % (args.down_fmt, args.shared_fmt)),
                    "global_batch": T * ws, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,

@@ -47,26 +47,45 @@ __device__ __forceinline__ uint32_t pair_1024(uint32_t t, uint32_t mask) {
     return 0x64006400u | (t & mask) | ((t >> 8) & mask) << 16;
 }
 
-// one row's A-fragment halves for sub-block (n, j, s) of the block at `blk`: words w0 (l = 2c, 2c+1) and w1
-// (l = 2c+8, 2c+9) of qs (and hm0/hm1 of hmask for Q3_K) -> two fp16x2 of the weights
+// one row's per-block constants, loaded once per 256-weight block: d (and dmin), and the scale bytes -- Q2_K:
+// scales[0..15] as four words; Q3_K: the 12 packed scale bytes as three words
+struct RowBlk { float d, dmin; uint32_t sc[4]; };
 template <int FMT>
-__device__ __forceinline__ void row_pair(const uint8_t* blk, uint32_t w0, uint32_t w1, uint32_t hm0, uint32_t hm1, int n, int j, int s,
+__device__ __forceinline__ RowBlk load_rowblk(const uint8_t* blk) {
+    RowBlk r;
+    if (FMT == FMT_Q2K) {                             // 84-byte blocks: 4-byte aligned
+        const uint32_t dd = __ldg((const unsigned*)(blk + Q2K_D));
+        r.d = __half2float(__ushort_as_half((uint16_t)(dd & 0xFFFFu)));
+        r.dmin = __half2float(__ushort_as_half((uint16_t)(dd >> 16)));
+        #pragma unroll
+        for (int w = 0; w < 4; ++w) r.sc[w] = __ldg((const unsigned*)(blk + 4 * w));
+    } else {                                          // 110-byte blocks: 2-byte aligned
+        r.d = __half2float(__ushort_as_half((uint16_t)ldg_u16(blk + Q3K_D)));
+        r.dmin = 0.0f;
+        #pragma unroll
+        for (int w = 0; w < 3; ++w) r.sc[w] = ldg_u16(blk + Q3K_SC + 4 * w) | (ldg_u16(blk + Q3K_SC + 4 * w + 2) << 16);
+        r.sc[3] = 0u;
+    }
+    return r;
+}
+
+// one row's A-fragment halves for sub-block (n, j, s): words w0 (l = 2c, 2c+1) and w1 (l = 2c+8, 2c+9) of qs
+// (and hm0/hm1 of hmask for Q3_K) -> two fp16x2 of the weights
+template <int FMT>
+__device__ __forceinline__ void row_pair(const RowBlk& rb, uint32_t w0, uint32_t w1, uint32_t hm0, uint32_t hm1, int n, int j, int s,
                                          uint32_t& o0, uint32_t& o1) {
     const int is = 8 * n + 2 * j + s;
     if (FMT == FMT_Q2K) {
-        const uint32_t dd = __ldg((const unsigned*)(blk + Q2K_D));
-        const float d = __half2float(__ushort_as_half((uint16_t)(dd & 0xFFFFu)));
-        const float dmin = __half2float(__ushort_as_half((uint16_t)(dd >> 16)));
-        const uint32_t sc = ldg_u8(blk + is);
-        const float ds = d * (float)(sc & 15u);
-        const uint32_t ds2 = half2_bits(ds), c2 = half2_bits(-1024.0f * ds), dm2 = half2_bits(dmin * (float)(sc >> 4));
+        const uint32_t sc = (rb.sc[is >> 2] >> (8 * (is & 3))) & 0xFFu;
+        const float ds = rb.d * (float)(sc & 15u);
+        const uint32_t ds2 = half2_bits(ds), c2 = half2_bits(-1024.0f * ds), dm2 = half2_bits(rb.dmin * (float)(sc >> 4));
         o0 = hsub2(hfma2(pair_1024(w0 >> (2 * j), 3u), ds2, c2), dm2);
         o1 = hsub2(hfma2(pair_1024(w1 >> (2 * j), 3u), ds2, c2), dm2);
-    } else {                                          // Q3_K
-        const float d = __half2float(__ushort_as_half((uint16_t)ldg_u16(blk + Q3K_D)));
-        const int lo = is < 8 ? (int)(ldg_u8(blk + Q3K_SC + is) & 15u) : (int)(ldg_u8(blk + Q3K_SC + is - 8) >> 4);
-        const int hi = (int)((ldg_u8(blk + Q3K_SC + 8 + (is & 3)) >> (2 * (is >> 2))) & 3u);
-        const float ds = d * (float)((lo | (hi << 4)) - 32);
+    } else {                                          // Q3_K: the kmask unpacking of moe_format.h q3k_scale
+        const uint32_t lob = (rb.sc[(is & 7) >> 2] >> (8 * (is & 3))) & 0xFFu;
+        const int lo = is < 8 ? (int)(lob & 15u) : (int)(lob >> 4);
+        const int hi = (int)((rb.sc[2] >> (8 * (is & 3) + 2 * (is >> 2))) & 3u);
+        const float ds = rb.d * (float)((lo | (hi << 4)) - 32);
         const uint32_t ds2 = half2_bits(ds), c2 = half2_bits(-1024.0f * ds), f2 = half2_bits(4.0f * ds);
         const int hb = 4 * n + j;
         const uint32_t t0 = ((w0 >> (2 * j)) & 0x0303u) | (((hm0 >> hb) & 0x0101u) << 2);
@@ -104,6 +123,7 @@ __global__ void __launch_bounds__(KM_WARPS * 32) k_kq_mma_down(MmaParams p) {
         for (int b = 0; b < MOE_INTER / QK; ++b) {
             const uint8_t* ba = wa + b * BLK;
             const uint8_t* bb = wb + b * BLK;
+            const RowBlk ra = load_rowblk<FMT>(ba), rbk = load_rowblk<FMT>(bb);
             #pragma unroll
             for (int n = 0; n < 2; ++n) {
                 #pragma unroll
@@ -118,8 +138,8 @@ __global__ void __launch_bounds__(KM_WARPS * 32) k_kq_mma_down(MmaParams p) {
                     #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         uint32_t a0, a2, a1, a3;                   // rows g (a0, a2) and g+8 (a1, a3); l = 2c.. and 2c+8..
-                        row_pair<FMT>(ba, wa0, wa1, ha0, ha1, n, j, sh, a0, a2);
-                        row_pair<FMT>(bb, wb0, wb1, hb0, hb1, n, j, sh, a1, a3);
+                        row_pair<FMT>(ra, wa0, wa1, ha0, ha1, n, j, sh, a0, a2);
+                        row_pair<FMT>(rbk, wb0, wb1, hb0, hb1, n, j, sh, a1, a3);
                         const int k0 = b * QK + 128 * n + 32 * j + 16 * sh + 2 * c;
                         #pragma unroll
                         for (int nt = 0; nt < 2; ++nt) {
