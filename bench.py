@@ -765,7 +765,11 @@ def run_prefill(args, ws, rank, local, dist):
                      "frac": round(gemm_bytes / (g_ms / 1e3) / 1e9 / hbm, 4), "traffic": ncu_traffic("k_prefill_gemm", "prefill_T512"),
                      "algorithmic_bytes_per_launch": gemm_bytes, "peak_source": peak_kind,
                      "tensor_tflops": round(flops * 0.999 / (g_ms / 1e3) / 1e12, 1), "tensor_peak_tflops": bf16},
-        "gpu_launches": args.steps * 5,
+        # this library's kernels per step (profiles/prefill_gemm_T512.md, prefill_real_model_formats_T512.md):
+        # IQ2_XXS downs -- router, slots, gate B tiles, gate/up GEMM, down GEMM, combine; K-quant downs -- the
+        # down GEMM becomes a second slot build + k_kq_mma_down; a Q5_K/Q6_K shared expert adds its 5 dense-path
+        # kernels (3 dequantisations, x to fp16, SwiGLU; its two GEMMs are cuBLAS's)
+        "gpu_launches": args.steps * ((6 if fmt == 4 else 7) + (5 if args.shared_fmt == "q5k" else 0)),
     }
     if cl:
         out["clocks"] = cl
