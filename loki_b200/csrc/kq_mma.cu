@@ -9,12 +9,15 @@
 // SwiGLU rows (hb, written by the gate/up phase), C accumulates in fp32 registers.  The numerics are those of
 // the IQ2_XXS tensor-core paths: h stays fp16 instead of being re-quantised to q8.
 //
-// K order: a 16-deep mma step is one sub-block (n, j, s) of a 256-weight block -- weights 128n + 32j + 16s + l,
-// l < 16 -- whose 2-bit fields sit in qs bytes 32n + 16s + l at bit pair j (Q3_K: plus hmask[16s + l] bit
-// 4n + j).  Lane (g, c) needs l in {2c, 2c+1} and {2c+8, 2c+9} of rows g and g+8: two 16-bit words per row,
-// shared by the four j of one (n, s); the B fragment reads the same feature indices of h.  A weight becomes
-// fp16 as (1024 + q) by OR-ing q into 0x6400, then fma((1024 + q), ds, -1024 ds) = q ds exactly rounded (1024 ds
-// is exact), minus dmin * min (Q2_K) or 4 ds (Q3_K: the value is q3 - 4 with q3 = low2 | hbit << 2).
+// K order: the k index of an mma step is free as long as A and B agree on it.  Lane (g, c) owns the sub-block
+// half (n, sh) = (c >> 1, c & 1) of every 256-weight block -- weights 128n + 32j + 16sh + l, l < 16, j < 4 --
+// whose 2-bit fields sit in qs bytes 32n + 16sh + l at bit pair j (Q3_K: plus hmask[16sh + l] bit 4n + j).  The
+// 16-deep step (j, w) places weights l = 4w, 4w+1 of each lane's own sub-block at k slots 2c, 2c+1 and
+// l = 4w+2, 4w+3 at 2c+8, 2c+9, so a lane's weights come from four consecutive qs bytes (one word) and its B
+// fragments of two steps from eight consecutive h features (one 16-byte load); every weight of the block is still
+// decoded exactly once per row.  A weight becomes fp16 as (1024 + q) by OR-ing q into 0x6400, then
+// fma((1024 + q), ds, -1024 ds) = q ds exactly rounded (1024 ds is exact), minus dmin * min (Q2_K) or 4 ds (Q3_K:
+// the value is q3 - 4 with q3 = low2 | hbit << 2).
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
@@ -23,6 +26,9 @@ namespace lk {
 namespace {
 
 constexpr int KM_WARPS = 8;
+// resident blocks per SM the register budget is set for: Q2_K fits 64 registers without spills, Q3_K's extra
+// hmask words need ~80
+template <int FMT> constexpr int km_min_blocks() { return FMT == FMT_Q2K ? 4 : 3; }
 constexpr int KM_ITEMS_PER_SLOT = HIDDEN / 16;         // 448 row blocks of 16
 
 __device__ __forceinline__ void mma16816_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -40,65 +46,108 @@ __device__ __forceinline__ uint32_t half2_bits(float v) {
     return h | (h << 16);
 }
 __device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) { return (uint32_t)__ldg((const unsigned short*)p); }
-__device__ __forceinline__ uint32_t ldg_u8(const uint8_t* p) { return (uint32_t)__ldg(p); }
 
 // two fp16 (1024 + q) from the fields of a 16-bit word: q0 in bits 0..w-1 of t, q1 in bits 8..8+w-1
 __device__ __forceinline__ uint32_t pair_1024(uint32_t t, uint32_t mask) {
     return 0x64006400u | (t & mask) | ((t >> 8) & mask) << 16;
 }
 
-// one row's per-block constants, loaded once per 256-weight block: d (and dmin), and the scale bytes -- Q2_K:
-// scales[0..15] as four words; Q3_K: the 12 packed scale bytes as three words
-struct RowBlk { float d, dmin; uint32_t sc[4]; };
+// the lane's data of one row and 256-weight block: qs words q[w] (bytes l = 4w..4w+3 of its sub-block half),
+// Q3_K's hmask words, the scale words covering sub-blocks 8n + 2j + sh (Q2_K: scales[8n..8n+7] as two words;
+// Q3_K: the 12 packed scale bytes as three words), d and dmin
+struct LaneBlk { uint32_t q[4], hm[4], sc[3]; float d, dmin; };
+__device__ __forceinline__ uint32_t ldg_u32_2(const uint8_t* p) { return ldg_u16(p) | (ldg_u16(p + 2) << 16); }
 template <int FMT>
-__device__ __forceinline__ RowBlk load_rowblk(const uint8_t* blk) {
-    RowBlk r;
+__device__ __forceinline__ LaneBlk load_lane(const uint8_t* blk, int n, int sh) {
+    LaneBlk r;
     if (FMT == FMT_Q2K) {                             // 84-byte blocks: 4-byte aligned
+        const uint8_t* q = blk + Q2K_QS + 32 * n + 16 * sh;
+        #pragma unroll
+        for (int w = 0; w < 4; ++w) { r.q[w] = __ldg((const unsigned*)(q + 4 * w)); r.hm[w] = 0u; }
+        r.sc[0] = __ldg((const unsigned*)(blk + 8 * n));
+        r.sc[1] = __ldg((const unsigned*)(blk + 8 * n + 4));
+        r.sc[2] = 0u;
         const uint32_t dd = __ldg((const unsigned*)(blk + Q2K_D));
         r.d = __half2float(__ushort_as_half((uint16_t)(dd & 0xFFFFu)));
         r.dmin = __half2float(__ushort_as_half((uint16_t)(dd >> 16)));
-        #pragma unroll
-        for (int w = 0; w < 4; ++w) r.sc[w] = __ldg((const unsigned*)(blk + 4 * w));
     } else {                                          // 110-byte blocks: 2-byte aligned
+        const uint8_t* q = blk + Q3K_QS + 32 * n + 16 * sh;
+        const uint8_t* h = blk + 16 * sh;
+        #pragma unroll
+        for (int w = 0; w < 4; ++w) { r.q[w] = ldg_u32_2(q + 4 * w); r.hm[w] = ldg_u32_2(h + 4 * w); }
+        #pragma unroll
+        for (int w = 0; w < 3; ++w) r.sc[w] = ldg_u32_2(blk + Q3K_SC + 4 * w);
         r.d = __half2float(__ushort_as_half((uint16_t)ldg_u16(blk + Q3K_D)));
         r.dmin = 0.0f;
-        #pragma unroll
-        for (int w = 0; w < 3; ++w) r.sc[w] = ldg_u16(blk + Q3K_SC + 4 * w) | (ldg_u16(blk + Q3K_SC + 4 * w + 2) << 16);
-        r.sc[3] = 0u;
     }
     return r;
 }
 
-// one row's A-fragment halves for sub-block (n, j, s): words w0 (l = 2c, 2c+1) and w1 (l = 2c+8, 2c+9) of qs
-// (and hm0/hm1 of hmask for Q3_K) -> two fp16x2 of the weights
+// the fp16x2 constants of the lane's sub-block 8n + 2j + sh in one row: scale ds, -1024 ds, and the offset
+// subtracted after the fma (dmin * min for Q2_K, 4 ds for Q3_K)
+struct SubScale { uint32_t ds2, c2, m2; };
 template <int FMT>
-__device__ __forceinline__ void row_pair(const RowBlk& rb, uint32_t w0, uint32_t w1, uint32_t hm0, uint32_t hm1, int n, int j, int s,
-                                         uint32_t& o0, uint32_t& o1) {
-    const int is = 8 * n + 2 * j + s;
+__device__ __forceinline__ SubScale sub_scale(const LaneBlk& r, int n, int sh, int j) {
+    const int bsh = 8 * (2 * (j & 1) + sh);          // byte (2j + sh) & 3 of word (2j + sh) >> 2 = j >> 1
+    const uint32_t scw = (j & 2) ? r.sc[1] : r.sc[0];
+    float ds, m;
     if (FMT == FMT_Q2K) {
-        const uint32_t sc = (rb.sc[is >> 2] >> (8 * (is & 3))) & 0xFFu;
-        const float ds = rb.d * (float)(sc & 15u);
-        const uint32_t ds2 = half2_bits(ds), c2 = half2_bits(-1024.0f * ds), dm2 = half2_bits(rb.dmin * (float)(sc >> 4));
-        o0 = hsub2(hfma2(pair_1024(w0 >> (2 * j), 3u), ds2, c2), dm2);
-        o1 = hsub2(hfma2(pair_1024(w1 >> (2 * j), 3u), ds2, c2), dm2);
-    } else {                                          // Q3_K: the kmask unpacking of moe_format.h q3k_scale
-        const uint32_t lob = (rb.sc[(is & 7) >> 2] >> (8 * (is & 3))) & 0xFFu;
-        const int lo = is < 8 ? (int)(lob & 15u) : (int)(lob >> 4);
-        const int hi = (int)((rb.sc[2] >> (8 * (is & 3) + 2 * (is >> 2))) & 3u);
-        const float ds = rb.d * (float)((lo | (hi << 4)) - 32);
-        const uint32_t ds2 = half2_bits(ds), c2 = half2_bits(-1024.0f * ds), f2 = half2_bits(4.0f * ds);
+        const uint32_t sc = (scw >> bsh) & 0xFFu;
+        ds = r.d * (float)(sc & 15u);
+        m = r.dmin * (float)(sc >> 4);
+    } else {                                          // the kmask unpacking of moe_format.h q3k_scale, is = 8n + 2j + sh
+        const uint32_t lob = (scw >> bsh) & 0xFFu;
+        const int lo = n == 0 ? (int)(lob & 15u) : (int)(lob >> 4);
+        const int hi = (int)((r.sc[2] >> (bsh + 2 * (2 * n + (j >> 1)))) & 3u);
+        ds = r.d * (float)((lo | (hi << 4)) - 32);
+        m = 4.0f * ds;
+    }
+    return SubScale{half2_bits(ds), half2_bits(-1024.0f * ds), half2_bits(m)};
+}
+
+// one row's two A-fragment words for step (j, w): weights l = 4w, 4w+1 (lo) and 4w+2, 4w+3 (hi) as fp16x2
+template <int FMT>
+__device__ __forceinline__ void lane_pair(const LaneBlk& r, const SubScale& s, int n, int j, int w, uint32_t& lo, uint32_t& hi) {
+    uint32_t t0, t1, mask;
+    if (FMT == FMT_Q2K) {
+        t0 = r.q[w] >> (2 * j); t1 = r.q[w] >> (16 + 2 * j); mask = 3u;
+    } else {
         const int hb = 4 * n + j;
-        const uint32_t t0 = ((w0 >> (2 * j)) & 0x0303u) | (((hm0 >> hb) & 0x0101u) << 2);
-        const uint32_t t1 = ((w1 >> (2 * j)) & 0x0303u) | (((hm1 >> hb) & 0x0101u) << 2);
-        o0 = hsub2(hfma2(pair_1024(t0, 7u), ds2, c2), f2);
-        o1 = hsub2(hfma2(pair_1024(t1, 7u), ds2, c2), f2);
+        t0 = ((r.q[w] >> (2 * j)) & 0x0303u) | (((r.hm[w] >> hb) & 0x0101u) << 2);
+        t1 = ((r.q[w] >> (16 + 2 * j)) & 0x0303u) | (((r.hm[w] >> (16 + hb)) & 0x0101u) << 2);
+        mask = 7u;
+    }
+    lo = hsub2(hfma2(pair_1024(t0, mask), s.ds2, s.c2), s.m2);
+    hi = hsub2(hfma2(pair_1024(t1, mask), s.ds2, s.c2), s.m2);
+}
+
+// steps (j, 0..3) of one block: both rows' A fragments against the two 8-token N tiles
+template <int FMT>
+__device__ __forceinline__ void block_steps(const LaneBlk& ra, const LaneBlk& rbk, const __half* h0, const __half* h1, int f, int n, int sh,
+                                            int j, float (&acc)[2][4]) {
+    const SubScale sa = sub_scale<FMT>(ra, n, sh, j), sb = sub_scale<FMT>(rbk, n, sh, j);
+    #pragma unroll
+    for (int v = 0; v < 2; ++v) {
+        uint4 h[2];
+        #pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+            const __half* hr = nt ? h1 : h0;
+            h[nt] = hr ? __ldg((const uint4*)(hr + f + 32 * j + 8 * v)) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        #pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            uint32_t a0, a2, a1, a3;                  // rows g (a0, a2) and g+8 (a1, a3)
+            lane_pair<FMT>(ra, sa, n, j, 2 * v + u, a0, a2);
+            lane_pair<FMT>(rbk, sb, n, j, 2 * v + u, a1, a3);
+            #pragma unroll
+            for (int nt = 0; nt < 2; ++nt) mma16816_f16(acc[nt], a0, a1, a2, a3, u ? h[nt].z : h[nt].x, u ? h[nt].w : h[nt].y);
+        }
     }
 }
 
 template <int FMT>
-__global__ void __launch_bounds__(KM_WARPS * 32) k_kq_mma_down(MmaParams p) {
+__global__ void __launch_bounds__(KM_WARPS * 32, km_min_blocks<FMT>()) k_kq_mma_down(MmaParams p) {
     constexpr int BLK = FMT == FMT_Q2K ? BLK_Q2K : BLK_Q3K;
-    constexpr int QS = FMT == FMT_Q2K ? Q2K_QS : Q3K_QS;
     constexpr int ROWB = (MOE_INTER / QK) * BLK;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
     const int nitems = *p.nslots * KM_ITEMS_PER_SLOT;
@@ -120,36 +169,12 @@ __global__ void __launch_bounds__(KM_WARPS * 32) k_kq_mma_down(MmaParams p) {
             hrow[nt] = out >= 0 ? p.hb + (size_t)out * MOE_INTER : nullptr;
         }
         float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const int n = c >> 1, sh = c & 1;
         for (int b = 0; b < MOE_INTER / QK; ++b) {
-            const uint8_t* ba = wa + b * BLK;
-            const uint8_t* bb = wb + b * BLK;
-            const RowBlk ra = load_rowblk<FMT>(ba), rbk = load_rowblk<FMT>(bb);
-            #pragma unroll
-            for (int n = 0; n < 2; ++n) {
-                #pragma unroll
-                for (int sh = 0; sh < 2; ++sh) {
-                    const int q0 = QS + 32 * n + 16 * sh + 2 * c;
-                    const uint32_t wa0 = ldg_u16(ba + q0), wa1 = ldg_u16(ba + q0 + 8), wb0 = ldg_u16(bb + q0), wb1 = ldg_u16(bb + q0 + 8);
-                    uint32_t ha0 = 0, ha1 = 0, hb0 = 0, hb1 = 0;
-                    if (FMT == FMT_Q3K) {
-                        const int m0 = 16 * sh + 2 * c;
-                        ha0 = ldg_u16(ba + m0); ha1 = ldg_u16(ba + m0 + 8); hb0 = ldg_u16(bb + m0); hb1 = ldg_u16(bb + m0 + 8);
-                    }
-                    #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t a0, a2, a1, a3;                   // rows g (a0, a2) and g+8 (a1, a3); l = 2c.. and 2c+8..
-                        row_pair<FMT>(ra, wa0, wa1, ha0, ha1, n, j, sh, a0, a2);
-                        row_pair<FMT>(rbk, wb0, wb1, hb0, hb1, n, j, sh, a1, a3);
-                        const int k0 = b * QK + 128 * n + 32 * j + 16 * sh + 2 * c;
-                        #pragma unroll
-                        for (int nt = 0; nt < 2; ++nt) {
-                            const uint32_t b0 = hrow[nt] ? __ldg((const unsigned*)(hrow[nt] + k0)) : 0u;
-                            const uint32_t b1 = hrow[nt] ? __ldg((const unsigned*)(hrow[nt] + k0 + 8)) : 0u;
-                            mma16816_f16(acc[nt], a0, a1, a2, a3, b0, b1);
-                        }
-                    }
-                }
-            }
+            const LaneBlk ra = load_lane<FMT>(wa + b * BLK, n, sh), rbk = load_lane<FMT>(wb + b * BLK, n, sh);
+            const int f = b * QK + 128 * n + 16 * sh;    // h features of the lane's sub-block half, j = 0
+            #pragma unroll 1
+            for (int j = 0; j < 4; ++j) block_steps<FMT>(ra, rbk, hrow[0], hrow[1], f, n, sh, j, acc);
         }
         // C fragment: acc[nt][0..1] = row g, tokens 8nt + 2c, +1; acc[nt][2..3] = row g + 8
         #pragma unroll
@@ -169,10 +194,18 @@ __global__ void __launch_bounds__(KM_WARPS * 32) k_kq_mma_down(MmaParams p) {
 
 }  // namespace
 
+// one wave of resident blocks: items are grid-strided, so blocks beyond the resident ones would only form a tail
+template <int FMT>
+static void launch_fmt(const MmaParams& p, int nsm, cudaStream_t st) {
+    static int per_sm = 0;
+    if (per_sm <= 0 && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_kq_mma_down<FMT>, KM_WARPS * 32, 0) != cudaSuccess || per_sm <= 0))
+        per_sm = km_min_blocks<FMT>();
+    k_kq_mma_down<FMT><<<per_sm * nsm, KM_WARPS * 32, 0, st>>>(p);
+}
+
 void launch_kq_mma_down(const MmaParams& p, int down_fmt, int nsm, cudaStream_t st) {
-    const int grid = 4 * nsm;
-    if (down_fmt == FMT_Q2K) k_kq_mma_down<FMT_Q2K><<<grid, KM_WARPS * 32, 0, st>>>(p);
-    else k_kq_mma_down<FMT_Q3K><<<grid, KM_WARPS * 32, 0, st>>>(p);
+    if (down_fmt == FMT_Q2K) launch_fmt<FMT_Q2K>(p, nsm, st);
+    else launch_fmt<FMT_Q3K>(p, nsm, st);
 }
 
 }  // namespace lk
