@@ -56,7 +56,23 @@ __device__ __forceinline__ uint32_t pair_1024(uint32_t t, uint32_t mask) {
 // Q3_K's hmask words, the scale words covering sub-blocks 8n + 2j + sh (Q2_K: scales[8n..8n+7] as two words;
 // Q3_K: the 12 packed scale bytes as three words), d and dmin
 struct LaneBlk { uint32_t q[4], hm[4], sc[3]; float d, dmin; };
-__device__ __forceinline__ uint32_t ldg_u32_2(const uint8_t* p) { return ldg_u16(p) | (ldg_u16(p + 2) << 16); }
+// four little-endian words from a 2-byte-aligned address by aligned loads: direct when p is 4-byte aligned,
+// else funnel-shifted out of the five aligned words around the 16 bytes.  Every word read contains a byte of
+// [p, p + 16), so no load reaches past the page of the data.  A warp's rows share their alignment (rows are
+// 4-byte multiples apart), so the branch is uniform.
+__device__ __forceinline__ void ldg_words4(const uint8_t* p, uint32_t (&o)[4]) {
+    if (((uintptr_t)p & 3u) == 0) {
+        #pragma unroll
+        for (int w = 0; w < 4; ++w) o[w] = __ldg((const unsigned*)(p + 4 * w));
+    } else {
+        const unsigned* a = (const unsigned*)(p - 2);
+        uint32_t v[5];
+        #pragma unroll
+        for (int i = 0; i < 5; ++i) v[i] = __ldg(a + i);
+        #pragma unroll
+        for (int w = 0; w < 4; ++w) o[w] = __funnelshift_r(v[w], v[w + 1], 16);
+    }
+}
 template <int FMT>
 __device__ __forceinline__ LaneBlk load_lane(const uint8_t* blk, int n, int sh) {
     LaneBlk r;
@@ -70,14 +86,24 @@ __device__ __forceinline__ LaneBlk load_lane(const uint8_t* blk, int n, int sh) 
         const uint32_t dd = __ldg((const unsigned*)(blk + Q2K_D));
         r.d = __half2float(__ushort_as_half((uint16_t)(dd & 0xFFFFu)));
         r.dmin = __half2float(__ushort_as_half((uint16_t)(dd >> 16)));
-    } else {                                          // 110-byte blocks: 2-byte aligned
-        const uint8_t* q = blk + Q3K_QS + 32 * n + 16 * sh;
-        const uint8_t* h = blk + 16 * sh;
-        #pragma unroll
-        for (int w = 0; w < 4; ++w) { r.q[w] = ldg_u32_2(q + 4 * w); r.hm[w] = ldg_u32_2(h + 4 * w); }
-        #pragma unroll
-        for (int w = 0; w < 3; ++w) r.sc[w] = ldg_u32_2(blk + Q3K_SC + 4 * w);
-        r.d = __half2float(__ushort_as_half((uint16_t)ldg_u16(blk + Q3K_D)));
+    } else {                                          // 110-byte blocks: 4-byte aligned for every other block
+        ldg_words4(blk + Q3K_QS + 32 * n + 16 * sh, r.q);
+        ldg_words4(blk + 16 * sh, r.hm);
+        uint32_t dw;
+        if (((uintptr_t)blk & 3u) == 0) {             // scale words at +96..+107, d at +108
+            #pragma unroll
+            for (int w = 0; w < 3; ++w) r.sc[w] = __ldg((const unsigned*)(blk + Q3K_SC + 4 * w));
+            dw = ldg_u16(blk + Q3K_D);
+        } else {                                      // aligned words at +94, +98, +102, +106 (d in the last one's high half)
+            const unsigned* a = (const unsigned*)(blk + Q3K_SC - 2);
+            uint32_t v[4];
+            #pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = __ldg(a + i);
+            #pragma unroll
+            for (int w = 0; w < 3; ++w) r.sc[w] = __funnelshift_r(v[w], v[w + 1], 16);
+            dw = v[3] >> 16;
+        }
+        r.d = __half2float(__ushort_as_half((uint16_t)dw));
         r.dmin = 0.0f;
     }
     return r;
