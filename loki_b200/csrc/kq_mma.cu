@@ -15,7 +15,7 @@
 // 16-deep step (j, w) places weights l = 4w, 4w+1 of each lane's own sub-block at k slots 2c, 2c+1 and
 // l = 4w+2, 4w+3 at 2c+8, 2c+9, so a lane's weights come from four consecutive qs bytes (one word) and its B
 // fragments of two steps from eight consecutive h features (one 16-byte load); every weight of the block is still
-// decoded exactly once per row.  A weight becomes fp16 as (1024 + q) by OR-ing q into 0x6400, then
+// decoded exactly once per row.  A weight becomes fp16 as (1024 + q) by placing q under a 0x64 high byte, then
 // fma((1024 + q), ds, -1024 ds) = q ds exactly rounded (1024 ds is exact), minus dmin * min (Q2_K) or 4 ds (Q3_K:
 // the value is q3 - 4 with q3 = low2 | hbit << 2).
 #include "moe_internal.h"
@@ -46,11 +46,6 @@ __device__ __forceinline__ uint32_t half2_bits(float v) {
     return h | (h << 16);
 }
 __device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) { return (uint32_t)__ldg((const unsigned short*)p); }
-
-// two fp16 (1024 + q) from the fields of a 16-bit word: q0 in bits 0..w-1 of t, q1 in bits 8..8+w-1
-__device__ __forceinline__ uint32_t pair_1024(uint32_t t, uint32_t mask) {
-    return 0x64006400u | (t & mask) | ((t >> 8) & mask) << 16;
-}
 
 // the lane's data of one row and 256-weight block: qs words q[w] (bytes l = 4w..4w+3 of its sub-block half),
 // Q3_K's hmask words, the scale words covering sub-blocks 8n + 2j + sh (Q2_K: scales[8n..8n+7] as two words;
@@ -131,20 +126,15 @@ __device__ __forceinline__ SubScale sub_scale(const LaneBlk& r, int n, int sh, i
     return SubScale{half2_bits(ds), half2_bits(-1024.0f * ds), half2_bits(m)};
 }
 
-// one row's two A-fragment words for step (j, w): weights l = 4w, 4w+1 (lo) and 4w+2, 4w+3 (hi) as fp16x2
+// one row's two A-fragment words for step (j, w): weights l = 4w, 4w+1 (lo) and 4w+2, 4w+3 (hi) as fp16x2.  One
+// shift and mask leave the four fields of qs word w in their bytes (Q3_K: the hmask bit ORed in as bit 2); a
+// byte permute then puts each field under a 0x64 high byte, the fp16 (1024 + q).
 template <int FMT>
 __device__ __forceinline__ void lane_pair(const LaneBlk& r, const SubScale& s, int n, int j, int w, uint32_t& lo, uint32_t& hi) {
-    uint32_t t0, t1, mask;
-    if (FMT == FMT_Q2K) {
-        t0 = r.q[w] >> (2 * j); t1 = r.q[w] >> (16 + 2 * j); mask = 3u;
-    } else {
-        const int hb = 4 * n + j;
-        t0 = ((r.q[w] >> (2 * j)) & 0x0303u) | (((r.hm[w] >> hb) & 0x0101u) << 2);
-        t1 = ((r.q[w] >> (16 + 2 * j)) & 0x0303u) | (((r.hm[w] >> (16 + hb)) & 0x0101u) << 2);
-        mask = 7u;
-    }
-    lo = hsub2(hfma2(pair_1024(t0, mask), s.ds2, s.c2), s.m2);
-    hi = hsub2(hfma2(pair_1024(t1, mask), s.ds2, s.c2), s.m2);
+    uint32_t t = (r.q[w] >> (2 * j)) & 0x03030303u;
+    if (FMT == FMT_Q3K) t |= ((r.hm[w] >> (4 * n + j)) & 0x01010101u) << 2;
+    lo = hsub2(hfma2(__byte_perm(t, 0x64646464u, 0x4140u), s.ds2, s.c2), s.m2);
+    hi = hsub2(hfma2(__byte_perm(t, 0x64646464u, 0x4342u), s.ds2, s.c2), s.m2);
 }
 
 // steps (j, 0..3) of one block: both rows' A fragments against the two 8-token N tiles
