@@ -28,7 +28,7 @@ namespace {
 constexpr int KM_WARPS = 8;
 // resident blocks per SM the register budget is set for: Q2_K fits 64 registers without spills, Q3_K's extra
 // hmask words need ~80
-template <int FMT> constexpr int km_min_blocks() { return FMT == FMT_Q2K ? 4 : 3; }
+template <int FMT> constexpr int km_min_blocks() { return FMT == FMT_Q2K ? 3 : 2; }
 constexpr int KM_ITEMS_PER_SLOT = HIDDEN / 16;         // 448 row blocks of 16
 
 __device__ __forceinline__ void mma16816_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -137,74 +137,105 @@ __device__ __forceinline__ void lane_pair(const LaneBlk& r, const SubScale& s, i
     hi = hsub2(hfma2(__byte_perm(t, 0x64646464u, 0x4342u), s.ds2, s.c2), s.m2);
 }
 
-// steps (j, 0..3) of one block: both rows' A fragments against the two 8-token N tiles
-template <int FMT>
-__device__ __forceinline__ void block_steps(const LaneBlk& ra, const LaneBlk& rbk, const __half* h0, const __half* h1, int f, int n, int sh,
-                                            int j, float (&acc)[2][4]) {
+// steps (j, 0..3) of one block: both rows' A fragments against the NT 8-token N tiles.  Token column g of
+// tile nt is the fp16 h row at element offset hoff[nt] (negative: no token there, B = 0).  The A fragments of
+// the two steps sharing a 16-byte h load are formed first, then h is loaded one tile pair at a time.
+template <int FMT, int NT>
+__device__ __forceinline__ void block_steps(const LaneBlk& ra, const LaneBlk& rbk, const __half* hb, const int (&hoff)[NT], int f, int n,
+                                            int sh, int j, float (&acc)[NT][4]) {
     const SubScale sa = sub_scale<FMT>(ra, n, sh, j), sb = sub_scale<FMT>(rbk, n, sh, j);
     #pragma unroll
     for (int v = 0; v < 2; ++v) {
-        uint4 h[2];
-        #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-            const __half* hr = nt ? h1 : h0;
-            h[nt] = hr ? __ldg((const uint4*)(hr + f + 32 * j + 8 * v)) : make_uint4(0u, 0u, 0u, 0u);
-        }
+        uint32_t a[2][4];                             // step u: rows g (a[u][0], a[u][2]) and g+8 (a[u][1], a[u][3])
         #pragma unroll
         for (int u = 0; u < 2; ++u) {
-            uint32_t a0, a2, a1, a3;                  // rows g (a0, a2) and g+8 (a1, a3)
-            lane_pair<FMT>(ra, sa, n, j, 2 * v + u, a0, a2);
-            lane_pair<FMT>(rbk, sb, n, j, 2 * v + u, a1, a3);
+            lane_pair<FMT>(ra, sa, n, j, 2 * v + u, a[u][0], a[u][2]);
+            lane_pair<FMT>(rbk, sb, n, j, 2 * v + u, a[u][1], a[u][3]);
+        }
+        #pragma unroll
+        for (int tp = 0; tp < NT; tp += 2) {
+            uint4 h[2];
             #pragma unroll
-            for (int nt = 0; nt < 2; ++nt) mma16816_f16(acc[nt], a0, a1, a2, a3, u ? h[nt].z : h[nt].x, u ? h[nt].w : h[nt].y);
+            for (int q = 0; q < 2; ++q)
+                h[q] = hoff[tp + q] >= 0 ? __ldg((const uint4*)(hb + hoff[tp + q] + f + 32 * j + 8 * v)) : make_uint4(0u, 0u, 0u, 0u);
+            #pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                #pragma unroll
+                for (int q = 0; q < 2; ++q)
+                    mma16816_f16(acc[tp + q], a[u][0], a[u][1], a[u][2], a[u][3], u ? h[q].z : h[q].x, u ? h[q].w : h[q].y);
+            }
         }
     }
 }
 
+// 16 rows (row block rb) of slot s's expert against NT 8-token N tiles: tiles 0, 1 hold slot s's tokens, tiles
+// 2, 3 (NT = 4) slot s + 1's, so one decode of the rows serves both slots of the pair
+template <int FMT, int NT>
+__device__ __forceinline__ void item_rows(const MmaParams& p, const uint8_t* W, int s, const int (&cnt)[2], int rb, int g, int c) {
+    constexpr int BLK = FMT == FMT_Q2K ? BLK_Q2K : BLK_Q3K;
+    constexpr int ROWB = (MOE_INTER / QK) * BLK;
+    const uint8_t* wa = W + (size_t)g * ROWB;
+    const uint8_t* wb = W + (size_t)(g + 8) * ROWB;
+    int hoff[NT];
+    #pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int sl = s + (nt >> 1), tn = 8 * (nt & 1) + g;
+        const int out = tn < cnt[nt >> 1] ? p.slot_out[sl * MM_NT + tn] : -1;
+        hoff[nt] = out >= 0 ? out * MOE_INTER : -1;
+    }
+    float acc[NT][4];
+    #pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+    const int n = c >> 1, sh = c & 1;
+    for (int b = 0; b < MOE_INTER / QK; ++b) {
+        const LaneBlk ra = load_lane<FMT>(wa + b * BLK, n, sh), rbk = load_lane<FMT>(wb + b * BLK, n, sh);
+        const int f = b * QK + 128 * n + 16 * sh;    // h features of the lane's sub-block half, j = 0
+        #pragma unroll 1
+        for (int j = 0; j < 4; ++j) block_steps<FMT, NT>(ra, rbk, p.hb, hoff, f, n, sh, j, acc);
+    }
+    // C fragment: acc[nt][0..1] = row g, tokens 8(nt & 1) + 2c, +1 of slot s + (nt >> 1); acc[nt][2..3] = row g + 8
+    #pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int sl = s + (nt >> 1);
+        #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int tn = 8 * (nt & 1) + 2 * c + (i & 1);
+            if (tn >= cnt[nt >> 1]) continue;
+            const int out = p.slot_out[sl * MM_NT + tn];
+            if (out < 0) continue;
+            const int row = rb * 16 + g + 8 * (i >> 1);
+            p.y[(size_t)out * HIDDEN + row] = p.slot_w[sl * MM_NT + tn] * acc[nt][i];
+        }
+    }
+}
+
+__device__ __forceinline__ int slot_tokens(const MmaParams& p, int s) {
+    if (p.slot_cnt) return p.slot_cnt[s];
+    int cnt = 0;                                      // counted here when no pre-pass ran
+    while (cnt < MM_NT && p.slot_tok[s * MM_NT + cnt] >= 0) ++cnt;
+    return cnt;
+}
+
+// Items are (slot, row block).  An expert's slots are consecutive; the first slot of a run also takes the second
+// (a decode of the rows feeds 4 N tiles), the second is then skipped, and later slots of a hot expert go alone.
 template <int FMT>
 __global__ void __launch_bounds__(KM_WARPS * 32, km_min_blocks<FMT>()) k_kq_mma_down(MmaParams p) {
     constexpr int BLK = FMT == FMT_Q2K ? BLK_Q2K : BLK_Q3K;
     constexpr int ROWB = (MOE_INTER / QK) * BLK;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
-    const int nitems = *p.nslots * KM_ITEMS_PER_SLOT;
+    const int nslots = *p.nslots;
+    const int nitems = nslots * KM_ITEMS_PER_SLOT;
     for (int item = blockIdx.x * KM_WARPS + warp; item < nitems; item += gridDim.x * KM_WARPS) {
         const int s = item / KM_ITEMS_PER_SLOT, rb = item % KM_ITEMS_PER_SLOT;
-        int cnt = 0;                                  // the slot's tokens (counted here when no pre-pass ran)
-        if (p.slot_cnt) cnt = p.slot_cnt[s];
-        else while (cnt < MM_NT && p.slot_tok[s * MM_NT + cnt] >= 0) ++cnt;
-        if (cnt <= 0) continue;
         const int e = p.slot_expert[s];
+        const bool first = s == 0 || p.slot_expert[s - 1] != e;
+        if (!first && (s == 1 || p.slot_expert[s - 2] != e)) continue;   // second of its run: done with the first
+        const bool pair = first && s + 1 < nslots && p.slot_expert[s + 1] == e;
+        const int cnt[2] = { slot_tokens(p, s), pair ? slot_tokens(p, s + 1) : 0 };
+        if (cnt[0] <= 0 && cnt[1] <= 0) continue;
         const uint8_t* W = (e == SHARED_SLOT ? p.sh_down : p.down + (size_t)e * p.down_stride) + (size_t)rb * 16 * ROWB;
-        const uint8_t* wa = W + (size_t)g * ROWB;
-        const uint8_t* wb = W + (size_t)(g + 8) * ROWB;
-        const __half* hrow[2];
-        #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-            const int tn = 8 * nt + g;
-            const int out = tn < cnt ? p.slot_out[s * MM_NT + tn] : -1;
-            hrow[nt] = out >= 0 ? p.hb + (size_t)out * MOE_INTER : nullptr;
-        }
-        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        const int n = c >> 1, sh = c & 1;
-        for (int b = 0; b < MOE_INTER / QK; ++b) {
-            const LaneBlk ra = load_lane<FMT>(wa + b * BLK, n, sh), rbk = load_lane<FMT>(wb + b * BLK, n, sh);
-            const int f = b * QK + 128 * n + 16 * sh;    // h features of the lane's sub-block half, j = 0
-            #pragma unroll 1
-            for (int j = 0; j < 4; ++j) block_steps<FMT>(ra, rbk, hrow[0], hrow[1], f, n, sh, j, acc);
-        }
-        // C fragment: acc[nt][0..1] = row g, tokens 8nt + 2c, +1; acc[nt][2..3] = row g + 8
-        #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-            #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int tn = 8 * nt + 2 * c + (i & 1);
-                if (tn >= cnt) continue;
-                const int out = p.slot_out[s * MM_NT + tn];
-                if (out < 0) continue;
-                const int row = rb * 16 + g + 8 * (i >> 1);
-                p.y[(size_t)out * HIDDEN + row] = p.slot_w[s * MM_NT + tn] * acc[nt][i];
-            }
-        }
+        if (pair) item_rows<FMT, 4>(p, W, s, cnt, rb, g, c);
+        else item_rows<FMT, 2>(p, W, s, cnt, rb, g, c);
     }
 }
 
