@@ -4,8 +4,9 @@
 //
 // The single-token dp4a kernel (expert_kq.cu) decodes a down matrix once per (token, expert) entry; at T=512
 // that makes the layer instruction-bound.  Here one warp owns 16 weight rows of one slot's expert (<= MM_NT =
-// 16 tokens) and all of K = 2048: each 16-weight sub-block of its rows is decoded once -- scale and min folded
-// in -- into an fp16 m16n8k16 A fragment and multiplied into both 8-token N tiles.  B is the slot tokens' fp16
+// 16 tokens; the first two slots of an expert's run together, <= 32) and all of K = 2048: each 16-weight
+// sub-block of its rows is decoded once -- scale and min folded in -- into an fp16 m16n8k16 A fragment and
+// multiplied into every 8-token N tile.  B is the slot tokens' fp16
 // SwiGLU rows (hb, written by the gate/up phase), C accumulates in fp32 registers.  The numerics are those of
 // the IQ2_XXS tensor-core paths: h stays fp16 instead of being re-quantised to q8.
 //
