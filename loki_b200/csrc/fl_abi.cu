@@ -53,6 +53,7 @@ struct FLCtx {
     int *w_expert[2] = {}, *w_tok[2] = {}, *w_out[2] = {}, *w_n[2] = {}, *w_cnt[2] = {}; float* w_w[2] = {};
     int* hw_tab[2] = {}; float* hw_w[2] = {};
     float* h_wh = nullptr; float* h_wmoe = nullptr;
+    float* wfin = nullptr;            // [2][wmax][HIDDEN]: fl_wide_finish's h and moe, fl_wide_skip's mo and h
     cudaEvent_t wev[2] = {}, em0 = nullptr, em1 = nullptr, ep0 = nullptr, ep1 = nullptr;
     cudaEvent_t eh2d = nullptr;       // after the last copy out of the pinned row mirrors (h_ncur / h_fi)
     double ms_moe = 0, ms_prep = 0;
@@ -174,7 +175,7 @@ void fl_free(FLCtx* c) {
     if (c->st) cudaStreamSynchronize(c->st);
     void* d[] = { c->blk[0], c->blk[1], c->blk[2], c->blk[3], c->logits, c->probs, c->shared_y, c->sh_gu, c->sh_pair, c->mo,
                   c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->counts, c->offsets, c->perm, c->hq, c->hd, c->y,
-                  c->ncur_all, c->base_all, c->out_all, c->wxh, c->whb, c->rcount };
+                  c->ncur_all, c->base_all, c->out_all, c->wxh, c->whb, c->rcount, c->wfin };
     for (void* p : d) if (p) cudaFree(p);
     for (int p = 0; p < 2; ++p) {
         void* dd[] = { c->w_expert[p], c->w_tok[p], c->w_out[p], c->w_n[p], c->w_cnt[p], c->w_w[p] };
@@ -571,7 +572,7 @@ int fl_wide_init(FLCtx* c, int wmax, int KE) {
     const size_t R = (size_t)wmax * HIDDEN;
     const size_t ent = (size_t)wmax * KE;
     if (dz(&c->ncur_all, R) || dz(&c->base_all, R) || dz(&c->out_all, ent * HIDDEN) || dz(&c->wxh, R) ||
-        dz(&c->whb, ent * MOE_INTER) || hz(&c->h_wh, R) || hz(&c->h_wmoe, R)) { fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0; }
+        dz(&c->whb, ent * MOE_INTER) || dz(&c->wfin, 2 * R) || hz(&c->h_wh, R) || hz(&c->h_wmoe, R)) { fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0; }
     c->wxh_rows = 0;
     for (int p = 0; p < 2; ++p) {
         // room for WIDE_SLOTS slots of MM_NT tokens (the mma.sync path's layout)
@@ -659,19 +660,17 @@ void fl_wide_finish(FLCtx* c, int n, int KE, FLOut* out) {
     std::memset(out, 0, sizeof(FLOut));
     if (!c->ncur_all || n < 1 || n > c->wmax || KE != c->wke) { fl_fail(c, LK_ERR_ARG, "fl_wide_finish: bad argument"); return; }
     cudaStream_t st = c->st;
-    // moe goes to ncur_all (free after the pass), h to a fresh pass over base_all into the pinned mirror
+    // h and moe of the pass into the finish buffer (allocated by fl_wide_init), then into the pinned mirrors
     CombineParams cp{};
     cp.y = c->out_all; cp.resid = c->base_all; cp.T = n; cp.keep = KE; cp.with_shared = 0; cp.shared = nullptr;
-    cp.h = c->ncur_all; cp.moe = nullptr; cp.ld_out = HIDDEN;
-    float* hbuf = nullptr;
-    FLCK(cudaMalloc(&hbuf, (size_t)n * HIDDEN * 4 * 2));
+    cp.ld_out = HIDDEN;
+    float* hbuf = c->wfin;
     cp.h = hbuf; cp.moe = hbuf + (size_t)n * HIDDEN;
     launch_combine(cp, st);
     FLCK(cudaMemcpyAsync(c->h_wh, hbuf, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
     FLCK(cudaMemcpyAsync(c->h_wmoe, hbuf + (size_t)n * HIDDEN, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
     queue_err(c);
     FLCK(cudaStreamSynchronize(st));
-    cudaFree(hbuf);
     check_dev(c);
     out->h = c->h_wh; out->moe = c->h_wmoe;
 }
@@ -680,8 +679,7 @@ void fl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
     if (!c || !out || !mo || !c->ncur_all || n < 1 || n > c->wmax) return;
     std::memset(out, 0, sizeof(FLOut));
     cudaStream_t st = c->st;
-    float* dmo = nullptr;
-    FLCK(cudaMalloc(&dmo, (size_t)n * HIDDEN * 4 * 2));
+    float* dmo = c->wfin;
     FLCK(cudaMemcpyAsync(dmo, mo, (size_t)n * HIDDEN * 4, cudaMemcpyHostToDevice, st));
     CombineParams cp{};
     cp.y = dmo; cp.resid = c->base_all; cp.T = n; cp.keep = 1; cp.with_shared = 0; cp.shared = nullptr;
@@ -689,7 +687,6 @@ void fl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
     launch_combine(cp, st);
     FLCK(cudaMemcpyAsync(c->h_wh, dmo + (size_t)n * HIDDEN, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
     FLCK(cudaStreamSynchronize(st));
-    cudaFree(dmo);
     out->h = c->h_wh;
 }
 
