@@ -53,9 +53,10 @@ __device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) { return (uint32_t
 // Q3_K: the 12 packed scale bytes as three words), d and dmin
 struct LaneBlk { uint32_t q[4], hm[4], sc[3]; float d, dmin; };
 // four little-endian words from a 2-byte-aligned address by aligned loads: direct when p is 4-byte aligned,
-// else funnel-shifted out of the five aligned words around the 16 bytes.  Every word read contains a byte of
-// [p, p + 16), so no load reaches past the page of the data.  A warp's rows share their alignment (rows are
-// 4-byte multiples apart), so the branch is uniform.
+// else funnel-shifted out of the five aligned words around the 16 bytes.  Every entry point takes 16-byte
+// aligned arenas and strides, and a Q3_K row is 880 bytes, so only odd blocks sit at 2 mod 4; the word before
+// their data lies in the previous block of the same row, and no load leaves the arena.  A warp's rows share
+// their alignment, so the branch is uniform.
 __device__ __forceinline__ void ldg_words4(const uint8_t* p, uint32_t (&o)[4]) {
     if (((uintptr_t)p & 3u) == 0) {
         #pragma unroll
