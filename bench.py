@@ -57,6 +57,9 @@ def shared_bytes(args):
 N_GROUP, TOPK_GROUP = 8, 4
 
 
+NOMINAL_HBM_GBS = 7700.0     # HBM3e nominal (HGX B200); frac is against the measured copy bandwidth
+
+
 def measured_peaks():
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -340,6 +343,7 @@ def run_decode(args, ws, rank, local, dist):
                                "k_gate_up<1> (routed gate/up + SwiGLU + q8)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "traffic": traffic, "algorithmic_bytes_per_launch": gu_bytes, "peak_source": peak_kind,
+                     "frac_of_nominal_7700": round(achieved / NOMINAL_HBM_GBS, 4),
                      "down_kernel_frac": round(dn_bytes / (float(dn.mean()) / 1e3) / 1e9 / hbm, 4)},
         # per layer: router (+top-k), gate/up, down, combine (+ the model-format shared expert's gate/up and down)
         "gpu_launches": args.steps * args.layers * (6 if model_sh else 4),
@@ -493,6 +497,7 @@ def run_ep_decode(args, ws, rank, local, dist):
         "roofline": {"kernel": "k_gate_up (expert-rank gate/up + SwiGLU + q8 on received rows)", "bound": "hbm",
                      "achieved": round(achieved_min, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved_min / hbm, 4),
                      "traffic": None, "algorithmic_bytes_per_launch": float(np.mean(gu_bytes)), "peak_source": peak_kind,
+                     "frac_of_nominal_7700": round(achieved_min / NOMINAL_HBM_GBS, 4),
                      "note": "min over ranks of the mean per-layer achieved bandwidth"},
         "e2e": {"value": round(n_e2e * ws / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": args.layers * 2 * HIDDEN * 4, "d2h_bytes_per_step": args.layers * HIDDEN * 4,
@@ -764,6 +769,7 @@ def run_prefill(args, ws, rank, local, dist):
                      "achieved": round(gemm_bytes / (g_ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(gemm_bytes / (g_ms / 1e3) / 1e9 / hbm, 4), "traffic": ncu_traffic("k_prefill_gemm", "prefill_T512"),
                      "algorithmic_bytes_per_launch": gemm_bytes, "peak_source": peak_kind,
+                     "frac_of_nominal_7700": round(gemm_bytes / (g_ms / 1e3) / 1e9 / NOMINAL_HBM_GBS, 4),
                      "tensor_tflops": round(flops * 0.999 / (g_ms / 1e3) / 1e12, 1), "tensor_peak_tflops": bf16},
         # this library's kernels per step (profiles/prefill_gemm_T512.md, prefill_real_model_formats_T512.md):
         # IQ2_XXS downs -- router, slots, gate B tiles, gate/up GEMM, down GEMM, combine; K-quant downs -- the
