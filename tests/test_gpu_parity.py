@@ -258,8 +258,8 @@ def _layer_case(moe, oracle, W, T, keep=8, n_group=1, topk_group=1, logits=None,
 
 
 def test_layer_config0_T16(moe, oracle, layer_weights):
-    """T=16, hidden 7168, 256 experts, top-8, shared expert."""
-    _layer_case(moe, oracle, layer_weights, 16)
+    """T=16, hidden 7168, 256 experts, top-8 with grouped routing (8 groups, top 4), shared expert."""
+    _layer_case(moe, oracle, layer_weights, 16, n_group=8, topk_group=4)
 
 
 @pytest.mark.parametrize("keep,n_group", [(8, 1), (2, 1), (8, 8), (2, 8)])
