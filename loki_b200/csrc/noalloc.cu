@@ -14,7 +14,8 @@
 //   * all calls share the one array and it keeps the last call's contents: calls that overlap on the GPU
 //     (two streams, or two host threads) race on it and must be serialised by the caller;
 //   * the kernel error word inside the array is cleared at the start of every call; everything else the
-//     kernels read is written earlier in the same call.
+//     kernels read is written earlier in the same call (y rows of absent entries -- negative ids -- are
+//     left stale, and the combine skips exactly those entries).
 #include <cstdio>
 #include <mutex>
 #include "../../include/loki_moe.h"
@@ -26,7 +27,10 @@ namespace {
 
 constexpr int NA_TOKENS = LK_NOALLOC_MAX_TOKENS;                  // 8
 constexpr int NA_ROWS = NA_TOKENS * MAX_TOPK + NA_TOKENS;         // routed entries + shared rows = 72
-constexpr int NA_SLOTS = NA_TOKENS * MAX_TOPK + NA_TOKENS + 8;    // >= max_slots_for(T, keep, 256, slot width of T, 1), T, keep <= 8
+// with single-token slots (slot width 1) every routed entry and every shared row is one slot, so a call uses
+// at most T*keep + T = 72 slots; 8 more are headroom
+constexpr int NA_SLOTS = NA_TOKENS * MAX_TOPK + NA_TOKENS + 8;
+static_assert(NA_SLOTS >= NA_TOKENS * MAX_TOPK + NA_TOKENS, "one slot per routed entry and per shared row");
 constexpr size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
 constexpr size_t OFF_ERR = 0;
 constexpr size_t OFF_NSLOTS = OFF_ERR + 256;
@@ -78,12 +82,13 @@ int scratch_for_current_device(unsigned char** out, int* nsm) {
 extern "C" int lk_moe_experts_noalloc(const LkMoeWeights* W, const float* x, const float* resid, int T, const int* sel,
                                       const float* w, int keep, int with_shared, float* h, float* moe, int* status,
                                       lk_stream_t stream) {
-    if (T < 1 || T > NA_TOKENS || keep < 1 || keep > MAX_TOPK) {
-        std::fprintf(stderr, "lk_moe_experts_noalloc: T=%d keep=%d outside the static scratch limits (1 <= T <= %d, 1 <= keep <= %d)\n",
+    if (!W || !x || !sel || !w || (h && !resid) || T < 0 || keep < 1) return LK_ERR_ARG;
+    if (T > NA_TOKENS || keep > MAX_TOPK) {
+        std::fprintf(stderr, "lk_moe_experts_noalloc: T=%d keep=%d outside the static scratch limits (T <= %d, keep <= %d)\n",
                      T, keep, NA_TOKENS, MAX_TOPK);
         return LK_ERR_CAPACITY;
     }
-    if (!W || !x || !sel || !w || (h && !resid)) return LK_ERR_ARG;
+    if (T == 0) return LK_OK;                         // as lk_moe_experts: nothing to do, status untouched
     if (W->down_fmt != LK_FMT_IQ2) return LK_ERR_UNSUPPORTED;
     if (with_shared && W->sh_fmt != 0 && W->sh_fmt != LK_FMT_IQ2) return LK_ERR_UNSUPPORTED;   // IQ2_XXS shared expert only
     const void* mats[] = { W->gate, W->up, W->down };
@@ -121,6 +126,7 @@ extern "C" int lk_moe_experts_noalloc(const LkMoeWeights* W, const float* x, con
         CombineParams cp{};
         cp.y = e.y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = with_shared ? 1 : 0; cp.shared = nullptr;
         cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN;
+        cp.sel = sel;                                 // absent entries (negative ids) own no y row: not summed
         launch_combine(cp, st);
     }
     if (status && cudaMemcpyAsync(status, err, sizeof(int), cudaMemcpyDeviceToDevice, st) != cudaSuccess) return LK_ERR_CUDA;
