@@ -19,8 +19,8 @@ LIB = os.path.join(HERE, "libloki_moe.so")
 # the engine-side replay harness (csrc/fl_replay.cpp): plain C++ against the fl_* ABI of LIB
 REPLAY_SRC = os.path.join(CSRC, "fl_replay.cpp")
 REPLAY_LIB = os.path.join(HERE, "libloki_replay.so")
-SOURCES = ["expert_gemv.cu", "expert_gemv1.cu", "aux_kernels.cu", "router.cu", "dispatch.cu", "prefill_gemm.cu", "moe_api.cu", "fl_abi.cu", "noalloc.cu", "ep.cu", "ep_comm.cu", "slot_mma.cu", "ep_p2p.cu", "expert_kq.cu", "shared_kq.cu", "kq_mma.cu"]
-HEADERS = ["moe_format.h", "moe_device.cuh", "moe_internal.h", "tcgen05.cuh", "iq2_grid.inc",
+SOURCES = ["expert_gemv.cu", "expert_gemv1.cu", "aux_kernels.cu", "router.cu", "dispatch.cu", "prefill_gemm.cu", "gate_up_q8.cu", "moe_api.cu", "fl_abi.cu", "noalloc.cu", "ep.cu", "ep_comm.cu", "slot_mma.cu", "ep_p2p.cu", "expert_kq.cu", "shared_kq.cu", "kq_mma.cu"]
+HEADERS = ["moe_format.h", "moe_device.cuh", "moe_internal.h", "tcgen05.cuh", "iq2_tc.cuh", "iq2_grid.inc",
            os.path.join("..", "..", "include", "loki_moe.h"), os.path.join("..", "..", "include", "loki_fused_moe.h"),
            os.path.join("..", "..", "include", "loki_ep.h")]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

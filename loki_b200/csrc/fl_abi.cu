@@ -48,10 +48,13 @@ struct FLCtx {
     // wide pass
     int wmax = 0, wke = 0;
     float* ncur_all = nullptr; float* base_all = nullptr; float* out_all = nullptr;
-    __half* wxh = nullptr; __half* whb = nullptr;   // the pass's rows and SwiGLU outputs in fp16 (mma.sync path)
-    int wxh_rows = 0;                               // rows of ncur_all already converted into wxh for this pass
+    __half* whb = nullptr;            // the pass's SwiGLU outputs: fp16 of the q8 values, one row per (row, k)
+    __half* wbt = nullptr;            // the q8 gate/up's activation tiles (gate_q8_tile_halfs(WIDE_SLOTS))
+    // per batch parity: the mma.sync down's slots (MM_NT tokens; w_*) and the q8 gate/up's slots (GEMM_NT
+    // tokens; g_*), device tables and their pinned host images (hw_tab: experts, tokens, outputs, count)
     int *w_expert[2] = {}, *w_tok[2] = {}, *w_out[2] = {}, *w_n[2] = {}, *w_cnt[2] = {}; float* w_w[2] = {};
-    int* hw_tab[2] = {}; float* hw_w[2] = {};
+    int *g_expert[2] = {}, *g_tok[2] = {}, *g_out[2] = {}, *g_n[2] = {}, *g_cnt[2] = {}; float* g_w[2] = {};
+    int* hw_tab[2] = {}; float* hw_w[2] = {}; int* hg_tab[2] = {}; float* hg_w[2] = {};
     float* h_wh = nullptr; float* h_wmoe = nullptr;
     float* wfin = nullptr;            // [2][wmax][HIDDEN]: fl_wide_finish's h and moe, fl_wide_skip's mo and h
     cudaEvent_t wev[2] = {}, em0 = nullptr, em1 = nullptr, ep0 = nullptr, ep1 = nullptr;
@@ -175,13 +178,14 @@ void fl_free(FLCtx* c) {
     if (c->st) cudaStreamSynchronize(c->st);
     void* d[] = { c->blk[0], c->blk[1], c->blk[2], c->blk[3], c->logits, c->probs, c->shared_y, c->sh_gu, c->sh_pair, c->mo,
                   c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n, c->counts, c->offsets, c->perm, c->hq, c->hd, c->y,
-                  c->ncur_all, c->base_all, c->out_all, c->wxh, c->whb, c->rcount, c->wfin };
+                  c->ncur_all, c->base_all, c->out_all, c->whb, c->wbt, c->rcount, c->wfin };
     for (void* p : d) if (p) cudaFree(p);
     for (int p = 0; p < 2; ++p) {
-        void* dd[] = { c->w_expert[p], c->w_tok[p], c->w_out[p], c->w_n[p], c->w_cnt[p], c->w_w[p] };
+        void* dd[] = { c->w_expert[p], c->w_tok[p], c->w_out[p], c->w_n[p], c->w_cnt[p], c->w_w[p],
+                       c->g_expert[p], c->g_tok[p], c->g_out[p], c->g_n[p], c->g_cnt[p], c->g_w[p] };
         for (void* q : dd) if (q) cudaFree(q);
-        if (c->hw_tab[p]) cudaFreeHost(c->hw_tab[p]);
-        if (c->hw_w[p]) cudaFreeHost(c->hw_w[p]);
+        void* hh[] = { c->hw_tab[p], c->hw_w[p], c->hg_tab[p], c->hg_w[p] };
+        for (void* q : hh) if (q) cudaFreeHost(q);
         if (c->wev[p]) cudaEventDestroy(c->wev[p]);
     }
     void* h[] = { c->hblk[0], c->hblk[1], c->hblk[2], c->hblk[3], c->h_in, c->h_wh, c->h_wmoe };
@@ -304,7 +308,6 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     c->prep_n = N;
     c->sh_pending = W->sh_gate && W->sh_up && W->sh_down && wrow < 0;
     c->sh_in_y_n = 0;                             // this prepare's shared expert supersedes the last one
-    if (wrow >= 0) c->wxh_rows = 0;               // rows of a wide pass change: their fp16 copy is redone
     c->sh_w[0] = W->sh_gate; c->sh_w[1] = W->sh_up; c->sh_w[2] = W->sh_down; c->sh_fmt = W->sh_fmt == FL_Q5K ? FL_Q5K : 0;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
@@ -571,15 +574,17 @@ int fl_wide_init(FLCtx* c, int wmax, int KE) {
     c->wmax = wmax; c->wke = KE;
     const size_t R = (size_t)wmax * HIDDEN;
     const size_t ent = (size_t)wmax * KE;
-    if (dz(&c->ncur_all, R) || dz(&c->base_all, R) || dz(&c->out_all, ent * HIDDEN) || dz(&c->wxh, R) ||
+    if (dz(&c->ncur_all, R) || dz(&c->base_all, R) || dz(&c->out_all, ent * HIDDEN) || dz(&c->wbt, gate_q8_tile_halfs(WIDE_SLOTS)) ||
         dz(&c->whb, ent * MOE_INTER) || dz(&c->wfin, 2 * R) || hz(&c->h_wh, R) || hz(&c->h_wmoe, R)) { fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0; }
-    c->wxh_rows = 0;
     for (int p = 0; p < 2; ++p) {
-        // room for WIDE_SLOTS slots of MM_NT tokens (the mma.sync path's layout)
-        const int e = WIDE_SLOTS * MM_NT;
+        // room for WIDE_SLOTS slots of MM_NT tokens (the down's layout) and of GEMM_NT tokens (the gate/up's):
+        // merging the engine's slots never makes more slots than it passed
+        const int e = WIDE_SLOTS * MM_NT, eg = WIDE_SLOTS * GEMM_NT;
         if (dz(&c->w_expert[p], WIDE_SLOTS) || dz(&c->w_tok[p], e) || dz(&c->w_out[p], e) || dz(&c->w_w[p], e) ||
             dz(&c->w_n[p], 1) || dz(&c->w_cnt[p], WIDE_SLOTS) || hz(&c->hw_tab[p], WIDE_SLOTS + 2 * e + 1) ||
-            hz(&c->hw_w[p], e) || cudaEventCreateWithFlags(&c->wev[p], cudaEventDisableTiming)) {
+            dz(&c->g_expert[p], WIDE_SLOTS) || dz(&c->g_tok[p], eg) || dz(&c->g_out[p], eg) || dz(&c->g_w[p], eg) ||
+            dz(&c->g_n[p], 1) || dz(&c->g_cnt[p], WIDE_SLOTS) || hz(&c->hg_tab[p], WIDE_SLOTS + 2 * eg + 1) ||
+            hz(&c->hw_w[p], e) || hz(&c->hg_w[p], eg) || cudaEventCreateWithFlags(&c->wev[p], cudaEventDisableTiming)) {
             fl_fail(c, LK_ERR_CUDA, "fl_wide_init: allocation failed"); return 0;
         }
     }
@@ -596,14 +601,16 @@ void fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, i
     cudaStream_t st = c->st;
     materialize_shared(c);
     const int64_t sg = (int64_t)EXPERT_GU_BYTES, sd = (int64_t)down_matrix_bytes(down_fmt);
-    // The engine's slots (<= NB (row, k) pairs of one expert each) merged, consecutive same-expert slots
-    // together, into the mma.sync path's slots of up to MM_NT tokens: IQ2_XXS gate/up decoded once per slot
-    // (slot_mma.cu), then the IQ2_XXS or K-quant (kq_mma.cu) down; h stays fp16.
+    // The engine's slots (<= NB (row, k) pairs of one expert each), consecutive same-expert slots merged:
+    // into slots of up to GEMM_NT tokens for the q8 gate/up (gate_up_q8.cu: tcgen05, the reference's numerics,
+    // h re-quantised to q8), and into slots of up to MM_NT tokens for the mma.sync down (IQ2_XXS slot_mma.cu or
+    // K-quant kq_mma.cu) that reads the q8 SwiGLU rows.
     for (int s0 = 0; s0 < nslots; s0 += WIDE_SLOTS) {
         const int ns = std::min(WIDE_SLOTS, nslots - s0);
         if (s0 > 0) FLCK(cudaStreamSynchronize(st));          // the tables of this parity are reused
         int* he = c->hw_tab[par]; int* ht = he + WIDE_SLOTS; int* ho = ht + WIDE_SLOTS * MM_NT; float* hw = c->hw_w[par];
-        int nout = 0, fill = 0, cur = -1, maxr = -1;
+        int* ge = c->hg_tab[par]; int* gt = ge + WIDE_SLOTS; int* go = gt + WIDE_SLOTS * GEMM_NT; float* gw = c->hg_w[par];
+        int nout = 0, fill = 0, cur = -1, gout = 0, gfill = 0, gcur = -1;
         for (int s = 0; s < ns; ++s) {
             const int m = midx[s0 + s];
             if (m < 0 || m >= nexp) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: slot expert out of range"); return; }
@@ -613,39 +620,52 @@ void fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, i
                 live += (r >= 0 && r < c->wmax && k >= 0 && k < KE) ? 1 : 0;
             }
             if (live == 0) continue;
-            if (m != cur || fill + live > MM_NT) {             // a new mma slot
+            if (m != cur || fill + live > MM_NT) {             // a new down slot
                 he[nout] = m; cur = m; fill = 0;
                 for (int i = 0; i < MM_NT; ++i) { ht[nout * MM_NT + i] = -1; ho[nout * MM_NT + i] = -1; hw[nout * MM_NT + i] = 0.f; }
                 ++nout;
             }
+            if (m != gcur || gfill + live > GEMM_NT) {         // a new gate/up slot
+                ge[gout] = m; gcur = m; gfill = 0;
+                for (int i = 0; i < GEMM_NT; ++i) { gt[gout * GEMM_NT + i] = -1; go[gout * GEMM_NT + i] = -1; gw[gout * GEMM_NT + i] = 0.f; }
+                ++gout;
+            }
             for (int i = 0; i < NB; ++i) {
                 const int r = rows[(size_t)(s0 + s) * NB + i], k = kidx[(size_t)(s0 + s) * NB + i];
                 if (!(r >= 0 && r < c->wmax && k >= 0 && k < KE)) continue;
-                const int q = (nout - 1) * MM_NT + fill++;
+                const int q = (nout - 1) * MM_NT + fill++, qg = (gout - 1) * GEMM_NT + gfill++;
                 ht[q] = r; ho[q] = r * KE + k; hw[q] = wk[(size_t)(s0 + s) * NB + i];
-                maxr = std::max(maxr, r);
+                gt[qg] = r; go[qg] = r * KE + k; gw[qg] = hw[q];
             }
         }
         if (nout == 0) continue;
         ho[nout * MM_NT] = nout;
+        go[gout * GEMM_NT] = gout;
         FLCK(cudaMemcpyAsync(c->w_expert[par], he, (size_t)nout * 4, cudaMemcpyHostToDevice, st));
         FLCK(cudaMemcpyAsync(c->w_tok[par], ht, (size_t)nout * MM_NT * 4, cudaMemcpyHostToDevice, st));
         FLCK(cudaMemcpyAsync(c->w_out[par], ho, (size_t)nout * MM_NT * 4, cudaMemcpyHostToDevice, st));
         FLCK(cudaMemcpyAsync(c->w_w[par], hw, (size_t)nout * MM_NT * 4, cudaMemcpyHostToDevice, st));
         FLCK(cudaMemcpyAsync(c->w_n[par], ho + nout * MM_NT, 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->g_expert[par], ge, (size_t)gout * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->g_tok[par], gt, (size_t)gout * GEMM_NT * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->g_out[par], go, (size_t)gout * GEMM_NT * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->g_w[par], gw, (size_t)gout * GEMM_NT * 4, cudaMemcpyHostToDevice, st));
+        FLCK(cudaMemcpyAsync(c->g_n[par], go + gout * GEMM_NT, 4, cudaMemcpyHostToDevice, st));
+        GemmParams g{};
+        g.gate = (const uint8_t*)gate; g.up = (const uint8_t*)up; g.gate_stride = sg; g.up_stride = sg;
+        g.x = c->ncur_all; g.ld_x = HIDDEN;
+        g.slot_expert = c->g_expert[par]; g.slot_tok = c->g_tok[par]; g.slot_out = c->g_out[par]; g.slot_w = c->g_w[par];
+        g.nslots = c->g_n[par]; g.max_slots = gout; g.slot_cnt = c->g_cnt[par]; g.bt = c->wbt; g.hb = c->whb; g.err = c->err;
+        launch_gate_up_q8(g, c->nsm, st);
         MmaParams m{};
-        m.gate = (const uint8_t*)gate; m.up = (const uint8_t*)up; m.down = (const uint8_t*)down;
-        m.gate_stride = sg; m.up_stride = sg; m.down_stride = sd;
-        m.x = c->ncur_all; m.ld_x = HIDDEN;
-        m.T = maxr + 1 > c->wxh_rows ? maxr + 1 : 0;          // the pass's rows into fp16 once (the prep kernel)
+        m.down = (const uint8_t*)down; m.down_stride = sd;
         m.slot_expert = c->w_expert[par]; m.slot_tok = c->w_tok[par]; m.slot_out = c->w_out[par]; m.slot_w = c->w_w[par];
         m.nslots = c->w_n[par]; m.max_slots = WIDE_SLOTS; m.slot_cnt = c->w_cnt[par];
-        m.xh = c->wxh; m.hb = c->whb; m.y = c->out_all; m.err = c->err;
-        if (m.T) c->wxh_rows = m.T;
+        m.hb = c->whb; m.y = c->out_all; m.err = c->err;
         if (down_fmt == FL_IQ2) {
-            launch_slot_mma(m, c->nsm, st);
+            launch_slot_mma_down(m, c->nsm, st);      // its prep pass writes slot_cnt
         } else {
-            launch_slot_mma_gate_up(m, c->nsm, st);
+            m.slot_cnt = nullptr;                     // the K-quant down counts each slot's tokens itself
             launch_kq_mma_down(m, down_fmt, c->nsm, st);
         }
     }

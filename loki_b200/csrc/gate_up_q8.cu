@@ -1,0 +1,418 @@
+// gate_up_q8.cu -- the gate/up + SwiGLU phase of the batch regimes (T >= the mma threshold) on the 5th-generation
+// tensor cores, with the reference's numerics: products as exact as its int8 group sums, then h re-quantised
+// to q8 per 32 (reference src/fused_layer.cu:334-341 swiglu_q8, as the wide pass uses it at :540-553).
+//
+// Why the products must be exact: the reference forms each 32-weight group sum in int32 (q8 x against the
+// IQ2 grid values) and scales it in float, then quantises h = silu(g)*u to q8.  A product that differs from
+// it by fp16 operand rounding (~2.4e-4 per element, the plain fp16 GEMM's error) moves h across q8 rounding
+// boundaries, and those flips alone cost ~2-3e-3 relative L2 in the layer output.  Here:
+//   * A (weights) = v * (2*scale + 1), an integer of at most 43*31 = 1333: exact in fp16.  The decode is the
+//     byte-permute + hfma2 of iq2_tc.cuh with s = 2*scale + 1 (1024*s exact, the fma result an exact
+//     integer).  The superblock's d/8 is applied outside the MMA, per superblock (below).
+//   * B (activations) = the q8-dequantised x, q*dx in fp32, as two fp16 rows: hi = fp16(q*dx) and
+//     lo = fp16(q*dx - hi).  hi + lo carries ~22 bits; products with the 11-bit A are exact in the fp32
+//     accumulator.  The two rows sit side by side along N, so one MMA of N' = 2N covers both.
+//   * Per superblock (256 weights, 2 K-blocks) the MMA accumulates P = sum A*B into a fresh TMEM buffer (two
+//     buffers alternate); epilogue warps fold R += (d/8) * (P_hi + P_lo) into a running sum R in TMEM.
+//   * After the last superblock, R is g (rows 0-63 of the tile) or u (rows 64-127); the epilogue forms
+//     h = silu(g)*u, quantises it per 32 (d = amax/127, round half even: quant_q8_group bit for bit) and
+//     writes fp16(q*d) -- exactly representable up to fp16 rounding of the product -- as the down's input:
+//     the down GEMM's B tiles (p.ht) or fp16 rows (p.hb) for the K-quant downs.
+//
+// Work item = (slot s, h tile rt of 64 rows, token half nh): M = 128 weight rows (64 gate rows + the same 64
+// up rows), N = up to 64 tokens (a slot of up to GEMM_NT = 128 tokens is two halves; the second is skipped
+// when the slot holds <= 64).  TMEM (512 columns): A stages [0,128) (2 x 64), R [128,192), P buffers
+// [256,384) and [384,512) (2N <= 128 each).
+//
+// Warp roles (736 threads, one CTA per SM, persistent over items):
+//   warps 0-15  decode: warp w = TMEM lane quarter w&3 (rows 32*(w&3)..), group w>>2 of each K-block; writes
+//               its 32 fp16 A values per K-block to tensor memory with tcgen05.st
+//   warp 16     MMA issuer (whole warp, warp-uniform operands, elect.sync issues), 8 MMAs per K-block; at a
+//               superblock's first K-block it waits for its P buffer to be drained, at its last it commits
+//   warp 17     B K-block tiles (hi and lo rows of the item's token half) by 1-D TMA bulk copies
+//   warp 18     raw superblocks: each weight row's next IQ2 superblock (80-byte 16-aligned window, 16-byte
+//               cp.async, coalesced) into a 4-stage raw ring
+//   warps 19-22 epilogue: warp w = lane quarter w&3; per superblock the P -> R fold, per item SwiGLU + q8
+// Every wait is bounded (moe_device.cuh); a timed-out wait records an error code and the CTA unwinds.
+#include "moe_internal.h"
+#include "moe_device.cuh"
+#include "tcgen05.cuh"
+#include "iq2_tc.cuh"
+
+namespace lk {
+
+namespace {
+
+constexpr int GQ_M = 128;                       // weight rows per item: 64 gate + 64 up
+constexpr int GQ_H = 64;                        // h rows per item
+constexpr int GQ_TILES = MOE_INTER / GQ_H;      // 32
+constexpr int GQ_NH = 64;                       // tokens per item (half of a GEMM_NT slot)
+constexpr int GQ_KB = 128;                      // K per stage
+constexpr int GQ_NKB = HIDDEN / GQ_KB;          // 56
+constexpr int GQ_NSB = HIDDEN / QK;             // 28 superblocks per row
+constexpr int GQ_NST = 2;
+constexpr int GQ_DWARPS = 16;
+constexpr int GQ_MMA_WARP = GQ_DWARPS, GQ_COPY_WARP = GQ_DWARPS + 1, GQ_RAW_WARP = GQ_DWARPS + 2;
+constexpr int GQ_EPI_WARP0 = GQ_DWARPS + 3, GQ_EWARPS = 4;
+constexpr int GQ_THREADS = (GQ_EPI_WARP0 + GQ_EWARPS) * 32;     // 736
+constexpr int GQ_B_HALF = 2 * GQ_NH * GQ_KB * 2;                // 32 KB: hi + lo rows of one half, N = 64
+constexpr int GQ_RAW_ROWB = 80;
+constexpr int GQ_RAW_STAGE = GQ_M * GQ_RAW_ROWB;                // 10 KB
+constexpr int GQ_RAW_NST = 4;
+constexpr int GQ_XS = GQ_NH + 1;                                // exchange row stride (floats)
+constexpr int GQ_OFF_GTAB = 0;
+constexpr int GQ_OFF_STAB = GQ_OFF_GTAB + IQ2TC_GTAB;
+constexpr int GQ_OFF_B = GQ_OFF_STAB + IQ2TC_STAB;
+constexpr int GQ_OFF_RAW = GQ_OFF_B + GQ_NST * GQ_B_HALF;
+constexpr int GQ_OFF_X = GQ_OFF_RAW + GQ_RAW_NST * GQ_RAW_STAGE + 64;   // + slack for the last row's over-read
+constexpr int GQ_OFF_BAR = GQ_OFF_X + GQ_H * GQ_XS * 4;
+constexpr int GQ_NBAR = 2 * GQ_NST + 4 + 1 + 2 * GQ_RAW_NST;
+constexpr int GQ_OFF_ROWP = GQ_OFF_BAR + GQ_NBAR * 8;
+constexpr int GQ_OFF_MISC = GQ_OFF_ROWP + GQ_M * 8;
+constexpr int GQ_SMEM_USED = GQ_OFF_MISC + 32;
+constexpr int GQ_SMEM = 232448;                                 // all of it: one CTA per SM (all 512 TMEM columns)
+static_assert(GQ_SMEM_USED <= GQ_SMEM, "shared memory layout exceeds the allocation");
+static_assert(GQ_OFF_B % 1024 == 0 && GQ_B_HALF % 1024 == 0, "B stages 16-byte (bulk copy) aligned");
+constexpr uint32_t GQ_TMEM_COLS = 512;
+constexpr uint32_t GQ_A_COLS = GQ_KB / 2;       // 64 per stage: 128 fp16 K values
+constexpr uint32_t GQ_R_COL = 128, GQ_P_COL = 256, GQ_P_COLS = 128;
+static_assert(GQ_NST * GQ_A_COLS <= GQ_R_COL && GQ_R_COL + GQ_NH <= GQ_P_COL && GQ_P_COL + 2 * GQ_P_COLS <= GQ_TMEM_COLS,
+              "tensor memory layout");
+constexpr int GQ_EPI_BAR = 1;                   // named barrier of the 4 epilogue warps
+
+__device__ __forceinline__ void tmem_st16f(uint32_t taddr, const float (&v)[16]) {
+    uint32_t r[16];
+    #pragma unroll
+    for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(v[i]);
+    tmem_st16(taddr, r);
+}
+
+// global weight row r (0..127) of item (expert e, h tile rt): rows 0-63 gate rows rt*64.., 64-127 the up rows
+__device__ __forceinline__ const uint8_t* gq_row(const GemmParams& p, int e, int rt, int r) {
+    const int mat = r >> 6, row = rt * GQ_H + (r & (GQ_H - 1));
+    const uint8_t* wm = e == SHARED_SLOT ? (mat ? p.sh_up : p.sh_gate)
+                                         : (mat ? p.up + (size_t)e * p.up_stride : p.gate + (size_t)e * p.gate_stride);
+    return wm + (size_t)row * ((HIDDEN / QK) * BLK_IQ2);
+}
+
+// item -> (slot, h tile, token half); false when the half holds no token
+__device__ __forceinline__ bool gq_item(const GemmParams& p, int item, int nslots, int& s, int& rt, int& nh, int& cnt_h) {
+    s = item % nslots;
+    const int rest = item / nslots;
+    rt = rest >> 1; nh = rest & 1;
+    cnt_h = p.slot_cnt[s] - GQ_NH * nh;
+    cnt_h = cnt_h > GQ_NH ? GQ_NH : cnt_h;
+    return cnt_h > 0;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint2* gtab = (const uint2*)(smem + GQ_OFF_GTAB);
+    const uint2* stab = (const uint2*)(smem + GQ_OFF_STAB);
+    uint8_t* bring = smem + GQ_OFF_B;
+    uint8_t* raw = smem + GQ_OFF_RAW;
+    float* xchg = (float*)(smem + GQ_OFF_X);
+    uint64_t* bars = (uint64_t*)(smem + GQ_OFF_BAR);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + GQ_NST;
+    uint64_t* pfull = bars + 2 * GQ_NST;
+    uint64_t* pempty = pfull + 2;
+    uint64_t* drain = pempty + 2;
+    uint64_t* rawfull = drain + 1;
+    uint64_t* rawempty = rawfull + GQ_RAW_NST;
+    uintptr_t* rowp = (uintptr_t*)(smem + GQ_OFF_ROWP);
+    uint32_t* tmem_slot = (uint32_t*)(smem + GQ_OFF_MISC);
+    volatile int* abort_flag = (volatile int*)(smem + GQ_OFF_MISC + 4);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nslots = *p.nslots;
+    const int nitems = nslots * GQ_TILES * 2;
+    if ((int)blockIdx.x >= nitems) return;
+
+    init_pair_tables((uint2*)(smem + GQ_OFF_GTAB), (uint2*)(smem + GQ_OFF_STAB), tid, GQ_THREADS);
+    if (tid == 0) {
+        *abort_flag = 0;
+        // full: 16 decode-warp arrivals + the copy warp's expect_tx arrival (B bytes)
+        for (int s = 0; s < GQ_NST; ++s) { mbar_init(&full[s], GQ_DWARPS + 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&pfull[b], 1); mbar_init(&pempty[b], GQ_EWARPS); }
+        mbar_init(drain, 1);
+        for (int s = 0; s < GQ_RAW_NST; ++s) { mbar_init(&rawfull[s], 32); mbar_init(&rawempty[s], GQ_DWARPS); }
+        fence_mbar_init();
+    }
+    if (warp == GQ_MMA_WARP) { tmem_alloc(tmem_slot, GQ_TMEM_COLS); tmem_relinquish(); }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == GQ_RAW_WARP) {
+        // ---------------------------------------------------------------- raw superblocks
+        uint32_t rit = 0;
+        const int rsub = lane / 5, chunk = lane - 5 * (lane / 5);
+        for (int item = blockIdx.x; item < nitems && !*abort_flag; item += gridDim.x) {
+            int s, rt, nh, cnt_h;
+            if (!gq_item(p, item, nslots, s, rt, nh, cnt_h)) continue;
+            const int e = p.slot_expert[s];
+            __syncwarp();
+            for (int r = lane; r < GQ_M; r += 32) rowp[r] = (uintptr_t)gq_row(p, e, rt, r);
+            __syncwarp();
+            for (int sb = 0; sb < GQ_NSB; ++sb, ++rit) {
+                const int rs = rit % GQ_RAW_NST;
+                if (!mbar_wait_backoff(&rawempty[rs], ((rit / GQ_RAW_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
+                uint8_t* dst = raw + rs * GQ_RAW_STAGE;
+                const size_t sboff = (size_t)sb * BLK_IQ2;
+                if (lane < 30) {                      // lane -> (row rsub of 6, 16-byte chunk of 5)
+                    #pragma unroll 4
+                    for (int r = rsub; r < GQ_M; r += 6) {
+                        const uintptr_t a = (rowp[r] + sboff) & ~(uintptr_t)15;
+                        cp_async16(dst + r * GQ_RAW_ROWB + chunk * 16, (const void*)(a + 16 * chunk));
+                    }
+                }
+                cp_async_mbar_arrive(&rawfull[rs]);
+            }
+        }
+        cp_async_wait_all();
+    } else if (warp == GQ_COPY_WARP) {
+        // ---------------------------------------------------------------- B tiles (one bulk copy per K-block)
+        uint32_t it = 0;
+        if (lane == 0) {
+            for (int item = blockIdx.x; item < nitems && !*abort_flag; item += gridDim.x) {
+                int s, rt, nh, cnt_h;
+                if (!gq_item(p, item, nslots, s, rt, nh, cnt_h)) continue;
+                const uint32_t bytes = (uint32_t)(2 * round16(cnt_h)) * GQ_KB * 2;
+                for (int kb = 0; kb < GQ_NKB; ++kb, ++it) {
+                    const int st = it % GQ_NST;
+                    if (!mbar_wait_backoff(&empty[st], ((it / GQ_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
+                    mbar_arrive_expect_tx(&full[st], bytes);
+                    bulk_g2s(bring + st * GQ_B_HALF, p.bt + (((size_t)s * GQ_NKB + kb) * 2 + nh) * (GQ_B_HALF / 2), bytes, &full[st]);
+                }
+                if (*abort_flag) break;
+            }
+            // every bulk copy issued must land before the CTA may exit
+            const uint32_t first = it > GQ_NST ? it - GQ_NST : 0;
+            for (uint32_t j = first; j < it; ++j) mbar_wait_backoff(&full[j % GQ_NST], (j / GQ_NST) & 1, nullptr, 0);
+        }
+    } else if (warp == GQ_MMA_WARP) {
+        // ---------------------------------------------------------------- MMA issuer (the whole warp, elect.sync)
+        uint32_t it = 0, psb = 0; int issued = 0;
+        const uint32_t bring_s = smem_u32(bring);
+        bool ok = true;
+        for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
+            int s, rt, nh, cnt_h;
+            if (!gq_item(p, item, nslots, s, rt, nh, cnt_h)) continue;
+            const int N2 = __shfl_sync(0xffffffffu, 2 * round16(cnt_h), 0);       // hi rows then lo rows
+            const uint32_t idesc = idesc_f16_f32(GQ_M, N2);
+            const uint32_t lbo = (uint32_t)(N2 >> 3) * 128;
+            const uint64_t bstep = (uint64_t)((2 * lbo) >> 4);                    // one K=16 step along the B tile
+            for (int kb = 0; kb < GQ_NKB; ++kb, ++it) {
+                const int st = it % GQ_NST;
+                const uint32_t b = psb & 1;
+                if ((kb & 1) == 0 &&
+                    !__all_sync(0xffffffffu, mbar_wait_backoff(&pempty[b], ((psb >> 1) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY))) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, mbar_wait_backoff(&full[st], (it / GQ_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))) { ok = false; break; }
+                tc_fence_after();
+                const uint64_t b0 = umma_desc(bring_s + st * GQ_B_HALF, lbo, 128);
+                const uint32_t a0 = tmem + st * GQ_A_COLS;
+                const uint32_t d = tmem + GQ_P_COL + b * GQ_P_COLS;
+                #pragma unroll
+                for (int ks = 0; ks < GQ_KB / 16; ++ks)
+                    umma_f16_ta_warp(d, a0 + ks * 8, b0 + (uint64_t)ks * bstep, idesc, ((kb & 1) | ks) != 0);
+                umma_commit_warp(&empty[st]);
+                issued = 1;
+                if (kb & 1) { umma_commit_warp(&pfull[b]); ++psb; }
+            }
+        }
+        if (!ok && lane == 0) *abort_flag = 1;
+        if (issued) {                                 // every issued MMA has completed before teardown
+            umma_commit_warp(drain);
+            mbar_wait_backoff(drain, 0, nullptr, 0);
+        }
+    } else if (warp < GQ_DWARPS) {
+        // ---------------------------------------------------------------- decode warps
+        const int q = warp & 3, gsel = warp >> 2;
+        const int row = 32 * q + lane;                                      // weight row of the item = TMEM lane
+        const uint2* gtl = gtab + lane;
+        const uint2* stl = stab + lane;
+        const uint8_t* rrow0 = raw + row * GQ_RAW_ROWB;
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        uint32_t it = 0, rit = 0;
+        for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+            int s, rt, nh, cnt_h;
+            if (!gq_item(p, item, nslots, s, rt, nh, cnt_h)) continue;
+            const int e = p.slot_expert[s];
+            const uint32_t wlo = (uint32_t)(uintptr_t)gq_row(p, e, rt, row);
+            for (int kb = 0; kb < GQ_NKB; ++kb, ++it) {
+                const int st = it % GQ_NST, rs = rit % GQ_RAW_NST;
+                if ((kb & 1) == 0 && !*abort_flag && !mbar_wait_backoff(&rawfull[rs], (rit / GQ_RAW_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))
+                    *abort_flag = 1;
+                const uint8_t* rrow = rrow0 + rs * GQ_RAW_STAGE;
+                const int delta = (int)((wlo + (uint32_t)(kb >> 1) * BLK_IQ2) & 15u);   // superblock offset in its window
+                const int g0 = (kb & 1) * 4 + gsel;                         // this thread's group in the superblock
+                uint32_t aux0, aux1;
+                load_group_smem(rrow, delta + 2 + 8 * g0, aux0, aux1);
+                // A = v * (2*scale + 1): integers <= 1333, exact in fp16; d/8 is applied per superblock
+                const uint32_t sc = 2u * (aux1 >> 28) + 1u;
+                const uint32_t s2 = (uint32_t)__half_as_ushort(__uint2half_rn(sc)) * 0x10001u;
+                const uint32_t c2 = (uint32_t)__half_as_ushort(__uint2half_rn(1024u * sc)) * 0x10001u ^ 0x80008000u;
+                uint32_t o[16];
+                decode_group_f16_s(aux0, aux1, s2, c2, gtl, stl, o);
+                if (!*abort_flag && !mbar_wait_backoff(&empty[st], ((it / GQ_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) *abort_flag = 1;
+                tc_fence_after();
+                tmem_st16(tmem + lane_base + st * GQ_A_COLS + gsel * 16, o);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&full[st]);
+                    if (kb & 1) mbar_arrive(&rawempty[rs]);
+                }
+                if (kb & 1) ++rit;
+                if (*abort_flag) break;
+            }
+            if (*abort_flag) break;
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue warps
+        const int q = warp & 3;                                             // TMEM lane quarter of this warp
+        const int row = 32 * q + lane, mat = q >> 1, j = 32 * (q & 1) + lane;   // j: h row in the tile
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        const uint32_t tR = tmem + lane_base + GQ_R_COL;
+        uint32_t psb = 0;
+        bool bad = false;
+        for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+            int s, rt, nh, cnt_h;
+            if (!gq_item(p, item, nslots, s, rt, nh, cnt_h)) continue;
+            const int e = p.slot_expert[s];
+            const int n16 = round16(cnt_h);
+            const __half* dptr = (const __half*)gq_row(p, e, rt, row);      // the superblock scales d of this row
+            float dnext = __half2float(dptr[0]);
+            for (int sb = 0; sb < GQ_NSB; ++sb, ++psb) {
+                const float dw = dnext * 0.125f;                            // d * (0.5 + scale) * 0.25 = d/8 * A's factor
+                if (sb + 1 < GQ_NSB) dnext = __half2float(dptr[(size_t)(sb + 1) * (BLK_IQ2 / 2)]);
+                const uint32_t b = psb & 1;
+                if (!bad && (*abort_flag || !mbar_wait_backoff(&pfull[b], (psb >> 1) & 1, p.err, DEV_ERR_TIMEOUT_FULL))) bad = true;
+                if (!bad) {
+                    tc_fence_after();
+                    const uint32_t tP = tmem + lane_base + GQ_P_COL + b * GQ_P_COLS;
+                    for (int c0 = 0; c0 < n16; c0 += 16) {
+                        float hi[16], lo[16], r[16];
+                        tmem_ld16(tP + c0, hi);
+                        tmem_ld16(tP + n16 + c0, lo);
+                        if (sb == 0) {
+                            #pragma unroll
+                            for (int i = 0; i < 16; ++i) r[i] = dw * (hi[i] + lo[i]);
+                        } else {
+                            tmem_ld16(tR + c0, r);
+                            #pragma unroll
+                            for (int i = 0; i < 16; ++i) r[i] = fmaf(dw, hi[i] + lo[i], r[i]);
+                        }
+                        if (sb + 1 < GQ_NSB || mat == 0) {
+                            tmem_st16f(tR + c0, r);                         // running sum (g kept here at the end)
+                        } else {                                            // final u -> the exchange for SwiGLU
+                            #pragma unroll
+                            for (int i = 0; i < 16; ++i) xchg[j * GQ_XS + c0 + i] = r[i];
+                        }
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                }
+                __syncwarp();
+                if (lane == 0 && !bad) mbar_arrive(&pempty[b]);
+            }
+            // ------------------------------------------------ item epilogue: h = silu(g)*u, q8 per 32, fp16(q*d) out
+            if (named_bar_or(GQ_EPI_BAR, GQ_EWARPS * 32, bad)) break;
+            if (mat == 0) {
+                const int hj = rt * GQ_H + j;                                  // h row of this lane
+                const int n16s = round16(p.slot_cnt[s]);                      // the down's N for the whole slot
+                for (int c0 = 0; c0 < n16; c0 += 16) {
+                    float g[16];
+                    tc_fence_after();
+                    tmem_ld16(tR + c0, g);
+                    #pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int n = c0 + i;
+                        if (n >= cnt_h) break;                                 // warp-uniform
+                        const float h = lk_swiglu(g[i], xchg[j * GQ_XS + n]);
+                        float amax = fabsf(h);
+                        #pragma unroll
+                        for (int o = 16; o >= 1; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                        const float dq = amax / 127.0f, id = dq > 0.0f ? 1.0f / dq : 0.0f;
+                        const __half hv = __float2half_rn((float)__float2int_rn(h * id) * dq);
+                        const int ng = GQ_NH * nh + n;                         // token position in the slot
+                        if (p.hb) {
+                            const int out = p.slot_out[s * GEMM_NT + ng];
+                            if (out >= 0) p.hb[(size_t)out * MOE_INTER + hj] = hv;
+                        } else {
+                            uint8_t* tile = (uint8_t*)(p.ht + ((size_t)s * (MOE_INTER / GQ_KB) + hj / GQ_KB) * (GEMM_NT * GQ_KB));
+                            *(__half*)(tile + btile_off(ng, hj % GQ_KB, n16s)) = hv;
+                        }
+                    }
+                }
+            }
+            if (named_bar_or(GQ_EPI_BAR, GQ_EWARPS * 32, bad)) break;       // the exchange is free again
+        }
+        if (bad) *abort_flag = 1;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == GQ_MMA_WARP) { tc_fence_after(); tmem_dealloc(tmem, GQ_TMEM_COLS); }
+}
+
+// gate/up B tiles with the q8 numerics: for slot s, K-block kb and token half nh, the q8-dequantised x of the
+// half's tokens (q * dx in fp32, quant_q8_group) as hi rows fp16(v) then lo rows fp16(v - hi), in the UMMA
+// K-major core-matrix layout of 2 * round16(half count) rows (pad rows zero); also the slot's token count
+constexpr int GQ_BT_THREADS = GEMM_NT * (GQ_KB / 32);   // one thread per (token row, 32-group of the K-block)
+__global__ void __launch_bounds__(GQ_BT_THREADS) k_gate_b_tiles_q8(GemmParams p) {
+    const int s = blockIdx.x, kb = blockIdx.y, tid = threadIdx.x;
+    if (s >= *p.nslots) return;
+    const int n = tid / (GQ_KB / 32), g = tid % (GQ_KB / 32);     // token row, 32-group within the K-block
+    const int tok = p.slot_tok[s * GEMM_NT + n];
+    const int cnt = __syncthreads_count(tok >= 0) / (GQ_KB / 32);   // pads are at the end of the slot
+    if (kb == 0 && tid == 0) p.slot_cnt[s] = cnt;
+    const int nh = n / GQ_NH, nl = n % GQ_NH;
+    int cnt_h = cnt - GQ_NH * nh;
+    cnt_h = cnt_h > GQ_NH ? GQ_NH : cnt_h;
+    if (cnt_h <= 0) return;
+    const int n16 = round16(cnt_h);
+    if (nl >= n16) return;
+    float v[32];
+    if (tok >= 0) {
+        const float4* src = (const float4*)(p.x + (size_t)tok * p.ld_x + kb * GQ_KB + g * 32);
+        #pragma unroll
+        for (int j = 0; j < 8; ++j) { const float4 a = src[j]; v[4*j] = a.x; v[4*j+1] = a.y; v[4*j+2] = a.z; v[4*j+3] = a.w; }
+    } else {
+        #pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+    }
+    int8_t qv[32];
+    const float d = quant_q8_group(v, qv);
+    uint8_t* tile = (uint8_t*)(p.bt + (((size_t)s * GQ_NKB + kb) * 2 + nh) * (GQ_B_HALF / 2));
+    #pragma unroll
+    for (int c = 0; c < 4; ++c) {                        // 4 k8 blocks of 8 fp16 (16 bytes) each
+        uint32_t whi[4], wlo[4];
+        #pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const int j = c * 8 + 2 * h;
+            const float a0 = (float)qv[j] * d, a1 = (float)qv[j + 1] * d;
+            const __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
+            const __half l0 = __float2half_rn(a0 - __half2float(h0)), l1 = __float2half_rn(a1 - __half2float(h1));
+            whi[h] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            wlo[h] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        *(uint4*)(tile + btile_off(nl, g * 32 + c * 8, 2 * n16)) = make_uint4(whi[0], whi[1], whi[2], whi[3]);
+        *(uint4*)(tile + btile_off(n16 + nl, g * 32 + c * 8, 2 * n16)) = make_uint4(wlo[0], wlo[1], wlo[2], wlo[3]);
+    }
+}
+
+void launch_gate_up_q8(const GemmParams& p, int grid, cudaStream_t st) {
+    static bool attr = false;
+    if (!attr) { cudaFuncSetAttribute(k_gate_up_q8, cudaFuncAttributeMaxDynamicSharedMemorySize, GQ_SMEM); attr = true; }
+    k_gate_b_tiles_q8<<<dim3(p.max_slots, GQ_NKB), GQ_BT_THREADS, 0, st>>>(p);
+    k_gate_up_q8<<<grid, GQ_THREADS, GQ_SMEM, st>>>(p);
+}
+
+size_t gate_q8_tile_halfs(int max_slots) { return (size_t)max_slots * GQ_NKB * 2 * (GQ_B_HALF / 2); }
+
+}  // namespace lk

@@ -34,12 +34,14 @@ struct LkMoeCtx {
     // stream capture: fp16 weights (88 MB), fp16 x and h rows, a cuBLAS handle and its workspace
     int sh_gemm_min = 16; __half* shw16 = nullptr; __half* shx16 = nullptr; __half* shh16 = nullptr;
     void* blas = nullptr; void* blas_ws = nullptr;
-    // tensor-core path (T >= gemm_min_tokens): 64-token slots and fp16 operand staging
+    // batch regimes (T >= mma_min_tokens): the q8 gate/up on GEMM_NT-token slots (bt: its hi/lo activation
+    // tiles), the IQ2_XXS down on tcgen05 from gemm_min_tokens (ht: its B tiles)
     int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
     __half* bt = nullptr; __half* ht = nullptr; int* g_cnt = nullptr; int gemm_min_tokens = 192;
-    // register-fed mma.sync path (mma_min_tokens <= T < gemm_min_tokens): MM_NT-token slots, fp16 activations
+    // the mma.sync downs (IQ2_XXS below gemm_min_tokens, K-quant always): MM_NT-token slots reading the fp16
+    // q8 SwiGLU rows hb
     int* m_expert = nullptr; int* m_tok = nullptr; int* m_out = nullptr; float* m_w = nullptr; int* m_n = nullptr;
-    int* m_cnt = nullptr; int m_max = 0; __half* xh = nullptr; __half* hb = nullptr; int mma_min_tokens = 48;
+    int* m_cnt = nullptr; int m_max = 0; __half* hb = nullptr; int mma_min_tokens = 48;
     // defaults from a per-layer sweep (keep 8, uniform routing): single-token dp4a matvecs fastest up to ~32
     // tokens (T=32: 1.67 ms vs 2.03 mma, 2.23 tcgen05), mma.sync from 48 (T=64: 2.65 vs 3.24 / 2.96 ms,
     // T=128: 3.26 vs 3.56 tcgen05), tcgen05 from 192 (T=256: 3.84 vs 4.13 mma; T=512: 4.31 vs 6.26)
@@ -143,13 +145,13 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     c->g_max = max_slots_for(T, KE, NE, GEMM_NT, cfg->with_shared);
     LK_CU(dalloc(&c->g_expert, c->g_max)); LK_CU(dalloc(&c->g_tok, (size_t)c->g_max * GEMM_NT));
     LK_CU(dalloc(&c->g_out, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_w, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_n, 1));
-    LK_CU(dalloc(&c->bt, gemm_tile_halfs(c->g_max, false))); LK_CU(dalloc(&c->ht, gemm_tile_halfs(c->g_max, true)));
+    LK_CU(dalloc(&c->bt, gate_q8_tile_halfs(c->g_max))); LK_CU(dalloc(&c->ht, gemm_tile_halfs(c->g_max, true)));
     LK_CU(dalloc(&c->g_cnt, c->g_max));
     c->m_max = max_slots_for(T, KE, NE, MM_NT, cfg->with_shared);
     LK_CU(dalloc(&c->m_expert, c->m_max)); LK_CU(dalloc(&c->m_tok, (size_t)c->m_max * MM_NT));
     LK_CU(dalloc(&c->m_out, (size_t)c->m_max * MM_NT)); LK_CU(dalloc(&c->m_w, (size_t)c->m_max * MM_NT)); LK_CU(dalloc(&c->m_n, 1));
     LK_CU(dalloc(&c->m_cnt, c->m_max));
-    LK_CU(dalloc(&c->xh, (size_t)T * HIDDEN)); LK_CU(dalloc(&c->hb, rows * MOE_INTER));
+    LK_CU(dalloc(&c->hb, rows * MOE_INTER));
     if (cfg->with_shared) {
         LK_CU(dalloc(&c->shgu, (size_t)T * 2 * MOE_INTER));
         LK_CU(dalloc(&c->shpair, (size_t)T * (MOE_INTER / 32)));
@@ -167,7 +169,7 @@ void lk_moe_destroy(LkMoeCtx* c) {
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
                      c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->xq, c->xqn, c->xd,
                      c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt,
-                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->xh, c->hb, c->shgu, c->shpair };
+                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->hb, c->shgu, c->shpair };
     for (void* p : ptrs) if (p) cudaFree(p);
     if (c->blas) cublasDestroy((cublasHandle_t)c->blas);
     void* gp[] = { c->shw16, c->shx16, c->shh16, c->blas_ws };
@@ -267,9 +269,13 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
     return LK_OK;
 }
 
-// the tensor-core path: 64-token slots, q8->fp16 activations, gate/up GEMM + SwiGLU, down GEMM, combine
-static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
-                         const float* w, int keep, float* h, float* moe, cudaStream_t st) {
+// the batch regimes (T >= the mma threshold): the gate/up + SwiGLU phase on tcgen05 with the reference's q8
+// numerics (gate_up_q8.cu) on slots of up to GEMM_NT tokens, then the down: IQ2_XXS from the GEMM threshold on
+// tcgen05 (its B tiles written by the gate/up epilogue), below it on mma.sync (MM_NT-token slots reading the
+// fp16 q8 rows hb); K-quant downs on kq_mma.cu's mma.sync kernel (MM_NT-token slots, hb); then the combine
+static int run_batch_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
+                          const float* w, int keep, float* h, float* moe, cudaStream_t st) {
+    const bool tc_down = W->down_fmt == LK_FMT_IQ2 && T >= c->gemm_min_tokens;
     SlotParams s{};
     s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = GEMM_NT; s.with_shared = c->rs;
     s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
@@ -283,58 +289,27 @@ static int run_gemm_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int
     g.x = x; g.ld_x = ld_x; g.T = T;
     g.slot_expert = c->g_expert; g.slot_tok = c->g_tok; g.slot_out = c->g_out; g.slot_w = c->g_w; g.nslots = c->g_n;
     g.max_slots = c->g_max; g.slot_cnt = c->g_cnt; g.bt = c->bt; g.ht = c->ht; g.y = c->y; g.err = c->err;
+    g.hb = tc_down ? nullptr : c->hb;
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
-    if (W->down_fmt == LK_FMT_IQ2) {
-        launch_prefill_gemm(g, c->nsm, st);
-    } else {   // K-quant downs: the tcgen05 gate/up GEMM writes fp16 SwiGLU rows, the mma.sync K-quant down reads them
-        g.hb = c->hb;
-        launch_prefill_gemm_gate_up(g, c->nsm, st);
-        SlotParams ms{};
-        ms.sel = sel; ms.w = w; ms.T = T; ms.keep = keep; ms.n_experts = c->cfg.n_experts; ms.nt = MM_NT; ms.with_shared = c->rs;
-        ms.counts = c->counts; ms.offsets = c->offsets; ms.perm = c->perm;
-        ms.slot_expert = c->m_expert; ms.slot_tok = c->m_tok; ms.slot_out = c->m_out; ms.slot_w = c->m_w; ms.nslots = c->m_n;
-        ms.max_slots = c->m_max; ms.err = c->err; ms.sh_t0 = c->sh_t0; ms.sh_n = c->sh_n;
+    launch_gate_up_q8(g, c->nsm, st);
+    if (c->ev[1]) LK_CU(record_event(c->ev[1], st));
+    if (tc_down) {
+        launch_prefill_gemm_down(g, c->nsm, st);
+    } else {
+        SlotParams ms = s;
+        ms.nt = MM_NT; ms.slot_expert = c->m_expert; ms.slot_tok = c->m_tok; ms.slot_out = c->m_out; ms.slot_w = c->m_w;
+        ms.nslots = c->m_n; ms.max_slots = c->m_max;
         launch_build_slots(ms, st);
         MmaParams m{};
         m.down = (const uint8_t*)W->down; m.down_stride = W->down_stride; m.sh_down = (const uint8_t*)W->sh_down;
         m.T = T; m.slot_expert = c->m_expert; m.slot_tok = c->m_tok; m.slot_out = c->m_out; m.slot_w = c->m_w; m.nslots = c->m_n;
-        m.max_slots = c->m_max; m.slot_cnt = nullptr; m.hb = c->hb; m.y = c->y; m.err = c->err;
-        launch_kq_mma_down(m, W->down_fmt, c->nsm, st);
-    }
-    if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
-    if (h || moe) {
-            CombineParams cp{};
-        cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
-        cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel; cp.sh_t0 = c->sh_t0; cp.sh_n = c->sh_n;
-        launch_combine(cp, st);
-    }
-    if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
-    LK_CU(cudaGetLastError());
-    return LK_OK;
-}
-
-// the register-fed mma.sync path: 16-token slots, IQ2 decoded into mma fragments, SwiGLU -> fp16 h, combine
-static int run_mma_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_x, const float* resid, int T, const int* sel,
-                        const float* w, int keep, float* h, float* moe, cudaStream_t st) {
-    SlotParams s{};
-    s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = MM_NT; s.with_shared = c->rs;
-    s.counts = c->counts; s.offsets = c->offsets; s.perm = c->perm;
-    s.slot_expert = c->m_expert; s.slot_tok = c->m_tok; s.slot_out = c->m_out; s.slot_w = c->m_w; s.nslots = c->m_n;
-    s.max_slots = c->m_max; s.err = c->err; s.sh_t0 = c->sh_t0; s.sh_n = c->sh_n;
-    launch_build_slots(s, st);
-    MmaParams m{};
-    m.gate = (const uint8_t*)W->gate; m.up = (const uint8_t*)W->up; m.down = (const uint8_t*)W->down;
-    m.gate_stride = W->gate_stride; m.up_stride = W->up_stride; m.down_stride = W->down_stride;
-    m.sh_gate = (const uint8_t*)W->sh_gate; m.sh_up = (const uint8_t*)W->sh_up; m.sh_down = (const uint8_t*)W->sh_down;
-    m.x = x; m.ld_x = ld_x; m.T = T;
-    m.slot_expert = c->m_expert; m.slot_tok = c->m_tok; m.slot_out = c->m_out; m.slot_w = c->m_w; m.nslots = c->m_n;
-    m.max_slots = c->m_max; m.slot_cnt = c->m_cnt; m.xh = c->xh; m.hb = c->hb; m.y = c->y; m.err = c->err;
-    if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
-    if (W->down_fmt == LK_FMT_IQ2) {
-        launch_slot_mma(m, c->nsm, st);
-    } else {                                          // K-quant downs: IQ2_XXS gate/up phase, then the K-quant mma down
-        launch_slot_mma_gate_up(m, c->nsm, st);
-        launch_kq_mma_down(m, W->down_fmt, c->nsm, st);
+        m.max_slots = c->m_max; m.slot_cnt = c->m_cnt; m.hb = c->hb; m.y = c->y; m.err = c->err;
+        if (W->down_fmt == LK_FMT_IQ2) {
+            launch_slot_mma_down(m, c->nsm, st);      // its prep pass writes slot_cnt
+        } else {
+            m.slot_cnt = nullptr;                     // the K-quant down counts each slot's tokens itself
+            launch_kq_mma_down(m, W->down_fmt, c->nsm, st);
+        }
     }
     if (c->ev[2]) LK_CU(record_event(c->ev[2], st));
     if (h || moe) {
@@ -383,8 +358,7 @@ static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_
             return LK_OK;
         }
     }
-    if (T >= c->gemm_min_tokens) return run_gemm_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
-    if (T >= c->mma_min_tokens) return run_mma_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
+    if (T >= c->mma_min_tokens) return run_batch_path(c, W, x, ld_x, resid, T, sel, w, keep, h, moe, st);
     if (!slots_ready) {
         SlotParams s{};
         s.sel = sel; s.w = w; s.T = T; s.keep = keep; s.n_experts = c->cfg.n_experts; s.nt = slot_nt(T);

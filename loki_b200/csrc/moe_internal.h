@@ -139,7 +139,13 @@ struct GemmParams {
 };
 void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st);
 void launch_prefill_gemm_gate_up(const GemmParams& p, int grid, cudaStream_t st);   // the gate/up GEMM alone
+void launch_prefill_gemm_down(const GemmParams& p, int grid, cudaStream_t st);      // the IQ2_XXS down GEMM alone (reads ht)
 size_t gemm_tile_halfs(int max_slots, bool down);     // size of bt (down = false) / ht (down = true)
+// the gate/up + SwiGLU phase with the reference's q8 numerics (gate_up_q8.cu): exact products, h re-quantised
+// to q8 per 32; writes fp16(q*d) as the down GEMM's B tiles (ht) or, with hb set, as fp16 rows [entry][MOE_INTER].
+// bt must hold gate_q8_tile_halfs(max_slots) halfs (hi and lo activation rows per token half).
+void launch_gate_up_q8(const GemmParams& p, int grid, cudaStream_t st);
+size_t gate_q8_tile_halfs(int max_slots);
 
 // ---- register-fed mma.sync grouped products (mid-size T): slots of up to MM_NT tokens
 struct MmaParams {
@@ -156,6 +162,8 @@ struct MmaParams {
     int* err;
 };
 void launch_slot_mma(const MmaParams& p, int nsm, cudaStream_t st);
+// the IQ2_XXS down alone on MM_NT slots, reading the fp16 SwiGLU rows hb (x and xh unused)
+void launch_slot_mma_down(const MmaParams& p, int nsm, cudaStream_t st);
 // the gate/up phase alone (SwiGLU output as fp16 rows hb), then the Q2_K / Q3_K down on mma.sync (kq_mma.cu)
 void launch_slot_mma_gate_up(const MmaParams& p, int nsm, cudaStream_t st);
 void launch_kq_mma_down(const MmaParams& p, int down_fmt, int nsm, cudaStream_t st);

@@ -37,6 +37,7 @@
 #include "moe_internal.h"
 #include "moe_device.cuh"
 #include "tcgen05.cuh"
+#include "iq2_tc.cuh"
 
 namespace lk {
 
@@ -53,8 +54,8 @@ constexpr int PG_B_TILE = PG_NMAX * PG_KB * 2;           // 32 KB: one K-block o
 constexpr int PG_RAW_ROWB = 80;                          // one superblock (66 B) in its 16-aligned 80-byte window
 constexpr int PG_RAW_STAGE = 2 * PG_M * PG_RAW_ROWB;     // 256 weight rows: 20 KB
 constexpr int PG_RAW_NST = 3;
-constexpr int PG_GTAB = 256 * 32 * 8;                    // 64 KB grid pair selectors
-constexpr int PG_STAB = 128 * 32 * 8;                    // 32 KB sign pair selectors
+constexpr int PG_GTAB = IQ2TC_GTAB;                      // 64 KB grid pair selectors
+constexpr int PG_STAB = IQ2TC_STAB;                      // 32 KB sign pair selectors
 constexpr int PG_OFF_GTAB = 0;
 constexpr int PG_OFF_STAB = PG_OFF_GTAB + PG_GTAB;
 constexpr int PG_OFF_B = PG_OFF_STAB + PG_STAB;
@@ -72,86 +73,21 @@ constexpr uint32_t PG_TMEM_COLS = 512;
 constexpr uint32_t PG_ACC_COLS = 2 * PG_NMAX;             // 256: 2 tiles x 128 fp32 columns
 constexpr uint32_t PG_A_COLS = 2 * (PG_KB / 2);          // 128 per stage: 2 tiles x 64 columns (128 fp16)
 static_assert(PG_ACC_COLS + PG_NST * PG_A_COLS <= PG_TMEM_COLS, "tensor memory layout");
-constexpr uint32_t F16_PAIR_LO = 0x642B1908u;            // bytes 08 19 2B 64
-constexpr uint32_t F16_PAIR_HI = 0x63AACEF0u;            // bytes F0 CE AA 63
-
-__device__ __forceinline__ uint32_t pair_codes(uint64_t g, int a) {   // elements a, a+1 of grid entry g
-    const uint32_t ma = (uint32_t)(g >> (8 * a)) & 0xFFu, mb = (uint32_t)(g >> (8 * a + 8)) & 0xFFu;
-    const uint32_t ca = ma == 0x08u ? 0u : (ma == 0x19u ? 1u : 2u), cb = mb == 0x08u ? 0u : (mb == 0x19u ? 1u : 2u);
-    return ca | (3u << 4) | (cb << 8) | (3u << 12);
-}
-__device__ __forceinline__ uint32_t pair_signs(uint32_t k, int a) {  // sign bits a, a+1 of ksigns value k
-    const uint32_t sa = (k >> a) & 1u, sb = (k >> (a + 1)) & 1u;
-    return (sa * 0x44u) | ((sb * 0x44u) << 8);
-}
-__device__ __forceinline__ void init_pair_tables(uint2* gt, uint2* st, int tid, int nthr) {
-    for (int t = tid; t < 256 + 128; t += nthr) {
-        uint2 v;
-        if (t < 256) {
-            const uint64_t g = c_iq2_grid[t];
-            v = make_uint2(pair_codes(g, 0) | (pair_codes(g, 2) << 16), pair_codes(g, 4) | (pair_codes(g, 6) << 16));
-        } else {
-            const uint32_t k = iq2_ksigns((uint32_t)(t - 256));
-            v = make_uint2(pair_signs(k, 0) | (pair_signs(k, 2) << 16), pair_signs(k, 4) | (pair_signs(k, 6) << 16));
-        }
-        uint4* row = (uint4*)(t < 256 ? gt + t * 32 : st + (t - 256) * 32);
-        const uint4 q = make_uint4(v.x, v.y, v.x, v.y);
-        #pragma unroll
-        for (int k = 0; k < 16; ++k) row[(k + t) & 15] = q;
-    }
-}
-
-__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t d; asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
-}
-
-// decode one IQ2_XXS group (32 weights) into 16 fp16x2 words in K order (word j = elements 2j, 2j+1)
+// decode one IQ2_XXS group into fp16 v*s, s = fp16(d*(2*scale+1)/8) (iq2_tc.cuh)
 __device__ __forceinline__ void decode_group_f16(uint32_t aux0, uint32_t aux1, float d, const uint2* gtl, const uint2* stl,
                                                  uint32_t (&o)[16]) {
-    // (1024 + v) * s - 1024 * s = v * s with s = fp16(d * (2*scale+1) / 8); 1024 * s is exact (power of two)
     const __half hs = __float2half_rn(d * (float)(2u * (aux1 >> 28) + 1u) * 0.125f);
     const uint32_t s2 = (uint32_t)__half_as_ushort(hs) * 0x10001u;
     const uint32_t c2 = (uint32_t)__half_as_ushort(__hmul(hs, __float2half_rn(-1024.0f))) * 0x10001u;
-    #pragma unroll
-    for (int l = 0; l < 4; ++l) {
-        const uint2 g = gtl[((aux0 >> (8 * l)) & 0xFFu) * 32];
-        const uint2 sg = stl[((aux1 >> (7 * l)) & 0x7Fu) * 32];
-        const uint32_t sx = g.x | sg.x, sy = g.y | sg.y;
-        o[4 * l + 0] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx), s2, c2);
-        o[4 * l + 1] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx >> 16), s2, c2);
-        o[4 * l + 2] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy), s2, c2);
-        o[4 * l + 3] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sy >> 16), s2, c2);
-    }
+    decode_group_f16_s(aux0, aux1, s2, c2, gtl, stl, o);
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
-}
-// arrive on `bar` once every cp.async this thread issued so far has landed (counts as one of its arrivals)
-__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-// registers -> tensor memory: 32 lanes x 16 consecutive 32-bit columns (thread i -> lane base + i)
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-                 :: "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-                    "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]) : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // D[tmem] (+)= A[tmem] x B[smem]^T, one 16-deep K step, issued by a single thread
 __device__ __forceinline__ void umma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
     asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                  "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
                  :: "r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
-
-// byte offset of element (n, k) in a B K-block tile of n16 rows (K-major core matrices, LBO = n16/8*128)
-__device__ __forceinline__ uint32_t btile_off(int n, int k, int n16) {
-    return (uint32_t)((k >> 3) * (n16 >> 3) * 128 + (n >> 3) * 128 + (n & 7) * 16 + (k & 7) * 2);
-}
-__device__ __forceinline__ int round16(int c) { return c <= 16 ? 16 : (c + 15) & ~15; }   // MMA N: 16..128
 
 // global weight row `r` (0..255) of work item (slot expert e, row tile rt): gate/up rows 0-127 gate,
 // 128-255 up (tile rows rt*128..); down rows rt*256 + r
@@ -437,6 +373,8 @@ void launch_prefill_gemm_gate_up(const GemmParams& p, int grid, cudaStream_t st)
     k_gate_b_tiles<<<dim3(p.max_slots, HIDDEN / PG_KB), PG_BT_THREADS, 0, st>>>(p);
     pg_launch<false>(p, grid, st);
 }
+
+void launch_prefill_gemm_down(const GemmParams& p, int grid, cudaStream_t st) { pg_launch<true>(p, grid, st); }
 
 void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st) {
     launch_prefill_gemm_gate_up(p, grid, st);

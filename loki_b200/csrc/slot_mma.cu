@@ -324,6 +324,13 @@ void launch_slot_mma_gate_up(const MmaParams& p, int nsm, cudaStream_t st) {
     mm_launch<false>(p, 2 * nsm, st);
 }
 
+void launch_slot_mma_down(const MmaParams& p, int nsm, cudaStream_t st) {
+    MmaParams q = p;
+    q.T = 0;                                          // the prep pass only counts each slot's tokens
+    k_mma_prep<<<(q.max_slots + 255) / 256, 256, 0, st>>>(q);
+    mm_launch<true>(q, 2 * nsm, st);
+}
+
 void launch_slot_mma(const MmaParams& p, int nsm, cudaStream_t st) {
     launch_slot_mma_gate_up(p, nsm, st);
     mm_launch<true>(p, 2 * nsm, st);

@@ -53,8 +53,9 @@ def _small_arena(native, M, fmt, NE, layer_id, with_shared=True):
 @pytest.mark.parametrize("fmt", KQ)
 @pytest.mark.parametrize("T,keep", [(1, 8), (1, 2), (3, 4), (8, 8), (47, 2), (64, 2), (200, 8)])
 def test_kq_experts_small_arena(native, oracle, fmt, T, keep):
-    """lk_moe_experts with K-quant downs: the single-token q8 matvecs below the mma threshold (48), the
-    mma.sync path (IQ2_XXS gate/up, kq_mma.cu's Q2_K/Q3_K down, fp16 h) from there."""
+    """lk_moe_experts with K-quant downs: the single-token q8 matvecs below the mma threshold (48), from there
+    the q8 gate/up on tcgen05 (h re-quantised to q8) and kq_mma.cu's Q2_K/Q3_K down; both against the oracle
+    with the reference's numerics."""
     from loki_b200 import moe as M
     NE, layer_id = 10, 21
     buf, ws = _small_arena(native, M, fmt, NE, layer_id)
@@ -67,7 +68,7 @@ def test_kq_experts_small_arena(native, oracle, fmt, T, keep):
     h, mo = layer.experts(ws, _dev(x), _dev(r), _dev(sel), _dev(w))
     layer.device_error()
     tok = list(range(T)) if T <= 8 else [0, 1, T // 2, T - 1]
-    ref = oracle_layer(oracle, SEED, layer_id, x, r, sel, w, tokens=tok, down_fmt=fmt, hq8=T < 48)
+    ref = oracle_layer(oracle, SEED, layer_id, x, r, sel, w, tokens=tok, down_fmt=fmt, hq8=True)
     e_moe, e_h = rel_l2(mo.cpu().numpy()[tok], ref["moe"]), rel_l2(h.cpu().numpy()[tok], ref["h"])
     assert e_moe < RTOL_L2 and e_h < RTOL_L2, (e_moe, e_h)
     del buf

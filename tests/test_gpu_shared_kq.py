@@ -74,8 +74,8 @@ def test_shared_model_fmt_experts(native, oracle, small_layer, T, keep):
 
 @pytest.mark.parametrize("T,regime", [(64, "mma"), (256, "gemm")])
 def test_shared_model_fmt_tensor_core_regimes(native, oracle, small_layer, T, regime):
-    """The routed experts on the mma.sync / tcgen05 paths (IQ2_XXS downs), the shared expert on its own
-    launches; the shared part keeps the reference's q8 numerics in every regime."""
+    """The routed experts on the batch regimes (the q8 gate/up, then the mma.sync / tcgen05 IQ2_XXS down: the
+    reference's numerics), the shared expert on its own launches."""
     from loki_b200 import moe as M
     fmt, W = small_layer
     if fmt != 4:
@@ -95,7 +95,7 @@ def test_shared_model_fmt_tensor_core_regimes(native, oracle, small_layer, T, re
     h, mo = layer.experts(W, _dev(x), _dev(r), _dev(sel), _dev(w))
     layer.device_error()
     tok = [0, 1, T // 2, T - 1]
-    ref = oracle_layer(oracle, SEED, 23, x, r, sel, w, tokens=tok, hq8=False, sh_fmt=FMT_Q5K)
+    ref = oracle_layer(oracle, SEED, 23, x, r, sel, w, tokens=tok, hq8=True, sh_fmt=FMT_Q5K)
     hn, mn = h.cpu().numpy()[tok], mo.cpu().numpy()[tok]
     e_moe = rel_l2(mn, ref["moe"])
     # the shared expert took the dense fp16 path (>= 16 tokens): against the float restatement
