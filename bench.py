@@ -184,6 +184,37 @@ def max_over_ranks(dist, v):
 
 
 # ------------------------------------------------------------------ CPU baseline (oracle)
+def cpu_layer(O, L, keep=8, seed=SEED):
+    """Layer L of the CPU decode workload, set up outside any timed region (the GPU arm's weights are resident
+    too): its seeded input row, residual, router weights and bias, and the IQ2_XXS weights of the experts its
+    token selects plus the shared expert."""
+    rng = np.random.default_rng(seed + L)
+    x = rng.standard_normal((1, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((1, HIDDEN)).astype(np.float32)
+    W = (rng.standard_normal((NE, HIDDEN)) * 0.02).astype(np.float32)
+    bias = (rng.standard_normal(NE) * 0.01).astype(np.float32)
+    cfg = O.route_cfg(8, keep, 1, N_GROUP, TOPK_GROUP)
+    _, sel, _ = O.router(x, W, bias, cfg)
+    used = sorted(set(int(e) for e in sel[0]))
+    remap = {e: i for i, e in enumerate(used)}
+    ids = np.array([[remap[int(e)] for e in sel[0]]], np.int32)
+    gate = np.concatenate([O.gen_iq2(seed, L, 0, e, INTER, HIDDEN) for e in used])
+    up = np.concatenate([O.gen_iq2(seed, L, 1, e, INTER, HIDDEN) for e in used])
+    down = np.concatenate([O.gen_iq2(seed, L, 2, e, HIDDEN, INTER) for e in used])
+    sh = [O.gen_iq2(seed, L, m, 256, *((INTER, HIDDEN) if m < 2 else (HIDDEN, INTER))) for m in range(3)]
+    return dict(x=x, r=r, W=W, bias=bias, cfg=cfg, ids=ids, gate=gate, up=up, down=down, sh=sh)
+
+
+def cpu_layer_forward(O, lay):
+    """One T=1 layer on the CPU oracle: router (sigmoid, grouped top-8, weights) + experts + combine."""
+    _, _, w = O.router(lay["x"], lay["W"], lay["bias"], lay["cfg"])
+    O.moe_layer(lay["x"], lay["r"], lay["gate"], lay["up"], lay["down"], MAT, lay["ids"], w, *lay["sh"])
+
+
+def cpu_cores():
+    return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+
+
 def cpu_decode_sample(n_layers, keep=8, seed=SEED):
     """Time the CPU oracle on T=1 decode for n_layers layers (router + experts + combine); returns
     (seconds per layer, cores).  Weights for the selected experts are generated before the clock starts."""
@@ -191,29 +222,29 @@ def cpu_decode_sample(n_layers, keep=8, seed=SEED):
     O.build()
     times = []
     for L in range(n_layers):
-        rng = np.random.default_rng(seed + L)
-        x = rng.standard_normal((1, HIDDEN)).astype(np.float32)
-        r = rng.standard_normal((1, HIDDEN)).astype(np.float32)
-        W = (rng.standard_normal((NE, HIDDEN)) * 0.02).astype(np.float32)
-        bias = (rng.standard_normal(NE) * 0.01).astype(np.float32)
-        cfg = O.route_cfg(8, keep, 1, N_GROUP, TOPK_GROUP)
-        _, sel, w = O.router(x, W, bias, cfg)
-        used = sorted(set(int(e) for e in sel[0]))
-        remap = {e: i for i, e in enumerate(used)}
-        ids = np.array([[remap[int(e)] for e in sel[0]]], np.int32)
-        gate = np.concatenate([O.gen_iq2(seed, L, 0, e, INTER, HIDDEN) for e in used])
-        up = np.concatenate([O.gen_iq2(seed, L, 1, e, INTER, HIDDEN) for e in used])
-        down = np.concatenate([O.gen_iq2(seed, L, 2, e, HIDDEN, INTER) for e in used])
-        sh = [O.gen_iq2(seed, L, m, 256, *((INTER, HIDDEN) if m < 2 else (HIDDEN, INTER))) for m in range(3)]
+        lay = cpu_layer(O, L, keep, seed)
         t0 = time.perf_counter()
-        _, sel2, w2 = O.router(x, W, bias, cfg)
-        O.moe_layer(x, r, gate, up, down, MAT, ids, w2, sh[0], sh[1], sh[2])
+        cpu_layer_forward(O, lay)
         times.append(time.perf_counter() - t0)
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return float(np.mean(times)), cores
+    return float(np.mean(times)), cpu_cores()
 
 
 # ------------------------------------------------------------------ decode workload (config 1)
+def decode_config(args, ws, distinct, fmt=4, model_sh=False, layer_bytes=None):
+    """The config object of the decode line (both arms)."""
+    if layer_bytes is None:
+        layer_bytes = args.keep * (2 * MAT + down_bytes(args)) + shared_bytes(args) + ROUTER_BYTES + 3 * 4 * HIDDEN
+    return {"workload": ("config1_decode_T1_58layers" if fmt == 4 else "decode_T1_58layers_%s_down" % args.down_fmt) +
+                        ("_q5k_q6k_shared" if model_sh else ""),
+            "model": ("DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)" if fmt == 4 else
+                      "DeepSeek-R1 MoE layer (IQ2_XXS gate/up, %s down as in the real model, 256 experts + shared)" % args.down_fmt) +
+                     ("; shared expert Q5_K gate/up + Q6_K down as in the real model" if model_sh else ""),
+            "global_batch": ws, "seq_len": 1, "layers": args.layers, "distinct_layers_resident": distinct,
+            "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP, "keep": args.keep,
+            "parallelism": "replicas" if ws > 1 else "single",
+            "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (args.layers * layer_bytes / 1e9)}
+
+
 def build_decode(dev, n_layers, keep, fmt=4, ds=MAT, sh_fmt=4, sh_bytes=None):
     import torch
     from loki_b200 import moe as M
@@ -321,14 +352,7 @@ def run_decode(args, ws, rank, local, dist):
                   "iq2_xxs gate/up, %s down x q8 (int8 dp4a, fp32 accumulate)" % args.down_fmt) +
                  ("; shared expert q5_k/q6_k x q8" if model_sh else ""),
         "data": "synthetic: seeded IQ2_XXS experts (BASELINE config 0 generator), router W N(0,0.02), bias N(0,0.01), x/resid N(0,1) fp32",
-        "config": {"workload": ("config1_decode_T1_58layers" if fmt == 4 else "decode_T1_58layers_%s_down" % args.down_fmt) +
-                               ("_q5k_q6k_shared" if model_sh else ""),
-                   "model": ("DeepSeek-R1 MoE layer (IQ2_XXS, 256 experts + shared)" if fmt == 4 else
-                             "DeepSeek-R1 MoE layer (IQ2_XXS gate/up, %s down as in the real model, 256 experts + shared)" % args.down_fmt) +
-                            ("; shared expert Q5_K gate/up + Q6_K down as in the real model" if model_sh else ""),
-                   "global_batch": ws, "seq_len": 1, "layers": args.layers, "distinct_layers_resident": distinct,
-                   "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP, "keep": args.keep, "parallelism": "replicas" if ws > 1 else "single",
-                   "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (args.layers * layer_bytes / 1e9)},
+        "config": decode_config(args, ws, distinct, fmt, model_sh, layer_bytes),
         "layer": {"ms_per_layer": round(ms_max / args.steps / args.layers * 1e3, 3), "unit_ms_per_layer": "us",
                   "bytes_per_layer": layer_bytes,
                   "achieved_gbs": round(layer_bytes * args.layers * args.steps / (ms_max / 1e3) / 1e9, 1),
@@ -677,20 +701,24 @@ def e2e_decode(args, layers, distinct, keep):
             "steps": n, "error": out[True][1] | out[False][1]}
 
 
-def run_prefill(args, ws, rank, local, dist):
-    """one MoE layer, T=512 tokens (bf16 N(0,1) hidden states, fed as fp32), top-8 of 256
-    experts chosen from uniform-random router logits (the router GEMV still runs), IQ2_XXS experts through the
-    tcgen05 grouped GEMMs, combine with the shared expert.  A step = one layer forward."""
+def run_prefill(args, ws, rank, local, dist, W=None, T=None, steps=None, warmup=None):
+    """BASELINE config 2 (T=512) and config 3's single-GPU shape (T=4096): one MoE layer, bf16 N(0,1) hidden
+    states (fed as fp32), top-8 of 256 experts chosen from uniform-random router logits (the router GEMV still
+    runs), the batch regime's kernels (q8 gate/up on tcgen05, IQ2_XXS down on tcgen05), combine with the shared
+    expert.  A step = one layer forward.  W: resident layer weights to reuse (default: layer 0 is built)."""
     import torch
     import ctypes
     from loki_b200 import moe as M
     from loki_b200 import native as N
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    T = args.tokens
+    T = T or args.tokens
+    steps = steps or args.steps
+    warmup = max(3, warmup or args.warmup)
     fmt, DS = DOWN_FMTS[args.down_fmt][0], down_bytes(args)
     model_fmt = fmt != 4 or args.shared_fmt == "q5k"
-    W = M.LayerWeights(dev, SEED, 0, down_fmt=fmt, sh_fmt=FMT_Q5K if args.shared_fmt == "q5k" else 4)
+    if W is None:
+        W = M.LayerWeights(dev, SEED, 0, down_fmt=fmt, sh_fmt=FMT_Q5K if args.shared_fmt == "q5k" else 4)
     g = torch.Generator(device=dev).manual_seed(4321 + rank)
     x = torch.randn(T, HIDDEN, device=dev, generator=g).to(torch.bfloat16).float()
     r = torch.randn(T, HIDDEN, device=dev, generator=g).to(torch.bfloat16).float()
@@ -714,7 +742,7 @@ def run_prefill(args, ws, rank, local, dist):
             L.lk_moe_set_events(ctx.ctx, None)
 
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             step()
     torch.cuda.synchronize(dev)
     ctx.device_error()
@@ -727,79 +755,112 @@ def run_prefill(args, ws, rank, local, dist):
     barrier(dist)
     with torch.cuda.stream(stream):
         t0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             step()
         t1.record(stream)
     barrier(dist)
     ms = t0.elapsed_time(t1)
-    gemm_ms = []
+    gu_ms, dn_ms = [], []
     with torch.cuda.stream(stream):
         for _ in range(3):
             step(events=True)
             torch.cuda.synchronize(dev)
-            gemm_ms.append(ev.elapsed(0, 2))
+            gu_ms.append(ev.elapsed(0, 1))
+            dn_ms.append(ev.elapsed(1, 2))
     cl = clocks.stop() if clocks else None
     ctx.device_error()
     ms_max = max_over_ranks(dist, ms)
-    value = T * args.steps * ws / (ms_max / 1e3)
+    value = T * steps * ws / (ms_max / 1e3)
     hbm, bf16, peak_kind = measured_peaks()
     # routing statistics of the step (distinct experts, tokens per expert)
     sel = torch.topk(torch.sigmoid(logits) + W.router_bias, 8, dim=1).indices
     distinct = int(torch.unique(sel).numel())
-    gemm_bytes = distinct * (2 * MAT + DS) + shared_bytes(args)         # routed + shared gate/up/down, each read once
-    layer_bytes = gemm_bytes + ROUTER_BYTES + T * HIDDEN * 4 * 4
+    sh_iq2 = args.shared_fmt != "q5k"
+    # algorithmic bytes and flops per launch: each distinct expert's matrices read once, the activations in and out
+    gu_bytes = (distinct + sh_iq2) * 2 * MAT + T * HIDDEN * 4 + T * (args.keep + 1) * INTER * 2
+    dn_bytes = (distinct + sh_iq2) * DS + T * (args.keep + 1) * (INTER * 2 + HIDDEN * 4)
+    entries = T * (args.keep + sh_iq2)
+    gu_flops, dn_flops = 2.0 * entries * 2 * HIDDEN * INTER, 2.0 * entries * HIDDEN * INTER
+    layer_bytes = distinct * (2 * MAT + DS) + shared_bytes(args) + ROUTER_BYTES + T * HIDDEN * 4 * 4
     flops = 2.0 * T * (args.keep + 1) * 3 * HIDDEN * INTER + 2.0 * T * HIDDEN * NE
-    g_ms = float(np.median(gemm_ms))
+    g_ms, d_ms = float(np.median(gu_ms)), float(np.median(dn_ms))
+    # HBM-bound where the weights' bytes at peak take longer than the flops at the bf16 peak (T=512); else tensor
+    tensor_bound = gu_flops / (bf16 * 1e12) > gu_bytes / (hbm * 1e9)
+    gu_gbs, gu_tf = gu_bytes / (g_ms / 1e3) / 1e9, gu_flops / (g_ms / 1e3) / 1e12
+    dn_gbs, dn_tf = dn_bytes / (d_ms / 1e3) / 1e9, dn_flops / (d_ms / 1e3) / 1e12
+    wl = "prefill_T%d" % T
     out = {
-        "metric": "MoE-layer tokens/s (T=512 prefill, one layer)", "value": round(value, 1), "unit": "tokens/s",
-        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "metric": "MoE-layer tokens/s (T=%d %s, one layer)" % (T, "prefill" if T <= 512 else "batch"),
+        "value": round(value, 1), "unit": "tokens/s",
+        "n_gpus": ws, "steps": steps, "warmup": warmup, "ms_per_step": round(ms_max / steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)" if not model_fmt else
-                 "the real model's formats (%s down, %s shared): IQ2_XXS gate/up tcgen05 fp16 x fp16, K-quant down mma.sync "
-                 "fp16 x fp16(h), Q5_K/Q6_K shared dequantised to fp16 + cuBLAS; fp32 accumulate" % (args.down_fmt, args.shared_fmt),
+        "dtype": "iq2_xxs x q8 activations: gate/up tcgen05 kind::f16 with exact integer weights and hi/lo fp16 activations "
+                 "(the reference's group sums), h re-quantised to q8; down tcgen05 fp16; fp32 accumulate" if not model_fmt else
+                 "the real model's formats (%s down, %s shared): IQ2_XXS q8 gate/up on tcgen05 (h re-quantised to q8), K-quant "
+                 "down mma.sync fp16; Q5_K/Q6_K shared dequantised to fp16 + cuBLAS; fp32 accumulate" % (args.down_fmt, args.shared_fmt),
         "data": "synthetic: seeded IQ2_XXS experts, uniform-random router logits U(-1,1), bf16 N(0,1) hidden states",
-        "config": {"workload": "config2_prefill_T%d" % T + ("" if not model_fmt else "_%s_down_%s_shared" % (args.down_fmt, args.shared_fmt)),
+        "config": {"workload": ("config2_prefill_T%d" % T if T == 512 else "config3_batch_T%d_1gpu" % T if T == 4096 else wl) +
+                               ("" if not model_fmt else "_%s_down_%s_shared" % (args.down_fmt, args.shared_fmt)),
                    "global_batch": T * ws, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,
                    "keep": args.keep, "distinct_experts": distinct, "parallelism": "replicas" if ws > 1 else "single",
-                   "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (gemm_bytes / 1e9)},
-        "layer": {"bytes": layer_bytes, "flops": flops, "achieved_gbs": round(layer_bytes / (ms_max / args.steps / 1e3) / 1e9, 1),
-                  "achieved_tflops": round(flops / (ms_max / args.steps / 1e3) / 1e12, 1),
-                  "frac_of_hbm": round(layer_bytes / (ms_max / args.steps / 1e3) / 1e9 / hbm, 4)},
-        "roofline": {"kernel": "k_prefill_gemm (gate/up + down tcgen05 GEMMs, incl. fp16 activation staging)", "bound": "hbm",
-                     "achieved": round(gemm_bytes / (g_ms / 1e3) / 1e9, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(gemm_bytes / (g_ms / 1e3) / 1e9 / hbm, 4), "traffic": ncu_traffic("k_prefill_gemm", "prefill_T512"),
-                     "algorithmic_bytes_per_launch": gemm_bytes, "peak_source": peak_kind,
-                     "frac_of_nominal_7700": round(gemm_bytes / (g_ms / 1e3) / 1e9 / NOMINAL_HBM_GBS, 4),
-                     "tensor_tflops": round(flops * 0.999 / (g_ms / 1e3) / 1e12, 1), "tensor_peak_tflops": bf16},
-        # this library's kernels per step (profiles/prefill_gemm_T512.md, prefill_real_model_formats_T512.md):
-        # IQ2_XXS downs -- router, slots, gate B tiles, gate/up GEMM, down GEMM, combine; K-quant downs -- the
-        # down GEMM becomes a second slot build + k_kq_mma_down; a Q5_K/Q6_K shared expert adds its 5 dense-path
-        # kernels (3 dequantisations, x to fp16, SwiGLU; its two GEMMs are cuBLAS's)
-        "gpu_launches": args.steps * ((6 if fmt == 4 else 7) + (5 if args.shared_fmt == "q5k" else 0)),
+                   "l2": "no flush: a step streams %.2f GB of distinct weights (> 126 MB L2)" % (layer_bytes / 1e9)},
+        "layer": {"bytes": layer_bytes, "flops": flops, "achieved_gbs": round(layer_bytes / (ms_max / steps / 1e3) / 1e9, 1),
+                  "achieved_tflops": round(flops / (ms_max / steps / 1e3) / 1e12, 1),
+                  "frac_of_hbm": round(layer_bytes / (ms_max / steps / 1e3) / 1e9 / hbm, 4),
+                  "frac_of_bf16": round(flops / (ms_max / steps / 1e3) / 1e12 / bf16, 4),
+                  "kernel_ms_event": {"gate_up": round(g_ms, 4), "down": round(d_ms, 4),
+                                      "rest": round(ms_max / steps - g_ms - d_ms, 4)}},
+        "roofline": {"kernel": "k_gate_up_q8 (+ its activation-tile pre-pass): q8 gate/up + SwiGLU + q8 of h",
+                     "bound": "tensor" if tensor_bound else "hbm",
+                     "achieved": round(gu_tf if tensor_bound else gu_gbs, 1), "peak": bf16 if tensor_bound else hbm,
+                     "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                     "frac": round(gu_tf / bf16 if tensor_bound else gu_gbs / hbm, 4),
+                     "traffic": ncu_traffic("k_gate_up_q8", wl), "algorithmic_bytes_per_launch": gu_bytes,
+                     "algorithmic_flops_per_launch": gu_flops, "peak_source": peak_kind,
+                     "hbm_gbs": round(gu_gbs, 1), "hbm_frac": round(gu_gbs / hbm, 4),
+                     "tensor_tflops": round(gu_tf, 1), "tensor_frac": round(gu_tf / bf16, 4),
+                     "frac_of_nominal_7700": round(gu_gbs / NOMINAL_HBM_GBS, 4),
+                     "down": {"kernel": "k_prefill_down" if fmt == 4 else "k_kq_mma_down", "ms": round(d_ms, 4),
+                              "hbm_gbs": round(dn_gbs, 1), "hbm_frac": round(dn_gbs / hbm, 4),
+                              "tensor_tflops": round(dn_tf, 1), "tensor_frac": round(dn_tf / bf16, 4),
+                              "traffic": ncu_traffic("k_prefill_down" if fmt == 4 else "k_kq_mma_down", wl)}},
+        # this library's kernels per step: router, slot build, gate/up activation tiles, gate/up GEMM, down GEMM,
+        # combine; K-quant downs add a second slot build and take k_kq_mma_down for the down; a Q5_K/Q6_K shared
+        # expert adds its 5 dense-path kernels (3 dequantisations, x to fp16, SwiGLU; its two GEMMs are cuBLAS's)
+        "gpu_launches": steps * ((6 if fmt == 4 else 7) + (5 if args.shared_fmt == "q5k" else 0)),
     }
     if cl:
         out["clocks"] = cl
+    del ctx
     return out
 
 
 def reference_arm(args, ws, rank):
-    """--impl reference: the CPU oracle (restatement of the reference's path) on the host cores."""
+    """--impl reference: the CPU oracle (the restatement of the reference's path) on the host cores, timed on the
+    same workload as the GPU arm's line: each step is T=1 through the 58 distinct layers (router, experts,
+    combine), every layer's weights set up before the clock starts."""
     if rank != 0:
         return None
+    from oracle import oracle as O
+    O.build()
+    layers = [cpu_layer(O, L, args.keep) for L in range(args.layers)]
     per_step = []
     for s in range(args.warmup + args.steps):
-        t, cores = cpu_decode_sample(1, keep=args.keep, seed=SEED + 1000 * s)
+        t0 = time.perf_counter()
+        for lay in layers:
+            cpu_layer_forward(O, lay)
         if s >= args.warmup:
-            per_step.append(t)
-    t_layer = float(np.mean(per_step))
-    value = 1.0 / (t_layer * args.layers)
-    sample = "1 layer (T=1, top-8 + shared) per step, scaled to %d layers" % args.layers
+            per_step.append(time.perf_counter() - t0)
+    t_step = float(np.mean(per_step))
+    value = 1.0 / t_step
+    cores = cpu_cores()
+    sample = "every step: T=1 through %d distinct layers (router, 8 routed + shared IQ2_XXS experts, combine)" % args.layers
     return {"impl": "reference", "metric": "MoE-layer tokens/s (T=1 decode through 58 layers)", "value": round(value, 4),
             "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(t_layer * args.layers * 1e3, 2), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "iq2_xxs x q8 (int32 dot, fp64 accumulate)", "data": "synthetic",
-            "config": {"workload": "config1_decode_T1_58layers", "global_batch": 1, "seq_len": 1, "layers": args.layers,
-                       "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP, "keep": args.keep, "parallelism": "cpu"},
+            "ms_per_step": round(t_step * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "iq2_xxs x q8 (int32 dot, fp64 accumulate)",
+            "data": "synthetic: seeded IQ2_XXS experts (BASELINE config 0 generator), router W N(0,0.02), bias N(0,0.01), x/resid N(0,1) fp32",
+            "config": decode_config(args, 1, args.layers),
             "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -820,6 +881,7 @@ def main():
     ap.add_argument("--shared-fmt", default="iq2", choices=["iq2", "q5k"],
                     help="decode workload: the shared expert's formats (q5k: the real model's Q5_K gate/up + Q6_K down)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample (profiling runs)")
+    ap.add_argument("--no-batch", action="store_true", help="decode workload: skip the T=512 / T=4096 sub-measurements")
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the CPU-baseline sample")
     ap.add_argument("--parallelism", default="ep", choices=["ep", "replicas"], help="N > 1: expert parallel or replicas")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"], help="EP decode row exchange")
@@ -871,6 +933,16 @@ def main():
         out["cpu_baseline"] = {"value": round(1.0 / (t_layer * args.layers), 4), "unit": "tokens/s", "cores": cores,
                                "kind": "port", "sample": "%d layers of T=1 decode through the C++ oracle, scaled to %d layers"
                                % (args.cpu_layers, args.layers)}
+    if ws == 1 and not args.no_batch and args.down_fmt == "iq2" and args.shared_fmt == "iq2":
+        # the metric's other two token counts on the same GPU, reusing resident layer 0: BASELINE config 2 (T=512)
+        # and config 3's shape on one GPU (T=4096)
+        del ctx, structs, xs, rs
+        W0 = layers[0]
+        del layers[1:]
+        torch.cuda.empty_cache()
+        out["prefill_T512"] = run_prefill(args, ws, rank, local, dist, W=W0, T=512, steps=10, warmup=3)
+        torch.cuda.empty_cache()
+        out["batch_T4096"] = run_prefill(args, ws, rank, local, dist, W=W0, T=4096, steps=5, warmup=3)
     if rank == 0:
         print(json.dumps(out), flush=True)
     if dist is not None:

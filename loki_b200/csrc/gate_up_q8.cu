@@ -14,6 +14,8 @@
 //     accumulator.  The two rows sit side by side along N, so one MMA of N' = 2N covers both.
 //   * Per superblock (256 weights, 2 K-blocks) the MMA accumulates P = sum A*B into a fresh TMEM buffer (two
 //     buffers alternate); epilogue warps fold R += (d/8) * (P_hi + P_lo) into a running sum R in TMEM.
+//     (hi + lo of one accumulator are summed in fp32 first, then the accumulators, then scaled: fp32 rounding
+//     at the level of the reference's own float reassociation.)
 //   * After the last superblock, R is g (rows 0-63 of the tile) or u (rows 64-127); the epilogue forms
 //     h = silu(g)*u, quantises it per 32 (d = amax/127, round half even: quant_q8_group bit for bit) and
 //     writes fp16(q*d) -- exactly representable up to fp16 rounding of the product -- as the down's input:
@@ -21,8 +23,11 @@
 //
 // Work item = (slot s, h tile rt of 64 rows, token half nh): M = 128 weight rows (64 gate rows + the same 64
 // up rows), N = up to 64 tokens (a slot of up to GEMM_NT = 128 tokens is two halves; the second is skipped
-// when the slot holds <= 64).  TMEM (512 columns): A stages [0,128) (2 x 64), R [128,192), P buffers
-// [256,384) and [384,512) (2N <= 128 each).
+// when the slot holds <= 64).  TMEM (512 columns): three A stages of 64 columns at 0, 64 and 192, R [128,192),
+// P buffers [256,384) and [384,512).  The decode tables have 16 lane copies (48 KB).
+//   A dependent tcgen05.mma (one accumulator, K = 16) measured ~260 cycles whatever N is up to 128, while one of
+//   M=128, N'=32 is ~16 cycles of tensor work.  So a superblock's K steps go round-robin to nacc = 128 / N'
+//   independent accumulators inside its P buffer (4 at N' = 32, 2 at N' = 64, 1 above), which the fold sums.
 //
 // Warp roles (736 threads, one CTA per SM, persistent over items):
 //   warps 0-15  decode: warp w = TMEM lane quarter w&3 (rows 32*(w&3)..), group w>>2 of each K-block; writes
@@ -50,7 +55,7 @@ constexpr int GQ_NH = 64;                       // tokens per item (half of a GE
 constexpr int GQ_KB = 128;                      // K per stage
 constexpr int GQ_NKB = HIDDEN / GQ_KB;          // 56
 constexpr int GQ_NSB = HIDDEN / QK;             // 28 superblocks per row
-constexpr int GQ_NST = 2;
+constexpr int GQ_NST = 3;                       // A (TMEM) / B (smem) stages
 constexpr int GQ_DWARPS = 16;
 constexpr int GQ_MMA_WARP = GQ_DWARPS, GQ_COPY_WARP = GQ_DWARPS + 1, GQ_RAW_WARP = GQ_DWARPS + 2;
 constexpr int GQ_EPI_WARP0 = GQ_DWARPS + 3, GQ_EWARPS = 4;
@@ -61,8 +66,8 @@ constexpr int GQ_RAW_STAGE = GQ_M * GQ_RAW_ROWB;                // 10 KB
 constexpr int GQ_RAW_NST = 4;
 constexpr int GQ_XS = GQ_NH + 1;                                // exchange row stride (floats)
 constexpr int GQ_OFF_GTAB = 0;
-constexpr int GQ_OFF_STAB = GQ_OFF_GTAB + IQ2TC_GTAB;
-constexpr int GQ_OFF_B = GQ_OFF_STAB + IQ2TC_STAB;
+constexpr int GQ_OFF_STAB = GQ_OFF_GTAB + IQ2TC_GTAB16;
+constexpr int GQ_OFF_B = GQ_OFF_STAB + IQ2TC_STAB16;
 constexpr int GQ_OFF_RAW = GQ_OFF_B + GQ_NST * GQ_B_HALF;
 constexpr int GQ_OFF_X = GQ_OFF_RAW + GQ_RAW_NST * GQ_RAW_STAGE + 64;   // + slack for the last row's over-read
 constexpr int GQ_OFF_BAR = GQ_OFF_X + GQ_H * GQ_XS * 4;
@@ -76,9 +81,23 @@ static_assert(GQ_OFF_B % 1024 == 0 && GQ_B_HALF % 1024 == 0, "B stages 16-byte (
 constexpr uint32_t GQ_TMEM_COLS = 512;
 constexpr uint32_t GQ_A_COLS = GQ_KB / 2;       // 64 per stage: 128 fp16 K values
 constexpr uint32_t GQ_R_COL = 128, GQ_P_COL = 256, GQ_P_COLS = 128;
-static_assert(GQ_NST * GQ_A_COLS <= GQ_R_COL && GQ_R_COL + GQ_NH <= GQ_P_COL && GQ_P_COL + 2 * GQ_P_COLS <= GQ_TMEM_COLS,
-              "tensor memory layout");
+// A stages at columns 0, 64 and 192 (R sits at 128 .. 192)
+__device__ __forceinline__ uint32_t gq_a_col(int st) { return st < 2 ? (uint32_t)st * GQ_A_COLS : 192u; }
+static_assert(2 * GQ_A_COLS <= GQ_R_COL && GQ_R_COL + GQ_NH <= 192 && 192 + GQ_A_COLS <= GQ_P_COL &&
+              GQ_P_COL + 2 * GQ_P_COLS <= GQ_TMEM_COLS, "tensor memory layout");
 constexpr int GQ_EPI_BAR = 1;                   // named barrier of the 4 epilogue warps
+
+// tensor memory -> registers without the wait (tcgen05.wait::ld before the values are used)
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                   "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr) : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// independent accumulators per P buffer for N' = 2 * round16(tokens) columns each (a power of two, <= 4)
+__device__ __forceinline__ int gq_nacc(int n2) { return n2 <= 32 ? 4 : (n2 <= 64 ? 2 : 1); }
 
 __device__ __forceinline__ void tmem_st16f(uint32_t taddr, const float (&v)[16]) {
     uint32_t r[16];
@@ -95,11 +114,15 @@ __device__ __forceinline__ const uint8_t* gq_row(const GemmParams& p, int e, int
     return wm + (size_t)row * ((HIDDEN / QK) * BLK_IQ2);
 }
 
-// item -> (slot, h tile, token half); false when the half holds no token
+// item -> (slot, h tile, token half); false when the half holds no token.  Slot-major: the CTAs working at one
+// time share a few slots, so each slot's activation tiles come from DRAM once and then from L2 for all of its
+// h tiles (h-tile-major order re-read them from DRAM per tile: 4.3x the algorithmic bytes at T=512), and a
+// hot expert's consecutive slots re-read its rows from L2
 __device__ __forceinline__ bool gq_item(const GemmParams& p, int item, int nslots, int& s, int& rt, int& nh, int& cnt_h) {
-    s = item % nslots;
-    const int rest = item / nslots;
-    rt = rest >> 1; nh = rest & 1;
+    (void)nslots;
+    s = item / (2 * GQ_TILES);
+    const int rest = item - s * (2 * GQ_TILES);
+    nh = rest / GQ_TILES; rt = rest - nh * GQ_TILES;
     cnt_h = p.slot_cnt[s] - GQ_NH * nh;
     cnt_h = cnt_h > GQ_NH ? GQ_NH : cnt_h;
     return cnt_h > 0;
@@ -130,7 +153,7 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
     const int nitems = nslots * GQ_TILES * 2;
     if ((int)blockIdx.x >= nitems) return;
 
-    init_pair_tables((uint2*)(smem + GQ_OFF_GTAB), (uint2*)(smem + GQ_OFF_STAB), tid, GQ_THREADS);
+    init_pair_tables16((uint2*)(smem + GQ_OFF_GTAB), (uint2*)(smem + GQ_OFF_STAB), tid, GQ_THREADS);
     if (tid == 0) {
         *abort_flag = 0;
         // full: 16 decode-warp arrivals + the copy warp's expect_tx arrival (B bytes)
@@ -183,7 +206,7 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
                 const uint32_t bytes = (uint32_t)(2 * round16(cnt_h)) * GQ_KB * 2;
                 for (int kb = 0; kb < GQ_NKB; ++kb, ++it) {
                     const int st = it % GQ_NST;
-                    if (!mbar_wait_backoff(&empty[st], ((it / GQ_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
+                    if (!mbar_wait(&empty[st], ((it / GQ_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) { *abort_flag = 1; break; }
                     mbar_arrive_expect_tx(&full[st], bytes);
                     bulk_g2s(bring + st * GQ_B_HALF, p.bt + (((size_t)s * GQ_NKB + kb) * 2 + nh) * (GQ_B_HALF / 2), bytes, &full[st]);
                 }
@@ -203,6 +226,7 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
             int s, rt, nh, cnt_h;
             if (!gq_item(p, item, nslots, s, rt, nh, cnt_h)) continue;
             const int N2 = __shfl_sync(0xffffffffu, 2 * round16(cnt_h), 0);       // hi rows then lo rows
+            const int nacc = gq_nacc(N2);
             const uint32_t idesc = idesc_f16_f32(GQ_M, N2);
             const uint32_t lbo = (uint32_t)(N2 >> 3) * 128;
             const uint64_t bstep = (uint64_t)((2 * lbo) >> 4);                    // one K=16 step along the B tile
@@ -210,15 +234,17 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
                 const int st = it % GQ_NST;
                 const uint32_t b = psb & 1;
                 if ((kb & 1) == 0 &&
-                    !__all_sync(0xffffffffu, mbar_wait_backoff(&pempty[b], ((psb >> 1) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY))) { ok = false; break; }
-                if (!__all_sync(0xffffffffu, mbar_wait_backoff(&full[st], (it / GQ_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))) { ok = false; break; }
+                    !__all_sync(0xffffffffu, mbar_wait(&pempty[b], ((psb >> 1) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY))) { ok = false; break; }
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (it / GQ_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))) { ok = false; break; }
                 tc_fence_after();
                 const uint64_t b0 = umma_desc(bring_s + st * GQ_B_HALF, lbo, 128);
-                const uint32_t a0 = tmem + st * GQ_A_COLS;
+                const uint32_t a0 = tmem + gq_a_col(st);
                 const uint32_t d = tmem + GQ_P_COL + b * GQ_P_COLS;
                 #pragma unroll
-                for (int ks = 0; ks < GQ_KB / 16; ++ks)
-                    umma_f16_ta_warp(d, a0 + ks * 8, b0 + (uint64_t)ks * bstep, idesc, ((kb & 1) | ks) != 0);
+                for (int ks = 0; ks < GQ_KB / 16; ++ks) {       // K step ks -> accumulator ks % nacc of the P buffer
+                    const int j = ks & (nacc - 1);
+                    umma_f16_ta_warp(d + (uint32_t)(j * N2), a0 + ks * 8, b0 + (uint64_t)ks * bstep, idesc, (kb & 1) || ks >= nacc);
+                }
                 umma_commit_warp(&empty[st]);
                 issued = 1;
                 if (kb & 1) { umma_commit_warp(&pfull[b]); ++psb; }
@@ -233,8 +259,8 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
         // ---------------------------------------------------------------- decode warps
         const int q = warp & 3, gsel = warp >> 2;
         const int row = 32 * q + lane;                                      // weight row of the item = TMEM lane
-        const uint2* gtl = gtab + lane;
-        const uint2* stl = stab + lane;
+        const uint2* gtl = gtab + (lane & 15);
+        const uint2* stl = stab + (lane & 15);
         const uint8_t* rrow0 = raw + row * GQ_RAW_ROWB;
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         uint32_t it = 0, rit = 0;
@@ -245,7 +271,7 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
             const uint32_t wlo = (uint32_t)(uintptr_t)gq_row(p, e, rt, row);
             for (int kb = 0; kb < GQ_NKB; ++kb, ++it) {
                 const int st = it % GQ_NST, rs = rit % GQ_RAW_NST;
-                if ((kb & 1) == 0 && !*abort_flag && !mbar_wait_backoff(&rawfull[rs], (rit / GQ_RAW_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))
+                if ((kb & 1) == 0 && !*abort_flag && !mbar_wait(&rawfull[rs], (rit / GQ_RAW_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))
                     *abort_flag = 1;
                 const uint8_t* rrow = rrow0 + rs * GQ_RAW_STAGE;
                 const int delta = (int)((wlo + (uint32_t)(kb >> 1) * BLK_IQ2) & 15u);   // superblock offset in its window
@@ -257,10 +283,10 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
                 const uint32_t s2 = (uint32_t)__half_as_ushort(__uint2half_rn(sc)) * 0x10001u;
                 const uint32_t c2 = (uint32_t)__half_as_ushort(__uint2half_rn(1024u * sc)) * 0x10001u ^ 0x80008000u;
                 uint32_t o[16];
-                decode_group_f16_s(aux0, aux1, s2, c2, gtl, stl, o);
-                if (!*abort_flag && !mbar_wait_backoff(&empty[st], ((it / GQ_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) *abort_flag = 1;
+                decode_group_f16_s<16>(aux0, aux1, s2, c2, gtl, stl, o);
+                if (!*abort_flag && !mbar_wait(&empty[st], ((it / GQ_NST) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY)) *abort_flag = 1;
                 tc_fence_after();
-                tmem_st16(tmem + lane_base + st * GQ_A_COLS + gsel * 16, o);
+                tmem_st16(tmem + lane_base + gq_a_col(st) + gsel * 16, o);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -292,21 +318,30 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
                 const float dw = dnext * 0.125f;                            // d * (0.5 + scale) * 0.25 = d/8 * A's factor
                 if (sb + 1 < GQ_NSB) dnext = __half2float(dptr[(size_t)(sb + 1) * (BLK_IQ2 / 2)]);
                 const uint32_t b = psb & 1;
-                if (!bad && (*abort_flag || !mbar_wait_backoff(&pfull[b], (psb >> 1) & 1, p.err, DEV_ERR_TIMEOUT_FULL))) bad = true;
+                if (!bad && (*abort_flag || !mbar_wait(&pfull[b], (psb >> 1) & 1, p.err, DEV_ERR_TIMEOUT_FULL))) bad = true;
                 if (!bad) {
                     tc_fence_after();
                     const uint32_t tP = tmem + lane_base + GQ_P_COL + b * GQ_P_COLS;
+                    const int n2 = 2 * n16, nacc = gq_nacc(n2);
                     for (int c0 = 0; c0 < n16; c0 += 16) {
-                        float hi[16], lo[16], r[16];
-                        tmem_ld16(tP + c0, hi);
-                        tmem_ld16(tP + n16 + c0, lo);
+                        float sum[16], r[16];
+                        #pragma unroll
+                        for (int i = 0; i < 16; ++i) sum[i] = 0.0f;
+                        for (int j = 0; j < nacc; ++j) {           // P = sum over the accumulators of hi + lo
+                            uint32_t hi[16], lo[16];
+                            tmem_ld16_nowait(tP + j * n2 + c0, hi);
+                            tmem_ld16_nowait(tP + j * n2 + n16 + c0, lo);
+                            tmem_ld_wait();
+                            #pragma unroll
+                            for (int i = 0; i < 16; ++i) sum[i] += __uint_as_float(hi[i]) + __uint_as_float(lo[i]);
+                        }
                         if (sb == 0) {
                             #pragma unroll
-                            for (int i = 0; i < 16; ++i) r[i] = dw * (hi[i] + lo[i]);
+                            for (int i = 0; i < 16; ++i) r[i] = dw * sum[i];
                         } else {
                             tmem_ld16(tR + c0, r);
                             #pragma unroll
-                            for (int i = 0; i < 16; ++i) r[i] = fmaf(dw, hi[i] + lo[i], r[i]);
+                            for (int i = 0; i < 16; ++i) r[i] = fmaf(dw, sum[i], r[i]);
                         }
                         if (sb + 1 < GQ_NSB || mat == 0) {
                             tmem_st16f(tR + c0, r);                         // running sum (g kept here at the end)

@@ -17,6 +17,10 @@ constexpr uint32_t F16_PAIR_LO = 0x642B1908u;            // bytes 08 19 2B 64
 constexpr uint32_t F16_PAIR_HI = 0x63AACEF0u;            // bytes F0 CE AA 63
 constexpr int IQ2TC_GTAB = 256 * 32 * 8;                 // 64 KB grid pair selectors (32 lane copies)
 constexpr int IQ2TC_STAB = 128 * 32 * 8;                 // 32 KB sign pair selectors
+// the same tables with 16 lane copies: a warp's 64-bit loads are served per half-warp, so lanes l and l + 16
+// share copy l & 15 without a bank conflict
+constexpr int IQ2TC_GTAB16 = 256 * 16 * 8;               // 32 KB
+constexpr int IQ2TC_STAB16 = 128 * 16 * 8;               // 16 KB
 
 __device__ __forceinline__ uint32_t pair_codes(uint64_t g, int a) {   // elements a, a+1 of grid entry g
     const uint32_t ma = (uint32_t)(g >> (8 * a)) & 0xFFu, mb = (uint32_t)(g >> (8 * a + 8)) & 0xFFu;
@@ -46,18 +50,34 @@ __device__ __forceinline__ void init_pair_tables(uint2* gt, uint2* st, int tid, 
     }
 }
 
+// 16-copy layout: entry i of copy l at (i * 16 + l) * 8 bytes
+__device__ __forceinline__ void init_pair_tables16(uint2* gt, uint2* st, int tid, int nthr) {
+    for (int t = tid; t < (256 + 128) * 16; t += nthr) {
+        const int e = t >> 4, l = t & 15;
+        if (e < 256) {
+            const uint64_t g = c_iq2_grid[e];
+            gt[e * 16 + l] = make_uint2(pair_codes(g, 0) | (pair_codes(g, 2) << 16), pair_codes(g, 4) | (pair_codes(g, 6) << 16));
+        } else {
+            const uint32_t k = iq2_ksigns((uint32_t)(e - 256));
+            st[(e - 256) * 16 + l] = make_uint2(pair_signs(k, 0) | (pair_signs(k, 2) << 16), pair_signs(k, 4) | (pair_signs(k, 6) << 16));
+        }
+    }
+}
+
 __device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d; asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c)); return d;
 }
 
 // decode one IQ2_XXS group (32 weights) into 16 fp16x2 words in K order (word j = elements 2j, 2j+1), each
-// weight times the fp16 scale whose broadcast pair is s2 (c2 = the pair of -1024 * that scale, exact)
+// weight times the fp16 scale whose broadcast pair is s2 (c2 = the pair of -1024 * that scale, exact);
+// COPIES = the lane copies of the tables (32 or 16), gtl/stl already offset to this lane's copy
+template <int COPIES = 32>
 __device__ __forceinline__ void decode_group_f16_s(uint32_t aux0, uint32_t aux1, uint32_t s2, uint32_t c2,
                                                    const uint2* gtl, const uint2* stl, uint32_t (&o)[16]) {
     #pragma unroll
     for (int l = 0; l < 4; ++l) {
-        const uint2 g = gtl[((aux0 >> (8 * l)) & 0xFFu) * 32];
-        const uint2 sg = stl[((aux1 >> (7 * l)) & 0x7Fu) * 32];
+        const uint2 g = gtl[((aux0 >> (8 * l)) & 0xFFu) * COPIES];
+        const uint2 sg = stl[((aux1 >> (7 * l)) & 0x7Fu) * COPIES];
         const uint32_t sx = g.x | sg.x, sy = g.y | sg.y;
         o[4 * l + 0] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx), s2, c2);
         o[4 * l + 1] = hfma2_u32(__byte_perm(F16_PAIR_LO, F16_PAIR_HI, sx >> 16), s2, c2);

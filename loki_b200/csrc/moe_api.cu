@@ -145,7 +145,7 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     c->g_max = max_slots_for(T, KE, NE, GEMM_NT, cfg->with_shared);
     LK_CU(dalloc(&c->g_expert, c->g_max)); LK_CU(dalloc(&c->g_tok, (size_t)c->g_max * GEMM_NT));
     LK_CU(dalloc(&c->g_out, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_w, (size_t)c->g_max * GEMM_NT)); LK_CU(dalloc(&c->g_n, 1));
-    LK_CU(dalloc(&c->bt, gate_q8_tile_halfs(c->g_max))); LK_CU(dalloc(&c->ht, gemm_tile_halfs(c->g_max, true)));
+    LK_CU(dalloc(&c->bt, gate_q8_tile_halfs(c->g_max))); LK_CU(dalloc(&c->ht, down_tile_halfs(c->g_max)));
     LK_CU(dalloc(&c->g_cnt, c->g_max));
     c->m_max = max_slots_for(T, KE, NE, MM_NT, cfg->with_shared);
     LK_CU(dalloc(&c->m_expert, c->m_max)); LK_CU(dalloc(&c->m_tok, (size_t)c->m_max * MM_NT));
@@ -302,7 +302,7 @@ static int run_batch_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, in
         launch_build_slots(ms, st);
         MmaParams m{};
         m.down = (const uint8_t*)W->down; m.down_stride = W->down_stride; m.sh_down = (const uint8_t*)W->sh_down;
-        m.T = T; m.slot_expert = c->m_expert; m.slot_tok = c->m_tok; m.slot_out = c->m_out; m.slot_w = c->m_w; m.nslots = c->m_n;
+        m.slot_expert = c->m_expert; m.slot_tok = c->m_tok; m.slot_out = c->m_out; m.slot_w = c->m_w; m.nslots = c->m_n;
         m.max_slots = c->m_max; m.slot_cnt = c->m_cnt; m.hb = c->hb; m.y = c->y; m.err = c->err;
         if (W->down_fmt == LK_FMT_IQ2) {
             launch_slot_mma_down(m, c->nsm, st);      // its prep pass writes slot_cnt

@@ -129,43 +129,37 @@ struct GemmParams {
     const float* x; int ld_x; int T;                  // activations [T][HIDDEN] fp32
     const int* slot_expert; const int* slot_tok; const int* slot_out; const float* slot_w; const int* nslots;  // [slot][GEMM_NT]
     int max_slots;
-    int* slot_cnt;                                    // [max_slots] tokens per slot (written by the B-tile pre-pass)
-    __half* bt;                                       // gate/up B tiles [max_slots][HIDDEN/64][64x64 fp16]
-    __half* ht;                                       // down B tiles (SwiGLU output) [max_slots][MOE_INTER/64][64x64]
+    int* slot_cnt;                                    // [max_slots] tokens per slot (written by the gate/up B-tile pre-pass)
+    __half* bt;                                       // gate/up activation tiles [max_slots][HIDDEN/128][2 halves][hi, lo rows][128]
+    __half* ht;                                       // down B tiles (fp16 of the q8 h) [max_slots][MOE_INTER/128][N x 128]
     float* y;                                         // [rows][HIDDEN] weighted expert outputs
     int* err;
     __half* hb;                                       // optional: the SwiGLU output as fp16 rows [entry][MOE_INTER]
-                                                      //   instead of the down B tiles (launch_prefill_gemm_gate_up)
+                                                      //   instead of the down B tiles (the mma.sync downs read them)
 };
-void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st);
-void launch_prefill_gemm_gate_up(const GemmParams& p, int grid, cudaStream_t st);   // the gate/up GEMM alone
-void launch_prefill_gemm_down(const GemmParams& p, int grid, cudaStream_t st);      // the IQ2_XXS down GEMM alone (reads ht)
-size_t gemm_tile_halfs(int max_slots, bool down);     // size of bt (down = false) / ht (down = true)
+// the IQ2_XXS down GEMM (prefill_gemm.cu), reading the B tiles ht that launch_gate_up_q8 wrote (hb null)
+void launch_prefill_gemm_down(const GemmParams& p, int grid, cudaStream_t st);
+size_t down_tile_halfs(int max_slots);                // size of ht in halfs
 // the gate/up + SwiGLU phase with the reference's q8 numerics (gate_up_q8.cu): exact products, h re-quantised
 // to q8 per 32; writes fp16(q*d) as the down GEMM's B tiles (ht) or, with hb set, as fp16 rows [entry][MOE_INTER].
 // bt must hold gate_q8_tile_halfs(max_slots) halfs (hi and lo activation rows per token half).
 void launch_gate_up_q8(const GemmParams& p, int grid, cudaStream_t st);
 size_t gate_q8_tile_halfs(int max_slots);
 
-// ---- register-fed mma.sync grouped products (mid-size T): slots of up to MM_NT tokens
+// ---- register-fed mma.sync downs (slot_mma.cu IQ2_XXS, kq_mma.cu Q2_K / Q3_K): slots of up to MM_NT tokens
+//      reading the fp16 q8 SwiGLU rows that the q8 gate/up wrote
 struct MmaParams {
-    const uint8_t* gate; const uint8_t* up; const uint8_t* down;
-    int64_t gate_stride, up_stride, down_stride;
-    const uint8_t* sh_gate; const uint8_t* sh_up; const uint8_t* sh_down;
-    const float* x; int ld_x; int T;                  // activations [T][HIDDEN] fp32, rows ld_x floats apart
+    const uint8_t* down; int64_t down_stride; const uint8_t* sh_down;
     const int* slot_expert; const int* slot_tok; const int* slot_out; const float* slot_w; const int* nslots;  // [slot][MM_NT]
     int max_slots;
-    int* slot_cnt;                                    // [max_slots] tokens per slot (written by the pre-pass)
-    __half* xh;                                       // [T][HIDDEN] fp16 of the q8-dequantised x
+    int* slot_cnt;                                    // [max_slots] tokens per slot (slot_mma's prep pass; null: counted in-kernel)
     __half* hb;                                       // [rows][MOE_INTER] fp16 SwiGLU output
     float* y;                                         // [rows][HIDDEN] weighted expert outputs
     int* err;
 };
-void launch_slot_mma(const MmaParams& p, int nsm, cudaStream_t st);
-// the IQ2_XXS down alone on MM_NT slots, reading the fp16 SwiGLU rows hb (x and xh unused)
+// the IQ2_XXS down on MM_NT slots (its prep pass writes slot_cnt)
 void launch_slot_mma_down(const MmaParams& p, int nsm, cudaStream_t st);
-// the gate/up phase alone (SwiGLU output as fp16 rows hb), then the Q2_K / Q3_K down on mma.sync (kq_mma.cu)
-void launch_slot_mma_gate_up(const MmaParams& p, int nsm, cudaStream_t st);
+// the Q2_K / Q3_K down on MM_NT slots (kq_mma.cu)
 void launch_kq_mma_down(const MmaParams& p, int down_fmt, int nsm, cudaStream_t st);
 
 // ---- seeded IQ2_XXS weight generation (moe_format.h generator) for n_experts consecutive experts

@@ -1,24 +1,19 @@
-// prefill_gemm.cu -- the prefill / batch regime: grouped expert GEMMs on the 5th-generation tensor cores.
+// prefill_gemm.cu -- the IQ2_XXS down projection of the tensor-core regime (T >= the GEMM threshold) on the
+// 5th-generation tensor cores.  The gate/up + SwiGLU phase before it is gate_up_q8.cu, whose epilogue writes this
+// kernel's B tiles: fp16 of the q8-re-quantised h (the reference's swiglu_q8, src/fused_layer.cu:334-341).
 //
-// Replaces the wide pass's tc_matvec<F_IQ2> (mma.sync int8, 8 rows per slot; reference
-// src/fused_layer.cu:540-553) for slots of up to 128 tokens per expert.  Per work item (slot, row tile):
-//   D[128 weight rows x N tokens] = A[128 x K] . B[N x K]^T   with tcgen05.mma.cta_group::1.kind::f16,
-//   fp32 accumulators in tensor memory (two tiles per item: gate+up rows, or two 128-row halves of down),
-//   N = the slot's token count rounded up to 16 (up to 128).  Measured per tcgen05.mma (M=128, K=16, issued
-//   warp-uniformly): 39 cycles at N=16, 64 at N=128, 128 at N=256 -- the decode of A, not the tensor pipe,
-//   sets the pace for the token counts of a prefill chunk.
+// Replaces the wide pass's tc_matvec down (mma.sync int8; reference src/fused_layer.cu:540-553) for slots of up to
+// 128 tokens per expert.  Per work item (slot, pair of 128-row tiles of the 7168 output rows):
+//   D[128 weight rows x N tokens] = A[128 x 2048] . B[N x 2048]^T   with tcgen05.mma.cta_group::1.kind::f16,
+//   fp32 accumulators in tensor memory (two tiles per item), N = the slot's token count rounded up to 16 (up to
+//   128).  The two tiles' MMAs alternate, so two accumulators are in flight.  The down is linear in its inputs,
+//   so A = fp16(v * s), s = fp16(d*(2*scale+1)/8), rounds each weight once (~2.4e-4) and that error passes to
+//   the output unamplified.
 //
-// A (weights) never touches shared memory as fp16: the IQ2_XXS groups are decoded in registers and
-// written to tensor memory with tcgen05.st (thread = weight row = TMEM lane, 32 weights = 16 columns), and
-// the MMA reads A from tensor memory.  Decode trick: for a weight v in {+-8, +-25, +-43}, fp16(1024 + v)
-// has a low byte in {08, 19, 2B, F0, CE, AA} and a high byte in {64, 63} -- eight bytes -- so one
-// byte-permute over the constant pair (0x642B1908, 0x63AACEF0) yields two fp16 values 1024+v; the selectors
-// are the OR of a per-grid-entry table (codes) and a per-sign-index table (signs), both 64-bit and
-// lane-private in shared memory.  One hfma2 (x*s - 1024*s, 1024*s exact) gives v*s, s = fp16(d*(2*scale+1)/8).
-// B (activations) arrives as pre-tiled K-blocks (UMMA K-major core-matrix layout, N rows, LBO = N/8 * 128
-// bytes): gate/up tiles from k_gate_b_tiles (fp16 of the q8-dequantised x of each slot's tokens), down
-// tiles written by the gate/up epilogue (h = silu(g)*u at fp16: with 16-bit operands a q8 re-quantisation
-// would only turn their rounding into q8 boundary flips).  One bulk copy (1-D TMA) per K-block.
+// A (weights) never touches shared memory as fp16: the IQ2_XXS groups are decoded in registers (iq2_tc.cuh) and
+// written to tensor memory with tcgen05.st (thread = weight row = TMEM lane, 32 weights = 16 columns), and the MMA
+// reads A from tensor memory.  B arrives as pre-tiled K-blocks (UMMA K-major core-matrix layout, N rows, LBO =
+// N/8 * 128 bytes), one bulk copy (1-D TMA) per K-block.
 //
 // Warp roles (608 threads, one CTA per SM, persistent over (slot, tile) items); one pipeline stage is a
 // 128-deep K-block (4 IQ2 groups), two stages in flight:
@@ -89,25 +84,13 @@ __device__ __forceinline__ void umma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, ui
                  :: "r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
 
-// global weight row `r` (0..255) of work item (slot expert e, row tile rt): gate/up rows 0-127 gate,
-// 128-255 up (tile rows rt*128..); down rows rt*256 + r
-template <bool DOWN>
+// global down row of weight row r (0..255) of work item (slot expert e, tile pair rt): rows rt*256 + r
 __device__ __forceinline__ const uint8_t* item_row(const GemmParams& p, int e, int rt, int r, size_t rowbytes) {
-    const int mat = r >> 7, row = r & (PG_M - 1);
-    const uint8_t* wm;
-    int grow;
-    if (DOWN) {
-        wm = e == SHARED_SLOT ? p.sh_down : p.down + (size_t)e * p.down_stride;
-        grow = rt * 2 * PG_M + mat * PG_M + row;
-    } else {
-        wm = e == SHARED_SLOT ? (mat ? p.sh_up : p.sh_gate) : (mat ? p.up + (size_t)e * p.up_stride : p.gate + (size_t)e * p.gate_stride);
-        grow = rt * PG_M + row;
-    }
-    return wm + (size_t)grow * rowbytes;
+    const uint8_t* wm = e == SHARED_SLOT ? p.sh_down : p.down + (size_t)e * p.down_stride;
+    return wm + (size_t)(rt * 2 * PG_M + r) * rowbytes;
 }
 
-template <bool DOWN>
-__global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
+__global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_down(GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const uint2* gtab = (const uint2*)(smem + PG_OFF_GTAB);
     const uint2* stab = (const uint2*)(smem + PG_OFF_STAB);
@@ -126,13 +109,13 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
     volatile int* abort_flag = (volatile int*)(smem + PG_OFF_MISC + 4);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nslots = *p.nslots;
-    constexpr int TILES = DOWN ? HIDDEN / (2 * PG_M) : MOE_INTER / PG_M;   // 28 down pairs, 16 gate/up tiles
+    constexpr int TILES = HIDDEN / (2 * PG_M);                            // 28 pairs of 128-row tiles
     const int nitems = nslots * TILES;
     if ((int)blockIdx.x >= nitems) return;
-    constexpr int K = DOWN ? MOE_INTER : HIDDEN;
+    constexpr int K = MOE_INTER;
     constexpr int NKB = K / PG_KB;
     const size_t rowbytes = (size_t)(K / QK) * BLK_IQ2;
-    const __half* btiles = DOWN ? p.ht : p.bt;
+    const __half* btiles = p.ht;
 
     init_pair_tables((uint2*)(smem + PG_OFF_GTAB), (uint2*)(smem + PG_OFF_STAB), tid, PG_THREADS);
     if (tid == 0) {
@@ -158,7 +141,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
             const int s = item % nslots, rt = item / nslots;
             const int e = p.slot_expert[s];
             __syncwarp();
-            for (int r = lane; r < 2 * PG_M; r += 32) rowp[r] = (uintptr_t)item_row<DOWN>(p, e, rt, r, rowbytes);
+            for (int r = lane; r < 2 * PG_M; r += 32) rowp[r] = (uintptr_t)item_row(p, e, rt, r, rowbytes);
             __syncwarp();
             for (int sb = 0; sb < K / QK; ++sb, ++rit) {
                 const int rs = rit % PG_RAW_NST;
@@ -251,7 +234,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
         for (int i = 0, item = blockIdx.x; item < nitems; ++i, item += gridDim.x) {
             const int s = item % nslots, rt = item / nslots;
             const int e = p.slot_expert[s];
-            const uintptr_t wrow = (uintptr_t)item_row<DOWN>(p, e, rt, mat * PG_M + row, rowbytes);   // global row
+            const uintptr_t wrow = (uintptr_t)item_row(p, e, rt, mat * PG_M + row, rowbytes);   // global row
             for (int kb = 0; kb < NKB; ++kb, ++it) {
                 const int st = it % PG_NST, rs = rit % PG_RAW_NST;
                 if ((kb & 1) == 0 && !*abort_flag && !mbar_wait_backoff(&rawfull[rs], (rit / PG_RAW_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))
@@ -286,7 +269,7 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
             // ------------------------------------------------ epilogue of item i
             if (!mbar_wait_backoff(accfull, i & 1, p.err, DEV_ERR_TIMEOUT_FULL)) { *abort_flag = 1; break; }
             tc_fence_after();
-            const int cnt = p.slot_cnt[s], n16 = round16(cnt);
+            const int cnt = p.slot_cnt[s];
             for (int cc = warp >> 2; cc * 16 < cnt; cc += 4) {              // tokens 16cc..16cc+15
                 const uint32_t t0 = tmem + (uint32_t)(cc * 16) + lane_base;
                 float v0[16], v1[16];
@@ -296,23 +279,11 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
                 for (int j = 0; j < 16; ++j) {
                     const int n = cc * 16 + j;
                     if (n < cnt) {
-                        if (DOWN) {
-                            const int out = p.slot_out[s * PG_NMAX + n];
-                            const float w = p.slot_w[s * PG_NMAX + n];
-                            const int r0 = rt * 2 * PG_M + row;
-                            p.y[(size_t)out * HIDDEN + r0] = w * v0[j];
-                            p.y[(size_t)out * HIDDEN + r0 + PG_M] = w * v1[j];
-                        } else {                          // h = silu(g)*u -> the down GEMM's B tile of this slot
-                            const int hj = rt * PG_M + row;
-                            __half* tile = p.ht + ((size_t)s * (MOE_INTER / PG_KB) + hj / PG_KB) * (PG_B_TILE / 2);
-                            const __half hv = __float2half_rn(lk_swiglu(v0[j], v1[j]));
-                            if (p.hb) {                   // fp16 rows for a down kernel of its own (K-quant downs)
-                                const int out = p.slot_out[s * PG_NMAX + n];
-                                if (out >= 0) p.hb[(size_t)out * MOE_INTER + hj] = hv;
-                            } else {
-                                *(__half*)((uint8_t*)tile + btile_off(n, hj % PG_KB, n16)) = hv;
-                            }
-                        }
+                        const int out = p.slot_out[s * PG_NMAX + n];
+                        const float w = p.slot_w[s * PG_NMAX + n];
+                        const int r0 = rt * 2 * PG_M + row;
+                        p.y[(size_t)out * HIDDEN + r0] = w * v0[j];
+                        p.y[(size_t)out * HIDDEN + r0 + PG_M] = w * v1[j];
                     }
                 }
             }
@@ -326,63 +297,12 @@ __global__ void __launch_bounds__(PG_THREADS, 1) k_prefill_gemm(GemmParams p) {
     if (warp == PG_MMA_WARP) { tc_fence_after(); tmem_dealloc(tmem, PG_TMEM_COLS); }
 }
 
-// gate/up B tiles: for slot s and K-block kb, the fp16 of the q8-dequantised x of the slot's tokens in the
-// UMMA K-major core-matrix layout of round16(count) rows (pad rows zero); also the slot's token count
-constexpr int PG_BT_THREADS = PG_NMAX * (PG_KB / 32);   // one thread per (token row, 32-group of the K-block)
-__global__ void __launch_bounds__(PG_BT_THREADS) k_gate_b_tiles(GemmParams p) {
-    const int s = blockIdx.x, kb = blockIdx.y, tid = threadIdx.x;
-    if (s >= *p.nslots) return;
-    const int n = tid / (PG_KB / 32), g = tid % (PG_KB / 32);   // token row, 32-group within the K-block
-    const int tok = p.slot_tok[s * PG_NMAX + n];
-    const int cnt = __syncthreads_count(tok >= 0) / (PG_KB / 32);   // pads are at the end of the slot
-    if (kb == 0 && tid == 0) p.slot_cnt[s] = cnt;
-    const int n16 = round16(cnt);
-    if (n >= n16) return;
-    float v[32];
-    if (tok >= 0) {
-        const float4* src = (const float4*)(p.x + (size_t)tok * p.ld_x + kb * PG_KB + g * 32);
-        #pragma unroll
-        for (int j = 0; j < 8; ++j) { const float4 a = src[j]; v[4*j] = a.x; v[4*j+1] = a.y; v[4*j+2] = a.z; v[4*j+3] = a.w; }
-    } else {
-        #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.0f;
-    }
-    int8_t qv[32];
-    const float d = quant_q8_group(v, qv);
-    uint8_t* tile = (uint8_t*)(p.bt + ((size_t)s * (HIDDEN / PG_KB) + kb) * (PG_B_TILE / 2));
-    #pragma unroll
-    for (int c = 0; c < 4; ++c) {                        // 4 k8 blocks of 8 fp16 (16 bytes) each
-        uint32_t w[4];
-        #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-            const int j = c * 8 + 2 * h;
-            w[h] = (uint32_t)__half_as_ushort(__float2half_rn((float)qv[j] * d)) |
-                   ((uint32_t)__half_as_ushort(__float2half_rn((float)qv[j + 1] * d)) << 16);
-        }
-        *(uint4*)(tile + btile_off(n, g * 32 + c * 8, n16)) = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-}
-
-template <bool DOWN> static void pg_launch(const GemmParams& p, int grid, cudaStream_t st) {
+void launch_prefill_gemm_down(const GemmParams& p, int grid, cudaStream_t st) {
     static bool attr = false;
-    if (!attr) { cudaFuncSetAttribute(k_prefill_gemm<DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, PG_SMEM); attr = true; }
-    k_prefill_gemm<DOWN><<<grid, PG_THREADS, PG_SMEM, st>>>(p);
+    if (!attr) { cudaFuncSetAttribute(k_prefill_down, cudaFuncAttributeMaxDynamicSharedMemorySize, PG_SMEM); attr = true; }
+    k_prefill_down<<<grid, PG_THREADS, PG_SMEM, st>>>(p);
 }
 
-void launch_prefill_gemm_gate_up(const GemmParams& p, int grid, cudaStream_t st) {
-    k_gate_b_tiles<<<dim3(p.max_slots, HIDDEN / PG_KB), PG_BT_THREADS, 0, st>>>(p);
-    pg_launch<false>(p, grid, st);
-}
-
-void launch_prefill_gemm_down(const GemmParams& p, int grid, cudaStream_t st) { pg_launch<true>(p, grid, st); }
-
-void launch_prefill_gemm(const GemmParams& p, int grid, cudaStream_t st) {
-    launch_prefill_gemm_gate_up(p, grid, st);
-    pg_launch<true>(p, grid, st);
-}
-
-size_t gemm_tile_halfs(int max_slots, bool down) {
-    return (size_t)max_slots * ((down ? MOE_INTER : HIDDEN) / PG_KB) * (PG_B_TILE / 2);
-}
+size_t down_tile_halfs(int max_slots) { return (size_t)max_slots * (MOE_INTER / PG_KB) * (PG_B_TILE / 2); }
 
 }  // namespace lk

@@ -1,26 +1,22 @@
-// slot_mma.cu -- the mid-size regime (2 <= T < the tcgen05 threshold): grouped expert products with the
-// IQ2_XXS weights dequantised straight into mma.sync A fragments in registers.
+// slot_mma.cu -- the IQ2_XXS down projection of the mid-size regime (the mma threshold <= T < the GEMM threshold)
+// with the weights dequantised straight into mma.sync A fragments in registers.  Its input is the fp16 of the
+// q8-re-quantised SwiGLU output that gate_up_q8.cu wrote as rows hb[entry][MOE_INTER].
 //
-// Why not tcgen05 here: a tcgen05.mma of M=128, K=16 occupies the tensor pipe ~128 cycles whatever N is
-// (N <= 256; measured), so with 2..64 tokens per expert the weights-on-M GEMM (prefill_gemm.cu) is bound by
-// MMA instructions, not by bytes; and putting the weights on N instead routes every decoded weight through
-// shared memory (written, then read by the tensor core) next to the decode tables.  Here each decoded
-// weight goes from the byte-permute straight into an mma.sync.m16n8k16 fragment and is reused for every
-// 8-token N tile of the slot (slots of up to MM_NT = 32 tokens).
+// Why not tcgen05 here: with 2..16 tokens per expert slot the weights-on-M GEMM (prefill_gemm.cu) is bound by MMA
+// instructions, not by bytes.  Here each decoded weight goes from the byte-permute straight into an
+// mma.sync.m16n8k16 fragment and is reused for every 8-token N tile of the slot (slots of up to MM_NT tokens).
 //
 // K permutation: mma's A fragment gives lane (g = lane/4, c = lane%4) the K positions {2c, 2c+1, 2c+8,
 // 2c+9} of each 16-deep step.  Within each 32-deep IQ2 group the kernel maps fragment position
 // p = 16*ks + 8*h + 2*c + e to weight k = 8*c + 4*ks + 2*h + e, so lane c's eight positions over the two
 // steps are exactly the 8 weights of the group's grid entry c -- one table lookup pair, four byte-permutes,
-// four hfma2 -- and the B fragments of token n are the 16 contiguous activations x[n][32j + 8c .. +8], one
+// four hfma2 -- and the B fragments of token n are the 16 contiguous activations h[n][32j + 8c .. +8], one
 // 16-byte load (the dot product is unchanged by permuting K on both sides).
 //
-// Per work item (slot, row block): gate/up -- 128 h rows, each of 8 warps owns 16 gate rows and the same
-// 16 up rows (two m16 tiles), so SwiGLU pairs inside one thread's accumulators; down -- 256 rows, 32 per
-// warp.  A copy warp stages each weight row's next IQ2 superblock (80-byte 16-aligned window, 16-byte
-// cp.async, coalesced) into a 3-stage raw ring; the decode tables are 16-lane private (64-bit lookups are
-// served per half-warp, so lanes l and l+16 share a copy without bank conflicts).  B rows: gate/up the fp16
-// of the q8-dequantised x (k_x_q8_f16), down the fp16 SwiGLU output; both L2-resident.
+// Per work item (slot, block of 256 output rows): each of 8 warps owns 32 rows (two m16 tiles).  A copy warp
+// stages each weight row's next IQ2 superblock (80-byte 16-aligned window, 16-byte cp.async, coalesced) into a
+// 3-stage raw ring; the decode tables are 16-lane private (64-bit lookups are served per half-warp, so lanes l
+// and l+16 share a copy without bank conflicts).  The B rows are L2-resident.
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
@@ -87,17 +83,10 @@ __device__ __forceinline__ void mm_cp_async_arrive(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(smem_u32(bar)) : "memory");
 }
 
-// global weight row r (0..255) of item (expert e, row block rb): gate/up r < 128 gate, else up (rows
-// rb*128 + r % 128); down rows rb*256 + r
-template <bool DOWN>
+// global down row of weight row r (0..255) of item (expert e, row block rb): rows rb*256 + r
 __device__ __forceinline__ const uint8_t* mm_row(const MmaParams& p, int e, int rb, int r) {
-    if (DOWN) {
-        const uint8_t* wm = e == SHARED_SLOT ? p.sh_down : p.down + (size_t)e * p.down_stride;
-        return wm + (size_t)(rb * 256 + r) * ((MOE_INTER / QK) * BLK_IQ2);
-    }
-    const int mat = r >> 7;
-    const uint8_t* wm = e == SHARED_SLOT ? (mat ? p.sh_up : p.sh_gate) : (mat ? p.up + (size_t)e * p.up_stride : p.gate + (size_t)e * p.gate_stride);
-    return wm + (size_t)(rb * 128 + (r & 127)) * ((HIDDEN / QK) * BLK_IQ2);
+    const uint8_t* wm = e == SHARED_SLOT ? p.sh_down : p.down + (size_t)e * p.down_stride;
+    return wm + (size_t)(rb * 256 + r) * ((MOE_INTER / QK) * BLK_IQ2);
 }
 
 // the two A fragments (k steps 0, 1) of one row's grid entry c of a group, i.e. weights 8c..8c+7 in the
@@ -120,8 +109,7 @@ __device__ __forceinline__ void mm_scale(float d, uint32_t aux1, uint32_t& s2, u
     c2 = (uint32_t)__half_as_ushort(__hmul(hs, __float2half_rn(-1024.0f))) * 0x10001u;
 }
 
-template <bool DOWN>
-__global__ void __launch_bounds__(MM_THREADS, 2) k_slot_mma(MmaParams p) {
+__global__ void __launch_bounds__(MM_THREADS, 2) k_slot_mma_down(MmaParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint8_t* raw = smem + MM_OFF_RAW;
     uint64_t* rawfull = (uint64_t*)(smem + MM_OFF_BAR);
@@ -130,8 +118,8 @@ __global__ void __launch_bounds__(MM_THREADS, 2) k_slot_mma(MmaParams p) {
     volatile int* abort_flag = (volatile int*)(smem + MM_OFF_MISC);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nslots = *p.nslots;
-    constexpr int BLOCKS = DOWN ? HIDDEN / 256 : MOE_INTER / 128;        // row blocks per slot: 28 / 16
-    constexpr int K = DOWN ? MOE_INTER : HIDDEN;
+    constexpr int BLOCKS = HIDDEN / 256;                                  // row blocks per slot: 28
+    constexpr int K = MOE_INTER;
     constexpr int NSB = K / QK;
     const int nitems = nslots * BLOCKS;
     if ((int)blockIdx.x >= nitems) return;
@@ -152,7 +140,7 @@ __global__ void __launch_bounds__(MM_THREADS, 2) k_slot_mma(MmaParams p) {
             const int s = item % nslots, rb = item / nslots;
             const int e = p.slot_expert[s];
             __syncwarp();
-            for (int r = lane; r < MM_RAW_ROWS; r += 32) rowp[r] = (uintptr_t)mm_row<DOWN>(p, e, rb, r);
+            for (int r = lane; r < MM_RAW_ROWS; r += 32) rowp[r] = (uintptr_t)mm_row(p, e, rb, r);
             __syncwarp();
             for (int sb = 0; sb < NSB; ++sb, ++rit) {
                 const int rs = rit % MM_RAW_NST;
@@ -183,7 +171,7 @@ __global__ void __launch_bounds__(MM_THREADS, 2) k_slot_mma(MmaParams p) {
     for (int t = 0; t < 2; ++t)
         #pragma unroll
         for (int h = 0; h < 2; ++h)
-            rr[t][h] = DOWN ? 32 * warp + 16 * t + g + 8 * h : 128 * t + 16 * warp + g + 8 * h;
+            rr[t][h] = 32 * warp + 16 * t + g + 8 * h;
     uint32_t rit = 0;
     for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
         const int s = item % nslots, rb = item / nslots;
@@ -191,19 +179,19 @@ __global__ void __launch_bounds__(MM_THREADS, 2) k_slot_mma(MmaParams p) {
         const int cnt = p.slot_cnt[s];
         const int n8 = (cnt + 7) >> 3;
         // B rows of this thread's token in each N tile (token n = 8*nt + g): element offsets, -1 = none
-        const __half* bbase = DOWN ? p.hb : p.xh;
+        const __half* bbase = p.hb;
         int boff[MM_NT / 8];
         #pragma unroll
         for (int nt = 0; nt < MM_NT / 8; ++nt) {
             const int n = 8 * nt + g;
-            const int src = n < cnt ? (DOWN ? p.slot_out[s * MM_NT + n] : p.slot_tok[s * MM_NT + n]) : -1;
+            const int src = n < cnt ? p.slot_out[s * MM_NT + n] : -1;
             boff[nt] = src >= 0 ? src * K + 8 * c : -1;
         }
         uint32_t wlo[2][2];                            // low bits of the global rows: the superblock's offset in its window
         #pragma unroll
         for (int t = 0; t < 2; ++t)
             #pragma unroll
-            for (int h = 0; h < 2; ++h) wlo[t][h] = (uint32_t)(uintptr_t)mm_row<DOWN>(p, e, rb, rr[t][h]);
+            for (int h = 0; h < 2; ++h) wlo[t][h] = (uint32_t)(uintptr_t)mm_row(p, e, rb, rr[t][h]);
         float acc[2][MM_NT / 8][4];
         #pragma unroll
         for (int t = 0; t < 2; ++t)
@@ -277,63 +265,29 @@ __global__ void __launch_bounds__(MM_THREADS, 2) k_slot_mma(MmaParams p) {
                 if (n >= cnt) continue;
                 const int out = p.slot_out[s * MM_NT + n];
                 if (out < 0) continue;
-                if (DOWN) {
-                    const float w = p.slot_w[s * MM_NT + n];
-                    const int row = rb * 256 + 32 * warp + g + 8 * (i >> 1);
-                    p.y[(size_t)out * HIDDEN + row] = w * acc[0][nt][i];
-                    p.y[(size_t)out * HIDDEN + row + 16] = w * acc[1][nt][i];
-                } else {
-                    const int hrow = rb * 128 + 16 * warp + g + 8 * (i >> 1);
-                    p.hb[(size_t)out * MOE_INTER + hrow] = __float2half_rn(lk_swiglu(acc[0][nt][i], acc[1][nt][i]));
-                }
+                const float w = p.slot_w[s * MM_NT + n];
+                const int row = rb * 256 + 32 * warp + g + 8 * (i >> 1);
+                p.y[(size_t)out * HIDDEN + row] = w * acc[0][nt][i];
+                p.y[(size_t)out * HIDDEN + row + 16] = w * acc[1][nt][i];
             }
         }
     }
 }
 
-// x (fp32 [T][ld]) -> fp16 of its q8-per-32 dequantisation; slot_cnt of every slot (pads are at the end)
-__global__ void k_mma_prep(MmaParams p) {
+// each slot's token count (pads are at the end of the slot)
+__global__ void k_mma_counts(MmaParams p) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < *p.nslots) {
-        int cnt = 0;
-        while (cnt < MM_NT && p.slot_tok[i * MM_NT + cnt] >= 0) ++cnt;
-        p.slot_cnt[i] = cnt;
-    }
-    if (i >= p.T * (HIDDEN / 32)) return;
-    const int t = i / (HIDDEN / 32), grp = i % (HIDDEN / 32);
-    float v[32];
-    const float4* src = (const float4*)(p.x + (size_t)t * p.ld_x + grp * 32);
-    #pragma unroll
-    for (int j = 0; j < 8; ++j) { const float4 a = src[j]; v[4*j] = a.x; v[4*j+1] = a.y; v[4*j+2] = a.z; v[4*j+3] = a.w; }
-    int8_t q[32];
-    const float d = quant_q8_group(v, q);
-    __half2* dst = (__half2*)(p.xh + (size_t)t * HIDDEN + grp * 32);
-    #pragma unroll
-    for (int j = 0; j < 16; ++j) dst[j] = __halves2half2(__float2half_rn((float)q[2*j] * d), __float2half_rn((float)q[2*j+1] * d));
-}
-
-template <bool DOWN> static void mm_launch(const MmaParams& p, int grid, cudaStream_t st) {
-    static bool attr = false;
-    if (!attr) { cudaFuncSetAttribute(k_slot_mma<DOWN>, cudaFuncAttributeMaxDynamicSharedMemorySize, MM_SMEM); attr = true; }
-    k_slot_mma<DOWN><<<grid, MM_THREADS, MM_SMEM, st>>>(p);
-}
-
-void launch_slot_mma_gate_up(const MmaParams& p, int nsm, cudaStream_t st) {
-    const int n = p.T * (HIDDEN / 32) > p.max_slots ? p.T * (HIDDEN / 32) : p.max_slots;
-    k_mma_prep<<<(n + 255) / 256, 256, 0, st>>>(p);
-    mm_launch<false>(p, 2 * nsm, st);
+    if (i >= *p.nslots) return;
+    int cnt = 0;
+    while (cnt < MM_NT && p.slot_tok[i * MM_NT + cnt] >= 0) ++cnt;
+    p.slot_cnt[i] = cnt;
 }
 
 void launch_slot_mma_down(const MmaParams& p, int nsm, cudaStream_t st) {
-    MmaParams q = p;
-    q.T = 0;                                          // the prep pass only counts each slot's tokens
-    k_mma_prep<<<(q.max_slots + 255) / 256, 256, 0, st>>>(q);
-    mm_launch<true>(q, 2 * nsm, st);
-}
-
-void launch_slot_mma(const MmaParams& p, int nsm, cudaStream_t st) {
-    launch_slot_mma_gate_up(p, nsm, st);
-    mm_launch<true>(p, 2 * nsm, st);
+    static bool attr = false;
+    if (!attr) { cudaFuncSetAttribute(k_slot_mma_down, cudaFuncAttributeMaxDynamicSharedMemorySize, MM_SMEM); attr = true; }
+    k_mma_counts<<<(p.max_slots + 255) / 256, 256, 0, st>>>(p);
+    k_slot_mma_down<<<2 * nsm, MM_THREADS, MM_SMEM, st>>>(p);
 }
 
 }  // namespace lk
