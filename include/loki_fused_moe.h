@@ -56,7 +56,9 @@ extern "C" {
 struct FLCtx;
 typedef struct FLCtx FLCtx;
 typedef struct CUevent_st* fl_event_t;        /* == cudaEvent_t */
+#ifndef LOKI_FL_NO_FORMAT_ENUM   /* a translation unit that already has src/fused_layer.h's identical enum defines this */
 enum { FL_Q4K = 0, FL_Q6K = 1, FL_Q80 = 2, FL_Q5K = 3, FL_IQ2 = 4, FL_Q2K = 5, FL_Q3K = 6 };
+#endif
 
 /* host (pinned) mirrors filled by fl_fetch / fl_moe / fl_skip / fl_wide_finish; null where not produced.
  * Field order and meaning as the reference's FLOut. */
@@ -108,6 +110,45 @@ LK_API void   fl_use_graphs(FLCtx* c, int enable);
 /* additive: last error recorded on the context (0 = none), cleared by the call */
 LK_API int    fl_moe_error(FLCtx* c);
 LK_API void   fl_free(FLCtx* c);
+
+/* ---- The same entry points under the lkfl_ prefix (identical behaviour), and three calls for a bridge library
+ * that re-exports all of src/fused_layer.h with its attention half from the reference's own fused_layer.cu
+ * (loki_b200/csrc/fl_bridge.cu, built as libloki_fused.so).  No counterpart in the reference: the prefix lets the
+ * bridge define fl_* itself and still reach this library in the same process. */
+LK_API FLCtx* lkfl_init(int kvp, int sc_cap);
+LK_API void   lkfl_free(FLCtx* c);
+LK_API int    lkfl_moe_error(FLCtx* c);
+LK_API void   lkfl_h2d(FLCtx* c, void* dst, const void* src, size_t bytes);
+LK_API void   lkfl_wait_event(FLCtx* c, fl_event_t ev);
+LK_API double lkfl_gpu_ms(FLCtx* c, int which);
+LK_API void   lkfl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow);
+LK_API void   lkfl_fetch(FLCtx* c, int n, int what, FLOut* out);
+LK_API void   lkfl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int nexp, int down_fmt,
+                       const int* ids, const float* w, int KE, int n, FLOut* out);
+LK_API void   lkfl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int renorm, int n,
+                            FLOut* out);
+LK_API void   lkfl_use_graphs(FLCtx* c, int enable);
+LK_API void   lkfl_skip(FLCtx* c, const float* mo, int n, FLOut* out);
+LK_API void   lkfl_moe_outs(FLCtx* c, int b, const int* ids, const float* w, int KE, float* out);
+LK_API int    lkfl_wide_init(FLCtx* c, int wmax, int KE);
+LK_API void   lkfl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int nexp,
+                            const int* midx, const int* rows, const int* kidx, const float* wk, int nslots, int KE, int par);
+LK_API void   lkfl_wide_mark(FLCtx* c, int par);
+LK_API void   lkfl_wide_wait(FLCtx* c, int par);
+LK_API void   lkfl_wide_finish(FLCtx* c, int n, int KE, FLOut* out);
+LK_API void   lkfl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out);
+LK_API void   lkfl_wide_outs(FLCtx* c, int row, int KE, float* out);
+/* bridge: a context that runs on `stream` (a cudaStream_t it does not own: the attention context's), so the two
+ * halves of a layer are ordered without events */
+LK_API FLCtx* lkfl_init_on_stream(void* stream);
+/* bridge: take over the MoE inputs that the attention half left on the device for N rows -- ncur, ffn_inp
+ * ([N][7168]), the router's top-8 ids / weights ([N][8]) and the shared expert's output as n_parts partial sums
+ * shared_parts[k][row] (k < n_parts, part_rows rows apart) -- instead of recomputing them (fl_moe_prepare's role);
+ * wrow >= 0 places the rows in the wide pass's buffers as fl_moe_prepare does.  Stream-ordered, no host wait. */
+LK_API void   lkfl_moe_adopt(FLCtx* c, const float* ncur, const float* ffn_inp, const float* shared_parts, int n_parts,
+                             size_t part_rows, const int* sel, const float* wts, int N, int wrow);
+/* bridge: the device rows of h written by the last fl_moe / fl_moe_auto / fl_skip ([n][7168]) */
+LK_API const float* lkfl_device_h(FLCtx* c);
 
 #ifdef __cplusplus
 }

@@ -84,10 +84,38 @@ def build(force=False, verbose=False, ptxas_verbose=False):
     return LIB
 
 
+BRIDGE_SRC = os.path.join(CSRC, "fl_bridge.cu")
+BRIDGE_LIB = os.path.join(HERE, "libloki_fused.so")
+
+
+def build_bridge(ref, force=False, verbose=False):
+    """libloki_fused.so: the engine-facing library exporting all of the reference's src/fused_layer.h -- its
+    attention half compiled from the reference checkout `ref` (src/fused_layer.cu, included at build time), its MoE
+    half this library (csrc/fl_bridge.cu).  Needs LIB built first."""
+    src_ref = os.path.join(ref, "src", "fused_layer.cu")
+    deps = [BRIDGE_SRC, LIB, src_ref, os.path.join(CSRC, "..", "..", "include", "loki_fused_moe.h")]
+    if not force and not _stale(BRIDGE_LIB, deps):
+        return BRIDGE_LIB
+    cmd = [nvcc(), "-ccbin", host_cxx()] + ARCH + ["-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+                                                "-w", "-shared", "-I" + os.path.join(ref, "src"), BRIDGE_SRC, "-o", BRIDGE_LIB,
+                                                "-L" + HERE, "-lloki_moe", "-Xlinker", "-rpath=$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("bridge build failed")
+    return BRIDGE_LIB
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
     ap.add_argument("--ptxas", action="store_true", help="print -Xptxas -v register/spill/smem reports")
+    ap.add_argument("--reference", default=os.environ.get("LOKI_REFERENCE"),
+                    help="reference checkout: also build libloki_fused.so (the engine-facing bridge)")
     a = ap.parse_args()
     print(build(a.force, a.verbose, a.ptxas))
+    if a.reference:
+        print(build_bridge(a.reference, a.force, a.verbose))

@@ -27,6 +27,7 @@ constexpr int P8 = PREP_ROWS * MAX_TOPK;           // router outputs of a prepar
 
 struct FLCtx {
     cudaStream_t st = nullptr; int dev = 0, nsm = 0;
+    bool own_stream = true;           // false: the stream was given to lkfl_init_on_stream (an attention context's)
     // prepare / narrow state (device)
     float* ncur = nullptr; float* ffn_inp = nullptr; float* logits = nullptr; float* probs = nullptr;
     int* sel = nullptr; float* wts = nullptr; float* shared_y = nullptr; float* h = nullptr; float* moe = nullptr;
@@ -75,6 +76,8 @@ struct FLCtx {
     std::vector<GraphEntry> graphs; bool use_graphs = true;
 };
 constexpr size_t FL_MAX_GRAPHS = 1024;
+
+void impl_fl_free(FLCtx* c);
 
 static int fl_fail(FLCtx* c, int code, const char* what, cudaError_t e = cudaSuccess) {
     std::fprintf(stderr, "[loki_moe] %s%s%s\n", what, e != cudaSuccess ? ": " : "", e != cudaSuccess ? cudaGetErrorString(e) : "");
@@ -130,11 +133,13 @@ static ExpertParams expert_params(FLCtx* c, const void* gate, const void* up, co
     return e;
 }
 
-extern "C" {
 
-FLCtx* fl_init(int kvp, int sc_cap) {
+// ext: run on the caller's stream (not owned) instead of a stream of the context's own
+FLCtx* impl_fl_init(int kvp, int sc_cap, cudaStream_t ext = nullptr) {
     (void)kvp; (void)sc_cap;          // attention-side sizes: not used by the MoE path
     FLCtx* c = new FLCtx();
+    c->own_stream = ext == nullptr;
+    if (ext) c->st = ext;
     cudaGetDevice(&c->dev);
     c->nsm = num_sms(c->dev);
     const size_t R = (size_t)PREP_ROWS * HIDDEN;
@@ -144,7 +149,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
     float *io = nullptr, *ho = nullptr, *h_io = nullptr, *h_ho = nullptr;
     int *iwe = nullptr, *sw = nullptr, *h_iwe = nullptr, *h_sw = nullptr;
     bool ok =
-        cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) == cudaSuccess &&
+        (ext || cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) == cudaSuccess) &&
         dz(&io, 2 * R) == cudaSuccess && dz(&ho, 2 * R) == cudaSuccess && dz(&iwe, 3 * NARROW_SLOTS) == cudaSuccess &&
         dz(&sw, 2 * P8) == cudaSuccess && hz(&h_io, 2 * R) == cudaSuccess && hz(&h_ho, 2 * R) == cudaSuccess &&
         hz(&h_iwe, 3 * NARROW_SLOTS) == cudaSuccess && hz(&h_sw, 2 * P8) == cudaSuccess &&
@@ -163,7 +168,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
         cudaEventCreateWithFlags(&c->eh2d, cudaEventDisableTiming) == cudaSuccess;
     c->blk[0] = io; c->blk[1] = ho; c->blk[2] = iwe; c->blk[3] = sw;
     c->hblk[0] = h_io; c->hblk[1] = h_ho; c->hblk[2] = h_iwe; c->hblk[3] = h_sw;
-    if (!ok) { fl_fail(c, LK_ERR_CUDA, "fl_init: allocation failed", cudaGetLastError()); fl_free(c); return nullptr; }
+    if (!ok) { fl_fail(c, LK_ERR_CUDA, "fl_init: allocation failed", cudaGetLastError()); impl_fl_free(c); return nullptr; }
     c->ncur = io; c->ffn_inp = io + R; c->h = ho; c->moe = ho + R;
     c->ids = iwe; c->w = (float*)(iwe + NARROW_SLOTS); c->err = iwe + 2 * NARROW_SLOTS;
     c->sel = sw; c->wts = (float*)(sw + P8);
@@ -173,7 +178,7 @@ FLCtx* fl_init(int kvp, int sc_cap) {
     return c;
 }
 
-void fl_free(FLCtx* c) {
+void impl_fl_free(FLCtx* c) {
     if (!c) return;
     if (c->st) cudaStreamSynchronize(c->st);
     void* d[] = { c->blk[0], c->blk[1], c->blk[2], c->blk[3], c->logits, c->probs, c->shared_y, c->sh_gu, c->sh_pair, c->mo,
@@ -193,20 +198,20 @@ void fl_free(FLCtx* c) {
     for (auto& g : c->graphs) if (g.exec) cudaGraphExecDestroy(g.exec);
     cudaEvent_t ev[] = { c->em0, c->em1, c->ep0, c->ep1, c->eh2d };
     for (cudaEvent_t e : ev) if (e) cudaEventDestroy(e);
-    if (c->st) cudaStreamDestroy(c->st);
+    if (c->st && c->own_stream) cudaStreamDestroy(c->st);
     delete c;
 }
 
-int fl_moe_error(FLCtx* c) { if (!c) return LK_ERR_ARG; const int e = c->last_err; c->last_err = 0; return e; }
+int impl_fl_moe_error(FLCtx* c) { if (!c) return LK_ERR_ARG; const int e = c->last_err; c->last_err = 0; return e; }
 
-void fl_h2d(FLCtx* c, void* dst, const void* src, size_t bytes) {
+void impl_fl_h2d(FLCtx* c, void* dst, const void* src, size_t bytes) {
     if (!c || !bytes) return;
     FLCK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, c->st));
 }
 
-void fl_wait_event(FLCtx* c, fl_event_t ev) { if (c) FLCK(cudaStreamWaitEvent(c->st, (cudaEvent_t)ev, 0)); }
+void impl_fl_wait_event(FLCtx* c, fl_event_t ev) { if (c) FLCK(cudaStreamWaitEvent(c->st, (cudaEvent_t)ev, 0)); }
 
-double fl_gpu_ms(FLCtx* c, int which) { return !c ? 0.0 : which == 1 ? c->ms_moe : c->ms_prep; }
+double impl_fl_gpu_ms(FLCtx* c, int which) { return !c ? 0.0 : which == 1 ? c->ms_moe : c->ms_prep; }
 
 // event record that is also a graph node while the stream is being captured
 static cudaError_t rec(cudaEvent_t ev, cudaStream_t st) {
@@ -295,7 +300,7 @@ static void ensure_shared(FLCtx* c) {
     c->sh_pending = false;
 }
 
-void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
+void impl_fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
     if (!c || !W || !ncur || !ffn_inp || N < 1 || N > PREP_ROWS) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: bad argument"); return; }
     if (wrow >= 0 && (!c->ncur_all || wrow + N > c->wmax)) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: wide rows outside fl_wide_init capacity"); return; }
     if (W->sh_fmt != 0 && W->sh_fmt != FL_IQ2 && W->sh_fmt != FL_Q5K) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe_prepare: shared-expert format must be FL_IQ2 or FL_Q5K"); return; }
@@ -347,7 +352,7 @@ void fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* f
     FLCK(cudaGetLastError());
 }
 
-void fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
+void impl_fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
     if (!c || !out) return;
     std::memset(out, 0, sizeof(FLOut));
     n = std::min(n, c->prep_n > 0 ? c->prep_n : n);
@@ -412,7 +417,7 @@ static void finish_narrow(FLCtx* c, int KE, int n, bool ids_back, FLOut* out) {
     out->h = c->h_h; out->moe = c->h_moe;
 }
 
-void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int nexp, int down_fmt, const int* ids, const float* w,
+void impl_fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int nexp, int down_fmt, const int* ids, const float* w,
             int KE, int n, FLOut* out) {
     if (!c || !out) return;
     std::memset(out, 0, sizeof(FLOut));
@@ -445,7 +450,6 @@ void fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int ne
     finish_narrow(c, KE, n, false, out);
 }
 
-}  // extern "C"
 
 // the engine's keep-KE pass (src/server_core_fused.cpp:793-813, without --share-experts) on the device: row i
 // of the router output (sel8 / w8 [n][8], top-8 by score) -> its KE highest-weight experts (equal weights in
@@ -502,9 +506,8 @@ __global__ void k_fl_keep1(Keep1Params p) {
     *p.sn = p.KE + (p.fold ? 1 : 0);
 }
 
-extern "C" {
 
-void fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int renorm, int n, FLOut* out) {
+void impl_fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int renorm, int n, FLOut* out) {
     if (!c || !out) return;
     std::memset(out, 0, sizeof(FLOut));
     if (!down_fmt_ok(down_fmt)) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe_auto: down format must be FL_IQ2, FL_Q2K or FL_Q3K"); return; }
@@ -536,9 +539,9 @@ void fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* down, i
     finish_narrow(c, KE, n, true, out);
 }
 
-void fl_use_graphs(FLCtx* c, int enable) { if (c) c->use_graphs = enable != 0; }
+void impl_fl_use_graphs(FLCtx* c, int enable) { if (c) c->use_graphs = enable != 0; }
 
-void fl_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
+void impl_fl_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
     if (!c || !out || !mo || n < 1 || n > PREP_ROWS) return;
     std::memset(out, 0, sizeof(FLOut));
     cudaStream_t st = c->st;
@@ -555,7 +558,7 @@ void fl_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
     out->h = c->h_h;
 }
 
-void fl_moe_outs(FLCtx* c, int b, const int* ids, const float* w, int KE, float* out) {
+void impl_fl_moe_outs(FLCtx* c, int b, const int* ids, const float* w, int KE, float* out) {
     if (!c || !ids || !w || !out || b < 0 || b >= c->last_n || KE != c->last_ke) { fl_fail(c, LK_ERR_ARG, "fl_moe_outs: no matching narrow pass"); return; }
     std::vector<float> rows((size_t)KE * HIDDEN);
     FLCK(cudaStreamSynchronize(c->st));
@@ -569,7 +572,7 @@ void fl_moe_outs(FLCtx* c, int b, const int* ids, const float* w, int KE, float*
     }
 }
 
-int fl_wide_init(FLCtx* c, int wmax, int KE) {
+int impl_fl_wide_init(FLCtx* c, int wmax, int KE) {
     if (!c || wmax < 1 || KE < 1 || KE > MAX_TOPK) return 0;
     c->wmax = wmax; c->wke = KE;
     const size_t R = (size_t)wmax * HIDDEN;
@@ -591,7 +594,7 @@ int fl_wide_init(FLCtx* c, int wmax, int KE) {
     return 1;
 }
 
-void fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int nexp, const int* midx, const int* rows,
+void impl_fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int nexp, const int* midx, const int* rows,
                  const int* kidx, const float* wk, int nslots, int KE, int par) {
     if (!c || !c->ncur_all) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: fl_wide_init first"); return; }
     if (!down_fmt_ok(down_fmt)) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_wide_moe: down format must be FL_IQ2, FL_Q2K or FL_Q3K"); return; }
@@ -672,10 +675,10 @@ void fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, i
     FLCK(cudaGetLastError());
 }
 
-void fl_wide_mark(FLCtx* c, int par) { if (c && c->wev[par & 1]) FLCK(cudaEventRecord(c->wev[par & 1], c->st)); }
-void fl_wide_wait(FLCtx* c, int par) { if (c && c->wev[par & 1]) FLCK(cudaEventSynchronize(c->wev[par & 1])); }
+void impl_fl_wide_mark(FLCtx* c, int par) { if (c && c->wev[par & 1]) FLCK(cudaEventRecord(c->wev[par & 1], c->st)); }
+void impl_fl_wide_wait(FLCtx* c, int par) { if (c && c->wev[par & 1]) FLCK(cudaEventSynchronize(c->wev[par & 1])); }
 
-void fl_wide_finish(FLCtx* c, int n, int KE, FLOut* out) {
+void impl_fl_wide_finish(FLCtx* c, int n, int KE, FLOut* out) {
     if (!c || !out) return;
     std::memset(out, 0, sizeof(FLOut));
     if (!c->ncur_all || n < 1 || n > c->wmax || KE != c->wke) { fl_fail(c, LK_ERR_ARG, "fl_wide_finish: bad argument"); return; }
@@ -695,7 +698,7 @@ void fl_wide_finish(FLCtx* c, int n, int KE, FLOut* out) {
     out->h = c->h_wh; out->moe = c->h_wmoe;
 }
 
-void fl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
+void impl_fl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
     if (!c || !out || !mo || !c->ncur_all || n < 1 || n > c->wmax) return;
     std::memset(out, 0, sizeof(FLOut));
     cudaStream_t st = c->st;
@@ -710,10 +713,86 @@ void fl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
     out->h = c->h_wh;
 }
 
-void fl_wide_outs(FLCtx* c, int row, int KE, float* out) {
+void impl_fl_wide_outs(FLCtx* c, int row, int KE, float* out) {
     if (!c || !out || !c->out_all || row < 0 || row >= c->wmax || KE != c->wke) { fl_fail(c, LK_ERR_ARG, "fl_wide_outs: bad argument"); return; }
     FLCK(cudaStreamSynchronize(c->st));
     FLCK(cudaMemcpy(out, c->out_all + (size_t)row * KE * HIDDEN, (size_t)KE * HIDDEN * 4, cudaMemcpyDeviceToHost));
 }
 
+// ---- the attention context's MoE inputs, taken over (lkfl_moe_adopt)
+// shared_y[i] = sum over the n_parts partial sums parts[k][i] ([k][part_rows][HIDDEN])
+__global__ void k_sum_parts(const float* __restrict__ parts, int n_parts, size_t part_rows, int n, float* __restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)n * HIDDEN) return;
+    float v = 0.0f;
+    for (int k = 0; k < n_parts; ++k) v += parts[(size_t)k * part_rows * HIDDEN + i];
+    out[i] = v;
+}
+
+void impl_fl_moe_adopt(FLCtx* c, const float* ncur, const float* ffn_inp, const float* shared_parts, int n_parts, size_t part_rows,
+                       const int* sel, const float* wts, int N, int wrow) {
+    if (!c || !ncur || !ffn_inp || !sel || !wts || N < 1 || N > PREP_ROWS || n_parts < 0 || (n_parts > 0 && !shared_parts)) {
+        fl_fail(c, LK_ERR_ARG, "lkfl_moe_adopt: bad argument"); return;
+    }
+    if (wrow >= 0 && (!c->ncur_all || wrow + N > c->wmax)) { fl_fail(c, LK_ERR_ARG, "lkfl_moe_adopt: wide rows outside fl_wide_init capacity"); return; }
+    cudaStream_t st = c->st;
+    const size_t bytes = (size_t)N * HIDDEN * 4;
+    c->prep_n = N; c->sh_pending = false; c->sh_in_y_n = 0;
+    FLCK(cudaMemcpyAsync(c->ncur, ncur, bytes, cudaMemcpyDeviceToDevice, st));
+    FLCK(cudaMemcpyAsync(c->ffn_inp, ffn_inp, bytes, cudaMemcpyDeviceToDevice, st));
+    FLCK(cudaMemcpyAsync(c->sel, sel, (size_t)N * MAX_TOPK * 4, cudaMemcpyDeviceToDevice, st));
+    FLCK(cudaMemcpyAsync(c->wts, wts, (size_t)N * MAX_TOPK * 4, cudaMemcpyDeviceToDevice, st));
+    if (n_parts > 0) k_sum_parts<<<(unsigned)(((size_t)N * HIDDEN + 255) / 256), 256, 0, st>>>(shared_parts, n_parts, part_rows, N, c->shared_y);
+    else FLCK(cudaMemsetAsync(c->shared_y, 0, bytes, st));
+    if (wrow >= 0) {                  // wide pass: this group's ncur and base = ffn_inp + shared
+        FLCK(cudaMemcpyAsync(c->ncur_all + (size_t)wrow * HIDDEN, c->ncur, bytes, cudaMemcpyDeviceToDevice, st));
+        CombineParams cp{};
+        cp.y = nullptr; cp.resid = c->ffn_inp; cp.T = N; cp.keep = 0; cp.with_shared = 0; cp.shared = c->shared_y;
+        cp.h = c->base_all + (size_t)wrow * HIDDEN; cp.moe = nullptr; cp.ld_out = HIDDEN;
+        launch_combine(cp, st);
+    }
+    FLCK(cudaGetLastError());
+}
+
+// ---- the exported entry points: each under its fused_layer.h name (fl_*) and under lkfl_*, the names a
+// bridge library calls when it re-exports fl_* itself (fl_bridge.cu).  The implementations above are internal
+// to this library, so a process that loads both libraries never routes this library's own calls into the
+// bridge's fl_* symbols.
+#define LKFL_EXPORT(ret, name, params, args) \
+    LK_API ret fl_##name params { return impl_fl_##name args; } \
+    LK_API ret lkfl_##name params { return impl_fl_##name args; }
+
+extern "C" {
+LKFL_EXPORT(FLCtx*, init, (int kvp, int sc_cap), (kvp, sc_cap))
+LKFL_EXPORT(void, free, (FLCtx* c), (c))
+LKFL_EXPORT(int, moe_error, (FLCtx* c), (c))
+LKFL_EXPORT(void, h2d, (FLCtx* c, void* dst, const void* src, size_t bytes), (c, dst, src, bytes))
+LKFL_EXPORT(void, wait_event, (FLCtx* c, fl_event_t ev), (c, ev))
+LKFL_EXPORT(double, gpu_ms, (FLCtx* c, int which), (c, which))
+LKFL_EXPORT(void, moe_prepare, (FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow),
+            (c, W, ncur, ffn_inp, N, host, wrow))
+LKFL_EXPORT(void, fetch, (FLCtx* c, int n, int what, FLOut* out), (c, n, what, out))
+LKFL_EXPORT(void, moe, (FLCtx* c, const void* gate, const void* up, const void* down, int nexp, int down_fmt, const int* ids,
+                        const float* w, int KE, int n, FLOut* out), (c, gate, up, down, nexp, down_fmt, ids, w, KE, n, out))
+LKFL_EXPORT(void, moe_auto, (FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int renorm, int n,
+                             FLOut* out), (c, gate, up, down, down_fmt, KE, renorm, n, out))
+LKFL_EXPORT(void, use_graphs, (FLCtx* c, int enable), (c, enable))
+LKFL_EXPORT(void, skip, (FLCtx* c, const float* mo, int n, FLOut* out), (c, mo, n, out))
+LKFL_EXPORT(void, moe_outs, (FLCtx* c, int b, const int* ids, const float* w, int KE, float* out), (c, b, ids, w, KE, out))
+LKFL_EXPORT(int, wide_init, (FLCtx* c, int wmax, int KE), (c, wmax, KE))
+LKFL_EXPORT(void, wide_moe, (FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int nexp, const int* midx,
+                             const int* rows, const int* kidx, const float* wk, int nslots, int KE, int par),
+            (c, gate, up, down, down_fmt, nexp, midx, rows, kidx, wk, nslots, KE, par))
+LKFL_EXPORT(void, wide_mark, (FLCtx* c, int par), (c, par))
+LKFL_EXPORT(void, wide_wait, (FLCtx* c, int par), (c, par))
+LKFL_EXPORT(void, wide_finish, (FLCtx* c, int n, int KE, FLOut* out), (c, n, KE, out))
+LKFL_EXPORT(void, wide_skip, (FLCtx* c, const float* mo, int n, FLOut* out), (c, mo, n, out))
+LKFL_EXPORT(void, wide_outs, (FLCtx* c, int row, int KE, float* out), (c, row, KE, out))
+
+LK_API FLCtx* lkfl_init_on_stream(void* stream) { return impl_fl_init(0, 0, (cudaStream_t)stream); }
+LK_API void lkfl_moe_adopt(FLCtx* c, const float* ncur, const float* ffn_inp, const float* shared_parts, int n_parts, size_t part_rows,
+                           const int* sel, const float* wts, int N, int wrow) {
+    impl_fl_moe_adopt(c, ncur, ffn_inp, shared_parts, n_parts, part_rows, sel, wts, N, wrow);
+}
+LK_API const float* lkfl_device_h(FLCtx* c) { return c ? c->h : nullptr; }
 }  // extern "C"

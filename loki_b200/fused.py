@@ -147,11 +147,22 @@ def replay_decode(fc, layers, x, resid, KE, warmup, steps, down_fmt=FL_IQ2, devi
 
 
 class FusedCtx:
-    def __init__(self, kvp=512, sc_cap=64):
-        self.c = lib().fl_init(kvp, sc_cap)
+    def __init__(self, kvp=512, sc_cap=64, stream=None):
+        """stream: a cudaStream_t (int) the context runs on without owning it (lkfl_init_on_stream, the bridge's
+        way of putting the MoE half on the attention context's stream); default: a stream of its own."""
+        self.c = lib().fl_init(kvp, sc_cap) if stream is None else lib().lkfl_init_on_stream(ctypes.c_void_p(stream))
         if not self.c:
             raise N.NativeError("fl_init failed")
         self.out = N.FLOut()
+
+    def adopt(self, ncur_ptr, ffn_ptr, parts_ptr, n_parts, part_rows, sel_ptr, wts_ptr, n, wrow=-1):
+        """lkfl_moe_adopt: take over device rows left by an attention half (ncur, ffn_inp, top-8 ids / weights, the
+        shared expert's output as n_parts partial sums [k][part_rows][7168]) instead of fl_moe_prepare."""
+        P = ctypes.c_void_p
+        lib().lkfl_moe_adopt(self.c, P(ncur_ptr), P(ffn_ptr), P(parts_ptr), n_parts, part_rows, P(sel_ptr), P(wts_ptr), n, wrow)
+
+    def device_h(self):
+        return lib().lkfl_device_h(self.c)
 
     def close(self):
         if self.c:

@@ -110,7 +110,12 @@ SIGNATURES = {
     "fl_moe_auto": (None, [_P, _P, _P, _P, _I, _I, _I, _I, ctypes.POINTER(FLOut)]),
     "fl_use_graphs": (None, [_P, _I]),
     "fl_free": (None, [_P]),
+    "lkfl_init_on_stream": (_P, [_P]),
+    "lkfl_moe_adopt": (None, [_P, _P, _P, _P, _I, _S, _P, _P, _I, _I]),
+    "lkfl_device_h": (_P, [_P]),
 }
+# the fused-layer entry points also under the lkfl_ prefix (what a bridge library that re-exports fl_* calls)
+SIGNATURES.update({"lk" + k: v for k, v in list(SIGNATURES.items()) if k.startswith("fl_")})
 
 _lib = None
 

@@ -14,7 +14,7 @@ def declared():
     names = []
     for h in HEADERS:
         txt = open(h).read()
-        names += re.findall(r"^LK_API\s+[\w\s\*]+?\b((?:lk|fl)_\w+)\s*\(", txt, re.M)
+        names += re.findall(r"^LK_API\s+[\w\s\*]+?\b((?:lkfl|lk|fl)_\w+)\s*\(", txt, re.M)
     return names
 
 

@@ -177,3 +177,103 @@ def test_fl_graphs_match_direct_launches(native, fl_layer, device_keep):
         finally:
             fc.close()
     np.testing.assert_array_equal(hs[0], hs[1])
+
+
+def oracle_layer_slots(oracle, x, r, ids, w, fmt):
+    """The oracle layer with its per-entry pushes (y_slot [T][KE][7168]) and shared-expert output."""
+    from moe_helpers import host_arena, down_bytes, shared_fmts, MAT
+    used = sorted(set(int(e) for e in ids.reshape(-1)))
+    remap = {e: i for i, e in enumerate(used)}
+    cids = np.vectorize(lambda e: remap[int(e)])(ids).astype(np.int32)
+    gate, up, down, sh = host_arena(oracle, SEED, 5, used, fmt, 4)
+    shg, shu, shd = sh if fmt == 4 else (None, None, None)
+    gf, df = shared_fmts(fmt, 4)
+    return oracle.moe_layer(x, r, gate, up, down, MAT, cids, w, shg, shu, shd, want_slots=True, down_fmt=fmt,
+                            down_stride=down_bytes(fmt), sh_gu_fmt=gf, sh_down_fmt=df)
+
+
+def test_fl_attribution_and_skip_vs_oracle(native, oracle, fl_layer):
+    """fl_moe_outs (narrow pass) and fl_wide_outs (wide pass) return each row's weighted expert pushes -- the
+    reference's out_all rows (src/fused_layer.cu:569-576) -- and fl_skip / fl_wide_skip add a stored output to the
+    shared expert and residual (:562-566, :613-618); all against the oracle's per-entry outputs."""
+    from loki_b200 import fused as F
+    fmt, W = fl_layer
+    n, KE = 6, 4
+    rng = np.random.default_rng(77 + fmt)
+    x = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    mo_stored = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    fc = F.FusedCtx()
+    try:
+        assert fc.wide_init(8, KE) == 1
+        fc.prepare(_mw(native, W, fmt), x, r)
+        got = fc.fetch(n, 1)
+        ids, w = F.keep_pass(got["sel"], got["wts"], KE)
+        fc.moe(W.gate, W.up, W.down, 256, ids, w, down_fmt=fmt)
+        ref = oracle_layer_slots(oracle, x, r, ids, w, fmt)
+        for b in range(n):
+            pushes = fc.moe_outs(b, ids[b], w[b])
+            assert rel_l2(pushes, ref["y_slot"][b]) < RTOL_L2, b
+        # fl_skip: h = stored output + shared expert + residual of the last prepare's rows
+        h = fc.skip(mo_stored)
+        want = mo_stored + r + (ref["shared"] if fmt == 4 else 0.0)
+        assert rel_l2(h, want) < RTOL_L2
+        # the same rows as a wide pass (one group), then its attribution and the wide skip
+        fc.prepare(_mw(native, W, fmt), x, r, wrow=0)
+        used = sorted(set(int(e) for e in ids.reshape(-1)))
+        for i, (batch, midx, rows, kidx, wk) in enumerate(F.wide_slots(ids, w, KE, used, eb=4)):
+            par = i & 1
+            if i >= 2:
+                fc.wide_wait(par)
+            fc.wide_moe(W.gate, W.up, W.down, 256, [batch[u] for u in midx], rows, kidx, wk, KE, par, down_fmt=fmt)
+            fc.wide_mark(par)
+        hw, mw_ = fc.wide_finish(n, KE)
+        assert rel_l2(mw_, ref["moe"]) < RTOL_L2
+        for row in range(n):
+            assert rel_l2(fc.wide_outs(row, KE), ref["y_slot"][row]) < RTOL_L2, row
+        hs = fc.wide_skip(mo_stored)
+        assert rel_l2(hs, mo_stored + r + (ref["shared"] if fmt == 4 else 0.0)) < RTOL_L2
+        assert fc.error() == 0
+    finally:
+        fc.close()
+
+
+def test_adopt_matches_prepare(native, oracle, fl_layer):
+    """The bridge's hand-off (libloki_fused.so): a context on a given stream that adopts ncur, ffn_inp, the router's
+    top-8 and the shared expert's output as two partial sums [2][8 rows][7168] (the layout the reference's fl_attn
+    leaves, src/fused_layer.cu:521-525) gives the narrow pass's h / moe of a context that ran fl_moe_prepare on
+    the same rows; lkfl_device_h holds the h rows the bridge hands to the next layer's attention."""
+    import ctypes
+    from loki_b200 import fused as F
+    fmt, W = fl_layer
+    n, KE = 5, 8
+    rng = np.random.default_rng(99 + fmt)
+    x = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    r = rng.standard_normal((n, HIDDEN)).astype(np.float32)
+    fa = F.FusedCtx()
+    stream = torch.cuda.Stream()
+    fb = F.FusedCtx(stream=stream.cuda_stream)
+    try:
+        fa.prepare(_mw(native, W, fmt), x, r)
+        got = fa.fetch(n, 1)
+        ids, w = F.keep_pass(got["sel"], got["wts"], KE)
+        h1, mo1 = [a.copy() for a in fa.moe(W.gate, W.up, W.down, 256, ids, w, down_fmt=fmt)]
+        shared = (h1 - mo1 - r).astype(np.float32)
+        parts = np.zeros((2, 8, HIDDEN), np.float32)
+        parts[0, :n] = shared * np.float32(0.5)
+        parts[1, :n] = shared - parts[0, :n]
+        dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        xd, rd, pd, sd, wd = dev(x), dev(r), dev(parts), dev(got["sel"]), dev(got["wts"])
+        torch.cuda.synchronize()
+        fb.adopt(xd.data_ptr(), rd.data_ptr(), pd.data_ptr(), 2, 8, sd.data_ptr(), wd.data_ptr(), n)
+        h2, mo2 = fb.moe(W.gate, W.up, W.down, 256, ids, w, down_fmt=fmt)
+        assert fa.error() == 0 and fb.error() == 0
+        assert rel_l2(mo2, mo1) < 1e-6 and rel_l2(h2, h1) < 1e-6
+        hdev = np.empty((n, HIDDEN), np.float32)
+        cu = ctypes.CDLL("libcuda.so.1")                   # the driver's copy, on the context torch made current
+        cu.cuMemcpyDtoH_v2.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_size_t]
+        assert cu.cuMemcpyDtoH_v2(hdev.ctypes.data, fb.device_h(), n * HIDDEN * 4) == 0
+        assert np.array_equal(hdev, h2)
+    finally:
+        fa.close()
+        fb.close()
