@@ -99,6 +99,21 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // independent accumulators per P buffer for N' = 2 * round16(tokens) columns each (a power of two, <= 4)
 __device__ __forceinline__ int gq_nacc(int n2) { return n2 <= 32 ? 4 : (n2 <= 64 ? 2 : 1); }
 
+// the 8 MMAs of one K-block with N' = N2 known at compile time: instruction descriptor, B step and accumulator
+// offsets are immediates (a runtime descriptor measured ~2x slower per tcgen05.mma)
+template <int N2>
+__device__ __forceinline__ void gq_issue_kblock(uint32_t d, uint32_t a0, uint32_t bring_st, int kb) {
+    constexpr int nacc = N2 <= 32 ? 4 : (N2 <= 64 ? 2 : 1);
+    constexpr uint32_t idesc = idesc_f16_f32(GQ_M, N2);
+    constexpr uint32_t lbo = (uint32_t)(N2 >> 3) * 128;
+    constexpr uint64_t bstep = (uint64_t)((2 * lbo) >> 4);             // one K=16 step along the B tile
+    const uint64_t b0 = umma_desc(bring_st, lbo, 128);
+    #pragma unroll
+    for (int ks = 0; ks < GQ_KB / 16; ++ks)                              // K step ks -> accumulator ks % nacc
+        umma_f16_ta_warp(d + (uint32_t)((ks % nacc) * N2), a0 + ks * 8, b0 + (uint64_t)ks * bstep, idesc,
+                         (kb & 1) || ks >= nacc);
+}
+
 __device__ __forceinline__ void tmem_st16f(uint32_t taddr, const float (&v)[16]) {
     uint32_t r[16];
     #pragma unroll
@@ -226,10 +241,6 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
             int s, rt, nh, cnt_h;
             if (!gq_item(p, item, nslots, s, rt, nh, cnt_h)) continue;
             const int N2 = __shfl_sync(0xffffffffu, 2 * round16(cnt_h), 0);       // hi rows then lo rows
-            const int nacc = gq_nacc(N2);
-            const uint32_t idesc = idesc_f16_f32(GQ_M, N2);
-            const uint32_t lbo = (uint32_t)(N2 >> 3) * 128;
-            const uint64_t bstep = (uint64_t)((2 * lbo) >> 4);                    // one K=16 step along the B tile
             for (int kb = 0; kb < GQ_NKB; ++kb, ++it) {
                 const int st = it % GQ_NST;
                 const uint32_t b = psb & 1;
@@ -237,13 +248,14 @@ __global__ void __launch_bounds__(GQ_THREADS, 1) k_gate_up_q8(GemmParams p) {
                     !__all_sync(0xffffffffu, mbar_wait(&pempty[b], ((psb >> 1) & 1) ^ 1, p.err, DEV_ERR_TIMEOUT_EMPTY))) { ok = false; break; }
                 if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (it / GQ_NST) & 1, p.err, DEV_ERR_TIMEOUT_FULL))) { ok = false; break; }
                 tc_fence_after();
-                const uint64_t b0 = umma_desc(bring_s + st * GQ_B_HALF, lbo, 128);
                 const uint32_t a0 = tmem + gq_a_col(st);
                 const uint32_t d = tmem + GQ_P_COL + b * GQ_P_COLS;
-                #pragma unroll
-                for (int ks = 0; ks < GQ_KB / 16; ++ks) {       // K step ks -> accumulator ks % nacc of the P buffer
-                    const int j = ks & (nacc - 1);
-                    umma_f16_ta_warp(d + (uint32_t)(j * N2), a0 + ks * 8, b0 + (uint64_t)ks * bstep, idesc, (kb & 1) || ks >= nacc);
+                const uint32_t bst = bring_s + st * GQ_B_HALF;
+                switch (N2) {
+                    case 32: gq_issue_kblock<32>(d, a0, bst, kb); break;
+                    case 64: gq_issue_kblock<64>(d, a0, bst, kb); break;
+                    case 96: gq_issue_kblock<96>(d, a0, bst, kb); break;
+                    default: gq_issue_kblock<128>(d, a0, bst, kb); break;
                 }
                 umma_commit_warp(&empty[st]);
                 issued = 1;
