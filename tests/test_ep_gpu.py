@@ -76,6 +76,54 @@ def test_ep_emulated_ranks_one_gpu(native, oracle, n_ranks, T_loc, fixed_cap_max
         _check_rank(oracle, shards[rank], *inputs[rank], *out[rank], n_group=n_group)
 
 
+@pytest.mark.parametrize("n_ranks,T_loc", [(2, 256), (4, 96)])
+def test_ep_emulated_ranks_batch_regime(native, oracle, n_ranks, T_loc):
+    """BASELINE config 3's path on emulated ranks with the default thresholds: every shard receives a few hundred
+    rows, so its experts run the batch regime (the q8 gate/up on tcgen05, then the tcgen05 or mma.sync down) on
+    the compact row layout; routing bit-exact, h / moe within RTOL_L2 of the oracle with the reference's numerics
+    on sampled tokens of every rank."""
+    from loki_b200.moe import LayerWeights
+    from loki_b200.ep import EpMoeLayer, NativeEpOps
+    from ep_ref import ThreadComm
+    E = 256 // n_ranks
+    comms = ThreadComm.group(n_ranks)
+    shards = [LayerWeights("cuda", SEED, 0, n_experts=E, expert0=r * E) for r in range(n_ranks)]
+    ops = [NativeEpOps(0, n_ranks, T_loc) for _ in range(n_ranks)]
+    inputs = [_inputs(T_loc, r) for r in range(n_ranks)]
+    torch.cuda.synchronize()
+    out, errs = [None] * n_ranks, []
+
+    def run(rank):
+        try:
+            layer = EpMoeLayer(comms[rank], ops[rank], fixed_cap_max=8)
+            x, r = (torch.from_numpy(a).cuda() for a in inputs[rank])
+            out[rank] = layer.forward(shards[rank], x, r)
+        except Exception as e:                     # surfaced below
+            errs.append(e)
+            comms[rank].hub.barrier.abort()
+
+    th = [threading.Thread(target=run, args=(k,)) for k in range(n_ranks)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(timeout=600)
+    assert not errs, errs
+    torch.cuda.synchronize()
+    tok = [0, 1, 17, T_loc // 2, T_loc - 2, T_loc - 1]
+    for rank in range(n_ranks):
+        ops[rank].device_error()
+        x, r = inputs[rank]
+        h, moe, sel, w = out[rank]
+        sel, w = sel.cpu().numpy(), w.cpu().numpy()
+        _, osel, ow = oracle.router(x, shards[rank].router_w.float().cpu().numpy(), shards[rank].router_bias.cpu().numpy(),
+                                    oracle.route_cfg(8, 8, 1, 1, 1))
+        np.testing.assert_array_equal(sel, osel)
+        np.testing.assert_array_equal(w, ow)
+        ref = oracle_layer(oracle, SEED, 0, x, r, sel, w, tokens=tok)
+        e_moe, e_h = rel_l2(moe.cpu().numpy()[tok], ref["moe"]), rel_l2(h.cpu().numpy()[tok], ref["h"])
+        assert e_moe < RTOL_L2 and e_h < RTOL_L2, (rank, e_moe, e_h)
+
+
 def _nccl_worker(rank, port, T_loc, fixed_cap_max, comm_kind, out_dir):
     import torch.distributed as dist
     from loki_b200.moe import LayerWeights
