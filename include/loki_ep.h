@@ -13,7 +13,10 @@
  *   home:   lk_ep_combine -> h = resid + shared + sum of partials, moe = sum of partials
  *
  * A row is LK_EP_ROW_BYTES: a 64-byte header (int32 sel[8]: the expert id local to the receiving rank or
- * -1, float w[8]: routing weights) and the token's activations (fp32 [7168]).  Rows for rank d form block
+ * -1, float w[8]: routing weights), then the token's activations as their q8 per 32 -- int8 codes [7168] at
+ * LK_EP_ROW_Q_OFF and fp32 scales [224] at LK_EP_ROW_D_OFF, the same quantisation the expert kernels apply
+ * (d = amax/32-group / 127, round half even), so the experts compute exactly what they would from fp32 rows,
+ * in 8 128 bytes instead of 28 736.  Rows for rank d form block
  * d of the send buffer, tokens ascending; block d starts at row d*cap (fixed capacity, cap >= T: no count
  * exchange needed, CUDA-graph friendly) or, with cap == 0, right after block d-1 (compact; the caller
  * exchanges send_counts first to size the transfer).  Unused rows of a fixed-capacity block have all sel
@@ -28,7 +31,9 @@ extern "C" {
 #endif
 
 #define LK_EP_ROW_HDR_BYTES 64
-#define LK_EP_ROW_BYTES (64 + 7168 * 4)
+#define LK_EP_ROW_Q_OFF 64
+#define LK_EP_ROW_D_OFF (64 + 7168)
+#define LK_EP_ROW_BYTES (64 + 7168 + 7168 / 32 * 4)
 #define LK_EP_MAX_RANKS 8
 
 /* home side: sel/w [T][keep] (global expert ids, from lk_moe_route) and x [T][7168] -> send rows,

@@ -11,8 +11,8 @@
 namespace lk {
 
 constexpr int EP_PLAN_THREADS = 1024;
-constexpr int EP_ROW_FLOATS = LK_EP_ROW_BYTES / 4;
-static_assert(LK_EP_ROW_BYTES % 16 == 0, "rows must keep 16-byte alignment");
+static_assert(LK_EP_ROW_BYTES % 16 == 0 && LK_EP_ROW_Q_OFF % 16 == 0 && LK_EP_ROW_D_OFF % 16 == 0,
+              "rows and their parts must keep 16-byte alignment");
 
 struct EpRowHdr { int sel[8]; float w[8]; };
 static_assert(sizeof(EpRowHdr) == LK_EP_ROW_HDR_BYTES, "header size");
@@ -108,13 +108,29 @@ __global__ void __launch_bounds__(256) k_ep_copy(const int* __restrict__ sel, co
             else ((float*)h)[j] = mine ? w[t * keep + k] : 0.f;
         }
     }
-    const float4* src = (const float4*)(x + (size_t)t * HIDDEN);
-    for (int i = tid; i < HIDDEN / 4; i += 256) {
-        const float4 v = src[i];
+    // the q8 of x, computed once and written to every row of the token
+    __shared__ __align__(16) int8_t q[HIDDEN];
+    __shared__ float dq[HIDDEN / 32];
+    ep_row_q8(x + (size_t)t * HIDDEN, q, dq, tid);
+    __syncthreads();
+    for (int i = tid; i < (HIDDEN + HIDDEN / 8) / 16; i += 256) {     // codes then scales, 16 bytes at a time
+        const uint4 v = i < HIDDEN / 16 ? ((const uint4*)q)[i] : ((const uint4*)dq)[i - HIDDEN / 16];
         #pragma unroll
         for (int d = 0; d < LK_EP_MAX_RANKS; ++d)
-            if (rows[d] >= 0) ((float4*)(send + (size_t)rows[d] * LK_EP_ROW_BYTES + LK_EP_ROW_HDR_BYTES))[i] = v;
+            if (rows[d] >= 0) ((uint4*)(send + (size_t)rows[d] * LK_EP_ROW_BYTES + LK_EP_ROW_Q_OFF))[i] = v;
     }
+}
+
+// received rows -> fp32 activations [R][HIDDEN] (q * d; the expert kernels' q8 of these values gives back q)
+__global__ void k_ep_dequant(const uint8_t* __restrict__ recv, int R, float* __restrict__ x) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;   // over R x HIDDEN / 4
+    if (i >= (size_t)R * (HIDDEN / 4)) return;
+    const int r = (int)(i / (HIDDEN / 4)), c = (int)(i % (HIDDEN / 4));
+    const uint8_t* row = recv + (size_t)r * LK_EP_ROW_BYTES;
+    const uint32_t qw = ((const uint32_t*)(row + LK_EP_ROW_Q_OFF))[c];
+    const float d = ((const float*)(row + LK_EP_ROW_D_OFF))[(4 * c) / 32];
+    ((float4*)(x + (size_t)r * HIDDEN))[c] = make_float4((float)(int8_t)qw * d, (float)(int8_t)(qw >> 8) * d,
+                                                         (float)(int8_t)(qw >> 16) * d, (float)(int8_t)(qw >> 24) * d);
 }
 
 __global__ void k_ep_unpack(const uint8_t* __restrict__ recv, int R, int keep, int* sel, float* w) {
@@ -155,9 +171,11 @@ int ep_plan(const int* sel, int T, int keep, int n_ranks, int self_rank, int cap
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
-void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, cudaStream_t st) {
+void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, float* x, cudaStream_t st) {
     const int n = R * keep;
     k_ep_unpack<<<(n + 255) / 256, 256, 0, st>>>((const uint8_t*)recv, R, keep, sel, w);
+    const size_t nx = (size_t)R * (HIDDEN / 4);
+    if (x && R > 0) k_ep_dequant<<<(unsigned)((nx + 255) / 256), 256, 0, st>>>((const uint8_t*)recv, R, x);
 }
 
 }  // namespace lk

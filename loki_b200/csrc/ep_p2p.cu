@@ -62,9 +62,7 @@ __global__ void __launch_bounds__(P2P_THREADS) k_p2p_send(const int* __restrict_
             if (tid < 8) ((int*)row)[tid] = mine ? e - d * epr : -1;
             else ((float*)row)[tid] = mine ? w[t * keep + k] : 0.f;
         }
-        const float4* src = (const float4*)(x + (size_t)t * HIDDEN);
-        float4* dst = (float4*)(row + LK_EP_ROW_HDR_BYTES);
-        for (int i = tid; i < HIDDEN / 4; i += P2P_THREADS) dst[i] = src[i];
+        ep_row_q8(x + (size_t)t * HIDDEN, (int8_t*)(row + LK_EP_ROW_Q_OFF), (float*)(row + LK_EP_ROW_D_OFF), tid);
         ++r;
     }
     for (int rr = r; rr < cap; ++rr)

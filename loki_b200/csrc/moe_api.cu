@@ -45,6 +45,7 @@ struct LkMoeCtx {
     // defaults from a per-layer sweep (keep 8, uniform routing): single-token dp4a matvecs fastest up to ~32
     // tokens (T=32: 1.67 ms vs 2.03 mma, 2.23 tcgen05), mma.sync from 48 (T=64: 2.65 vs 3.24 / 2.96 ms,
     // T=128: 3.26 vs 3.56 tcgen05), tcgen05 from 192 (T=256: 3.84 vs 4.13 mma; T=512: 4.31 vs 6.26)
+    float* ep_x = nullptr;            // lk_ep_experts: the received rows' activations, dequantised (on first use)
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     char msg[256] = {0};
 };
@@ -169,7 +170,7 @@ void lk_moe_destroy(LkMoeCtx* c) {
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
                      c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->xq, c->xqn, c->xd,
                      c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt,
-                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->hb, c->shgu, c->shpair };
+                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->hb, c->ep_x, c->shgu, c->shpair };
     for (void* p : ptrs) if (p) cudaFree(p);
     if (c->blas) cublasDestroy((cublasHandle_t)c->blas);
     void* gp[] = { c->shw16, c->shx16, c->shh16, c->blas_ws };
@@ -435,9 +436,15 @@ int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int
     int rc = check_weights(c, W, false);
     if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
-    launch_ep_unpack(recv_rows, R, keep, c->sel, c->w, st);
-    const float* x = (const float*)((const uint8_t*)recv_rows + LK_EP_ROW_HDR_BYTES);
-    const int ld = LK_EP_ROW_BYTES / 4;
+    if (!c->ep_x) {                   // the rows' fp32 activations: allocated on first use, outside a capture
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+            return set_err(c, LK_ERR_ARG, "the first lk_ep_experts call on a context must run outside a stream capture");
+        LK_CU(dalloc(&c->ep_x, (size_t)c->cfg.max_tokens * HIDDEN));
+    }
+    launch_ep_unpack(recv_rows, R, keep, c->sel, c->w, c->ep_x, st);
+    const float* x = c->ep_x;
+    const int ld = HIDDEN;
     // out = the routed partial sums; the shared expert runs in the same launches on the rows
     // [shared_row0, +shared_rows), and its outputs (entry rows R*keep + j) are copied to shared_out
     c->sh_t0 = shared_row0; c->sh_n = shared_rows > 0 ? shared_rows : -1;

@@ -238,6 +238,22 @@ __device__ __forceinline__ int iq2_dot_xs(uint32_t aux0, uint32_t aux1, const ui
     return acc;
 }
 
+// an expert-parallel row's activations (include/loki_ep.h): the q8 per 32 of the fp32 row x (quant_q8_group,
+// bit for bit) as int8 codes at q and fp32 scales at d; threads tid < 224 of the block each take one group
+__device__ __forceinline__ void ep_row_q8(const float* __restrict__ x, int8_t* q, float* d, int tid) {
+    if (tid >= HIDDEN / 32) return;
+    float v[32];
+    const float4* src = (const float4*)(x + tid * 32);
+    #pragma unroll
+    for (int j = 0; j < 8; ++j) { const float4 a = src[j]; v[4*j] = a.x; v[4*j+1] = a.y; v[4*j+2] = a.z; v[4*j+3] = a.w; }
+    int8_t qv[32];
+    d[tid] = quant_q8_group(v, qv);
+    uint4 w[2];
+    memcpy(w, qv, 32);
+    ((uint4*)(q + tid * 32))[0] = w[0];
+    ((uint4*)(q + tid * 32))[1] = w[1];
+}
+
 // the 8 bytes of IQ2 group `g` of a row staged in shared memory (row start 4-byte aligned): the group
 // starts at 2 + 66*(g/8) + 8*(g%8), i.e. 2-byte aligned; read 3 aligned words and funnel-shift
 __device__ __forceinline__ void load_group_smem(const uint8_t* row, int goff, uint32_t& aux0, uint32_t& aux1) {

@@ -169,8 +169,8 @@ void launch_gen_iq2(uint8_t* dst, uint64_t seed, int layer, int matrix, int expe
 void launch_gen_weights(int fmt, uint8_t* dst, uint64_t seed, int layer, int matrix, int expert0, int n_exp, int rows, int K,
                         int64_t stride, cudaStream_t st);
 
-// ---- expert-parallel row headers -> sel/w [R][keep]
-void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, cudaStream_t st);
+// ---- expert-parallel row headers -> sel/w [R][keep], and (x non-null) the rows' q8 activations -> fp32
+void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, float* x, cudaStream_t st);   // x: [R][HIDDEN]
 // ---- expert-parallel row plan only: counts [n_ranks], row_map [T][n_ranks] (and, with `send`, the
 //      headers of unused fixed-capacity rows)
 int ep_plan(const int* sel, int T, int keep, int n_ranks, int self_rank, int cap, int* counts, int* row_map, uint8_t* send,

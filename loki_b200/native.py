@@ -25,7 +25,7 @@ DOWN_MATRIX_BYTES = {f: HIDDEN * (MOE_INTER // QK) * b for f, b in BLOCK_BYTES.i
 # bytes of one gate (or up) matrix [MOE_INTER][HIDDEN] per format
 GU_MATRIX_BYTES = {f: MOE_INTER * (HIDDEN // QK) * b for f, b in BLOCK_BYTES.items()}
 EP_ROW_HDR_BYTES = 64
-EP_ROW_BYTES = EP_ROW_HDR_BYTES + HIDDEN * 4      # 28 736
+EP_ROW_BYTES = EP_ROW_HDR_BYTES + HIDDEN + HIDDEN // 32 * 4   # 8 128: header, q8 codes, fp32 scales
 EP_MAX_RANKS = 8
 EP_COMM_ID_BYTES = 128
 EP_IPC_HANDLE_BYTES = 64

@@ -51,25 +51,26 @@ extern "C" {
 
 // ------------------------------------------------------------------ formats
 // out[rows*K] = dequantised IQ2_XXS weights (gguf-py dequantize_blocks semantics)
-void orc_iq2_dequant(const uint8_t* blocks, int64_t nblk, float* out) {
-    #pragma omp parallel for schedule(static)
-    for (int64_t b = 0; b < nblk; ++b) {
-        const uint8_t* blk = blocks + b * BLK_IQ2;
-        uint16_t dh; memcpy(&dh, blk, 2);
-        const float d = half_to_float(dh);
-        for (int g = 0; g < 8; ++g) {
-            uint32_t aux0, aux1; memcpy(&aux0, blk + 2 + 8 * g, 4); memcpy(&aux1, blk + 6 + 8 * g, 4);
-            const float db = d * (0.5f + (float)(aux1 >> 28)) * 0.25f;
-            for (int l = 0; l < 4; ++l) {
-                const uint64_t gv = IQ2_GRID[(aux0 >> (8 * l)) & 0xFF];
-                const uint32_t s = iq2_ksigns((aux1 >> (7 * l)) & 127u);
-                for (int j = 0; j < 8; ++j) {
-                    const float m = (float)((gv >> (8 * j)) & 0xFF);
-                    out[b * 256 + g * 32 + l * 8 + j] = db * m * ((s >> j) & 1 ? -1.0f : 1.0f);
-                }
+static void iq2_deq_block(const uint8_t* blk, float* out) {
+    uint16_t dh; memcpy(&dh, blk, 2);
+    const float d = half_to_float(dh);
+    for (int g = 0; g < 8; ++g) {
+        uint32_t aux0, aux1; memcpy(&aux0, blk + 2 + 8 * g, 4); memcpy(&aux1, blk + 6 + 8 * g, 4);
+        const float db = d * (0.5f + (float)(aux1 >> 28)) * 0.25f;
+        for (int l = 0; l < 4; ++l) {
+            const uint64_t gv = IQ2_GRID[(aux0 >> (8 * l)) & 0xFF];
+            const uint32_t s = iq2_ksigns((aux1 >> (7 * l)) & 127u);
+            for (int j = 0; j < 8; ++j) {
+                const float m = (float)((gv >> (8 * j)) & 0xFF);
+                out[g * 32 + l * 8 + j] = db * m * ((s >> j) & 1 ? -1.0f : 1.0f);
             }
         }
     }
+}
+
+void orc_iq2_dequant(const uint8_t* blocks, int64_t nblk, float* out) {
+    #pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nblk; ++b) iq2_deq_block(blocks + b * BLK_IQ2, out + b * 256);
 }
 
 // seeded generator (moe_format.h): rows x K matrix of (layer, matrix, expert)
@@ -88,51 +89,52 @@ void orc_gen_d_only(uint64_t seed, int layer, int matrix, int expert, int64_t nb
 // out[nblk*256] = dequantised Q2_K (fmt 5), Q3_K (6), Q5_K (3) or Q6_K (1) blocks (gguf-py
 // dequantize_blocks semantics: Q2_K d*(sc&15)*q - dmin*(sc>>4); Q3_K d*(scale-32)*q3; Q5_K
 // (d*scale)*q - dmin*min; Q6_K (d*scale)*(q-32); each product in fp32 as written)
+static void kq_deq_block(int fmt, const uint8_t* blk, float* out) {
+    if (fmt == FMT_Q5K) {
+        uint16_t dh, mh; memcpy(&dh, blk, 2); memcpy(&mh, blk + 2, 2);
+        const float d = half_to_float(dh), dmin = half_to_float(mh);
+        for (int i = 0; i < QK; ++i) {
+            const int j = i >> 6, u = (i >> 5) & 1, l = i & 31;
+            const int q = ((blk[Q5K_QS + 32 * j + l] >> (4 * u)) & 15) | (((blk[Q5K_QH + l] >> (2 * j + u)) & 1) << 4);
+            int sc, mn; q5k_scale_min(blk + Q5K_SC, 2 * j + u, sc, mn);
+            out[i] = (d * (float)sc) * (float)q - dmin * (float)mn;
+        }
+        return;
+    }
+    if (fmt == FMT_Q6K) {
+        uint16_t dh; memcpy(&dh, blk + Q6K_D, 2);
+        const float d = half_to_float(dh);
+        for (int i = 0; i < QK; ++i) {
+            const int n = i >> 7, c = (i >> 5) & 3, l = i & 31;
+            const int q = ((blk[64 * n + 32 * (c & 1) + l] >> (4 * (c >> 1))) & 15) | (((blk[Q6K_QH + 32 * n + l] >> (2 * c)) & 3) << 4);
+            out[i] = (d * (float)(int8_t)blk[Q6K_SC + i / 16]) * (float)(q - 32);
+        }
+        return;
+    }
+    for (int i = 0; i < QK; ++i) {
+        const int n = i >> 7, j = (i >> 5) & 3, s = (i >> 4) & 1, l = i & 15;
+        const int is = 8 * n + 2 * j + s;
+        float v;
+        if (fmt == FMT_Q2K) {
+            uint16_t dh, mh; memcpy(&dh, blk + Q2K_D, 2); memcpy(&mh, blk + Q2K_DMIN, 2);
+            const int q = (blk[Q2K_QS + 32 * n + 16 * s + l] >> (2 * j)) & 3;
+            const float dl = half_to_float(dh) * (float)(blk[is] & 15), ml = half_to_float(mh) * (float)(blk[is] >> 4);
+            v = dl * (float)q - ml;
+        } else {
+            uint16_t dh; memcpy(&dh, blk + Q3K_D, 2);
+            const int lo = (blk[Q3K_QS + 32 * n + 16 * s + l] >> (2 * j)) & 3;
+            const int hb = (blk[16 * s + l] >> (4 * n + j)) & 1;
+            const float dl = half_to_float(dh) * (float)q3k_scale(blk + Q3K_SC, is);
+            v = dl * (float)(lo - (hb ? 0 : 4));
+        }
+        out[i] = v;
+    }
+}
+
 void orc_kq_dequant(int fmt, const uint8_t* blocks, int64_t nblk, float* out) {
     const int nb = fmt_block_bytes(fmt);
     #pragma omp parallel for schedule(static)
-    for (int64_t b = 0; b < nblk; ++b) {
-        const uint8_t* blk = blocks + b * nb;
-        if (fmt == FMT_Q5K) {
-            uint16_t dh, mh; memcpy(&dh, blk, 2); memcpy(&mh, blk + 2, 2);
-            const float d = half_to_float(dh), dmin = half_to_float(mh);
-            for (int i = 0; i < QK; ++i) {
-                const int j = i >> 6, u = (i >> 5) & 1, l = i & 31;
-                const int q = ((blk[Q5K_QS + 32 * j + l] >> (4 * u)) & 15) | (((blk[Q5K_QH + l] >> (2 * j + u)) & 1) << 4);
-                int sc, mn; q5k_scale_min(blk + Q5K_SC, 2 * j + u, sc, mn);
-                out[b * QK + i] = (d * (float)sc) * (float)q - dmin * (float)mn;
-            }
-            continue;
-        }
-        if (fmt == FMT_Q6K) {
-            uint16_t dh; memcpy(&dh, blk + Q6K_D, 2);
-            const float d = half_to_float(dh);
-            for (int i = 0; i < QK; ++i) {
-                const int n = i >> 7, c = (i >> 5) & 3, l = i & 31;
-                const int q = ((blk[64 * n + 32 * (c & 1) + l] >> (4 * (c >> 1))) & 15) | (((blk[Q6K_QH + 32 * n + l] >> (2 * c)) & 3) << 4);
-                out[b * QK + i] = (d * (float)(int8_t)blk[Q6K_SC + i / 16]) * (float)(q - 32);
-            }
-            continue;
-        }
-        for (int i = 0; i < QK; ++i) {
-            const int n = i >> 7, j = (i >> 5) & 3, s = (i >> 4) & 1, l = i & 15;
-            const int is = 8 * n + 2 * j + s;
-            float v;
-            if (fmt == FMT_Q2K) {
-                uint16_t dh, mh; memcpy(&dh, blk + Q2K_D, 2); memcpy(&mh, blk + Q2K_DMIN, 2);
-                const int q = (blk[Q2K_QS + 32 * n + 16 * s + l] >> (2 * j)) & 3;
-                const float dl = half_to_float(dh) * (float)(blk[is] & 15), ml = half_to_float(mh) * (float)(blk[is] >> 4);
-                v = dl * (float)q - ml;
-            } else {
-                uint16_t dh; memcpy(&dh, blk + Q3K_D, 2);
-                const int lo = (blk[Q3K_QS + 32 * n + 16 * s + l] >> (2 * j)) & 3;
-                const int hb = (blk[16 * s + l] >> (4 * n + j)) & 1;
-                const float dl = half_to_float(dh) * (float)q3k_scale(blk + Q3K_SC, is);
-                v = dl * (float)(lo - (hb ? 0 : 4));
-            }
-            out[b * QK + i] = v;
-        }
-    }
+    for (int64_t b = 0; b < nblk; ++b) kq_deq_block(fmt, blocks + b * nb, out + b * QK);
 }
 
 // seeded K-quant matrix (moe_format.h kq_gen_block): rows x K in format fmt of (layer, matrix, expert)
@@ -579,4 +581,124 @@ int orc_moe_layer(const float* x, const float* resid, int T, const OrcLayerW* Wl
     return orc_moe_layer_ex(x, resid, T, Wl, ids, w, KE, h, moe, y_slot, shared_out, 1);
 }
 
+// ------------------------------------------------------------------ ggml CPU numerics (an oracle mode)
+// The reference's non-fused MoE path (src/server_core_fused.cpp:956-980) is a ggml graph: ggml_mul_mat_id for
+// up, gate and down, ggml_swiglu_split, ggml_mul by the routing weights, the k slots added in order (:973),
+// the shared expert by ggml_mul_mat (:974-975), then (moe + shared) + ffn_inp (:976).  On ggml's CPU backend
+// the activations of IQ2_XXS and K-quant matrices are quantised to q8_K: one fp32 scale per 256 values.
+// ggml is not vendored in the reference, so this mode restates ggml's published algorithm and is unpinned:
+//   quantize_row_q8_K: per 256-block, max = the value of largest magnitude (the first on ties),
+//     iscale = -127/max, q = min(127, round-half-even(iscale * x)), d = 1/iscale; an all-zero block gives
+//     d = 0 and q = 0 (d is negative when max is positive: q * d still reconstructs x);
+//   vec_dot_<fmt>_q8_K: exact integer sums of weight codes times q per sub-block, scaled in fp32 by the
+//     block scales and d.  Here the same dot is evaluated in double from the dequantised weights (gguf-py
+//     semantics, as above) and q * d: the ideal value of the q8_K scheme, which ggml's fp32 block
+//     accumulation differs from by reassociation only;
+//   silu(g) * u with g / (1 + exp(-g)) as lk_swiglu (ggml's expf and this file's lk_expf differ by an ulp
+//     or so, far below the q8_K noise).
+void orc_quant_q8_K(const float* x, int64_t n, int8_t* q, float* d) {
+    for (int64_t b = 0; b < n / QK; ++b) {
+        const float* xb = x + b * QK;
+        int8_t* qb = q + b * QK;
+        float amax = 0.0f, mx = 0.0f;
+        for (int j = 0; j < QK; ++j) { const float a = fabsf(xb[j]); if (a > amax) { amax = a; mx = xb[j]; } }
+        if (amax == 0.0f) { d[b] = 0.0f; memset(qb, 0, QK); continue; }
+        const float iscale = -127.0f / mx;
+        for (int j = 0; j < QK; ++j) qb[j] = (int8_t)std::min(127, (int)rintf(iscale * xb[j]));
+        d[b] = 1.0f / iscale;
+    }
+}
+
+// y[t][r] = W[r] . (q8_K of x[t]) for `ntok` rows given as codes xq[t][K] and scales xd[t][K/256]; W = rows x K
+// in fmt (FMT_IQ2 or a K-quant), dequantised a row at a time
+static void q8K_matvec_multi(int fmt, const uint8_t* W, int rows, int K, const int8_t* const* xq, const float* const* xd,
+                             int ntok, float* const* y) {
+    const int NB = K / QK, nb = fmt_block_bytes(fmt);
+    #pragma omp parallel
+    {
+        std::vector<float> wr(K);
+        std::vector<double> acc(ntok);
+        #pragma omp for schedule(static)
+        for (int r = 0; r < rows; ++r) {
+            const uint8_t* row = W + (size_t)r * NB * nb;
+            for (int b = 0; b < NB; ++b) {
+                if (fmt == FMT_IQ2) iq2_deq_block(row + (size_t)b * nb, wr.data() + (size_t)b * QK);
+                else kq_deq_block(fmt, row + (size_t)b * nb, wr.data() + (size_t)b * QK);
+            }
+            for (int t = 0; t < ntok; ++t) {
+                double a = 0.0;
+                for (int b = 0; b < NB; ++b) {
+                    double s = 0.0;
+                    for (int j = 0; j < QK; ++j) s += (double)wr[(size_t)b * QK + j] * (double)xq[t][(size_t)b * QK + j];
+                    a += s * (double)xd[t][b];
+                }
+                acc[t] = a;
+            }
+            for (int t = 0; t < ntok; ++t) y[t][r] = (float)acc[t];
+        }
+    }
+}
+
+// one expert (gate/up in gu_fmt, down in dn_fmt) on n tokens: xq/xd are the tokens' q8_K codes and scales,
+// y[i][HIDDEN] its outputs
+static void q8K_expert(const uint8_t* gate, const uint8_t* up, const uint8_t* down, int gu_fmt, int dn_fmt,
+                       const int8_t* const* xq, const float* const* xd, int n, float* const* y) {
+    const int E = HIDDEN, H = MOE_INTER;
+    std::vector<float> g((size_t)n * H), u((size_t)n * H), hf(H);
+    std::vector<int8_t> hq((size_t)n * H); std::vector<float> hd((size_t)n * H / QK);
+    std::vector<float*> gp(n), upp(n); std::vector<const int8_t*> hqp(n); std::vector<const float*> hdp(n);
+    for (int i = 0; i < n; ++i) { gp[i] = g.data() + (size_t)i * H; upp[i] = u.data() + (size_t)i * H; }
+    q8K_matvec_multi(gu_fmt, gate, H, E, xq, xd, n, gp.data());
+    q8K_matvec_multi(gu_fmt, up, H, E, xq, xd, n, upp.data());
+    for (int i = 0; i < n; ++i) {
+        for (int j = 0; j < H; ++j) hf[j] = lk_swiglu(gp[i][j], upp[i][j]);
+        orc_quant_q8_K(hf.data(), H, hq.data() + (size_t)i * H, hd.data() + (size_t)i * H / QK);
+        hqp[i] = hq.data() + (size_t)i * H; hdp[i] = hd.data() + (size_t)i * H / QK;
+    }
+    q8K_matvec_multi(dn_fmt, down, E, H, hqp.data(), hdp.data(), n, y);
+}
+
+// The layer in ggml's CPU numerics: the arguments of orc_moe_layer_fmt2 (no slot outputs; hq8 does not apply:
+// ggml always quantises h to q8_K).  moe = sum over k in order of fp32 w_k * y_k; h = (moe + shared) + resid.
+int orc_moe_layer_ggml(const float* x, const float* resid, int T, const OrcLayerW* Wl, const int* ids, const float* w,
+                       int KE, float* h, float* moe, float* shared_out, int down_fmt, int sh_gu_fmt, int sh_down_fmt) {
+    if (down_fmt != FMT_IQ2 && down_fmt != FMT_Q2K && down_fmt != FMT_Q3K) return 1;
+    if ((sh_gu_fmt != FMT_IQ2 && sh_gu_fmt != FMT_Q5K) || (sh_down_fmt != down_fmt && sh_down_fmt != FMT_Q6K)) return 1;
+    const int E = HIDDEN;
+    std::vector<int8_t> xq((size_t)T * E); std::vector<float> xd((size_t)T * E / QK);
+    orc_quant_q8_K(x, (int64_t)T * E, xq.data(), xd.data());
+    int maxid = 0; for (int i = 0; i < T * KE; ++i) maxid = std::max(maxid, ids[i]);
+    const int NE = maxid + 1;
+    std::vector<int> cnt(NE), off(NE + 1), perm((size_t)T * KE);
+    orc_permute(ids, T, KE, NE, cnt.data(), off.data(), perm.data());
+    std::vector<float> ys((size_t)T * KE * E);
+    for (int m = 0; m < NE; ++m) {
+        const int n = cnt[m];
+        if (n == 0) continue;
+        std::vector<const int8_t*> xqp(n); std::vector<const float*> xdp(n); std::vector<float*> yp(n);
+        for (int i = 0; i < n; ++i) {
+            const int s = perm[off[m] + i], t = s / KE;
+            xqp[i] = xq.data() + (size_t)t * E; xdp[i] = xd.data() + (size_t)t * E / QK; yp[i] = ys.data() + (size_t)s * E;
+        }
+        q8K_expert(Wl->gate + m * Wl->gate_stride, Wl->up + m * Wl->up_stride, Wl->down + m * Wl->down_stride, FMT_IQ2,
+                   down_fmt, xqp.data(), xdp.data(), n, yp.data());
+    }
+    std::vector<float> sh((size_t)T * E, 0.0f);
+    if (Wl->sh_gate) {
+        std::vector<const int8_t*> xqp(T); std::vector<const float*> xdp(T); std::vector<float*> yp(T);
+        for (int t = 0; t < T; ++t) { xqp[t] = xq.data() + (size_t)t * E; xdp[t] = xd.data() + (size_t)t * E / QK; yp[t] = sh.data() + (size_t)t * E; }
+        q8K_expert(Wl->sh_gate, Wl->sh_up, Wl->sh_down, sh_gu_fmt, sh_down_fmt, xqp.data(), xdp.data(), T, yp.data());
+    }
+    for (int t = 0; t < T; ++t)
+        for (int j = 0; j < E; ++j) {
+            float r = w[(size_t)t * KE] * ys[(size_t)t * KE * E + j];
+            for (int k = 1; k < KE; ++k) r += w[(size_t)t * KE + k] * ys[((size_t)t * KE + k) * E + j];
+            if (moe) moe[(size_t)t * E + j] = r;
+            if (h) h[(size_t)t * E + j] = (r + sh[(size_t)t * E + j]) + resid[(size_t)t * E + j];
+        }
+    if (shared_out) memcpy(shared_out, sh.data(), sh.size() * 4);
+    return 0;
+}
+
 }  // extern "C"
+

@@ -73,6 +73,10 @@ def lib():
         L.orc_gen_kq.argtypes = [ctypes.c_int, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                  ctypes.c_int, P]
         L.orc_kq_matvec.argtypes = [ctypes.c_int, P, ctypes.c_int, ctypes.c_int, P, P, P]
+        L.orc_quant_q8_K.argtypes = [P, ctypes.c_int64, P, P]
+        L.orc_moe_layer_ggml.argtypes = [P, P, ctypes.c_int, ctypes.POINTER(LayerW), P, P, ctypes.c_int, P, P, P,
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_int]
+        L.orc_moe_layer_ggml.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -210,3 +214,34 @@ def moe_layer(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None
         out["y_slot"] = ys
         out["shared"] = sh
     return out
+
+
+def quant_q8_K(x):
+    """ggml's q8_K of x (len % 256 == 0): codes int8 [n], scales float32 [n/256] (orc_quant_q8_K)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    q = np.empty(x.size, np.int8)
+    d = np.empty(x.size // 256, np.float32)
+    lib().orc_quant_q8_K(_p(x), x.size, _p(q), _p(d))
+    return q, d
+
+
+def moe_layer_ggml(x, resid, gate, up, down, stride, ids, w, sh_gate=None, sh_up=None, sh_down=None, down_fmt=FMT_IQ2,
+                   down_stride=None, sh_gu_fmt=FMT_IQ2, sh_down_fmt=None):
+    """moe_layer's arguments in ggml's CPU numerics (q8_K activations and h, fp32 combine in k order;
+    orc_moe_layer_ggml).  Returns dict(h, moe, shared)."""
+    x = np.ascontiguousarray(x, np.float32)
+    resid = np.ascontiguousarray(resid, np.float32)
+    ids = np.ascontiguousarray(ids, np.int32)
+    w = np.ascontiguousarray(w, np.float32)
+    T, KE = ids.shape
+    lw = LayerW(_p(gate).value, _p(up).value, _p(down).value, stride, stride, stride if down_stride is None else down_stride,
+                None if sh_gate is None else _p(sh_gate).value,
+                None if sh_up is None else _p(sh_up).value,
+                None if sh_down is None else _p(sh_down).value)
+    h = np.empty((T, HIDDEN), np.float32)
+    moe = np.empty((T, HIDDEN), np.float32)
+    sh = np.empty((T, HIDDEN), np.float32)
+    rc = lib().orc_moe_layer_ggml(_p(x), _p(resid), T, ctypes.byref(lw), _p(ids), _p(w), KE, _p(h), _p(moe), _p(sh),
+                                  down_fmt, sh_gu_fmt, down_fmt if sh_down_fmt is None else sh_down_fmt)
+    assert rc == 0
+    return {"h": h, "moe": moe, "shared": sh}

@@ -14,8 +14,17 @@ import torch
 from moe_helpers import HIDDEN, INTER, MAT
 
 ROW_HDR = 64
-ROW_BYTES = ROW_HDR + HIDDEN * 4
+ROW_Q = ROW_HDR                       # int8 q8 codes [HIDDEN]
+ROW_D = ROW_HDR + HIDDEN              # fp32 scales [HIDDEN / 32]
+ROW_BYTES = ROW_D + HIDDEN // 32 * 4
 N_EXPERTS = 256
+
+
+def _row_x(rows):
+    """fp32 activations of rows: q * d per 32 (what the CUDA path's experts read back)."""
+    q = rows[:, ROW_Q:ROW_D].copy().view(np.int8).astype(np.float32)
+    d = rows[:, ROW_D:].copy().view(np.float32)
+    return (q.reshape(len(rows), HIDDEN // 32, 32) * d[:, :, None]).reshape(len(rows), HIDDEN)
 
 
 class RefShard:
@@ -50,6 +59,8 @@ class RefEpOps:
         sel, w, x = sel.numpy(), w.numpy(), x.numpy()
         T, keep = sel.shape
         NR, epr = self.n_ranks, N_EXPERTS // self.n_ranks
+        q, dq = self.oracle.quant_q8(x) if T else (np.zeros(0, np.int8), np.zeros(0, np.float32))
+        q, dq = q.reshape(T, HIDDEN), dq.reshape(T, HIDDEN // 32)
         owner = sel // epr
         lists = [[t for t in range(T) if d == self_rank or (owner[t] == d).any()] for d in range(NR)]
         counts = np.array([len(l) for l in lists], np.int32)
@@ -71,7 +82,8 @@ class RefEpOps:
                 hw[:keep] = np.where(mine, w[t], 0)
                 send[row, :32] = hs.view(np.uint8)
                 send[row, 32:64] = hw.view(np.uint8)
-                send[row, 64:] = x[t].view(np.uint8)
+                send[row, ROW_Q:ROW_D] = q[t].view(np.uint8)
+                send[row, ROW_D:] = dq[t].view(np.uint8)
         return torch.from_numpy(send), torch.from_numpy(counts), torch.from_numpy(row_map)
 
     def _shared(self, W, x):
@@ -87,8 +99,7 @@ class RefEpOps:
         ret = np.zeros((R, HIDDEN), np.float32)
         shared = np.zeros((shared_rows, HIDDEN), np.float32)
         if shared_rows:
-            xs = recv[shared_row0:shared_row0 + shared_rows, 64:].copy().view(np.float32)
-            shared = self._shared(W, xs)
+            shared = self._shared(W, _row_x(recv[shared_row0:shared_row0 + shared_rows]))
         ret, shared = self._routed(W, recv, R, keep, ret), torch.from_numpy(shared)
         return ret, shared
 
@@ -97,7 +108,7 @@ class RefEpOps:
             return torch.from_numpy(ret)
         sel = recv[:, :32].copy().view(np.int32)[:, :keep]
         w = recv[:, 32:64].copy().view(np.float32)[:, :keep]
-        x = recv[:, 64:].copy().view(np.float32)
+        x = _row_x(recv)
         live = [r for r in range(R) if (sel[r] >= 0).any()]
         if not live:
             return torch.from_numpy(ret)

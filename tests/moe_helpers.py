@@ -52,3 +52,16 @@ def oracle_layer(oracle, seed, layer, x, resid, sel, w, with_shared=True, tokens
     gf, df = shared_fmts(down_fmt, sh_fmt)
     return oracle.moe_layer(x[tokens], resid[tokens], gate, up, down, MAT, ids, np.asarray(w)[tokens], shg, shu, shd, hq8=hq8,
                             down_fmt=down_fmt, down_stride=down_bytes(down_fmt), sh_gu_fmt=gf, sh_down_fmt=df)
+
+
+def oracle_layer_ggml(oracle, seed, layer, x, resid, sel, w, tokens=None, down_fmt=4, sh_fmt=4):
+    """The oracle's ggml CPU mode (q8_K activations and h) for routing (sel, w) on the given tokens."""
+    tokens = list(range(x.shape[0])) if tokens is None else list(tokens)
+    sel = np.asarray(sel)[tokens]
+    used = sorted(set(int(e) for e in sel.reshape(-1)))
+    remap = {e: i for i, e in enumerate(used)}
+    ids = np.vectorize(lambda e: remap[int(e)])(sel).astype(np.int32)
+    gate, up, down, sh = host_arena(oracle, seed, layer, used, down_fmt, sh_fmt)
+    gf, df = shared_fmts(down_fmt, sh_fmt)
+    return oracle.moe_layer_ggml(x[tokens], resid[tokens], gate, up, down, MAT, ids, np.asarray(w)[tokens], *sh,
+                                 down_fmt=down_fmt, down_stride=down_bytes(down_fmt), sh_gu_fmt=gf, sh_down_fmt=df)

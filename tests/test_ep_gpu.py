@@ -188,3 +188,31 @@ def test_ep_nccl_two_gpus(native, oracle, tmp_path, T_loc, fixed_cap_max, comm_k
         ref = oracle_layer(oracle, SEED, 0, x, r, osel, ow)
         assert rel_l2(got["moe"], ref["moe"]) < RTOL_L2
         assert rel_l2(got["h"], ref["h"]) < RTOL_L2
+
+
+def test_p2p_wait_runs_out_with_error_status(native):
+    """A rank that never sends: rank 0 of a 2-rank mailbox, nothing ever publishes its flags.  The rows wait
+    and the returns wait each give up after their bounded spin (2 s of globaltimer) and leave their error word
+    (1: rows never arrived, 2: returns never arrived); the context stays usable for the next launches."""
+    import ctypes
+    from loki_b200.native import lib, check, EP_IPC_HANDLE_BYTES
+    L = lib()
+    mb, h = ctypes.c_void_p(), ctypes.create_string_buffer(EP_IPC_HANDLE_BYTES)
+    check(L.lk_ep_mailbox_create(2, 0, 4, torch.cuda.current_device(), ctypes.byref(mb), h))
+    try:
+        st = torch.cuda.current_stream()
+        err = torch.zeros(2, dtype=torch.int32, device="cuda")
+        rows = ctypes.c_void_p()
+        check(L.lk_ep_p2p_rows(mb, ctypes.byref(rows), ctypes.c_void_p(err.data_ptr()), ctypes.c_void_p(st.cuda_stream)))
+        row_map = torch.full((1, 2), -1, dtype=torch.int32, device="cuda")
+        resid = torch.ones(1, HIDDEN, device="cuda")
+        hh, moe = torch.empty_like(resid), torch.empty_like(resid)
+        check(L.lk_ep_p2p_combine(mb, ctypes.c_void_p(row_map.data_ptr()), 1, ctypes.c_void_p(resid.data_ptr()), None,
+                                  ctypes.c_void_p(hh.data_ptr()), ctypes.c_void_p(moe.data_ptr()),
+                                  ctypes.c_void_p(err.data_ptr() + 4), ctypes.c_void_p(st.cuda_stream)))
+        torch.cuda.synchronize()
+        assert err.tolist() == [1, 2]
+        assert torch.equal(hh, resid) and not moe.any()       # nothing returned: h = resid, moe = 0
+        assert float(torch.ones(1 << 20, device="cuda").sum()) == float(1 << 20)
+    finally:
+        L.lk_ep_mailbox_destroy(mb)
