@@ -1,6 +1,6 @@
 // ep_p2p.cu -- the expert-parallel decode exchange over NVLink peer memory (include/loki_ep.h).
 //
-// For small per-layer messages (decode: a few 28 KB rows per rank pair) a collective library's launch and
+// For small per-layer messages (decode: a few 8 KB rows per rank pair) a collective library's launch and
 // protocol latency dominates.  Here every rank owns a mailbox in its HBM -- rows received from each
 // source rank, partial sums returned by each owner rank, and two flag arrays -- exported with CUDA IPC and
 // mapped by every peer.  Senders store straight into the destination's mailbox over NVLink, then publish
