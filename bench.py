@@ -582,7 +582,7 @@ def run_ep_prefill(args, ws, rank, local, dist):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)" if not model_fmt else
                  "the real model's formats (%s down, %s shared): IQ2_XXS gate/up tcgen05 fp16 x fp16, K-quant down mma.sync "
-                 "fp16 x fp16(h), Q5_K/Q6_K shared dequantised to fp16 + cuBLAS; fp32 accumulate" % (args.down_fmt, args.shared_fmt),
+                 "fp16 x fp16(h), Q5_K/Q6_K shared on tcgen05 (fp16 hi/lo gate/up operands, q8 h); fp32 accumulate" % (args.down_fmt, args.shared_fmt),
         "data": "synthetic: seeded IQ2_XXS experts, router W N(0,0.02), bias N(0,0.01), bf16 N(0,1) hidden states",
         "config": {"workload": "config3_ep_batch_T%d" % T, "global_batch": T, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,
                    "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": NE // ws, "rows_sent": sent,
@@ -797,7 +797,7 @@ def run_prefill(args, ws, rank, local, dist, W=None, T=None, steps=None, warmup=
         "dtype": "iq2_xxs x q8 activations: gate/up tcgen05 kind::f16 with exact integer weights and hi/lo fp16 activations "
                  "(the reference's group sums), h re-quantised to q8; down tcgen05 fp16; fp32 accumulate" if not model_fmt else
                  "the real model's formats (%s down, %s shared): IQ2_XXS q8 gate/up on tcgen05 (h re-quantised to q8), K-quant "
-                 "down mma.sync fp16; Q5_K/Q6_K shared dequantised to fp16 + cuBLAS; fp32 accumulate" % (args.down_fmt, args.shared_fmt),
+                 "down mma.sync fp16; Q5_K/Q6_K shared on tcgen05 (fp16 hi/lo gate/up operands, q8 h); fp32 accumulate" % (args.down_fmt, args.shared_fmt),
         "data": "synthetic: seeded IQ2_XXS experts, uniform-random router logits U(-1,1), bf16 N(0,1) hidden states",
         "config": {"workload": ("config2_prefill_T%d" % T if T == 512 else "config3_batch_T%d_1gpu" % T if T == 4096 else wl) +
                                ("" if not model_fmt else "_%s_down_%s_shared" % (args.down_fmt, args.shared_fmt)),
@@ -826,8 +826,8 @@ def run_prefill(args, ws, rank, local, dist, W=None, T=None, steps=None, warmup=
                               "traffic": ncu_traffic("k_prefill_down" if fmt == 4 else "k_kq_mma_down", wl)}},
         # this library's kernels per step: router, slot build, gate/up activation tiles, gate/up GEMM, down GEMM,
         # combine; K-quant downs add a second slot build and take k_kq_mma_down for the down; a Q5_K/Q6_K shared
-        # expert adds its 5 dense-path kernels (3 dequantisations, x to fp16, SwiGLU; its two GEMMs are cuBLAS's)
-        "gpu_launches": steps * ((6 if fmt == 4 else 7) + (5 if args.shared_fmt == "q5k" else 0)),
+        # expert adds its 6 dense-path kernels (3 dequantisations, the q8 of x, the gate/up and down GEMMs)
+        "gpu_launches": steps * ((6 if fmt == 4 else 7) + (6 if args.shared_fmt == "q5k" else 0)),
     }
     if cl:
         out["clocks"] = cl

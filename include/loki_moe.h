@@ -107,10 +107,10 @@ LK_API int lk_moe_set_gemm_threshold(LkMoeCtx* ctx, int min_tokens);
  * mma.sync path (IQ2 decoded into tensor-core fragments, reused by up to 16 tokens per expert slot);
  * smaller calls take the single-token dp4a matvecs */
 LK_API int lk_moe_set_mma_threshold(LkMoeCtx* ctx, int min_tokens);
-/* calls with >= min_tokens tokens (default 16) run a Q5_K/Q6_K shared expert (sh_fmt = LK_FMT_Q5K) as dense
- * fp16 GEMMs with fp32 accumulation (its weights dequantised once per call, cuBLAS); fewer tokens take the
- * per-token q8 kernels (the reference's numerics).  The dense path's buffers (~90 MB + 18 KB per token) are
- * allocated on its first use outside a stream capture. */
+/* calls with >= min_tokens tokens (default 16) run a Q5_K/Q6_K shared expert (sh_fmt = LK_FMT_Q5K) as two
+ * dense tcgen05 GEMMs (its weights dequantised once per call; the q8 of x and of h as in the per-token path,
+ * fp16 hi/lo operands, fp32 accumulation); fewer tokens take the per-token q8 kernels.  The dense path's
+ * buffers (~147 MB + 32 KB per token) are allocated on its first use outside a stream capture. */
 LK_API int lk_moe_set_shared_gemm_threshold(LkMoeCtx* ctx, int min_tokens);
 
 /* optional per-kernel timing: events[0..3] (cudaEvent_t) recorded on the launch stream before the gate/up

@@ -19,7 +19,7 @@ LIB = os.path.join(HERE, "libloki_moe.so")
 # the engine-side replay harness (csrc/fl_replay.cpp): plain C++ against the fl_* ABI of LIB
 REPLAY_SRC = os.path.join(CSRC, "fl_replay.cpp")
 REPLAY_LIB = os.path.join(HERE, "libloki_replay.so")
-SOURCES = ["expert_gemv.cu", "expert_gemv1.cu", "aux_kernels.cu", "router.cu", "dispatch.cu", "prefill_gemm.cu", "gate_up_q8.cu", "moe_api.cu", "fl_abi.cu", "noalloc.cu", "ep.cu", "ep_comm.cu", "slot_mma.cu", "ep_p2p.cu", "expert_kq.cu", "shared_kq.cu", "kq_mma.cu"]
+SOURCES = ["expert_gemv.cu", "expert_gemv1.cu", "aux_kernels.cu", "router.cu", "dispatch.cu", "prefill_gemm.cu", "gate_up_q8.cu", "moe_api.cu", "fl_abi.cu", "noalloc.cu", "ep.cu", "ep_comm.cu", "slot_mma.cu", "ep_p2p.cu", "expert_kq.cu", "shared_kq.cu", "shared_gemm.cu", "kq_mma.cu"]
 HEADERS = ["moe_format.h", "moe_device.cuh", "moe_internal.h", "tcgen05.cuh", "iq2_tc.cuh", "iq2_grid.inc",
            os.path.join("..", "..", "include", "loki_moe.h"), os.path.join("..", "..", "include", "loki_fused_moe.h"),
            os.path.join("..", "..", "include", "loki_ep.h")]
@@ -68,7 +68,7 @@ def build(force=False, verbose=False, ptxas_verbose=False):
                 raise RuntimeError("nvcc failed on %s" % src)
     if force or _stale(LIB, objs):
         cuda_lib = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "lib64")
-        cmd = [nv, "-ccbin", host_cxx()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda", "-ldl", "-lcublas",
+        cmd = [nv, "-ccbin", host_cxx()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda", "-ldl",
                                                                                 "-Xlinker", "-rpath=" + cuda_lib]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

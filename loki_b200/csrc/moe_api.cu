@@ -6,7 +6,6 @@
 #include <cstdarg>
 #include <string>
 #include <algorithm>
-#include <cublas_v2.h>
 #include "../../include/loki_moe.h"
 #include "../../include/loki_ep.h"
 #include "moe_internal.h"
@@ -30,10 +29,9 @@ struct LkMoeCtx {
     // the shared expert in the real model's formats (W->sh_fmt == LK_FMT_Q5K) runs as its own launches
     // (shared_kq.cu); the routed slot tables then carry no shared slots (rs = 0).  shgu: its fp32 gate/up rows
     int rs = 0; float* shgu = nullptr; int* shpair = nullptr;
-    // its dense path for calls of >= sh_gemm_min tokens (launch_shared_gemm), allocated on first use outside a
-    // stream capture: fp16 weights (88 MB), fp16 x and h rows, a cuBLAS handle and its workspace
-    int sh_gemm_min = 16; __half* shw16 = nullptr; __half* shx16 = nullptr; __half* shh16 = nullptr;
-    void* blas = nullptr; void* blas_ws = nullptr;
+    // its dense path for calls of >= sh_gemm_min tokens (launch_shared_gemm, tcgen05), allocated on first use
+    // outside a stream capture: dequantised weights (147 MB), x and h token tiles
+    int sh_gemm_min = 16; uint8_t* shw16 = nullptr; uint8_t* shx16 = nullptr; uint8_t* shh16 = nullptr;
     // batch regimes (T >= mma_min_tokens): the q8 gate/up on GEMM_NT-token slots (bt: its hi/lo activation
     // tiles), the IQ2_XXS down on tcgen05 from gemm_min_tokens (ht: its B tiles)
     int* g_expert = nullptr; int* g_tok = nullptr; int* g_out = nullptr; float* g_w = nullptr; int* g_n = nullptr; int g_max = 0;
@@ -58,26 +56,16 @@ static int set_err(LkMoeCtx* c, int code, const char* fmt, ...) {
 #define LK_CU(call) do { cudaError_t e_ = (call); if (e_ != cudaSuccess) \
     return set_err(c, LK_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); } while (0)
 
-constexpr size_t SH_W16_HALVES = (size_t)3 * MOE_INTER * HIDDEN;   // gate, up, down in fp16
-constexpr size_t BLAS_WS_BYTES = (size_t)32 << 20;
-
-// the shared expert's dense path: buffers and the cuBLAS handle on first use; false while a stream capture
-// is active and they are missing (the caller then takes the per-token kernels)
+// the shared expert's dense path: its buffers on first use; false while a stream capture is active and they
+// are missing, or an allocation failed (the caller then takes the per-token kernels)
 static bool ensure_shared_gemm(LkMoeCtx* c, cudaStream_t st) {
-    if (c->blas) return true;
+    if (c->shh16) return true;
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
-    const size_t T = (size_t)c->cfg.max_tokens;
-    cublasHandle_t h = nullptr;
-    if (cudaMalloc((void**)&c->shw16, SH_W16_HALVES * sizeof(__half)) != cudaSuccess ||
-        cudaMalloc((void**)&c->shx16, T * HIDDEN * sizeof(__half)) != cudaSuccess ||
-        cudaMalloc((void**)&c->shh16, T * MOE_INTER * sizeof(__half)) != cudaSuccess ||
-        cudaMalloc(&c->blas_ws, BLAS_WS_BYTES) != cudaSuccess || cublasCreate(&h) != CUBLAS_STATUS_SUCCESS ||
-        cublasSetWorkspace(h, c->blas_ws, BLAS_WS_BYTES) != CUBLAS_STATUS_SUCCESS) {
-        if (h) cublasDestroy(h);
-        return false;
-    }
-    c->blas = h;
+    const size_t T = (size_t)(c->cfg.max_tokens + 127) / 128 * 128;    // >= sh_gemm_pad(n) for every n <= max_tokens
+    if (!c->shw16 && cudaMalloc((void**)&c->shw16, SH_GEMM_W16_BYTES) != cudaSuccess) { c->shw16 = nullptr; return false; }
+    if (!c->shx16 && cudaMalloc((void**)&c->shx16, T * HIDDEN * 4) != cudaSuccess) { c->shx16 = nullptr; return false; }
+    if (cudaMalloc((void**)&c->shh16, T * MOE_INTER * 2) != cudaSuccess) { c->shh16 = nullptr; return false; }
     return true;
 }
 
@@ -172,8 +160,7 @@ void lk_moe_destroy(LkMoeCtx* c) {
                      c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt,
                      c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->hb, c->ep_x, c->shgu, c->shpair };
     for (void* p : ptrs) if (p) cudaFree(p);
-    if (c->blas) cublasDestroy((cublasHandle_t)c->blas);
-    void* gp[] = { c->shw16, c->shx16, c->shh16, c->blas_ws };
+    void* gp[] = { c->shw16, c->shx16, c->shh16 };
     for (void* p : gp) if (p) cudaFree(p);
     delete c;
 }
@@ -342,9 +329,8 @@ static int run_stage(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int ld_
         if (sp.n >= c->sh_gemm_min && ensure_shared_gemm(c, st)) {
             SharedGemmParams gp{};
             gp.gate = sp.gate; gp.up = sp.up; gp.down = sp.down; gp.x = x; gp.ld_x = ld_x; gp.t0 = sp.t0; gp.n = sp.n; gp.row0 = sp.row0;
-            gp.w16 = c->shw16; gp.x16 = c->shx16; gp.h16 = c->shh16; gp.gu = c->shgu; gp.y = c->y; gp.blas = c->blas;
-            const int bs = launch_shared_gemm(gp, st);
-            if (bs) return set_err(c, LK_ERR_CUDA, "shared-expert GEMM: cuBLAS status %d", bs);
+            gp.w16 = c->shw16; gp.x16 = c->shx16; gp.h16 = c->shh16; gp.y = c->y; gp.err = c->err;
+            if (launch_shared_gemm(gp, st)) LK_CU(cudaGetLastError());
         } else {
             launch_shared_kq(sp, c->nsm, st);
         }

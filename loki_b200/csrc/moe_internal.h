@@ -98,16 +98,19 @@ struct SharedKqParams {
 };
 void launch_shared_kq(const SharedKqParams& p, int grid, cudaStream_t st);
 
-// the same shared expert for many tokens as dense GEMMs: its three matrices dequantised to fp16 (w16:
-// [gate 2048 | up 2048][7168] then down [7168][2048]), x rows to fp16 (x16 [n][7168]), gate/up = cuBLAS fp16
-// GEMM with fp32 accumulation into gu, SwiGLU in fp32 rounded to fp16 (h16 [n][2048]), the down GEMM into y
-// rows row0 + j.  blas: a cublasHandle_t with its workspace set.  Returns a cublasStatus_t.
+// the same shared expert for many tokens as dense tcgen05 GEMMs (shared_gemm.cu): its three matrices
+// dequantised (w16: SH_GEMM_W16_BYTES; gate/up as fp16 hi/lo pairs, down fp16), the q8 of x as fp16 hi/lo
+// token tiles (x16: 4 * HIDDEN bytes per padded token), gate/up with SwiGLU and the q8 of h as fp16 into h16
+// (2 * MOE_INTER bytes per padded token), the down into y rows row0 + j.  Tokens are padded to
+// sh_gemm_pad(n).  Returns 0, or 1 on a launch error.
+constexpr size_t SH_GEMM_W16_BYTES = (size_t)2 * 2 * MOE_INTER * HIDDEN * 2 + (size_t)HIDDEN * MOE_INTER * 2;
 struct SharedGemmParams {
     const uint8_t* gate; const uint8_t* up; const uint8_t* down;
     const float* x; int ld_x; int t0, n, row0;
-    __half* w16; __half* x16; __half* h16; float* gu; float* y;
-    void* blas;
+    uint8_t* w16; uint8_t* x16; uint8_t* h16; float* y; int* err;
 };
+int sh_gemm_tile_tokens(int n);
+inline int sh_gemm_pad(int n) { const int nt = sh_gemm_tile_tokens(n); return (n + nt - 1) / nt * nt; }
 int launch_shared_gemm(const SharedGemmParams& p, cudaStream_t st);
 
 // ---- combine: h = resid + shared + sum_k y[t*keep+k], moe = sum_k y[t*keep+k]

@@ -18,11 +18,7 @@
 // the reference's swiglu_q8) from its own sums and the partner's, and resets the counter.
 // down: k_down1_kq<FMT_Q6K> (expert_kq.cu) in its shared-only mode, reading those q8 rows.
 //
-// Many tokens (launch_shared_gemm): the kernels above re-stream the 32 MB of weights once per token, so for
-// batches the three matrices are dequantised to fp16 once per call (k_kq_to_f16, the gguf-py values rounded
-// to fp16), x is rounded to fp16, and the two products are dense cuBLAS GEMMs with fp32 accumulation; SwiGLU
-// runs in fp32 between them.
-#include <cublas_v2.h>
+// Many tokens: shared_gemm.cu (the same expert as two dense tcgen05 GEMMs on fp16-dequantised weights).
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
@@ -214,97 +210,7 @@ __global__ void __launch_bounds__(S5_THREADS, 1) k_sh_gate_up_q5k(SharedKqParams
     }
 }
 
-// ---- the dense path for many tokens
-// one thread per 8 consecutive weights (one 16-byte fp16 store): block b = i / 32, weights 8(i % 32) ..
-template <int FMT>
-__global__ void __launch_bounds__(256) k_kq_to_f16(const uint8_t* __restrict__ W, int64_t nblk, __half* __restrict__ out) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= nblk * 32) return;
-    const uint8_t* blk = W + (i >> 5) * fmt_block_bytes(FMT);
-    const int w0 = 8 * (int)(i & 31);
-    float v[8];
-    if (FMT == FMT_Q5K) {
-        const int j = w0 >> 6, u = (w0 >> 5) & 1, l0 = w0 & 31;
-        int sc, mn;
-        q5k_scale_min(blk + Q5K_SC, 2 * j + u, sc, mn);
-        const float d = __half2float(__ushort_as_half((uint16_t)(blk[0] | (blk[1] << 8))));
-        const float dmin = __half2float(__ushort_as_half((uint16_t)(blk[2] | (blk[3] << 8))));
-        const float dl = d * (float)sc, ml = dmin * (float)mn;
-        #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int q = ((blk[Q5K_QS + 32 * j + l0 + k] >> (4 * u)) & 15) | (((blk[Q5K_QH + l0 + k] >> (2 * j + u)) & 1) << 4);
-            v[k] = dl * (float)q - ml;
-        }
-    } else {                                          // Q6_K
-        const int n = w0 >> 7, c = (w0 >> 5) & 3, l0 = w0 & 31;
-        const float d = __half2float(__ushort_as_half((uint16_t)(blk[Q6K_D] | (blk[Q6K_D + 1] << 8))));
-        const float dl = d * (float)(int8_t)blk[Q6K_SC + w0 / 16];
-        #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int q = ((blk[64 * n + 32 * (c & 1) + l0 + k] >> (4 * (c >> 1))) & 15) | (((blk[Q6K_QH + 32 * n + l0 + k] >> (2 * c)) & 3) << 4);
-            v[k] = dl * (float)(q - 32);
-        }
-    }
-    __half2 h[4];
-    #pragma unroll
-    for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
-    *(uint4*)(out + 8 * i) = *(const uint4*)h;
-}
-
-// rows [t0, t0 + n) of an fp32 matrix [.][K] (row stride ld) -> fp16 [n][K], 8 values per thread
-__global__ void __launch_bounds__(256) k_rows_to_f16(const float* __restrict__ x, int ld, int t0, int n, int K, __half* __restrict__ out) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int per = K / 8;
-    if (i >= (int64_t)n * per) return;
-    const int r = (int)(i / per), c = (int)(i % per) * 8;
-    const float4* src = (const float4*)(x + (size_t)(t0 + r) * ld + c);
-    const float4 a = src[0], b = src[1];
-    __half2 h[4] = { __floats2half2_rn(a.x, a.y), __floats2half2_rn(a.z, a.w), __floats2half2_rn(b.x, b.y), __floats2half2_rn(b.z, b.w) };
-    *(uint4*)(out + (size_t)r * K + c) = *(const uint4*)h;
-}
-
-// h16[j][k] = fp16(SwiGLU(gu[j][k], gu[j][2048 + k])), 8 values per thread
-__global__ void __launch_bounds__(256) k_swiglu_f16(const float* __restrict__ gu, int n, __half* __restrict__ h16) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    constexpr int per = MOE_INTER / 8;
-    if (i >= (int64_t)n * per) return;
-    const int r = (int)(i / per), c = (int)(i % per) * 8;
-    const float* g = gu + (size_t)r * 2 * MOE_INTER + c;
-    __half2 h[4];
-    #pragma unroll
-    for (int k = 0; k < 4; ++k)
-        h[k] = __floats2half2_rn(lk_swiglu(g[2 * k], g[MOE_INTER + 2 * k]), lk_swiglu(g[2 * k + 1], g[MOE_INTER + 2 * k + 1]));
-    *(uint4*)(h16 + (size_t)r * MOE_INTER + c) = *(const uint4*)h;
-}
-
 }  // namespace
-
-int launch_shared_gemm(const SharedGemmParams& p, cudaStream_t st) {
-    if (p.n <= 0) return 0;
-    const int64_t gblk = (int64_t)MOE_INTER * (HIDDEN / QK), dblk = (int64_t)HIDDEN * (MOE_INTER / QK);
-    __half* wg = p.w16;
-    __half* wu = p.w16 + (size_t)MOE_INTER * HIDDEN;
-    __half* wd = p.w16 + (size_t)2 * MOE_INTER * HIDDEN;
-    k_kq_to_f16<FMT_Q5K><<<(unsigned)((gblk * 32 + 255) / 256), 256, 0, st>>>(p.gate, gblk, wg);
-    k_kq_to_f16<FMT_Q5K><<<(unsigned)((gblk * 32 + 255) / 256), 256, 0, st>>>(p.up, gblk, wu);
-    k_kq_to_f16<FMT_Q6K><<<(unsigned)((dblk * 32 + 255) / 256), 256, 0, st>>>(p.down, dblk, wd);
-    const int64_t nx = (int64_t)p.n * (HIDDEN / 8);
-    k_rows_to_f16<<<(unsigned)((nx + 255) / 256), 256, 0, st>>>(p.x, p.ld_x, p.t0, p.n, HIDDEN, p.x16);
-    cublasHandle_t hb = (cublasHandle_t)p.blas;
-    cublasStatus_t s = cublasSetStream(hb, st);
-    const float one = 1.0f, zero = 0.0f;
-    // gu[n][4096] = x16[n][7168] . [gate; up][4096][7168]^T   (column-major: C = A^T B)
-    if (s == CUBLAS_STATUS_SUCCESS)
-        s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, 2 * MOE_INTER, p.n, HIDDEN, &one, wg, CUDA_R_16F, HIDDEN, p.x16, CUDA_R_16F,
-                         HIDDEN, &zero, p.gu, CUDA_R_32F, 2 * MOE_INTER, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-    if (s != CUBLAS_STATUS_SUCCESS) return (int)s;
-    const int64_t nh = (int64_t)p.n * (MOE_INTER / 8);
-    k_swiglu_f16<<<(unsigned)((nh + 255) / 256), 256, 0, st>>>(p.gu, p.n, p.h16);
-    // y[row0 + j][7168] = h16[n][2048] . down[7168][2048]^T
-    s = cublasGemmEx(hb, CUBLAS_OP_T, CUBLAS_OP_N, HIDDEN, p.n, MOE_INTER, &one, wd, CUDA_R_16F, MOE_INTER, p.h16, CUDA_R_16F,
-                     MOE_INTER, &zero, p.y + (size_t)p.row0 * HIDDEN, CUDA_R_32F, HIDDEN, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
-    return (int)s;
-}
 
 void launch_shared_kq(const SharedKqParams& p, int grid, cudaStream_t st) {
     static bool attr = false;
