@@ -9,10 +9,11 @@
 //   The last CTA to finish a token tile (an atomic count after a fence) runs the top-k for it, so the
 //   router is one launch.
 // k_router_batch (T >= 64): the same logits in the same order, with the data movement turned around: a CTA
-//   keeps a tile of 4 tokens' rows in shared memory and streams expert rows past it, so each (token,
-//   expert) pair costs ~7 KB of L2 traffic instead of the 31.5 KB of one expert x 8 tokens per CTA.  Thread
-//   p still owns partial p (chunks p + 256 j of every row, fmaf in the same order, the same butterfly and
-//   warp tree), so the results are bit-identical to k_router_logits and the oracle.
+//   keeps a tile of 8 tokens' rows in shared memory and streams expert rows past it, 4 experts at a time
+//   against all 8 tokens (32 accumulators per thread, expert chunks 3 deep in registers), so each (token,
+//   expert) pair costs ~3.5 KB of L2 traffic and each fmaf 1 B of shared-memory traffic.  Thread p still owns partial p (chunks p + 256 j
+//   of every row, fmaf in the same order, the butterfly's pair sums and the same warp tree), so the results
+//   are bit-identical to k_router_logits and the oracle.
 // router_topk_token: one warp per token: top-k of p + bias with ties to the lower expert id (reference
 //   router_topk, src/fused_layer.cu:323-332), or the DeepSeek-V3 grouped mode (n_group groups of 32
 //   experts, group score = sum of the group's top-2, keep topk_group groups); weights p/max(sum, 2^-14)
@@ -117,90 +118,136 @@ __global__ void __launch_bounds__(256) k_router_logits(RouterParams p) {
     if (tid == 0) p.tile_count[blockIdx.y] = 0;       // ready for the next call
 }
 
-constexpr int RB_TT = 4;                          // tokens per CTA tile
-constexpr int RB_EB = 8;                          // experts per barrier round (the 8 warp sums per pair)
-constexpr int RB_SMEM = RB_TT * HIDDEN * 4;       // the token tile: 112 KB, two CTAs per SM
+constexpr int RB_TT = 8;                          // tokens per CTA tile
+constexpr int RB_EG = 4;                          // experts per group: 8 x 4 (token, expert) accumulators per thread
+constexpr int RB_NP = RB_TT * RB_EG;              // 32 pairs per group: one per lane after the warp reduction
+constexpr int RB_SMEM = RB_TT * HIDDEN * 4;       // the token tile: 224 KB, one CTA per SM
+constexpr int RB_J = HIDDEN / 1024;               // 7 float4 chunks per thread and row
+constexpr int RB_RING = 4;                        // expert chunks in flight per thread (registers)
 
-__device__ __forceinline__ void rb_load_w(const RouterParams& p, int e, int tid, float4 (&w)[HIDDEN / 1024]) {
+// chunk j (float4 tid + 256 j) of the rows of experts e .. e + RB_EG - 1
+__device__ __forceinline__ void rb_load_wc(const RouterParams& p, int e, int j, int tid, float4 (&w)[RB_EG]) {
+    const int c = tid + 256 * j;
     #pragma unroll
-    for (int j = 0; j < HIDDEN / 1024; ++j) {
-        const int c = tid + 256 * j;
+    for (int k = 0; k < RB_EG; ++k) {
         if (p.w_f16) {
-            const uint2 raw = __ldg((const uint2*)((const __half*)p.W + (size_t)e * HIDDEN) + c);
+            const uint2 raw = __ldg((const uint2*)((const __half*)p.W + (size_t)(e + k) * HIDDEN) + c);
             const float2 a = __half22float2(*(const __half2*)&raw.x), b = __half22float2(*(const __half2*)&raw.y);
-            w[j] = make_float4(a.x, a.y, b.x, b.y);
+            w[k] = make_float4(a.x, a.y, b.x, b.y);
         } else {
-            w[j] = __ldg((const float4*)((const float*)p.W + (size_t)e * HIDDEN) + c);
+            w[k] = __ldg((const float4*)((const float*)p.W + (size_t)(e + k) * HIDDEN) + c);
         }
     }
 }
 
-// one CTA = RB_TT tokens x experts [e0, e0 + n_experts / esplit); the top-k of a token tile runs in the
-// CTA that finishes it (its only CTA when esplit == 1)
-__global__ void __launch_bounds__(256) k_router_batch(RouterParams p) {
+// acc[RB_EG t + k] += the 4 products of chunk w[k] with x chunk xv[t], in component order (fmaf), the 32 pairs
+// interleaved component by component
+__device__ __forceinline__ void rb_fma(float (&acc)[RB_NP], const float4 (&w)[RB_EG], const float4 (&xv)[RB_TT]) {
+    #pragma unroll
+    for (int t = 0; t < RB_TT; ++t)
+        #pragma unroll
+        for (int k = 0; k < RB_EG; ++k) acc[RB_EG * t + k] = fmaf(w[k].x, xv[t].x, acc[RB_EG * t + k]);
+    #pragma unroll
+    for (int t = 0; t < RB_TT; ++t)
+        #pragma unroll
+        for (int k = 0; k < RB_EG; ++k) acc[RB_EG * t + k] = fmaf(w[k].y, xv[t].y, acc[RB_EG * t + k]);
+    #pragma unroll
+    for (int t = 0; t < RB_TT; ++t)
+        #pragma unroll
+        for (int k = 0; k < RB_EG; ++k) acc[RB_EG * t + k] = fmaf(w[k].z, xv[t].z, acc[RB_EG * t + k]);
+    #pragma unroll
+    for (int t = 0; t < RB_TT; ++t)
+        #pragma unroll
+        for (int k = 0; k < RB_EG; ++k) acc[RB_EG * t + k] = fmaf(w[k].w, xv[t].w, acc[RB_EG * t + k]);
+}
+
+// one CTA = RB_TT tokens x experts [e0, e0 + n_experts / esplit) in groups of RB_EG; the top-k of a token
+// tile runs in the CTA that finishes it (its only CTA when esplit == 1).
+// Thread p owns partial p of every (token, expert) pair: chunks p + 256 j (j = 0..6) with fmaf over the 4
+// components in order -- k_router_logits' order.  The token rows sit in shared memory (each thread reads only
+// its own chunks, which it stored itself).  The expert chunks stream through registers as one sequence
+// q = 7 * group + j, RB_RING chunks ahead of their use.  A warp's 32 partials of each of the 32 pairs of a group
+// are summed by halving exchanges (offsets 16, 8, 4, 2, 1: at each step a lane keeps half of its values and
+// adds the partner's copy of the same pair), which forms exactly the xor butterfly's pair sums and leaves pair
+// `lane` in lane `lane`; the 8 warp sums as ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7)).  So the logits are
+// bit-identical to k_router_logits and to the oracle.
+__global__ void __launch_bounds__(256, 1) k_router_batch(RouterParams p) {
     const int esplit = p.esplit;
-    extern __shared__ __align__(16) float4 xt[];  // [RB_TT][HIDDEN / 4]; thread tid only touches chunks tid + 256 j
-    __shared__ float ws[8][RB_TT][RB_EB];
+    extern __shared__ __align__(16) float4 xt[];  // [RB_TT][HIDDEN / 4]
+    __shared__ float ws[2][8][RB_NP];             // warp sums, double-buffered by group parity
     __shared__ int last;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr int NCH = HIDDEN / 4, J = NCH / 256;
+    constexpr int NCH = HIDDEN / 4;
     const int t0 = blockIdx.x * RB_TT, nt = min(RB_TT, p.T - t0);
     const int per = p.n_experts / esplit, e0 = blockIdx.y * per;
-    float4 w[J];
-    rb_load_w(p, e0, tid, w);                     // router weights are never written by a kernel
+    const int nq = per / RB_EG * RB_J;            // chunks of this CTA's expert rows, in use order
+    float4 ring[RB_RING][RB_EG];
+    #pragma unroll
+    for (int r = 0; r < RB_RING; ++r)             // router weights are never written by a kernel
+        if (r < nq) rb_load_wc(p, e0 + r / RB_J * RB_EG, r % RB_J, tid, ring[r]);
+    int pf_g = e0 + RB_RING / RB_J * RB_EG, pf_j = RB_RING % RB_J;   // the chunk RB_RING ahead
     pdl_trigger();
     pdl_wait();
     #pragma unroll
     for (int t = 0; t < RB_TT; ++t)
         #pragma unroll
-        for (int j = 0; j < J; ++j)
+        for (int j = 0; j < RB_J; ++j)
             xt[t * NCH + tid + 256 * j] = t < nt ? ((const float4*)(p.x + (size_t)(t0 + t) * p.ld_x))[tid + 256 * j]
                                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int eb = e0; eb < e0 + per; eb += RB_EB) {
-        #pragma unroll 1
-        for (int k = 0; k < RB_EB; ++k) {
-            const int e = eb + k;
-            const bool more = e + 1 < e0 + per;
-            float4 wn[J];
-            if (more) rb_load_w(p, e + 1, tid, wn);   // the next row is in flight during this one's sums
-            float a[RB_TT];
+    float acc[RB_NP];                             // pair i = RB_EG * t + k
+    #pragma unroll
+    for (int i = 0; i < RB_NP; ++i) acc[i] = 0.0f;
+    int j = 0, gi = 0;                            // chunk and group of q
+    for (int q0 = 0; q0 < nq; q0 += RB_RING) {
+        #pragma unroll
+        for (int r = 0; r < RB_RING; ++r) {
+            const int q = q0 + r;
+            if (q >= nq) break;                   // uniform across the CTA
+            float4 xv[RB_TT];
             #pragma unroll
-            for (int t = 0; t < RB_TT; ++t) {
-                a[t] = 0.0f;
+            for (int t = 0; t < RB_TT; ++t) xv[t] = xt[t * NCH + tid + 256 * j];
+            rb_fma(acc, ring[r], xv);
+            if (q + RB_RING < nq) {               // refill this ring slot with the chunk RB_RING ahead
+                rb_load_wc(p, pf_g, pf_j, tid, ring[r]);
+                if (++pf_j == RB_J) { pf_j = 0; pf_g += RB_EG; }
+            }
+            if (j == RB_J - 1) {                  // the group's sums: warp reduction, then the warp tree
                 #pragma unroll
-                for (int j = 0; j < J; ++j) {
-                    const float4 xv = xt[t * NCH + tid + 256 * j];
-                    a[t] = fmaf(w[j].x, xv.x, a[t]);
-                    a[t] = fmaf(w[j].y, xv.y, a[t]);
-                    a[t] = fmaf(w[j].z, xv.z, a[t]);
-                    a[t] = fmaf(w[j].w, xv.w, a[t]);
+                for (int o = 16, h = RB_NP / 2; o >= 1; o >>= 1, h >>= 1) {
+                    const bool up = (lane & o) != 0;
+                    #pragma unroll
+                    for (int i = 0; i < h; ++i) {
+                        const float send = up ? acc[i] : acc[i + h];
+                        const float keep = up ? acc[i + h] : acc[i];
+                        acc[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+                    }
                 }
-            }
-            #pragma unroll
-            for (int t = 0; t < RB_TT; ++t) {
+                // pair index bits 4..0 = lane bits 4..0.  One barrier per group: group n's sums go to buffer
+                // n & 1 and are read by warp n % 8 after the barrier; buffer n & 1 is next written after the
+                // following group's barrier, which that reader has passed only once it finished reading.
+                float (*wb)[RB_NP] = ws[gi & 1];
+                wb[warp][lane] = acc[0];
+                __syncthreads();
+                if (warp == (gi & 7)) {
+                    const int t = lane / RB_EG, k = lane % RB_EG;
+                    if (t < nt) {
+                        const float lg = __fadd_rn(__fadd_rn(__fadd_rn(wb[0][lane], wb[1][lane]), __fadd_rn(wb[2][lane], wb[3][lane])),
+                                                   __fadd_rn(__fadd_rn(wb[4][lane], wb[5][lane]), __fadd_rn(wb[6][lane], wb[7][lane])));
+                        const size_t o = (size_t)(t0 + t) * p.n_experts + e0 + gi * RB_EG + k;
+                        p.logits[o] = lg;
+                        const float v = p.logits_override ? p.logits_override[o] : lg;
+                        p.probs[o] = lk_sigmoid(v);
+                    }
+                }
                 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) a[t] = __fadd_rn(a[t], __shfl_xor_sync(0xffffffffu, a[t], o));
-                if (lane == 0) ws[warp][t][k] = a[t];
-            }
-            if (more) {
-                #pragma unroll
-                for (int j = 0; j < J; ++j) w[j] = wn[j];
+                for (int i = 0; i < RB_NP; ++i) acc[i] = 0.0f;
+                j = 0; ++gi;
+            } else {
+                ++j;
             }
         }
-        __syncthreads();
-        if (tid < RB_TT * RB_EB) {
-            const int t = tid / RB_EB, k = tid % RB_EB;
-            if (t < nt) {
-                const float lg = __fadd_rn(__fadd_rn(__fadd_rn(ws[0][t][k], ws[1][t][k]), __fadd_rn(ws[2][t][k], ws[3][t][k])),
-                                           __fadd_rn(__fadd_rn(ws[4][t][k], ws[5][t][k]), __fadd_rn(ws[6][t][k], ws[7][t][k])));
-                const size_t o = (size_t)(t0 + t) * p.n_experts + eb + k;
-                p.logits[o] = lg;
-                const float v = p.logits_override ? p.logits_override[o] : lg;
-                p.probs[o] = lk_sigmoid(v);
-            }
-        }
-        __syncthreads();
     }
+    __syncthreads();                              // every group's probabilities are written
     if (!p.tile_count) return;
     if (esplit > 1) {                             // as k_router_logits: acquire-release count per token tile
         if (tid == 0) last = atom_add_acq_rel_gpu(&p.tile_count[blockIdx.x], 1) == esplit - 1;
@@ -405,7 +452,7 @@ __device__ void router_topk_cta(const RouterParams& p, int t) {
     }
 }
 
-// p.tile_count: T zeroed ints (one per token tile of 8, or of 4 for the batch kernel; left zeroed again)
+// p.tile_count: T zeroed ints (one per token tile of 8; left zeroed again)
 void launch_router(const RouterParams& p, cudaStream_t st) {
     const int ne = p.n_experts;
     if (p.T <= 1) launch_pdl(k_router_logits<1>, dim3(ne, 1), dim3(256), 0, st, p);
@@ -416,9 +463,9 @@ void launch_router(const RouterParams& p, cudaStream_t st) {
         static bool attr = false;
         if (!attr) { cudaFuncSetAttribute(k_router_batch, cudaFuncAttributeMaxDynamicSharedMemorySize, RB_SMEM); attr = true; }
         int dev = 0; cudaGetDevice(&dev);
-        const int tiles = (p.T + RB_TT - 1) / RB_TT, target = 2 * num_sms(dev);
-        int esplit = 1;                           // split the experts until there are ~2 CTAs per SM
-        while (tiles * esplit < target && (ne / (2 * esplit)) % RB_EB == 0) esplit *= 2;
+        const int tiles = (p.T + RB_TT - 1) / RB_TT, target = num_sms(dev);
+        int esplit = 1;                           // split the experts until every SM has a CTA
+        while (tiles * esplit < target && (ne / (2 * esplit)) % RB_EG == 0) esplit *= 2;
         RouterParams q = p;
         q.esplit = esplit;
         launch_pdl(k_router_batch, dim3(tiles, esplit), dim3(256), RB_SMEM, st, q);

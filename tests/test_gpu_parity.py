@@ -52,10 +52,13 @@ ROUTE_MODES = {
 }
 
 
-@pytest.mark.parametrize("T", [1, 3, 16, 512])
+@pytest.mark.parametrize("T", [1, 3, 16, 100, 512, 4096])
 @pytest.mark.parametrize("f16", [False, True])
 @pytest.mark.parametrize("mode", list(ROUTE_MODES))
 def test_router_bitexact(native, moe, oracle, T, f16, mode):
+    """Probabilities, ids and weights bit-identical to the oracle: the per-expert kernel (T < 64) and the
+    token-tile batch kernel (T >= 64; T = 100 ends on a partial tile of 4 tokens, T = 512 splits the experts
+    over 4 CTAs per tile, T = 4096 does not split)."""
     md = ROUTE_MODES[mode]
     rng = np.random.default_rng(100 + T)
     x = rng.standard_normal((T, HIDDEN)).astype(np.float32)
