@@ -23,6 +23,8 @@ int max_slots_for(int T, int keep, int n_experts, int nt, int with_shared) {
 }
 
 __global__ void __launch_bounds__(DS_THREADS) k_build_slots(SlotParams p) {
+    pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
+    pdl_wait();                                   // the predecessor grid has completed
     __shared__ int cnt[N_EXPERTS], off[N_EXPERTS + 1], soff[N_EXPERTS + 1], run[N_EXPERTS];
     __shared__ unsigned short wcnt[DS_THREADS / 32][N_EXPERTS];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -102,7 +104,7 @@ __global__ void __launch_bounds__(DS_THREADS) k_build_slots(SlotParams p) {
 }
 
 void launch_build_slots(const SlotParams& p, cudaStream_t st) {
-    k_build_slots<<<1, DS_THREADS, 0, st>>>(p);
+    launch_pdl(k_build_slots, dim3(1), dim3(DS_THREADS), 0, st, p);
 }
 
 }  // namespace lk

@@ -22,6 +22,8 @@ static_assert(sizeof(EpRowHdr) == LK_EP_ROW_HDR_BYTES, "header size");
 __global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(const int* __restrict__ sel, int T, int keep, int n_ranks,
                                                               int self_rank, int cap, int* counts, int* row_map, uint8_t* send,
                                                               int* err) {
+    pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
+    pdl_wait();                                   // the predecessor grid has completed
     __shared__ int wc[LK_EP_MAX_RANKS][32], pre[LK_EP_MAX_RANKS][32], base[LK_EP_MAX_RANKS], off[LK_EP_MAX_RANKS + 1];
     __shared__ int cnt[LK_EP_MAX_RANKS];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -93,6 +95,8 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS) k_ep_plan(const int* __restri
 __global__ void __launch_bounds__(256) k_ep_copy(const int* __restrict__ sel, const float* __restrict__ w,
                                                   const float* __restrict__ x, int keep, int n_ranks,
                                                   const int* __restrict__ row_map, uint8_t* send) {
+    pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
+    pdl_wait();                                   // the predecessor grid has completed
     const int t = blockIdx.x, tid = threadIdx.x;
     const int epr = N_EXPERTS / n_ranks;
     int rows[LK_EP_MAX_RANKS];
@@ -123,6 +127,8 @@ __global__ void __launch_bounds__(256) k_ep_copy(const int* __restrict__ sel, co
 
 // received rows -> fp32 activations [R][HIDDEN] (q * d; the expert kernels' q8 of these values gives back q)
 __global__ void k_ep_dequant(const uint8_t* __restrict__ recv, int R, float* __restrict__ x) {
+    pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
+    pdl_wait();                                   // the predecessor grid has completed
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;   // over R x HIDDEN / 4
     if (i >= (size_t)R * (HIDDEN / 4)) return;
     const int r = (int)(i / (HIDDEN / 4)), c = (int)(i % (HIDDEN / 4));
@@ -134,6 +140,8 @@ __global__ void k_ep_dequant(const uint8_t* __restrict__ recv, int R, float* __r
 }
 
 __global__ void k_ep_unpack(const uint8_t* __restrict__ recv, int R, int keep, int* sel, float* w) {
+    pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
+    pdl_wait();                                   // the predecessor grid has completed
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= R * keep) return;
     const int r = i / keep, k = i % keep;
@@ -144,6 +152,8 @@ __global__ void k_ep_unpack(const uint8_t* __restrict__ recv, int R, int keep, i
 
 __global__ void k_ep_combine(const float* __restrict__ ret, const int* __restrict__ row_map, int T, int n_ranks,
                              const float* __restrict__ hpart, const float* __restrict__ shared, float* h, float* moe) {
+    pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
+    pdl_wait();                                   // the predecessor grid has completed
     const int i = blockIdx.x * blockDim.x + threadIdx.x;       // float4 index over T x HIDDEN
     if (i >= T * (HIDDEN / 4)) return;
     const int t = i / (HIDDEN / 4), c = i % (HIDDEN / 4);
@@ -167,15 +177,15 @@ __global__ void k_ep_combine(const float* __restrict__ ret, const int* __restric
 
 int ep_plan(const int* sel, int T, int keep, int n_ranks, int self_rank, int cap, int* counts, int* row_map, uint8_t* send,
             int* err, cudaStream_t st) {
-    k_ep_plan<<<1, EP_PLAN_THREADS, 0, st>>>(sel, T, keep, n_ranks, self_rank, cap, counts, row_map, send, err);
+    launch_pdl_n(k_ep_plan, dim3(1), dim3(EP_PLAN_THREADS), 0, st, sel, T, keep, n_ranks, self_rank, cap, counts, row_map, send, err);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
 void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, float* x, cudaStream_t st) {
     const int n = R * keep;
-    k_ep_unpack<<<(n + 255) / 256, 256, 0, st>>>((const uint8_t*)recv, R, keep, sel, w);
+    launch_pdl_n(k_ep_unpack, dim3((n + 255) / 256), dim3(256), 0, st, (const uint8_t*)recv, R, keep, sel, w);
     const size_t nx = (size_t)R * (HIDDEN / 4);
-    if (x && R > 0) k_ep_dequant<<<(unsigned)((nx + 255) / 256), 256, 0, st>>>((const uint8_t*)recv, R, x);
+    if (x && R > 0) launch_pdl_n(k_ep_dequant, dim3((unsigned)((nx + 255) / 256)), dim3(256), 0, st, (const uint8_t*)recv, R, x);
 }
 
 }  // namespace lk
@@ -193,7 +203,7 @@ int lk_ep_pack(const int* sel, const float* w, const float* x, int T, int keep, 
     if (((uintptr_t)send_rows & 15) || ((uintptr_t)x & 15)) return LK_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
     if (ep_plan(sel, T, keep, n_ranks, self_rank, cap, send_counts, row_map, (uint8_t*)send_rows, err, st)) return LK_ERR_CUDA;
-    if (T > 0) k_ep_copy<<<T, 256, 0, st>>>(sel, w, x, keep, n_ranks, row_map, (uint8_t*)send_rows);
+    if (T > 0) launch_pdl_n(k_ep_copy, dim3(T), dim3(256), 0, st, sel, w, x, keep, n_ranks, (const int*)row_map, (uint8_t*)send_rows);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
@@ -203,7 +213,7 @@ int lk_ep_combine(const float* ret, const int* row_map, int T, int n_ranks, cons
         return LK_ERR_ARG;
     if (T == 0) return LK_OK;
     const int n = T * (HIDDEN / 4);
-    k_ep_combine<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(ret, row_map, T, n_ranks, h_partial, shared, h, moe);
+    launch_pdl_n(k_ep_combine, dim3((n + 255) / 256), dim3(256), 0, (cudaStream_t)stream, ret, row_map, T, n_ranks, h_partial, shared, h, moe);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 

@@ -45,6 +45,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 __global__ void __launch_bounds__(P2P_THREADS) k_p2p_send(const int* __restrict__ sel, const float* __restrict__ w,
                                                            const float* __restrict__ x, int T, int keep, int n_ranks,
                                                            int self, int cap, P2PPeers peers) {
+    pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
+    pdl_wait();                                   // the predecessor grid has completed
     const int d = blockIdx.x, tid = threadIdx.x;
     const int epr = N_EXPERTS / n_ranks;
     const uint32_t epoch = *mb_epoch(peers.mb[self]) + 1u;
@@ -77,6 +79,8 @@ __global__ void __launch_bounds__(P2P_THREADS) k_p2p_send(const int* __restrict_
 // one CTA per source rank s: this rank's partial sums for s's rows into s's mailbox block `self`
 __global__ void __launch_bounds__(P2P_THREADS) k_p2p_return(const float* __restrict__ partial, int n_ranks, int self,
                                                              int cap, P2PPeers peers) {
+    pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
+    pdl_wait();                                   // the predecessor grid has completed
     const int s = blockIdx.x, tid = threadIdx.x;
     const uint32_t epoch = *mb_epoch(peers.mb[self]) + 1u;
     const float4* src = (const float4*)(partial + (size_t)s * cap * HIDDEN);
@@ -92,6 +96,8 @@ __global__ void __launch_bounds__(P2P_THREADS) k_p2p_return(const float* __restr
 // lane s waits (bounded) until flag `which` of source s reaches this layer's epoch; `advance`: then the
 // epoch moves on (the layer's last wait)
 __global__ void k_p2p_wait(uint8_t* mb, int which, int n_ranks, int advance, int* err) {
+    pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
+    pdl_wait();                                   // the predecessor grid has completed
     const int s = threadIdx.x;
     const uint32_t want = *mb_epoch(mb) + 1u;
     bool ok = true;
@@ -184,20 +190,20 @@ int lk_ep_p2p_dispatch(LkEpMailbox* m, const int* sel, const float* w, const flo
     int* counts = (int*)(m->local + 2 * LK_EP_MAX_RANKS * 4 + 4);   // scratch in the mailbox header (8 ints)
     int rc = ep_plan(sel, T, keep, m->n_ranks, m->rank, m->cap, counts, row_map, nullptr, err, st);
     if (rc) return rc;
-    k_p2p_send<<<m->n_ranks, P2P_THREADS, 0, st>>>(sel, w, x, T, keep, m->n_ranks, m->rank, m->cap, m->peers);
+    launch_pdl_n(k_p2p_send, dim3(m->n_ranks), dim3(P2P_THREADS), 0, st, sel, w, x, T, keep, m->n_ranks, m->rank, m->cap, m->peers);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
 int lk_ep_p2p_rows(LkEpMailbox* m, const void** rows, int* err, lk_stream_t stream) {
     if (!m || !rows) return LK_ERR_ARG;
-    k_p2p_wait<<<1, 32, 0, (cudaStream_t)stream>>>(m->local, 0, m->n_ranks, 0, err);
+    launch_pdl_n(k_p2p_wait, dim3(1), dim3(32), 0, (cudaStream_t)stream, m->local, 0, m->n_ranks, 0, err);
     *rows = m->local + P2P_HDR;
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
 int lk_ep_p2p_return(LkEpMailbox* m, const float* partial, lk_stream_t stream) {
     if (!m || !partial) return LK_ERR_ARG;
-    k_p2p_return<<<m->n_ranks, P2P_THREADS, 0, (cudaStream_t)stream>>>(partial, m->n_ranks, m->rank, m->cap, m->peers);
+    launch_pdl_n(k_p2p_return, dim3(m->n_ranks), dim3(P2P_THREADS), 0, (cudaStream_t)stream, partial, m->n_ranks, m->rank, m->cap, m->peers);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
@@ -205,7 +211,7 @@ int lk_ep_p2p_combine(LkEpMailbox* m, const int* row_map, int T, const float* re
                       float* moe, int* err, lk_stream_t stream) {
     if (!m || T < 1 || T > m->cap || !row_map) return LK_ERR_ARG;
     cudaStream_t st = (cudaStream_t)stream;
-    k_p2p_wait<<<1, 32, 0, st>>>(m->local, 1, m->n_ranks, 1, err);
+    launch_pdl_n(k_p2p_wait, dim3(1), dim3(32), 0, st, m->local, 1, m->n_ranks, 1, err);
     if (cudaGetLastError() != cudaSuccess) return LK_ERR_CUDA;
     const float* rets = (const float*)(m->local + P2P_HDR + (size_t)m->n_ranks * m->cap * LK_EP_ROW_BYTES);
     return lk_ep_combine(rets, row_map, T, m->n_ranks, resid, shared, h, moe, stream);

@@ -9,6 +9,7 @@
 //     over units of 32 rows (one 16 896-byte copy each), 4 warps per unit, each warp 8 rows: 8 row
 //     sums by one warp_reduce8, y = w * 0.125 * sum.  Decode: the selector table (iq2_dot1), which
 //     measured faster here than the sign-on-activation core.
+#include "../../include/loki_ep.h"
 #include "moe_internal.h"
 #include "moe_device.cuh"
 
@@ -167,7 +168,13 @@ __global__ void __launch_bounds__(G1_THREADS, 1) k_gate_up1(ExpertParams p) {
                 nx[0] = b0.x; nx[1] = b0.y; nx[2] = b0.z; nx[3] = b0.w; nx[4] = b1.x; nx[5] = b1.y; nx[6] = b1.z; nx[7] = b1.w;
                 dx = p.xd[g];
             } else {
-                if (tok >= 0) dx = q8_group_global(p.x + (size_t)tok * p.ld_x, g, xr);
+                if (tok >= 0 && p.xrows) {           // an expert-parallel row: its q8 codes and scale as sent
+                    const uint8_t* row = p.xrows + (size_t)tok * LK_EP_ROW_BYTES;
+                    const uint4 a0 = ((const uint4*)(row + LK_EP_ROW_Q_OFF + g * 32))[0];
+                    const uint4 a1 = ((const uint4*)(row + LK_EP_ROW_Q_OFF + g * 32))[1];
+                    xr[0] = a0.x; xr[1] = a0.y; xr[2] = a0.z; xr[3] = a0.w; xr[4] = a1.x; xr[5] = a1.y; xr[6] = a1.z; xr[7] = a1.w;
+                    dx = ((const float*)(row + LK_EP_ROW_D_OFF))[g];
+                } else if (tok >= 0) dx = q8_group_global(p.x + (size_t)tok * p.ld_x, g, xr);
                 else { dx = 0.0f; for (int j = 0; j < 8; ++j) xr[j] = 0u; }
                 #pragma unroll
                 for (int j = 0; j < 8; ++j) nx[j] = neg_i8x4(xr[j]);

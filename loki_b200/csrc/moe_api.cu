@@ -44,6 +44,7 @@ struct LkMoeCtx {
     // tokens (T=32: 1.67 ms vs 2.03 mma, 2.23 tcgen05), mma.sync from 48 (T=64: 2.65 vs 3.24 / 2.96 ms,
     // T=128: 3.26 vs 3.56 tcgen05), tcgen05 from 192 (T=256: 3.84 vs 4.13 mma; T=512: 4.31 vs 6.26)
     float* ep_x = nullptr;            // lk_ep_experts: the received rows' activations, dequantised (on first use)
+    const uint8_t* ep_rows = nullptr; // lk_ep_experts on the single-token path: the rows themselves (their q8 codes)
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     char msg[256] = {0};
 };
@@ -241,6 +242,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
     e.slot_expert = c->slot_expert; e.slot_tok = c->slot_tok; e.slot_out = c->slot_out; e.slot_w = c->slot_w; e.nslots = c->nslots;
     e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err; e.down_fmt = W->down_fmt;
     if (c->xq_ready && x == c->xq_src) { e.xq = c->xq; e.xqn = c->xqn; e.xd = c->xd; }
+    e.xrows = c->ep_rows;
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
     if (c->ev[1]) LK_CU(record_event(c->ev[1], st));
@@ -422,20 +424,24 @@ int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int
     int rc = check_weights(c, W, false);
     if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
-    if (!c->ep_x) {                   // the rows' fp32 activations: allocated on first use, outside a capture
+    // the single-token path with an IQ2_XXS (or no) shared expert reads the rows' q8 codes directly; every other
+    // path reads fp32 activations, the rows dequantised to q * d (their q8 is again q and d)
+    const bool direct = R < c->mma_min_tokens && (c->rs || !c->cfg.with_shared);
+    if (!direct && !c->ep_x) {        // the rows' fp32 activations: allocated on first use, outside a capture
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
         if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
-            return set_err(c, LK_ERR_ARG, "the first lk_ep_experts call on a context must run outside a stream capture");
+            return set_err(c, LK_ERR_ARG, "the first lk_ep_experts call of a batch on a context must run outside a stream capture");
         LK_CU(dalloc(&c->ep_x, (size_t)c->cfg.max_tokens * HIDDEN));
     }
-    launch_ep_unpack(recv_rows, R, keep, c->sel, c->w, c->ep_x, st);
-    const float* x = c->ep_x;
+    launch_ep_unpack(recv_rows, R, keep, c->sel, c->w, direct ? nullptr : c->ep_x, st);
+    const float* x = direct ? nullptr : c->ep_x;
     const int ld = HIDDEN;
+    c->ep_rows = direct ? (const uint8_t*)recv_rows : nullptr;
     // out = the routed partial sums; the shared expert runs in the same launches on the rows
     // [shared_row0, +shared_rows), and its outputs (entry rows R*keep + j) are copied to shared_out
     c->sh_t0 = shared_row0; c->sh_n = shared_rows > 0 ? shared_rows : -1;
     rc = run_stage(c, W, x, ld, nullptr, R, c->sel, c->w, keep, nullptr, out, false, st);
-    c->sh_t0 = 0; c->sh_n = 0;
+    c->sh_t0 = 0; c->sh_n = 0; c->ep_rows = nullptr;
     if (rc) return rc;
     if (shared_rows > 0)
         LK_CU(cudaMemcpyAsync(shared_out, c->y + (size_t)R * keep * HIDDEN, (size_t)shared_rows * HIDDEN * sizeof(float),

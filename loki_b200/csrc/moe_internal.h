@@ -47,6 +47,17 @@ inline cudaError_t launch_pdl(void (*kernel)(P), dim3 grid, dim3 block, size_t s
     cfg.attrs = attr; cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, params);
 }
+// the same for kernels with several parameters
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_n(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid; cfg.blockDim = block; cfg.dynamicSmemBytes = smem; cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 // ---- dispatch: per-expert stable token lists and the work-slot table of the grouped matvecs
 struct SlotParams {
@@ -73,6 +84,9 @@ struct ExpertParams {
     const float* x; int ld_x;                         // activations [T][HIDDEN] (fp32; quantised to q8 in-kernel)
     const int* slot_expert; const int* slot_tok; const int* slot_out; const float* slot_w; const int* nslots;
     const int8_t* xq; const int8_t* xqn; const float* xd;   // optional: token 0's q8 activations from the router
+    // optional: the activations as expert-parallel rows (include/loki_ep.h): token t's q8 codes and scales read
+    // from row t (the single-token gate/up only; x is then not read)
+    const uint8_t* xrows;
     int8_t* hq; float* hd;                            // SwiGLU output q8: [rows][MOE_INTER], scales [rows][MOE_INTER/32]
     float* y;                                         // weighted expert outputs [rows][HIDDEN]
     int* err;
