@@ -23,9 +23,11 @@ __global__ void __launch_bounds__(64) k_combine(CombineParams p) {
         v[k] = k < p.keep ? ((const float4*)(p.y + ((size_t)t * p.keep + k) * HIDDEN))[c] : zero;
     }
     const int nsh = p.sh_n < 0 ? 0 : (p.sh_n > 0 ? p.sh_n : p.T), j = t - p.sh_t0;
-    const bool has_sh = p.h && p.with_shared && j >= 0 && j < nsh;
+    const bool in_sh = p.with_shared && j >= 0 && j < nsh;
+    const bool has_sh = p.h && in_sh;
     const float4 hr = p.h && p.resid ? ((const float4*)(p.resid + (size_t)t * p.ld_out))[c] : zero;
-    const float4 hs = has_sh ? ((const float4*)(p.y + ((size_t)p.T * p.keep + j) * HIDDEN))[c] : zero;
+    const float4 hs = in_sh && (p.h || p.shared_out) ? ((const float4*)(p.y + ((size_t)p.T * p.keep + j) * HIDDEN))[c] : zero;
+    if (in_sh && p.shared_out) ((float4*)(p.shared_out + (size_t)j * HIDDEN))[c] = hs;
     const float4 he = p.h && p.shared ? ((const float4*)(p.shared + (size_t)t * HIDDEN))[c] : zero;
     float4 r = zero;
     #pragma unroll

@@ -45,6 +45,7 @@ struct LkMoeCtx {
     // T=128: 3.26 vs 3.56 tcgen05), tcgen05 from 192 (T=256: 3.84 vs 4.13 mma; T=512: 4.31 vs 6.26)
     float* ep_x = nullptr;            // lk_ep_experts: the received rows' activations, dequantised (on first use)
     const uint8_t* ep_rows = nullptr; // lk_ep_experts on the single-token path: the rows themselves (their q8 codes)
+    float* ep_shared_out = nullptr;   // lk_ep_experts: where the combine copies the shared expert's rows
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     char msg[256] = {0};
 };
@@ -252,6 +253,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
         CombineParams cp{};
         cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
         cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel; cp.sh_t0 = c->sh_t0; cp.sh_n = c->sh_n;
+        cp.shared_out = c->ep_shared_out;
         launch_combine(cp, st);
     }
     if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
@@ -306,6 +308,7 @@ static int run_batch_path(LkMoeCtx* c, const LkMoeWeights* W, const float* x, in
         CombineParams cp{};
         cp.y = c->y; cp.resid = resid; cp.T = T; cp.keep = keep; cp.with_shared = c->cfg.with_shared; cp.shared = nullptr;
         cp.h = h; cp.moe = moe; cp.ld_out = HIDDEN; cp.sel = sel; cp.sh_t0 = c->sh_t0; cp.sh_n = c->sh_n;
+        cp.shared_out = c->ep_shared_out;
         launch_combine(cp, st);
     }
     if (c->ev[3]) LK_CU(record_event(c->ev[3], st));
@@ -437,16 +440,13 @@ int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int
     const float* x = direct ? nullptr : c->ep_x;
     const int ld = HIDDEN;
     c->ep_rows = direct ? (const uint8_t*)recv_rows : nullptr;
+    c->ep_shared_out = shared_rows > 0 ? shared_out : nullptr;   // the combine writes them (no copy node)
     // out = the routed partial sums; the shared expert runs in the same launches on the rows
     // [shared_row0, +shared_rows), and its outputs (entry rows R*keep + j) are copied to shared_out
     c->sh_t0 = shared_row0; c->sh_n = shared_rows > 0 ? shared_rows : -1;
     rc = run_stage(c, W, x, ld, nullptr, R, c->sel, c->w, keep, nullptr, out, false, st);
-    c->sh_t0 = 0; c->sh_n = 0; c->ep_rows = nullptr;
-    if (rc) return rc;
-    if (shared_rows > 0)
-        LK_CU(cudaMemcpyAsync(shared_out, c->y + (size_t)R * keep * HIDDEN, (size_t)shared_rows * HIDDEN * sizeof(float),
-                              cudaMemcpyDeviceToDevice, st));
-    return LK_OK;
+    c->sh_t0 = 0; c->sh_n = 0; c->ep_rows = nullptr; c->ep_shared_out = nullptr;
+    return rc;
 }
 
 int lk_ep_shared(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, float* h_partial,

@@ -135,6 +135,7 @@ struct CombineParams {
     float* h; float* moe; int ld_out;
     const int* sel;                   // optional [T][keep]: entries with a negative id are not summed
     int sh_t0, sh_n;                  // shared-expert rows as in SlotParams; resid may be null (zero)
+    float* shared_out;                // optional: the shared expert's output of rows [sh_t0, +sh_n) -> row j here
 };
 void launch_combine(const CombineParams& p, cudaStream_t st);
 
