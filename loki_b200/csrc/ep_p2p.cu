@@ -5,9 +5,10 @@
 // source rank, partial sums returned by each owner rank, and two flag arrays -- exported with CUDA IPC and
 // mapped by every peer.  Senders store straight into the destination's mailbox over NVLink, then publish
 // a flag (fence + release store, system scope); receivers poll their local flags (acquire loads, system
-// scope) with a bounded wait before reading.  Flags carry a per-rank epoch that the last wait of a layer
-// advances, so the same kernels replay correctly inside a captured CUDA graph.  No rank can run a layer
-// ahead: each layer ends with a wait for every owner's return.
+// scope) with a bounded wait before reading.  Flags carry a per-rank epoch E: a layer's sends publish E + 1,
+// the rows wait (one CTA) waits for E + 1 and then advances the epoch, and the returns publish, and the
+// combine waits for, the advanced value; so the same kernels replay correctly inside a captured CUDA graph.
+// No rank can run a layer ahead: each layer ends with a wait for every owner's return.
 //
 // Layout of one mailbox (bytes): [flags: 2 x LK_EP_MAX_RANKS u32, epoch u32, pad to 256]
 //   [rows: n_ranks x cap x LK_EP_ROW_BYTES] [rets: n_ranks x cap x 7168 fp32]
@@ -42,9 +43,10 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 
 // one CTA per destination rank d: this rank's rows for d (tokens with an entry on d, and every token to
 // itself) into d's mailbox block `self`, unused rows with empty headers, then the dispatch flag
+// (and row_map[t][d]: block d's row of token t, d * cap + r, or -1 -- the fixed-capacity pack's map)
 __global__ void __launch_bounds__(P2P_THREADS) k_p2p_send(const int* __restrict__ sel, const float* __restrict__ w,
                                                            const float* __restrict__ x, int T, int keep, int n_ranks,
-                                                           int self, int cap, P2PPeers peers) {
+                                                           int self, int cap, P2PPeers peers, int* row_map, int* err) {
     pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
     pdl_wait();                                   // the predecessor grid has completed
     const int d = blockIdx.x, tid = threadIdx.x;
@@ -54,7 +56,12 @@ __global__ void __launch_bounds__(P2P_THREADS) k_p2p_send(const int* __restrict_
     int r = 0;
     for (int t = 0; t < T; ++t) {
         bool has = d == self;
-        for (int k = 0; k < keep && !has; ++k) { const int e = sel[t * keep + k]; has = e >= d * epr && e < (d + 1) * epr; }
+        for (int k = 0; k < keep; ++k) {
+            const int e = sel[t * keep + k];
+            has = has || (e >= d * epr && e < (d + 1) * epr);
+            if ((e < 0 || e >= N_EXPERTS) && tid == 0 && d == 0 && err) atomicCAS(err, 0, DEV_ERR_BAD_SLOT);
+        }
+        if (tid == 0) row_map[(size_t)t * n_ranks + d] = has ? d * cap + r : -1;
         if (!has) continue;                            // uniform across the CTA
         uint8_t* row = block + (size_t)r * LK_EP_ROW_BYTES;
         if (tid < 16) {
@@ -82,7 +89,7 @@ __global__ void __launch_bounds__(P2P_THREADS) k_p2p_return(const float* __restr
     pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
     pdl_wait();                                   // the predecessor grid has completed
     const int s = blockIdx.x, tid = threadIdx.x;
-    const uint32_t epoch = *mb_epoch(peers.mb[self]) + 1u;
+    const uint32_t epoch = *mb_epoch(peers.mb[self]);            // advanced by this layer's rows wait
     const float4* src = (const float4*)(partial + (size_t)s * cap * HIDDEN);
     float4* dst = (float4*)(mb_rets(peers.mb[s], n_ranks, cap) + (size_t)self * cap * HIDDEN);
     for (int i = tid; i < cap * HIDDEN / 4; i += P2P_THREADS) dst[i] = src[i];
@@ -93,8 +100,8 @@ __global__ void __launch_bounds__(P2P_THREADS) k_p2p_return(const float* __restr
     }
 }
 
-// lane s waits (bounded) until flag `which` of source s reaches this layer's epoch; `advance`: then the
-// epoch moves on (the layer's last wait)
+// the rows wait: lane s waits (bounded) until source s's rows flag reaches this layer's epoch + 1, then the
+// epoch advances to it (one CTA: every lane has read the old value before lane 0 writes)
 __global__ void k_p2p_wait(uint8_t* mb, int which, int n_ranks, int advance, int* err) {
     pdl_trigger();                                // the next kernel may be scheduled; it waits for this grid
     pdl_wait();                                   // the predecessor grid has completed
@@ -113,6 +120,48 @@ __global__ void k_p2p_wait(uint8_t* mb, int which, int n_ranks, int advance, int
     }
     __syncwarp();
     if (advance && s == 0) *mb_epoch(mb) = want;
+}
+
+// the home combine fused with the returns wait: in every CTA, threads s < n_ranks wait (bounded) for owner s's
+// return flag to reach this layer's (already advanced) epoch; then h = resid + shared + sum over ranks (rank
+// order) and moe = that sum, as k_ep_combine
+__global__ void k_p2p_combine(const uint8_t* mb, int n_ranks, int cap, const int* __restrict__ row_map, int T,
+                              const float* __restrict__ hpart, const float* __restrict__ shared, float* h, float* moe,
+                              int* err) {
+    pdl_trigger();
+    pdl_wait();
+    const int tid = threadIdx.x;
+    if (tid < n_ranks) {
+        const uint32_t want = *mb_epoch((uint8_t*)mb);
+        const uint32_t* f = mb_flags((uint8_t*)mb, 1) + tid;
+        if ((int)(ld_acquire_sys(f) - want) < 0) {
+            const unsigned long long t0 = globaltimer_ns();
+            while ((int)(ld_acquire_sys(f) - want) < 0) {
+                if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) { if (err) atomicCAS(err, 0, DEV_ERR_TIMEOUT_EMPTY); break; }
+            }
+        }
+    }
+    __syncthreads();
+    const float* ret = mb_rets((uint8_t*)mb, n_ranks, cap);
+    const int i = blockIdx.x * blockDim.x + tid;                     // float4 index over T x HIDDEN
+    if (i >= T * (HIDDEN / 4)) return;
+    const int t = i / (HIDDEN / 4), c = i % (HIDDEN / 4);
+    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int d = 0; d < n_ranks; ++d) {
+        const int row = row_map[(size_t)t * n_ranks + d];
+        if (row < 0) continue;
+        const float4 v = ((const float4*)(ret + (size_t)row * HIDDEN))[c];
+        r.x += v.x; r.y += v.y; r.z += v.z; r.w += v.w;
+    }
+    if (moe) ((float4*)(moe + (size_t)t * HIDDEN))[c] = r;
+    if (h && hpart) {
+        float4 b = ((const float4*)(hpart + (size_t)t * HIDDEN))[c];
+        if (shared) {
+            const float4 v = ((const float4*)(shared + (size_t)t * HIDDEN))[c];
+            b.x += v.x; b.y += v.y; b.z += v.z; b.w += v.w;
+        }
+        ((float4*)(h + (size_t)t * HIDDEN))[c] = make_float4(b.x + r.x, b.y + r.y, b.z + r.z, b.w + r.w);
+    }
 }
 
 }  // namespace lk
@@ -186,17 +235,15 @@ int lk_ep_p2p_dispatch(LkEpMailbox* m, const int* sel, const float* w, const flo
     if (!m || T < 1 || T > m->cap || keep < 1 || keep > MAX_TOPK || !sel || !w || !x || !row_map) return LK_ERR_ARG;
     for (int r = 0; r < m->n_ranks; ++r) if (!m->peers.mb[r]) return LK_ERR_ARG;   // not connected
     cudaStream_t st = (cudaStream_t)stream;
-    // row_map and counts as the fixed-capacity pack computes them (rows ordered by token per destination)
-    int* counts = (int*)(m->local + 2 * LK_EP_MAX_RANKS * 4 + 4);   // scratch in the mailbox header (8 ints)
-    int rc = ep_plan(sel, T, keep, m->n_ranks, m->rank, m->cap, counts, row_map, nullptr, err, st);
-    if (rc) return rc;
-    launch_pdl_n(k_p2p_send, dim3(m->n_ranks), dim3(P2P_THREADS), 0, st, sel, w, x, T, keep, m->n_ranks, m->rank, m->cap, m->peers);
+    // the send kernel also writes row_map (the fixed-capacity pack's map) and checks the ids
+    launch_pdl_n(k_p2p_send, dim3(m->n_ranks), dim3(P2P_THREADS), 0, st, sel, w, x, T, keep, m->n_ranks, m->rank, m->cap, m->peers,
+                 row_map, err);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
 int lk_ep_p2p_rows(LkEpMailbox* m, const void** rows, int* err, lk_stream_t stream) {
     if (!m || !rows) return LK_ERR_ARG;
-    launch_pdl_n(k_p2p_wait, dim3(1), dim3(32), 0, (cudaStream_t)stream, m->local, 0, m->n_ranks, 0, err);
+    launch_pdl_n(k_p2p_wait, dim3(1), dim3(32), 0, (cudaStream_t)stream, m->local, 0, m->n_ranks, 1, err);
     *rows = m->local + P2P_HDR;
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
@@ -210,11 +257,10 @@ int lk_ep_p2p_return(LkEpMailbox* m, const float* partial, lk_stream_t stream) {
 int lk_ep_p2p_combine(LkEpMailbox* m, const int* row_map, int T, const float* resid, const float* shared, float* h,
                       float* moe, int* err, lk_stream_t stream) {
     if (!m || T < 1 || T > m->cap || !row_map) return LK_ERR_ARG;
-    cudaStream_t st = (cudaStream_t)stream;
-    launch_pdl_n(k_p2p_wait, dim3(1), dim3(32), 0, st, m->local, 1, m->n_ranks, 1, err);
-    if (cudaGetLastError() != cudaSuccess) return LK_ERR_CUDA;
-    const float* rets = (const float*)(m->local + P2P_HDR + (size_t)m->n_ranks * m->cap * LK_EP_ROW_BYTES);
-    return lk_ep_combine(rets, row_map, T, m->n_ranks, resid, shared, h, moe, stream);
+    const int n = T * (HIDDEN / 4);
+    launch_pdl_n(k_p2p_combine, dim3((n + 255) / 256), dim3(256), 0, (cudaStream_t)stream, (const uint8_t*)m->local, m->n_ranks,
+                 m->cap, row_map, T, resid, shared, h, moe, err);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
 }  // extern "C"
