@@ -99,19 +99,49 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // independent accumulators per P buffer for N' = 2 * round16(tokens) columns each (a power of two, <= 4)
 __device__ __forceinline__ int gq_nacc(int n2) { return n2 <= 32 ? 4 : (n2 <= 64 ? 2 : 1); }
 
-// the 8 MMAs of one K-block with N' = N2 known at compile time: instruction descriptor, B step and accumulator
-// offsets are immediates (a runtime descriptor measured ~2x slower per tcgen05.mma)
+// the 8 MMAs of one K-block with N' = N2 known at compile time, as one asm block: one elect.sync, the
+// instruction descriptor and the A / B / accumulator steps as immediates, the descriptor's high word shared
+// (the MMA warp shares its sub-partition with busy decode warps, so its issue slots are scarce)
 template <int N2>
 __device__ __forceinline__ void gq_issue_kblock(uint32_t d, uint32_t a0, uint32_t bring_st, int kb) {
     constexpr int nacc = N2 <= 32 ? 4 : (N2 <= 64 ? 2 : 1);
     constexpr uint32_t idesc = idesc_f16_f32(GQ_M, N2);
     constexpr uint32_t lbo = (uint32_t)(N2 >> 3) * 128;
-    constexpr uint64_t bstep = (uint64_t)((2 * lbo) >> 4);             // one K=16 step along the B tile
+    constexpr uint32_t bstep = (2 * lbo) >> 4;                          // one K=16 step along the B tile
     const uint64_t b0 = umma_desc(bring_st, lbo, 128);
-    #pragma unroll
-    for (int ks = 0; ks < GQ_KB / 16; ++ks)                              // K step ks -> accumulator ks % nacc
-        umma_f16_ta_warp(d + (uint32_t)((ks % nacc) * N2), a0 + ks * 8, b0 + (uint64_t)ks * bstep, idesc,
-                         (kb & 1) || ks >= nacc);
+    const uint32_t blo = (uint32_t)b0, bhi = (uint32_t)(b0 >> 32);
+    // K step ks: A columns a0 + 8 ks, B start + ks * bstep, accumulator ks % nacc; the first nacc steps
+    // accumulate only in the superblock's second K-block
+    asm volatile("{\n\t.reg .pred e, q0, q1, q2, q3, q4, q5, q6, q7;\n\t.reg .b32 aa, bl, dd;\n\t.reg .b64 bd;\n\t"
+        "setp.ne.b32 q0, %5, 0;\n\t"
+        "setp.ne.b32 q1, %5, %30;\n\t" "setp.ne.b32 q2, %5, %31;\n\t" "setp.ne.b32 q3, %5, %32;\n\t"
+        "setp.ne.b32 q4, %5, %33;\n\t" "setp.ne.b32 q5, %5, %34;\n\t" "setp.ne.b32 q6, %5, %35;\n\t" "setp.ne.b32 q7, %5, %36;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "add.u32 aa, %1, %6;\n\t" "add.u32 bl, %2, %14;\n\t" "mov.b64 bd, {bl, %3};\n\t" "add.u32 dd, %0, %22;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [dd], [aa], bd, %4, q0;\n\t"
+        "add.u32 aa, %1, %7;\n\t" "add.u32 bl, %2, %15;\n\t" "mov.b64 bd, {bl, %3};\n\t" "add.u32 dd, %0, %23;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [dd], [aa], bd, %4, q1;\n\t"
+        "add.u32 aa, %1, %8;\n\t" "add.u32 bl, %2, %16;\n\t" "mov.b64 bd, {bl, %3};\n\t" "add.u32 dd, %0, %24;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [dd], [aa], bd, %4, q2;\n\t"
+        "add.u32 aa, %1, %9;\n\t" "add.u32 bl, %2, %17;\n\t" "mov.b64 bd, {bl, %3};\n\t" "add.u32 dd, %0, %25;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [dd], [aa], bd, %4, q3;\n\t"
+        "add.u32 aa, %1, %10;\n\t" "add.u32 bl, %2, %18;\n\t" "mov.b64 bd, {bl, %3};\n\t" "add.u32 dd, %0, %26;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [dd], [aa], bd, %4, q4;\n\t"
+        "add.u32 aa, %1, %11;\n\t" "add.u32 bl, %2, %19;\n\t" "mov.b64 bd, {bl, %3};\n\t" "add.u32 dd, %0, %27;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [dd], [aa], bd, %4, q5;\n\t"
+        "add.u32 aa, %1, %12;\n\t" "add.u32 bl, %2, %20;\n\t" "mov.b64 bd, {bl, %3};\n\t" "add.u32 dd, %0, %28;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [dd], [aa], bd, %4, q6;\n\t"
+        "add.u32 aa, %1, %13;\n\t" "add.u32 bl, %2, %21;\n\t" "mov.b64 bd, {bl, %3};\n\t" "add.u32 dd, %0, %29;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [dd], [aa], bd, %4, q7;\n\t"
+        "}"
+        :: "r"(d), "r"(a0), "r"(blo), "r"(bhi), "n"(idesc), "r"((uint32_t)(kb & 1)),
+           "n"(0), "n"(8), "n"(16), "n"(24), "n"(32), "n"(40), "n"(48), "n"(56),
+           "n"(0), "n"(bstep), "n"(2 * bstep), "n"(3 * bstep), "n"(4 * bstep), "n"(5 * bstep), "n"(6 * bstep), "n"(7 * bstep),
+           "n"(0), "n"((1 % nacc) * N2), "n"((2 % nacc) * N2), "n"((3 % nacc) * N2), "n"((4 % nacc) * N2),
+           "n"((5 % nacc) * N2), "n"((6 % nacc) * N2), "n"((7 % nacc) * N2),
+           "n"(1 < nacc ? 0 : 7), "n"(2 < nacc ? 0 : 7), "n"(3 < nacc ? 0 : 7), "n"(4 < nacc ? 0 : 7),
+           "n"(5 < nacc ? 0 : 7), "n"(6 < nacc ? 0 : 7), "n"(7 < nacc ? 0 : 7)
+        : "memory");
 }
 
 __device__ __forceinline__ void tmem_st16f(uint32_t taddr, const float (&v)[16]) {
