@@ -436,15 +436,23 @@ int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int
             return set_err(c, LK_ERR_ARG, "the first lk_ep_experts call of a batch on a context must run outside a stream capture");
         LK_CU(dalloc(&c->ep_x, (size_t)c->cfg.max_tokens * HIDDEN));
     }
-    launch_ep_unpack(recv_rows, R, keep, c->sel, c->w, direct ? nullptr : c->ep_x, st);
+    // out = the routed partial sums; the shared expert runs in the same launches on the rows
+    // [shared_row0, +shared_rows), and the combine writes its outputs (entry rows R*keep + j) to shared_out
+    c->sh_t0 = shared_row0; c->sh_n = shared_rows > 0 ? shared_rows : -1;
+    if (direct) {                     // headers and single-token slot tables in one kernel
+        SlotParams sp{};
+        sp.slot_expert = c->slot_expert; sp.slot_tok = c->slot_tok; sp.slot_out = c->slot_out; sp.slot_w = c->slot_w;
+        sp.nslots = c->nslots; sp.max_slots = c->max_slots; sp.err = c->err; sp.with_shared = c->rs;
+        sp.sh_t0 = c->sh_t0; sp.sh_n = c->sh_n;
+        launch_ep_slots(recv_rows, R, keep, c->cfg.n_experts, c->sel, c->w, sp, st);
+    } else {
+        launch_ep_unpack(recv_rows, R, keep, c->sel, c->w, c->ep_x, st);
+    }
     const float* x = direct ? nullptr : c->ep_x;
     const int ld = HIDDEN;
     c->ep_rows = direct ? (const uint8_t*)recv_rows : nullptr;
     c->ep_shared_out = shared_rows > 0 ? shared_out : nullptr;   // the combine writes them (no copy node)
-    // out = the routed partial sums; the shared expert runs in the same launches on the rows
-    // [shared_row0, +shared_rows), and its outputs (entry rows R*keep + j) are copied to shared_out
-    c->sh_t0 = shared_row0; c->sh_n = shared_rows > 0 ? shared_rows : -1;
-    rc = run_stage(c, W, x, ld, nullptr, R, c->sel, c->w, keep, nullptr, out, false, st);
+    rc = run_stage(c, W, x, ld, nullptr, R, c->sel, c->w, keep, nullptr, out, direct, st);
     c->sh_t0 = 0; c->sh_n = 0; c->ep_rows = nullptr; c->ep_shared_out = nullptr;
     return rc;
 }

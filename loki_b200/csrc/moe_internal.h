@@ -189,6 +189,10 @@ void launch_gen_weights(int fmt, uint8_t* dst, uint64_t seed, int layer, int mat
 
 // ---- expert-parallel row headers -> sel/w [R][keep], and (x non-null) the rows' q8 activations -> fp32
 void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, float* x, cudaStream_t st);   // x: [R][HIDDEN]
+// the same headers -> sel/w, plus the single-token slot tables of sp (slot_*, nslots, max_slots, with_shared,
+// sh_t0, sh_n, err) built directly: one slot per live entry, then the shared expert's slots
+struct SlotParams;
+void launch_ep_slots(const void* recv, int R, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, cudaStream_t st);
 // ---- expert-parallel row plan only: counts [n_ranks], row_map [T][n_ranks] (and, with `send`, the
 //      headers of unused fixed-capacity rows)
 int ep_plan(const int* sel, int T, int keep, int n_ranks, int self_rank, int cap, int* counts, int* row_map, uint8_t* send,
