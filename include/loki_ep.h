@@ -86,11 +86,15 @@ LK_API int lk_ep_all_to_all(LkEpComm* comm, const void* send, void* recv, const 
  * bounded wait (a timeout sets `err`).  Setup: lk_ep_mailbox_create on every rank (cap = the largest
  * per-rank token count, <= 64) gives an IPC handle; gather all n_ranks handles (LK_EP_IPC_HANDLE_BYTES
  * each, rank order) and pass them to lk_ep_mailbox_connect.  Per layer, on one stream:
- *   lk_ep_p2p_dispatch (plan + rows into the owners' mailboxes; every token also to itself)
+ *   lk_ep_p2p_dispatch (rows into the owners' mailboxes; every token also to itself; row_map)
  *   lk_ep_p2p_rows (wait for all ranks' rows; *rows = n_ranks*cap rows in fixed-capacity order)
  *   lk_ep_experts(rows, n_ranks*cap, ..., own rows rank*cap .. +T, partial, shared)
  *   lk_ep_p2p_return(partial)  (each block of cap partial sums to its home rank)
  *   lk_ep_p2p_combine (wait for all returns; h = resid + shared + sum, moe = sum)
+ * or, for the single-token expert path (n_ranks*cap rows below the context's mma threshold, an IQ2_XXS or no
+ * shared expert: decode), the middle three as one call:
+ *   lk_ep_p2p_experts(mb, ctx, W, keep, T, partial, shared, err)  (the rows wait fused with the slot tables,
+ *     the expert kernels reading the rows' q8 codes, then the return; LK_ERR_UNSUPPORTED outside that path)
  * All kernels are capturable; the flags carry an epoch that advances per layer on the device. */
 #define LK_EP_IPC_HANDLE_BYTES 64
 typedef struct LkEpMailbox LkEpMailbox;
@@ -103,6 +107,11 @@ LK_API int lk_ep_p2p_rows(LkEpMailbox* mb, const void** rows, int* err, lk_strea
 LK_API int lk_ep_p2p_return(LkEpMailbox* mb, const float* partial, lk_stream_t stream);
 LK_API int lk_ep_p2p_combine(LkEpMailbox* mb, const int* row_map, int T, const float* resid, const float* shared,
                              float* h, float* moe, int* err, lk_stream_t stream);
+/* no reference counterpart (the reference runs on one GPU): lk_ep_p2p_rows + lk_ep_experts + lk_ep_p2p_return
+ * with the rows wait, the header unpack and the slot building in one kernel; partial: [n_ranks*cap][7168]
+ * scratch; shared [T][7168] receives the shared expert of this rank's own T rows */
+LK_API int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* ctx, const LkMoeWeights* W, int keep, int T, float* partial,
+                             float* shared, int* err, lk_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -4,9 +4,7 @@
 // No counterpart in the reference (one GPU, experts streamed from NVMe by src/moe_stream_buffer.h).  The
 // arithmetic the rows feed is the single-GPU expert stage; only the order of the final sum differs: the
 // home rank adds the per-rank partial sums (each summed in entry order on its rank) in rank order.
-#include "../../include/loki_ep.h"
-#include "moe_internal.h"
-#include "moe_device.cuh"
+#include "ep_device.cuh"
 
 namespace lk {
 
@@ -14,8 +12,6 @@ constexpr int EP_PLAN_THREADS = 1024;
 static_assert(LK_EP_ROW_BYTES % 16 == 0 && LK_EP_ROW_Q_OFF % 16 == 0 && LK_EP_ROW_D_OFF % 16 == 0,
               "rows and their parts must keep 16-byte alignment");
 
-struct EpRowHdr { int sel[8]; float w[8]; };
-static_assert(sizeof(EpRowHdr) == LK_EP_ROW_HDR_BYTES, "header size");
 
 // one CTA: per destination rank the stable (token-ascending) row index of every token that has an entry
 // there, the per-rank counts, block offsets (fixed capacity or compact) and the headers of unused rows
@@ -182,50 +178,12 @@ int ep_plan(const int* sel, int T, int keep, int n_ranks, int self_rank, int cap
 }
 
 // received rows -> sel/w [R][keep] and, for single-token slots, the slot tables directly (the general slot
-// builder is a histogram over 256 experts with many barriers, ~20 us for a handful of rows): one slot per live
-// entry in (row, k) order, then the shared expert's slots of rows [sh_t0, +sh_n) (sh_n < 0: none); ids outside
-// [0, n_experts) are reported (DEV_ERR_BAD_SLOT) and dropped.  Every slot writes its own output row, so the
-// order of the slots changes no result.  One CTA.
-constexpr int EPS_THREADS = 256;
+// builder is a histogram over 256 experts with many barriers, ~20 us for a handful of rows)
 __global__ void __launch_bounds__(EPS_THREADS) k_ep_slots(const uint8_t* __restrict__ recv, int R, int keep, int n_experts,
                                                           int* sel, float* w, SlotParams sp) {
     pdl_trigger();
     pdl_wait();
-    __shared__ int wsum[EPS_THREADS / 32];
-    __shared__ int base;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int entries = R * keep;
-    if (tid == 0) base = 0;
-    __syncthreads();
-    for (int c0 = 0; c0 < entries; c0 += EPS_THREADS) {
-        const int i = c0 + tid;
-        int e = -1; float wv = 0.0f;
-        if (i < entries) {
-            const EpRowHdr* h = (const EpRowHdr*)(recv + (size_t)(i / keep) * LK_EP_ROW_BYTES);
-            e = h->sel[i % keep]; wv = h->w[i % keep];
-            sel[i] = e; w[i] = wv;
-            if (e >= n_experts && sp.err) atomicCAS(sp.err, 0, DEV_ERR_BAD_SLOT);
-        }
-        const bool live = i < entries && e >= 0 && e < n_experts;
-        const unsigned b = __ballot_sync(0xffffffffu, live);
-        if (lane == 0) wsum[warp] = __popc(b);
-        __syncthreads();
-        int before = base;
-        for (int k = 0; k < warp; ++k) before += wsum[k];
-        const int s = before + __popc(b & ((1u << lane) - 1u));
-        if (live && s < sp.max_slots) { sp.slot_expert[s] = e; sp.slot_tok[s] = i / keep; sp.slot_out[s] = i; sp.slot_w[s] = wv; }
-        __syncthreads();
-        if (tid == 0) { int t = base; for (int k = 0; k < EPS_THREADS / 32; ++k) t += wsum[k]; base = t; }
-        __syncthreads();
-    }
-    const int nrs = base;
-    const int nsh = !sp.with_shared || sp.sh_n < 0 ? 0 : (sp.sh_n > 0 ? sp.sh_n : R);
-    for (int j = tid; j < nsh; j += EPS_THREADS) {
-        const int s = nrs + j;
-        if (s >= sp.max_slots) continue;
-        sp.slot_expert[s] = SHARED_SLOT; sp.slot_tok[s] = sp.sh_t0 + j; sp.slot_out[s] = entries + j; sp.slot_w[s] = 1.0f;
-    }
-    if (tid == 0) *sp.nslots = min(nrs + nsh, sp.max_slots);
+    ep_slots_dev(recv, R, keep, n_experts, sel, w, sp);
 }
 
 void launch_ep_slots(const void* recv, int R, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, cudaStream_t st) {

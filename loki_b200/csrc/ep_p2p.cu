@@ -15,9 +15,7 @@
 // Row (s, r) is source rank s's r-th row for this rank; ret (d, r) is owner d's partial sum for this rank's
 // r-th row sent to d -- the same indices as the fixed-capacity send buffer, so row_map indexes rets.
 #include <cstring>
-#include "../../include/loki_ep.h"
-#include "moe_internal.h"
-#include "moe_device.cuh"
+#include "ep_device.cuh"
 
 namespace lk {
 
@@ -164,6 +162,28 @@ __global__ void k_p2p_combine(const uint8_t* mb, int n_ranks, int cap, const int
     }
 }
 
+// lk_ep_p2p_experts, first kernel: the rows wait of k_p2p_wait (lanes s < n_ranks of warp 0; every thread has
+// read the old epoch before thread 0 advances it) fused with the single-token slot tables of the received rows
+__global__ void __launch_bounds__(EPS_THREADS) k_p2p_wait_slots(uint8_t* mb, int n_ranks, int cap, int keep, int n_experts,
+                                                                int* sel, float* w, SlotParams sp, int* err) {
+    pdl_trigger();
+    pdl_wait();
+    const int tid = threadIdx.x;
+    const uint32_t want = *mb_epoch(mb) + 1u;
+    if (tid < n_ranks) {
+        const uint32_t* f = mb_flags(mb, 0) + tid;
+        if ((int)(ld_acquire_sys(f) - want) < 0) {
+            const unsigned long long t0 = globaltimer_ns();
+            while ((int)(ld_acquire_sys(f) - want) < 0) {
+                if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) { if (err) atomicCAS(err, 0, DEV_ERR_TIMEOUT_FULL); break; }
+            }
+        }
+    }
+    __syncthreads();
+    if (tid == 0) *mb_epoch(mb) = want;
+    ep_slots_dev(mb_rows(mb), n_ranks * cap, keep, n_experts, sel, w, sp);
+}
+
 }  // namespace lk
 
 using namespace lk;
@@ -264,3 +284,19 @@ int lk_ep_p2p_combine(LkEpMailbox* m, const int* row_map, int T, const float* re
 }
 
 }  // extern "C"
+
+namespace lk {
+
+int p2p_rows_count(const LkEpMailbox* m) { return m->n_ranks * m->cap; }
+int p2p_rank(const LkEpMailbox* m) { return m->rank; }
+int p2p_cap(const LkEpMailbox* m) { return m->cap; }
+
+int p2p_wait_slots(LkEpMailbox* m, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, int* err,
+                   cudaStream_t st, const uint8_t** rows) {
+    for (int r = 0; r < m->n_ranks; ++r) if (!m->peers.mb[r]) return LK_ERR_ARG;   // not connected
+    *rows = m->local + P2P_HDR;
+    launch_pdl_n(k_p2p_wait_slots, dim3(1), dim3(EPS_THREADS), 0, st, m->local, m->n_ranks, m->cap, keep, n_experts, sel, w, sp, err);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+}  // namespace lk

@@ -457,6 +457,35 @@ int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int
     return rc;
 }
 
+int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* c, const LkMoeWeights* W, int keep, int T, float* partial, float* shared_out,
+                      int* err, lk_stream_t stream) {
+    if (!mb || !c || !W || keep < 1 || T < 0 || !partial || (T > 0 && !shared_out)) return set_err(c, LK_ERR_ARG, "bad argument");
+    const int R = p2p_rows_count(mb), cap = p2p_cap(mb), rank = p2p_rank(mb);
+    if (T > cap) return set_err(c, LK_ERR_ARG, "T=%d above the mailbox capacity %d", T, cap);
+    if (R > c->cfg.max_tokens || keep > c->cfg.keep) return set_err(c, LK_ERR_CAPACITY, "R=%d keep=%d above capacity", R, keep);
+    if (T > 0 && !c->cfg.with_shared) return set_err(c, LK_ERR_ARG, "shared rows need a with_shared context");
+    int rc = check_weights(c, W, false);
+    if (rc) return rc;
+    if (!(R < c->mma_min_tokens && (c->rs || !c->cfg.with_shared)))
+        return set_err(c, LK_ERR_UNSUPPORTED, "the fused exchange serves the single-token path (R=%d rows)", R);
+    cudaStream_t st = (cudaStream_t)stream;
+    c->sh_t0 = rank * cap; c->sh_n = T > 0 ? T : -1;
+    SlotParams sp{};
+    sp.slot_expert = c->slot_expert; sp.slot_tok = c->slot_tok; sp.slot_out = c->slot_out; sp.slot_w = c->slot_w;
+    sp.nslots = c->nslots; sp.max_slots = c->max_slots; sp.err = c->err; sp.with_shared = c->rs;
+    sp.sh_t0 = c->sh_t0; sp.sh_n = c->sh_n;
+    const uint8_t* rows = nullptr;
+    rc = p2p_wait_slots(mb, keep, c->cfg.n_experts, c->sel, c->w, sp, err, st, &rows);
+    if (rc == LK_OK) {
+        c->ep_rows = rows;
+        c->ep_shared_out = T > 0 ? shared_out : nullptr;
+        rc = run_experts(c, W, nullptr, HIDDEN, nullptr, R, keep, c->sel, nullptr, partial, 1, st);
+        if (rc == LK_OK) rc = lk_ep_p2p_return(mb, partial, stream);
+    }
+    c->sh_t0 = 0; c->sh_n = 0; c->ep_rows = nullptr; c->ep_shared_out = nullptr;
+    return rc ? set_err(c, rc, "fused peer exchange: launch failed") : LK_OK;
+}
+
 int lk_ep_shared(LkMoeCtx* c, const LkMoeWeights* W, const float* x, const float* resid, int T, float* h_partial,
                  lk_stream_t stream) {
     if (!c || !W || T < 0 || (T > 0 && (!x || !resid || !h_partial))) return set_err(c, LK_ERR_ARG, "bad argument");

@@ -193,6 +193,17 @@ void launch_ep_unpack(const void* recv, int R, int keep, int* sel, float* w, flo
 // sh_t0, sh_n, err) built directly: one slot per live entry, then the shared expert's slots
 struct SlotParams;
 void launch_ep_slots(const void* recv, int R, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, cudaStream_t st);
+}  // namespace lk
+struct LkEpMailbox;
+namespace lk {
+// the peer exchange's fused stage (ep_p2p.cu) for lk_ep_p2p_experts: the rows wait + the single-token slot tables
+// of the received rows (*rows: the mailbox's rows)
+int p2p_rows_count(const LkEpMailbox* m);
+int p2p_rank(const LkEpMailbox* m);
+int p2p_cap(const LkEpMailbox* m);
+int p2p_wait_slots(LkEpMailbox* m, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, int* err,
+                   cudaStream_t st, const uint8_t** rows);
+
 // ---- expert-parallel row plan only: counts [n_ranks], row_map [T][n_ranks] (and, with `send`, the
 //      headers of unused fixed-capacity rows)
 int ep_plan(const int* sel, int T, int keep, int n_ranks, int self_rank, int cap, int* counts, int* row_map, uint8_t* send,

@@ -216,3 +216,54 @@ def test_p2p_wait_runs_out_with_error_status(native):
         assert float(torch.ones(1 << 20, device="cuda").sum()) == float(1 << 20)
     finally:
         L.lk_ep_mailbox_destroy(mb)
+
+
+def _one_rank_worker(rank, port, T_loc, out_dir):
+    import torch.distributed as dist
+    from loki_b200.moe import LayerWeights
+    from loki_b200.ep import EpMoeLayer, NativeEpOps, NativeComm, P2PExchange
+    torch.cuda.set_device(0)
+    dist.init_process_group("nccl", init_method="tcp://127.0.0.1:%d" % port, rank=0, world_size=1,
+                            device_id=torch.device("cuda", 0))
+    try:
+        W = LayerWeights("cuda:0", SEED, 0)
+        ops = NativeEpOps(0, 1, T_loc)
+        comm = NativeComm(0)
+        p2p = P2PExchange(0, T_loc)
+        layer = EpMoeLayer(comm, ops, p2p=p2p)
+        x, r = (torch.from_numpy(a).cuda() for a in _inputs(T_loc, 0))
+        outs = [layer.forward(W, x, r) for _ in range(3)]          # three layers: the epoch advances
+        torch.cuda.synchronize()
+        for o in outs[1:]:
+            assert torch.equal(o[0], outs[0][0]) and torch.equal(o[1], outs[0][1])
+        h, moe, sel, w = outs[0]
+        p2p.close()
+        comm.close()
+        ops.device_error()
+        np.savez(os.path.join(out_dir, "r0.npz"), h=h.cpu().numpy(), moe=moe.cpu().numpy(), sel=sel.cpu().numpy(),
+                 w=w.cpu().numpy(), Wr=W.router_w.float().cpu().numpy(), b=W.router_bias.cpu().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("T_loc", [1, 3])
+def test_ep_p2p_one_rank(native, oracle, tmp_path, T_loc):
+    """The peer-memory exchange with a single rank (every expert local, the rows sent to itself) on one GPU:
+    dispatch, the fused lk_ep_p2p_experts (rows wait + slot tables, the expert kernels reading the rows' q8
+    codes, partial sums stored into the home mailbox + flags) and the waiting combine, three layers in a row;
+    routing bit-exact and h / moe within RTOL_L2 of the oracle."""
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.start_processes(_one_rank_worker, args=(port, T_loc, str(tmp_path)), nprocs=1, join=True, start_method="spawn")
+    got = np.load(os.path.join(str(tmp_path), "r0.npz"))
+    x, r = _inputs(T_loc, 0)
+    _, osel, ow = oracle.router(x, got["Wr"], got["b"], oracle.route_cfg(8, 8, 1, 1, 1))
+    np.testing.assert_array_equal(got["sel"], osel)
+    np.testing.assert_array_equal(got["w"], ow)
+    ref = oracle_layer(oracle, SEED, 0, x, r, osel, ow)
+    assert rel_l2(got["moe"], ref["moe"]) < RTOL_L2
+    assert rel_l2(got["h"], ref["h"]) < RTOL_L2
