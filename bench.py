@@ -526,8 +526,9 @@ def run_ep_decode(args, ws, rank, local, dist):
         "e2e": {"value": round(n_e2e * ws / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": args.layers * 2 * HIDDEN * 4, "d2h_bytes_per_step": args.layers * HIDDEN * 4,
                 "path": "pinned host x/resid -> CUDA-graph step of EpMoeLayer.forward x58 -> pinned host h (stream events)"},
-        "gpu_launches": args.steps * args.layers * 11,     # router, plan, send/pack, wait, unpack, slots, gate/up, down,
-                                                           # combine, return, wait + EP combine
+        # per layer: router, send (p2p; with NCCL: pack, all-to-all and unpack kernels instead), the rows wait +
+        # slot tables, gate/up, down, combine, return, waiting combine
+        "gpu_launches": args.steps * args.layers * 8,
     }
     if cl:
         out["clocks"] = cl
