@@ -581,9 +581,8 @@ def run_ep_prefill(args, ws, rank, local, dist):
         "metric": "MoE-layer tokens/s (T=%d expert-parallel batch, one layer)" % T, "value": round(value, 1), "unit": "tokens/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "iq2_xxs weights -> fp16 x fp16(q8 activations), fp32 accumulate (tcgen05.mma kind::f16)" if not model_fmt else
-                 "the real model's formats (%s down, %s shared): IQ2_XXS gate/up tcgen05 fp16 x fp16, K-quant down mma.sync "
-                 "fp16 x fp16(h), Q5_K/Q6_K shared on tcgen05 (fp16 hi/lo gate/up operands, q8 h); fp32 accumulate" % (args.down_fmt, args.shared_fmt),
+        "dtype": "iq2_xxs x q8 activations: gate/up tcgen05 kind::f16 with exact integer weights and hi/lo fp16 activations "
+                 "(the reference's group sums), h re-quantised to q8; down tcgen05 fp16; fp32 accumulate; rows exchanged as q8",
         "data": "synthetic: seeded IQ2_XXS experts, router W N(0,0.02), bias N(0,0.01), bf16 N(0,1) hidden states",
         "config": {"workload": "config3_ep_batch_T%d" % T, "global_batch": T, "seq_len": T, "layers": 1, "top_k": 8, "n_group": N_GROUP, "topk_group": TOPK_GROUP,
                    "keep": args.keep, "parallelism": "ep%d" % ws, "experts_per_gpu": NE // ws, "rows_sent": sent,
