@@ -91,10 +91,13 @@ LK_API int lk_ep_all_to_all(LkEpComm* comm, const void* send, void* recv, const 
  *   lk_ep_experts(rows, n_ranks*cap, ..., own rows rank*cap .. +T, partial, shared)
  *   lk_ep_p2p_return(partial)  (each block of cap partial sums to its home rank)
  *   lk_ep_p2p_combine (wait for all returns; h = resid + shared + sum, moe = sum)
- * or, for the single-token expert path (n_ranks*cap rows below the context's mma threshold, an IQ2_XXS or no
- * shared expert: decode), the middle three as one call:
- *   lk_ep_p2p_experts(mb, ctx, W, keep, T, partial, shared, err)  (the rows wait fused with the slot tables,
- *     the expert kernels reading the rows' q8 codes, then the return; LK_ERR_UNSUPPORTED outside that path)
+ * or, for the single-token expert path (n_ranks*cap rows below the context's mma threshold and at most 64, an
+ * IQ2_XXS or no shared expert: decode), the direct return:
+ *   lk_ep_p2p_experts(mb, ctx, W, keep, T, shared, err)  (the rows wait fused with the slot tables, the expert
+ *     kernels reading the rows' q8 codes, the down kernel storing each entry's weighted row straight into its
+ *     home rank's mailbox, then the return flags; LK_ERR_UNSUPPORTED outside that path)
+ *   lk_ep_p2p_combine_entries(mb, sel, keep, row_map, ...)  (wait for all owners; h = resid + shared + the
+ *     entries summed in k order, moe = that sum: the single-GPU combine's order)
  * All kernels are capturable; the flags carry an epoch that advances per layer on the device. */
 #define LK_EP_IPC_HANDLE_BYTES 64
 typedef struct LkEpMailbox LkEpMailbox;
@@ -108,10 +111,16 @@ LK_API int lk_ep_p2p_return(LkEpMailbox* mb, const float* partial, lk_stream_t s
 LK_API int lk_ep_p2p_combine(LkEpMailbox* mb, const int* row_map, int T, const float* resid, const float* shared,
                              float* h, float* moe, int* err, lk_stream_t stream);
 /* no reference counterpart (the reference runs on one GPU): lk_ep_p2p_rows + lk_ep_experts + lk_ep_p2p_return
- * with the rows wait, the header unpack and the slot building in one kernel; partial: [n_ranks*cap][7168]
- * scratch; shared [T][7168] receives the shared expert of this rank's own T rows */
-LK_API int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* ctx, const LkMoeWeights* W, int keep, int T, float* partial,
-                             float* shared, int* err, lk_stream_t stream);
+ * with the rows wait, the header unpack and the slot building in one kernel, and the return stored by the
+ * down kernel itself (one row per routed entry, in the home mailbox); shared [T][7168] receives the shared
+ * expert of this rank's own T rows.  Pair it with lk_ep_p2p_combine_entries. */
+LK_API int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* ctx, const LkMoeWeights* W, int keep, int T, float* shared,
+                             int* err, lk_stream_t stream);
+/* no reference counterpart: the home combine of lk_ep_p2p_experts' direct return; sel [T][keep] the routing
+ * passed to lk_ep_p2p_dispatch (global ids, negative = absent), row_map its output */
+LK_API int lk_ep_p2p_combine_entries(LkEpMailbox* mb, const int* sel, int keep, const int* row_map, int T,
+                                     const float* resid, const float* shared, float* h, float* moe, int* err,
+                                     lk_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -12,8 +12,12 @@
 //
 // Layout of one mailbox (bytes): [flags: 2 x LK_EP_MAX_RANKS u32, epoch u32, pad to 256]
 //   [rows: n_ranks x cap x LK_EP_ROW_BYTES] [rets: n_ranks x cap x 7168 fp32]
+//   [entry rets, when n_ranks x cap <= P2P_DIRECT_ROWS: n_ranks x cap x 8 x 7168 fp32]
 // Row (s, r) is source rank s's r-th row for this rank; ret (d, r) is owner d's partial sum for this rank's
 // r-th row sent to d -- the same indices as the fixed-capacity send buffer, so row_map indexes rets.
+// Entry ret ((d, r), k) is owner d's weighted expert output for entry k of that row: the direct return of
+// lk_ep_p2p_experts, where the down kernel stores each entry's row straight into the home mailbox and the
+// home combine sums the entries in k order (the single-GPU combine's order).
 #include <cstring>
 #include "ep_device.cuh"
 
@@ -21,6 +25,7 @@ namespace lk {
 
 constexpr int P2P_HDR = 256;
 constexpr int P2P_THREADS = 256;
+constexpr int P2P_DIRECT_ROWS = 64;             // mailboxes of at most this many rows carry the entry rets
 
 struct P2PPeers {
     uint8_t* mb[LK_EP_MAX_RANKS];     // every rank's mailbox base, as mapped in this process
@@ -31,6 +36,9 @@ __device__ __forceinline__ uint32_t* mb_epoch(uint8_t* mb) { return (uint32_t*)m
 __device__ __forceinline__ uint8_t* mb_rows(uint8_t* mb) { return mb + P2P_HDR; }
 __device__ __forceinline__ float* mb_rets(uint8_t* mb, int n_ranks, int cap) {
     return (float*)(mb + P2P_HDR + (size_t)n_ranks * cap * LK_EP_ROW_BYTES);
+}
+__host__ __device__ __forceinline__ float* mb_erets(uint8_t* mb, int n_ranks, int cap) {
+    return (float*)(mb + P2P_HDR + (size_t)n_ranks * cap * LK_EP_ROW_BYTES) + (size_t)n_ranks * cap * HIDDEN;
 }
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
@@ -165,7 +173,7 @@ __global__ void k_p2p_combine(const uint8_t* mb, int n_ranks, int cap, const int
 // lk_ep_p2p_experts, first kernel: the rows wait of k_p2p_wait (lanes s < n_ranks of warp 0; every thread has
 // read the old epoch before thread 0 advances it) fused with the single-token slot tables of the received rows
 __global__ void __launch_bounds__(EPS_THREADS) k_p2p_wait_slots(uint8_t* mb, int n_ranks, int cap, int keep, int n_experts,
-                                                                int* sel, float* w, SlotParams sp, int* err) {
+                                                                int* sel, float* w, SlotParams sp, EpYDst yd, int* err) {
     pdl_trigger();
     pdl_wait();
     const int tid = threadIdx.x;
@@ -181,7 +189,72 @@ __global__ void __launch_bounds__(EPS_THREADS) k_p2p_wait_slots(uint8_t* mb, int
     }
     __syncthreads();
     if (tid == 0) *mb_epoch(mb) = want;
-    ep_slots_dev(mb_rows(mb), n_ranks * cap, keep, n_experts, sel, w, sp);
+    ep_slots_dev(mb_rows(mb), n_ranks * cap, keep, n_experts, sel, w, sp, yd.ydst ? &yd : nullptr);
+}
+
+// the direct return's flags (one thread per home rank s): the down kernel that stored the entry rows has completed
+// (griddepcontrol.wait: its stores are performed and visible), so a system-scope release of this layer's epoch into
+// s's return flag `self` publishes them.  (The same release raised by the down kernel's last CTA, after a
+// system-scope fence in every CTA, measured ~2.5 us slower per layer.)
+__global__ void k_p2p_ret_flags(int n_ranks, int self, P2PPeers peers) {
+    pdl_trigger();
+    pdl_wait();
+    const int s = threadIdx.x;
+    if (s >= n_ranks) return;
+    const uint32_t epoch = *mb_epoch(peers.mb[self]);            // advanced by this layer's rows wait
+    __threadfence_system();
+    st_release_sys(mb_flags(peers.mb[s], 1) + self, epoch);
+}
+
+// the home combine of the direct return (one token per CTA of 64 threads, 28 CTAs per token): before the wait,
+// threads s < n_ranks poll owner s's flag (bounded) while warp 1 resolves the CTA's token's entries -- the owner d
+// of sel[t][k] stored its row at entry ret (row_map[t][d], k) -- and every thread loads its resid and shared
+// values; after it, moe = the entries summed in k order and h = resid + shared + moe (the single-GPU order)
+constexpr int P2PC_THREADS = 64;
+__global__ void __launch_bounds__(P2PC_THREADS) k_p2p_combine_k(const uint8_t* mb, int n_ranks, int cap, const int* __restrict__ sel,
+                                                                int keep, const int* __restrict__ row_map, int T,
+                                                                const float* __restrict__ hpart, const float* __restrict__ shared,
+                                                                float* h, float* moe, int* err) {
+    __shared__ int eoff[MAX_TOPK];
+    pdl_trigger();
+    pdl_wait();
+    const int tid = threadIdx.x;
+    const int i = blockIdx.x * P2PC_THREADS + tid;                   // float4 index over T x HIDDEN
+    const int t = (blockIdx.x * P2PC_THREADS) / (HIDDEN / 4), c = i % (HIDDEN / 4);   // HIDDEN / 4 = 28 CTAs
+    if (tid < n_ranks) {
+        const uint32_t want = *mb_epoch((uint8_t*)mb);
+        const uint32_t* f = mb_flags((uint8_t*)mb, 1) + tid;
+        if ((int)(ld_acquire_sys(f) - want) < 0) {
+            const unsigned long long t0 = globaltimer_ns();
+            while ((int)(ld_acquire_sys(f) - want) < 0) {
+                if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) { if (err) atomicCAS(err, 0, DEV_ERR_TIMEOUT_EMPTY); break; }
+            }
+        }
+    } else if (tid >= 32 && tid < 32 + MAX_TOPK) {
+        const int k = tid - 32;
+        const int e = k < keep ? sel[t * keep + k] : -1;
+        const int row = e >= 0 && e < N_EXPERTS ? row_map[(size_t)t * n_ranks + e / (N_EXPERTS / n_ranks)] : -1;
+        eoff[k] = row;
+    }
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 b0 = h && hpart ? ((const float4*)(hpart + (size_t)t * HIDDEN))[c] : zero;
+    const float4 b1 = h && hpart && shared ? ((const float4*)(shared + (size_t)t * HIDDEN))[c] : zero;
+    __syncthreads();
+    const float* eret = mb_erets((uint8_t*)mb, n_ranks, cap);
+    float4 v[MAX_TOPK];
+    #pragma unroll
+    for (int k = 0; k < MAX_TOPK; ++k)                                // every load before any sum
+        v[k] = eoff[k] >= 0 ? ((const float4*)(eret + ((size_t)eoff[k] * MAX_TOPK + k) * HIDDEN))[c] : zero;
+    float4 r = zero;
+    #pragma unroll
+    for (int k = 0; k < MAX_TOPK; ++k)
+        if (eoff[k] >= 0) { r.x += v[k].x; r.y += v[k].y; r.z += v[k].z; r.w += v[k].w; }
+    if (moe) ((float4*)(moe + (size_t)t * HIDDEN))[c] = r;
+    if (h && hpart) {
+        float4 b = b0;
+        if (shared) { b.x += b1.x; b.y += b1.y; b.z += b1.z; b.w += b1.w; }
+        ((float4*)(h + (size_t)t * HIDDEN))[c] = make_float4(b.x + r.x, b.y + r.y, b.z + r.z, b.w + r.w);
+    }
 }
 
 }  // namespace lk
@@ -196,8 +269,11 @@ struct LkEpMailbox {
     bool opened[LK_EP_MAX_RANKS] = {};
 };
 
+static bool has_erets(int n_ranks, int cap) { return n_ranks * cap <= P2P_DIRECT_ROWS; }
 static size_t mailbox_bytes(int n_ranks, int cap) {
-    return (size_t)P2P_HDR + (size_t)n_ranks * cap * LK_EP_ROW_BYTES + (size_t)n_ranks * cap * HIDDEN * sizeof(float);
+    const size_t rows = (size_t)n_ranks * cap;
+    return (size_t)P2P_HDR + rows * LK_EP_ROW_BYTES + rows * HIDDEN * sizeof(float) +
+           (has_erets(n_ranks, cap) ? rows * MAX_TOPK * HIDDEN * sizeof(float) : 0);
 }
 
 extern "C" {
@@ -283,6 +359,16 @@ int lk_ep_p2p_combine(LkEpMailbox* m, const int* row_map, int T, const float* re
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 
+int lk_ep_p2p_combine_entries(LkEpMailbox* m, const int* sel, int keep, const int* row_map, int T, const float* resid,
+                              const float* shared, float* h, float* moe, int* err, lk_stream_t stream) {
+    if (!m || T < 1 || T > m->cap || !sel || keep < 1 || keep > MAX_TOPK || !row_map) return LK_ERR_ARG;
+    if (!has_erets(m->n_ranks, m->cap)) return LK_ERR_UNSUPPORTED;
+    static_assert((HIDDEN / 4) % P2PC_THREADS == 0, "a combine CTA covers one token");
+    launch_pdl_n(k_p2p_combine_k, dim3(T * (HIDDEN / 4) / P2PC_THREADS), dim3(P2PC_THREADS), 0, (cudaStream_t)stream, (const uint8_t*)m->local,
+                 m->n_ranks, m->cap, sel, keep, row_map, T, resid, shared, h, moe, err);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
 }  // extern "C"
 
 namespace lk {
@@ -291,11 +377,25 @@ int p2p_rows_count(const LkEpMailbox* m) { return m->n_ranks * m->cap; }
 int p2p_rank(const LkEpMailbox* m) { return m->rank; }
 int p2p_cap(const LkEpMailbox* m) { return m->cap; }
 
+bool p2p_direct_ok(const LkEpMailbox* m) { return has_erets(m->n_ranks, m->cap); }
+
 int p2p_wait_slots(LkEpMailbox* m, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, int* err,
-                   cudaStream_t st, const uint8_t** rows) {
+                   cudaStream_t st, const uint8_t** rows, float** ydst, float* shared_out) {
     for (int r = 0; r < m->n_ranks; ++r) if (!m->peers.mb[r]) return LK_ERR_ARG;   // not connected
+    EpYDst yd{};
+    if (ydst) {
+        if (!has_erets(m->n_ranks, m->cap)) return LK_ERR_UNSUPPORTED;
+        for (int r = 0; r < m->n_ranks; ++r) yd.ret[r] = mb_erets(m->peers.mb[r], m->n_ranks, m->cap);
+        yd.self = m->rank; yd.cap = m->cap; yd.shared_out = shared_out; yd.ydst = ydst;
+    }
     *rows = m->local + P2P_HDR;
-    launch_pdl_n(k_p2p_wait_slots, dim3(1), dim3(EPS_THREADS), 0, st, m->local, m->n_ranks, m->cap, keep, n_experts, sel, w, sp, err);
+    launch_pdl_n(k_p2p_wait_slots, dim3(1), dim3(EPS_THREADS), 0, st, m->local, m->n_ranks, m->cap, keep, n_experts, sel, w, sp,
+                 yd, err);
+    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+int p2p_ret_flags(LkEpMailbox* m, cudaStream_t st) {
+    launch_pdl_n(k_p2p_ret_flags, dim3(1), dim3(32), 0, st, m->n_ranks, m->rank, m->peers);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 

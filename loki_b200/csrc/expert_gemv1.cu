@@ -294,10 +294,12 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
     uint32_t xr[2][8]; float dx[2] = {0.0f, 0.0f};
     int xslot = -1, out = -1;
     float wv = 0.0f;
+    float* yrow = nullptr;
     for (int j = grp; j < nu; j += D1_GROUPS) {
         const int u = u0 + j, s = u / D1_UNITS_PER_SLOT, cu = u % D1_UNITS_PER_SLOT;
         if (s != xslot) {                             // this slot's h (q8) as the activations
             xslot = s; out = p.slot_out[s]; wv = p.slot_w[s];
+            yrow = out < 0 ? nullptr : (p.ydst ? p.ydst[s] : p.y + (size_t)out * HIDDEN);
             #pragma unroll
             for (int q = 0; q < 2; ++q) {
                 const int g = lane + 32 * q;
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(D1_THREADS, 1) k_down1(ExpertParams p) {
         if (lane == 0) mbar_arrive(&empty[st]);
         const float sum = warp_reduce8(v, lane);   // lane l: row (l >> 2), 4 replicas
         const int row0 = cu * D1_CROWS + sub * D1_UROWS;
-        if ((lane & 3) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 2)] = wv * (sum * 0.125f);
+        if ((lane & 3) == 0 && yrow) yrow[row0 + (lane >> 2)] = wv * (sum * 0.125f);
         if (*abort_flag) break;
     }
 }

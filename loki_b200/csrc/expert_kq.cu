@@ -216,10 +216,12 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
     uint32_t xr[16]; float dx[2] = {0.0f, 0.0f}; int xs[4] = {0, 0, 0, 0};
     int xslot = -1, out = -1;
     float wv = 0.0f;
+    float* yrow = nullptr;
     for (int j = grp; j < nu; j += KQ_GROUPS) {
         const int u = u0 + j, s = u / UPS, cu = u % UPS;
         if (s != xslot) {                             // this slot's h (q8): K [256b + 64q, +64)
             xslot = s; out = sh_only ? p.sh_row0 + s : p.slot_out[s]; wv = sh_only ? 1.0f : p.slot_w[s];
+            yrow = out < 0 ? nullptr : (p.ydst && !sh_only ? p.ydst[s] : p.y + (size_t)out * HIDDEN);
             if (out >= 0) {
                 const uint4* src = (const uint4*)(p.hq + (size_t)out * MOE_INTER + b * QK + 64 * q);
                 #pragma unroll
@@ -250,10 +252,10 @@ __global__ void __launch_bounds__(KQ_THREADS, 1) k_down1_kq(ExpertParams p) {
         const int row0 = cu * UROWS + sub * WROWS;
         if constexpr (WROWS == 8) {
             const float sum = warp_reduce8(*reinterpret_cast<float(*)[8]>(v), lane);   // lane l: row l >> 2, 4 replicas
-            if ((lane & 3) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 2)] = wv * sum;
+            if ((lane & 3) == 0 && yrow) yrow[row0 + (lane >> 2)] = wv * sum;
         } else {
             const float sum = warp_reduce4(*reinterpret_cast<float(*)[4]>(v), lane);   // lane l: row l >> 3, 8 replicas
-            if ((lane & 7) == 0 && out >= 0) p.y[(size_t)out * HIDDEN + row0 + (lane >> 3)] = wv * sum;
+            if ((lane & 7) == 0 && yrow) yrow[row0 + (lane >> 3)] = wv * sum;
         }
         if (*abort_flag) break;
     }

@@ -46,6 +46,8 @@ struct LkMoeCtx {
     float* ep_x = nullptr;            // lk_ep_experts: the received rows' activations, dequantised (on first use)
     const uint8_t* ep_rows = nullptr; // lk_ep_experts on the single-token path: the rows themselves (their q8 codes)
     float* ep_shared_out = nullptr;   // lk_ep_experts: where the combine copies the shared expert's rows
+    float** ydst = nullptr;           // [max_slots] lk_ep_p2p_experts: each slot's output row (the direct return)
+    bool ydst_on = false;             // set while lk_ep_p2p_experts' expert kernels run
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     char msg[256] = {0};
 };
@@ -125,7 +127,7 @@ int lk_moe_create(const LkMoeConfig* cfg, int device, LkMoeCtx** out) {
     LK_CU(dalloc(&c->counts, NE)); LK_CU(dalloc(&c->offsets, NE + 1)); LK_CU(dalloc(&c->perm, (size_t)T * KE));
     LK_CU(dalloc(&c->slot_expert, c->max_slots)); LK_CU(dalloc(&c->slot_tok, (size_t)c->max_slots * MAX_NT));
     LK_CU(dalloc(&c->slot_out, (size_t)c->max_slots * MAX_NT)); LK_CU(dalloc(&c->slot_w, (size_t)c->max_slots * MAX_NT));
-    LK_CU(dalloc(&c->nslots, 1));
+    LK_CU(dalloc(&c->nslots, 1)); LK_CU(dalloc(&c->ydst, c->max_slots));
     LK_CU(dalloc(&c->hq, rows * MOE_INTER)); LK_CU(dalloc(&c->hd, rows * (MOE_INTER / 32)));
     LK_CU(dalloc(&c->y, rows * HIDDEN));
     LK_CU(dalloc(&c->err, 1));
@@ -160,7 +162,8 @@ void lk_moe_destroy(LkMoeCtx* c) {
     void* ptrs[] = { c->logits, c->probs, c->sel, c->w, c->counts, c->offsets, c->perm, c->slot_expert, c->slot_tok,
                      c->slot_out, c->slot_w, c->nslots, c->hq, c->hd, c->y, c->err, c->tile_count, c->xq, c->xqn, c->xd,
                      c->g_expert, c->g_tok, c->g_out, c->g_w, c->g_n, c->bt, c->ht, c->g_cnt,
-                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->hb, c->ep_x, c->shgu, c->shpair };
+                     c->m_expert, c->m_tok, c->m_out, c->m_w, c->m_n, c->m_cnt, c->hb, c->ep_x, c->shgu, c->shpair,
+                     c->ydst };
     for (void* p : ptrs) if (p) cudaFree(p);
     void* gp[] = { c->shw16, c->shx16, c->shh16 };
     for (void* p : gp) if (p) cudaFree(p);
@@ -244,6 +247,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
     e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err; e.down_fmt = W->down_fmt;
     if (c->xq_ready && x == c->xq_src) { e.xq = c->xq; e.xqn = c->xqn; e.xd = c->xd; }
     e.xrows = c->ep_rows;
+    if (c->ydst_on) e.ydst = c->ydst;
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
     if (c->ev[1]) LK_CU(record_event(c->ev[1], st));
@@ -457,16 +461,16 @@ int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int
     return rc;
 }
 
-int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* c, const LkMoeWeights* W, int keep, int T, float* partial, float* shared_out,
-                      int* err, lk_stream_t stream) {
-    if (!mb || !c || !W || keep < 1 || T < 0 || !partial || (T > 0 && !shared_out)) return set_err(c, LK_ERR_ARG, "bad argument");
+int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* c, const LkMoeWeights* W, int keep, int T, float* shared_out, int* err,
+                      lk_stream_t stream) {
+    if (!mb || !c || !W || keep < 1 || T < 0 || (T > 0 && !shared_out)) return set_err(c, LK_ERR_ARG, "bad argument");
     const int R = p2p_rows_count(mb), cap = p2p_cap(mb), rank = p2p_rank(mb);
     if (T > cap) return set_err(c, LK_ERR_ARG, "T=%d above the mailbox capacity %d", T, cap);
     if (R > c->cfg.max_tokens || keep > c->cfg.keep) return set_err(c, LK_ERR_CAPACITY, "R=%d keep=%d above capacity", R, keep);
     if (T > 0 && !c->cfg.with_shared) return set_err(c, LK_ERR_ARG, "shared rows need a with_shared context");
     int rc = check_weights(c, W, false);
     if (rc) return rc;
-    if (!(R < c->mma_min_tokens && (c->rs || !c->cfg.with_shared)))
+    if (!(R < c->mma_min_tokens && (c->rs || !c->cfg.with_shared)) || !p2p_direct_ok(mb))
         return set_err(c, LK_ERR_UNSUPPORTED, "the fused exchange serves the single-token path (R=%d rows)", R);
     cudaStream_t st = (cudaStream_t)stream;
     c->sh_t0 = rank * cap; c->sh_n = T > 0 ? T : -1;
@@ -475,14 +479,17 @@ int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* c, const LkMoeWeights* W, int k
     sp.nslots = c->nslots; sp.max_slots = c->max_slots; sp.err = c->err; sp.with_shared = c->rs;
     sp.sh_t0 = c->sh_t0; sp.sh_n = c->sh_n;
     const uint8_t* rows = nullptr;
-    rc = p2p_wait_slots(mb, keep, c->cfg.n_experts, c->sel, c->w, sp, err, st, &rows);
+    // the slot tables carry each slot's destination row: the down kernel stores the routed entries' rows straight
+    // into their home ranks' mailboxes and the shared rows into shared_out; one small kernel then publishes the
+    // return flags (no combine or copy)
+    rc = p2p_wait_slots(mb, keep, c->cfg.n_experts, c->sel, c->w, sp, err, st, &rows, c->ydst, T > 0 ? shared_out : nullptr);
     if (rc == LK_OK) {
         c->ep_rows = rows;
-        c->ep_shared_out = T > 0 ? shared_out : nullptr;
-        rc = run_experts(c, W, nullptr, HIDDEN, nullptr, R, keep, c->sel, nullptr, partial, 1, st);
-        if (rc == LK_OK) rc = lk_ep_p2p_return(mb, partial, stream);
+        c->ydst_on = true;
+        rc = run_experts(c, W, nullptr, HIDDEN, nullptr, R, keep, c->sel, nullptr, nullptr, 1, st);
+        if (rc == LK_OK) rc = p2p_ret_flags(mb, st);
     }
-    c->sh_t0 = 0; c->sh_n = 0; c->ep_rows = nullptr; c->ep_shared_out = nullptr;
+    c->sh_t0 = 0; c->sh_n = 0; c->ep_rows = nullptr; c->ydst_on = false;
     return rc ? set_err(c, rc, "fused peer exchange: launch failed") : LK_OK;
 }
 

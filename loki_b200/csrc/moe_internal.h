@@ -89,6 +89,9 @@ struct ExpertParams {
     const uint8_t* xrows;
     int8_t* hq; float* hd;                            // SwiGLU output q8: [rows][MOE_INTER], scales [rows][MOE_INTER/32]
     float* y;                                         // weighted expert outputs [rows][HIDDEN]
+    // optional (single-token downs): slot s writes its weighted output row to ydst[s] instead of y row
+    // slot_out[s] (the expert-parallel direct return: rows in the home rank's mailbox, over NVLink)
+    float* const* ydst;
     int* err;
     int down_fmt;                                     // FMT_IQ2 (default, 0 reads as IQ2), FMT_Q2K or FMT_Q3K: every down matrix
     // shared-only launches of launch_down1_kq (slot_expert == null): sh_count single-token slots, slot j
@@ -201,8 +204,14 @@ namespace lk {
 int p2p_rows_count(const LkEpMailbox* m);
 int p2p_rank(const LkEpMailbox* m);
 int p2p_cap(const LkEpMailbox* m);
+// ydst (with shared_out): also the slots' destination rows for the direct return -- a routed entry's row in its
+// home rank's mailbox, a shared slot's row of shared_out; null: none
 int p2p_wait_slots(LkEpMailbox* m, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, int* err,
-                   cudaStream_t st, const uint8_t** rows);
+                   cudaStream_t st, const uint8_t** rows, float** ydst = nullptr, float* shared_out = nullptr);
+bool p2p_direct_ok(const LkEpMailbox* m);
+// the direct return's flags: once the down kernel (the previous launch) has stored every entry row, this layer's
+// epoch into every home rank's return flag of this rank
+int p2p_ret_flags(LkEpMailbox* m, cudaStream_t st);
 
 // ---- expert-parallel row plan only: counts [n_ranks], row_map [T][n_ranks] (and, with `send`, the
 //      headers of unused fixed-capacity rows)

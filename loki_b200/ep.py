@@ -178,21 +178,22 @@ class NativeEpOps:
         check(lib().lk_ep_p2p_dispatch(p2p.mb, _ptr(sel), _ptr(w), _ptr(x), T, keep, _ptr(row_map), _ptr(self.err),
                                        _stream()))
         shared = torch.empty(max(T, 1), HIDDEN, device=self.device)
-        partial = torch.empty(NR * p2p.cap, HIDDEN, device=self.device)
         ws = W.struct()
-        rc = lib().lk_ep_p2p_experts(p2p.mb, self.expert.ctx, ctypes.byref(ws), keep, T, _ptr(partial), _ptr(shared),
-                                     _ptr(self.err), _stream())
+        rc = lib().lk_ep_p2p_experts(p2p.mb, self.expert.ctx, ctypes.byref(ws), keep, T, _ptr(shared), _ptr(self.err),
+                                     _stream())
+        h = torch.empty(T, HIDDEN, device=self.device)
+        moe = torch.empty(T, HIDDEN, device=self.device)
         if rc == N.LK_ERR_UNSUPPORTED:                 # a batch-sized or K-quant-shared expert stage: separate calls
             rows = ctypes.c_void_p()
             check(lib().lk_ep_p2p_rows(p2p.mb, ctypes.byref(rows), _ptr(self.err), _stream()))
             partial, shared = self.experts(W, rows, NR * p2p.cap, keep, p2p.rank * p2p.cap, T)
             check(lib().lk_ep_p2p_return(p2p.mb, _ptr(partial), _stream()))
-        else:
+            check(lib().lk_ep_p2p_combine(p2p.mb, _ptr(row_map), T, _ptr(resid), _ptr(shared), _ptr(h), _ptr(moe),
+                                          _ptr(self.err), _stream()))
+        else:                                          # the direct return: entry rows in this rank's mailbox
             self.expert._check(rc)
-        h = torch.empty(T, HIDDEN, device=self.device)
-        moe = torch.empty(T, HIDDEN, device=self.device)
-        check(lib().lk_ep_p2p_combine(p2p.mb, _ptr(row_map), T, _ptr(resid), _ptr(shared), _ptr(h), _ptr(moe),
-                                      _ptr(self.err), _stream()))
+            check(lib().lk_ep_p2p_combine_entries(p2p.mb, _ptr(sel), keep, _ptr(row_map), T, _ptr(resid), _ptr(shared),
+                                                  _ptr(h), _ptr(moe), _ptr(self.err), _stream()))
         return h, moe
 
     def combine(self, ret_home, row_map, hpart, shared=None):

@@ -90,7 +90,8 @@ SIGNATURES = {
     "lk_ep_p2p_rows": (_I, [_P, ctypes.POINTER(_P), _P, _P]),
     "lk_ep_p2p_return": (_I, [_P, _P, _P]),
     "lk_ep_p2p_combine": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P]),
-    "lk_ep_p2p_experts": (_I, [_P, _P, _P, _I, _I, _P, _P, _P, _P]),
+    "lk_ep_p2p_experts": (_I, [_P, _P, _P, _I, _I, _P, _P, _P]),
+    "lk_ep_p2p_combine_entries": (_I, [_P, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
     "fl_init": (_P, [_I, _I]),
     "fl_wide_init": (_I, [_P, _I, _I]),
     "fl_wide_moe": (None, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _I, _I, _I]),

@@ -240,8 +240,16 @@ def _one_rank_worker(rank, port, T_loc, out_dir):
         p2p.close()
         comm.close()
         ops.device_error()
+        extra = {}
+        if T_loc == 1:                                              # the single-GPU forward on the same layer
+            from loki_b200.moe import MoeLayer
+            one = MoeLayer(0, max_tokens=1)
+            h1, moe1, _, _ = one.forward(W, x, r)
+            torch.cuda.synchronize()
+            extra = {"h1": h1.cpu().numpy(), "moe1": moe1.cpu().numpy()}
+            one.close()
         np.savez(os.path.join(out_dir, "r0.npz"), h=h.cpu().numpy(), moe=moe.cpu().numpy(), sel=sel.cpu().numpy(),
-                 w=w.cpu().numpy(), Wr=W.router_w.float().cpu().numpy(), b=W.router_bias.cpu().numpy())
+                 w=w.cpu().numpy(), Wr=W.router_w.float().cpu().numpy(), b=W.router_bias.cpu().numpy(), **extra)
     finally:
         dist.destroy_process_group()
 
@@ -250,8 +258,10 @@ def _one_rank_worker(rank, port, T_loc, out_dir):
 def test_ep_p2p_one_rank(native, oracle, tmp_path, T_loc):
     """The peer-memory exchange with a single rank (every expert local, the rows sent to itself) on one GPU:
     dispatch, the fused lk_ep_p2p_experts (rows wait + slot tables, the expert kernels reading the rows' q8
-    codes, partial sums stored into the home mailbox + flags) and the waiting combine, three layers in a row;
-    routing bit-exact and h / moe within RTOL_L2 of the oracle."""
+    codes, the down kernel storing each entry's row into the home mailbox, the return flags) and the waiting
+    combine, three layers in a row; routing bit-exact and h / moe within RTOL_L2 of the oracle.  At one token
+    the exchange runs the single-GPU kernels on the same q8 codes and sums in the same order, so h and moe
+    equal lk_moe_forward's bit for bit."""
     import torch.multiprocessing as mp
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -267,3 +277,6 @@ def test_ep_p2p_one_rank(native, oracle, tmp_path, T_loc):
     ref = oracle_layer(oracle, SEED, 0, x, r, osel, ow)
     assert rel_l2(got["moe"], ref["moe"]) < RTOL_L2
     assert rel_l2(got["h"], ref["h"]) < RTOL_L2
+    if T_loc == 1:
+        np.testing.assert_array_equal(got["moe"], got["moe1"])
+        np.testing.assert_array_equal(got["h"], got["h1"])
