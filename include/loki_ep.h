@@ -91,7 +91,8 @@ LK_API int lk_ep_all_to_all(LkEpComm* comm, const void* send, void* recv, const 
  *   lk_ep_experts(rows, n_ranks*cap, ..., own rows rank*cap .. +T, partial, shared)
  *   lk_ep_p2p_return(partial)  (each block of cap partial sums to its home rank)
  *   lk_ep_p2p_combine (wait for all returns; h = resid + shared + sum, moe = sum)
- * or, for the single-token expert path (n_ranks*cap rows below the context's mma threshold and at most 64, an
+ * (with one token, lk_ep_p2p_route_dispatch does the routing and the dispatch in the router's launch), or, for
+ * the single-token expert path (n_ranks*cap rows below the context's mma threshold and at most 64, an
  * IQ2_XXS or no shared expert: decode), the direct return:
  *   lk_ep_p2p_experts(mb, ctx, W, keep, T, shared, err)  (the rows wait fused with the slot tables, the expert
  *     kernels reading the rows' q8 codes, the down kernel storing each entry's weighted row straight into its
@@ -116,6 +117,13 @@ LK_API int lk_ep_p2p_combine(LkEpMailbox* mb, const int* row_map, int T, const f
  * expert of this rank's own T rows.  Pair it with lk_ep_p2p_combine_entries. */
 LK_API int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* ctx, const LkMoeWeights* W, int keep, int T, float* shared,
                              int* err, lk_stream_t stream);
+/* no reference counterpart: lk_moe_route + lk_ep_p2p_dispatch for one token (T == 1, else LK_ERR_UNSUPPORTED)
+ * as one launch -- the router's last CTA, after its top-k, stores the token's row (the router's q8 of x) into
+ * every rank's mailbox and publishes the flags.  ctx: the home (256-expert) context; sel/w [1][keep] and
+ * row_map [1][n_ranks] out, as the two calls give them. */
+LK_API int lk_ep_p2p_route_dispatch(LkEpMailbox* mb, LkMoeCtx* ctx, const LkMoeWeights* W, const float* x, int T,
+                                    const float* logits_override, int* sel, float* w, int* row_map, int* err,
+                                    lk_stream_t stream);
 /* no reference counterpart: the home combine of lk_ep_p2p_experts' direct return; sel [T][keep] the routing
  * passed to lk_ep_p2p_dispatch (global ids, negative = absent), row_map its output */
 LK_API int lk_ep_p2p_combine_entries(LkEpMailbox* mb, const int* sel, int keep, const int* row_map, int T,

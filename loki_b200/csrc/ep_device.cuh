@@ -12,6 +12,76 @@ static_assert(sizeof(EpRowHdr) == LK_EP_ROW_HDR_BYTES, "header size");
 
 constexpr int EPS_THREADS = 256;
 
+// ---- the peer-exchange mailbox (ep_p2p.cu): [flags: 2 x LK_EP_MAX_RANKS u32, epoch u32, pad to P2P_HDR]
+// [rows: n_ranks x cap x LK_EP_ROW_BYTES] [rets: n_ranks x cap x 7168 fp32] [entry rets (direct return), when
+// n_ranks x cap <= P2P_DIRECT_ROWS: n_ranks x cap x 8 x 7168 fp32]
+constexpr int P2P_HDR = 256;
+constexpr int P2P_DIRECT_ROWS = 64;             // mailboxes of at most this many rows carry the entry rets
+
+struct P2PPeers {
+    uint8_t* mb[LK_EP_MAX_RANKS];     // every rank's mailbox base, as mapped in this process
+};
+
+__device__ __forceinline__ uint32_t* mb_flags(uint8_t* mb, int which) { return (uint32_t*)mb + which * LK_EP_MAX_RANKS; }
+__device__ __forceinline__ uint32_t* mb_epoch(uint8_t* mb) { return (uint32_t*)mb + 2 * LK_EP_MAX_RANKS; }
+__device__ __forceinline__ uint8_t* mb_rows(uint8_t* mb) { return mb + P2P_HDR; }
+__device__ __forceinline__ float* mb_rets(uint8_t* mb, int n_ranks, int cap) {
+    return (float*)(mb + P2P_HDR + (size_t)n_ranks * cap * LK_EP_ROW_BYTES);
+}
+__host__ __device__ __forceinline__ float* mb_erets(uint8_t* mb, int n_ranks, int cap) {
+    return (float*)(mb + P2P_HDR + (size_t)n_ranks * cap * LK_EP_ROW_BYTES) + (size_t)n_ranks * cap * HIDDEN;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v; asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory"); return v;
+}
+
+// the router's send for one token (EpSendParams, moe_internal.h), by all threads of the router's last CTA after
+// its top-k (sel, w: the token's [keep] entries; xq, xd: its q8 codes and scales): for every rank d the token's
+// row in d's mailbox block `self` -- row 0, when the token has an entry on d or d is this rank (its shared
+// expert), with the header of d's entries (local ids) and the codes, else an empty header; rows 1 .. cap-1
+// empty -- and row_map[d] (d * cap or -1); then each rank's rows flag gets this layer's epoch + 1 (as
+// k_p2p_send)
+__device__ __forceinline__ void ep_send_token(const EpSendParams& sp, const int* sel, const float* w, int keep,
+                                              const int8_t* xq, const float* xd) {
+    const int tid = threadIdx.x;
+    const int epr = N_EXPERTS / sp.n_ranks;
+    int es[MAX_TOPK];
+    #pragma unroll
+    for (int k = 0; k < MAX_TOPK; ++k) es[k] = k < keep ? sel[k] : -1;
+    const uint32_t epoch = *mb_epoch(sp.mb[sp.self]) + 1u;
+    for (int d = 0; d < sp.n_ranks; ++d) {
+        bool has = d == sp.self;
+        #pragma unroll
+        for (int k = 0; k < MAX_TOPK; ++k) has = has || (es[k] >= d * epr && es[k] < (d + 1) * epr);
+        uint8_t* block = mb_rows(sp.mb[d]) + (size_t)sp.self * sp.cap * LK_EP_ROW_BYTES;
+        if (tid == 0) sp.row_map[d] = has ? d * sp.cap : -1;
+        if (has) {
+            if (tid < 16) {
+                const int k = tid & 7, e = es[k];
+                const bool mine = e >= d * epr && e < (d + 1) * epr;
+                if (tid < 8) ((int*)block)[tid] = mine ? e - d * epr : -1;
+                else ((float*)block)[tid] = mine ? w[k] : 0.f;
+            }
+            if (tid < HIDDEN / 32) {
+                const uint4* src = (const uint4*)(xq + tid * 32);
+                uint4* dst = (uint4*)(block + LK_EP_ROW_Q_OFF + tid * 32);
+                dst[0] = src[0]; dst[1] = src[1];
+                ((float*)(block + LK_EP_ROW_D_OFF))[tid] = xd[tid];
+            }
+        }
+        for (int rr = has ? 1 : 0; rr < sp.cap; ++rr)
+            if (tid < 16) ((int*)(block + (size_t)rr * LK_EP_ROW_BYTES))[tid] = tid < 8 ? -1 : 0;
+    }
+    __syncthreads();
+    if (tid < sp.n_ranks) {
+        __threadfence_system();
+        st_release_sys(mb_flags(sp.mb[tid], 0) + sp.self, epoch);
+    }
+}
+
 // the direct return's destinations: entry (row i / keep, k = i % keep) of received row (source s = row / cap,
 // r = row % cap) goes to ret[s] + ((self * cap + r) * MAX_TOPK + k) * HIDDEN -- its row in the home rank's
 // mailbox -- and shared slot j to shared_out + j * HIDDEN; ydst [max_slots] receives the row pointers

@@ -23,29 +23,7 @@
 
 namespace lk {
 
-constexpr int P2P_HDR = 256;
 constexpr int P2P_THREADS = 256;
-constexpr int P2P_DIRECT_ROWS = 64;             // mailboxes of at most this many rows carry the entry rets
-
-struct P2PPeers {
-    uint8_t* mb[LK_EP_MAX_RANKS];     // every rank's mailbox base, as mapped in this process
-};
-
-__device__ __forceinline__ uint32_t* mb_flags(uint8_t* mb, int which) { return (uint32_t*)mb + which * LK_EP_MAX_RANKS; }
-__device__ __forceinline__ uint32_t* mb_epoch(uint8_t* mb) { return (uint32_t*)mb + 2 * LK_EP_MAX_RANKS; }
-__device__ __forceinline__ uint8_t* mb_rows(uint8_t* mb) { return mb + P2P_HDR; }
-__device__ __forceinline__ float* mb_rets(uint8_t* mb, int n_ranks, int cap) {
-    return (float*)(mb + P2P_HDR + (size_t)n_ranks * cap * LK_EP_ROW_BYTES);
-}
-__host__ __device__ __forceinline__ float* mb_erets(uint8_t* mb, int n_ranks, int cap) {
-    return (float*)(mb + P2P_HDR + (size_t)n_ranks * cap * LK_EP_ROW_BYTES) + (size_t)n_ranks * cap * HIDDEN;
-}
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v; asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory"); return v;
-}
 
 // one CTA per destination rank d: this rank's rows for d (tokens with an entry on d, and every token to
 // itself) into d's mailbox block `self`, unused rows with empty headers, then the dispatch flag
@@ -392,6 +370,16 @@ int p2p_wait_slots(LkEpMailbox* m, int keep, int n_experts, int* sel, float* w, 
     launch_pdl_n(k_p2p_wait_slots, dim3(1), dim3(EPS_THREADS), 0, st, m->local, m->n_ranks, m->cap, keep, n_experts, sel, w, sp,
                  yd, err);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+}
+
+bool p2p_send_params(const LkEpMailbox* m, int* row_map, EpSendParams* out) {
+    *out = EpSendParams{};
+    for (int r = 0; r < m->n_ranks; ++r) {
+        if (!m->peers.mb[r]) return false;
+        out->mb[r] = m->peers.mb[r];
+    }
+    out->n_ranks = m->n_ranks; out->self = m->rank; out->cap = m->cap; out->row_map = row_map;
+    return true;
 }
 
 int p2p_ret_flags(LkEpMailbox* m, cudaStream_t st) {

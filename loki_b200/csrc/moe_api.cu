@@ -461,6 +461,21 @@ int lk_ep_experts(LkMoeCtx* c, const LkMoeWeights* W, const void* recv_rows, int
     return rc;
 }
 
+int lk_ep_p2p_route_dispatch(LkEpMailbox* mb, LkMoeCtx* c, const LkMoeWeights* W, const float* x, int T,
+                             const float* logits_override, int* sel, float* w, int* row_map, int* err, lk_stream_t stream) {
+    (void)err;                                        // the router's ids are in range by construction
+    if (!mb || !c || !x || !sel || !w || !row_map || T < 0) return set_err(c, LK_ERR_ARG, "null argument");
+    if (T != 1) return set_err(c, LK_ERR_UNSUPPORTED, "the router's send serves one token (T=%d)", T);
+    if (!W || !W->router_w || !W->router_bias) return set_err(c, LK_ERR_ARG, "router weights missing");
+    if (c->cfg.n_experts != N_EXPERTS) return set_err(c, LK_ERR_UNSUPPORTED, "the router needs a 256-expert context");
+    RouterParams p = router_params(c, W, x, T, logits_override, sel, w, false);
+    p.xq = c->xq; p.xqn = c->xqn; p.xd = c->xd;
+    if (!p2p_send_params(mb, row_map, &p.send)) return set_err(c, LK_ERR_ARG, "mailbox not connected");
+    launch_router(p, (cudaStream_t)stream);
+    LK_CU(cudaGetLastError());
+    return LK_OK;
+}
+
 int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* c, const LkMoeWeights* W, int keep, int T, float* shared_out, int* err,
                       lk_stream_t stream) {
     if (!mb || !c || !W || keep < 1 || T < 0 || (T > 0 && !shared_out)) return set_err(c, LK_ERR_ARG, "bad argument");

@@ -13,6 +13,15 @@ constexpr int GEMM_NT = 128;         // tokens per work slot of the tensor-core 
 constexpr int MM_NT = 16;            // tokens per work slot of the register-fed mma.sync products (mid-size T)
 
 // ---- router
+// optional, T == 1 (expert-parallel decode over the peer mailboxes, ep_p2p.cu): after the top-k, the router's last
+// CTA sends the token's row to every rank (include/loki_ep.h row format, the q8 of x from xq/xd), writes
+// row_map [n_ranks] and publishes every rank's rows flag; n_ranks = 0: no send
+struct EpSendParams {
+    uint8_t* mb[8];                         // every rank's mailbox base, as mapped in this process
+    int n_ranks, self, cap;
+    int* row_map;
+};
+
 struct RouterParams {
     const float* x; int T; int ld_x;        // activations [T][HIDDEN], row stride ld_x floats
     const void* W; int w_f16;               // router weights [n_experts][HIDDEN], fp32 or fp16
@@ -28,6 +37,7 @@ struct RouterParams {
     // optional, T == 1: the q8 of x for the expert kernels -- CTA e < HIDDEN/32 writes group e: int8 values
     // xq, their negations xqn (HIDDEN bytes each) and the scale xd[e] (quant_q8_group, bit for bit)
     int8_t* xq; int8_t* xqn; float* xd;
+    EpSendParams send;                      // optional, T == 1 (needs xq): the expert-parallel send
     int esplit;                             // set by launch_router: expert splits of the batch kernel
 };
 void launch_router(const RouterParams& p, cudaStream_t st);
@@ -212,6 +222,8 @@ bool p2p_direct_ok(const LkEpMailbox* m);
 // the direct return's flags: once the down kernel (the previous launch) has stored every entry row, this layer's
 // epoch into every home rank's return flag of this rank
 int p2p_ret_flags(LkEpMailbox* m, cudaStream_t st);
+// the router's send parameters for mailbox m (row_map [n_ranks] out); false: not connected
+bool p2p_send_params(const LkEpMailbox* m, int* row_map, EpSendParams* out);
 
 // ---- expert-parallel row plan only: counts [n_ranks], row_map [T][n_ranks] (and, with `send`, the
 //      headers of unused fixed-capacity rows)

@@ -22,6 +22,7 @@
 //   table (one slot per kept expert + the shared expert), so no dispatch kernel is needed at decode.
 #include "moe_internal.h"
 #include "moe_device.cuh"
+#include "ep_device.cuh"
 #include <cuda_fp16.h>
 
 namespace lk {
@@ -116,6 +117,9 @@ __global__ void __launch_bounds__(256) k_router_logits(RouterParams p) {
     else if (warp < nt) router_topk_token(p, t0 + warp, lane);
     __syncthreads();
     if (tid == 0) p.tile_count[blockIdx.y] = 0;       // ready for the next call
+    // expert-parallel decode: the token's rows to every rank (the other CTAs' q8 groups of x were acquired
+    // with the count; this CTA's sel / w are ordered before the barrier above)
+    if (NTT == 1 && p.send.n_ranks && p.xq) ep_send_token(p.send, p.sel + (size_t)t0 * p.keep, p.w + (size_t)t0 * p.keep, p.keep, p.xq, p.xd);
 }
 
 constexpr int RB_TT = 8;                          // tokens per CTA tile

@@ -171,12 +171,29 @@ class NativeEpOps:
                                                shared_rows, _ptr(ret), _ptr(shared), _stream()))
         return ret[:R], shared[:shared_rows]
 
-    def p2p_layer(self, p2p, W, x, resid, sel, w):
-        """One fixed-capacity layer over the peer-memory exchange (after routing): h, moe."""
+    def p2p_route_dispatch(self, p2p, W, x, logits_override=None):
+        """Routing and the peer-memory send as the router's one launch (one token): (sel, w, row_map), or None
+        where that path does not apply (then route + p2p_layer)."""
+        T = x.shape[0]
+        sel = torch.empty(T, self.home.keep, dtype=torch.int32, device=self.device)
+        w = torch.empty(T, self.home.keep, device=self.device)
+        row_map = torch.empty(T, self.n_ranks, dtype=torch.int32, device=self.device)
+        ws = W.struct()
+        rc = lib().lk_ep_p2p_route_dispatch(p2p.mb, self.home.ctx, ctypes.byref(ws), _ptr(x), T, _ptr(logits_override),
+                                            _ptr(sel), _ptr(w), _ptr(row_map), _ptr(self.err), _stream())
+        if rc == N.LK_ERR_UNSUPPORTED:
+            return None
+        self.home._check(rc)
+        return sel, w, row_map
+
+    def p2p_layer(self, p2p, W, x, resid, sel, w, row_map=None):
+        """One fixed-capacity layer over the peer-memory exchange (after routing; row_map given: after the
+        dispatch too): h, moe."""
         T, keep, NR = x.shape[0], sel.shape[1], self.n_ranks
-        row_map = torch.empty(T, NR, dtype=torch.int32, device=self.device)
-        check(lib().lk_ep_p2p_dispatch(p2p.mb, _ptr(sel), _ptr(w), _ptr(x), T, keep, _ptr(row_map), _ptr(self.err),
-                                       _stream()))
+        if row_map is None:
+            row_map = torch.empty(T, NR, dtype=torch.int32, device=self.device)
+            check(lib().lk_ep_p2p_dispatch(p2p.mb, _ptr(sel), _ptr(w), _ptr(x), T, keep, _ptr(row_map), _ptr(self.err),
+                                           _stream()))
         shared = torch.empty(max(T, 1), HIDDEN, device=self.device)
         ws = W.struct()
         rc = lib().lk_ep_p2p_experts(p2p.mb, self.expert.ctx, ctypes.byref(ws), keep, T, _ptr(shared), _ptr(self.err),
@@ -233,11 +250,17 @@ class EpMoeLayer:
         ops, comm, NR = self.ops, self.comm, self.n_ranks
         T = x.shape[0]
         me = comm.rank
+        if self.p2p is not None and T <= self.p2p.cap:
+            fused = ops.p2p_route_dispatch(self.p2p, W, x, logits_override) if T == 1 else None
+            if fused is not None:
+                sel, w, row_map = fused
+                h, moe = ops.p2p_layer(self.p2p, W, x, resid, sel, w, row_map)
+            else:
+                sel, w = ops.route(W, x, logits_override)
+                h, moe = ops.p2p_layer(self.p2p, W, x, resid, sel, w)
+            return h, moe, sel, w
         sel, w = ops.route(W, x, logits_override)
         keep = sel.shape[1]
-        if self.p2p is not None and T <= self.p2p.cap:
-            h, moe = ops.p2p_layer(self.p2p, W, x, resid, sel, w)
-            return h, moe, sel, w
         fixed = T <= self.fixed_cap_max
         cap = T if fixed else 0
         send, counts, row_map = ops.pack(sel, w, x, cap, me)

@@ -92,6 +92,7 @@ SIGNATURES = {
     "lk_ep_p2p_combine": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P]),
     "lk_ep_p2p_experts": (_I, [_P, _P, _P, _I, _I, _P, _P, _P]),
     "lk_ep_p2p_combine_entries": (_I, [_P, _P, _I, _P, _I, _P, _P, _P, _P, _P, _P]),
+    "lk_ep_p2p_route_dispatch": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _P]),
     "fl_init": (_P, [_I, _I]),
     "fl_wide_init": (_I, [_P, _I, _I]),
     "fl_wide_moe": (None, [_P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _I, _I, _I]),
