@@ -20,7 +20,7 @@ LIB = os.path.join(HERE, "libloki_moe.so")
 REPLAY_SRC = os.path.join(CSRC, "fl_replay.cpp")
 REPLAY_LIB = os.path.join(HERE, "libloki_replay.so")
 SOURCES = ["expert_gemv.cu", "expert_gemv1.cu", "aux_kernels.cu", "router.cu", "dispatch.cu", "prefill_gemm.cu", "gate_up_q8.cu", "moe_api.cu", "fl_abi.cu", "noalloc.cu", "ep.cu", "ep_comm.cu", "slot_mma.cu", "ep_p2p.cu", "expert_kq.cu", "shared_kq.cu", "shared_gemm.cu", "kq_mma.cu"]
-HEADERS = ["moe_format.h", "moe_device.cuh", "moe_internal.h", "tcgen05.cuh", "iq2_tc.cuh", "iq2_grid.inc",
+HEADERS = ["moe_format.h", "moe_device.cuh", "moe_internal.h", "ep_device.cuh", "tcgen05.cuh", "iq2_tc.cuh", "iq2_grid.inc",
            os.path.join("..", "..", "include", "loki_moe.h"), os.path.join("..", "..", "include", "loki_fused_moe.h"),
            os.path.join("..", "..", "include", "loki_ep.h")]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -68,8 +68,10 @@ def build(force=False, verbose=False, ptxas_verbose=False):
                 raise RuntimeError("nvcc failed on %s" % src)
     if force or _stale(LIB, objs):
         cuda_lib = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "lib64")
+        # --no-undefined: a symbol declared but defined nowhere fails the link instead of the first dlopen
         cmd = [nv, "-ccbin", host_cxx()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda", "-ldl",
-                                                                                "-Xlinker", "-rpath=" + cuda_lib]
+                                                                                "-Xlinker", "-rpath=" + cuda_lib,
+                                                                                "-Xlinker", "--no-undefined"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)

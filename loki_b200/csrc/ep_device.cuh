@@ -82,29 +82,24 @@ __device__ __forceinline__ void ep_send_token(const EpSendParams& sp, const int*
     }
 }
 
-// the direct return's destinations: entry (row i / keep, k = i % keep) of received row (source s = row / cap,
-// r = row % cap) goes to ret[s] + ((self * cap + r) * MAX_TOPK + k) * HIDDEN -- its row in the home rank's
-// mailbox -- and shared slot j to shared_out + j * HIDDEN; ydst [max_slots] receives the row pointers
-struct EpYDst {
-    float* ret[LK_EP_MAX_RANKS];
-    int self, cap;
-    float* shared_out;
-    float** ydst;
-};
+static_assert(LK_EP_MAX_RANKS == 8, "EpYDst / EpSendParams hold 8 ranks");
 
 // rows -> sel/w [R][keep] and the single-token slot tables of sp: one slot per live entry in (row, k) order,
 // then the shared expert's slots of rows [sh_t0, +sh_n) (sh_n < 0: none); ids outside [0, n_experts) are
 // reported (DEV_ERR_BAD_SLOT) and dropped.  Every slot writes its own output row, so the order of the slots
 // changes no result.  Called by all EPS_THREADS threads of one CTA.
+// NT: the CTA's thread count (every thread calls; the function synchronises the CTA).
+template <int NT = EPS_THREADS>
 __device__ __forceinline__ void ep_slots_dev(const uint8_t* __restrict__ recv, int R, int keep, int n_experts, int* sel,
                                              float* w, const SlotParams& sp, const EpYDst* yd = nullptr) {
-    __shared__ int wsum[EPS_THREADS / 32];
+    static_assert(NT % 32 == 0, "whole warps");
+    __shared__ int wsum[NT / 32];
     __shared__ int base;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int entries = R * keep;
     if (tid == 0) base = 0;
     __syncthreads();
-    for (int c0 = 0; c0 < entries; c0 += EPS_THREADS) {
+    for (int c0 = 0; c0 < entries; c0 += NT) {
         const int i = c0 + tid;
         int e = -1; float wv = 0.0f;
         if (i < entries) {
@@ -128,18 +123,41 @@ __device__ __forceinline__ void ep_slots_dev(const uint8_t* __restrict__ recv, i
             }
         }
         __syncthreads();
-        if (tid == 0) { int t = base; for (int k = 0; k < EPS_THREADS / 32; ++k) t += wsum[k]; base = t; }
+        if (tid == 0) { int t = base; for (int k = 0; k < NT / 32; ++k) t += wsum[k]; base = t; }
         __syncthreads();
     }
     const int nrs = base;
     const int nsh = !sp.with_shared || sp.sh_n < 0 ? 0 : (sp.sh_n > 0 ? sp.sh_n : R);
-    for (int j = tid; j < nsh; j += EPS_THREADS) {
+    for (int j = tid; j < nsh; j += NT) {
         const int s = nrs + j;
         if (s >= sp.max_slots) continue;
         sp.slot_expert[s] = SHARED_SLOT; sp.slot_tok[s] = sp.sh_t0 + j; sp.slot_out[s] = entries + j; sp.slot_w[s] = 1.0f;
         if (yd) yd->ydst[s] = yd->shared_out + (size_t)j * HIDDEN;
     }
     if (tid == 0) *sp.nslots = min(nrs + nsh, sp.max_slots);
+}
+
+// the expert-parallel rows wait fused into a single-token expert kernel (EpWait, moe_internal.h), by all NT threads
+// of each CTA after its griddepcontrol.wait: threads s < n_ranks wait (bounded) until source s's rows flag reaches
+// this layer's epoch + 1 (the epoch itself advances later, in the return flags kernel, once every CTA has read
+// it); then every CTA builds the same slot tables (and destination rows) from the received rows
+template <int NT>
+__device__ __forceinline__ void ep_rows_wait_slots(const EpWait& ew) {
+    const int tid = threadIdx.x;
+    if (tid < ew.n_ranks) {
+        const uint32_t want = *mb_epoch(ew.mb) + 1u;
+        const uint32_t* f = mb_flags(ew.mb, 0) + tid;
+        if ((int)(ld_acquire_sys(f) - want) < 0) {
+            const unsigned long long t0 = globaltimer_ns();
+            while ((int)(ld_acquire_sys(f) - want) < 0) {
+                if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) { if (ew.err) atomicCAS(ew.err, 0, DEV_ERR_TIMEOUT_FULL); break; }
+            }
+        }
+    }
+    __syncthreads();
+    ep_slots_dev<NT>(mb_rows(ew.mb), ew.n_ranks * ew.cap, ew.keep, ew.n_experts, ew.sel, ew.w, ew.sp,
+                     ew.yd.ydst ? &ew.yd : nullptr);
+    __syncthreads();
 }
 
 }  // namespace lk

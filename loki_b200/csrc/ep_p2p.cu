@@ -148,40 +148,23 @@ __global__ void k_p2p_combine(const uint8_t* mb, int n_ranks, int cap, const int
     }
 }
 
-// lk_ep_p2p_experts, first kernel: the rows wait of k_p2p_wait (lanes s < n_ranks of warp 0; every thread has
-// read the old epoch before thread 0 advances it) fused with the single-token slot tables of the received rows
-__global__ void __launch_bounds__(EPS_THREADS) k_p2p_wait_slots(uint8_t* mb, int n_ranks, int cap, int keep, int n_experts,
-                                                                int* sel, float* w, SlotParams sp, EpYDst yd, int* err) {
-    pdl_trigger();
-    pdl_wait();
-    const int tid = threadIdx.x;
-    const uint32_t want = *mb_epoch(mb) + 1u;
-    if (tid < n_ranks) {
-        const uint32_t* f = mb_flags(mb, 0) + tid;
-        if ((int)(ld_acquire_sys(f) - want) < 0) {
-            const unsigned long long t0 = globaltimer_ns();
-            while ((int)(ld_acquire_sys(f) - want) < 0) {
-                if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) { if (err) atomicCAS(err, 0, DEV_ERR_TIMEOUT_FULL); break; }
-            }
-        }
-    }
-    __syncthreads();
-    if (tid == 0) *mb_epoch(mb) = want;
-    ep_slots_dev(mb_rows(mb), n_ranks * cap, keep, n_experts, sel, w, sp, yd.ydst ? &yd : nullptr);
-}
-
 // the direct return's flags (one thread per home rank s): the down kernel that stored the entry rows has completed
-// (griddepcontrol.wait: its stores are performed and visible), so a system-scope release of this layer's epoch into
-// s's return flag `self` publishes them.  (The same release raised by the down kernel's last CTA, after a
-// system-scope fence in every CTA, measured ~2.5 us slower per layer.)
+// (griddepcontrol.wait: its stores are performed and visible), so a system-scope release of this layer's epoch + 1
+// into s's return flag `self` publishes them; then the local epoch advances (every lane has read it first).  The
+// single-token gate/up's rows wait read the epoch unadvanced.  (The same release raised by the down kernel's last
+// CTA, after a system-scope fence in every CTA, measured ~2.5 us slower per layer.)
 __global__ void k_p2p_ret_flags(int n_ranks, int self, P2PPeers peers) {
     pdl_trigger();
     pdl_wait();
     const int s = threadIdx.x;
-    if (s >= n_ranks) return;
-    const uint32_t epoch = *mb_epoch(peers.mb[self]);            // advanced by this layer's rows wait
-    __threadfence_system();
-    st_release_sys(mb_flags(peers.mb[s], 1) + self, epoch);
+    const uint32_t epoch = *mb_epoch(peers.mb[self]) + 1u;
+    __syncwarp();
+    if (s < n_ranks) {
+        __threadfence_system();
+        st_release_sys(mb_flags(peers.mb[s], 1) + self, epoch);
+    }
+    __syncwarp();
+    if (s == 0) *mb_epoch(peers.mb[self]) = epoch;
 }
 
 // the home combine of the direct return (one token per CTA of 64 threads, 28 CTAs per token): before the wait,
@@ -357,19 +340,20 @@ int p2p_cap(const LkEpMailbox* m) { return m->cap; }
 
 bool p2p_direct_ok(const LkEpMailbox* m) { return has_erets(m->n_ranks, m->cap); }
 
-int p2p_wait_slots(LkEpMailbox* m, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, int* err,
-                   cudaStream_t st, const uint8_t** rows, float** ydst, float* shared_out) {
+int p2p_rows_wait(LkEpMailbox* m, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, int* err,
+                  float** ydst, float* shared_out, EpWait* out, const uint8_t** rows) {
     for (int r = 0; r < m->n_ranks; ++r) if (!m->peers.mb[r]) return LK_ERR_ARG;   // not connected
-    EpYDst yd{};
+    EpWait ew{};
+    ew.mb = m->local; ew.n_ranks = m->n_ranks; ew.cap = m->cap; ew.keep = keep; ew.n_experts = n_experts;
+    ew.sel = sel; ew.w = w; ew.sp = sp; ew.err = err;
     if (ydst) {
         if (!has_erets(m->n_ranks, m->cap)) return LK_ERR_UNSUPPORTED;
-        for (int r = 0; r < m->n_ranks; ++r) yd.ret[r] = mb_erets(m->peers.mb[r], m->n_ranks, m->cap);
-        yd.self = m->rank; yd.cap = m->cap; yd.shared_out = shared_out; yd.ydst = ydst;
+        for (int r = 0; r < m->n_ranks; ++r) ew.yd.ret[r] = mb_erets(m->peers.mb[r], m->n_ranks, m->cap);
+        ew.yd.self = m->rank; ew.yd.cap = m->cap; ew.yd.shared_out = shared_out; ew.yd.ydst = ydst;
     }
+    *out = ew;
     *rows = m->local + P2P_HDR;
-    launch_pdl_n(k_p2p_wait_slots, dim3(1), dim3(EPS_THREADS), 0, st, m->local, m->n_ranks, m->cap, keep, n_experts, sel, w, sp,
-                 yd, err);
-    return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
+    return LK_OK;
 }
 
 bool p2p_send_params(const LkEpMailbox* m, int* row_map, EpSendParams* out) {

@@ -12,6 +12,7 @@
 #include "../../include/loki_ep.h"
 #include "moe_internal.h"
 #include "moe_device.cuh"
+#include "ep_device.cuh"
 
 namespace lk {
 
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) k_gate_up1(ExpertParams p) {
     __syncthreads();
     pdl_trigger();
     pdl_wait();
+    if (p.epw.mb) ep_rows_wait_slots<G1_THREADS>(p.epw);   // expert-parallel: the rows wait + slot tables, per CTA
     const int nslots = *p.nslots;
     const int ntiles = nslots * G1_TILES_PER_SLOT;
     const int t0 = (int)((long long)blockIdx.x * ntiles / gridDim.x);

@@ -47,7 +47,8 @@ struct LkMoeCtx {
     const uint8_t* ep_rows = nullptr; // lk_ep_experts on the single-token path: the rows themselves (their q8 codes)
     float* ep_shared_out = nullptr;   // lk_ep_experts: where the combine copies the shared expert's rows
     float** ydst = nullptr;           // [max_slots] lk_ep_p2p_experts: each slot's output row (the direct return)
-    bool ydst_on = false;             // set while lk_ep_p2p_experts' expert kernels run
+    bool ydst_on = false;             // set while lk_ep_p2p_experts' expert kernels run (with epw: their rows wait)
+    EpWait epw{};
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
     char msg[256] = {0};
 };
@@ -247,7 +248,7 @@ static int run_experts(LkMoeCtx* c, const LkMoeWeights* W, const float* x, int l
     e.hq = c->hq; e.hd = c->hd; e.y = c->y; e.err = c->err; e.down_fmt = W->down_fmt;
     if (c->xq_ready && x == c->xq_src) { e.xq = c->xq; e.xqn = c->xqn; e.xd = c->xd; }
     e.xrows = c->ep_rows;
-    if (c->ydst_on) e.ydst = c->ydst;
+    if (c->ydst_on) { e.ydst = c->ydst; e.epw = c->epw; }
     if (c->ev[0]) LK_CU(record_event(c->ev[0], st));
     launch_gate_up(e, nt, c->nsm, st);
     if (c->ev[1]) LK_CU(record_event(c->ev[1], st));
@@ -494,10 +495,10 @@ int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* c, const LkMoeWeights* W, int k
     sp.nslots = c->nslots; sp.max_slots = c->max_slots; sp.err = c->err; sp.with_shared = c->rs;
     sp.sh_t0 = c->sh_t0; sp.sh_n = c->sh_n;
     const uint8_t* rows = nullptr;
-    // the slot tables carry each slot's destination row: the down kernel stores the routed entries' rows straight
-    // into their home ranks' mailboxes and the shared rows into shared_out; one small kernel then publishes the
-    // return flags (no combine or copy)
-    rc = p2p_wait_slots(mb, keep, c->cfg.n_experts, c->sel, c->w, sp, err, st, &rows, c->ydst, T > 0 ? shared_out : nullptr);
+    // the gate/up kernel itself waits for the rows and builds the slot tables, each slot with its destination row:
+    // the down kernel stores the routed entries' rows straight into their home ranks' mailboxes and the shared
+    // rows into shared_out; one small kernel then publishes the return flags (no combine or copy)
+    rc = p2p_rows_wait(mb, keep, c->cfg.n_experts, c->sel, c->w, sp, err, c->ydst, T > 0 ? shared_out : nullptr, &c->epw, &rows);
     if (rc == LK_OK) {
         c->ep_rows = rows;
         c->ydst_on = true;

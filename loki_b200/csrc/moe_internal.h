@@ -85,6 +85,27 @@ struct SlotParams {
 void launch_build_slots(const SlotParams& p, cudaStream_t st);
 int max_slots_for(int T, int keep, int n_experts, int nt, int with_shared);
 
+// ---- expert-parallel single-token stage (ep_p2p.cu, ep_device.cuh)
+// the direct return's destinations: entry (row i / keep, k = i % keep) of received row (source s = row / cap,
+// r = row % cap) goes to ret[s] + ((self * cap + r) * MAX_TOPK + k) * HIDDEN -- its row in the home rank's
+// mailbox -- and shared slot j to shared_out + j * HIDDEN; ydst [max_slots] receives the row pointers
+struct EpYDst {
+    float* ret[8];
+    int self, cap;
+    float* shared_out;
+    float** ydst;
+};
+// the rows wait + slot tables run by the single-token gate/up kernel itself (every CTA): mb this rank's mailbox,
+// sel/w [n_ranks*cap][keep] out, sp the slot tables, yd the destinations (yd.ydst null: none); mb null: none
+struct EpWait {
+    uint8_t* mb;
+    int n_ranks, cap, keep, n_experts;
+    int* sel; float* w;
+    SlotParams sp;
+    EpYDst yd;
+    int* err;
+};
+
 // ---- grouped IQ2_XXS matvecs on work slots
 struct ExpertParams {
     // arenas: routed expert e's matrices at base + e*stride; the shared expert's at sh_*
@@ -102,6 +123,7 @@ struct ExpertParams {
     // optional (single-token downs): slot s writes its weighted output row to ydst[s] instead of y row
     // slot_out[s] (the expert-parallel direct return: rows in the home rank's mailbox, over NVLink)
     float* const* ydst;
+    EpWait epw;                                       // optional (single-token gate/up): the rows wait + slot tables
     int* err;
     int down_fmt;                                     // FMT_IQ2 (default, 0 reads as IQ2), FMT_Q2K or FMT_Q3K: every down matrix
     // shared-only launches of launch_down1_kq (slot_expert == null): sh_count single-token slots, slot j
@@ -214,13 +236,14 @@ namespace lk {
 int p2p_rows_count(const LkEpMailbox* m);
 int p2p_rank(const LkEpMailbox* m);
 int p2p_cap(const LkEpMailbox* m);
-// ydst (with shared_out): also the slots' destination rows for the direct return -- a routed entry's row in its
-// home rank's mailbox, a shared slot's row of shared_out; null: none
-int p2p_wait_slots(LkEpMailbox* m, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, int* err,
-                   cudaStream_t st, const uint8_t** rows, float** ydst = nullptr, float* shared_out = nullptr);
+// the single-token gate/up's rows wait + slot tables for mailbox m (ydst with shared_out: the direct return's
+// destinations); *rows: the received rows.  LK_ERR_ARG: not connected
+int p2p_rows_wait(LkEpMailbox* m, int keep, int n_experts, int* sel, float* w, const SlotParams& sp, int* err,
+                  float** ydst, float* shared_out, EpWait* out, const uint8_t** rows);
 bool p2p_direct_ok(const LkEpMailbox* m);
 // the direct return's flags: once the down kernel (the previous launch) has stored every entry row, this layer's
-// epoch into every home rank's return flag of this rank
+// epoch + 1 into every home rank's return flag of this rank, and the local epoch advances to it (after
+// p2p_rows_wait, whose waits read the epoch unadvanced)
 int p2p_ret_flags(LkEpMailbox* m, cudaStream_t st);
 // the router's send parameters for mailbox m (row_map [n_ranks] out); false: not connected
 bool p2p_send_params(const LkEpMailbox* m, int* row_map, EpSendParams* out);
