@@ -527,9 +527,10 @@ def run_ep_decode(args, ws, rank, local, dist):
                 "h2d_bytes_per_step": args.layers * 2 * HIDDEN * 4, "d2h_bytes_per_step": args.layers * HIDDEN * 4,
                 "path": "pinned host x/resid -> CUDA-graph step of EpMoeLayer.forward x58 -> pinned host h (stream events)"},
         # per layer (p2p): router + send (one launch), gate/up (with the rows wait + slot tables), down (storing
-        # each entry's row in its home mailbox), the return flags, the waiting combine; with NCCL: router, pack,
-        # unpack, gate/up, down, combine, return unpack and the home combine around the library's all-to-alls
-        "gpu_launches": args.steps * args.layers * (5 if args.exchange == "p2p" else 8),
+        # each entry's row in its home mailbox), the combine (publishing the return flags, then waiting for every
+        # owner's); with NCCL: router, pack, unpack, gate/up, down, combine, return unpack and the home combine
+        # around the library's all-to-alls
+        "gpu_launches": args.steps * args.layers * (4 if args.exchange == "p2p" else 8),
     }
     if cl:
         out["clocks"] = cl

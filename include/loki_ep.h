@@ -96,9 +96,10 @@ LK_API int lk_ep_all_to_all(LkEpComm* comm, const void* send, void* recv, const 
  * IQ2_XXS or no shared expert: decode), the direct return:
  *   lk_ep_p2p_experts(mb, ctx, W, keep, T, shared, err)  (the rows wait fused with the slot tables, the expert
  *     kernels reading the rows' q8 codes, the down kernel storing each entry's weighted row straight into its
- *     home rank's mailbox, then the return flags; LK_ERR_UNSUPPORTED outside that path)
- *   lk_ep_p2p_combine_entries(mb, sel, keep, row_map, ...)  (wait for all owners; h = resid + shared + the
- *     entries summed in k order, moe = that sum: the single-GPU combine's order)
+ *     home rank's mailbox; LK_ERR_UNSUPPORTED outside that path)
+ *   lk_ep_p2p_combine_entries(mb, sel, keep, row_map, ...)  (publish this rank's return flags, wait for all
+ *     owners; h = resid + shared + the entries summed in k order, moe = that sum: the single-GPU combine's
+ *     order).  A rank with T = 0 calls no combine: its lk_ep_p2p_experts publishes the flags itself.
  * All kernels are capturable; the flags carry an epoch that advances per layer on the device. */
 #define LK_EP_IPC_HANDLE_BYTES 64
 typedef struct LkEpMailbox LkEpMailbox;

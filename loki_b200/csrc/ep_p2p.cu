@@ -148,7 +148,8 @@ __global__ void k_p2p_combine(const uint8_t* mb, int n_ranks, int cap, const int
     }
 }
 
-// the direct return's flags (one thread per home rank s): the down kernel that stored the entry rows has completed
+// the direct return's flags for a rank with no tokens of its own (no entry combine follows; otherwise the combine's
+// first CTA publishes them), one thread per home rank s: the down kernel that stored the entry rows has completed
 // (griddepcontrol.wait: its stores are performed and visible), so a system-scope release of this layer's epoch + 1
 // into s's return flag `self` publishes them; then the local epoch advances (every lane has read it first).  The
 // single-token gate/up's rows wait read the epoch unadvanced.  (The same release raised by the down kernel's last
@@ -167,23 +168,31 @@ __global__ void k_p2p_ret_flags(int n_ranks, int self, P2PPeers peers) {
     if (s == 0) *mb_epoch(peers.mb[self]) = epoch;
 }
 
-// the home combine of the direct return (one token per CTA of 64 threads, 28 CTAs per token): before the wait,
-// threads s < n_ranks poll owner s's flag (bounded) while warp 1 resolves the CTA's token's entries -- the owner d
-// of sel[t][k] stored its row at entry ret (row_map[t][d], k) -- and every thread loads its resid and shared
-// values; after it, moe = the entries summed in k order and h = resid + shared + moe (the single-GPU order)
+// the home combine of the direct return (one token per CTA of 64 threads, 28 CTAs per token).  CTA 0 first
+// publishes this rank's own return flags (the owner side of the layer: its down kernel has completed) and advances
+// the epoch.  Then, in every CTA, threads s < n_ranks poll owner s's flag (bounded) while warp 1 resolves the CTA's
+// token's entries -- the owner d of sel[t][k] stored its row at entry ret (row_map[t][d], k) -- and every thread
+// loads its resid and shared values; after the wait, moe = the entries summed in k order and h = resid + shared +
+// moe (the single-GPU order).  Every rank publishes before it waits, so no rank waits on one that has not.
 constexpr int P2PC_THREADS = 64;
 __global__ void __launch_bounds__(P2PC_THREADS) k_p2p_combine_k(const uint8_t* mb, int n_ranks, int cap, const int* __restrict__ sel,
                                                                 int keep, const int* __restrict__ row_map, int T,
                                                                 const float* __restrict__ hpart, const float* __restrict__ shared,
-                                                                float* h, float* moe, int* err) {
+                                                                float* h, float* moe, int self, P2PPeers peers, int* err) {
     __shared__ int eoff[MAX_TOPK];
     pdl_trigger();
     pdl_wait();
     const int tid = threadIdx.x;
     const int i = blockIdx.x * P2PC_THREADS + tid;                   // float4 index over T x HIDDEN
     const int t = (blockIdx.x * P2PC_THREADS) / (HIDDEN / 4), c = i % (HIDDEN / 4);   // HIDDEN / 4 = 28 CTAs
+    // this layer's value: the rows flag this rank's own send published to itself (no peer writes that word)
+    const uint32_t want = *(const volatile uint32_t*)(mb_flags((uint8_t*)mb, 0) + self);
+    if (blockIdx.x == 0 && tid < n_ranks) {          // this rank's return flags: its down kernel (an earlier
+        __threadfence_system();                      // launch) has stored every entry row it owns
+        st_release_sys(mb_flags(peers.mb[tid], 1) + self, want);
+        if (tid == 0) *mb_epoch((uint8_t*)mb) = want;   // the layer's epoch advance (the gate/up waits read it)
+    }
     if (tid < n_ranks) {
-        const uint32_t want = *mb_epoch((uint8_t*)mb);
         const uint32_t* f = mb_flags((uint8_t*)mb, 1) + tid;
         if ((int)(ld_acquire_sys(f) - want) < 0) {
             const unsigned long long t0 = globaltimer_ns();
@@ -323,10 +332,11 @@ int lk_ep_p2p_combine(LkEpMailbox* m, const int* row_map, int T, const float* re
 int lk_ep_p2p_combine_entries(LkEpMailbox* m, const int* sel, int keep, const int* row_map, int T, const float* resid,
                               const float* shared, float* h, float* moe, int* err, lk_stream_t stream) {
     if (!m || T < 1 || T > m->cap || !sel || keep < 1 || keep > MAX_TOPK || !row_map) return LK_ERR_ARG;
+    for (int r = 0; r < m->n_ranks; ++r) if (!m->peers.mb[r]) return LK_ERR_ARG;   // not connected
     if (!has_erets(m->n_ranks, m->cap)) return LK_ERR_UNSUPPORTED;
     static_assert((HIDDEN / 4) % P2PC_THREADS == 0, "a combine CTA covers one token");
     launch_pdl_n(k_p2p_combine_k, dim3(T * (HIDDEN / 4) / P2PC_THREADS), dim3(P2PC_THREADS), 0, (cudaStream_t)stream, (const uint8_t*)m->local,
-                 m->n_ranks, m->cap, sel, keep, row_map, T, resid, shared, h, moe, err);
+                 m->n_ranks, m->cap, sel, keep, row_map, T, resid, shared, h, moe, m->rank, m->peers, err);
     return cudaGetLastError() == cudaSuccess ? LK_OK : LK_ERR_CUDA;
 }
 

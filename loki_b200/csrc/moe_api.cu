@@ -497,13 +497,14 @@ int lk_ep_p2p_experts(LkEpMailbox* mb, LkMoeCtx* c, const LkMoeWeights* W, int k
     const uint8_t* rows = nullptr;
     // the gate/up kernel itself waits for the rows and builds the slot tables, each slot with its destination row:
     // the down kernel stores the routed entries' rows straight into their home ranks' mailboxes and the shared
-    // rows into shared_out; one small kernel then publishes the return flags (no combine or copy)
+    // rows into shared_out (no combine or copy)
     rc = p2p_rows_wait(mb, keep, c->cfg.n_experts, c->sel, c->w, sp, err, c->ydst, T > 0 ? shared_out : nullptr, &c->epw, &rows);
     if (rc == LK_OK) {
         c->ep_rows = rows;
         c->ydst_on = true;
         rc = run_experts(c, W, nullptr, HIDDEN, nullptr, R, keep, c->sel, nullptr, nullptr, 1, st);
-        if (rc == LK_OK) rc = p2p_ret_flags(mb, st);
+        // the return flags: published by lk_ep_p2p_combine_entries' first CTA, or here when no combine follows
+        if (rc == LK_OK && T == 0) rc = p2p_ret_flags(mb, st);
     }
     c->sh_t0 = 0; c->sh_n = 0; c->ep_rows = nullptr; c->ydst_on = false;
     return rc ? set_err(c, rc, "fused peer exchange: launch failed") : LK_OK;
