@@ -33,13 +33,16 @@ __global__ void __launch_bounds__(64) k_combine(CombineParams p) {
     #pragma unroll
     for (int k = 0; k < MAX_TOPK; ++k)
         if (use[k]) { r.x += v[k].x; r.y += v[k].y; r.z += v[k].z; r.w += v[k].w; }
+    if (i == 0 && p.err2) *p.err2 = *p.err;          // every earlier kernel's error (they have completed)
     if (p.moe) ((float4*)(p.moe + (size_t)t * p.ld_out))[c] = r;
+    if (p.moe2) ((float4*)(p.moe2 + (size_t)t * p.ld_out))[c] = r;
     if (!p.h) return;
     float4 h = hr;
     if (has_sh) { h.x += hs.x; h.y += hs.y; h.z += hs.z; h.w += hs.w; }
     if (p.shared) { h.x += he.x; h.y += he.y; h.z += he.z; h.w += he.w; }
     h.x += r.x; h.y += r.y; h.z += r.z; h.w += r.w;
     ((float4*)(p.h + (size_t)t * p.ld_out))[c] = h;
+    if (p.h2) ((float4*)(p.h2 + (size_t)t * p.ld_out))[c] = h;
 }
 
 void launch_combine(const CombineParams& p, cudaStream_t st) {

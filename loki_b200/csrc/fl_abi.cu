@@ -46,6 +46,9 @@ struct FLCtx {
     // host mirrors (pinned)
     int* h_sel = nullptr; float* h_wts = nullptr; float* h_ncur = nullptr; float* h_fi = nullptr; float* h_h = nullptr;
     float* h_moe = nullptr; int* h_tab = nullptr; float* h_tabw = nullptr; float* h_in = nullptr;
+    // device views of h_h / h_moe / h_tab / h_tabw / h_err (null where the page-locked block is not mapped): the
+    // one-row fl_moe_auto graph's kernels store its host outputs there directly instead of copying them back
+    float* hd_h = nullptr; float* hd_moe = nullptr; int* hd_tab = nullptr; float* hd_tabw = nullptr; int* hd_err = nullptr;
     // wide pass
     int wmax = 0, wke = 0;
     float* ncur_all = nullptr; float* base_all = nullptr; float* out_all = nullptr;
@@ -175,6 +178,14 @@ FLCtx* impl_fl_init(int kvp, int sc_cap, cudaStream_t ext = nullptr) {
     c->h_ncur = h_io; c->h_fi = h_io + R; c->h_h = h_ho; c->h_moe = h_ho + R;
     c->h_tab = h_iwe; c->h_tabw = (float*)(h_iwe + NARROW_SLOTS); c->h_err = h_iwe + 2 * NARROW_SLOTS;
     c->h_sel = h_sw; c->h_wts = (float*)(h_sw + P8);
+    float* dho = nullptr; int* diwe = nullptr;
+    if (cudaHostGetDevicePointer((void**)&dho, h_ho, 0) == cudaSuccess && cudaHostGetDevicePointer((void**)&diwe, h_iwe, 0) == cudaSuccess &&
+        dho && diwe) {
+        c->hd_h = dho; c->hd_moe = dho + R;
+        c->hd_tab = diwe; c->hd_tabw = (float*)(diwe + NARROW_SLOTS); c->hd_err = diwe + 2 * NARROW_SLOTS;
+    } else {
+        cudaGetLastError();                       // not mapped: the copies stay
+    }
     return c;
 }
 
@@ -372,8 +383,10 @@ void impl_fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
 
 // the narrow pass from routing already on the device (c->ids, c->w [n][KE]): slots, experts, combine, and the
 // result copies into the pinned mirrors (h, moe; with ids_back also the routing), then the stream sync
+// host_direct (the one-row fl_moe_auto, its keep kernel having stored ids / w into the host mirror): the combine
+// stores h, moe and the error word straight into the page-locked mirrors, so no copy node ends the graph
 static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int n, bool ids_back,
-                           bool fold_shared = false, bool slots_ready = false) {
+                           bool fold_shared = false, bool slots_ready = false, bool host_direct = false) {
     cudaStream_t st = c->st;
     const int nt = nt_for(n);
     if (!slots_ready) {                           // slot tables from the device routing (k_fl_keep1 writes them for n == 1)
@@ -396,12 +409,15 @@ static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const voi
     cp.y = c->y; cp.resid = c->ffn_inp; cp.T = n; cp.keep = KE; cp.with_shared = fold_shared ? 1 : 0;
     cp.shared = fold_shared ? nullptr : c->shared_y;
     cp.h = c->h; cp.moe = c->moe; cp.ld_out = HIDDEN;
+    if (host_direct) { cp.h2 = c->hd_h; cp.moe2 = c->hd_moe; cp.err = c->err; cp.err2 = c->hd_err; }
     launch_combine(cp, st);
     // the folded shared rows stay in y until a later call needs shared_y (materialize_shared)
-    FLCK(copy_pair(c->h_h, c->h, (size_t)PREP_ROWS * HIDDEN * 4, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
-    if (ids_back)                                 // ids, w and the error word: three rows of one block
-        FLCK(cudaMemcpy2DAsync(c->h_tab, (size_t)NARROW_SLOTS * 4, c->ids, (size_t)NARROW_SLOTS * 4, (size_t)n * KE * 4, 3,
-                               cudaMemcpyDeviceToHost, st));
+    if (!host_direct) {
+        FLCK(copy_pair(c->h_h, c->h, (size_t)PREP_ROWS * HIDDEN * 4, (size_t)n * HIDDEN * 4, cudaMemcpyDeviceToHost, st));
+        if (ids_back)                             // ids, w and the error word: three rows of one block
+            FLCK(cudaMemcpy2DAsync(c->h_tab, (size_t)NARROW_SLOTS * 4, c->ids, (size_t)NARROW_SLOTS * 4, (size_t)n * KE * 4, 3,
+                                   cudaMemcpyDeviceToHost, st));
+    }
     FLCK(rec(c->em1, st));
     if (!ids_back) queue_err(c);
 }
@@ -495,6 +511,7 @@ __global__ void k_fl_keep(const int* sel8, const float* w8, int n, int KE, int r
 struct Keep1Params {
     const int* sel8; const float* w8; int KE, renorm, fold;
     int* ids; float* w; int* se; int* stok; int* sout; float* sw; int* sn;
+    int* ids2; float* w2;                         // optional: a second copy of ids / w (the page-locked host mirror)
 };
 __global__ void k_fl_keep1(Keep1Params p) {
     pdl_trigger();
@@ -502,6 +519,7 @@ __global__ void k_fl_keep1(Keep1Params p) {
     if (threadIdx.x != 0) return;
     keep_row(p.sel8, p.w8, 0, p.KE, p.renorm, p.ids, p.w);
     for (int k = 0; k < p.KE; ++k) { p.se[k] = p.ids[k]; p.stok[k] = 0; p.sout[k] = k; p.sw[k] = p.w[k]; }
+    if (p.ids2) for (int k = 0; k < p.KE; ++k) { p.ids2[k] = p.ids[k]; p.w2[k] = p.w[k]; }
     if (p.fold) { p.se[p.KE] = SHARED_SLOT; p.stok[p.KE] = 0; p.sout[p.KE] = p.KE; p.sw[p.KE] = 1.0f; }
     *p.sn = p.KE + (p.fold ? 1 : 0);
 }
@@ -527,13 +545,15 @@ void impl_fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* do
     if (fold) { key.p[3] = c->sh_w[0]; key.p[4] = c->sh_w[1]; key.p[5] = c->sh_w[2]; }
     run_graph(c, key, [&]() {
         FLCK(rec(c->em0, st));
+        const bool direct = n == 1 && c->hd_h;
         if (n == 1) {
-            const Keep1Params kp{ c->sel, c->wts, KE, renorm, fold ? 1 : 0, c->ids, c->w, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n };
+            const Keep1Params kp{ c->sel, c->wts, KE, renorm, fold ? 1 : 0, c->ids, c->w, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n,
+                                  direct ? c->hd_tab : nullptr, direct ? c->hd_tabw : nullptr };
             FLCK(launch_pdl(k_fl_keep1, dim3(1), dim3(32), 0, st, kp));
         } else {
             k_fl_keep<<<1, 64, 0, st>>>(c->sel, c->wts, n, KE, renorm, c->ids, c->w);
         }
-        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, true, fold, n == 1);
+        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, true, fold, n == 1, direct);
     });
     if (fold) { c->sh_in_y_n = n; c->sh_in_y_ke = KE; }
     finish_narrow(c, KE, n, true, out);

@@ -171,6 +171,9 @@ struct CombineParams {
     const int* sel;                   // optional [T][keep]: entries with a negative id are not summed
     int sh_t0, sh_n;                  // shared-expert rows as in SlotParams; resid may be null (zero)
     float* shared_out;                // optional: the shared expert's output of rows [sh_t0, +sh_n) -> row j here
+    // optional second destinations of h and moe (ld_out as well): page-locked host memory the kernel stores into
+    // directly, so no device-to-host copy follows; err2 (with err): a copy of the device error word, by one thread
+    float* h2; float* moe2; const int* err; int* err2;
 };
 void launch_combine(const CombineParams& p, cudaStream_t st);
 
