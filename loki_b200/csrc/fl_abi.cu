@@ -383,8 +383,8 @@ void impl_fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
 
 // the narrow pass from routing already on the device (c->ids, c->w [n][KE]): slots, experts, combine, and the
 // result copies into the pinned mirrors (h, moe; with ids_back also the routing), then the stream sync
-// host_direct (the one-row fl_moe_auto, its keep kernel having stored ids / w into the host mirror): the combine
-// stores h, moe and the error word straight into the page-locked mirrors, so no copy node ends the graph
+// host_direct (fl_moe, and the one-row fl_moe_auto whose keep kernel stores ids / w into the host mirror): the
+// combine stores h, moe and the error word straight into the page-locked mirrors, so no copy node ends the graph
 static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int KE, int n, bool ids_back,
                            bool fold_shared = false, bool slots_ready = false, bool host_direct = false) {
     cudaStream_t st = c->st;
@@ -419,7 +419,7 @@ static void enqueue_narrow(FLCtx* c, const void* gate, const void* up, const voi
                                    cudaMemcpyDeviceToHost, st));
     }
     FLCK(rec(c->em1, st));
-    if (!ids_back) queue_err(c);
+    if (!ids_back && !host_direct) queue_err(c);
 }
 
 // after the enqueued narrow pass: wait for it, account its time, read the error word and the routing back
@@ -460,7 +460,7 @@ void impl_fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, i
         if (pend && !fold) enqueue_shared(c, c->sh_w[0], c->sh_w[1], c->sh_w[2], pn, c->sh_fmt);
         FLCK(rec(c->em0, st));
         FLCK(copy_pair(c->ids, hi, (size_t)NARROW_SLOTS * 4, (size_t)n * KE * 4, cudaMemcpyHostToDevice, st));   // ids, w
-        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, false, fold);
+        enqueue_narrow(c, gate, up, down, down_fmt, KE, n, false, fold, false, c->hd_h != nullptr);
     });
     if (fold) { c->sh_in_y_n = n; c->sh_in_y_ke = KE; }
     finish_narrow(c, KE, n, false, out);
