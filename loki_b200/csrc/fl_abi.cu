@@ -49,6 +49,8 @@ struct FLCtx {
     // device views of h_h / h_moe / h_tab / h_tabw / h_err (null where the page-locked block is not mapped): the
     // one-row fl_moe_auto graph's kernels store its host outputs there directly instead of copying them back
     float* hd_h = nullptr; float* hd_moe = nullptr; int* hd_tab = nullptr; float* hd_tabw = nullptr; int* hd_err = nullptr;
+    // ... and of h_ncur / h_fi: a host-input prepare's first kernel reads the rows from there (no copy node)
+    const float* hd_ncur = nullptr; const float* hd_fi = nullptr;
     // wide pass
     int wmax = 0, wke = 0;
     float* ncur_all = nullptr; float* base_all = nullptr; float* out_all = nullptr;
@@ -178,11 +180,12 @@ FLCtx* impl_fl_init(int kvp, int sc_cap, cudaStream_t ext = nullptr) {
     c->h_ncur = h_io; c->h_fi = h_io + R; c->h_h = h_ho; c->h_moe = h_ho + R;
     c->h_tab = h_iwe; c->h_tabw = (float*)(h_iwe + NARROW_SLOTS); c->h_err = h_iwe + 2 * NARROW_SLOTS;
     c->h_sel = h_sw; c->h_wts = (float*)(h_sw + P8);
-    float* dho = nullptr; int* diwe = nullptr;
+    float* dho = nullptr; int* diwe = nullptr; float* dio = nullptr;
     if (cudaHostGetDevicePointer((void**)&dho, h_ho, 0) == cudaSuccess && cudaHostGetDevicePointer((void**)&diwe, h_iwe, 0) == cudaSuccess &&
-        dho && diwe) {
+        cudaHostGetDevicePointer((void**)&dio, h_io, 0) == cudaSuccess && dho && diwe && dio) {
         c->hd_h = dho; c->hd_moe = dho + R;
         c->hd_tab = diwe; c->hd_tabw = (float*)(diwe + NARROW_SLOTS); c->hd_err = diwe + 2 * NARROW_SLOTS;
+        c->hd_ncur = dio; c->hd_fi = dio + R;
     } else {
         cudaGetLastError();                       // not mapped: the copies stay
     }
@@ -311,6 +314,18 @@ static void ensure_shared(FLCtx* c) {
     c->sh_pending = false;
 }
 
+// a host-input prepare's rows: every thread reads one float4 of each from the page-locked mirrors (over PCIe,
+// through their device view) and stores it to ncur / ffn_inp.  Programmatic dependent launch lets the router that
+// follows load its weights meanwhile; the wait first keeps the previous call's kernels' reads of ncur / ffn_inp
+// ordered before these stores.
+__global__ void __launch_bounds__(256) k_fl_h2d_rows(const float4* __restrict__ a, const float4* __restrict__ b, float4* da,
+                                                     float4* db, int n4) {
+    pdl_trigger();
+    pdl_wait();
+    const int i = blockIdx.x * 256 + threadIdx.x;
+    if (i < n4) { const float4 u = a[i], v = b[i]; da[i] = u; db[i] = v; }
+}
+
 void impl_fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
     if (!c || !W || !ncur || !ffn_inp || N < 1 || N > PREP_ROWS) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: bad argument"); return; }
     if (wrow >= 0 && (!c->ncur_all || wrow + N > c->wmax)) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: wide rows outside fl_wide_init capacity"); return; }
@@ -333,7 +348,13 @@ void impl_fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const flo
     run_graph(c, key, [&]() {
     FLCK(rec(c->ep0, st));
     if (host) {
-        FLCK(copy_pair(c->ncur, c->h_ncur, (size_t)PREP_ROWS * HIDDEN * 4, bytes, cudaMemcpyHostToDevice, st));
+        if (c->hd_ncur) {
+            const int n4 = N * (HIDDEN / 4);
+            FLCK(launch_pdl_n(k_fl_h2d_rows, dim3((n4 + 255) / 256), dim3(256), 0, st, (const float4*)c->hd_ncur, (const float4*)c->hd_fi,
+                            (float4*)c->ncur, (float4*)c->ffn_inp, n4));
+        } else {
+            FLCK(copy_pair(c->ncur, c->h_ncur, (size_t)PREP_ROWS * HIDDEN * 4, bytes, cudaMemcpyHostToDevice, st));
+        }
         FLCK(rec(c->eh2d, st));
     } else {
         FLCK(cudaMemcpyAsync(c->ncur, ncur, bytes, cudaMemcpyDeviceToDevice, st));
