@@ -51,6 +51,9 @@ struct FLCtx {
     float* hd_h = nullptr; float* hd_moe = nullptr; int* hd_tab = nullptr; float* hd_tabw = nullptr; int* hd_err = nullptr;
     // ... and of h_ncur / h_fi: a host-input prepare's first kernel reads the rows from there (no copy node)
     const float* hd_ncur = nullptr; const float* hd_fi = nullptr;
+    // a host-input, non-wide fl_moe_prepare is deferred (its rows already in the mirrors): the next fl_moe_auto
+    // that folds the shared expert runs it in its own graph, any other call first runs it alone (flush_prepare)
+    bool prep_deferred = false; FLMoeW prep_w{};
     // wide pass
     int wmax = 0, wke = 0;
     float* ncur_all = nullptr; float* base_all = nullptr; float* out_all = nullptr;
@@ -83,6 +86,7 @@ struct FLCtx {
 constexpr size_t FL_MAX_GRAPHS = 1024;
 
 void impl_fl_free(FLCtx* c);
+static void flush_prepare_any(FLCtx* c);          // a deferred fl_moe_prepare runs now (defined with the prepare)
 
 static int fl_fail(FLCtx* c, int code, const char* what, cudaError_t e = cudaSuccess) {
     std::fprintf(stderr, "[loki_moe] %s%s%s\n", what, e != cudaSuccess ? ": " : "", e != cudaSuccess ? cudaGetErrorString(e) : "");
@@ -223,7 +227,7 @@ void impl_fl_h2d(FLCtx* c, void* dst, const void* src, size_t bytes) {
     FLCK(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, c->st));
 }
 
-void impl_fl_wait_event(FLCtx* c, fl_event_t ev) { if (c) FLCK(cudaStreamWaitEvent(c->st, (cudaEvent_t)ev, 0)); }
+void impl_fl_wait_event(FLCtx* c, fl_event_t ev) { flush_prepare_any(c); if (c) FLCK(cudaStreamWaitEvent(c->st, (cudaEvent_t)ev, 0)); }
 
 double impl_fl_gpu_ms(FLCtx* c, int which) { return !c ? 0.0 : which == 1 ? c->ms_moe : c->ms_prep; }
 
@@ -326,36 +330,21 @@ __global__ void __launch_bounds__(256) k_fl_h2d_rows(const float4* __restrict__ 
     if (i < n4) { const float4 u = a[i], v = b[i]; da[i] = u; db[i] = v; }
 }
 
-void impl_fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
-    if (!c || !W || !ncur || !ffn_inp || N < 1 || N > PREP_ROWS) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: bad argument"); return; }
-    if (wrow >= 0 && (!c->ncur_all || wrow + N > c->wmax)) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: wide rows outside fl_wide_init capacity"); return; }
-    if (W->sh_fmt != 0 && W->sh_fmt != FL_IQ2 && W->sh_fmt != FL_Q5K) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe_prepare: shared-expert format must be FL_IQ2 or FL_Q5K"); return; }
+// the prepare's launches: rows in (from the host mirrors or device pointers), router, the shared expert for a wide
+// pass; events: record ep0 / ep1 around them (the fetch accounts that time).  eh2d follows the router, so that
+// no event node separates the row-reading kernel from the router (programmatic dependent launch)
+static void enqueue_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow, bool events) {
     cudaStream_t st = c->st;
     const size_t bytes = (size_t)N * HIDDEN * 4;
-    if (host) {                                   // the mirrors may still feed the previous call's queued copy
-        FLCK(cudaEventSynchronize(c->eh2d));
-        std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes);
-    }
-    c->prep_n = N;
-    c->sh_pending = W->sh_gate && W->sh_up && W->sh_down && wrow < 0;
-    c->sh_in_y_n = 0;                             // this prepare's shared expert supersedes the last one
-    c->sh_w[0] = W->sh_gate; c->sh_w[1] = W->sh_up; c->sh_w[2] = W->sh_down; c->sh_fmt = W->sh_fmt == FL_Q5K ? FL_Q5K : 0;
-    FLCtx::GraphKey key;
-    std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
-    key.kind = 1; key.a = N; key.b = host; key.c = wrow; key.d = W->gate_f16 | (c->sh_fmt << 4);
-    const void* kp[8] = { W->gate_inp, W->probs_b, W->sh_gate, W->sh_up, W->sh_down, host ? nullptr : ncur, host ? nullptr : ffn_inp, nullptr };
-    std::memcpy(key.p, kp, sizeof(kp));
-    run_graph(c, key, [&]() {
-    FLCK(rec(c->ep0, st));
+    if (events) FLCK(rec(c->ep0, st));
     if (host) {
         if (c->hd_ncur) {
             const int n4 = N * (HIDDEN / 4);
             FLCK(launch_pdl_n(k_fl_h2d_rows, dim3((n4 + 255) / 256), dim3(256), 0, st, (const float4*)c->hd_ncur, (const float4*)c->hd_fi,
-                            (float4*)c->ncur, (float4*)c->ffn_inp, n4));
+                              (float4*)c->ncur, (float4*)c->ffn_inp, n4));
         } else {
             FLCK(copy_pair(c->ncur, c->h_ncur, (size_t)PREP_ROWS * HIDDEN * 4, bytes, cudaMemcpyHostToDevice, st));
         }
-        FLCK(rec(c->eh2d, st));
     } else {
         FLCK(cudaMemcpyAsync(c->ncur, ncur, bytes, cudaMemcpyDeviceToDevice, st));
         FLCK(cudaMemcpyAsync(c->ffn_inp, ffn_inp, bytes, cudaMemcpyDeviceToDevice, st));
@@ -366,6 +355,7 @@ void impl_fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const flo
     rp.logits = c->logits; rp.probs = c->probs; rp.sel = c->sel; rp.w = c->wts; rp.tile_count = c->rcount;
     rp.n_experts = N_EXPERTS; rp.topk = MAX_TOPK; rp.keep = MAX_TOPK; rp.renorm = 0; rp.n_group = 1; rp.topk_group = 1; rp.scale = 2.5f;
     launch_router(rp, st);
+    if (host) FLCK(rec(c->eh2d, st));             // the mirrors have been read
     // shared expert on all rows: now for a wide pass (its base rows need it), else when first needed
     if (W->sh_gate && W->sh_up && W->sh_down && wrow >= 0) {
         enqueue_shared(c, W->sh_gate, W->sh_up, W->sh_down, N, c->sh_fmt);
@@ -379,12 +369,54 @@ void impl_fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const flo
         cp.h = c->base_all + (size_t)wrow * HIDDEN; cp.moe = nullptr; cp.ld_out = HIDDEN;
         launch_combine(cp, st);
     }
-    FLCK(rec(c->ep1, st));
-    });
+    if (events) FLCK(rec(c->ep1, st));
+}
+
+static FLCtx::GraphKey prepare_key(const FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
+    FLCtx::GraphKey key;
+    std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
+    key.kind = 1; key.a = N; key.b = host; key.c = wrow; key.d = W->gate_f16 | (c->sh_fmt << 4);
+    const void* kp[8] = { W->gate_inp, W->probs_b, W->sh_gate, W->sh_up, W->sh_down, host ? nullptr : ncur, host ? nullptr : ffn_inp, nullptr };
+    std::memcpy(key.p, kp, sizeof(kp));
+    return key;
+}
+
+// a deferred prepare runs now, alone (every entry point but fl_moe_auto calls this first)
+static void flush_prepare(FLCtx* c) {
+    if (!c || !c->prep_deferred) return;
+    c->prep_deferred = false;
+    const FLMoeW W = c->prep_w;
+    const int N = c->prep_n;
+    run_graph(c, prepare_key(c, &W, nullptr, nullptr, N, 1, -1), [&]() { enqueue_prepare(c, &W, nullptr, nullptr, N, 1, -1, true); });
+    FLCK(cudaGetLastError());
+}
+
+static void flush_prepare_any(FLCtx* c) { flush_prepare(c); }
+
+void impl_fl_moe_prepare(FLCtx* c, const FLMoeW* W, const float* ncur, const float* ffn_inp, int N, int host, int wrow) {
+    flush_prepare(c);                             // an earlier deferred prepare first: its rows are in the mirrors
+    if (!c || !W || !ncur || !ffn_inp || N < 1 || N > PREP_ROWS) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: bad argument"); return; }
+    if (wrow >= 0 && (!c->ncur_all || wrow + N > c->wmax)) { fl_fail(c, LK_ERR_ARG, "fl_moe_prepare: wide rows outside fl_wide_init capacity"); return; }
+    if (W->sh_fmt != 0 && W->sh_fmt != FL_IQ2 && W->sh_fmt != FL_Q5K) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe_prepare: shared-expert format must be FL_IQ2 or FL_Q5K"); return; }
+    const size_t bytes = (size_t)N * HIDDEN * 4;
+    if (host) {                                   // the mirrors may still feed the previous call's queued copy
+        FLCK(cudaEventSynchronize(c->eh2d));
+        std::memcpy(c->h_ncur, ncur, bytes); std::memcpy(c->h_fi, ffn_inp, bytes);
+    }
+    c->prep_n = N;
+    c->sh_pending = W->sh_gate && W->sh_up && W->sh_down && wrow < 0;
+    c->sh_in_y_n = 0;                             // this prepare's shared expert supersedes the last one
+    c->sh_w[0] = W->sh_gate; c->sh_w[1] = W->sh_up; c->sh_w[2] = W->sh_down; c->sh_fmt = W->sh_fmt == FL_Q5K ? FL_Q5K : 0;
+    if (host && wrow < 0 && c->use_graphs) {      // the rows are in the mirrors: launch with the next call
+        c->prep_deferred = true; c->prep_w = *W;
+        return;
+    }
+    run_graph(c, prepare_key(c, W, ncur, ffn_inp, N, host, wrow), [&]() { enqueue_prepare(c, W, ncur, ffn_inp, N, host, wrow, true); });
     FLCK(cudaGetLastError());
 }
 
 void impl_fl_fetch(FLCtx* c, int n, int what, FLOut* out) {
+    flush_prepare_any(c);
     if (!c || !out) return;
     std::memset(out, 0, sizeof(FLOut));
     n = std::min(n, c->prep_n > 0 ? c->prep_n : n);
@@ -456,6 +488,7 @@ static void finish_narrow(FLCtx* c, int KE, int n, bool ids_back, FLOut* out) {
 
 void impl_fl_moe(FLCtx* c, const void* gate, const void* up, const void* down, int nexp, int down_fmt, const int* ids, const float* w,
             int KE, int n, FLOut* out) {
+    flush_prepare_any(c);
     if (!c || !out) return;
     std::memset(out, 0, sizeof(FLOut));
     if (!down_fmt_ok(down_fmt)) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_moe: down format must be FL_IQ2, FL_Q2K or FL_Q3K"); return; }
@@ -555,17 +588,26 @@ void impl_fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* do
     cudaStream_t st = c->st;
     // the pending shared expert (IQ2_XXS) joins the routed launches when the downs are IQ2_XXS too; with a
     // K-quant down format, or in the real model's Q5_K / Q6_K formats, it runs on its own first
-    materialize_shared(c);
     const bool fold = c->sh_pending && c->sh_fmt == 0 && down_fmt == FL_IQ2 && n == c->prep_n;
+    // a deferred prepare joins this call's graph when the shared expert folds in (nothing else needs its rows
+    // before the experts); otherwise it runs alone first.  In the joined graph em0 precedes the prepare, so
+    // fl_gpu_ms(1) then counts the prepare too, and no event node separates its router from the keep kernel.
+    const bool merge = c->prep_deferred && fold;
+    if (!merge) flush_prepare(c);
+    materialize_shared(c);
     if (!fold) ensure_shared(c);
     c->sh_pending = false;
+    const FLMoeW pw = c->prep_w;
+    c->prep_deferred = false;
     FLCtx::GraphKey key;
     std::memset(&key, 0, sizeof(key));            // padding included: keys compare with memcmp
-    key.kind = 3; key.a = n; key.b = KE; key.c = down_fmt; key.d = renorm | (fold ? 2 : 0);
+    key.kind = merge ? 4 : 3; key.a = n; key.b = KE; key.c = down_fmt; key.d = renorm | (fold ? 2 : 0);
     key.p[0] = gate; key.p[1] = up; key.p[2] = down;
     if (fold) { key.p[3] = c->sh_w[0]; key.p[4] = c->sh_w[1]; key.p[5] = c->sh_w[2]; }
+    if (merge) { key.p[6] = pw.gate_inp; key.p[7] = pw.probs_b; key.d |= (pw.gate_f16 << 4) | (c->prep_n << 8); }
     run_graph(c, key, [&]() {
         FLCK(rec(c->em0, st));
+        if (merge) enqueue_prepare(c, &pw, nullptr, nullptr, c->prep_n, 1, -1, false);
         const bool direct = n == 1 && c->hd_h;
         if (n == 1) {
             const Keep1Params kp{ c->sel, c->wts, KE, renorm, fold ? 1 : 0, c->ids, c->w, c->s_expert, c->s_tok, c->s_out, c->s_w, c->s_n,
@@ -580,9 +622,10 @@ void impl_fl_moe_auto(FLCtx* c, const void* gate, const void* up, const void* do
     finish_narrow(c, KE, n, true, out);
 }
 
-void impl_fl_use_graphs(FLCtx* c, int enable) { if (c) c->use_graphs = enable != 0; }
+void impl_fl_use_graphs(FLCtx* c, int enable) { flush_prepare_any(c); if (c) c->use_graphs = enable != 0; }
 
 void impl_fl_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
+    flush_prepare_any(c);
     if (!c || !out || !mo || n < 1 || n > PREP_ROWS) return;
     std::memset(out, 0, sizeof(FLOut));
     cudaStream_t st = c->st;
@@ -600,6 +643,7 @@ void impl_fl_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
 }
 
 void impl_fl_moe_outs(FLCtx* c, int b, const int* ids, const float* w, int KE, float* out) {
+    flush_prepare_any(c);
     if (!c || !ids || !w || !out || b < 0 || b >= c->last_n || KE != c->last_ke) { fl_fail(c, LK_ERR_ARG, "fl_moe_outs: no matching narrow pass"); return; }
     std::vector<float> rows((size_t)KE * HIDDEN);
     FLCK(cudaStreamSynchronize(c->st));
@@ -614,6 +658,7 @@ void impl_fl_moe_outs(FLCtx* c, int b, const int* ids, const float* w, int KE, f
 }
 
 int impl_fl_wide_init(FLCtx* c, int wmax, int KE) {
+    flush_prepare_any(c);
     if (!c || wmax < 1 || KE < 1 || KE > MAX_TOPK) return 0;
     c->wmax = wmax; c->wke = KE;
     const size_t R = (size_t)wmax * HIDDEN;
@@ -637,6 +682,7 @@ int impl_fl_wide_init(FLCtx* c, int wmax, int KE) {
 
 void impl_fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* down, int down_fmt, int nexp, const int* midx, const int* rows,
                  const int* kidx, const float* wk, int nslots, int KE, int par) {
+    flush_prepare_any(c);
     if (!c || !c->ncur_all) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: fl_wide_init first"); return; }
     if (!down_fmt_ok(down_fmt)) { fl_fail(c, LK_ERR_UNSUPPORTED, "fl_wide_moe: down format must be FL_IQ2, FL_Q2K or FL_Q3K"); return; }
     if (KE != c->wke || nslots < 0 || nexp < 1) { fl_fail(c, LK_ERR_ARG, "fl_wide_moe: bad argument"); return; }
@@ -716,10 +762,11 @@ void impl_fl_wide_moe(FLCtx* c, const void* gate, const void* up, const void* do
     FLCK(cudaGetLastError());
 }
 
-void impl_fl_wide_mark(FLCtx* c, int par) { if (c && c->wev[par & 1]) FLCK(cudaEventRecord(c->wev[par & 1], c->st)); }
-void impl_fl_wide_wait(FLCtx* c, int par) { if (c && c->wev[par & 1]) FLCK(cudaEventSynchronize(c->wev[par & 1])); }
+void impl_fl_wide_mark(FLCtx* c, int par) { flush_prepare_any(c); if (c && c->wev[par & 1]) FLCK(cudaEventRecord(c->wev[par & 1], c->st)); }
+void impl_fl_wide_wait(FLCtx* c, int par) { flush_prepare_any(c); if (c && c->wev[par & 1]) FLCK(cudaEventSynchronize(c->wev[par & 1])); }
 
 void impl_fl_wide_finish(FLCtx* c, int n, int KE, FLOut* out) {
+    flush_prepare_any(c);
     if (!c || !out) return;
     std::memset(out, 0, sizeof(FLOut));
     if (!c->ncur_all || n < 1 || n > c->wmax || KE != c->wke) { fl_fail(c, LK_ERR_ARG, "fl_wide_finish: bad argument"); return; }
@@ -740,6 +787,7 @@ void impl_fl_wide_finish(FLCtx* c, int n, int KE, FLOut* out) {
 }
 
 void impl_fl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
+    flush_prepare_any(c);
     if (!c || !out || !mo || !c->ncur_all || n < 1 || n > c->wmax) return;
     std::memset(out, 0, sizeof(FLOut));
     cudaStream_t st = c->st;
@@ -755,6 +803,7 @@ void impl_fl_wide_skip(FLCtx* c, const float* mo, int n, FLOut* out) {
 }
 
 void impl_fl_wide_outs(FLCtx* c, int row, int KE, float* out) {
+    flush_prepare_any(c);
     if (!c || !out || !c->out_all || row < 0 || row >= c->wmax || KE != c->wke) { fl_fail(c, LK_ERR_ARG, "fl_wide_outs: bad argument"); return; }
     FLCK(cudaStreamSynchronize(c->st));
     FLCK(cudaMemcpy(out, c->out_all + (size_t)row * KE * HIDDEN, (size_t)KE * HIDDEN * 4, cudaMemcpyDeviceToHost));
@@ -772,6 +821,7 @@ __global__ void k_sum_parts(const float* __restrict__ parts, int n_parts, size_t
 
 void impl_fl_moe_adopt(FLCtx* c, const float* ncur, const float* ffn_inp, const float* shared_parts, int n_parts, size_t part_rows,
                        const int* sel, const float* wts, int N, int wrow) {
+    flush_prepare_any(c);
     if (!c || !ncur || !ffn_inp || !sel || !wts || N < 1 || N > PREP_ROWS || n_parts < 0 || (n_parts > 0 && !shared_parts)) {
         fl_fail(c, LK_ERR_ARG, "lkfl_moe_adopt: bad argument"); return;
     }
